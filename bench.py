@@ -1,0 +1,348 @@
+#!/usr/bin/env python
+"""Decode throughput of the Qwen3 token loop on B200 (batch 1).
+
+Workload (default): the Qwen3-8B-shaped bf16 model (36 layers, hidden 4096,
+32/8 heads, FFN 12288, untied lm_head, vocab 151936) as a seeded synthetic
+GGUF; a 4096-token random prompt is prefilled, then greedy decode. One step is
+one decode token at batch 1.
+
+  value  tokens/s with everything resident in HBM: `steps` greedy tokens whose
+         argmax feeds the next token on the device (chained CUDA-graph frames),
+         timed with CUDA events on the launching stream.
+  e2e    the same through the reference-facing C ABI call per token
+         (mf_model_forward: step record H2D from pinned memory, frame, step
+         record with the greedy id D2H), timed the same way.
+Each step reads ~16.4 GB (weights + KV), far more than L2, so no flush is
+needed between steps.
+
+`--impl reference` runs the reference's own CPU token loop (oracle/_ref, built
+from the reference sources; the oracle port if absent) on the host cores on a
+bounded sample of the same workload.
+Multi-GPU runs (torchrun) use one rank per GPU, each decoding its own copy
+("replicas"): no tensor parallelism yet.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from minfer_b200.gguf_synth import CONFIGS, ensure_gguf  # noqa: E402
+
+METRIC = "decode tokens/s (batch 1) and % HBM roofline at 1/2/4/8 B200; prefill tok/s"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def model_path(workload: str) -> Path:
+    d = Path(os.environ.get("MF_MODEL_DIR", "/dev/shm" if Path("/dev/shm").is_dir() else "/tmp"))
+    return d / f"minfer_b200_{workload}.gguf"
+
+
+def prepare_model(workload: str, rank: int, world: int):
+    path = model_path(workload)
+    cfg = CONFIGS[workload]
+    if rank == 0:
+        ensure_gguf(path, cfg)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    return str(path), cfg
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.tmp,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        self.tmp.flush()
+        rows = [r.split(",") for r in Path(self.tmp.name).read_text().strip().splitlines() if r.strip()]
+        os.unlink(self.tmp.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def token_bytes(info, ctx: int) -> float:
+    """Algorithmic bytes of one decode token at context ctx: every weight byte
+    the forward reads (lm_head included) plus the KV rows read (ctx+1 rows)."""
+    return float(info.read_bytes_logits) + float(info.kv_bytes_per_pos) * (ctx + 1)
+
+
+def time_dominant_kernel(cfg, peaks, iters: int = 20) -> dict:
+    """The fused gate/up + SiLU GEMV of one layer (the largest weight stream of
+    a dense decode step), timed alone with CUDA events on torch's stream."""
+    import torch
+
+    from minfer_b200 import ops
+
+    d, F = cfg.d_model, cfg.d_ff
+    g = torch.Generator(device="cuda").manual_seed(1)
+    w = (torch.randn(2 * F, d, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    x = torch.randn(d, generator=g, device="cuda")
+    nw = torch.ones(d, device="cuda")
+    h = torch.empty(F, device="cuda")
+    for _ in range(3):
+        ops.swiglu_matmul(h, x, nw, 1e-6, w, F, d)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        ops.swiglu_matmul(h, x, nw, 1e-6, w, F, d)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    algo = 2 * F * d * 2 + 2 * d * 4 + F * 4
+    achieved = algo / (ms * 1e-3) / 1e9
+    traffic = None
+    prof = ROOT / "profiles" / "gemv_swiglu_qwen3-8b.txt"
+    if prof.exists():
+        for line in prof.read_text().splitlines():
+            if line.startswith("dram_bytes_per_launch:"):
+                traffic = float(line.split(":")[1])
+    return {"kernel": "gemv_kernel<W_BF16,...,X_NORM,Y_SWIGLU> (gate/up + SiLU, one layer)",
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic, "algo_bytes": algo,
+            "avg_launch_us": round(ms * 1e3, 2)}
+
+
+def run_reference_cpu(path: str, ctx: int, steps: int, warmup: int, threads: int) -> dict:
+    """Reference CPU token loop at context ctx: `steps` timed decode forwards."""
+    from oracle import oracle_py
+
+    with tempfile.TemporaryDirectory() as td:
+        if oracle_py.ref_available():
+            res = oracle_py.run_reference(path, f"{td}/r", bench_context=ctx, bench_steps=steps,
+                                          bench_warmup=warmup, threads=threads, timeout=1800)
+            kind = "reference"
+        else:
+            pm = oracle_py.PortModel(path, max_seq=ctx + steps + warmup + 1)
+            ts = []
+            for s in range(warmup + steps):
+                t0 = time.perf_counter()
+                pm.forward(1 + s, ctx + s, True)
+                if s >= warmup:
+                    ts.append(time.perf_counter() - t0)
+            res = {"tok_per_s": len(ts) / sum(ts), "seconds": sum(ts)}
+            kind = "port"
+    return {"value": res["tok_per_s"], "unit": "tokens/s", "cores": threads, "kind": kind,
+            "sample": f"{steps} decode tokens (+{warmup} warm-up) at context {ctx} on the same GGUF, "
+                      f"KV rows below the context zero-filled, OMP_NUM_THREADS={threads}",
+            "seconds": res["seconds"]}
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="minfer_b200", choices=["minfer_b200", "reference"])
+    ap.add_argument("--workload", default="qwen3-8b-bf16", choices=sorted(CONFIGS))
+    ap.add_argument("--context", type=int, default=4096, help="prompt tokens prefilled before decode")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-steps", type=int, default=6)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank, world, local_rank = dist_env()
+    cfgshape = CONFIGS[args.workload]
+    config = {"workload": f"{args.workload} greedy decode at batch 1 after a {args.context}-token prompt",
+              "context": args.context, "batch": 1,
+              "l2": "inputs larger than L2 (each step streams all weights and the KV cache)",
+              "parallelism": "single" if world == 1 else f"replicas{world}"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        path, _ = prepare_model(args.workload, 0, 1)
+        thr = host_threads()
+        cb = run_reference_cpu(path, args.context, args.steps, args.warmup, thr)
+        line = {"metric": METRIC, "value": round(cb["value"], 4), "unit": "tokens/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 / cb["value"], 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": config, "impl": "reference", "cpu_baseline": cb,
+                "e2e": {"value": round(cb["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local_rank))
+    from minfer_b200 import model as mm
+    from minfer_b200._lib import check, cuda_lib
+
+    mm.init(1, [local_rank])
+    lib = cuda_lib()
+    path, cfg = prepare_model(args.workload, rank, world)
+    ctx = args.context
+    n_tok = args.warmup + 2 * args.steps + 4
+    t_load = time.perf_counter()
+    m = mm.Qwen3Model(path, mm.RunParams(num_iters=n_tok, max_seq_len=ctx + n_tok + 2), device=local_rank)
+    m.set_device("cuda")
+    t_load = time.perf_counter() - t_load
+    info = m.info
+    prompt = mm.random_prompt(ctx, info.vocab_size, 30 + rank)
+
+    # prefill (token by token through the decode frames), timed on the device
+    check(lib.mf_timer_start(0))
+    for i, t in enumerate(prompt):
+        m.forward(int(t), i, i == ctx - 1, False)
+    ms = C.c_float()
+    check(lib.mf_timer_stop(0, C.byref(ms)))
+    prefill_s = ms.value / 1e3
+    tok = m.argmax()
+
+    # warm-up (graphs captured, clocks up)
+    tok = m.decode_chained(tok, ctx, args.warmup)
+    pos = ctx + args.warmup
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        import torch.distributed as dist
+
+        t = torch.tensor([v], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    # ---- value: chained device-side decode
+    barrier()
+    with Clocks(local_rank) as clk:
+        check(lib.mf_timer_start(0))
+        tok = m.decode_chained(tok, pos, args.steps)
+        check(lib.mf_timer_stop(0, C.byref(ms)))
+    barrier()
+    dev_ms = max_over_ranks(ms.value)
+    pos += args.steps
+    value = world * args.steps / (dev_ms / 1e3)
+
+    # ---- e2e: one reference-facing call per token, host in the loop
+    barrier()
+    check(lib.mf_timer_start(0))
+    for i in range(args.steps):
+        m.forward(int(tok), pos + i, True, False)
+        tok = m.argmax()
+    check(lib.mf_timer_stop(0, C.byref(ms)))
+    barrier()
+    e2e_ms = max_over_ranks(ms.value)
+    e2e = world * args.steps / (e2e_ms / 1e3)
+
+    peaks, peak_kind = load_peaks()
+    ctx_mid = ctx + args.warmup + args.steps // 2
+    tb = token_bytes(info, ctx_mid)
+    step_gbs = tb / (dev_ms / args.steps / 1e3) / 1e9
+    roof = time_dominant_kernel(cfgshape, peaks) if rank == 0 else None
+
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline:
+            try:
+                cpu = run_reference_cpu(path, ctx, args.cpu_steps, 1, host_threads())
+            except Exception as e:  # reported, not fatal
+                cpu = {"value": None, "error": str(e)[:200]}
+        launches_per_step = 2 + 5 * info.n_layers if info.n_experts == 0 else 2 + 6 * info.n_layers
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "compute": "fp32 accumulate, fp32 activations/KV",
+            "data": "synthetic (seeded GGUF, random prompt ids)", "config": config,
+            "e2e": {"value": round(e2e, 3), "unit": "tokens/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 16,
+                    "ms_per_step": round(e2e_ms / args.steps, 4)},
+            "gpu_launches": launches_per_step * args.steps,
+            "hbm_roofline": {"bytes_per_token": tb, "achieved_gbs": round(step_gbs, 1), "peak_gbs": peaks["hbm_gbs"],
+                             "frac": round(step_gbs / peaks["hbm_gbs"], 4), "peak_kind": peak_kind},
+            "roofline": dict(roof, peak_kind=peak_kind),
+            "prefill": {"tokens": ctx, "seconds": round(prefill_s, 3), "tok_per_s": round(ctx / prefill_s, 1),
+                        "method": "token-by-token decode frames"},
+            "cpu_baseline": cpu, "clocks": clk.summary(), "load_seconds": round(t_load, 2),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

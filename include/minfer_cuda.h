@@ -1,0 +1,233 @@
+/*
+ * minfer_cuda.h — C ABI of libmfcuda.so, the sm_100a (B200) device layer of the
+ * Qwen3 token loop.
+ *
+ * It takes the place of two reference interfaces:
+ *   - the Metal device manager, include/minfer/interfaces/metal_interface.hpp:9-37
+ *     (MetalManager::init/upload/release/cpu_ptr/begin_frame/end_frame/dispatch*);
+ *   - the name-addressed GPU kernels dispatched from src/models/qwen3/module.cpp
+ *     (MetalManager::dispatch1d/2d("linear_proj_bf16", ...) and friends), which
+ *     become typed entry points below.
+ *
+ * Conventions
+ *   - Every entry point returns MF_OK (0) or a negative MF_E_* status; the
+ *     message of the last failure on the calling thread is available through
+ *     mf_last_error(). No C++ exception crosses this boundary.
+ *   - Device buffers are plain device addresses (`void*`, `float*`), obtained
+ *     from mf_upload/mf_alloc (mf_ptr) or from any other CUDA allocator.
+ *   - `stream` is a cudaStream_t passed as void*; NULL means the manager stream
+ *     of the current device (mf_init must have been called).
+ *   - Weight dtypes use the reference's DataType codes
+ *     (include/minfer/base/types.hpp:5): MF_F32 = 0, MF_F16 = 1, MF_BF16 = 2.
+ *   - Activations, KV cache, logits: fp32, as in the reference's RunState
+ *     (include/minfer/base/config.hpp:77-102).
+ *   - Not thread-safe, like the reference's process-global Metal context
+ *     (src/interfaces/metal_interface.mm:59): drive a manager from one thread.
+ */
+#ifndef MINFER_CUDA_H
+#define MINFER_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define MF_OK 0
+#define MF_E_INVALID (-1)     /* bad argument (null pointer, size, dtype, shape) */
+#define MF_E_CUDA (-2)        /* a CUDA runtime call failed */
+#define MF_E_OOM (-3)         /* device allocation failed or request too large */
+#define MF_E_TIMEOUT (-4)     /* a bounded wait gave up (peer never arrived) */
+#define MF_E_UNSUPPORTED (-5) /* shape/dtype combination without a kernel */
+#define MF_E_STATE (-6)       /* call out of order (e.g. no mf_init) */
+#define MF_E_IO (-7)          /* file could not be read or parsed */
+
+/* ---- dtypes (reference DataType, include/minfer/base/types.hpp:5) ---- */
+#define MF_F32 0
+#define MF_F16 1
+#define MF_BF16 2
+
+/* ---- frames --------------------------------------------------------- */
+#define MF_FRAME_RECORD 0 /* begin_frame: ops issued now are captured */
+#define MF_FRAME_REPLAY 1 /* begin_frame: a captured frame exists; issue nothing */
+#define MF_FRAME_NO_UPLOAD 1 /* begin_frame_ex flag: keep the device step record as is */
+
+typedef struct mf_buf mf_buf;
+
+/* ===================================================================== */
+/* Manager — replaces MetalManager (metal_interface.hpp:9-37)             */
+/* ===================================================================== */
+
+/* MetalManager::init (src/interfaces/metal_interface.mm:81-109). Selects the
+ * devices of `n_ranks` ranks (devices == NULL: 0..n_ranks-1) and creates one
+ * stream per rank. Calling it again with the same arguments is a no-op. */
+int mf_init(int n_ranks, const int* devices);
+/* Releases every frame, stream and buffer still owned by the manager. */
+int mf_shutdown(void);
+/* Number of visible CUDA devices. */
+int mf_device_count(int* count);
+/* Message of the last failure on this thread (always NUL-terminated). */
+int mf_last_error(char* buf, size_t n);
+
+/* MetalManager::upload (metal_interface.mm:65-70): copy `bytes` from host
+ * memory into a new device buffer of rank `rank`. */
+int mf_upload(const void* host, size_t bytes, int rank, mf_buf** out);
+/* Zero-filled device buffer of `bytes` on rank `rank`. */
+int mf_alloc(size_t bytes, int rank, mf_buf** out);
+/* MetalManager::release (metal_interface.mm:72-74). NULL is ignored. */
+void mf_release(mf_buf* buf);
+/* Device address of a buffer (the handle the ops take). */
+void* mf_ptr(const mf_buf* buf);
+size_t mf_size(const mf_buf* buf);
+/* Explicit copies replace MetalManager::cpu_ptr's shared-memory view
+ * (metal_interface.mm:76-78). Both synchronise the rank's stream. */
+int mf_read(const mf_buf* buf, size_t offset, void* host, size_t bytes);
+int mf_write(mf_buf* buf, size_t offset, const void* host, size_t bytes);
+
+/* Strided upload: `rows` runs of `width` bytes from host (src_pitch apart)
+ * into buf at offset, dst_pitch apart. Used to lay weights out for the
+ * kernels (e.g. gate/up rows interleaved) straight from the mapped file. */
+int mf_write_2d(mf_buf* buf, size_t offset, size_t dst_pitch, const void* host, size_t src_pitch, size_t width,
+                size_t rows);
+/* Device-to-device copy inside one rank's buffers (synchronous). */
+int mf_copy(mf_buf* dst, size_t dst_off, const mf_buf* src, size_t src_off, size_t bytes);
+/* Page-locked host memory (for per-token logits / ids). */
+int mf_host_alloc(size_t bytes, void** out);
+void mf_host_free(void* p);
+/* Asynchronous device->host copy on `stream` (capturable inside a frame). */
+int mf_copy_to_host_async(void* host, const void* dev, size_t bytes, void* stream);
+
+/* MetalManager::begin_frame / end_frame (metal_interface.mm:111-137): one
+ * frame is one token step. The first frame with a given id is captured into
+ * a CUDA graph (returns MF_FRAME_RECORD: issue the ops now); later frames with
+ * that id return MF_FRAME_REPLAY and the caller issues nothing. end_frame
+ * launches the graph and waits for it, like the reference's commit+wait. */
+int mf_begin_frame(int rank, int frame_id);
+/* As begin_frame; with MF_FRAME_NO_UPLOAD the captured frame does not copy the
+ * host step record in, so a chained record (see mf_lm_head) drives it. */
+int mf_begin_frame_ex(int rank, int frame_id, int flags);
+int mf_end_frame(int rank);
+/* Same as end_frame without the wait (frames pipelined on the stream). */
+int mf_end_frame_async(int rank);
+/* Ends an open frame without launching it (a failed capture is discarded). */
+int mf_abort_frame(int rank);
+/* Drops every captured frame of `rank` (after buffers were reallocated). */
+int mf_reset_frames(int rank);
+/* Waits for all work on the rank's stream. */
+int mf_sync(int rank);
+/* The rank's stream as a cudaStream_t. */
+void* mf_stream(int rank);
+/* Device-side timing of everything issued on the rank's stream between
+ * start and stop (CUDA events; stop waits for the stop event). */
+int mf_timer_start(int rank);
+int mf_timer_stop(int rank, float* ms);
+/* Host-visible step record copied to the device at the start of every frame
+ * launch: {token, pos, next_token, chain}. Returns a pinned host pointer and the
+ * matching device pointer. */
+int mf_step_state(int rank, int32_t** host, void** device);
+
+/* ===================================================================== */
+/* Token-loop ops (fused). Each replaces a run of Metal dispatches of     */
+/* src/models/qwen3/module.cpp; the cited lines are the CPU path they     */
+/* reproduce.                                                             */
+/* ===================================================================== */
+
+/* Qwen3Embed (module.cpp:19-44): x[0:d) = fp32(emb[token]), token read from
+ * the device step record (an id outside [0, vocab) reads row 0). */
+int mf_embed_step(float* x, const void* emb, int dtype, int vocab, int d_model, const void* step_state,
+                  void* stream);
+
+/* Host helper: the NeoX RoPE (cos, sin) table, out[(p*(d_rot/2) + i)*2 + {0,1}]
+ * for positions p < n_pos, with freq_i = 1.0f / powf(base, 2.0f*i/d_rot) and
+ * angle = p * freq_i in float (src/ops/kernels.cpp:71-79). */
+int mf_rope_table(float* out, int n_pos, int d_rot, float base);
+
+/* y[0:d_out) = W · rmsnorm(x, norm_w, eps)  (rmsnorm + linear_proj,
+ * module.cpp:187-191 fused; Q/K/V are one concatenated weight). */
+int mf_rmsnorm_matmul(float* y, const float* x, const float* norm_w, float eps, const void* w, int dtype,
+                      int d_out, int d_in, void* stream);
+
+/* x[0:d_out) += W · a  (linear_proj + resadd, module.cpp:236-240). */
+int mf_matmul_residual(float* x, const float* a, const void* w, int dtype, int d_out, int d_in, void* stream);
+
+/* h[i] = silu(g_i) * u_i, g/u = rows 2i / 2i+1 of the interleaved gate/up
+ * weight [2*d_ff, d_in] applied to rmsnorm(x)  (module.cpp:446,464-468). */
+int mf_swiglu_matmul(float* h, const float* x, const float* norm_w, float eps, const void* w_gate_up, int dtype,
+                     int d_ff, int d_in, void* stream);
+
+/* Attention for one token (module.cpp:193-234 fused): per-head Q/K RMSNorm,
+ * NeoX RoPE, append of K/V row `pos`, GQA attention over positions [0, pos].
+ * qkv = [Hq*D | Hkv*D | Hkv*D] (output of the fused projection); caches are
+ * [n_kv_heads][max_seq][d_head] fp32 for this layer. The workspace must hold
+ * mf_attn_workspace_bytes() bytes and be zero-filled before its first use;
+ * every call leaves its counters zero again. d_head must be 128. */
+typedef struct mf_attn_desc {
+    const float* qkv;
+    const float* q_norm_w;
+    const float* k_norm_w;
+    float eps;
+    const void* rope_table; /* mf_rope_table for >= max_seq positions (device) */
+    float* k_cache;
+    float* v_cache;
+    int max_seq;
+    const void* step_state; /* device step record (pos) */
+    float* out;            /* [Hq*D] */
+    int n_heads;
+    int n_kv_heads;
+    int d_head;
+    int n_split;           /* position slices per KV head (mf_attn_default_split) */
+    void* workspace;
+} mf_attn_desc;
+size_t mf_attn_workspace_bytes(int n_heads, int n_kv_heads, int d_head, int n_split);
+int mf_attn_default_split(int n_kv_heads, int max_seq);
+int mf_attn_decode(const mf_attn_desc* desc, void* stream);
+
+/* MoE router + top-k + renormalisation (module.cpp:446-457, kernels.cpp:113-139):
+ * scores = W_router(f32 [E, d]) · rmsnorm(x); ids/weights of the k best. */
+int mf_router_topk(int* ids, float* weights, float* scores, const float* x, const float* norm_w, float eps,
+                   const float* w_router, int d_model, int n_experts, int k, void* stream);
+
+/* Selected experts' SwiGLU (module.cpp:459-468): h[s*d_ff + i] for slot s < k
+ * from the interleaved per-expert gate/up weight [E][2*d_ff][d_in]. */
+int mf_moe_swiglu(float* h, const float* x, const float* norm_w, float eps, const void* w_gate_up_exps, int dtype,
+                  const int* ids, int k, int d_ff, int d_in, void* stream);
+
+/* Selected experts' down projection + weighted residual (module.cpp:469-474):
+ * x[j] += sum over slots s in order of w_s * (W_down[ids[s]] · h_s)[j]. */
+int mf_moe_down_residual(float* x, const float* h, const void* w_down_exps, int dtype, const int* ids,
+                         const float* weights, int k, int d_model, int d_ff, void* stream);
+
+/* Final RMSNorm + lm_head (module.cpp:54-79,113-126): logits = W · rmsnorm(x).
+ * When step_state (a device step record) is non-NULL the greedy id (first
+ * maximum, sampler.cpp:37) is written to its next_token field, and if its
+ * chain field is non-zero the record advances (token = next_token, pos += 1)
+ * for the next frame. The workspace (mf_lm_head_workspace_bytes, zero-filled
+ * before first use) is then required. vocab_offset shifts the reported id
+ * (vocab-split lm_head). */
+size_t mf_lm_head_workspace_bytes(void);
+int mf_lm_head(float* logits, const float* x, const float* norm_w, float eps, const void* w, int dtype, int vocab,
+               int d_model, int vocab_offset, void* step_state, void* workspace, void* stream);
+
+/* ===================================================================== */
+/* Single ops with the reference's CPU signatures                        */
+/* (include/minfer/ops/kernels.hpp:13-32) on device buffers.              */
+/* ===================================================================== */
+int mf_matmul(float* y, const float* x, const void* w, int dtype, size_t offset, int d_out, int d_in, void* stream);
+int mf_rmsnorm(float* out, const float* x, const float* w, int dim, float eps, int n_rows, void* stream);
+int mf_softmax(float* out, const float* x, int n, int n_rows, void* stream);
+int mf_silu(float* out, const float* x, int n, void* stream);
+int mf_neox_rope(float* out, const float* x, int head, int d_head, int d_rot, float base, int pos, void* stream);
+int mf_il_rope(float* out, const float* x, int head, int d_head, int d_rot, float base, int pos, void* stream);
+int mf_attn(float* scores, float* out, const float* q, const float* k, const float* v, int seq_len, int d_head,
+            int kv_dim, void* stream);
+int mf_route(const float* x, int* ids, float* weights, float* scores, const float* w_router, int d_model,
+             int n_experts, int k, void* stream);
+int mf_embed(float* x, const void* w, int dtype, uint32_t token, int d_model, void* stream);
+int mf_argmax(const float* logits, int n, int* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MINFER_CUDA_H */

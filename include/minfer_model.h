@@ -1,0 +1,116 @@
+/*
+ * minfer_model.h — C ABI of libminfer_host.so, the C++17 host runtime of the
+ * Qwen3 token loop on CUDA (GGUF loader, Config/RunState, Qwen3 layers,
+ * sampler, token loop) built over libmfcuda (minfer_cuda.h).
+ *
+ * It exposes what the reference's apps and tests reach through BaseModel
+ * (include/minfer/base/model.hpp:17-41): construction from a GGUF file
+ * (Qwen3Model::Qwen3Model, src/models/qwen3/model.cpp:9-86), set_device,
+ * forward, generate and benchmark — with token ids instead of text, since the
+ * tokenizer is not part of this path.
+ *
+ * Status codes are the MF_* codes of minfer_cuda.h; mf_last_error() returns
+ * the message of the last failure (host-runtime failures included).
+ */
+#ifndef MINFER_MODEL_H
+#define MINFER_MODEL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "minfer_cuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct mf_model mf_model;
+
+/* Message of the last failure of this library or of libmfcuda on this thread. */
+int mf_host_last_error(char* buf, size_t n);
+
+/* RunParams (include/minfer/base/config.hpp:37-51) */
+typedef struct mf_run_params {
+    size_t num_iters;
+    size_t max_seq_len;
+    size_t top_k;
+    float temp;
+    float top_p;
+    float min_p;
+    float penalty_pres;
+    int seed;
+} mf_run_params;
+
+/* Config fields a caller needs (include/minfer/base/config.hpp:53-75) */
+typedef struct mf_model_info {
+    size_t vocab_size;
+    size_t max_seq_len;
+    int d_model, n_layers, n_heads, n_kv_heads, d_head, d_ff, n_experts, n_active_experts;
+    int weight_dtype; /* MF_F32 / MF_F16 / MF_BF16 */
+    int untied_head;
+    uint32_t eos_token_id;
+    float rms_norm_eps, freq_base;
+    size_t read_bytes_logits;    /* weight bytes one forward with logits reads */
+    size_t read_bytes_no_logits; /* ... without the lm_head */
+    size_t kv_bytes_per_pos;     /* 2 * n_layers * n_kv_heads * d_head * 4 */
+} mf_model_info;
+
+/* GenStats (include/minfer/base/stats.hpp:3-15) */
+typedef struct mf_gen_stats {
+    int num_tokens_gen;
+    float ttft, throughput, prefill_time, bandwidth;
+    double decode_seconds;
+    double bytes_read;
+} mf_gen_stats;
+
+/* Parse the GGUF file and build the layer list; rank selects the manager
+ * rank (device) the model lives on. mf_init must have been called. */
+int mf_model_load(const char* gguf_path, const mf_run_params* rp, int rank, mf_model** out);
+/* BaseModel::set_device(DeviceType::CUDA): upload weights, allocate RunState. */
+int mf_model_to_cuda(mf_model* m);
+int mf_model_info_get(const mf_model* m, mf_model_info* out);
+void mf_model_free(mf_model* m);
+
+/* BaseModel::forward for one token at `pos` (src/base/model.cpp:36-59).
+ * host_logits != 0 copies the logits to host memory (mf_model_logits). */
+int mf_model_forward(mf_model* m, uint32_t token, int pos, int compute_logits, int host_logits);
+/* Logits of the last forward that computed them with host_logits set. */
+int mf_model_logits(const mf_model* m, float* out, size_t n);
+/* Greedy id (first maximum) of the last forward that computed logits. */
+int mf_model_argmax(const mf_model* m, uint32_t* out);
+
+/* BaseModel::generate without the tokenizer (src/base/model.cpp:99-186):
+ * prompt, then sample -> append -> forward. flags: bit0 stop at EOS,
+ * bit1 record the top-2 logit margin of every step into margins[n_gen].
+ * forced (may be NULL): teacher forcing — the model's pick of step i is
+ * reported in out_ids[i] but forced[i] is fed back. Returns the number of
+ * generated ids in *n_out. */
+int mf_model_generate(mf_model* m, const uint32_t* prompt, size_t n_prompt, size_t n_gen, int flags,
+                      const uint32_t* forced, uint32_t* out_ids, size_t* n_out, float* margins,
+                      mf_gen_stats* stats);
+#define MF_GEN_STOP_AT_EOS 1
+#define MF_GEN_MARGINS 2
+
+/* Greedy decode of n tokens with the device feeding itself (no host round
+ * trip between tokens), starting with `token` at `start_pos`. Blocks until
+ * done; returns the last greedy id. */
+int mf_model_decode_chained(mf_model* m, uint32_t token, int start_pos, int n, uint32_t* last_id);
+
+/* Resets the sampler (RNG stream and presence set) to its initial state. */
+int mf_model_reset_sampler(mf_model* m);
+
+/* Test access: experts selected at `layer` by the last forward (k ids and
+ * weights), the KV rows [0, n_pos) of `layer` in the reference's
+ * [pos][kv_head][d_head] order, and the residual stream x. */
+int mf_model_experts(const mf_model* m, int layer, int* ids, float* weights);
+int mf_model_kv(const mf_model* m, int layer, float* k, float* v, int n_pos);
+int mf_model_x(const mf_model* m, float* x);
+
+/* Prompt ids as BaseModel::benchmark draws them (src/base/model.cpp:189-193):
+ * std::mt19937(seed) + std::uniform_int_distribution<>(0, vocab-1). */
+int mf_random_prompt(int seed, uint32_t vocab, size_t n, uint32_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MINFER_MODEL_H */

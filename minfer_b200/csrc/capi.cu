@@ -1,0 +1,840 @@
+// libmfcuda: C ABI over the sm_100a kernels (see include/minfer_cuda.h).
+//
+// The manager part replaces the reference's Metal context
+// (src/interfaces/metal_interface.mm): a process-global table of ranks, each
+// with its device, one stream, pinned step record and the captured CUDA graphs
+// of its frames. Ops launch with programmatic dependent launch so a kernel's
+// weight prefetch overlaps its predecessor's tail, inside captured graphs too.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "gemv_inst.cuh"
+#include "minfer_cuda.h"
+#include "misc.cuh"
+
+struct mf_buf {
+    void* ptr;
+    size_t bytes;
+    int rank;
+};
+
+namespace mf {
+const void* attn_kernel_ptr(int group);
+}
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+#define MF_CK(expr)                                                                              \
+    do {                                                                                         \
+        cudaError_t e_ = (expr);                                                                 \
+        if (e_ != cudaSuccess) return fail(MF_E_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+    } while (0)
+
+#define MF_REQUIRE(cond, code, ...)                 \
+    do {                                            \
+        if (!(cond)) return fail(code, __VA_ARGS__); \
+    } while (0)
+
+struct Rank {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int32_t* h_step = nullptr;  // pinned {token, pos, next_token, pad}
+    void* d_step = nullptr;
+    std::map<int, cudaGraphExec_t> frames;
+    cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
+    int recording = -1;  // frame id being captured
+    int pending = -1;    // frame id to launch at end_frame
+};
+
+struct Ctx {
+    bool inited = false;
+    std::vector<Rank> ranks;
+    std::set<mf_buf*> bufs;
+};
+
+Ctx g;
+
+bool pdl_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = std::getenv("MF_PDL");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+
+int num_sms() {
+    static int n[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (n[dev] == 0) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        n[dev] = v > 0 ? v : 148;
+    }
+    return n[dev];
+}
+
+cudaStream_t resolve(void* s) {
+    if (s) return (cudaStream_t)s;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    for (auto& r : g.ranks)
+        if (r.device == dev) return r.stream;
+    return (cudaStream_t)0;
+}
+
+// Launch with the programmatic-serialization attribute.
+cudaError_t launch(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+// Per-kernel one-time attribute setup + occupancy cache.
+struct KInfo {
+    int max_smem_set = 0;
+    std::map<size_t, int> occ;
+};
+std::map<std::pair<int, const void*>, KInfo> g_kinfo;
+std::mutex g_kmu;
+
+int prepare(const void* fn, int threads, size_t smem, int* blocks_per_sm) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(g_kmu);
+    KInfo& ki = g_kinfo[{dev, fn}];
+    if ((int)smem > ki.max_smem_set && smem > 48 * 1024) {
+        MF_CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        ki.max_smem_set = (int)smem;
+    }
+    auto it = ki.occ.find(smem);
+    if (it == ki.occ.end()) {
+        int b = 0;
+        MF_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, fn, threads, smem));
+        it = ki.occ.emplace(smem, b).first;
+    }
+    *blocks_per_sm = it->second;
+    MF_REQUIRE(it->second > 0, MF_E_UNSUPPORTED, "kernel does not fit on an SM (smem %zu B)", smem);
+    return MF_OK;
+}
+
+const void* gemv_ptr(int dtype, int xm, int ym, int T, int R) {
+    switch (dtype) {
+        case MF_F32: return mf::gemv_kernel_ptr_f32(xm, ym, T, R);
+        case MF_F16: return mf::gemv_kernel_ptr_f16(xm, ym, T, R);
+        case MF_BF16: return mf::gemv_kernel_ptr_bf16(xm, ym, T, R);
+        default: return nullptr;
+    }
+}
+
+int vec_of(int dtype) { return dtype == MF_F32 ? 4 : 8; }
+size_t esz_of(int dtype) { return dtype == MF_F32 ? 4 : 2; }
+
+// Pick (T, R): the fewest idle lanes over K, then more threads, then taller tiles.
+void choose_shape(int K, int dtype, int ym, int* T_out, int* R_out) {
+    const int vec = vec_of(dtype);
+    const int Ts[3] = {256, 128, 64};
+    const int Rs[3] = {8, 4, 2};
+    double best = 1e30;
+    int bT = 256, bR = 8;
+    for (int ti = 0; ti < 3; ++ti) {
+        for (int ri = 0; ri < 3; ++ri) {
+            const int T = Ts[ti], R = Rs[ri], PC = 8 / R;
+            if (ym == mf::Y_MOE_DOWN && R != 8) continue;
+            const long long step = (long long)PC * T * vec;
+            const long long nsteps = (K + step - 1) / step;
+            const double waste = (double)(nsteps * step) / K;
+            // prefer exact fits; among equals more threads, then R=4 (balanced)
+            const double score = waste * 1000.0 - T * 0.01 - (R == 4 ? 0.001 : 0.0);
+            if (score < best) {
+                best = score;
+                bT = T;
+                bR = R;
+            }
+        }
+    }
+    *T_out = bT;
+    *R_out = bR;
+}
+
+int run_gemv(int dtype, int xm, int ym, mf::GemvParams& p, long long units, cudaStream_t st, int max_grid = 0) {
+    MF_REQUIRE(p.K > 0 && p.K % 16 == 0, MF_E_INVALID, "d_in must be a positive multiple of 16 (got %d)", p.K);
+    MF_REQUIRE(p.rows > 0, MF_E_INVALID, "d_out must be positive");
+    MF_REQUIRE(((uintptr_t)p.w + p.w_offset * esz_of(dtype)) % 16 == 0, MF_E_INVALID,
+               "weight rows must start 16-byte aligned");
+    MF_REQUIRE(((uintptr_t)p.x) % 16 == 0, MF_E_INVALID, "activation vector must be 16-byte aligned");
+    int T, R;
+    choose_shape(p.K, dtype, ym, &T, &R);
+    const void* fn = gemv_ptr(dtype, xm, ym, T, R);
+    MF_REQUIRE(fn != nullptr, MF_E_UNSUPPORTED, "no GEMV kernel for dtype %d", dtype);
+    const size_t xfloats = (ym == mf::Y_MOE_DOWN) ? (size_t)p.K * p.n_slots : (size_t)p.K;
+    const size_t smem = xfloats * sizeof(float);
+    MF_REQUIRE(smem <= 200 * 1024, MF_E_UNSUPPORTED, "activation vector of %zu floats exceeds shared memory", xfloats);
+    int bps = 0;
+    int rc = prepare(fn, T, smem, &bps);
+    if (rc) return rc;
+    long long grid = (long long)num_sms() * bps;
+    if (grid > units) grid = units;
+    if (max_grid > 0 && grid > max_grid) grid = max_grid;
+    if (grid < 1) grid = 1;
+    void* args[] = {&p};
+    MF_CK(launch(fn, dim3((unsigned)grid), dim3(T), smem, st, args));
+    return MF_OK;
+}
+
+bool valid_dtype(int dt) { return dt == MF_F32 || dt == MF_F16 || dt == MF_BF16; }
+
+constexpr int LMH_MAX_GRID = 4096;
+
+}  // namespace
+
+extern "C" {
+
+// ===================================================================== manager
+
+int mf_last_error(char* buf, size_t n) {
+    if (!buf || n == 0) return MF_E_INVALID;
+    std::snprintf(buf, n, "%s", g_err);
+    return MF_OK;
+}
+
+int mf_device_count(int* count) {
+    MF_REQUIRE(count, MF_E_INVALID, "null count");
+    int c = 0;
+    cudaError_t e = cudaGetDeviceCount(&c);
+    if (e != cudaSuccess) {
+        *count = 0;
+        return fail(MF_E_CUDA, "cudaGetDeviceCount: %s", cudaGetErrorString(e));
+    }
+    *count = c;
+    return MF_OK;
+}
+
+int mf_init(int n_ranks, const int* devices) {
+    MF_REQUIRE(n_ranks >= 1 && n_ranks <= 64, MF_E_INVALID, "n_ranks out of range: %d", n_ranks);
+    if (g.inited) {
+        bool same = (int)g.ranks.size() == n_ranks;
+        for (int i = 0; same && i < n_ranks; ++i) same = g.ranks[i].device == (devices ? devices[i] : i);
+        MF_REQUIRE(same, MF_E_STATE, "mf_init called again with different ranks; call mf_shutdown first");
+        return MF_OK;
+    }
+    int ndev = 0;
+    MF_CK(cudaGetDeviceCount(&ndev));
+    g.ranks.assign(n_ranks, Rank{});
+    for (int i = 0; i < n_ranks; ++i) {
+        Rank& r = g.ranks[i];
+        r.device = devices ? devices[i] : i;
+        MF_REQUIRE(r.device >= 0 && r.device < ndev, MF_E_INVALID, "device %d not present (%d visible)", r.device,
+                   ndev);
+        MF_CK(cudaSetDevice(r.device));
+        MF_CK(cudaStreamCreateWithFlags(&r.stream, cudaStreamNonBlocking));
+        MF_CK(cudaHostAlloc((void**)&r.h_step, 16, cudaHostAllocDefault));
+        std::memset(r.h_step, 0, 16);
+        MF_CK(cudaMalloc(&r.d_step, 16));
+        MF_CK(cudaMemset(r.d_step, 0, 16));
+    }
+    MF_CK(cudaSetDevice(g.ranks[0].device));
+    g.inited = true;
+    return MF_OK;
+}
+
+int mf_shutdown(void) {
+    if (!g.inited) return MF_OK;
+    for (auto& r : g.ranks) {
+        cudaSetDevice(r.device);
+        if (r.stream) cudaStreamSynchronize(r.stream);
+        for (auto& kv : r.frames) cudaGraphExecDestroy(kv.second);
+        r.frames.clear();
+        if (r.ev_start) cudaEventDestroy(r.ev_start);
+        if (r.ev_stop) cudaEventDestroy(r.ev_stop);
+        if (r.stream) cudaStreamDestroy(r.stream);
+        if (r.h_step) cudaFreeHost(r.h_step);
+        if (r.d_step) cudaFree(r.d_step);
+    }
+    for (mf_buf* b : g.bufs) {
+        cudaSetDevice(g.ranks[b->rank].device);
+        cudaFree(b->ptr);
+        delete b;
+    }
+    g.bufs.clear();
+    g.ranks.clear();
+    g.inited = false;
+    return MF_OK;
+}
+
+static int alloc_impl(size_t bytes, int rank, mf_buf** out) {
+    MF_REQUIRE(g.inited, MF_E_STATE, "mf_init not called");
+    MF_REQUIRE(out, MF_E_INVALID, "null out");
+    MF_REQUIRE(rank >= 0 && rank < (int)g.ranks.size(), MF_E_INVALID, "rank %d out of range", rank);
+    MF_REQUIRE(bytes > 0, MF_E_INVALID, "zero-byte buffer");
+    MF_CK(cudaSetDevice(g.ranks[rank].device));
+    size_t free_b = 0, total_b = 0;
+    MF_CK(cudaMemGetInfo(&free_b, &total_b));
+    MF_REQUIRE(bytes <= free_b, MF_E_OOM, "buffer of %zu bytes exceeds free device memory (%zu)", bytes, free_b);
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(MF_E_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    }
+    mf_buf* b = new mf_buf{p, bytes, rank};
+    g.bufs.insert(b);
+    *out = b;
+    return MF_OK;
+}
+
+int mf_alloc(size_t bytes, int rank, mf_buf** out) {
+    int rc = alloc_impl(bytes, rank, out);
+    if (rc) return rc;
+    MF_CK(cudaMemsetAsync((*out)->ptr, 0, bytes, g.ranks[rank].stream));
+    MF_CK(cudaStreamSynchronize(g.ranks[rank].stream));
+    return MF_OK;
+}
+
+int mf_upload(const void* host, size_t bytes, int rank, mf_buf** out) {
+    MF_REQUIRE(host, MF_E_INVALID, "null host pointer");
+    int rc = alloc_impl(bytes, rank, out);
+    if (rc) return rc;
+    MF_CK(cudaMemcpyAsync((*out)->ptr, host, bytes, cudaMemcpyHostToDevice, g.ranks[rank].stream));
+    MF_CK(cudaStreamSynchronize(g.ranks[rank].stream));
+    return MF_OK;
+}
+
+void mf_release(mf_buf* buf) {
+    if (!buf || !g.bufs.count(buf)) return;
+    cudaSetDevice(g.ranks[buf->rank].device);
+    cudaStreamSynchronize(g.ranks[buf->rank].stream);
+    cudaFree(buf->ptr);
+    g.bufs.erase(buf);
+    delete buf;
+}
+
+void* mf_ptr(const mf_buf* buf) { return buf ? buf->ptr : nullptr; }
+size_t mf_size(const mf_buf* buf) { return buf ? buf->bytes : 0; }
+
+int mf_read(const mf_buf* buf, size_t offset, void* host, size_t bytes) {
+    MF_REQUIRE(buf && host, MF_E_INVALID, "null argument");
+    MF_REQUIRE(offset + bytes <= buf->bytes, MF_E_INVALID, "read past the end of the buffer");
+    Rank& r = g.ranks[buf->rank];
+    MF_CK(cudaSetDevice(r.device));
+    MF_CK(cudaMemcpyAsync(host, (char*)buf->ptr + offset, bytes, cudaMemcpyDeviceToHost, r.stream));
+    MF_CK(cudaStreamSynchronize(r.stream));
+    return MF_OK;
+}
+
+int mf_write(mf_buf* buf, size_t offset, const void* host, size_t bytes) {
+    MF_REQUIRE(buf && host, MF_E_INVALID, "null argument");
+    MF_REQUIRE(offset + bytes <= buf->bytes, MF_E_INVALID, "write past the end of the buffer");
+    Rank& r = g.ranks[buf->rank];
+    MF_CK(cudaSetDevice(r.device));
+    MF_CK(cudaMemcpyAsync((char*)buf->ptr + offset, host, bytes, cudaMemcpyHostToDevice, r.stream));
+    MF_CK(cudaStreamSynchronize(r.stream));
+    return MF_OK;
+}
+
+int mf_write_2d(mf_buf* buf, size_t offset, size_t dst_pitch, const void* host, size_t src_pitch, size_t width,
+                size_t rows) {
+    MF_REQUIRE(buf && host, MF_E_INVALID, "null argument");
+    MF_REQUIRE(width <= dst_pitch && width <= src_pitch, MF_E_INVALID, "width exceeds pitch");
+    MF_REQUIRE(rows == 0 || offset + (rows - 1) * dst_pitch + width <= buf->bytes, MF_E_INVALID,
+               "2-D write past the end of the buffer");
+    if (rows == 0 || width == 0) return MF_OK;
+    Rank& r = g.ranks[buf->rank];
+    MF_CK(cudaSetDevice(r.device));
+    MF_CK(cudaMemcpy2DAsync((char*)buf->ptr + offset, dst_pitch, host, src_pitch, width, rows,
+                            cudaMemcpyHostToDevice, r.stream));
+    MF_CK(cudaStreamSynchronize(r.stream));
+    return MF_OK;
+}
+
+int mf_copy(mf_buf* dst, size_t dst_off, const mf_buf* src, size_t src_off, size_t bytes) {
+    MF_REQUIRE(dst && src, MF_E_INVALID, "null argument");
+    MF_REQUIRE(dst->rank == src->rank, MF_E_INVALID, "copy across ranks");
+    MF_REQUIRE(dst_off + bytes <= dst->bytes && src_off + bytes <= src->bytes, MF_E_INVALID, "copy out of bounds");
+    Rank& r = g.ranks[dst->rank];
+    MF_CK(cudaSetDevice(r.device));
+    MF_CK(cudaMemcpyAsync((char*)dst->ptr + dst_off, (const char*)src->ptr + src_off, bytes,
+                          cudaMemcpyDeviceToDevice, r.stream));
+    MF_CK(cudaStreamSynchronize(r.stream));
+    return MF_OK;
+}
+
+int mf_host_alloc(size_t bytes, void** out) {
+    MF_REQUIRE(out && bytes > 0, MF_E_INVALID, "bad arguments");
+    MF_CK(cudaHostAlloc(out, bytes, cudaHostAllocDefault));
+    return MF_OK;
+}
+
+void mf_host_free(void* p) {
+    if (p) cudaFreeHost(p);
+}
+
+int mf_copy_to_host_async(void* host, const void* dev, size_t bytes, void* stream) {
+    MF_REQUIRE(host && dev, MF_E_INVALID, "null argument");
+    MF_CK(cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, resolve(stream)));
+    return MF_OK;
+}
+
+void* mf_stream(int rank) {
+    if (rank < 0 || rank >= (int)g.ranks.size()) return nullptr;
+    return (void*)g.ranks[rank].stream;
+}
+
+int mf_step_state(int rank, int32_t** host, void** device) {
+    MF_REQUIRE(g.inited, MF_E_STATE, "mf_init not called");
+    MF_REQUIRE(rank >= 0 && rank < (int)g.ranks.size(), MF_E_INVALID, "rank %d out of range", rank);
+    if (host) *host = g.ranks[rank].h_step;
+    if (device) *device = g.ranks[rank].d_step;
+    return MF_OK;
+}
+
+int mf_timer_start(int rank) {
+    MF_REQUIRE(rank >= 0 && rank < (int)g.ranks.size(), MF_E_INVALID, "rank %d out of range", rank);
+    Rank& r = g.ranks[rank];
+    MF_CK(cudaSetDevice(r.device));
+    if (!r.ev_start) {
+        MF_CK(cudaEventCreate(&r.ev_start));
+        MF_CK(cudaEventCreate(&r.ev_stop));
+    }
+    MF_CK(cudaEventRecord(r.ev_start, r.stream));
+    return MF_OK;
+}
+
+int mf_timer_stop(int rank, float* ms) {
+    MF_REQUIRE(rank >= 0 && rank < (int)g.ranks.size() && ms, MF_E_INVALID, "bad arguments");
+    Rank& r = g.ranks[rank];
+    MF_REQUIRE(r.ev_start, MF_E_STATE, "mf_timer_start not called");
+    MF_CK(cudaSetDevice(r.device));
+    MF_CK(cudaEventRecord(r.ev_stop, r.stream));
+    MF_CK(cudaEventSynchronize(r.ev_stop));
+    MF_CK(cudaEventElapsedTime(ms, r.ev_start, r.ev_stop));
+    return MF_OK;
+}
+
+int mf_sync(int rank) {
+    MF_REQUIRE(rank >= 0 && rank < (int)g.ranks.size(), MF_E_INVALID, "rank %d out of range", rank);
+    MF_CK(cudaSetDevice(g.ranks[rank].device));
+    MF_CK(cudaStreamSynchronize(g.ranks[rank].stream));
+    return MF_OK;
+}
+
+int mf_begin_frame(int rank, int frame_id) { return mf_begin_frame_ex(rank, frame_id, 0); }
+
+int mf_begin_frame_ex(int rank, int frame_id, int flags) {
+    MF_REQUIRE(g.inited, MF_E_STATE, "mf_init not called");
+    MF_REQUIRE(rank >= 0 && rank < (int)g.ranks.size(), MF_E_INVALID, "rank %d out of range", rank);
+    Rank& r = g.ranks[rank];
+    MF_REQUIRE(r.recording < 0 && r.pending < 0, MF_E_STATE, "begin_frame while a frame is open");
+    MF_CK(cudaSetDevice(r.device));
+    r.pending = frame_id;
+    if (r.frames.count(frame_id)) return MF_FRAME_REPLAY;
+    // Capture: the step record upload is the first node of the graph, so every
+    // replay reads the host values current at launch time.
+    MF_CK(cudaStreamBeginCapture(r.stream, cudaStreamCaptureModeThreadLocal));
+    r.recording = frame_id;
+    cudaError_t e = (flags & MF_FRAME_NO_UPLOAD)
+                        ? cudaSuccess
+                        : cudaMemcpyAsync(r.d_step, r.h_step, 16, cudaMemcpyHostToDevice, r.stream);
+    if (e != cudaSuccess) {
+        cudaGraph_t gr = nullptr;
+        cudaStreamEndCapture(r.stream, &gr);
+        if (gr) cudaGraphDestroy(gr);
+        r.recording = -1;
+        r.pending = -1;
+        return fail(MF_E_CUDA, "step upload during capture: %s", cudaGetErrorString(e));
+    }
+    return MF_FRAME_RECORD;
+}
+
+static int end_frame_impl(int rank, bool wait) {
+    MF_REQUIRE(rank >= 0 && rank < (int)g.ranks.size(), MF_E_INVALID, "rank %d out of range", rank);
+    Rank& r = g.ranks[rank];
+    MF_REQUIRE(r.pending >= 0, MF_E_STATE, "end_frame without begin_frame");
+    MF_CK(cudaSetDevice(r.device));
+    const int id = r.pending;
+    r.pending = -1;
+    if (r.recording >= 0) {
+        r.recording = -1;
+        cudaGraph_t gr = nullptr;
+        MF_CK(cudaStreamEndCapture(r.stream, &gr));
+        cudaGraphExec_t ex = nullptr;
+        cudaError_t e = cudaGraphInstantiate(&ex, gr, 0);
+        cudaGraphDestroy(gr);
+        if (e != cudaSuccess) return fail(MF_E_CUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(e));
+        r.frames[id] = ex;
+    }
+    MF_CK(cudaGraphLaunch(r.frames[id], r.stream));
+    if (wait) MF_CK(cudaStreamSynchronize(r.stream));
+    return MF_OK;
+}
+
+int mf_end_frame(int rank) { return end_frame_impl(rank, true); }
+
+int mf_abort_frame(int rank) {
+    MF_REQUIRE(rank >= 0 && rank < (int)g.ranks.size(), MF_E_INVALID, "rank %d out of range", rank);
+    Rank& r = g.ranks[rank];
+    MF_CK(cudaSetDevice(r.device));
+    if (r.recording >= 0) {
+        cudaGraph_t gr = nullptr;
+        cudaStreamEndCapture(r.stream, &gr);
+        if (gr) cudaGraphDestroy(gr);
+        cudaGetLastError();
+    }
+    r.recording = -1;
+    r.pending = -1;
+    return MF_OK;
+}
+int mf_end_frame_async(int rank) { return end_frame_impl(rank, false); }
+
+int mf_reset_frames(int rank) {
+    MF_REQUIRE(rank >= 0 && rank < (int)g.ranks.size(), MF_E_INVALID, "rank %d out of range", rank);
+    Rank& r = g.ranks[rank];
+    MF_CK(cudaSetDevice(r.device));
+    MF_CK(cudaStreamSynchronize(r.stream));
+    for (auto& kv : r.frames) cudaGraphExecDestroy(kv.second);
+    r.frames.clear();
+    return MF_OK;
+}
+
+// ===================================================================== token-loop ops
+
+int mf_rope_table(float* out, int n_pos, int d_rot, float base) {
+    MF_REQUIRE(out && n_pos > 0 && d_rot > 0 && d_rot % 2 == 0, MF_E_INVALID, "bad rope arguments");
+    const int half = d_rot / 2;
+    std::vector<float> freq(half);
+    // src/ops/kernels.cpp:72-73 with the float overloads of pow/cos/sin
+    for (int i = 0; i < half; ++i) freq[i] = 1.0f / powf(base, 2.0f * i / d_rot);
+    for (int p = 0; p < n_pos; ++p) {
+        for (int i = 0; i < half; ++i) {
+            const float angle = p * freq[i];
+            out[((size_t)p * half + i) * 2 + 0] = cosf(angle);
+            out[((size_t)p * half + i) * 2 + 1] = sinf(angle);
+        }
+    }
+    return MF_OK;
+}
+
+int mf_embed_step(float* x, const void* emb, int dtype, int vocab, int d_model, const void* step_state,
+                  void* stream) {
+    MF_REQUIRE(x && emb && step_state, MF_E_INVALID, "null argument");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    MF_REQUIRE(d_model > 0 && vocab > 0, MF_E_INVALID, "bad sizes");
+    const void* fn = dtype == MF_F32   ? (const void*)&mf::embed_kernel<mf::W_F32>
+                     : dtype == MF_F16 ? (const void*)&mf::embed_kernel<mf::W_F16>
+                                       : (const void*)&mf::embed_kernel<mf::W_BF16>;
+    const mf::StepState* st = (const mf::StepState*)step_state;
+    void* args[] = {&x, (void*)&emb, &d_model, &vocab, (void*)&st};
+    const int blocks = (d_model + 1023) / 1024;
+    MF_CK(launch(fn, dim3(blocks), dim3(256), 0, resolve(stream), args));
+    return MF_OK;
+}
+
+int mf_rmsnorm_matmul(float* y, const float* x, const float* norm_w, float eps, const void* w, int dtype, int d_out,
+                      int d_in, void* stream) {
+    MF_REQUIRE(y && x && norm_w && w, MF_E_INVALID, "null argument");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    mf::GemvParams p = {};
+    p.w = w;
+    p.x = x;
+    p.nw = norm_w;
+    p.eps = eps;
+    p.y = y;
+    p.rows = d_out;
+    p.K = d_in;
+    return run_gemv(dtype, mf::X_NORM, mf::Y_STORE, p, d_out, resolve(stream));
+}
+
+int mf_matmul_residual(float* x, const float* a, const void* w, int dtype, int d_out, int d_in, void* stream) {
+    MF_REQUIRE(x && a && w, MF_E_INVALID, "null argument");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    mf::GemvParams p = {};
+    p.w = w;
+    p.x = a;
+    p.y = x;
+    p.rows = d_out;
+    p.K = d_in;
+    return run_gemv(dtype, mf::X_PLAIN, mf::Y_RESID, p, d_out, resolve(stream));
+}
+
+int mf_swiglu_matmul(float* h, const float* x, const float* norm_w, float eps, const void* w_gate_up, int dtype,
+                     int d_ff, int d_in, void* stream) {
+    MF_REQUIRE(h && x && norm_w && w_gate_up, MF_E_INVALID, "null argument");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    mf::GemvParams p = {};
+    p.w = w_gate_up;
+    p.x = x;
+    p.nw = norm_w;
+    p.eps = eps;
+    p.y = h;
+    p.rows = 2 * d_ff;
+    p.K = d_in;
+    return run_gemv(dtype, mf::X_NORM, mf::Y_SWIGLU, p, d_ff, resolve(stream));
+}
+
+size_t mf_attn_workspace_bytes(int n_heads, int n_kv_heads, int d_head, int n_split) {
+    if (n_kv_heads <= 0 || n_heads <= 0 || n_split <= 0) return 0;
+    const size_t G = (size_t)n_heads / n_kv_heads;
+    const size_t po = (size_t)n_kv_heads * n_split * G * d_head * sizeof(float);
+    const size_t pml = (size_t)n_kv_heads * n_split * G * 2 * sizeof(float);
+    const size_t cnt = (size_t)n_kv_heads * sizeof(int);
+    return ((cnt + 255) / 256 * 256) + ((pml + 255) / 256 * 256) + po;
+}
+
+int mf_attn_default_split(int n_kv_heads, int max_seq) {
+    if (n_kv_heads <= 0) return 1;
+    int sms = num_sms();
+    int s = sms / n_kv_heads;
+    if (s < 1) s = 1;
+    const int max_useful = (max_seq + mf::ATT_TILE - 1) / mf::ATT_TILE;
+    if (s > max_useful) s = max_useful;
+    return s < 1 ? 1 : s;
+}
+
+int mf_attn_decode(const mf_attn_desc* d, void* stream) {
+    MF_REQUIRE(d, MF_E_INVALID, "null descriptor");
+    MF_REQUIRE(d->qkv && d->q_norm_w && d->k_norm_w && d->rope_table && d->k_cache && d->v_cache && d->step_state &&
+                   d->out && d->workspace,
+               MF_E_INVALID, "null pointer in attention descriptor");
+    MF_REQUIRE(d->d_head == mf::ATT_D, MF_E_UNSUPPORTED, "d_head %d (kernel is built for 128)", d->d_head);
+    MF_REQUIRE(d->n_kv_heads > 0 && d->n_heads % d->n_kv_heads == 0, MF_E_INVALID, "n_heads %% n_kv_heads != 0");
+    MF_REQUIRE(d->n_split >= 1 && d->max_seq >= 1, MF_E_INVALID, "bad n_split/max_seq");
+    const int G = d->n_heads / d->n_kv_heads;
+    const void* fn = mf::attn_kernel_ptr(G);
+    MF_REQUIRE(fn, MF_E_UNSUPPORTED, "%d query heads per KV head has no kernel", G);
+    const size_t smem = mf::attn_smem_bytes();
+    int bps = 0;
+    int rc = prepare(fn, mf::ATT_WARPS * 32, smem, &bps);
+    if (rc) return rc;
+    char* ws = (char*)d->workspace;
+    const size_t cnt = ((size_t)d->n_kv_heads * sizeof(int) + 255) / 256 * 256;
+    const size_t pml = ((size_t)d->n_kv_heads * d->n_split * G * 2 * sizeof(float) + 255) / 256 * 256;
+    mf::AttnParams p = {};
+    p.qkv = d->qkv;
+    p.q_norm_w = d->q_norm_w;
+    p.k_norm_w = d->k_norm_w;
+    p.eps = d->eps;
+    p.rope = (const float2*)d->rope_table;
+    p.k_cache = d->k_cache;
+    p.v_cache = d->v_cache;
+    p.max_seq = d->max_seq;
+    p.pos_ptr = &((const mf::StepState*)d->step_state)->pos;
+    p.out = d->out;
+    p.counters = (int*)ws;
+    p.part_ml = (float*)(ws + cnt);
+    p.part_o = (float*)(ws + cnt + pml);
+    p.n_heads = d->n_heads;
+    p.n_kv_heads = d->n_kv_heads;
+    p.n_split = d->n_split;
+    void* args[] = {&p};
+    MF_CK(launch(fn, dim3(d->n_split, d->n_kv_heads), dim3(mf::ATT_WARPS * 32), smem, resolve(stream), args));
+    return MF_OK;
+}
+
+int mf_router_topk(int* ids, float* weights, float* scores, const float* x, const float* norm_w, float eps,
+                   const float* w_router, int d_model, int n_experts, int k, void* stream) {
+    MF_REQUIRE(ids && weights && scores && x && norm_w && w_router, MF_E_INVALID, "null argument");
+    MF_REQUIRE(n_experts >= 1 && n_experts <= 256, MF_E_UNSUPPORTED, "n_experts %d (1..256)", n_experts);
+    MF_REQUIRE(k >= 1 && k <= n_experts && k <= 32, MF_E_INVALID, "k %d", k);
+    cudaStream_t st = resolve(stream);
+    mf::GemvParams p = {};
+    p.w = w_router;
+    p.x = x;
+    p.nw = norm_w;
+    p.eps = eps;
+    p.y = scores;
+    p.rows = n_experts;
+    p.K = d_model;
+    int rc = run_gemv(MF_F32, mf::X_NORM, mf::Y_STORE, p, n_experts, st);
+    if (rc) return rc;
+    void* args[] = {(void*)&scores, &n_experts, &k, &ids, &weights};
+    MF_CK(launch((const void*)&mf::topk_softmax_kernel, dim3(1), dim3(32), 0, st, args));
+    return MF_OK;
+}
+
+int mf_moe_swiglu(float* h, const float* x, const float* norm_w, float eps, const void* w_gate_up_exps, int dtype,
+                  const int* ids, int k, int d_ff, int d_in, void* stream) {
+    MF_REQUIRE(h && x && norm_w && w_gate_up_exps && ids, MF_E_INVALID, "null argument");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    MF_REQUIRE(k >= 1 && d_ff > 0, MF_E_INVALID, "bad k/d_ff");
+    mf::GemvParams p = {};
+    p.w = w_gate_up_exps;
+    p.x = x;
+    p.nw = norm_w;
+    p.eps = eps;
+    p.y = h;
+    p.rows = 2 * d_ff * k;
+    p.K = d_in;
+    p.expert_ids = ids;
+    p.rows_per_expert = 2 * d_ff;
+    return run_gemv(dtype, mf::X_NORM, mf::Y_SWIGLU, p, (long long)d_ff * k, resolve(stream));
+}
+
+int mf_moe_down_residual(float* x, const float* h, const void* w_down_exps, int dtype, const int* ids,
+                         const float* weights, int k, int d_model, int d_ff, void* stream) {
+    MF_REQUIRE(x && h && w_down_exps && ids && weights, MF_E_INVALID, "null argument");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    MF_REQUIRE(k >= 1 && k <= 8, MF_E_UNSUPPORTED, "k %d (grouped down projection supports 1..8)", k);
+    mf::GemvParams p = {};
+    p.w = w_down_exps;
+    p.x = h;
+    p.y = x;
+    p.rows = d_model;
+    p.K = d_ff;
+    p.expert_ids = ids;
+    p.expert_w = weights;
+    p.rows_per_expert = d_model;
+    p.n_slots = k;
+    return run_gemv(dtype, mf::X_PLAIN, mf::Y_MOE_DOWN, p, d_model, resolve(stream));
+}
+
+size_t mf_lm_head_workspace_bytes(void) { return 256 + (size_t)LMH_MAX_GRID * (sizeof(float) + sizeof(int)); }
+
+int mf_lm_head(float* logits, const float* x, const float* norm_w, float eps, const void* w, int dtype, int vocab,
+               int d_model, int vocab_offset, void* step_state, void* workspace, void* stream) {
+    MF_REQUIRE(logits && x && norm_w && w, MF_E_INVALID, "null argument");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    MF_REQUIRE(!step_state || workspace, MF_E_INVALID, "argmax needs a workspace");
+    mf::GemvParams p = {};
+    p.w = w;
+    p.x = x;
+    p.nw = norm_w;
+    p.eps = eps;
+    p.y = logits;
+    p.rows = vocab;
+    p.K = d_model;
+    p.vocab_offset = vocab_offset;
+    if (step_state) {
+        char* ws = (char*)workspace;
+        p.counter = (int*)ws;
+        p.best_val = (float*)(ws + 256);
+        p.best_idx = (int*)(ws + 256 + (size_t)LMH_MAX_GRID * sizeof(float));
+        p.step = (int*)step_state;
+    }
+    return run_gemv(dtype, mf::X_NORM, mf::Y_STORE, p, vocab, resolve(stream), LMH_MAX_GRID);
+}
+
+// ===================================================================== single ops
+
+int mf_matmul(float* y, const float* x, const void* w, int dtype, size_t offset, int d_out, int d_in, void* stream) {
+    MF_REQUIRE(y && x && w, MF_E_INVALID, "null argument");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    mf::GemvParams p = {};
+    p.w = w;
+    p.w_offset = offset;
+    p.x = x;
+    p.y = y;
+    p.rows = d_out;
+    p.K = d_in;
+    return run_gemv(dtype, mf::X_PLAIN, mf::Y_STORE, p, d_out, resolve(stream));
+}
+
+int mf_rmsnorm(float* out, const float* x, const float* w, int dim, float eps, int n_rows, void* stream) {
+    MF_REQUIRE(out && x && w && dim > 0 && n_rows > 0, MF_E_INVALID, "bad arguments");
+    mf::rmsnorm_rows_kernel<<<n_rows, 256, 0, resolve(stream)>>>(out, x, w, dim, eps);
+    MF_CK(cudaGetLastError());
+    return MF_OK;
+}
+
+int mf_softmax(float* out, const float* x, int n, int n_rows, void* stream) {
+    MF_REQUIRE(out && x && n > 0 && n_rows > 0, MF_E_INVALID, "bad arguments");
+    mf::softmax_rows_kernel<<<n_rows, 256, 0, resolve(stream)>>>(out, x, n);
+    MF_CK(cudaGetLastError());
+    return MF_OK;
+}
+
+int mf_silu(float* out, const float* x, int n, void* stream) {
+    MF_REQUIRE(out && x && n > 0, MF_E_INVALID, "bad arguments");
+    mf::silu_kernel<<<(n + 255) / 256, 256, 0, resolve(stream)>>>(out, x, n);
+    MF_CK(cudaGetLastError());
+    return MF_OK;
+}
+
+static int rope_impl(float* out, const float* x, int head, int d_head, int d_rot, float base, int pos, int neox,
+                     void* stream) {
+    MF_REQUIRE(out && x && head >= 0 && d_head > 0 && d_rot > 0 && d_rot <= d_head, MF_E_INVALID, "bad arguments");
+    mf::rope_head_kernel<<<1, 128, 0, resolve(stream)>>>(out, x, head, d_head, d_rot, base, pos, neox);
+    MF_CK(cudaGetLastError());
+    return MF_OK;
+}
+
+int mf_neox_rope(float* out, const float* x, int head, int d_head, int d_rot, float base, int pos, void* stream) {
+    return rope_impl(out, x, head, d_head, d_rot, base, pos, 1, stream);
+}
+
+int mf_il_rope(float* out, const float* x, int head, int d_head, int d_rot, float base, int pos, void* stream) {
+    return rope_impl(out, x, head, d_head, d_rot, base, pos, 0, stream);
+}
+
+int mf_attn(float* scores, float* out, const float* q, const float* k, const float* v, int seq_len, int d_head,
+            int kv_dim, void* stream) {
+    MF_REQUIRE(scores && out && q && k && v && seq_len > 0 && d_head > 0 && kv_dim >= d_head, MF_E_INVALID,
+               "bad arguments");
+    mf::attn_head_kernel<<<1, 256, 0, resolve(stream)>>>(scores, out, q, k, v, seq_len, d_head, kv_dim);
+    MF_CK(cudaGetLastError());
+    return MF_OK;
+}
+
+int mf_route(const float* x, int* ids, float* weights, float* scores, const float* w_router, int d_model,
+             int n_experts, int k, void* stream) {
+    MF_REQUIRE(x && ids && weights && scores && w_router, MF_E_INVALID, "null argument");
+    MF_REQUIRE(n_experts >= 1 && n_experts <= 256, MF_E_UNSUPPORTED, "n_experts %d (1..256)", n_experts);
+    MF_REQUIRE(k >= 1 && k <= n_experts && k <= 32, MF_E_INVALID, "k %d", k);
+    cudaStream_t st = resolve(stream);
+    int rc = mf_matmul(scores, x, w_router, MF_F32, 0, n_experts, d_model, st);
+    if (rc) return rc;
+    void* args[] = {(void*)&scores, &n_experts, &k, &ids, &weights};
+    MF_CK(launch((const void*)&mf::topk_softmax_kernel, dim3(1), dim3(32), 0, st, args));
+    return MF_OK;
+}
+
+int mf_embed(float* x, const void* w, int dtype, uint32_t token, int d_model, void* stream) {
+    MF_REQUIRE(x && w && d_model > 0, MF_E_INVALID, "bad arguments");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    cudaStream_t st = resolve(stream);
+    const int blocks = (d_model + 255) / 256;
+    if (dtype == MF_F32) mf::embed_row_kernel<mf::W_F32><<<blocks, 256, 0, st>>>(x, w, token, d_model);
+    else if (dtype == MF_F16) mf::embed_row_kernel<mf::W_F16><<<blocks, 256, 0, st>>>(x, w, token, d_model);
+    else mf::embed_row_kernel<mf::W_BF16><<<blocks, 256, 0, st>>>(x, w, token, d_model);
+    MF_CK(cudaGetLastError());
+    return MF_OK;
+}
+
+int mf_argmax(const float* logits, int n, int* out, void* stream) {
+    MF_REQUIRE(logits && out && n > 0, MF_E_INVALID, "bad arguments");
+    mf::argmax_kernel<<<1, 1024, 0, resolve(stream)>>>(logits, n, out);
+    MF_CK(cudaGetLastError());
+    return MF_OK;
+}
+
+}  // extern "C"

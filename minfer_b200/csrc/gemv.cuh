@@ -1,0 +1,327 @@
+// Decode GEMV family: y = W x for one fp32 activation vector, W streamed from
+// HBM once per token.
+//
+// What it computes follows the reference's matmul_{fp32,fp16,bf16}
+// (src/ops/kernels.cpp:211-343): weights widened to fp32, fp32 FMAs, fp32
+// result per row. The summation order differs (the reference keeps 16 NEON
+// lanes per row; here a CTA splits each row over its threads), so results
+// agree to fp32 rounding, not bitwise.
+//
+// Structure (B200):
+//  * A CTA owns a contiguous, balanced range of "units" (rows, gate/up row
+//    pairs, or output rows of a grouped expert product), so per-SM bytes are
+//    equal to within one unit.
+//  * All T threads of a CTA span the K axis: thread t reads 16-byte vectors at
+//    columns (pass*T + t)*VEC. A tile of R rows is read PC passes at a time,
+//    so every thread keeps R*PC = 8 independent 16-byte loads in flight, and
+//    the next step's loads are issued before the current step is reduced
+//    (two register buffers).
+//  * The activation vector lives in shared memory (optionally RMS-normalised
+//    in the prologue, which fuses the reference's separate rmsnorm pass).
+//  * Programmatic dependent launch: dense weight loads are issued before
+//    griddepcontrol.wait, so they overlap the previous kernel's tail.
+//    Everything written by earlier kernels is read through L2 (ld.cg).
+#pragma once
+
+#include "mf_common.cuh"
+
+namespace mf {
+
+enum XMode { X_PLAIN = 0, X_NORM = 1 };
+enum YMode { Y_STORE = 0, Y_RESID = 1, Y_SWIGLU = 2, Y_MOE_DOWN = 3 };
+
+struct GemvParams {
+    const void* w;        // weight rows, dtype given by the template
+    size_t w_offset;      // element offset added to w (reference `offset` argument)
+    const float* x;       // activation vector(s)
+    const float* nw;      // RMSNorm weight for X_NORM
+    float eps;
+    float* y;             // output
+    int rows;             // logical rows (Y_MOE_DOWN: output rows)
+    int K;                // row length (elements)
+    // expert indirection (Y_SWIGLU over experts, Y_MOE_DOWN)
+    const int* expert_ids;      // [k] device, or null for dense weights
+    const float* expert_w;      // [k] device (Y_MOE_DOWN)
+    int rows_per_expert;        // physical rows per expert matrix
+    int n_slots;                // k for Y_MOE_DOWN
+    // greedy argmax finisher (Y_STORE only; counter may be null)
+    float* best_val;            // [gridDim.x]
+    int* best_idx;              // [gridDim.x]
+    int* counter;               // zero-initialised; reset by the last CTA
+    int* step;                  // device step record {token, pos, next_token, chain}
+    int vocab_offset;           // index of row 0 (vocab-split lm_head)
+};
+
+template <typename W, int T, int R, int PC, int XM, int YM>
+__global__ void __launch_bounds__(T) gemv_kernel(const GemvParams p) {
+    constexpr int VEC = W::VEC;
+    constexpr int NW = T / 32;
+    constexpr int RU = (YM == Y_SWIGLU) ? 2 : 1;  // rows per unit
+    static_assert(R * PC == 8, "8 loads in flight per thread");
+    static_assert(YM != Y_SWIGLU || R % 2 == 0, "gate/up pairs");
+    static_assert(R <= 32, "tile rows fit one warp");
+    extern __shared__ float4 smem_f4[];
+    float* xs = reinterpret_cast<float*>(smem_f4);
+    __shared__ float red[2][NW][R];
+    __shared__ float scratch[32];
+    __shared__ int scratch_i[32];
+    __shared__ float cta_best_v;
+    __shared__ int cta_best_i;
+    __shared__ int is_last;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = p.K;
+    constexpr size_t esz = sizeof(typename W::T);
+    const char* wbase = reinterpret_cast<const char*>(p.w) + p.w_offset * esz;
+    const size_t row_bytes = (size_t)K * esz;
+
+    // ---- unit range of this CTA
+    const long long units = (YM == Y_MOE_DOWN) ? p.rows : p.rows / RU;
+    const long long u0 = (long long)blockIdx.x * units / gridDim.x;
+    const long long u1 = (long long)(blockIdx.x + 1) * units / gridDim.x;
+    const int rows0 = (int)(u0 * RU), rows1 = (int)(u1 * RU);
+    // Y_MOE_DOWN: one output row per tile, tile row r = expert slot r.
+    const int ntiles = (YM == Y_MOE_DOWN) ? (rows1 - rows0) : (rows1 - rows0 + R - 1) / R;
+    constexpr int STEP_COLS = PC * T * VEC;
+    const int nsteps = (K + STEP_COLS - 1) / STEP_COLS;
+    const int nitems = ntiles * nsteps;
+    const bool indirect = (YM == Y_MOE_DOWN) || (p.expert_ids != nullptr);
+
+    int eid[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) eid[r] = 0;
+
+    auto load = [&](uint4 (&buf)[R][PC], int it) {
+        const int tile = it / nsteps, step = it - tile * nsteps;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            bool valid;
+            long long phys;
+            if (YM == Y_MOE_DOWN) {
+                const int j = rows0 + tile;
+                valid = r < p.n_slots;
+                phys = (long long)eid[r] * p.rows_per_expert + j;
+            } else {
+                const int lr = rows0 + tile * R + r;
+                valid = lr < rows1;
+                phys = lr;
+                if (indirect) {
+                    const int slot = lr / p.rows_per_expert;
+                    phys = (long long)__ldcg(p.expert_ids + slot) * p.rows_per_expert +
+                           (lr - slot * p.rows_per_expert);
+                }
+            }
+            const char* rp = wbase + phys * row_bytes;
+#pragma unroll
+            for (int c = 0; c < PC; ++c) {
+                const int col = ((step * PC + c) * T + tid) * VEC;
+                if (valid && col < K) buf[r][c] = ld_stream(rp + (size_t)col * esz);
+                else buf[r][c] = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+    };
+
+    uint4 bufA[R][PC], bufB[R][PC];
+    // Dense weights do not depend on earlier kernels: start streaming them
+    // before the dependency wait. Expert ids come from the router kernel.
+    if (!indirect && nitems > 0) load(bufA, 0);
+    pdl_launch_dependents();
+    pdl_wait();
+    if (YM == Y_MOE_DOWN) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) eid[r] = (r < p.n_slots) ? __ldcg(p.expert_ids + r) : 0;
+    }
+    if (indirect && nitems > 0) load(bufA, 0);
+
+    // ---- prologue: activation vector(s) -> shared memory
+    if (XM == X_NORM) {
+        float ss = 0.f;
+        for (int i = tid; i < K; i += T) {
+            const float v = __ldcg(p.x + i);
+            ss = fmaf(v, v, ss);
+        }
+        ss = block_sum(ss, scratch);
+        // src/ops/kernels.cpp:355-363: rms = sqrtf(ss/dim + eps); inv = 1/rms; out = inv*x*w
+        const float inv = 1.0f / sqrtf(ss / (float)K + p.eps);
+        for (int i = tid; i < K; i += T) xs[i] = (inv * __ldcg(p.x + i)) * __ldg(p.nw + i);
+    } else {
+        const int xlen = (YM == Y_MOE_DOWN) ? K * p.n_slots : K;
+        for (int i = tid * 4; i < xlen; i += T * 4) {
+            *reinterpret_cast<float4*>(xs + i) = __ldcg(reinterpret_cast<const float4*>(p.x + i));
+        }
+    }
+    if (tid == 0) {
+        cta_best_v = -INFINITY;
+        cta_best_i = 0x7fffffff;
+    }
+    __syncthreads();
+
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.f;
+    int par = 0;
+
+    auto consume = [&](const uint4 (&buf)[R][PC], int it) {
+        const int tile = it / nsteps, step = it - tile * nsteps;
+#pragma unroll
+        for (int c = 0; c < PC; ++c) {
+            const int col = ((step * PC + c) * T + tid) * VEC;
+            if (col < K) {
+                if (YM == Y_MOE_DOWN) {
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        if (r >= p.n_slots) break;  // xs holds n_slots vectors only
+                        float wv[VEC];
+                        unpack16<W>(buf[r][c], wv);
+                        const float* xr = xs + r * K + col;
+#pragma unroll
+                        for (int e = 0; e < VEC; e += 4) {
+                            const float4 t4 = *reinterpret_cast<const float4*>(xr + e);
+                            acc[r] = fmaf(t4.x, wv[e], acc[r]);
+                            acc[r] = fmaf(t4.y, wv[e + 1], acc[r]);
+                            acc[r] = fmaf(t4.z, wv[e + 2], acc[r]);
+                            acc[r] = fmaf(t4.w, wv[e + 3], acc[r]);
+                        }
+                    }
+                } else {
+                    float xv[VEC];
+#pragma unroll
+                    for (int e = 0; e < VEC; e += 4) {
+                        const float4 t4 = *reinterpret_cast<const float4*>(xs + col + e);
+                        xv[e] = t4.x; xv[e + 1] = t4.y; xv[e + 2] = t4.z; xv[e + 3] = t4.w;
+                    }
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        float wv[VEC];
+                        unpack16<W>(buf[r][c], wv);
+#pragma unroll
+                        for (int e = 0; e < VEC; ++e) acc[r] = fmaf(xv[e], wv[e], acc[r]);
+                    }
+                }
+            }
+        }
+        if (step != nsteps - 1) return;
+        // ---- tile complete: CTA-wide reduction in a fixed order
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const float v = warp_sum(acc[r]);
+            if (lane == 0) red[par][warp][r] = v;
+            acc[r] = 0.f;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            if (YM == Y_MOE_DOWN) {
+                if (lane == 0) {
+                    const int j = rows0 + tile;
+                    // src/models/qwen3/module.cpp:471-474: x += expert_out * weight, one expert at a time
+                    float xo = __ldcg(p.y + j);
+                    for (int r = 0; r < p.n_slots; ++r) {
+                        float s = 0.f;
+                        for (int w2 = 0; w2 < NW; ++w2) s += red[par][w2][r];
+                        xo = fmaf(s, __ldcg(p.expert_w + r), xo);
+                    }
+                    p.y[j] = xo;
+                }
+            } else if (YM == Y_SWIGLU) {
+                const int lr = rows0 + tile * R + 2 * lane;
+                if (lane < R / 2 && lr < rows1) {
+                    float g = 0.f, u = 0.f;
+                    for (int w2 = 0; w2 < NW; ++w2) {
+                        g += red[par][w2][2 * lane];
+                        u += red[par][w2][2 * lane + 1];
+                    }
+                    // src/models/qwen3/module.cpp:466-468: h = silu(g) * u
+                    p.y[lr / 2] = silu(g) * u;
+                }
+            } else {
+                const int lr = rows0 + tile * R + lane;
+                const bool valid = lane < R && lr < rows1;
+                float s = 0.f;
+                if (valid) {
+                    for (int w2 = 0; w2 < NW; ++w2) s += red[par][w2][lane];
+                    if (YM == Y_RESID) {
+                        p.y[lr] = __ldcg(p.y + lr) + s;  // src/models/qwen3/module.cpp:238-240
+                    } else {
+                        p.y[lr] = s;
+                    }
+                }
+                if (YM == Y_STORE && p.counter != nullptr) {
+                    float bv = valid ? s : -INFINITY;
+                    int bi = valid ? p.vocab_offset + lr : 0x7fffffff;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                        if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+                    }
+                    if (lane == 0 && better(bv, bi, cta_best_v, cta_best_i)) {
+                        cta_best_v = bv;
+                        cta_best_i = bi;
+                    }
+                }
+            }
+        }
+        par ^= 1;
+    };
+
+    for (int it = 0; it < nitems; it += 2) {
+        if (it + 1 < nitems) load(bufB, it + 1);
+        consume(bufA, it);
+        if (it + 1 >= nitems) break;
+        if (it + 2 < nitems) load(bufA, it + 2);
+        consume(bufB, it + 1);
+    }
+
+    // ---- greedy argmax finisher: the last CTA reduces the per-CTA candidates
+    if (YM == Y_STORE && p.counter != nullptr) {
+        __syncthreads();
+        if (tid == 0) {
+            p.best_val[blockIdx.x] = cta_best_v;
+            p.best_idx[blockIdx.x] = cta_best_i;
+            __threadfence();
+            const int ticket = atomicAdd(p.counter, 1);
+            is_last = (ticket == (int)gridDim.x - 1);
+        }
+        __syncthreads();
+        if (is_last) {
+            __threadfence();
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+            for (int b = tid; b < (int)gridDim.x; b += T) {
+                const float v = __ldcg(p.best_val + b);
+                const int i = __ldcg(p.best_idx + b);
+                if (better(v, i, bv, bi)) { bv = v; bi = i; }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+            }
+            if (lane == 0) {
+                scratch[warp] = bv;
+                scratch_i[warp] = bi;
+            }
+            __syncthreads();
+            if (tid == 0) {
+                float fv = scratch[0];
+                int fi = scratch_i[0];
+                for (int w2 = 1; w2 < NW; ++w2) {
+                    if (better(scratch[w2], scratch_i[w2], fv, fi)) { fv = scratch[w2]; fi = scratch_i[w2]; }
+                }
+                // no candidate (every logit NaN): std::max_element returns the first element
+                if (fi == 0x7fffffff) fi = p.vocab_offset;
+                // greedy id -> next_token; a chained record also becomes the
+                // next step's input so decode can continue without the host
+                p.step[2] = fi;
+                if (p.step[3] != 0) {
+                    p.step[0] = fi;
+                    p.step[1] = p.step[1] + 1;
+                }
+                *p.counter = 0;
+            }
+        }
+    }
+}
+
+}  // namespace mf

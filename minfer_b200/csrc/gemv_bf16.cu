@@ -1,0 +1,6 @@
+// GEMV kernel instantiations for BF16 weights.
+#include "gemv_inst.cuh"
+
+namespace mf {
+const void* gemv_kernel_ptr_bf16(int xm, int ym, int T, int R) { return gemv_kernel_ptr<W_BF16>(xm, ym, T, R); }
+}  // namespace mf

@@ -1,0 +1,201 @@
+// extern "C" surface of the host runtime (include/minfer_model.h).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <random>
+#include <stdexcept>
+
+#include "minfer_model.h"
+#include "model.hpp"
+
+struct mf_model {
+    std::unique_ptr<minfer::Qwen3Model> m;
+};
+
+namespace {
+thread_local char g_host_err[512] = "";
+int herr(int code, const char* msg) {
+    std::snprintf(g_host_err, sizeof(g_host_err), "%s", msg);
+    return code;
+}
+}  // namespace
+
+#define MF_TRY(body)                                   \
+    try {                                              \
+        body;                                          \
+    } catch (const std::bad_alloc&) {                  \
+        return herr(MF_E_OOM, "host allocation failed"); \
+    } catch (const std::invalid_argument& e) {         \
+        return herr(MF_E_INVALID, e.what());           \
+    } catch (const std::exception& e) {                \
+        return herr(MF_E_STATE, e.what());             \
+    }
+
+extern "C" {
+
+// Host-runtime failures are reported through this function; libmfcuda's own
+// message is used when the host layer has none.
+int mf_host_last_error(char* buf, size_t n) {
+    if (!buf || n == 0) return MF_E_INVALID;
+    if (g_host_err[0]) {
+        std::snprintf(buf, n, "%s", g_host_err);
+        return MF_OK;
+    }
+    return mf_last_error(buf, n);
+}
+
+int mf_model_load(const char* gguf_path, const mf_run_params* rp, int rank, mf_model** out) {
+    if (!gguf_path || !rp || !out) return herr(MF_E_INVALID, "null argument");
+    g_host_err[0] = 0;
+    minfer::RunParams p;
+    p.num_iters = rp->num_iters;
+    p.max_seq_len = rp->max_seq_len;
+    p.top_k = rp->top_k;
+    p.temp = rp->temp;
+    p.top_p = rp->top_p;
+    p.min_p = rp->min_p;
+    p.penalty_pres = rp->penalty_pres;
+    p.seed = rp->seed;
+    MF_TRY({
+        auto* h = new mf_model;
+        try {
+            h->m = std::make_unique<minfer::Qwen3Model>(gguf_path, p, rank);
+        } catch (...) {
+            delete h;
+            throw;
+        }
+        *out = h;
+    });
+    return MF_OK;
+}
+
+int mf_model_to_cuda(mf_model* m) {
+    if (!m) return herr(MF_E_INVALID, "null model");
+    g_host_err[0] = 0;
+    MF_TRY(m->m->set_device(minfer::DeviceType::CUDA));
+    return MF_OK;
+}
+
+int mf_model_info_get(const mf_model* m, mf_model_info* out) {
+    if (!m || !out) return herr(MF_E_INVALID, "null argument");
+    const minfer::Config& c = m->m->config();
+    std::memset(out, 0, sizeof(*out));
+    out->vocab_size = c.vocab_size;
+    out->max_seq_len = c.user_max_seq_len;
+    out->d_model = c.d_model;
+    out->n_layers = c.n_layers;
+    out->n_heads = c.n_heads;
+    out->n_kv_heads = c.n_kv_heads;
+    out->d_head = c.d_head;
+    out->d_ff = c.d_ff;
+    out->n_experts = c.n_experts;
+    out->n_active_experts = c.n_active_experts;
+    out->weight_dtype = (int)c.weight_dtype;
+    out->untied_head = c.untied_head ? 1 : 0;
+    out->eos_token_id = c.eos_token_id;
+    out->rms_norm_eps = c.rms_norm_eps;
+    out->freq_base = c.freq_base;
+    if (m->m->device() == minfer::DeviceType::CUDA) {
+        out->read_bytes_logits = m->m->read_bytes(true);
+        out->read_bytes_no_logits = m->m->read_bytes(false);
+    }
+    out->kv_bytes_per_pos = 2ull * c.n_layers * c.n_kv_heads * c.d_head * sizeof(float);
+    return MF_OK;
+}
+
+void mf_model_free(mf_model* m) { delete m; }
+
+int mf_model_forward(mf_model* m, uint32_t token, int pos, int compute_logits, int host_logits) {
+    if (!m) return herr(MF_E_INVALID, "null model");
+    g_host_err[0] = 0;
+    MF_TRY(m->m->forward(token, pos, compute_logits != 0, host_logits != 0));
+    return MF_OK;
+}
+
+int mf_model_logits(const mf_model* m, float* out, size_t n) {
+    if (!m || !out) return herr(MF_E_INVALID, "null argument");
+    const size_t V = m->m->config().vocab_size;
+    if (n > V) return herr(MF_E_INVALID, "more logits requested than the vocabulary holds");
+    if (!m->m->host_logits()) return herr(MF_E_STATE, "model is not on CUDA");
+    std::memcpy(out, m->m->host_logits(), n * sizeof(float));
+    return MF_OK;
+}
+
+int mf_model_argmax(const mf_model* m, uint32_t* out) {
+    if (!m || !out) return herr(MF_E_INVALID, "null argument");
+    *out = m->m->device_argmax();
+    return MF_OK;
+}
+
+int mf_model_generate(mf_model* m, const uint32_t* prompt, size_t n_prompt, size_t n_gen, int flags,
+                      const uint32_t* forced, uint32_t* out_ids, size_t* n_out, float* margins,
+                      mf_gen_stats* stats) {
+    if (!m || !prompt || !out_ids || !n_out) return herr(MF_E_INVALID, "null argument");
+    g_host_err[0] = 0;
+    MF_TRY({
+        minfer::Qwen3Model::GenOptions o;
+        o.stop_at_eos = (flags & MF_GEN_STOP_AT_EOS) != 0;
+        o.trace = (flags & MF_GEN_MARGINS) != 0;
+        o.forced = forced;
+        std::vector<uint32_t> pr(prompt, prompt + n_prompt);
+        minfer::GenStats st;
+        std::vector<float> mg;
+        std::vector<uint32_t> ids = m->m->generate(pr, n_gen, o, &st, o.trace ? &mg : nullptr);
+        std::memcpy(out_ids, ids.data(), ids.size() * sizeof(uint32_t));
+        *n_out = ids.size();
+        if (margins && o.trace) std::memcpy(margins, mg.data(), mg.size() * sizeof(float));
+        if (stats) {
+            stats->num_tokens_gen = st.num_tokens_gen;
+            stats->ttft = st.ttft;
+            stats->throughput = st.throughput;
+            stats->prefill_time = st.prefill_time;
+            stats->bandwidth = st.bandwidth;
+            stats->decode_seconds = st.decode_seconds;
+            stats->bytes_read = st.bytes_read;
+        }
+    });
+    return MF_OK;
+}
+
+int mf_model_decode_chained(mf_model* m, uint32_t token, int start_pos, int n, uint32_t* last_id) {
+    if (!m) return herr(MF_E_INVALID, "null model");
+    g_host_err[0] = 0;
+    MF_TRY({
+        const uint32_t id = m->m->decode_chained(token, start_pos, n);
+        if (last_id) *last_id = id;
+    });
+    return MF_OK;
+}
+
+int mf_model_reset_sampler(mf_model* m) {
+    if (!m) return herr(MF_E_INVALID, "null model");
+    MF_TRY(m->m->reset_sampler());
+    return MF_OK;
+}
+
+int mf_model_experts(const mf_model* m, int layer, int* ids, float* weights) {
+    if (!m || !ids) return herr(MF_E_INVALID, "null argument");
+    const int rc = m->m->read_experts(layer, ids, weights);
+    return rc ? herr(rc, "no experts at this layer") : MF_OK;
+}
+
+int mf_model_kv(const mf_model* m, int layer, float* k, float* v, int n_pos) {
+    if (!m) return herr(MF_E_INVALID, "null model");
+    const int rc = m->m->read_kv(layer, k, v, n_pos);
+    return rc ? herr(rc, "kv read failed") : MF_OK;
+}
+
+int mf_model_x(const mf_model* m, float* x) {
+    if (!m || !x) return herr(MF_E_INVALID, "null argument");
+    return m->m->read_x(x);
+}
+
+int mf_random_prompt(int seed, uint32_t vocab, size_t n, uint32_t* out) {
+    if (!out || vocab == 0) return herr(MF_E_INVALID, "bad arguments");
+    std::mt19937 gen(seed);
+    std::uniform_int_distribution<> distrib(0, (int)vocab - 1);
+    for (size_t i = 0; i < n; ++i) out[i] = (uint32_t)distrib(gen);
+    return MF_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,585 @@
+#include "model.hpp"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+
+namespace minfer {
+
+namespace {
+
+void check(int rc, const char* what) {
+    if (rc != MF_OK) {
+        char msg[512];
+        mf_last_error(msg, sizeof(msg));
+        throw std::runtime_error(std::string(what) + " failed (" + std::to_string(rc) + "): " + msg);
+    }
+}
+
+int mf_dtype(DataType t) {
+    switch (t) {
+        case DataType::F32: return MF_F32;
+        case DataType::F16: return MF_F16;
+        case DataType::BF16: return MF_BF16;
+        default: throw std::runtime_error("unsupported weight dtype");
+    }
+}
+
+mf_buf* upload_tensor(const TensorView& t, int rank) {
+    mf_buf* b = nullptr;
+    check(mf_upload(t.data, t.bytes, rank, &b), ("upload " + t.name).c_str());
+    return b;
+}
+
+void expect_shape(const TensorView& t, std::initializer_list<uint64_t> shape) {
+    std::vector<uint64_t> want(shape);
+    if (t.shape != want) {
+        std::string w, g;
+        for (auto v : want) w += std::to_string(v) + " ";
+        for (auto v : t.shape) g += std::to_string(v) + " ";
+        throw std::runtime_error("tensor " + t.name + " has shape [" + g + "], expected [" + w + "]");
+    }
+}
+
+void expect_f32(const TensorView& t) {
+    // norms and the router are fp32 (src/base/module.cpp:64,88-93,130-134)
+    if (t.dtype != DataType::F32) throw std::runtime_error("tensor " + t.name + " must be F32");
+}
+
+double now_s() {
+    using namespace std::chrono;
+    return duration_cast<duration<double>>(steady_clock::now().time_since_epoch()).count();
+}
+
+// ---------------------------------------------------------------- layers
+
+// Qwen3Embed (src/models/qwen3/module.cpp:13-44)
+class Qwen3Embed : public BaseLayer {
+public:
+    Qwen3Embed(const Config& c) : c_(c) {}
+    void upload(const GGUFFile& f, int rank) override {
+        const TensorView& t = f.tensor("token_embd.weight");
+        expect_shape(t, {c_.vocab_size, (uint64_t)c_.d_model});
+        dtype_ = mf_dtype(t.dtype);
+        w_ = upload_tensor(t, rank);
+        own(w_);
+        read_bytes_ = t.bytes / c_.vocab_size;  // one row (src/base/module.cpp:33)
+    }
+    void cuda_forward(RunState& rs) override {
+        check(mf_embed_step((float*)mf_ptr(rs.x), mf_ptr(w_), dtype_, (int)c_.vocab_size, c_.d_model, rs.d_step,
+                            rs.stream),
+              "embed");
+    }
+    mf_buf* weight() const { return w_; }
+    int dtype() const { return dtype_; }
+
+private:
+    const Config& c_;
+    mf_buf* w_ = nullptr;
+    int dtype_ = MF_F32;
+};
+
+// Qwen3GQA (src/models/qwen3/module.cpp:142-241)
+class Qwen3GQA : public BaseLayer {
+public:
+    Qwen3GQA(const Config& c, int layer) : c_(c), layer_(layer) {}
+    void upload(const GGUFFile& f, int rank) override {
+        const std::string p = "blk." + std::to_string(layer_) + ".";
+        const TensorView& wq = f.tensor(p + "attn_q.weight");
+        const TensorView& wk = f.tensor(p + "attn_k.weight");
+        const TensorView& wv = f.tensor(p + "attn_v.weight");
+        const TensorView& wo = f.tensor(p + "attn_output.weight");
+        const TensorView& qn = f.tensor(p + "attn_q_norm.weight");
+        const TensorView& kn = f.tensor(p + "attn_k_norm.weight");
+        const TensorView& an = f.tensor(p + "attn_norm.weight");
+        const uint64_t d = c_.d_model, q = (uint64_t)c_.n_heads * c_.d_head, kv = (uint64_t)c_.n_kv_heads * c_.d_head;
+        expect_shape(wq, {q, d});
+        expect_shape(wk, {kv, d});
+        expect_shape(wv, {kv, d});
+        expect_shape(wo, {d, q});
+        expect_shape(qn, {(uint64_t)c_.d_head});
+        expect_shape(kn, {(uint64_t)c_.d_head});
+        expect_shape(an, {d});
+        if (!(wq.dtype == wk.dtype && wk.dtype == wv.dtype && wv.dtype == wo.dtype))
+            throw std::runtime_error("Q/K/V/O weights of layer " + std::to_string(layer_) + " differ in dtype");
+        expect_f32(qn);
+        expect_f32(kn);
+        expect_f32(an);
+        dtype_ = mf_dtype(wq.dtype);
+        // fused [Wq; Wk; Wv] so one streaming pass computes q|k|v
+        check(mf_alloc(wq.bytes + wk.bytes + wv.bytes, rank, &wqkv_), "alloc qkv");
+        check(mf_write(wqkv_, 0, wq.data, wq.bytes), "upload q");
+        check(mf_write(wqkv_, wq.bytes, wk.data, wk.bytes), "upload k");
+        check(mf_write(wqkv_, wq.bytes + wk.bytes, wv.data, wv.bytes), "upload v");
+        own(wqkv_);
+        own(wo_ = upload_tensor(wo, rank));
+        own(qn_ = upload_tensor(qn, rank));
+        own(kn_ = upload_tensor(kn, rank));
+        own(an_ = upload_tensor(an, rank));
+        read_bytes_ = wq.bytes + wk.bytes + wv.bytes + wo.bytes + qn.bytes + kn.bytes + an.bytes;
+    }
+    void cuda_forward(RunState& rs) override {
+        const int d = c_.d_model, H = c_.n_heads, Hkv = c_.n_kv_heads, D = c_.d_head;
+        check(mf_rmsnorm_matmul((float*)mf_ptr(rs.qkv), (const float*)mf_ptr(rs.x), (const float*)mf_ptr(an_),
+                                c_.rms_norm_eps, mf_ptr(wqkv_), dtype_, (H + 2 * Hkv) * D, d, rs.stream),
+              "qkv projection");
+        mf_attn_desc a = {};
+        a.qkv = (const float*)mf_ptr(rs.qkv);
+        a.q_norm_w = (const float*)mf_ptr(qn_);
+        a.k_norm_w = (const float*)mf_ptr(kn_);
+        a.eps = c_.rms_norm_eps;
+        a.rope_table = mf_ptr(rs.rope);
+        a.k_cache = (float*)mf_ptr(rs.k_cache) + (size_t)layer_ * rs.kv_layer_floats;
+        a.v_cache = (float*)mf_ptr(rs.v_cache) + (size_t)layer_ * rs.kv_layer_floats;
+        a.max_seq = (int)c_.user_max_seq_len;
+        a.step_state = rs.d_step;
+        a.out = (float*)mf_ptr(rs.att);
+        a.n_heads = H;
+        a.n_kv_heads = Hkv;
+        a.d_head = D;
+        a.n_split = rs.attn_split;
+        a.workspace = mf_ptr(rs.attn_ws);
+        check(mf_attn_decode(&a, rs.stream), "attention");
+        check(mf_matmul_residual((float*)mf_ptr(rs.x), (const float*)mf_ptr(rs.att), mf_ptr(wo_), dtype_, d, H * D,
+                                 rs.stream),
+              "output projection");
+    }
+
+private:
+    const Config& c_;
+    int layer_;
+    int dtype_ = MF_BF16;
+    mf_buf *wqkv_ = nullptr, *wo_ = nullptr, *qn_ = nullptr, *kn_ = nullptr, *an_ = nullptr;
+};
+
+// Qwen3MoE (src/models/qwen3/module.cpp:405-476): dense SwiGLU FFN when the
+// model has no experts (the reference's "expert 0 with weight 1").
+class Qwen3MoE : public BaseLayer {
+public:
+    Qwen3MoE(const Config& c, int layer) : c_(c), layer_(layer) {}
+    void upload(const GGUFFile& f, int rank) override {
+        const std::string p = "blk." + std::to_string(layer_) + ".";
+        const bool moe = c_.n_experts > 0;
+        const TensorView& fn = f.tensor(p + "ffn_norm.weight");
+        const TensorView& wg = f.tensor(p + (moe ? "ffn_gate_exps.weight" : "ffn_gate.weight"));
+        const TensorView& wu = f.tensor(p + (moe ? "ffn_up_exps.weight" : "ffn_up.weight"));
+        const TensorView& wd = f.tensor(p + (moe ? "ffn_down_exps.weight" : "ffn_down.weight"));
+        const uint64_t d = c_.d_model, F = c_.d_ff, E = c_.n_experts;
+        expect_shape(fn, {d});
+        expect_f32(fn);
+        if (moe) {
+            expect_shape(wg, {E, F, d});
+            expect_shape(wu, {E, F, d});
+            expect_shape(wd, {E, d, F});
+        } else {
+            expect_shape(wg, {F, d});
+            expect_shape(wu, {F, d});
+            expect_shape(wd, {d, F});
+        }
+        if (!(wg.dtype == wu.dtype && wu.dtype == wd.dtype))
+            throw std::runtime_error("FFN weights of layer " + std::to_string(layer_) + " differ in dtype");
+        dtype_ = mf_dtype(wg.dtype);
+        own(fn_ = upload_tensor(fn, rank));
+        // gate/up interleaved by row: row 2i = gate_i, 2i+1 = up_i (per expert)
+        const size_t row = (size_t)d * dtype_size(wg.dtype);
+        const size_t nrows = wg.numel / d;
+        check(mf_alloc(wg.bytes + wu.bytes, rank, &wgu_), "alloc gate/up");
+        check(mf_write_2d(wgu_, 0, 2 * row, wg.data, row, row, nrows), "upload gate");
+        check(mf_write_2d(wgu_, row, 2 * row, wu.data, row, row, nrows), "upload up");
+        own(wgu_);
+        own(wd_ = upload_tensor(wd, rank));
+        const size_t k = moe ? (size_t)c_.n_active_experts : 1, ne = moe ? E : 1;
+        read_bytes_ = fn.bytes + (wg.bytes / ne + wu.bytes / ne + wd.bytes / ne) * k;
+        if (moe) {
+            const TensorView& wr = f.tensor(p + "ffn_gate_inp.weight");
+            expect_shape(wr, {E, d});
+            expect_f32(wr);
+            own(wr_ = upload_tensor(wr, rank));
+            read_bytes_ += wr.bytes;
+        }
+    }
+    void cuda_forward(RunState& rs) override {
+        const int d = c_.d_model, F = c_.d_ff;
+        float* x = (float*)mf_ptr(rs.x);
+        float* h = (float*)mf_ptr(rs.h);
+        if (c_.n_experts == 0) {
+            check(mf_swiglu_matmul(h, x, (const float*)mf_ptr(fn_), c_.rms_norm_eps, mf_ptr(wgu_), dtype_, F, d,
+                                   rs.stream),
+                  "gate/up projection");
+            check(mf_matmul_residual(x, h, mf_ptr(wd_), dtype_, d, F, rs.stream), "down projection");
+            return;
+        }
+        const int k = c_.n_active_experts;
+        int* ids = (int*)mf_ptr(rs.expert_ids) + (size_t)layer_ * k;
+        float* w = (float*)mf_ptr(rs.expert_w) + (size_t)layer_ * k;
+        check(mf_router_topk(ids, w, (float*)mf_ptr(rs.scores), x, (const float*)mf_ptr(fn_), c_.rms_norm_eps,
+                             (const float*)mf_ptr(wr_), d, c_.n_experts, k, rs.stream),
+              "router");
+        check(mf_moe_swiglu(h, x, (const float*)mf_ptr(fn_), c_.rms_norm_eps, mf_ptr(wgu_), dtype_, ids, k, F, d,
+                            rs.stream),
+              "expert gate/up");
+        check(mf_moe_down_residual(x, h, mf_ptr(wd_), dtype_, ids, w, k, d, F, rs.stream), "expert down");
+    }
+
+private:
+    const Config& c_;
+    int layer_;
+    int dtype_ = MF_BF16;
+    mf_buf *fn_ = nullptr, *wgu_ = nullptr, *wd_ = nullptr, *wr_ = nullptr;
+};
+
+// Qwen3FinalRMSNorm (module.cpp:105-138) + Qwen3LMHead (module.cpp:46-103):
+// the final norm is applied in the lm_head prologue.
+class Qwen3LMHead : public BaseLayer {
+public:
+    Qwen3LMHead(const Config& c, const Qwen3Embed* embed) : c_(c), embed_(embed) {}
+    void upload(const GGUFFile& f, int rank) override {
+        const TensorView& on = f.tensor("output_norm.weight");
+        expect_shape(on, {(uint64_t)c_.d_model});
+        expect_f32(on);
+        own(on_ = upload_tensor(on, rank));
+        if (c_.untied_head) {
+            const TensorView& t = f.tensor("output.weight");
+            expect_shape(t, {c_.vocab_size, (uint64_t)c_.d_model});
+            dtype_ = mf_dtype(t.dtype);
+            own(w_ = upload_tensor(t, rank));
+            head_bytes_ = t.bytes;
+        } else {
+            const TensorView& t = f.tensor("token_embd.weight");
+            w_ = embed_->weight();  // tied (src/models/qwen3/model.cpp:79-85)
+            dtype_ = embed_->dtype();
+            head_bytes_ = t.bytes;
+        }
+        norm_bytes_ = on.bytes;
+        read_bytes_ = head_bytes_ + norm_bytes_;
+    }
+    void cuda_forward(RunState& rs) override {
+        if (!rs.compute_logits) return;
+        check(mf_lm_head((float*)mf_ptr(rs.logits), (const float*)mf_ptr(rs.x), (const float*)mf_ptr(on_),
+                         c_.rms_norm_eps, mf_ptr(w_), dtype_, (int)c_.vocab_size, c_.d_model, 0, rs.d_step,
+                         mf_ptr(rs.lmh_ws), rs.stream),
+              "lm_head");
+    }
+    size_t head_bytes() const { return head_bytes_; }
+    size_t norm_bytes() const { return norm_bytes_; }
+
+private:
+    const Config& c_;
+    const Qwen3Embed* embed_;
+    int dtype_ = MF_BF16;
+    mf_buf *on_ = nullptr, *w_ = nullptr;
+    size_t head_bytes_ = 0, norm_bytes_ = 0;
+};
+
+}  // namespace
+
+BaseLayer::~BaseLayer() {
+    for (mf_buf* b : bufs_) mf_release(b);
+}
+
+Config Config::from_gguf(const GGUFFile& f, const RunParams& rp) {
+    Config c;
+    const std::string arch = f.get_string("general.architecture");
+    if (arch != "qwen3") throw std::runtime_error("unsupported architecture " + arch);
+    const std::string p = arch + ".";
+    c.model_max_seq_len = f.get_uint(p + "context_length");
+    c.d_model = (int)f.get_uint(p + "embedding_length");
+    c.n_layers = (int)f.get_uint(p + "block_count");
+    c.n_heads = (int)f.get_uint(p + "attention.head_count");
+    c.n_kv_heads = (int)f.get_uint(p + "attention.head_count_kv");
+    const int dk = (int)f.get_uint(p + "attention.key_length");
+    const int dv = (int)f.get_uint(p + "attention.value_length");
+    if (dk != dv) throw std::runtime_error("key_length != value_length");
+    c.d_head = dk;
+    c.d_ff = (int)(f.has(p + "expert_feed_forward_length") ? f.get_uint(p + "expert_feed_forward_length")
+                                                           : f.get_uint(p + "feed_forward_length"));
+    c.rms_norm_eps = (float)f.get_float(p + "attention.layer_norm_rms_epsilon");
+    c.d_rotary = c.d_head;  // src/base/config.cpp:308
+    c.freq_base = (float)f.get_float(p + "rope.freq_base");
+    c.n_experts = f.has(p + "expert_count") ? (int)f.get_uint(p + "expert_count") : 0;
+    c.n_active_experts = f.has(p + "expert_used_count") ? (int)f.get_uint(p + "expert_used_count") : 0;
+    if (c.n_active_experts > c.n_experts) throw std::runtime_error("expert_used_count > expert_count");
+    const MetaValue* toks = f.get("tokenizer.ggml.tokens");
+    if (!toks || toks->kind != MetaValue::ARRAY_STR) throw std::runtime_error("missing tokenizer.ggml.tokens");
+    c.vocab_size = toks->strs.size();
+    c.eos_token_id = (uint32_t)f.get_uint("tokenizer.ggml.eos_token_id");
+    c.padding_token_id = (uint32_t)f.get_uint("tokenizer.ggml.padding_token_id");
+    if (c.n_heads <= 0 || c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads != 0)
+        throw std::runtime_error("head counts are inconsistent");
+    c.num_iters = rp.num_iters;
+    c.user_max_seq_len = rp.max_seq_len;
+    if (c.user_max_seq_len == 0 || c.user_max_seq_len > c.model_max_seq_len)
+        throw std::runtime_error("max_seq_len must be in [1, context_length]");
+    c.top_k = rp.top_k;
+    c.temp = rp.temp;
+    c.top_p = rp.top_p;
+    c.min_p = rp.min_p;
+    c.penalty_pres = rp.penalty_pres;
+    c.seed = rp.seed;
+    c.weight_dtype = f.tensor("blk.0.attn_q.weight").dtype;
+    c.untied_head = f.has_tensor("output.weight");
+    c.head_dtype = f.tensor(c.untied_head ? "output.weight" : "token_embd.weight").dtype;
+    return c;
+}
+
+Qwen3Model::Qwen3Model(const std::string& path, const RunParams& rp, int rank) : path_(path), rp_(rp), rank_(rank) {
+    if (file_.open(path) != 0) throw std::runtime_error("failed to load model file " + path + ": " + file_.error());
+    cfg_ = Config::from_gguf(file_, rp);
+    reset_sampler();
+    build_layers();
+}
+
+Qwen3Model::~Qwen3Model() {
+    if (device_ == DeviceType::CUDA) {
+        mf_sync(rank_);
+        mf_reset_frames(rank_);
+    }
+    layers_.clear();
+    for (mf_buf* b : state_bufs_) mf_release(b);
+    if (rs_.h_logits) mf_host_free(rs_.h_logits);
+}
+
+void Qwen3Model::reset_sampler() {
+    SamplerParams sp;
+    sp.vocab_size = cfg_.vocab_size;
+    sp.top_k = cfg_.top_k;
+    sp.temp = cfg_.temp;
+    sp.top_p = cfg_.top_p;
+    sp.min_p = cfg_.min_p;
+    sp.penalty_pres = cfg_.penalty_pres;
+    sp.seed = cfg_.seed;
+    sampler_ = std::make_unique<Sampler>(sp);
+}
+
+void Qwen3Model::build_layers() {
+    auto embed = std::make_unique<Qwen3Embed>(cfg_);
+    Qwen3Embed* e = embed.get();
+    layers_.push_back(std::move(embed));
+    for (int i = 0; i < cfg_.n_layers; ++i) {
+        layers_.push_back(std::make_unique<Qwen3GQA>(cfg_, i));
+        layers_.push_back(std::make_unique<Qwen3MoE>(cfg_, i));
+    }
+    layers_.push_back(std::make_unique<Qwen3LMHead>(cfg_, e));
+}
+
+void Qwen3Model::set_device(DeviceType d) {
+    if (d == device_) return;
+    if (d != DeviceType::CUDA) throw std::runtime_error("this runtime moves models to CUDA only");
+    for (auto& l : layers_) l->upload(file_, rank_);
+    alloc_state();
+    device_ = d;
+}
+
+void Qwen3Model::alloc_state() {
+    const Config& c = cfg_;
+    RunState& rs = rs_;
+    rs.rank = rank_;
+    rs.stream = mf_stream(rank_);
+    auto alloc = [&](size_t bytes, const char* what) {
+        mf_buf* b = nullptr;
+        check(mf_alloc(bytes < 16 ? 16 : bytes, rank_, &b), what);
+        state_bufs_.push_back(b);
+        return b;
+    };
+    const size_t S = c.user_max_seq_len;
+    const int k = std::max(c.n_active_experts, 1);
+    rs.x = alloc((size_t)c.d_model * 4, "x");
+    rs.qkv = alloc((size_t)(c.n_heads + 2 * c.n_kv_heads) * c.d_head * 4, "qkv");
+    rs.att = alloc((size_t)c.n_heads * c.d_head * 4, "att_out");
+    rs.h = alloc((size_t)c.d_ff * k * 4, "hidden");
+    rs.logits = alloc(c.vocab_size * 4, "logits");
+    rs.scores = alloc((size_t)std::max(c.n_experts, 1) * 4, "moe_scores");
+    rs.expert_ids = alloc((size_t)c.n_layers * k * 4, "active_experts");
+    rs.expert_w = alloc((size_t)c.n_layers * k * 4, "active_experts_weights");
+    rs.kv_layer_floats = (size_t)c.n_kv_heads * S * c.d_head;
+    rs.k_cache = alloc(rs.kv_layer_floats * c.n_layers * 4, "k_cache");
+    rs.v_cache = alloc(rs.kv_layer_floats * c.n_layers * 4, "v_cache");
+    {
+        std::vector<float> tab(S * (size_t)c.d_rotary);
+        check(mf_rope_table(tab.data(), (int)S, c.d_rotary, c.freq_base), "rope table");
+        rs.rope = alloc(tab.size() * 4, "rope table");
+        check(mf_write(rs.rope, 0, tab.data(), tab.size() * 4), "upload rope table");
+    }
+    rs.attn_split = mf_attn_default_split(c.n_kv_heads, (int)S);
+    rs.attn_ws = alloc(mf_attn_workspace_bytes(c.n_heads, c.n_kv_heads, c.d_head, rs.attn_split), "attn workspace");
+    rs.lmh_ws = alloc(mf_lm_head_workspace_bytes(), "lm_head workspace");
+    check(mf_step_state(rank_, &rs.h_step, &rs.d_step), "step state");
+    void* hl = nullptr;
+    check(mf_host_alloc(c.vocab_size * 4, &hl), "pinned logits");
+    rs.h_logits = (float*)hl;
+    rs.kv_bytes_per_pos = 2ull * c.n_layers * c.n_kv_heads * c.d_head * sizeof(float);
+}
+
+size_t Qwen3Model::read_bytes(bool with_logits) const {
+    size_t b = 0;
+    for (size_t i = 0; i + 1 < layers_.size(); ++i) b += layers_[i]->read_bytes();
+    const auto* head = static_cast<const Qwen3LMHead*>(layers_.back().get());
+    b += head->norm_bytes();
+    if (with_logits) b += head->head_bytes();
+    return b;
+}
+
+void Qwen3Model::issue_frame(bool readback) {
+    for (auto& l : layers_) l->cuda_forward(rs_);
+    // the step record (greedy id) comes back with every host-driven frame;
+    // logits when asked
+    if (readback) check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, 16, rs_.stream), "step readback");
+    if (rs_.compute_logits && rs_.host_logits)
+        check(mf_copy_to_host_async(rs_.h_logits, mf_ptr(rs_.logits), cfg_.vocab_size * 4, rs_.stream),
+              "logits readback");
+}
+
+void Qwen3Model::forward(uint32_t token, int pos, bool compute_logits, bool host_logits) {
+    if (device_ != DeviceType::CUDA) throw std::runtime_error("call set_device(CUDA) first");
+    if (pos < 0 || (size_t)pos >= cfg_.user_max_seq_len) throw std::runtime_error("position outside the KV cache");
+    if (token >= cfg_.vocab_size) throw std::runtime_error("token id outside the vocabulary");
+    rs_.cur_pos = pos;
+    rs_.token_id = token;
+    rs_.compute_logits = compute_logits;
+    rs_.host_logits = compute_logits && host_logits;
+    rs_.h_step[0] = (int32_t)token;
+    rs_.h_step[1] = pos;
+    rs_.h_step[3] = 0;
+    const int frame = compute_logits ? (host_logits ? 2 : 0) : 1;
+    const int rc = mf_begin_frame(rank_, frame);
+    if (rc < 0) check(rc, "begin_frame");
+    if (rc == MF_FRAME_RECORD) {
+        try {
+            issue_frame(true);
+        } catch (...) {
+            mf_abort_frame(rank_);
+            throw;
+        }
+    }
+    check(mf_end_frame(rank_), "end_frame");
+}
+
+std::vector<uint32_t> Qwen3Model::generate(const std::vector<uint32_t>& prompt, size_t n_gen, const GenOptions& opt,
+                                           GenStats* stats, std::vector<float>* margins) {
+    if (prompt.empty()) throw std::runtime_error("empty prompt");
+    if (prompt.size() > cfg_.user_max_seq_len) throw std::runtime_error("prompt longer than max_seq_len");
+    const bool greedy = sampler_->greedy();
+    const bool need_host = !greedy || opt.trace;
+    GenStats st;
+    size_t model_bytes = 0, kv_bytes = 0;
+    const double t0 = now_s();
+    // prefill, token by token (src/base/model.cpp:120-129)
+    for (size_t i = 0; i < prompt.size(); ++i) {
+        const bool last = i + 1 == prompt.size();
+        forward(prompt[i], (int)i, last, last && need_host);
+        model_bytes += read_bytes(last);
+        kv_bytes += rs_.kv_bytes_per_pos * (i + 1);
+    }
+    st.prefill_time = (float)(now_s() - t0);
+    for (uint32_t t : prompt) sampler_->add_token(t);
+    std::vector<uint32_t> tokens = prompt, out;
+    const size_t num_iters = std::min(n_gen, cfg_.user_max_seq_len - tokens.size());
+    size_t generated = 0;
+    const double t1 = now_s();
+    while (generated < num_iters) {
+        uint32_t next;
+        if (need_host) {
+            const float* lg = rs_.h_logits;
+            next = sampler_->sample(lg);
+            if (margins) {
+                float v1 = -INFINITY, v2 = -INFINITY;
+                for (size_t i = 0; i < cfg_.vocab_size; ++i) {
+                    if (lg[i] > v1) {
+                        v2 = v1;
+                        v1 = lg[i];
+                    } else if (lg[i] > v2) {
+                        v2 = lg[i];
+                    }
+                }
+                margins->push_back(v1 - v2);
+            }
+            if (opt.on_step) opt.on_step(generated, lg, next);
+        } else {
+            next = device_argmax();
+            if (opt.on_step) opt.on_step(generated, nullptr, next);
+        }
+        out.push_back(next);
+        const uint32_t fed = opt.forced ? opt.forced[generated] : next;
+        sampler_->add_token(fed);
+        tokens.push_back(fed);
+        generated++;
+        if (generated == 1) st.ttft = st.prefill_time + (float)(now_s() - t1);
+        if (opt.stop_at_eos && fed == cfg_.eos_token_id) break;
+        forward(fed, (int)tokens.size() - 1, true, need_host);
+        model_bytes += read_bytes(true);
+        kv_bytes += rs_.kv_bytes_per_pos * tokens.size();
+    }
+    const double dt = now_s() - t1;
+    st.num_tokens_gen = (int)generated;
+    st.decode_seconds = dt;
+    st.throughput = dt > 0 ? (float)(generated / dt) : 0.f;
+    st.bytes_read = (double)(model_bytes + kv_bytes);
+    st.bandwidth = (float)(st.bytes_read / 1e9 / (dt + st.prefill_time));
+    if (stats) *stats = st;
+    return out;
+}
+
+uint32_t Qwen3Model::decode_chained(uint32_t token, int start_pos, int n) {
+    if (device_ != DeviceType::CUDA) throw std::runtime_error("call set_device(CUDA) first");
+    if (n <= 0) return token;
+    if (start_pos < 0 || (size_t)(start_pos + n) > cfg_.user_max_seq_len)
+        throw std::runtime_error("chained decode runs past max_seq_len");
+    rs_.compute_logits = true;
+    rs_.host_logits = false;
+    rs_.h_step[0] = (int32_t)token;
+    rs_.h_step[1] = start_pos;
+    rs_.h_step[3] = 1;
+    for (int i = 0; i < n; ++i) {
+        // frame 3 uploads the host record once; frame 4 continues on the device
+        const int frame = i == 0 ? 3 : 4;
+        const int rc = mf_begin_frame_ex(rank_, frame, i == 0 ? 0 : MF_FRAME_NO_UPLOAD);
+        if (rc < 0) check(rc, "begin_frame");
+        if (rc == MF_FRAME_RECORD) {
+            try {
+                issue_frame(i + 1 == n);
+            } catch (...) {
+                mf_abort_frame(rank_);
+                throw;
+            }
+        }
+        check(mf_end_frame_async(rank_), "end_frame");
+    }
+    check(mf_sync(rank_), "sync");
+    rs_.h_step[3] = 0;
+    int32_t rec[4];
+    std::memcpy(rec, rs_.h_step, sizeof(rec));
+    return (uint32_t)rec[2];
+}
+
+int Qwen3Model::read_experts(int layer, int* ids, float* w) const {
+    if (cfg_.n_experts == 0 || layer < 0 || layer >= cfg_.n_layers) return MF_E_INVALID;
+    const size_t k = cfg_.n_active_experts;
+    int rc = mf_read(rs_.expert_ids, (size_t)layer * k * 4, ids, k * 4);
+    if (rc == MF_OK && w) rc = mf_read(rs_.expert_w, (size_t)layer * k * 4, w, k * 4);
+    return rc;
+}
+
+int Qwen3Model::read_kv(int layer, float* k, float* v, int n_pos) const {
+    // returns rows [0, n_pos) in the reference's [pos][kv_head][d_head] order
+    if (layer < 0 || layer >= cfg_.n_layers || n_pos < 0 || (size_t)n_pos > cfg_.user_max_seq_len) return MF_E_INVALID;
+    const size_t D = cfg_.d_head, S = cfg_.user_max_seq_len;
+    std::vector<float> tmp(rs_.kv_layer_floats);
+    for (int which = 0; which < 2; ++which) {
+        float* dst = which == 0 ? k : v;
+        if (!dst) continue;
+        int rc = mf_read(which == 0 ? rs_.k_cache : rs_.v_cache, (size_t)layer * rs_.kv_layer_floats * 4, tmp.data(),
+                         tmp.size() * 4);
+        if (rc) return rc;
+        for (int p = 0; p < n_pos; ++p)
+            for (int hh = 0; hh < cfg_.n_kv_heads; ++hh)
+                std::memcpy(dst + ((size_t)p * cfg_.n_kv_heads + hh) * D, tmp.data() + ((size_t)hh * S + p) * D,
+                            D * 4);
+    }
+    return MF_OK;
+}
+
+int Qwen3Model::read_x(float* x) const { return mf_read(rs_.x, 0, x, (size_t)cfg_.d_model * 4); }
+
+}  // namespace minfer

@@ -1,0 +1,152 @@
+// CUDA host runtime of the Qwen3 token loop: the reference's host object model
+// (Config / RunState / BaseLayer subclasses / BaseModel, include/minfer/base/*.hpp,
+// include/minfer/models/qwen3/module.hpp) rebuilt over the libmfcuda C ABI.
+// Each layer class has a `cuda_forward` that issues the fused device ops;
+// BaseModel::forward becomes one frame (a captured CUDA graph per frame kind).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gguf.hpp"
+#include "minfer_cuda.h"
+#include "sampler.hpp"
+
+namespace minfer {
+
+// include/minfer/base/config.hpp:22 plus the CUDA device this runtime adds
+enum class DeviceType : int { CPU = 0, METAL = 1, CUDA = 2 };
+
+// include/minfer/base/config.hpp:37-51 (RunParams)
+struct RunParams {
+    size_t num_iters = 0;
+    size_t max_seq_len = 0;
+    size_t top_k = 1;
+    float temp = 0.0f;
+    float top_p = 1.0f;
+    float min_p = 0.0f;
+    float penalty_pres = 0.0f;
+    int seed = 0;
+};
+
+// include/minfer/base/config.hpp:53-75 (Config), filled from GGUF metadata as
+// src/base/config.cpp:277-337 does.
+struct Config {
+    size_t vocab_size = 0, model_max_seq_len = 0;
+    int d_model = 0, n_layers = 0, n_heads = 0, n_kv_heads = 0, d_head = 0, d_rotary = 0, d_ff = 0;
+    int n_active_experts = 0, n_experts = 0;
+    float rms_norm_eps = 1e-6f, freq_base = 1e6f;
+    uint32_t eos_token_id = 0, padding_token_id = 0;
+    size_t user_max_seq_len = 0, top_k = 1, num_iters = 0;
+    int seed = 0;
+    float temp = 0.f, top_p = 1.f, min_p = 0.f, penalty_pres = 0.f;
+    DataType weight_dtype = DataType::INVALID;  // projection weights
+    DataType head_dtype = DataType::INVALID;    // lm_head weight
+    bool untied_head = false;
+
+    static Config from_gguf(const GGUFFile& f, const RunParams& rp);
+};
+
+// include/minfer/base/stats.hpp:3-15
+struct GenStats {
+    int num_tokens_gen = 0;
+    float ttft = 0.f;
+    float throughput = 0.f;
+    float prefill_time = 0.f;
+    float bandwidth = 0.f;
+    double decode_seconds = 0.0;
+    double bytes_read = 0.0;
+};
+
+// Device-resident run state (include/minfer/base/config.hpp:77-102). The KV
+// cache layout is [layer][kv_head][position][d_head] fp32.
+struct RunState {
+    int rank = 0;
+    void* stream = nullptr;
+    mf_buf *x = nullptr, *qkv = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+    mf_buf *scores = nullptr, *expert_ids = nullptr, *expert_w = nullptr;
+    mf_buf *k_cache = nullptr, *v_cache = nullptr, *rope = nullptr;
+    mf_buf *attn_ws = nullptr, *lmh_ws = nullptr;
+    int32_t* h_step = nullptr;  // pinned {token, pos, next_token, chain}
+    void* d_step = nullptr;
+    float* h_logits = nullptr;  // pinned copy of the last logits (host-logit frames)
+    int attn_split = 1;
+    int cur_pos = 0;
+    uint32_t token_id = 0;
+    bool compute_logits = false;
+    bool host_logits = false;
+    size_t kv_bytes_per_pos = 0;
+    size_t kv_layer_floats = 0;  // n_kv_heads * max_seq * d_head
+};
+
+class BaseLayer {
+public:
+    virtual ~BaseLayer();
+    virtual void cuda_forward(RunState& rs) = 0;
+    virtual void upload(const GGUFFile& f, int rank) = 0;
+    size_t read_bytes() const { return read_bytes_; }
+
+protected:
+    void own(mf_buf* b) { bufs_.push_back(b); }
+    size_t read_bytes_ = 0;
+    std::vector<mf_buf*> bufs_;
+};
+
+class Qwen3Model {
+public:
+    Qwen3Model(const std::string& path, const RunParams& rp, int rank = 0);
+    ~Qwen3Model();
+
+    void set_device(DeviceType d);  // CUDA: upload weights, allocate the run state
+    DeviceType device() const { return device_; }
+    const Config& config() const { return cfg_; }
+
+    // One token step (BaseModel::forward, src/base/model.cpp:36-59) as one frame.
+    void forward(uint32_t token, int pos, bool compute_logits, bool host_logits);
+    const float* host_logits() const { return rs_.h_logits; }
+    uint32_t device_argmax() const { return (uint32_t)rs_.h_step[2]; }
+    // Bytes the reference counts per forward (src/base/module.cpp read bytes).
+    size_t read_bytes(bool with_logits) const;
+
+    struct GenOptions {
+        bool stop_at_eos = false;
+        const uint32_t* forced = nullptr;  // teacher forcing: feed forced[i] after step i
+        bool trace = false;                // host logits every step (margins, callbacks)
+        std::function<void(size_t step, const float* logits, uint32_t picked)> on_step;
+    };
+    // BaseModel::generate without the tokenizer (src/base/model.cpp:99-186).
+    std::vector<uint32_t> generate(const std::vector<uint32_t>& prompt, size_t n_gen, const GenOptions& opt,
+                                   GenStats* stats, std::vector<float>* margins);
+    // Greedy decode with the device feeding itself: frame i embeds the argmax
+    // of frame i-1 (chained step record), frames are queued back to back with
+    // no host round trip. Returns the last greedy id; the caller times it.
+    uint32_t decode_chained(uint32_t token, int start_pos, int n);
+
+    // Test access
+    int read_experts(int layer, int* ids, float* w) const;
+    int read_kv(int layer, float* k, float* v, int n_pos) const;
+    int read_x(float* x) const;
+    void reset_sampler();
+
+private:
+    void build_layers();
+    void alloc_state();
+    void issue_frame(bool readback);
+
+    std::string path_;
+    GGUFFile file_;
+    Config cfg_;
+    RunParams rp_;
+    int rank_ = 0;
+    DeviceType device_ = DeviceType::CPU;
+    std::vector<std::unique_ptr<BaseLayer>> layers_;
+    RunState rs_;
+    std::unique_ptr<Sampler> sampler_;
+    std::vector<mf_buf*> state_bufs_;
+};
+
+}  // namespace minfer

@@ -1,0 +1,75 @@
+#include "sampler.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <numeric>
+#include <stdexcept>
+
+namespace minfer {
+
+Sampler::Sampler(const SamplerParams& p)
+    : p_(p), logits_(p.vocab_size), probs_(p.vocab_size), idx_(p.vocab_size), rng_(p.seed), dist_(0.0f, 1.0f) {
+    // parameter ranges checked by the reference's constructor (src/base/sampler.cpp:24-27)
+    if (p.top_k == 0 || p.top_k > p.vocab_size) throw std::invalid_argument("top_k must be in [1, vocab_size]");
+    if (!(p.top_p >= 0.0f && p.top_p <= 1.0f)) throw std::invalid_argument("top_p must be in [0, 1]");
+    if (!(p.min_p >= 0.0f && p.min_p <= 1.0f)) throw std::invalid_argument("min_p must be in [0, 1]");
+    if (!(p.penalty_pres >= 0.0f && p.penalty_pres <= 2.0f)) throw std::invalid_argument("penalty_pres must be in [0, 2]");
+}
+
+void Sampler::add_token(uint32_t token) { seen_.insert(token); }
+
+uint32_t Sampler::sample(const float* logits) {
+    const size_t V = p_.vocab_size;
+    if (p_.temp == 0.0f) return (uint32_t)(std::max_element(logits, logits + V) - logits);
+
+    for (size_t i = 0; i < V; ++i) logits_[i] = logits[i] - float(seen_.count((uint32_t)i)) * p_.penalty_pres;
+    std::iota(idx_.begin(), idx_.end(), 0u);
+    auto by_logit = [&](size_t a, size_t b) { return logits_[a] > logits_[b]; };
+    std::nth_element(idx_.begin(), idx_.begin() + p_.top_k, idx_.end(), by_logit);
+    std::sort(idx_.begin(), idx_.begin() + p_.top_k, by_logit);
+
+    size_t cut = p_.top_k;
+    const float top = logits_[idx_[0]];
+    float acc = 0.0f;
+    for (size_t i = 0; i < cut; ++i) {
+        probs_[idx_[i]] = std::exp(logits_[idx_[i]] - top);
+        acc += probs_[idx_[i]];
+    }
+    for (size_t i = 0; i < cut; ++i) probs_[idx_[i]] /= acc;
+
+    acc = 0.0f;
+    for (size_t i = 0; i < cut; ++i) {
+        acc += probs_[idx_[i]];
+        if (acc >= p_.top_p) {
+            cut = i + 1;
+            break;
+        }
+    }
+    if (p_.min_p > 0.0f) {
+        const float thr = top + std::log(p_.min_p);
+        for (size_t i = 0; i < cut; ++i) {
+            if (logits_[idx_[i]] < thr) {
+                cut = i;
+                break;
+            }
+        }
+    }
+    if (cut == 0) throw std::runtime_error("sampling filters removed every token");
+
+    acc = 0.0f;
+    for (size_t i = 0; i < cut; ++i) {
+        probs_[idx_[i]] = std::exp((logits_[idx_[i]] - top) / p_.temp);
+        acc += probs_[idx_[i]];
+    }
+    for (size_t i = 0; i < cut; ++i) probs_[idx_[i]] /= acc;
+
+    const float r = dist_(rng_);
+    acc = 0.0f;
+    for (size_t i = 0; i < cut; ++i) {
+        acc += probs_[idx_[i]];
+        if (acc >= r) return idx_[i];
+    }
+    return idx_[cut - 1];
+}
+
+}  // namespace minfer

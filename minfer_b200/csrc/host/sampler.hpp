@@ -1,0 +1,45 @@
+// Host-side token sampler of the token loop. Same algorithm and the same
+// libstdc++ primitives as the reference's Sampler (src/base/sampler.cpp:10-117),
+// so identical logits give identical ids:
+//   temp == 0  -> first maximum (std::max_element);
+//   otherwise  -> presence penalty, nth_element + sort for the top-k,
+//                 softmax over the top-k, top-p cut, min-p cut, temperature
+//                 softmax, one std::uniform_real_distribution<float> draw from
+//                 std::mt19937_64(seed).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <random>
+#include <unordered_set>
+#include <vector>
+
+namespace minfer {
+
+struct SamplerParams {
+    size_t vocab_size = 0;
+    size_t top_k = 1;
+    float temp = 0.0f;
+    float top_p = 1.0f;
+    float min_p = 0.0f;
+    float penalty_pres = 0.0f;
+    int seed = 0;
+};
+
+class Sampler {
+public:
+    explicit Sampler(const SamplerParams& p);
+    void add_token(uint32_t token);
+    uint32_t sample(const float* logits);
+    bool greedy() const { return p_.temp == 0.0f; }
+
+private:
+    SamplerParams p_;
+    std::vector<float> logits_, probs_;
+    std::vector<uint32_t> idx_;
+    std::unordered_set<uint32_t> seen_;
+    std::mt19937_64 rng_;
+    std::uniform_real_distribution<float> dist_;
+};
+
+}  // namespace minfer

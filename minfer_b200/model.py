@@ -1,0 +1,163 @@
+"""Python face of the CUDA host runtime (include/minfer_model.h), shaped like
+the reference's BaseModel / Qwen3Model (include/minfer/base/model.hpp:17-41,
+include/minfer/models/qwen3/model.hpp): construct from a GGUF path and
+RunParams, `set_device("cuda")`, then `forward`, `generate`, `benchmark`.
+Token ids stand in for text (the tokenizer is not on this path).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import dataclasses
+
+import numpy as np
+
+from ._lib import (MF_GEN_MARGINS, MF_GEN_STOP_AT_EOS, check, cuda_lib, host_lib, mf_gen_stats, mf_model_info,
+                   mf_run_params)
+
+
+@dataclasses.dataclass
+class RunParams:
+    """include/minfer/base/config.hpp:37-51."""
+
+    num_iters: int = 0
+    max_seq_len: int = 4096
+    top_k: int = 1
+    temp: float = 0.0
+    top_p: float = 1.0
+    min_p: float = 0.0
+    penalty_pres: float = 0.0
+    seed: int = 0
+
+    def to_c(self) -> mf_run_params:
+        return mf_run_params(self.num_iters, self.max_seq_len, self.top_k, self.temp, self.top_p, self.min_p,
+                             self.penalty_pres, self.seed)
+
+
+@dataclasses.dataclass
+class GenStats:
+    """include/minfer/base/stats.hpp:3-15."""
+
+    num_tokens_gen: int
+    ttft: float
+    throughput: float
+    prefill_time: float
+    bandwidth: float
+    decode_seconds: float
+    bytes_read: float
+
+
+_initialised: set = set()
+
+
+def init(n_ranks: int = 1, devices: list[int] | None = None) -> None:
+    """MetalManager::init equivalent: pick devices, create per-rank streams."""
+    key = (n_ranks, tuple(devices) if devices else None)
+    if key in _initialised:
+        return
+    arr = (C.c_int * n_ranks)(*(devices or range(n_ranks)))
+    check(cuda_lib().mf_init(n_ranks, arr))
+    _initialised.add(key)
+
+
+class Qwen3Model:
+    def __init__(self, model_file: str, run_params: RunParams, rank: int = 0, device: int | None = None):
+        if not _initialised:
+            init(1, [device if device is not None else 0])
+        self._lib = host_lib()
+        self._h = C.c_void_p()
+        self.run_params = run_params
+        self._rp = run_params.to_c()
+        check(self._lib.mf_model_load(str(model_file).encode(), C.byref(self._rp), rank, C.byref(self._h)))
+        self.device = "cpu"
+        self._refresh_info()
+
+    def _refresh_info(self):
+        info = mf_model_info()
+        check(self._lib.mf_model_info_get(self._h, C.byref(info)))
+        self.info = info
+        self.vocab_size = info.vocab_size
+
+    def set_device(self, device: str) -> "Qwen3Model":
+        if device != "cuda":
+            raise ValueError("this runtime runs the model on CUDA only")
+        check(self._lib.mf_model_to_cuda(self._h))
+        self.device = "cuda"
+        self._refresh_info()
+        return self
+
+    def close(self):
+        if self._h:
+            self._lib.mf_model_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- BaseModel::forward
+    def forward(self, token: int, pos: int, compute_logits: bool = True, host_logits: bool = True):
+        check(self._lib.mf_model_forward(self._h, int(token), int(pos), int(compute_logits), int(host_logits)))
+
+    def logits(self) -> np.ndarray:
+        out = np.empty(self.vocab_size, dtype=np.float32)
+        check(self._lib.mf_model_logits(self._h, out.ctypes.data, self.vocab_size))
+        return out
+
+    def argmax(self) -> int:
+        v = C.c_uint32()
+        check(self._lib.mf_model_argmax(self._h, C.byref(v)))
+        return v.value
+
+    # -- BaseModel::generate (ids in, ids out)
+    def generate(self, prompt, n_gen: int, stop_at_eos: bool = False, forced=None, margins: bool = False):
+        prompt = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.zeros(n_gen, dtype=np.uint32)
+        mg = np.zeros(n_gen, dtype=np.float32)
+        n_out = C.c_size_t()
+        st = mf_gen_stats()
+        flags = (MF_GEN_STOP_AT_EOS if stop_at_eos else 0) | (MF_GEN_MARGINS if margins else 0)
+        forced_arr = None if forced is None else np.ascontiguousarray(forced, dtype=np.uint32)
+        check(self._lib.mf_model_generate(self._h, prompt.ctypes.data, prompt.size, n_gen, flags,
+                                          None if forced_arr is None else forced_arr.ctypes.data, out.ctypes.data,
+                                          C.byref(n_out), mg.ctypes.data, C.byref(st)))
+        n = n_out.value
+        stats = GenStats(st.num_tokens_gen, st.ttft, st.throughput, st.prefill_time, st.bandwidth,
+                         st.decode_seconds, st.bytes_read)
+        return out[:n], (mg[:n] if margins else None), stats
+
+    def decode_chained(self, token: int, start_pos: int, n: int) -> int:
+        last = C.c_uint32()
+        check(self._lib.mf_model_decode_chained(self._h, int(token), int(start_pos), int(n), C.byref(last)))
+        return last.value
+
+    def reset_sampler(self):
+        check(self._lib.mf_model_reset_sampler(self._h))
+
+    # -- test access
+    def experts(self, layer: int):
+        k = self.info.n_active_experts
+        ids = np.zeros(k, dtype=np.int32)
+        w = np.zeros(k, dtype=np.float32)
+        check(self._lib.mf_model_experts(self._h, layer, ids.ctypes.data, w.ctypes.data))
+        return ids, w
+
+    def kv(self, layer: int, n_pos: int):
+        n = n_pos * self.info.n_kv_heads * self.info.d_head
+        k = np.zeros(n, dtype=np.float32)
+        v = np.zeros(n, dtype=np.float32)
+        check(self._lib.mf_model_kv(self._h, layer, k.ctypes.data, v.ctypes.data, n_pos))
+        return k, v
+
+    def x(self) -> np.ndarray:
+        out = np.zeros(self.info.d_model, dtype=np.float32)
+        check(self._lib.mf_model_x(self._h, out.ctypes.data))
+        return out
+
+
+def random_prompt(n: int, vocab: int, seed: int) -> np.ndarray:
+    """Prompt ids as BaseModel::benchmark draws them (src/base/model.cpp:189-193)."""
+    out = np.zeros(n, dtype=np.uint32)
+    check(host_lib().mf_random_prompt(seed, vocab, n, out.ctypes.data))
+    return out

@@ -1,0 +1,3 @@
+/* The reference includes <arm_bf16.h>; the types it needs live in arm_neon.h here. */
+#pragma once
+#include "arm_neon.h"

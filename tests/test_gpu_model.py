@@ -1,0 +1,157 @@
+"""Token-loop parity of the CUDA runtime against the oracle on seeded synthetic
+GGUF models: greedy ids, sampled ids, MoE expert ids, KV cache, logits.
+
+Ids must be bit-exact. A step whose top-2 logit margin (reference side) is
+below MARGIN_TOL is a tolerance event (fp32 summation order can flip it); the
+test then keeps comparing under teacher forcing (the runtime is fed the
+oracle's ids) and reports the event instead of failing on it.
+Logits: max-abs <= 1e-3 for fp32 weights, 2e-2 for bf16/fp16 (relative to the
+oracle's fp32 path).
+"""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from conftest import TINY, tiny_model
+from oracle.oracle_py import PortModel
+
+pytestmark = pytest.mark.gpu
+
+MARGIN_TOL = 1e-4
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def logit_tol(dtype: str) -> float:
+    return 1e-3 if dtype == "f32" else 2e-2
+
+
+def check_ids(got, ref, margins, what):
+    events = []
+    for i, (a, b) in enumerate(zip(got, ref)):
+        if a != b:
+            assert margins[i] < MARGIN_TOL, f"{what}: id mismatch at step {i} ({a} vs {b}), margin {margins[i]}"
+            events.append(i)
+    return events
+
+
+@pytest.fixture(scope="module")
+def Model(gpu):
+    from minfer_b200.model import Qwen3Model, RunParams
+
+    return Qwen3Model, RunParams
+
+
+@pytest.mark.parametrize("name", list(TINY))
+def test_greedy_vs_oracle(Model, name):
+    Qwen3Model, RunParams = Model
+    path = tiny_model(name)
+    cfg = TINY[name]
+    P, G = 12, 40
+    from minfer_b200.model import random_prompt
+
+    prompt = random_prompt(P, cfg.vocab, 30)
+    orc = PortModel(path, max_seq=P + G + 1)
+    ref_ids, ref_mg = orc.generate(prompt, G)
+    m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=P + G + 1)).set_device("cuda")
+    ids, mg, st = m.generate(prompt, G, forced=ref_ids, margins=True)
+    ev = check_ids(ids, ref_ids, ref_mg, name)
+    np.testing.assert_allclose(mg, ref_mg, atol=logit_tol(cfg.dtype))
+    assert st.num_tokens_gen == G and len(ev) <= 1
+    # free-running greedy (no forcing) agrees up to the first tolerance event
+    m2 = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=P + G + 1)).set_device("cuda")
+    free, _, _ = m2.generate(prompt, G)
+    first = ev[0] if ev else G
+    assert list(free[:first]) == list(ref_ids[:first])
+
+
+@pytest.mark.parametrize("name", ["tiny-f32", "tiny-bf16", "tiny-moe"])
+def test_logits_and_kv_vs_oracle(Model, name):
+    Qwen3Model, RunParams = Model
+    path = tiny_model(name)
+    cfg = TINY[name]
+    P = 20
+    from minfer_b200.model import random_prompt
+
+    prompt = random_prompt(P, cfg.vocab, 7)
+    orc = PortModel(path, max_seq=P + 1)
+    m = Qwen3Model(path, RunParams(max_seq_len=P + 1)).set_device("cuda")
+    kvd = cfg.n_kv_heads * cfg.d_head
+    if cfg.moe:
+        orc.record_experts(True)
+    n_events = 0
+    for i, t in enumerate(prompt):
+        orc.forward(int(t), i, True)
+        m.forward(int(t), i, True, True)
+        lo, lg = orc.logits(), m.logits()
+        assert np.max(np.abs(lo - lg)) <= logit_tol(cfg.dtype), f"step {i}: {np.max(np.abs(lo - lg))}"
+        assert m.argmax() == int(np.argmax(lg))
+        if cfg.moe:
+            ref_ids, _ = orc.recorded_experts(cfg.n_active)
+            for layer in range(cfg.n_layers):
+                ids, w = m.experts(layer)
+                if list(ids) != list(ref_ids[i * cfg.n_layers + layer]):
+                    n_events += 1
+    assert n_events == 0
+    for layer in range(cfg.n_layers):
+        k, v = m.kv(layer, P)
+        ko, vo = orc.kv(layer, P, kvd)
+        np.testing.assert_allclose(k, ko, rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(v, vo, rtol=1e-4, atol=1e-5)
+
+
+def test_sampled_vs_oracle(Model):
+    """Temperature 0.7, top-k 20, top-p 0.9, seed 42 (the sampled workload's settings)."""
+    Qwen3Model, RunParams = Model
+    name = "tiny-bf16"
+    path = tiny_model(name)
+    cfg = TINY[name]
+    P, G = 16, 48
+    from minfer_b200.model import random_prompt
+
+    prompt = random_prompt(P, cfg.vocab, 42)
+    kw = dict(top_k=20, temp=0.7, top_p=0.9, seed=42)
+    orc = PortModel(path, max_seq=P + G + 1, **kw)
+    ref_ids, ref_mg = orc.generate(prompt, G)
+    m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=P + G + 1, **kw)).set_device("cuda")
+    ids, mg, _ = m.generate(prompt, G, forced=ref_ids, margins=True)
+    mism = [i for i in range(G) if ids[i] != ref_ids[i]]
+    assert len(mism) <= 1, mism
+    assert len(set(ref_ids.tolist())) > 1  # really sampling
+
+
+def test_chained_matches_host_loop(Model):
+    Qwen3Model, RunParams = Model
+    path = tiny_model("tiny-bf16")
+    P, G = 8, 24
+    from minfer_b200.model import random_prompt
+
+    prompt = random_prompt(P, TINY["tiny-bf16"].vocab, 3)
+    m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=P + G + 2)).set_device("cuda")
+    ids, _, _ = m.generate(prompt, G)
+    m2 = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=P + G + 2)).set_device("cuda")
+    for i, t in enumerate(prompt):
+        m2.forward(int(t), i, i == P - 1, False)
+    first = m2.argmax()
+    assert first == ids[0]
+    last = m2.decode_chained(first, P, G - 1)
+    assert last == ids[G - 1]
+
+
+def test_golden_fixtures(Model):
+    """Runtime vs the reference's own CPU run (fixtures made by tests/golden/make_golden.py)."""
+    Qwen3Model, RunParams = Model
+    files = sorted(GOLDEN.glob("model_*.json"))
+    assert files, "golden fixtures missing"
+    for f in files:
+        g = json.loads(f.read_text())
+        cfg = TINY[g["model"]]
+        path = tiny_model(g["model"])
+        kw = g["sampler"]
+        P, G = len(g["prompt"]), len(g["ids"])
+        m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=P + G + 1, **kw)).set_device("cuda")
+        ids, mg, _ = m.generate(np.array(g["prompt"], np.uint32), G, forced=np.array(g["ids"], np.uint32),
+                                margins=True)
+        check_ids(ids, g["ids"], g["margins"], f.name)
+        np.testing.assert_allclose(mg, g["margins"], atol=logit_tol(cfg.dtype))
