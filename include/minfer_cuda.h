@@ -115,6 +115,8 @@ int mf_end_frame_async(int rank);
 int mf_abort_frame(int rank);
 /* Drops every captured frame of `rank` (after buffers were reallocated). */
 int mf_reset_frames(int rank);
+/* Drops the captured frames of `rank` with ids in [first_id, last_id]. */
+int mf_drop_frames(int rank, int first_id, int last_id);
 /* Waits for all work on the rank's stream. */
 int mf_sync(int rank);
 /* The rank's stream as a cudaStream_t. */

@@ -103,6 +103,7 @@ CUDA_API = {
     "mf_end_frame_async": (I, [I]),
     "mf_abort_frame": (I, [I]),
     "mf_reset_frames": (I, [I]),
+    "mf_drop_frames": (I, [I, I, I]),
     "mf_sync": (I, [I]),
     "mf_stream": (P, [I]),
     "mf_timer_start": (I, [I]),

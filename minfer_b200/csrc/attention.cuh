@@ -4,7 +4,7 @@
 // Reference semantics (src/models/qwen3/module.cpp:187-234, src/ops/kernels.cpp:31-110):
 //  * q_h <- rmsnorm(q_h, q_norm), k_h <- rmsnorm(k_h, k_norm) over d_head;
 //  * NeoX RoPE on pairs (i, i + d_rot/2): x0' = cos*x0 - sin*x1,
-//    x1' = sin*x0 + cos*x1 in float with separate roundings; (cos, sin) of
+//    x1' = sin*x0 + cos*x1 in float, first product fused; (cos, sin) of
 //    each position come from a host-built table (same float libm as the
 //    reference), so the rotation is bit-exact;
 //  * K/V row `pos` appended to the cache, then for every query head h of KV
@@ -85,10 +85,12 @@ MF_DEVICE float4 norm_rope_head(float4 v, const float* nw, float eps, const floa
     for (int e = 0; e < 4; ++e) {
         const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
         const float2 c = __ldg(cs + 4 * (lane & 15) + e);
+        // x0' = cos*x0 - sin*x1, x1' = sin*x0 + cos*x1, with the first product
+        // fused as the reference's compiler contracts it: fma(cos, x0, -(sin*x1))
         if (lane < 16) {
-            o[e] = __fsub_rn(__fmul_rn(c.x, x[e]), __fmul_rn(c.y, other));  // x0' = cos*x0 - sin*x1
+            o[e] = fmaf(c.x, x[e], -__fmul_rn(c.y, other));
         } else {
-            o[e] = __fadd_rn(__fmul_rn(c.y, other), __fmul_rn(c.x, x[e]));  // x1' = sin*x0 + cos*x1
+            o[e] = fmaf(c.y, other, __fmul_rn(c.x, x[e]));
         }
     }
     return make_float4(o[0], o[1], o[2], o[3]);

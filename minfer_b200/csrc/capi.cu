@@ -134,7 +134,8 @@ int prepare(const void* fn, int threads, size_t smem, int* blocks_per_sm) {
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lk(g_kmu);
     KInfo& ki = g_kinfo[{dev, fn}];
-    if ((int)smem > ki.max_smem_set && smem > 48 * 1024) {
+    // opt in to large dynamic shared memory (static + dynamic above 48 KB)
+    if ((int)smem > ki.max_smem_set && smem >= 32 * 1024) {
         MF_CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         ki.max_smem_set = (int)smem;
     }
@@ -516,6 +517,22 @@ int mf_abort_frame(int rank) {
     return MF_OK;
 }
 int mf_end_frame_async(int rank) { return end_frame_impl(rank, false); }
+
+int mf_drop_frames(int rank, int first_id, int last_id) {
+    MF_REQUIRE(rank >= 0 && rank < (int)g.ranks.size(), MF_E_INVALID, "rank %d out of range", rank);
+    Rank& r = g.ranks[rank];
+    MF_CK(cudaSetDevice(r.device));
+    MF_CK(cudaStreamSynchronize(r.stream));
+    for (auto it = r.frames.begin(); it != r.frames.end();) {
+        if (it->first >= first_id && it->first <= last_id) {
+            cudaGraphExecDestroy(it->second);
+            it = r.frames.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    return MF_OK;
+}
 
 int mf_reset_frames(int rank) {
     MF_REQUIRE(rank >= 0 && rank < (int)g.ranks.size(), MF_E_INVALID, "rank %d out of range", rank);

@@ -324,7 +324,20 @@ Config Config::from_gguf(const GGUFFile& f, const RunParams& rp) {
     return c;
 }
 
-Qwen3Model::Qwen3Model(const std::string& path, const RunParams& rp, int rank) : path_(path), rp_(rp), rank_(rank) {
+namespace {
+// Frames are captured per manager rank; every model instance owns a disjoint
+// block of frame ids so two models on one device never replay each other's graphs.
+constexpr int kFrameKinds = 8;
+int next_frame_base() {
+    static int next = 0;
+    const int b = next;
+    next += kFrameKinds;
+    return b;
+}
+}  // namespace
+
+Qwen3Model::Qwen3Model(const std::string& path, const RunParams& rp, int rank)
+    : path_(path), rp_(rp), rank_(rank), frame_base_(next_frame_base()) {
     if (file_.open(path) != 0) throw std::runtime_error("failed to load model file " + path + ": " + file_.error());
     cfg_ = Config::from_gguf(file_, rp);
     reset_sampler();
@@ -334,7 +347,7 @@ Qwen3Model::Qwen3Model(const std::string& path, const RunParams& rp, int rank) :
 Qwen3Model::~Qwen3Model() {
     if (device_ == DeviceType::CUDA) {
         mf_sync(rank_);
-        mf_reset_frames(rank_);
+        mf_drop_frames(rank_, frame_base_, frame_base_ + kFrameKinds - 1);
     }
     layers_.clear();
     for (mf_buf* b : state_bufs_) mf_release(b);
@@ -442,7 +455,7 @@ void Qwen3Model::forward(uint32_t token, int pos, bool compute_logits, bool host
     rs_.h_step[0] = (int32_t)token;
     rs_.h_step[1] = pos;
     rs_.h_step[3] = 0;
-    const int frame = compute_logits ? (host_logits ? 2 : 0) : 1;
+    const int frame = frame_base_ + (compute_logits ? (host_logits ? 2 : 0) : 1);
     const int rc = mf_begin_frame(rank_, frame);
     if (rc < 0) check(rc, "begin_frame");
     if (rc == MF_FRAME_RECORD) {
@@ -524,6 +537,7 @@ std::vector<uint32_t> Qwen3Model::generate(const std::vector<uint32_t>& prompt, 
 uint32_t Qwen3Model::decode_chained(uint32_t token, int start_pos, int n) {
     if (device_ != DeviceType::CUDA) throw std::runtime_error("call set_device(CUDA) first");
     if (n <= 0) return token;
+    if (token >= cfg_.vocab_size) throw std::runtime_error("token id outside the vocabulary");
     if (start_pos < 0 || (size_t)(start_pos + n) > cfg_.user_max_seq_len)
         throw std::runtime_error("chained decode runs past max_seq_len");
     rs_.compute_logits = true;
@@ -532,13 +546,14 @@ uint32_t Qwen3Model::decode_chained(uint32_t token, int start_pos, int n) {
     rs_.h_step[1] = start_pos;
     rs_.h_step[3] = 1;
     for (int i = 0; i < n; ++i) {
-        // frame 3 uploads the host record once; frame 4 continues on the device
-        const int frame = i == 0 ? 3 : 4;
+        // frame kind 3 uploads the host record once; kind 4 continues from the
+        // record the previous frame's lm_head advanced on the device
+        const int frame = frame_base_ + (i == 0 ? 3 : 4);
         const int rc = mf_begin_frame_ex(rank_, frame, i == 0 ? 0 : MF_FRAME_NO_UPLOAD);
         if (rc < 0) check(rc, "begin_frame");
         if (rc == MF_FRAME_RECORD) {
             try {
-                issue_frame(i + 1 == n);
+                issue_frame(false);
             } catch (...) {
                 mf_abort_frame(rank_);
                 throw;
@@ -546,11 +561,11 @@ uint32_t Qwen3Model::decode_chained(uint32_t token, int start_pos, int n) {
         }
         check(mf_end_frame_async(rank_), "end_frame");
     }
+    check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, 16, rs_.stream), "step readback");
     check(mf_sync(rank_), "sync");
+    const uint32_t last = (uint32_t)rs_.h_step[2];
     rs_.h_step[3] = 0;
-    int32_t rec[4];
-    std::memcpy(rec, rs_.h_step, sizeof(rec));
-    return (uint32_t)rec[2];
+    return last;
 }
 
 int Qwen3Model::read_experts(int layer, int* ids, float* w) const {

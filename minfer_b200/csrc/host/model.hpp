@@ -142,6 +142,7 @@ private:
     Config cfg_;
     RunParams rp_;
     int rank_ = 0;
+    int frame_base_ = 0;  // this model's frame ids: frame_base_ + kind
     DeviceType device_ = DeviceType::CPU;
     std::vector<std::unique_ptr<BaseLayer>> layers_;
     RunState rs_;

@@ -159,14 +159,14 @@ __global__ void rope_head_kernel(float* out, const float* in, int head, int d_he
     const int half = d_rot / 2;
     for (int i = threadIdx.x; i < half; i += blockDim.x) {
         // float pow/cos/sin (the overloads the reference's unqualified calls
-        // resolve to with <math.h> in scope); separate roundings, no FMA
+        // resolve to with <math.h> in scope)
         const float freq = 1.0f / powf(base, 2.0f * (float)i / (float)d_rot);
         const float angle = (float)pos * freq;
         const float c = cosf(angle), s = sinf(angle);
         const int a = neox ? i : 2 * i, b = neox ? i + half : 2 * i + 1;
         const float x0 = hi[a], x1 = hi[b];  // each thread owns its pair: in-place safe
-        ho[a] = __fsub_rn(__fmul_rn(c, x0), __fmul_rn(s, x1));
-        ho[b] = __fadd_rn(__fmul_rn(s, x0), __fmul_rn(c, x1));
+        ho[a] = fmaf(c, x0, -__fmul_rn(s, x1));  // first product fused, as the reference's build
+        ho[b] = fmaf(s, x0, __fmul_rn(c, x1));
     }
 }
 

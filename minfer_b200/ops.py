@@ -27,8 +27,13 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return t.data_ptr()
 
 
+_CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy: the C ABI reads a NULL stream as "manager stream"
+
+
 def _stream() -> int:
-    return torch.cuda.current_stream().cuda_stream
+    """torch's current stream as a cudaStream_t for the C ABI."""
+    s = torch.cuda.current_stream().cuda_stream
+    return s if s else _CUDA_STREAM_LEGACY
 
 
 def dtype_code(w: torch.Tensor, dtype: str | None = None) -> int:

@@ -77,7 +77,7 @@ def test_kat_matmul_offset(ops, gpu):
         res.append(out.cpu().numpy())
     np.testing.assert_allclose(res[1], res[0], atol=1e-6, rtol=0)
     np.testing.assert_allclose(res[2], res[0], atol=1e-6, rtol=0)
-    np.testing.assert_allclose(res[0], np.full(d_out, -136.0, np.float32), atol=1e-6)
+    np.testing.assert_allclose(res[0], np.full(d_out, 136.0, np.float32), atol=1e-6)  # expert 2: +1 weights
 
 
 def test_kat_rmsnorm(ops, gpu):
@@ -387,7 +387,11 @@ def test_rope_table_matches_oracle(ops, orc):
     for pos in (0, 1, 39):
         c, s = tab[pos, :, 0], tab[pos, :, 1]
         x0, x1 = x[:64], x[64:]
-        mine = np.concatenate([c * x0 - s * x1, s * x0 + c * x1]).astype(np.float32)
+        # first product fused, as the reference's compiled code contracts it
+        f64 = np.float64
+        r0 = (c.astype(f64) * x0.astype(f64) - (s * x1).astype(f64)).astype(np.float32)
+        r1 = (s.astype(f64) * x0.astype(f64) + (c * x1).astype(f64)).astype(np.float32)
+        mine = np.concatenate([r0, r1])
         np.testing.assert_array_equal(mine, orc.rope(x, 0, 128, 128, 1e6, pos))
 
 
