@@ -57,8 +57,20 @@ def dist_env():
 
 
 def model_path(workload: str) -> Path:
-    d = Path(os.environ.get("MF_MODEL_DIR", "/dev/shm" if Path("/dev/shm").is_dir() else "/tmp"))
-    return d / f"minfer_b200_{workload}.gguf"
+    """Where the synthetic GGUF lives: $MF_MODEL_DIR, else /dev/shm when it has
+    room for the file, else /tmp."""
+    import shutil
+
+    if os.environ.get("MF_MODEL_DIR"):
+        return Path(os.environ["MF_MODEL_DIR"]) / f"minfer_b200_{workload}.gguf"
+    need = CONFIGS[workload].weight_bytes() * 1.1 + (1 << 30)
+    for d in ("/dev/shm", "/tmp"):
+        p = Path(d) / f"minfer_b200_{workload}.gguf"
+        if p.exists():
+            return p
+        if Path(d).is_dir() and shutil.disk_usage(d).free > need:
+            return p
+    return Path("/tmp") / f"minfer_b200_{workload}.gguf"
 
 
 def prepare_model(workload: str, rank: int, world: int):
