@@ -36,6 +36,8 @@ constexpr int ATT_D = 128;       // head dim (Qwen3)
 constexpr int ATT_TILE = 16;     // positions per warp tile
 constexpr int ATT_WARPS = 4;
 constexpr int ATT_KSTRIDE = ATT_D + 4;  // padded K row (floats): conflict-free row-per-lane reads
+constexpr int ATT_PF_ROWS = 256;        // L2 prefetch window per CTA (rows of K and of V)
+constexpr int ATT_MIN_CHUNK = 128;      // fewest positions per split
 
 struct AttnParams {
     const float* qkv;        // [Hq*D | Hkv*D | Hkv*D] (this rank's heads)
@@ -118,10 +120,50 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) attn_decode_kernel(const AttnP
     const int pos = __ldcg(p.pos_ptr);
     const int len = pos + 1;
     const float2* cs = p.rope + (size_t)pos * (ATT_D / 2);
-    int chunk = (len + p.n_split - 1) / p.n_split;
+    // Effective split count for this context: slices of at least
+    // ATT_MIN_CHUNK positions (short contexts use fewer CTAs and a cheaper
+    // merge); CTAs past it only append K/V if they own `pos` (never: the
+    // last effective slice ends at len).
+    const int eff_split = min(p.n_split, max(1, (len + ATT_MIN_CHUNK - 1) / ATT_MIN_CHUNK));
+    if (split >= eff_split) return;
+    int chunk = (len + eff_split - 1) / eff_split;
     chunk = (chunk + ATT_TILE - 1) / ATT_TILE * ATT_TILE;
     const int start = split * chunk;
     const int end = min(start + chunk, len);
+
+    // The CTA's K and V rows are contiguous: bulk-prefetch the first
+    // ATT_PF_ROWS of each into L2 now; every tile issue below extends the
+    // window by one tile, so the cp.async stream mostly hits L2.
+    if (tid == 0 && end > start) {
+        const uint32_t nb = (uint32_t)min(end - start, ATT_PF_ROWS) * ATT_D * sizeof(float);
+        prefetch_l2(kc + (size_t)start * ATT_D, nb);
+        prefetch_l2(vc + (size_t)start * ATT_D, nb);
+    }
+    float* ks = smem + warp * AttnSmemLayout::WARP_FLOATS;
+    float* vs = ks + 2 * AttnSmemLayout::K_STAGE;
+    const int ntiles = end > start ? (end - start + ATT_TILE - 1) / ATT_TILE : 0;
+    auto issue = [&](int t, int stage) {
+        const int p0 = start + t * ATT_TILE;
+        const int nv = min(ATT_TILE, end - p0);
+        float* kd = ks + stage * AttnSmemLayout::K_STAGE;
+        float* vd = vs + stage * AttnSmemLayout::V_STAGE;
+        const int pf = p0 + ATT_PF_ROWS;  // tile entering the prefetch window
+        if (lane == 0 && pf < end) {
+            const uint32_t nb = (uint32_t)min(ATT_TILE, end - pf) * ATT_D * sizeof(float);
+            prefetch_l2(kc + (size_t)pf * ATT_D, nb);
+            prefetch_l2(vc + (size_t)pf * ATT_D, nb);
+        }
+#pragma unroll 4
+        for (int r = 0; r < nv; ++r) {
+            cp_async16(kd + r * ATT_KSTRIDE + 4 * lane, kc + (size_t)(p0 + r) * ATT_D + 4 * lane);
+            cp_async16(vd + r * ATT_D + 4 * lane, vc + (size_t)(p0 + r) * ATT_D + 4 * lane);
+        }
+        cp_async_commit();
+    };
+    // The warp's first tile does not depend on the queries: start its copy
+    // now, unless it holds row `pos` (written by the append below).
+    const bool early = warp < ntiles && (start + (warp + 1) * ATT_TILE <= pos);
+    if (early) issue(warp, 0);
 
     // ---- prologue: normalised + rotated queries of this group
     for (int g = warp; g < G; g += ATT_WARPS) {
@@ -143,22 +185,6 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) attn_decode_kernel(const AttnP
     __syncthreads();
 
     const float scale = 1.0f / sqrtf((float)ATT_D);  // src/ops/kernels.cpp:88
-    float* ks = smem + warp * AttnSmemLayout::WARP_FLOATS;
-    float* vs = ks + 2 * AttnSmemLayout::K_STAGE;
-
-    const int ntiles = end > start ? (end - start + ATT_TILE - 1) / ATT_TILE : 0;
-    auto issue = [&](int t, int stage) {
-        const int p0 = start + t * ATT_TILE;
-        const int nv = min(ATT_TILE, end - p0);
-        float* kd = ks + stage * AttnSmemLayout::K_STAGE;
-        float* vd = vs + stage * AttnSmemLayout::V_STAGE;
-#pragma unroll 4
-        for (int r = 0; r < nv; ++r) {
-            cp_async16(kd + r * ATT_KSTRIDE + 4 * lane, kc + (size_t)(p0 + r) * ATT_D + 4 * lane);
-            cp_async16(vd + r * ATT_D + 4 * lane, vc + (size_t)(p0 + r) * ATT_D + 4 * lane);
-        }
-        cp_async_commit();
-    };
 
     float m[G], l[G];
     float4 o[G];
@@ -171,7 +197,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) attn_decode_kernel(const AttnP
 
     const int j = lane & 15, half = lane >> 4;
     int stage = 0;
-    if (warp < ntiles) issue(warp, 0);
+    if (warp < ntiles && !early) issue(warp, 0);
     for (int t = warp; t < ntiles; t += ATT_WARPS) {
         const int tn = t + ATT_WARPS;
         if (tn < ntiles) {
@@ -248,6 +274,23 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) attn_decode_kernel(const AttnP
         }
     }
     __syncthreads();
+    if (eff_split == 1) {  // one slice: finish here, no partials
+        for (int idx = tid; idx < G * ATT_D; idx += ATT_WARPS * 32) {
+            const int g = idx / ATT_D, d = idx - g * ATT_D;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < ATT_WARPS; ++w) M = fmaxf(M, wm[w][g]);
+            float acc = 0.f, L = 0.f;
+#pragma unroll
+            for (int w = 0; w < ATT_WARPS; ++w) {
+                const float f = (wm[w][g] == -INFINITY) ? 0.f : expf(wm[w][g] - M);
+                acc = fmaf(f, wo[((size_t)w * G + g) * ATT_D + d], acc);
+                L = fmaf(f, wl[w][g], L);
+            }
+            p.out[((size_t)kvh * G + g) * ATT_D + d] = acc / L;
+        }
+        return;
+    }
     const size_t pbase = ((size_t)kvh * p.n_split + split) * G;
     for (int idx = tid; idx < G * ATT_D; idx += ATT_WARPS * 32) {
         const int g = idx / ATT_D, d = idx - g * ATT_D;
@@ -275,28 +318,49 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) attn_decode_kernel(const AttnP
     if (tid == 0) {
         __threadfence();
         const int ticket = atomicAdd(p.counters + kvh, 1);
-        is_last = (ticket == p.n_split - 1);
+        is_last = (ticket == eff_split - 1);
     }
     __syncthreads();
     if (!is_last) return;
     __threadfence();
+    // merge in three parallel passes through shared memory (the warp stages
+    // are free now): (m, l) of every split, then the per-split scale factors,
+    // then the weighted sum of the partial outputs with independent loads.
+    const int ns = eff_split;
+    float* ml = smem;                    // [ns][G][2]
+    float* fs = smem + 2 * ns * G;       // [G][ns] scale factors
+    float* Ls = fs + ns * G;             // [G] denominators
+    const size_t hb = (size_t)kvh * p.n_split * G;
+    for (int i = tid; i < ns * G * 2; i += ATT_WARPS * 32) ml[i] = __ldcg(p.part_ml + hb * 2 + i);
+    __syncthreads();
+    if (tid < G) {
+        const int g = tid;
+        float M = -INFINITY;
+        for (int sidx = 0; sidx < ns; ++sidx) M = fmaxf(M, ml[(sidx * G + g) * 2]);
+        float L = 0.f;
+        for (int sidx = 0; sidx < ns; ++sidx) {
+            const float ms = ml[(sidx * G + g) * 2];
+            const float f = (ms == -INFINITY) ? 0.f : expf(ms - M);
+            fs[g * ns + sidx] = f;
+            L = fmaf(f, ml[(sidx * G + g) * 2 + 1], L);
+        }
+        Ls[g] = L;
+    }
+    __syncthreads();
     for (int idx = tid; idx < G * ATT_D; idx += ATT_WARPS * 32) {
         const int g = idx / ATT_D, d = idx - g * ATT_D;
-        float M = -INFINITY;
-        for (int sidx = 0; sidx < p.n_split; ++sidx) {
-            const size_t b = ((size_t)kvh * p.n_split + sidx) * G + g;
-            M = fmaxf(M, __ldcg(p.part_ml + b * 2));
+        const float* po = p.part_o + (hb + g) * ATT_D + d;
+        const float* f = fs + g * ns;
+        float acc = 0.f;
+        for (int s0 = 0; s0 < ns; s0 += 16) {
+            float o[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) o[u] = (s0 + u < ns) ? __ldcg(po + (size_t)(s0 + u) * G * ATT_D) : 0.f;
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+                if (s0 + u < ns) acc = fmaf(f[s0 + u], o[u], acc);
         }
-        float acc = 0.f, L = 0.f;
-        for (int sidx = 0; sidx < p.n_split; ++sidx) {
-            const size_t b = ((size_t)kvh * p.n_split + sidx) * G + g;
-            const float ms = __ldcg(p.part_ml + b * 2);
-            if (ms == -INFINITY) continue;
-            const float f = expf(ms - M);
-            acc = fmaf(f, __ldcg(p.part_o + b * ATT_D + d), acc);
-            L = fmaf(f, __ldcg(p.part_ml + b * 2 + 1), L);
-        }
-        p.out[((size_t)kvh * G + g) * ATT_D + d] = acc / L;
+        p.out[((size_t)kvh * G + g) * ATT_D + d] = acc / Ls[g];
     }
     if (tid == 0) p.counters[kvh] = 0;
 }

@@ -106,8 +106,32 @@ cudaStream_t resolve(void* s) {
     return (cudaStream_t)0;
 }
 
+// Launch-shape knobs for tuning sweeps (defaults are the tuned values):
+// MF_GEMV_CTAS_PER_SM caps resident GEMV CTAs per SM (0 = occupancy limit),
+// MF_GEMV_PF_TILES sets the L2 prefetch depth in tiles.
+int env_int(const char* name, int dflt) {
+    const char* e = std::getenv(name);
+    return (e && *e) ? std::atoi(e) : dflt;
+}
+
+// Optional uniform shared-memory carveout for every kernel of the token loop
+// (MF_CARVEOUT=percent): consecutive kernels then never make an SM drain to
+// reconfigure L1/shared. Off by default (measured slower on B200).
+void set_carveout_once(const void* fn) {
+    static const int carveout = env_int("MF_CARVEOUT", -1);  // -1: driver default, else percent
+    if (carveout < 0) return;
+    static std::set<std::pair<int, const void*>> done;
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.insert({dev, fn}).second)
+        cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, carveout);
+}
+
 // Launch with the programmatic-serialization attribute.
 cudaError_t launch(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
+    set_carveout_once(fn);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -190,6 +214,9 @@ void choose_shape(int K, int dtype, int ym, int* T_out, int* R_out) {
 }
 
 int run_gemv(int dtype, int xm, int ym, mf::GemvParams& p, long long units, cudaStream_t st, int max_grid = 0) {
+    static const int cps_cap = env_int("MF_GEMV_CTAS_PER_SM", 0);
+    static const int pf_tiles = env_int("MF_GEMV_PF_TILES", 2);
+    p.pf_tiles = pf_tiles;
     MF_REQUIRE(p.K > 0 && p.K % 16 == 0, MF_E_INVALID, "d_in must be a positive multiple of 16 (got %d)", p.K);
     MF_REQUIRE(p.rows > 0, MF_E_INVALID, "d_out must be positive");
     MF_REQUIRE(((uintptr_t)p.w + p.w_offset * esz_of(dtype)) % 16 == 0, MF_E_INVALID,
@@ -205,6 +232,7 @@ int run_gemv(int dtype, int xm, int ym, mf::GemvParams& p, long long units, cuda
     int bps = 0;
     int rc = prepare(fn, T, smem, &bps);
     if (rc) return rc;
+    if (cps_cap > 0 && bps > cps_cap) bps = cps_cap;
     long long grid = (long long)num_sms() * bps;
     if (grid > units) grid = units;
     if (max_grid > 0 && grid > max_grid) grid = max_grid;

@@ -50,10 +50,15 @@ struct GemvParams {
     int* counter;               // zero-initialised; reset by the last CTA
     int* step;                  // device step record {token, pos, next_token, chain}
     int vocab_offset;           // index of row 0 (vocab-split lm_head)
+    int pf_tiles;               // L2 prefetch depth in tiles (tiles <= 48 KB)
 };
 
+#ifndef MF_GEMV_MIN_BLOCKS
+#define MF_GEMV_MIN_BLOCKS 1
+#endif
+
 template <typename W, int T, int R, int PC, int XM, int YM>
-__global__ void __launch_bounds__(T) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(T, MF_GEMV_MIN_BLOCKS) gemv_kernel(const GemvParams p) {
     constexpr int VEC = W::VEC;
     constexpr int NW = T / 32;
     constexpr int RU = (YM == Y_SWIGLU) ? 2 : 1;  // rows per unit
@@ -91,8 +96,33 @@ __global__ void __launch_bounds__(T) gemv_kernel(const GemvParams p) {
 #pragma unroll
     for (int r = 0; r < R; ++r) eid[r] = 0;
 
+    constexpr size_t CSTRIDE = (size_t)T * VEC * esz;  // bytes between a thread's passes
+    const bool k_exact = (K % STEP_COLS) == 0;
     auto load = [&](uint4 (&buf)[R][PC], int it) {
         const int tile = it / nsteps, step = it - tile * nsteps;
+        const size_t coff = ((size_t)(step * PC) * T + tid) * VEC * esz;
+        if (!indirect) {
+            const int r0 = rows0 + tile * R;
+            const char* tp = wbase + (size_t)r0 * row_bytes + coff;
+            if (k_exact && r0 + R <= rows1) {
+                // full tile: every lane loads, addresses are base + constants
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+#pragma unroll
+                    for (int c = 0; c < PC; ++c) buf[r][c] = ld_stream(tp + r * row_bytes + c * CSTRIDE);
+                return;
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+#pragma unroll
+                for (int c = 0; c < PC; ++c) {
+                    const int col = ((step * PC + c) * T + tid) * VEC;
+                    if (r0 + r < rows1 && col < K) buf[r][c] = ld_stream(tp + r * row_bytes + c * CSTRIDE);
+                    else buf[r][c] = make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            return;
+        }
 #pragma unroll
         for (int r = 0; r < R; ++r) {
             bool valid;
@@ -104,26 +134,39 @@ __global__ void __launch_bounds__(T) gemv_kernel(const GemvParams p) {
             } else {
                 const int lr = rows0 + tile * R + r;
                 valid = lr < rows1;
-                phys = lr;
-                if (indirect) {
-                    const int slot = lr / p.rows_per_expert;
-                    phys = (long long)__ldcg(p.expert_ids + slot) * p.rows_per_expert +
-                           (lr - slot * p.rows_per_expert);
-                }
+                const int slot = lr / p.rows_per_expert;
+                phys = valid ? (long long)__ldcg(p.expert_ids + slot) * p.rows_per_expert +
+                                   (lr - slot * p.rows_per_expert)
+                             : 0;
             }
-            const char* rp = wbase + phys * row_bytes;
+            const char* rp = wbase + phys * row_bytes + coff;
 #pragma unroll
             for (int c = 0; c < PC; ++c) {
                 const int col = ((step * PC + c) * T + tid) * VEC;
-                if (valid && col < K) buf[r][c] = ld_stream(rp + (size_t)col * esz);
+                if (valid && col < K) buf[r][c] = ld_stream(rp + c * CSTRIDE);
                 else buf[r][c] = make_uint4(0u, 0u, 0u, 0u);
             }
         }
     };
 
+    // L2 prefetch window (dense weights): the CTA's rows are one contiguous
+    // byte range, so one bulk prefetch per tile keeps `pf_ahead` tiles in
+    // flight ahead of the register loads without holding registers.
+    const size_t tile_bytes = (size_t)R * row_bytes;
+    const int pf_ahead = indirect ? -1
+                                  : (tile_bytes <= 48 * 1024 ? p.pf_tiles : (tile_bytes <= 128 * 1024 ? 1 : -1));
+    auto prefetch_tile = [&](int t) {
+        if (t >= ntiles) return;
+        const int r0 = rows0 + t * R;
+        const int r1 = min(r0 + R, rows1);
+        prefetch_l2(wbase + (size_t)r0 * row_bytes, (uint32_t)((size_t)(r1 - r0) * row_bytes));
+    };
+
     uint4 bufA[R][PC], bufB[R][PC];
     // Dense weights do not depend on earlier kernels: start streaming them
     // before the dependency wait. Expert ids come from the router kernel.
+    if (tid == 0)
+        for (int t = 0; t <= pf_ahead; ++t) prefetch_tile(t);
     if (!indirect && nitems > 0) load(bufA, 0);
     pdl_launch_dependents();
     pdl_wait();
@@ -264,13 +307,26 @@ __global__ void __launch_bounds__(T) gemv_kernel(const GemvParams p) {
         par ^= 1;
     };
 
+    auto advance_prefetch = [&](int it) {
+        if (pf_ahead >= 0 && tid == 0 && it % nsteps == 0) prefetch_tile(it / nsteps + pf_ahead + 1);
+    };
+#ifdef MF_GEMV_SINGLE_BUFFER
+    for (int it = 0; it < nitems; ++it) {
+        advance_prefetch(it);
+        if (it > 0) load(bufA, it);
+        consume(bufA, it);
+    }
+#else
     for (int it = 0; it < nitems; it += 2) {
+        advance_prefetch(it);
         if (it + 1 < nitems) load(bufB, it + 1);
         consume(bufA, it);
         if (it + 1 >= nitems) break;
+        advance_prefetch(it + 1);
         if (it + 2 < nitems) load(bufA, it + 2);
         consume(bufB, it + 1);
     }
+#endif
 
     // ---- greedy argmax finisher: the last CTA reduces the per-CTA candidates
     if (YM == Y_STORE && p.counter != nullptr) {

@@ -51,6 +51,12 @@ MF_DEVICE uint4 ld_stream(const void* p) {
     return r;
 }
 
+// TMA bulk prefetch of [p, p+bytes) into L2 (p 16-byte aligned, bytes a
+// multiple of 16). Issued by one thread; nothing waits on it.
+MF_DEVICE void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // L2-coherent loads (bypass L1) for data written by other CTAs of the same grid.
 MF_DEVICE float ld_cg(const float* p) { return __ldcg(p); }
 MF_DEVICE int ld_cg(const int* p) { return __ldcg(p); }

@@ -1,0 +1,116 @@
+"""Single-kernel timing of the token-loop ops on synthetic operands.
+
+    python -m minfer_b200.perf gemv --rows 24576 --k 4096 --mode swiglu
+    python -m minfer_b200.perf attn --hq 32 --hkv 8 --ctx 4096
+
+Prints one JSON line per case: average device time per launch (CUDA events
+around a CUDA-graph replay of `--iters` launches on torch's stream, after
+warm-up launches) and the algorithmic bytes per launch divided by that time. Operand sets larger than L2 are rotated between launches
+(`--copies`) so every launch streams from HBM.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import model as mm
+
+
+def _time(fn, iters: int, warmup: int) -> float:
+    """Average device time per launch: the `iters` launches are captured into
+    one CUDA graph and replayed, so host launch cost is not measured."""
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(iters):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters * 1e3  # us
+
+
+def gemv(args) -> dict:
+    from . import ops
+
+    tdt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[args.dtype]
+    esz = 4 if args.dtype == "f32" else 2
+    K, rows = args.k, args.rows
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ws = [(torch.randn(rows, K, generator=g, device="cuda") * 0.02).to(tdt) for _ in range(args.copies)]
+    x = torch.randn(K, generator=g, device="cuda")
+    nw = torch.ones(K, device="cuda")
+    if args.mode == "swiglu":
+        out = torch.empty(rows // 2, device="cuda")
+        fn = lambda i: ops.swiglu_matmul(out, x, nw, 1e-6, ws[i % len(ws)], rows // 2, K)
+        extra = 2 * K * 4 + rows // 2 * 4
+    elif args.mode == "norm":
+        out = torch.empty(rows, device="cuda")
+        fn = lambda i: ops.rmsnorm_matmul(out, x, nw, 1e-6, ws[i % len(ws)], rows, K)
+        extra = 2 * K * 4 + rows * 4
+    else:
+        out = torch.zeros(rows, device="cuda")
+        fn = lambda i: ops.matmul_residual(out, x, ws[i % len(ws)], rows, K)
+        extra = K * 4 + 2 * rows * 4
+    us = _time(fn, args.iters, args.warmup)
+    algo = rows * K * esz + extra
+    return {"op": f"gemv-{args.mode}", "rows": rows, "k": K, "dtype": args.dtype, "us": round(us, 2),
+            "algo_bytes": algo, "gbs": round(algo / us / 1e3, 1)}
+
+
+def attn(args) -> dict:
+    from . import ops
+
+    H, Hkv, D, ctx = args.hq, args.hkv, 128, args.ctx
+    S = ctx + 16
+    g = torch.Generator(device="cuda").manual_seed(0)
+    kcs = [torch.randn(Hkv * S * D, generator=g, device="cuda") for _ in range(args.copies)]
+    vcs = [torch.randn(Hkv * S * D, generator=g, device="cuda") for _ in range(args.copies)]
+    qkv = torch.randn((H + 2 * Hkv) * D, generator=g, device="cuda")
+    nw = torch.ones(D, device="cuda")
+    rope = ops.rope_table(S, D, 1e6).cuda()
+    split = args.split or ops.attn_default_split(Hkv, S)
+    wsp = torch.zeros(ops.attn_workspace_bytes(H, Hkv, D, split) // 4 + 1, dtype=torch.int32, device="cuda")
+    st = torch.tensor([0, ctx, 0, 0], dtype=torch.int32, device="cuda")
+    out = torch.empty(H * D, device="cuda")
+    fn = lambda i: ops.attn_decode(qkv, nw, nw, 1e-6, rope, kcs[i % len(kcs)], vcs[i % len(vcs)], S, st, out, H,
+                                   Hkv, D, split, wsp)
+    us = _time(fn, args.iters, args.warmup)
+    algo = 2 * Hkv * (ctx + 1) * D * 4 + (H + 2 * Hkv) * D * 4 + H * D * 4
+    return {"op": "attn-decode", "hq": H, "hkv": Hkv, "ctx": ctx, "split": split, "us": round(us, 2),
+            "algo_bytes": algo, "gbs": round(algo / us / 1e3, 1)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="what", required=True)
+    a = sub.add_parser("gemv")
+    a.add_argument("--rows", type=int, default=24576)
+    a.add_argument("--k", type=int, default=4096)
+    a.add_argument("--dtype", default="bf16")
+    a.add_argument("--mode", default="swiglu", choices=["swiglu", "norm", "resid"])
+    b = sub.add_parser("attn")
+    b.add_argument("--hq", type=int, default=32)
+    b.add_argument("--hkv", type=int, default=8)
+    b.add_argument("--ctx", type=int, default=4096)
+    b.add_argument("--split", type=int, default=0)
+    for p in (a, b):
+        p.add_argument("--iters", type=int, default=20)
+        p.add_argument("--warmup", type=int, default=5)
+        p.add_argument("--copies", type=int, default=2)
+    args = ap.parse_args()
+    mm.init(1, [torch.cuda.current_device()])
+    res = gemv(args) if args.what == "gemv" else attn(args)
+    print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()
