@@ -186,6 +186,19 @@ size_t mf_attn_workspace_bytes(int n_heads, int n_kv_heads, int d_head, int n_sp
 int mf_attn_default_split(int n_kv_heads, int max_seq);
 int mf_attn_decode(const mf_attn_desc* desc, void* stream);
 
+/* Decode attention for callers that cannot allocate device memory (no
+ * counterpart in the reference). Same computation and descriptor as
+ * mf_attn_decode, but desc->workspace is ignored: the scratch is a static
+ * device array of MF_ATTN_NOALLOC_SCRATCH_BYTES that every GPU loading this
+ * library keeps until exit. For code that must not call cudaMalloc, e.g.
+ * while a stream is captured in global mode, inside stream callbacks, or
+ * when another runtime owns the device memory. The first call on a device
+ * caches the array's address (make it before any stream capture); calls that
+ * overlap on the GPU race on the shared array; a request needing more scratch
+ * than the array holds returns MF_E_UNSUPPORTED. Allocates nothing. */
+#define MF_ATTN_NOALLOC_SCRATCH_BYTES (1u << 20)
+int mf_attn_decode_noalloc(const mf_attn_desc* desc, void* stream);
+
 /* MoE router + top-k + renormalisation (module.cpp:446-457, kernels.cpp:113-139):
  * scores = W_router(f32 [E, d]) · rmsnorm(x); ids/weights of the k best. */
 int mf_router_topk(int* ids, float* weights, float* scores, const float* x, const float* norm_w, float eps,

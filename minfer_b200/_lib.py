@@ -117,6 +117,7 @@ CUDA_API = {
     "mf_attn_workspace_bytes": (SZ, [I, I, I, I]),
     "mf_attn_default_split": (I, [I, I]),
     "mf_attn_decode": (I, [P, P]),
+    "mf_attn_decode_noalloc": (I, [P, P]),
     "mf_router_topk": (I, [P, P, P, P, P, F, P, I, I, I, P]),
     "mf_moe_swiglu": (I, [P, P, P, F, P, I, P, I, I, I, P]),
     "mf_moe_down_residual": (I, [P, P, P, I, P, P, I, I, I, P]),

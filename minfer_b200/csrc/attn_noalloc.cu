@@ -1,0 +1,121 @@
+// mf_attn_decode_noalloc: the decode-attention op for callers that cannot
+// allocate device memory.
+//
+// mf_attn_decode needs a caller-provided workspace (per-split partial results
+// and completion counters). Some callers cannot obtain one: code that issues
+// work while a stream is being captured in global mode (where cudaMalloc is
+// not permitted), code running in stream callbacks or other contexts where
+// CUDA allocation calls are forbidden, and hosts whose device memory is owned
+// by another runtime's allocator or a fixed budget. This entry point takes
+// only the inputs and outputs; its scratch is one file-scope device array of
+// MF_ATTN_NOALLOC_SCRATCH_BYTES bytes that every GPU loading this library
+// holds until the process exits.
+//
+// Properties a caller must know:
+//  * The first call on a device looks up the array's device address
+//    (cudaGetSymbolAddress, with that device current) and caches it; make that
+//    first call before any stream capture on the device.
+//  * The array is shared by every call. It keeps the last call's contents;
+//    the completion counters are cleared at the start of each call on the
+//    caller's stream. Calls whose executions overlap on the GPU (different
+//    streams, no ordering between them) race on the array and give wrong
+//    results.
+//  * A request whose scratch would exceed MF_ATTN_NOALLOC_SCRATCH_BYTES is
+//    rejected with MF_E_UNSUPPORTED; nothing is launched.
+//  * It calls no cudaMalloc, cudaFree or other allocating routine.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "attention.cuh"
+#include "minfer_cuda.h"
+
+namespace mf {
+const void* attn_kernel_ptr(int group);
+int record_error(int code, const char* msg);  // capi.cu: message for mf_last_error
+cudaStream_t resolve_stream(void* stream);    // capi.cu: NULL -> manager stream of the current device
+}
+
+namespace {
+
+constexpr size_t kCounterBytes = 256;  // room for 64 KV heads' counters
+static __device__ __align__(256) unsigned char g_attn_scratch[MF_ATTN_NOALLOC_SCRATCH_BYTES];
+
+int noalloc_fail(int code, const char* msg) { return mf::record_error(code, msg); }
+
+// Device address of g_attn_scratch for the current device (looked up once).
+int scratch_address(void** out) {
+    static std::mutex mu;
+    static void* addr[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return noalloc_fail(MF_E_CUDA, "no usable current device");
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_scratch);
+        if (e != cudaSuccess) return noalloc_fail(MF_E_CUDA, cudaGetErrorString(e));
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return MF_OK;
+}
+
+}  // namespace
+
+extern "C" int mf_attn_decode_noalloc(const mf_attn_desc* d, void* stream) {
+    if (!d) return noalloc_fail(MF_E_INVALID, "null descriptor");
+    if (!(d->qkv && d->q_norm_w && d->k_norm_w && d->rope_table && d->k_cache && d->v_cache && d->step_state &&
+          d->out))
+        return noalloc_fail(MF_E_INVALID, "null pointer in attention descriptor");
+    if (d->d_head != mf::ATT_D) return noalloc_fail(MF_E_UNSUPPORTED, "d_head must be 128");
+    if (d->n_kv_heads <= 0 || d->n_heads % d->n_kv_heads != 0)
+        return noalloc_fail(MF_E_INVALID, "n_heads must be a multiple of n_kv_heads");
+    if (d->n_split < 1 || d->max_seq < 1) return noalloc_fail(MF_E_INVALID, "bad n_split/max_seq");
+    const int G = d->n_heads / d->n_kv_heads;
+    const void* fn = mf::attn_kernel_ptr(G);
+    if (!fn) return noalloc_fail(MF_E_UNSUPPORTED, "query heads per KV head without a kernel");
+    // scratch layout: counters | (m, l) per split and head | partial outputs
+    const size_t pml = ((size_t)d->n_kv_heads * d->n_split * G * 2 * sizeof(float) + 255) / 256 * 256;
+    const size_t po = (size_t)d->n_kv_heads * d->n_split * G * mf::ATT_D * sizeof(float);
+    if ((size_t)d->n_kv_heads * sizeof(int) > kCounterBytes || kCounterBytes + pml + po > MF_ATTN_NOALLOC_SCRATCH_BYTES)
+        return noalloc_fail(MF_E_UNSUPPORTED, "request needs more scratch than MF_ATTN_NOALLOC_SCRATCH_BYTES");
+    void* base = nullptr;
+    int rc = scratch_address(&base);
+    if (rc) return rc;
+    cudaStream_t st = mf::resolve_stream(stream);
+    char* ws = (char*)base;
+    // the counters must start at zero; a previous call may have been cut short
+    cudaError_t e = cudaMemsetAsync(ws, 0, kCounterBytes, st);
+    if (e != cudaSuccess) return noalloc_fail(MF_E_CUDA, cudaGetErrorString(e));
+    const size_t smem = mf::attn_smem_bytes();
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return noalloc_fail(MF_E_CUDA, cudaGetErrorString(e));
+    mf::AttnParams p = {};
+    p.qkv = d->qkv;
+    p.q_norm_w = d->q_norm_w;
+    p.k_norm_w = d->k_norm_w;
+    p.eps = d->eps;
+    p.rope = (const float2*)d->rope_table;
+    p.k_cache = d->k_cache;
+    p.v_cache = d->v_cache;
+    p.max_seq = d->max_seq;
+    p.pos_ptr = (const int*)d->step_state + 1;  // {token, pos, next_token, chain}
+    p.out = d->out;
+    p.counters = (int*)ws;
+    p.part_ml = (float*)(ws + kCounterBytes);
+    p.part_o = (float*)(ws + kCounterBytes + pml);
+    p.n_heads = d->n_heads;
+    p.n_kv_heads = d->n_kv_heads;
+    p.n_split = d->n_split;
+    void* args[] = {&p};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(d->n_split, d->n_kv_heads);
+    cfg.blockDim = dim3(mf::ATT_WARPS * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    e = cudaLaunchKernelExC(&cfg, fn, args);
+    if (e != cudaSuccess) return noalloc_fail(MF_E_CUDA, cudaGetErrorString(e));
+    return MF_OK;
+}

@@ -248,6 +248,12 @@ constexpr int LMH_MAX_GRID = 4096;
 
 }  // namespace
 
+namespace mf {
+// Used by entry points compiled in other files of this library.
+int record_error(int code, const char* msg) { return fail(code, "%s", msg); }
+cudaStream_t resolve_stream(void* stream) { return resolve(stream); }
+}  // namespace mf
+
 extern "C" {
 
 // ===================================================================== manager
