@@ -106,6 +106,13 @@ int mf_model_experts(const mf_model* m, int layer, int* ids, float* weights);
 int mf_model_kv(const mf_model* m, int layer, float* k, float* v, int n_pos);
 int mf_model_x(const mf_model* m, float* x);
 
+/* The host sampler alone (Sampler::sample, src/base/sampler.cpp:34-117): a
+ * fresh sampler with rp's settings, the `n_seen` ids of `seen` added for the
+ * presence penalty, then `n_draws` draws from the same logits (the RNG
+ * advances between draws). No GPU involved. */
+int mf_sample(const float* logits, size_t vocab, const mf_run_params* rp, const uint32_t* seen, size_t n_seen,
+              size_t n_draws, uint32_t* out);
+
 /* Prompt ids as BaseModel::benchmark draws them (src/base/model.cpp:189-193):
  * std::mt19937(seed) + std::uniform_int_distribution<>(0, vocab-1). */
 int mf_random_prompt(int seed, uint32_t vocab, size_t n, uint32_t* out);

@@ -151,6 +151,7 @@ HOST_API = {
     "mf_model_kv": (I, [P, I, P, P, I]),
     "mf_model_x": (I, [P, P]),
     "mf_random_prompt": (I, [I, U32, SZ, P]),
+    "mf_sample": (I, [P, SZ, P, P, SZ, SZ, P]),
 }
 
 _cuda = None

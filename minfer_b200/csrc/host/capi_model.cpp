@@ -190,6 +190,25 @@ int mf_model_x(const mf_model* m, float* x) {
     return m->m->read_x(x);
 }
 
+int mf_sample(const float* logits, size_t vocab, const mf_run_params* rp, const uint32_t* seen, size_t n_seen,
+              size_t n_draws, uint32_t* out) {
+    if (!logits || !rp || !out || vocab == 0 || (n_seen && !seen)) return herr(MF_E_INVALID, "bad arguments");
+    MF_TRY({
+        minfer::SamplerParams sp;
+        sp.vocab_size = vocab;
+        sp.top_k = rp->top_k;
+        sp.temp = rp->temp;
+        sp.top_p = rp->top_p;
+        sp.min_p = rp->min_p;
+        sp.penalty_pres = rp->penalty_pres;
+        sp.seed = rp->seed;
+        minfer::Sampler smp(sp);
+        for (size_t i = 0; i < n_seen; ++i) smp.add_token(seen[i]);
+        for (size_t i = 0; i < n_draws; ++i) out[i] = smp.sample(logits);
+    });
+    return MF_OK;
+}
+
 int mf_random_prompt(int seed, uint32_t vocab, size_t n, uint32_t* out) {
     if (!out || vocab == 0) return herr(MF_E_INVALID, "bad arguments");
     std::mt19937 gen(seed);

@@ -165,8 +165,13 @@ __global__ void rope_head_kernel(float* out, const float* in, int head, int d_he
         const float c = cosf(angle), s = sinf(angle);
         const int a = neox ? i : 2 * i, b = neox ? i + half : 2 * i + 1;
         const float x0 = hi[a], x1 = hi[b];  // each thread owns its pair: in-place safe
-        ho[a] = fmaf(c, x0, -__fmul_rn(s, x1));  // first product fused, as the reference's build
-        ho[b] = fmaf(s, x0, __fmul_rn(c, x1));
+        if (neox) {  // first product fused, as the reference's build evaluates it
+            ho[a] = fmaf(c, x0, -__fmul_rn(s, x1));
+            ho[b] = fmaf(s, x0, __fmul_rn(c, x1));
+        } else {  // separate roundings
+            ho[a] = __fsub_rn(__fmul_rn(c, x0), __fmul_rn(s, x1));
+            ho[b] = __fadd_rn(__fmul_rn(s, x0), __fmul_rn(c, x1));
+        }
     }
 }
 

@@ -102,23 +102,34 @@ void orc_softmax(float* out, const float* in, int n) {
 // The reference calls unqualified pow/cos/sin on floats; with <math.h> in
 // scope (libc++ on its own platform, and the libstdc++ build of the reference
 // here) those are the float overloads, so the whole rotation is float math.
-static void rope_impl(float* out, const float* in, int head, int d_head, int d_rot, float base, int pos, bool neox) {
+// The reference build evaluates the interleaved rotation with separate
+// roundings (no contraction), the NeoX one with the first product fused:
+// each restatement reproduces its counterpart.
+__attribute__((optimize("fp-contract=off")))
+void orc_il_rope(float* out, const float* in, int head, int d_head, int d_rot, float base, int pos) {
     const float* hi = in + head * d_head;
     float* ho = out + head * d_head;
     for (int i = 0; i < d_rot / 2; ++i) {
         const float freq = 1.0f / powf(base, 2.0f * i / d_rot);
         const float angle = pos * freq;
-        const int a = neox ? i : 2 * i, b = neox ? i + d_rot / 2 : 2 * i + 1;
-        const float x0 = hi[a], x1 = hi[b];
-        ho[a] = cosf(angle) * x0 - sinf(angle) * x1;
-        ho[b] = sinf(angle) * x0 + cosf(angle) * x1;
+        const float x0 = hi[2 * i];
+        const float x1 = hi[2 * i + 1];
+        ho[2 * i] = cosf(angle) * x0 - sinf(angle) * x1;
+        ho[2 * i + 1] = sinf(angle) * x0 + cosf(angle) * x1;
     }
 }
+
 void orc_neox_rope(float* out, const float* in, int head, int d_head, int d_rot, float base, int pos) {
-    rope_impl(out, in, head, d_head, d_rot, base, pos, true);
-}
-void orc_il_rope(float* out, const float* in, int head, int d_head, int d_rot, float base, int pos) {
-    rope_impl(out, in, head, d_head, d_rot, base, pos, false);
+    const float* hi = in + head * d_head;
+    float* ho = out + head * d_head;
+    for (int i = 0; i < d_rot / 2; ++i) {
+        const float freq = 1.0f / powf(base, 2.0f * i / d_rot);
+        const float angle = pos * freq;
+        const float x0 = hi[i];
+        const float x1 = hi[i + d_rot / 2];
+        ho[i] = cosf(angle) * x0 - sinf(angle) * x1;
+        ho[i + d_rot / 2] = sinf(angle) * x0 + cosf(angle) * x1;
+    }
 }
 
 // src/ops/kernels.cpp:83-110

@@ -1,0 +1,165 @@
+"""Host-side pieces on the CPU: the C-ABI libraries load and export every
+symbol their headers declare; the GGUF reader accepts the synthetic models
+and rejects malformed files with a status and a message; the prompt-id draw,
+the RoPE table and the sampler agree with the oracle. No kernel is launched.
+"""
+import ctypes as C
+import re
+import struct
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from conftest import TINY, tiny_model
+from minfer_b200._lib import (HOST_API, CUDA_API, MF_E_INVALID, MF_OK, cuda_lib, host_lib, last_error,
+                              mf_model_info, mf_run_params)
+from minfer_b200.gguf_synth import Qwen3Shape, random_prompt, write_qwen3_gguf
+from oracle.oracle_py import PortModel, PortOps
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def header_functions(name: str) -> set[str]:
+    text = (ROOT / "include" / name).read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"^\s*(?:int|void\*?|size_t)\s+\*?(mf_\w+)\s*\(", text, flags=re.M))
+
+
+def test_every_declared_symbol_is_exported():
+    cuda, host = cuda_lib(), host_lib()
+    for hdr, lib in (("minfer_cuda.h", cuda), ("minfer_model.h", host)):
+        names = header_functions(hdr)
+        assert len(names) > 10
+        for n in sorted(names):
+            assert hasattr(lib, n), f"{n} declared in {hdr} but not exported"
+    # the ctypes prototype table covers the headers exactly
+    assert header_functions("minfer_cuda.h") == set(CUDA_API)
+    assert header_functions("minfer_model.h") == set(HOST_API)
+
+
+def load(path, **kw):
+    rp = mf_run_params(kw.get("num_iters", 8), kw.get("max_seq", 64), kw.get("top_k", 1), kw.get("temp", 0.0),
+                       kw.get("top_p", 1.0), 0.0, 0.0, kw.get("seed", 0))
+    m = C.c_void_p()
+    rc = host_lib().mf_model_load(str(path).encode(), C.byref(rp), 0, C.byref(m))
+    return rc, m
+
+
+@pytest.mark.parametrize("name", list(TINY))
+def test_gguf_config(name):
+    rc, m = load(tiny_model(name))
+    assert rc == MF_OK, last_error()
+    info = mf_model_info()
+    assert host_lib().mf_model_info_get(m, C.byref(info)) == MF_OK
+    cfg = TINY[name]
+    assert (info.d_model, info.n_layers, info.n_heads, info.n_kv_heads, info.d_head, info.d_ff) == (
+        cfg.d_model, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.d_head, cfg.d_ff)
+    assert (info.n_experts, info.n_active_experts, info.vocab_size) == (cfg.n_experts, cfg.n_active, cfg.vocab)
+    assert info.untied_head == (0 if cfg.tied else 1)
+    assert info.weight_dtype == {"f32": 0, "f16": 1, "bf16": 2}[cfg.dtype]
+    assert abs(info.freq_base - 1e6) < 1 and abs(info.rms_norm_eps - 1e-6) < 1e-12
+    host_lib().mf_model_free(m)
+
+
+def _corrupt(tmp_path, fn, data: bytes) -> Path:
+    p = tmp_path / fn
+    p.write_bytes(data)
+    return p
+
+
+def test_gguf_rejects_malformed(tmp_path):
+    good = Path(tiny_model("tiny-bf16")).read_bytes()
+    cases = {
+        "bad_magic.gguf": b"XXXX" + good[4:],
+        "v2.gguf": good[:4] + struct.pack("<I", 2) + good[8:],
+        "truncated.gguf": good[:4096],
+        "empty.gguf": b"",
+        "zero_tensors.gguf": good[:8] + struct.pack("<Q", 0) + good[16:],
+    }
+    for fn, data in cases.items():
+        rc, _ = load(_corrupt(tmp_path, fn, data))
+        assert rc != MF_OK, fn
+        assert last_error(), fn
+    rc, _ = load(tmp_path / "missing.gguf")
+    assert rc != MF_OK and "missing.gguf" in last_error()
+
+
+def test_gguf_rejects_bad_run_params(tmp_path):
+    rc, _ = load(tiny_model("tiny-bf16"), max_seq=10 ** 9)  # beyond context_length
+    assert rc != MF_OK and "max_seq_len" in last_error()
+
+
+def test_gguf_rejects_unsupported_dtype(tmp_path):
+    cfg = Qwen3Shape(1, 64, 2, 1, 128, 64, 300, "bf16", True, seed=1)
+    p = write_qwen3_gguf(tmp_path / "m.gguf", cfg)
+    data = bytearray(Path(p).read_bytes())
+    # the first tensor info's type field (BF16 = 30) -> Q4_0 (2)
+    idx = data.find(b"token_embd.weight")
+    off = idx + len(b"token_embd.weight") + 4 + 2 * 8
+    assert struct.unpack_from("<I", data, off)[0] == 30
+    struct.pack_into("<I", data, off, 2)
+    rc, _ = load(_corrupt(tmp_path, "q4.gguf", bytes(data)))
+    assert rc != MF_OK and "unsupported type" in last_error()
+
+
+def test_random_prompt_matches_benchmark_draw():
+    # C++ std::mt19937 + uniform_int_distribution (host library) vs the Python restatement
+    out = np.zeros(2000, np.uint32)
+    assert host_lib().mf_random_prompt(30, 151936, 2000, out.ctypes.data) == MF_OK
+    assert np.array_equal(out, random_prompt(2000, 151936, 30))
+    out = np.zeros(500, np.uint32)
+    host_lib().mf_random_prompt(7, 1000, 500, out.ctypes.data)
+    assert np.array_equal(out, random_prompt(500, 1000, 7))
+
+
+def test_rope_table_matches_oracle():
+    tab = np.zeros((64, 64, 2), np.float32)
+    assert cuda_lib().mf_rope_table(tab.ctypes.data, 64, 128, 1e6) == MF_OK
+    po = PortOps()
+    for pos in (0, 1, 63):
+        for i in (0, 17, 63):
+            e = np.zeros(128, np.float32)
+            e[i] = 1
+            o = po.rope(e, 0, 128, 128, 1e6, pos)
+            assert o[i] == tab[pos, i, 0] and o[i + 64] == tab[pos, i, 1]
+
+
+@pytest.mark.parametrize("temp,top_k,top_p,min_p,pres", [(0.0, 1, 1.0, 0.0, 0.0), (0.7, 20, 0.9, 0.0, 0.0),
+                                                         (0.6, 20, 0.95, 0.0, 1.5), (1.0, 50, 1.0, 0.05, 0.0)])
+def test_sampler_matches_oracle(temp, top_k, top_p, min_p, pres):
+    V = TINY["tiny-bf16"].vocab
+    rng = np.random.default_rng(int(temp * 10) + top_k)
+    logits = (rng.standard_normal(V) * 2).astype(np.float32)
+    logits[5] = logits[6] = logits.max() + 1  # a tie at the top
+    seen = np.array([5, 9, 100, 200], np.uint32)
+    rp = mf_run_params(0, 64, top_k, temp, top_p, min_p, pres, 42)
+    n = 64
+    out = np.zeros(n, np.uint32)
+    assert host_lib().mf_sample(logits.ctypes.data, V, C.byref(rp), seen.ctypes.data, seen.size, n,
+                                out.ctypes.data) == MF_OK
+    pm = PortModel(tiny_model("tiny-bf16"), max_seq=8, top_k=top_k, temp=temp, top_p=top_p, min_p=min_p, pres=pres,
+                   seed=42)
+    for s in seen:
+        pm.add_token(int(s))
+    ref = [pm.sample(logits) for _ in range(n)]
+    assert out.tolist() == ref
+    if temp == 0.0:
+        assert set(ref) == {5}  # first maximum
+
+
+def test_sampler_rejects_bad_params():
+    logits = np.zeros(16, np.float32)
+    out = np.zeros(1, np.uint32)
+    rp = mf_run_params(0, 8, 0, 0.7, 0.9, 0.0, 0.0, 1)  # top_k = 0
+    assert host_lib().mf_sample(logits.ctypes.data, 16, C.byref(rp), None, 0, 1, out.ctypes.data) == MF_E_INVALID
+
+
+def test_ops_validate_before_touching_the_device():
+    lib = cuda_lib()
+    # null pointers and bad sizes are rejected on the host, no GPU needed
+    assert lib.mf_matmul(None, None, None, 2, 0, 16, 16, None) == MF_E_INVALID
+    assert lib.mf_rmsnorm(None, None, None, 0, 1e-6, 1, None) == MF_E_INVALID
+    assert lib.mf_attn_decode(None, None) == MF_E_INVALID
+    assert lib.mf_attn_decode_noalloc(None, None) == MF_E_INVALID
+    assert lib.mf_lm_head(None, None, None, 1e-6, None, 2, 10, 16, 0, None, None, None) == MF_E_INVALID
