@@ -15,29 +15,43 @@
 // rounding.
 //
 // B200 structure (split-K flash decode):
-//  * grid = (n_split, n_kv_heads); each CTA serves ALL kv_mul query heads of
-//    its KV head over one contiguous slice of positions, so every K/V row is
-//    read from HBM exactly once per token.
-//  * The cache layout is [kv_head][position][d_head] (fp32), so a slice is one
-//    contiguous run of rows. Each warp streams 16-row K and V tiles into a
-//    double-buffered shared-memory stage with cp.async (no register staging),
-//    computes 16 scores per head with lanes owning positions (conflict-free
-//    padded K rows), and accumulates P.V with lanes owning 4 dims each.
-//  * Warps, then CTAs, are merged with the usual (max, sum, vector) rescaling;
-//    the CTA that finishes last for a KV head merges the n_split partials in a
-//    fixed order (deterministic; no spin-waits).
+//  * grid = (n_split, n_kv_heads), 8 warps per CTA, two CTAs per SM; each CTA
+//    serves ALL kv_mul query heads of its KV head over one contiguous slice of
+//    positions, so every K/V row is read from HBM exactly once per token.
+//  * The cache layout is [kv_head][position][d_head] (fp32): a slice is one
+//    contiguous run of rows, streamed as 32-row (16 KB) tiles through a
+//    5-stage CTA-wide cp.async ring with one barrier per tile.
+//  * Two phases per 256-position super-chunk: (1) the K tiles -> scaled
+//    scores of every query head into shared memory (8 lanes per position,
+//    16 dims each, finished by a reduce-scatter over the 8 lanes); (2) one
+//    CTA-wide softmax step (running max, rescale factor, exponentials in
+//    place), then the V tiles -> P.V with the probabilities read as
+//    broadcast float4s (each warp owns 4 rows of a tile, each lane 4 dims).
+//    All warps share the CTA's running max, so warp partials just add.
+//  * Slices are merged with the usual (max, sum, vector) rescaling by the CTA
+//    that finishes last for its KV head, which pulls every partial in with one
+//    burst of copies and merges in a fixed order (deterministic; no waits).
 #pragma once
 
 #include "mf_common.cuh"
 
 namespace mf {
 
-constexpr int ATT_D = 128;       // head dim (Qwen3)
-constexpr int ATT_TILE = 16;     // positions per warp tile
-constexpr int ATT_WARPS = 4;
-constexpr int ATT_KSTRIDE = ATT_D + 4;  // padded K row (floats): conflict-free row-per-lane reads
-constexpr int ATT_PF_ROWS = 256;        // L2 prefetch window per CTA (rows of K and of V)
-constexpr int ATT_MIN_CHUNK = 128;      // fewest positions per split
+constexpr int ATT_D = 128;          // head dim (Qwen3)
+constexpr int ATT_TILE = 32;        // positions per pipeline tile
+constexpr int ATT_TILE_FLOATS = ATT_TILE * ATT_D;
+constexpr int ATT_WARPS = 8;
+constexpr int ATT_STAGES = 5;
+constexpr int ATT_CTAS_PER_SM = 2;
+constexpr int ATT_SC_TILES = 8;     // tiles per super-chunk
+constexpr int ATT_SC = ATT_SC_TILES * ATT_TILE;
+constexpr int ATT_SC_STRIDE = ATT_SC + 4;  // per-head score row (padded against bank conflicts)
+constexpr int ATT_MIN_CHUNK = 64;   // fewest positions per split
+constexpr int ATT_MAX_SPLIT = 128;  // merge tables live in the score area
+// Per query head, the score area holds one super-chunk of scores and, in the
+// merge, (m, l) and a scale factor per slice.
+constexpr int ATT_HEAD_AREA = ATT_SC_STRIDE > 3 * ATT_MAX_SPLIT ? ATT_SC_STRIDE : 3 * ATT_MAX_SPLIT;
+constexpr int ATT_PF_ROWS = 128;    // rows of K and of V prefetched into L2 before the dependency wait
 
 struct AttnParams {
     const float* qkv;        // [Hq*D | Hkv*D | Hkv*D] (this rank's heads)
@@ -58,18 +72,14 @@ struct AttnParams {
     int n_split;
 };
 
-struct AttnSmemLayout {
-    static constexpr int K_STAGE = ATT_TILE * ATT_KSTRIDE;  // floats
-    static constexpr int V_STAGE = ATT_TILE * ATT_D;
-    static constexpr int WARP_FLOATS = 2 * (K_STAGE + V_STAGE);
-};
-
 MF_DEVICE void cp_async16(void* smem, const void* gmem) {
     const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
 }
 MF_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N> MF_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+MF_DEVICE float f4_get(const float4& v, int i) { return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w)); }
 
 // RMSNorm + NeoX RoPE of one 128-dim head held by a warp (lane owns dims 4l..4l+3).
 MF_DEVICE float4 norm_rope_head(float4 v, const float* nw, float eps, const float2* cs, int lane) {
@@ -98,273 +108,388 @@ MF_DEVICE float4 norm_rope_head(float4 v, const float* nw, float eps, const floa
     return make_float4(o[0], o[1], o[2], o[3]);
 }
 
+// Split geometry for a context of `len` positions: effective slice count
+// (slices of at least ATT_MIN_CHUNK positions, tile-aligned, none empty) and
+// this slice's [start, end). The last slice ends at len and so owns len - 1.
+struct AttnSlice {
+    int eff, start, end;
+};
+MF_DEVICE AttnSlice attn_slice(int len, int n_split, int split) {
+    int eff = min(n_split, max(1, (len + ATT_MIN_CHUNK - 1) / ATT_MIN_CHUNK));
+    int chunk = (len + eff - 1) / eff;
+    chunk = (chunk + ATT_TILE - 1) / ATT_TILE * ATT_TILE;
+    eff = (len + chunk - 1) / chunk;
+    const int start = split * chunk;
+    return {eff, start, min(start + chunk, len)};
+}
+
+// The K (or V) tile at position q of a slice's copy sequence: per super-chunk
+// its K tiles, then its V tiles.
+struct AttnSeq {
+    int sc, t, n_sc, row0;
+    bool is_v;
+};
+MF_DEVICE AttnSeq attn_seq(int q, int start, int nrows) {
+    AttnSeq s;
+    s.sc = q / (2 * ATT_SC_TILES);
+    const int w = q - s.sc * 2 * ATT_SC_TILES;
+    s.n_sc = min(ATT_SC_TILES, (nrows - s.sc * ATT_SC + ATT_TILE - 1) / ATT_TILE);
+    s.is_v = w >= s.n_sc;
+    s.t = s.is_v ? w - s.n_sc : w;
+    s.row0 = start + s.sc * ATT_SC + s.t * ATT_TILE;
+    return s;
+}
+
+// Query heads per KV head up to ATT_QREG_MAX keep their score-lane query
+// slices in registers; larger groups read them from shared memory (the reads
+// are broadcast within each quarter-warp and conflict-free across it).
+constexpr int ATT_QREG_MAX = 4;
+
 template <int G>
-__global__ void __launch_bounds__(ATT_WARPS * 32) attn_decode_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)) attn_decode_kernel(const AttnParams p) {
+    static_assert(G >= 1 && G <= 16 && (G & (G - 1)) == 0, "power-of-two query groups");
+    constexpr int NT = ATT_WARPS * 32;
     extern __shared__ float4 att_smem4[];
-    float* smem = reinterpret_cast<float*>(att_smem4);
+    float* ring = reinterpret_cast<float*>(att_smem4);      // [ATT_STAGES][ATT_TILE_FLOATS]
+    float* sc_s = ring + ATT_STAGES * ATT_TILE_FLOATS;       // [G][ATT_SC_STRIDE] within [G][ATT_HEAD_AREA]
     __shared__ __align__(16) float q_s[G][ATT_D];
-    __shared__ float p_s[ATT_WARPS][G][ATT_TILE];
-    __shared__ float wm[ATT_WARPS][G], wl[ATT_WARPS][G];
+    __shared__ __align__(16) float knew_s[ATT_D], vnew_s[ATT_D];  // row `pos`, never re-read from HBM
+    __shared__ float m_s[G], l_s[G], a_s[G];
     __shared__ int is_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int split = blockIdx.x, kvh = blockIdx.y;
     const int Hq = p.n_heads, Hkv = p.n_kv_heads;
     const size_t head_stride = (size_t)p.max_seq * ATT_D;
-    float* kc = p.k_cache + (size_t)kvh * head_stride;
-    float* vc = p.v_cache + (size_t)kvh * head_stride;
+    const float* kc = p.k_cache + (size_t)kvh * head_stride;
+    const float* vc = p.v_cache + (size_t)kvh * head_stride;
 
+    // Before the dependency wait nothing produced by earlier kernels may be
+    // used; a possibly stale position only steers an L2 prefetch of cache rows
+    // (clamped into this head's cache, so always in bounds).
+    if (tid == 0) {
+        const int ps = min(max(__ldcg(p.pos_ptr), 0), p.max_seq - 1);
+        const AttnSlice sl = attn_slice(ps + 1, p.n_split, split);
+        if (split < sl.eff && sl.end > sl.start) {
+            const uint32_t nb = (uint32_t)min(sl.end - sl.start, ATT_PF_ROWS) * ATT_D * sizeof(float);
+            prefetch_l2(kc + (size_t)sl.start * ATT_D, nb);
+            prefetch_l2(vc + (size_t)sl.start * ATT_D, nb);
+        }
+    }
     pdl_launch_dependents();
     pdl_wait();
 
     const int pos = __ldcg(p.pos_ptr);
-    const int len = pos + 1;
-    const float2* cs = p.rope + (size_t)pos * (ATT_D / 2);
-    // Effective split count for this context: slices of at least
-    // ATT_MIN_CHUNK positions (short contexts use fewer CTAs and a cheaper
-    // merge); CTAs past it only append K/V if they own `pos` (never: the
-    // last effective slice ends at len).
-    const int eff_split = min(p.n_split, max(1, (len + ATT_MIN_CHUNK - 1) / ATT_MIN_CHUNK));
-    if (split >= eff_split) return;
-    int chunk = (len + eff_split - 1) / eff_split;
-    chunk = (chunk + ATT_TILE - 1) / ATT_TILE * ATT_TILE;
-    const int start = split * chunk;
-    const int end = min(start + chunk, len);
-
-    // The CTA's K and V rows are contiguous: bulk-prefetch the first
-    // ATT_PF_ROWS of each into L2 now; every tile issue below extends the
-    // window by one tile, so the cp.async stream mostly hits L2.
-    if (tid == 0 && end > start) {
-        const uint32_t nb = (uint32_t)min(end - start, ATT_PF_ROWS) * ATT_D * sizeof(float);
-        prefetch_l2(kc + (size_t)start * ATT_D, nb);
-        prefetch_l2(vc + (size_t)start * ATT_D, nb);
+    if (pos < 0 || pos >= p.max_seq) {  // no such cache row: write nothing but a zero output
+        if (split == 0)
+            for (int i = tid; i < G * ATT_D; i += NT) p.out[(size_t)kvh * G * ATT_D + i] = 0.f;
+        return;
     }
-    float* ks = smem + warp * AttnSmemLayout::WARP_FLOATS;
-    float* vs = ks + 2 * AttnSmemLayout::K_STAGE;
-    const int ntiles = end > start ? (end - start + ATT_TILE - 1) / ATT_TILE : 0;
-    auto issue = [&](int t, int stage) {
-        const int p0 = start + t * ATT_TILE;
-        const int nv = min(ATT_TILE, end - p0);
-        float* kd = ks + stage * AttnSmemLayout::K_STAGE;
-        float* vd = vs + stage * AttnSmemLayout::V_STAGE;
-        const int pf = p0 + ATT_PF_ROWS;  // tile entering the prefetch window
-        if (lane == 0 && pf < end) {
-            const uint32_t nb = (uint32_t)min(ATT_TILE, end - pf) * ATT_D * sizeof(float);
-            prefetch_l2(kc + (size_t)pf * ATT_D, nb);
-            prefetch_l2(vc + (size_t)pf * ATT_D, nb);
-        }
-#pragma unroll 4
-        for (int r = 0; r < nv; ++r) {
-            cp_async16(kd + r * ATT_KSTRIDE + 4 * lane, kc + (size_t)(p0 + r) * ATT_D + 4 * lane);
-            cp_async16(vd + r * ATT_D + 4 * lane, vc + (size_t)(p0 + r) * ATT_D + 4 * lane);
-        }
-        cp_async_commit();
-    };
-    // The warp's first tile does not depend on the queries: start its copy
-    // now, unless it holds row `pos` (written by the append below).
-    const bool early = warp < ntiles && (start + (warp + 1) * ATT_TILE <= pos);
-    if (early) issue(warp, 0);
+    const int len = pos + 1;
+    const AttnSlice sl = attn_slice(len, p.n_split, split);
+    if (split >= sl.eff) return;
+    const int start = sl.start, end = sl.end, nrows = end - start;
+    const int nseq = 2 * ((nrows + ATT_TILE - 1) / ATT_TILE);
+    const float2* cs = p.rope + (size_t)pos * (ATT_D / 2);
+    // Row `pos` (the last row of the last slice) is appended by this kernel;
+    // its values are taken from shared memory, so it is never copied.
+    const int copy_end = (end == len) ? end - 1 : end;
 
-    // ---- prologue: normalised + rotated queries of this group
+    auto issue = [&](int q) {
+        if (q < nseq) {
+            const AttnSeq sq = attn_seq(q, start, nrows);
+            const int nvalid = min(ATT_TILE, copy_end - sq.row0);
+            float* dst = ring + (q % ATT_STAGES) * ATT_TILE_FLOATS;
+            const float* src = (sq.is_v ? vc : kc) + (size_t)sq.row0 * ATT_D;
+#pragma unroll
+            for (int i = 0; i < ATT_TILE_FLOATS / 4 / NT; ++i) {
+                const int piece = tid + i * NT;
+                const int r = piece >> 5, c4 = piece & 31;
+                if (r < nvalid) cp_async16(dst + r * ATT_D + 4 * c4, src + (size_t)r * ATT_D + 4 * c4);
+            }
+        }
+        cp_async_commit();  // one group per sequence slot, empty groups included
+    };
+#pragma unroll 1
+    for (int q = 0; q < ATT_STAGES - 1; ++q) issue(q);
+
+    // ---- prologue: normalised + rotated queries; the KV append
     for (int g = warp; g < G; g += ATT_WARPS) {
         const int h = kvh * G + g;
         const float4 v = __ldcg(reinterpret_cast<const float4*>(p.qkv + (size_t)h * ATT_D) + lane);
-        const float4 r = norm_rope_head(v, p.q_norm_w, p.eps, cs, lane);
-        *reinterpret_cast<float4*>(&q_s[g][4 * lane]) = r;
+        *reinterpret_cast<float4*>(&q_s[g][4 * lane]) = norm_rope_head(v, p.q_norm_w, p.eps, cs, lane);
     }
-    // ---- KV append: the CTA whose slice holds `pos` writes row pos
-    if (start <= pos && pos < end && warp == 0) {
+    if (end == len && warp == ATT_WARPS - 1) {
         const float* kraw = p.qkv + (size_t)Hq * ATT_D + (size_t)kvh * ATT_D;
         const float* vraw = p.qkv + (size_t)(Hq + Hkv) * ATT_D + (size_t)kvh * ATT_D;
         const float4 k = norm_rope_head(__ldcg(reinterpret_cast<const float4*>(kraw) + lane), p.k_norm_w, p.eps,
                                         cs, lane);
         const float4 v = __ldcg(reinterpret_cast<const float4*>(vraw) + lane);
-        reinterpret_cast<float4*>(kc + (size_t)pos * ATT_D)[lane] = k;
-        reinterpret_cast<float4*>(vc + (size_t)pos * ATT_D)[lane] = v;
+        reinterpret_cast<float4*>(p.k_cache + (size_t)kvh * head_stride + (size_t)pos * ATT_D)[lane] = k;
+        reinterpret_cast<float4*>(p.v_cache + (size_t)kvh * head_stride + (size_t)pos * ATT_D)[lane] = v;
+        reinterpret_cast<float4*>(knew_s)[lane] = k;
+        reinterpret_cast<float4*>(vnew_s)[lane] = v;
+    }
+    if (tid < G) {
+        m_s[tid] = -INFINITY;
+        l_s[tid] = 0.f;
     }
     __syncthreads();
 
     const float scale = 1.0f / sqrtf((float)ATT_D);  // src/ops/kernels.cpp:88
+    // score mapping: tile row r_k, 16 dims {4*(c8 + 8j) + e}
+    const int r_k = tid >> 3, c8 = tid & 7;
+    constexpr int QG = G <= ATT_QREG_MAX ? G : 1;
+    float4 qreg[QG][4];
+    if constexpr (G <= ATT_QREG_MAX) {
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) qreg[g][j] = *reinterpret_cast<const float4*>(&q_s[g][4 * (c8 + 8 * j)]);
+    }
+    // after the reduce-scatter a lane holds the sums of heads h_lane .. h_lane + HPL - 1
+    constexpr int HPL = G >= 8 ? G / 8 : 1;
+    constexpr int LPH = G >= 8 ? 1 : 8 / G;  // lanes holding each head
+    int h_lane = 0;
+    {
+        int n = G;
+#pragma unroll
+        for (int m = 4; m >= 1; m >>= 1)
+            if (n >= 2) {
+                n >>= 1;
+                if (c8 & m) h_lane += n;
+            }
+    }
 
-    float m[G], l[G];
     float4 o[G];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        m[g] = -INFINITY;
-        l[g] = 0.f;
-        o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    for (int g = 0; g < G; ++g) o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
 
-    const int j = lane & 15, half = lane >> 4;
-    int stage = 0;
-    if (warp < ntiles && !early) issue(warp, 0);
-    for (int t = warp; t < ntiles; t += ATT_WARPS) {
-        const int tn = t + ATT_WARPS;
-        if (tn < ntiles) {
-            issue(tn, stage ^ 1);
-            cp_async_wait<1>();
+    for (int q = 0; q < nseq; ++q) {
+        cp_async_wait<ATT_STAGES - 2>();
+        __syncthreads();  // tile q landed for every thread; slot (q - 1) is free
+        issue(q + ATT_STAGES - 1);
+        const AttnSeq sq = attn_seq(q, start, nrows);
+        const float* tile = ring + (q % ATT_STAGES) * ATT_TILE_FLOATS;
+        const int nvalid = min(ATT_TILE, end - sq.row0);  // rows of the slice in this tile
+        if (!sq.is_v) {
+            // ---- phase 1: scores of this tile's rows
+            float s[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) s[g] = 0.f;
+            if (r_k < nvalid) {
+                const float* krow = (sq.row0 + r_k == pos ? knew_s : tile + r_k * ATT_D) + 4 * c8;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float4 k4 = *reinterpret_cast<const float4*>(krow + 32 * j);
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        float4 q4;
+                        if constexpr (G <= ATT_QREG_MAX) q4 = qreg[g][j];
+                        else q4 = *reinterpret_cast<const float4*>(&q_s[g][4 * (c8 + 8 * j)]);
+                        s[g] = fmaf(q4.x, k4.x, s[g]);
+                        s[g] = fmaf(q4.y, k4.y, s[g]);
+                        s[g] = fmaf(q4.z, k4.z, s[g]);
+                        s[g] = fmaf(q4.w, k4.w, s[g]);
+                    }
+                }
+            }
+            // reduce-scatter over the 8 lanes of the row (xor 4, 2, 1)
+            int n = G;
+#pragma unroll
+            for (int m = 4; m >= 1; m >>= 1) {
+                if (n >= 2) {
+                    const int hn = n >> 1;
+                    const bool upper = (c8 & m) != 0;
+#pragma unroll
+                    for (int i = 0; i < hn; ++i) {
+                        const float send = upper ? s[i] : s[i + hn];
+                        const float keep = upper ? s[i + hn] : s[i];
+                        s[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+                    }
+                    n = hn;
+                } else {
+                    s[0] += __shfl_xor_sync(0xffffffffu, s[0], m);
+                }
+            }
+            if (c8 % LPH == 0) {
+                const int col = sq.t * ATT_TILE + r_k;
+                const bool valid = r_k < nvalid;
+#pragma unroll
+                for (int i = 0; i < HPL; ++i) sc_s[(h_lane + i) * ATT_SC_STRIDE + col] = valid ? s[i] * scale : -INFINITY;
+            }
         } else {
-            cp_async_wait<0>();
-        }
-        __syncwarp();
-        const int p0 = start + t * ATT_TILE;
-        const int nv = min(ATT_TILE, end - p0);
-        const float* kt = ks + stage * AttnSmemLayout::K_STAGE;
-        const float* vt = vs + stage * AttnSmemLayout::V_STAGE;
-        // scores: lane (j, half) -> position j, dims [64*half, 64*half+64)
-        float s[G];
+            if (sq.t == 0) {
+                // ---- softmax step over the super-chunk (every K tile done: barrier above)
+                const int rows_sc = min(ATT_SC, end - (start + sq.sc * ATT_SC));
+                for (int g = warp; g < G; g += ATT_WARPS) {
+                    float* srow = sc_s + g * ATT_SC_STRIDE;
+                    float mx = -INFINITY;
+                    for (int i = lane; i < rows_sc; i += 32) mx = fmaxf(mx, srow[i]);
+                    mx = warp_max(mx);
+                    const float m_old = m_s[g];
+                    const float mn = fmaxf(m_old, mx);
+                    float sum = 0.f;
+                    for (int i = lane; i < rows_sc; i += 32) {
+                        const float e = expf(srow[i] - mn);
+                        srow[i] = e;
+                        sum += e;
+                    }
+                    sum = warp_sum(sum);
+                    if (lane == 0) {
+                        const float a = (m_old == -INFINITY) ? 0.f : expf(m_old - mn);
+                        a_s[g] = a;
+                        l_s[g] = fmaf(l_s[g], a, sum);
+                        m_s[g] = mn;
+                    }
+                }
+                __syncthreads();
 #pragma unroll
-        for (int g = 0; g < G; ++g) s[g] = 0.f;
-        const float* krow = kt + j * ATT_KSTRIDE + 64 * half;
-#pragma unroll 4
-        for (int d4 = 0; d4 < 16; ++d4) {
-            const float4 k4 = *reinterpret_cast<const float4*>(krow + 4 * d4);
+                for (int g = 0; g < G; ++g) {
+                    const float a = a_s[g];
+                    o[g].x *= a; o[g].y *= a; o[g].z *= a; o[g].w *= a;
+                }
+            }
+            // ---- phase 2: P.V, warp rows rb .. rb + 3, lane dims 4*lane .. 4*lane + 3
+            const int rb = 4 * warp;
+            if (rb < nvalid) {
+                float4 pv[G];
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float4 q4 = *reinterpret_cast<const float4*>(&q_s[g][64 * half + 4 * d4]);
-                s[g] = fmaf(q4.x, k4.x, s[g]);
-                s[g] = fmaf(q4.y, k4.y, s[g]);
-                s[g] = fmaf(q4.z, k4.z, s[g]);
-                s[g] = fmaf(q4.w, k4.w, s[g]);
+                for (int g = 0; g < G; ++g)
+                    pv[g] = *reinterpret_cast<const float4*>(sc_s + g * ATT_SC_STRIDE + sq.t * ATT_TILE + rb);
+#pragma unroll
+                for (int rr = 0; rr < 4; ++rr) {
+                    if (rb + rr < nvalid) {  // rows past the slice end were never copied
+                        const float* vrow = (sq.row0 + rb + rr == pos) ? vnew_s : tile + (rb + rr) * ATT_D;
+                        const float4 v4 = *reinterpret_cast<const float4*>(vrow + 4 * lane);
+#pragma unroll
+                        for (int g = 0; g < G; ++g) {
+                            const float pg = f4_get(pv[g], rr);
+                            o[g].x = fmaf(pg, v4.x, o[g].x);
+                            o[g].y = fmaf(pg, v4.y, o[g].y);
+                            o[g].z = fmaf(pg, v4.z, o[g].z);
+                            o[g].w = fmaf(pg, v4.w, o[g].w);
+                        }
+                    }
+                }
             }
         }
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            float sc = (s[g] + __shfl_xor_sync(0xffffffffu, s[g], 16)) * scale;
-            if (j >= nv) sc = -INFINITY;
-            float mt = sc;
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
-            const float mn = fmaxf(m[g], mt);
-            const float alpha = expf(m[g] - mn);
-            const float pj = expf(sc - mn);
-            float ps = pj;
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-            l[g] = l[g] * alpha + ps;
-            m[g] = mn;
-            o[g].x *= alpha; o[g].y *= alpha; o[g].z *= alpha; o[g].w *= alpha;
-            if (half == 0) p_s[warp][g][j] = pj;
-        }
-        __syncwarp();
-        for (int jj = 0; jj < nv; ++jj) {
-            const float4 v4 = *reinterpret_cast<const float4*>(vt + jj * ATT_D + 4 * lane);
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float pg = p_s[warp][g][jj];
-                o[g].x = fmaf(pg, v4.x, o[g].x);
-                o[g].y = fmaf(pg, v4.y, o[g].y);
-                o[g].z = fmaf(pg, v4.z, o[g].z);
-                o[g].w = fmaf(pg, v4.w, o[g].w);
-            }
-        }
-        __syncwarp();
-        stage ^= 1;
     }
+    cp_async_wait<0>();
 
-    // ---- merge the warps of this CTA (reuse the warp stages as scratch)
+    // ---- sum the warps' accumulators (they share the CTA's running max)
     __syncthreads();
-    float* wo = smem;  // [ATT_WARPS][G][D]
+    float* wo = ring;  // [ATT_WARPS][G][D]
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        reinterpret_cast<float4*>(wo + ((size_t)warp * G + g) * ATT_D)[lane] = o[g];
-        if (lane == 0) {
-            wm[warp][g] = m[g];
-            wl[warp][g] = l[g];
-        }
-    }
+    for (int g = 0; g < G; ++g) reinterpret_cast<float4*>(wo + ((size_t)warp * G + g) * ATT_D)[lane] = o[g];
     __syncthreads();
-    if (eff_split == 1) {  // one slice: finish here, no partials
-        for (int idx = tid; idx < G * ATT_D; idx += ATT_WARPS * 32) {
-            const int g = idx / ATT_D, d = idx - g * ATT_D;
-            float M = -INFINITY;
+    if (sl.eff == 1) {  // one slice: finish here, no partials
+        for (int idx = tid; idx < G * ATT_D; idx += NT) {
+            const int g = idx / ATT_D;
+            float acc = 0.f;
 #pragma unroll
-            for (int w = 0; w < ATT_WARPS; ++w) M = fmaxf(M, wm[w][g]);
-            float acc = 0.f, L = 0.f;
-#pragma unroll
-            for (int w = 0; w < ATT_WARPS; ++w) {
-                const float f = (wm[w][g] == -INFINITY) ? 0.f : expf(wm[w][g] - M);
-                acc = fmaf(f, wo[((size_t)w * G + g) * ATT_D + d], acc);
-                L = fmaf(f, wl[w][g], L);
-            }
-            p.out[((size_t)kvh * G + g) * ATT_D + d] = acc / L;
+            for (int w = 0; w < ATT_WARPS; ++w) acc += wo[(size_t)w * G * ATT_D + idx];
+            p.out[(size_t)kvh * G * ATT_D + idx] = acc / l_s[g];
         }
         return;
     }
     const size_t pbase = ((size_t)kvh * p.n_split + split) * G;
-    for (int idx = tid; idx < G * ATT_D; idx += ATT_WARPS * 32) {
-        const int g = idx / ATT_D, d = idx - g * ATT_D;
-        float M = -INFINITY;
+    for (int idx = tid; idx < G * ATT_D; idx += NT) {
+        float acc = 0.f;
 #pragma unroll
-        for (int w = 0; w < ATT_WARPS; ++w) M = fmaxf(M, wm[w][g]);
-        float acc = 0.f, L = 0.f;
-        if (M != -INFINITY) {
-#pragma unroll
-            for (int w = 0; w < ATT_WARPS; ++w) {
-                const float f = expf(wm[w][g] - M);
-                acc = fmaf(f, wo[((size_t)w * G + g) * ATT_D + d], acc);
-                L = fmaf(f, wl[w][g], L);
-            }
-        }
-        p.part_o[(pbase + g) * ATT_D + d] = acc;
-        if (d == 0) {
-            p.part_ml[(pbase + g) * 2 + 0] = M;
-            p.part_ml[(pbase + g) * 2 + 1] = L;
-        }
+        for (int w = 0; w < ATT_WARPS; ++w) acc += wo[(size_t)w * G * ATT_D + idx];
+        p.part_o[pbase * ATT_D + idx] = acc;
+    }
+    if (tid < G) {
+        p.part_ml[(pbase + tid) * 2 + 0] = m_s[tid];
+        p.part_ml[(pbase + tid) * 2 + 1] = l_s[tid];
     }
 
-    // ---- the last CTA of this KV head merges the n_split partials
+    // ---- the last CTA of this KV head merges the slices
     __syncthreads();
     if (tid == 0) {
         __threadfence();
         const int ticket = atomicAdd(p.counters + kvh, 1);
-        is_last = (ticket == eff_split - 1);
+        is_last = (ticket == sl.eff - 1);
     }
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    // merge in three parallel passes through shared memory (the warp stages
-    // are free now): (m, l) of every split, then the per-split scale factors,
-    // then the weighted sum of the partial outputs with independent loads.
-    const int ns = eff_split;
-    float* ml = smem;                    // [ns][G][2]
-    float* fs = smem + 2 * ns * G;       // [G][ns] scale factors
-    float* Ls = fs + ns * G;             // [G] denominators
+    const int ns = sl.eff;
     const size_t hb = (size_t)kvh * p.n_split * G;
-    for (int i = tid; i < ns * G * 2; i += ATT_WARPS * 32) ml[i] = __ldcg(p.part_ml + hb * 2 + i);
+    float* ml = sc_s;    // [ns][G][2], then the scale factors [ns][G] (ns <= ATT_MAX_SPLIT: both fit G * ATT_HEAD_AREA)
+    float* fs = sc_s + 2 * ATT_MAX_SPLIT * G;
+    float* po = ring;    // a batch of partial outputs [nb][G][D]
+    constexpr int NB = (ATT_STAGES * ATT_TILE_FLOATS) / (G * ATT_D);
+    auto issue_batch = [&](int s0) {
+        const int nb = min(NB, ns - s0);
+        const float* src = p.part_o + (hb + (size_t)s0 * G) * ATT_D;
+        for (int i = tid; i < nb * G * ATT_D / 4; i += NT) cp_async16(po + 4 * i, src + 4 * i);
+        cp_async_commit();
+    };
+    issue_batch(0);
+    for (int i = tid; i < ns * G * 2; i += NT) ml[i] = __ldcg(p.part_ml + hb * 2 + i);
     __syncthreads();
-    if (tid < G) {
-        const int g = tid;
+    // per head: global max, per-slice factors, denominator (one warp per head)
+    for (int g = warp; g < G; g += ATT_WARPS) {
         float M = -INFINITY;
-        for (int sidx = 0; sidx < ns; ++sidx) M = fmaxf(M, ml[(sidx * G + g) * 2]);
+        for (int s0 = lane; s0 < ns; s0 += 32) M = fmaxf(M, ml[(s0 * G + g) * 2]);
+        M = warp_max(M);
         float L = 0.f;
-        for (int sidx = 0; sidx < ns; ++sidx) {
-            const float ms = ml[(sidx * G + g) * 2];
+        for (int s0 = lane; s0 < ns; s0 += 32) {
+            const float ms = ml[(s0 * G + g) * 2];
             const float f = (ms == -INFINITY) ? 0.f : expf(ms - M);
-            fs[g * ns + sidx] = f;
-            L = fmaf(f, ml[(sidx * G + g) * 2 + 1], L);
+            fs[s0 * G + g] = f;
+            L = fmaf(f, ml[(s0 * G + g) * 2 + 1], L);
         }
-        Ls[g] = L;
+        L = warp_sum(L);
+        if (lane == 0) a_s[g] = L;
     }
-    __syncthreads();
-    for (int idx = tid; idx < G * ATT_D; idx += ATT_WARPS * 32) {
-        const int g = idx / ATT_D, d = idx - g * ATT_D;
-        const float* po = p.part_o + (hb + g) * ATT_D + d;
-        const float* f = fs + g * ns;
-        float acc = 0.f;
-        for (int s0 = 0; s0 < ns; s0 += 16) {
-            float o[16];
+    // every thread owns float4 outputs idx4 = tid + k*NT of [G][D/4]
+    constexpr int PER = (G * ATT_D / 4 + NT - 1) / NT;
+    float4 acc[PER];
 #pragma unroll
-            for (int u = 0; u < 16; ++u) o[u] = (s0 + u < ns) ? __ldcg(po + (size_t)(s0 + u) * G * ATT_D) : 0.f;
+    for (int k = 0; k < PER; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < ns; s0 += NB) {
+        cp_async_wait<0>();
+        __syncthreads();
+        const int nb = min(NB, ns - s0);
 #pragma unroll
-            for (int u = 0; u < 16; ++u)
-                if (s0 + u < ns) acc = fmaf(f[s0 + u], o[u], acc);
+        for (int k = 0; k < PER; ++k) {
+            const int idx4 = tid + k * NT;
+            if (idx4 < G * ATT_D / 4) {
+                const int g = idx4 / (ATT_D / 4);
+                for (int b = 0; b < nb; ++b) {
+                    const float f = fs[(s0 + b) * G + g];
+                    const float4 v = reinterpret_cast<const float4*>(po + (size_t)b * G * ATT_D)[idx4];
+                    acc[k].x = fmaf(f, v.x, acc[k].x);
+                    acc[k].y = fmaf(f, v.y, acc[k].y);
+                    acc[k].z = fmaf(f, v.z, acc[k].z);
+                    acc[k].w = fmaf(f, v.w, acc[k].w);
+                }
+            }
         }
-        p.out[((size_t)kvh * G + g) * ATT_D + d] = acc / Ls[g];
+        if (s0 + NB < ns) {
+            __syncthreads();  // the batch buffer is refilled
+            issue_batch(s0 + NB);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int idx4 = tid + k * NT;
+        if (idx4 < G * ATT_D / 4) {
+            const float L = a_s[idx4 / (ATT_D / 4)];
+            reinterpret_cast<float4*>(p.out + (size_t)kvh * G * ATT_D)[idx4] =
+                make_float4(acc[k].x / L, acc[k].y / L, acc[k].z / L, acc[k].w / L);
+        }
     }
     if (tid == 0) p.counters[kvh] = 0;
 }
 
-inline size_t attn_smem_bytes() { return (size_t)ATT_WARPS * AttnSmemLayout::WARP_FLOATS * sizeof(float); }
+inline size_t attn_smem_bytes(int G) {
+    return ((size_t)ATT_STAGES * ATT_TILE_FLOATS + (size_t)G * ATT_HEAD_AREA) * sizeof(float);
+}
+// Largest n_split the merge supports.
+inline int attn_max_split(int G) { return ATT_MAX_SPLIT; }
 
 }  // namespace mf

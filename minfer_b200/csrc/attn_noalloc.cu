@@ -81,6 +81,7 @@ extern "C" int mf_attn_decode_noalloc(const mf_attn_desc* d, void* stream) {
     const size_t po = (size_t)d->n_kv_heads * d->n_split * G * mf::ATT_D * sizeof(float);
     if ((size_t)d->n_kv_heads * sizeof(int) > kCounterBytes || kCounterBytes + pml + po > MF_ATTN_NOALLOC_SCRATCH_BYTES)
         return noalloc_fail(MF_E_UNSUPPORTED, "request needs more scratch than MF_ATTN_NOALLOC_SCRATCH_BYTES");
+    if (d->n_split > mf::attn_max_split(G)) return noalloc_fail(MF_E_UNSUPPORTED, "n_split above the merge table size");
     void* base = nullptr;
     int rc = scratch_address(&base);
     if (rc) return rc;
@@ -89,7 +90,7 @@ extern "C" int mf_attn_decode_noalloc(const mf_attn_desc* d, void* stream) {
     // the counters must start at zero; a previous call may have been cut short
     cudaError_t e = cudaMemsetAsync(ws, 0, kCounterBytes, st);
     if (e != cudaSuccess) return noalloc_fail(MF_E_CUDA, cudaGetErrorString(e));
-    const size_t smem = mf::attn_smem_bytes();
+    const size_t smem = mf::attn_smem_bytes(G);
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return noalloc_fail(MF_E_CUDA, cudaGetErrorString(e));
     mf::AttnParams p = {};

@@ -665,10 +665,11 @@ size_t mf_attn_workspace_bytes(int n_heads, int n_kv_heads, int d_head, int n_sp
 int mf_attn_default_split(int n_kv_heads, int max_seq) {
     if (n_kv_heads <= 0) return 1;
     int sms = num_sms();
-    int s = sms / n_kv_heads;
+    int s = sms * mf::ATT_CTAS_PER_SM / n_kv_heads;
     if (s < 1) s = 1;
-    const int max_useful = (max_seq + mf::ATT_TILE - 1) / mf::ATT_TILE;
+    const int max_useful = (max_seq + mf::ATT_MIN_CHUNK - 1) / mf::ATT_MIN_CHUNK;
     if (s > max_useful) s = max_useful;
+    if (s > mf::attn_max_split(16)) s = mf::attn_max_split(16);
     return s < 1 ? 1 : s;
 }
 
@@ -683,7 +684,9 @@ int mf_attn_decode(const mf_attn_desc* d, void* stream) {
     const int G = d->n_heads / d->n_kv_heads;
     const void* fn = mf::attn_kernel_ptr(G);
     MF_REQUIRE(fn, MF_E_UNSUPPORTED, "%d query heads per KV head has no kernel", G);
-    const size_t smem = mf::attn_smem_bytes();
+    MF_REQUIRE(d->n_split <= mf::attn_max_split(G), MF_E_UNSUPPORTED, "n_split %d above %d", d->n_split,
+               mf::attn_max_split(G));
+    const size_t smem = mf::attn_smem_bytes(G);
     int bps = 0;
     int rc = prepare(fn, mf::ATT_WARPS * 32, smem, &bps);
     if (rc) return rc;

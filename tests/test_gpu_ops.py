@@ -289,9 +289,9 @@ def _attn_reference(orc, qkv, qn, kn, eps, rope, kc_hist, vc_hist, pos, H, Hkv, 
     return out, k.reshape(Hkv, D), v.reshape(Hkv, D)
 
 
-@pytest.mark.parametrize("H,Hkv", [(4, 2), (16, 2), (8, 8), (32, 4)])
-@pytest.mark.parametrize("pos", [0, 15, 16, 17, 300, 2049])
-@pytest.mark.parametrize("split", ["default", 1])
+@pytest.mark.parametrize("H,Hkv", [(4, 2), (16, 2), (8, 8), (32, 4), (32, 8), (16, 1)])
+@pytest.mark.parametrize("pos", [0, 15, 16, 17, 255, 256, 300, 2049])
+@pytest.mark.parametrize("split", ["default", 1, 7])
 def test_attn_decode(ops, orc, gpu, H, Hkv, pos, split):
     D, S = 128, 2100
     rng = np.random.default_rng(H * 1000 + pos)
@@ -304,7 +304,7 @@ def test_attn_decode(ops, orc, gpu, H, Hkv, pos, split):
     # device cache layout [Hkv][S][D]
     kc = T(np.ascontiguousarray(kc_hist.transpose(1, 0, 2)), gpu)
     vc = T(np.ascontiguousarray(vc_hist.transpose(1, 0, 2)), gpu)
-    n_split = ops.attn_default_split(Hkv, S) if split == "default" else 1
+    n_split = ops.attn_default_split(Hkv, S) if split == "default" else split
     ws = torch.zeros(ops.attn_workspace_bytes(H, Hkv, D, n_split) // 4 + 1, dtype=torch.int32, device=gpu)
     st = torch.tensor([0, pos, 0, 0], dtype=torch.int32, device=gpu)
     out = torch.zeros(H * D, device=gpu)
@@ -320,6 +320,28 @@ def test_attn_decode(ops, orc, gpu, H, Hkv, pos, split):
     untouched = np.delete(kcn, pos, axis=1)
     np.testing.assert_array_equal(untouched, np.delete(kc_hist.transpose(1, 0, 2), pos, axis=1))
     assert ws[:Hkv].abs().sum().item() == 0  # counters back to zero
+
+
+def test_attn_decode_position_out_of_range(ops, gpu):
+    # a step record whose position has no cache row: nothing is written, the output is zero
+    D, S, H, Hkv = 128, 64, 8, 2
+    rng = np.random.default_rng(1)
+    kc = T(rng.standard_normal(Hkv * S * D).astype(np.float32), gpu)
+    vc = T(rng.standard_normal(Hkv * S * D).astype(np.float32), gpu)
+    k0, v0 = kc.clone(), vc.clone()
+    qkv = T(rng.standard_normal((H + 2 * Hkv) * D).astype(np.float32), gpu)
+    nw = torch.ones(D, device=gpu)
+    rope = ops.rope_table(S, D, 1e6).to(gpu)
+    n_split = ops.attn_default_split(Hkv, S)
+    ws = torch.zeros(ops.attn_workspace_bytes(H, Hkv, D, n_split) // 4 + 1, dtype=torch.int32, device=gpu)
+    for pos in (S, S + 1000, -1):
+        st = torch.tensor([0, pos, 0, 0], dtype=torch.int32, device=gpu)
+        out = torch.full((H * D,), 7.0, device=gpu)
+        ops.attn_decode(qkv, nw, nw, 1e-6, rope, kc, vc, S, st, out, H, Hkv, D, n_split, ws)
+        torch.cuda.synchronize()
+        assert out.abs().sum().item() == 0
+        assert torch.equal(kc, k0) and torch.equal(vc, v0)
+    assert ws[:Hkv].abs().sum().item() == 0
 
 
 # ------------------------------------------------------------------ MoE
