@@ -123,27 +123,39 @@ MF_DEVICE AttnSlice attn_slice(int len, int n_split, int split) {
     return {eff, start, min(start + chunk, len)};
 }
 
-// The K (or V) tile at position q of a slice's copy sequence: per super-chunk
-// its K tiles, then its V tiles.
+// Walks a slice's copy sequence: per super-chunk its K tiles, then its V
+// tiles. Advanced once per tile by the producer and by the consumer alike.
 struct AttnSeq {
-    int sc, t, n_sc, row0;
+    int sc_row0;  // first row of the current super-chunk
+    int t;        // tile within the K or V run
+    int n_sc;     // tiles in this super-chunk
     bool is_v;
+    MF_DEVICE void init(int start, int end) {
+        sc_row0 = start;
+        t = 0;
+        is_v = false;
+        n_sc = min(ATT_SC_TILES, (end - start + ATT_TILE - 1) / ATT_TILE);
+    }
+    MF_DEVICE int row0() const { return sc_row0 + t * ATT_TILE; }
+    MF_DEVICE void advance(int end) {
+        if (++t < n_sc) return;
+        t = 0;
+        if (!is_v) {
+            is_v = true;
+        } else {
+            is_v = false;
+            sc_row0 += ATT_SC;
+            n_sc = min(ATT_SC_TILES, (end - sc_row0 + ATT_TILE - 1) / ATT_TILE);
+        }
+    }
 };
-MF_DEVICE AttnSeq attn_seq(int q, int start, int nrows) {
-    AttnSeq s;
-    s.sc = q / (2 * ATT_SC_TILES);
-    const int w = q - s.sc * 2 * ATT_SC_TILES;
-    s.n_sc = min(ATT_SC_TILES, (nrows - s.sc * ATT_SC + ATT_TILE - 1) / ATT_TILE);
-    s.is_v = w >= s.n_sc;
-    s.t = s.is_v ? w - s.n_sc : w;
-    s.row0 = start + s.sc * ATT_SC + s.t * ATT_TILE;
-    return s;
-}
 
-// Query heads per KV head up to ATT_QREG_MAX keep their score-lane query
-// slices in registers; larger groups read them from shared memory (the reads
-// are broadcast within each quarter-warp and conflict-free across it).
-constexpr int ATT_QREG_MAX = 4;
+// Score lanes keep their query slices in registers when all heads' slices
+// take at most MF_ATT_QREG_FLOATS floats; otherwise they read them from
+// shared memory (broadcast within each quarter-warp, conflict-free across it).
+#ifndef MF_ATT_QREG_FLOATS
+#define MF_ATT_QREG_FLOATS 64
+#endif
 
 template <int G>
 __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)) attn_decode_kernel(const AttnParams p) {
@@ -195,20 +207,32 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
     // its values are taken from shared memory, so it is never copied.
     const int copy_end = (end == len) ? end - 1 : end;
 
+    // Copy pieces: thread (warp, lane) moves the 16 bytes at column 4*lane of
+    // tile rows warp + 8*i, i < 4 (one 512-byte row per warp instruction).
+    constexpr int CP_ROWS = NT / 32;  // rows per copy instruction
+    const int toff = warp * ATT_D + 4 * lane;
+    AttnSeq ps;  // producer position
+    ps.init(start, end);
+    int pslot = 0;
     auto issue = [&](int q) {
         if (q < nseq) {
-            const AttnSeq sq = attn_seq(q, start, nrows);
-            const int nvalid = min(ATT_TILE, copy_end - sq.row0);
-            float* dst = ring + (q % ATT_STAGES) * ATT_TILE_FLOATS;
-            const float* src = (sq.is_v ? vc : kc) + (size_t)sq.row0 * ATT_D;
+            const int row0 = ps.row0();
+            float* dst = ring + pslot * ATT_TILE_FLOATS + toff;
+            const float* src = (ps.is_v ? vc : kc) + (size_t)row0 * ATT_D + toff;
+            const int ncopy = copy_end - row0;
+            if (ncopy >= ATT_TILE) {
 #pragma unroll
-            for (int i = 0; i < ATT_TILE_FLOATS / 4 / NT; ++i) {
-                const int piece = tid + i * NT;
-                const int r = piece >> 5, c4 = piece & 31;
-                if (r < nvalid) cp_async16(dst + r * ATT_D + 4 * c4, src + (size_t)r * ATT_D + 4 * c4);
+                for (int i = 0; i < ATT_TILE / CP_ROWS; ++i)
+                    cp_async16(dst + i * CP_ROWS * ATT_D, src + (size_t)i * CP_ROWS * ATT_D);
+            } else {
+#pragma unroll
+                for (int i = 0; i < ATT_TILE / CP_ROWS; ++i)
+                    if (warp + i * CP_ROWS < ncopy) cp_async16(dst + i * CP_ROWS * ATT_D, src + (size_t)i * CP_ROWS * ATT_D);
             }
+            ps.advance(end);
         }
         cp_async_commit();  // one group per sequence slot, empty groups included
+        pslot = (pslot + 1 == ATT_STAGES) ? 0 : pslot + 1;
     };
 #pragma unroll 1
     for (int q = 0; q < ATT_STAGES - 1; ++q) issue(q);
@@ -237,27 +261,33 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
     __syncthreads();
 
     const float scale = 1.0f / sqrtf((float)ATT_D);  // src/ops/kernels.cpp:88
-    // score mapping: tile row r_k, 16 dims {4*(c8 + 8j) + e}
-    const int r_k = tid >> 3, c8 = tid & 7;
-    constexpr int QG = G <= ATT_QREG_MAX ? G : 1;
-    float4 qreg[QG][4];
-    if constexpr (G <= ATT_QREG_MAX) {
+    // score mapping: LPR lanes per tile row, each summing DPL dims
+    // {4*(c + LPR*j) + e}; a quarter-warp reads 128 contiguous bytes of one row
+    constexpr int LPR = G >= 8 ? 16 : 8;
+    constexpr int NJ = ATT_D / 4 / LPR;  // float4 chunks per lane
+    constexpr int RPP = NT / LPR;        // rows per pass
+    constexpr int NP = ATT_TILE / RPP;   // passes per tile
+    const int r_k = tid / LPR, c = tid % LPR;
+    constexpr bool QREG = G * NJ * 4 <= MF_ATT_QREG_FLOATS;
+    constexpr int QG = QREG ? G : 1;
+    float4 qreg[QG][NJ];
+    if constexpr (QREG) {
 #pragma unroll
         for (int g = 0; g < G; ++g)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) qreg[g][j] = *reinterpret_cast<const float4*>(&q_s[g][4 * (c8 + 8 * j)]);
+            for (int j = 0; j < NJ; ++j) qreg[g][j] = *reinterpret_cast<const float4*>(&q_s[g][4 * (c + LPR * j)]);
     }
     // after the reduce-scatter a lane holds the sums of heads h_lane .. h_lane + HPL - 1
-    constexpr int HPL = G >= 8 ? G / 8 : 1;
-    constexpr int LPH = G >= 8 ? 1 : 8 / G;  // lanes holding each head
+    constexpr int HPL = G >= LPR ? G / LPR : 1;
+    constexpr int LPH = G >= LPR ? 1 : LPR / G;  // lanes holding each head
     int h_lane = 0;
     {
         int n = G;
 #pragma unroll
-        for (int m = 4; m >= 1; m >>= 1)
+        for (int m = LPR / 2; m >= 1; m >>= 1)
             if (n >= 2) {
                 n >>= 1;
-                if (c8 & m) h_lane += n;
+                if (c & m) h_lane += n;
             }
     }
 
@@ -265,63 +295,74 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
 #pragma unroll
     for (int g = 0; g < G; ++g) o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
 
+    AttnSeq cq;  // consumer position
+    cq.init(start, end);
+    int cslot = 0;
+#pragma unroll 1
     for (int q = 0; q < nseq; ++q) {
         cp_async_wait<ATT_STAGES - 2>();
         __syncthreads();  // tile q landed for every thread; slot (q - 1) is free
         issue(q + ATT_STAGES - 1);
-        const AttnSeq sq = attn_seq(q, start, nrows);
-        const float* tile = ring + (q % ATT_STAGES) * ATT_TILE_FLOATS;
-        const int nvalid = min(ATT_TILE, end - sq.row0);  // rows of the slice in this tile
-        if (!sq.is_v) {
+        const float* tile = ring + cslot * ATT_TILE_FLOATS;
+        const int row0 = cq.row0();
+        const int nvalid = min(ATT_TILE, end - row0);  // rows of the slice in this tile
+        const bool has_pos = pos < row0 + ATT_TILE && pos >= row0;
+        if (!cq.is_v) {
             // ---- phase 1: scores of this tile's rows
-            float s[G];
 #pragma unroll
-            for (int g = 0; g < G; ++g) s[g] = 0.f;
-            if (r_k < nvalid) {
-                const float* krow = (sq.row0 + r_k == pos ? knew_s : tile + r_k * ATT_D) + 4 * c8;
+            for (int pp = 0; pp < NP; ++pp) {
+                const int r = r_k + pp * RPP;
+                float sv[G];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float4 k4 = *reinterpret_cast<const float4*>(krow + 32 * j);
+                for (int g = 0; g < G; ++g) sv[g] = 0.f;
+                if (r < nvalid) {
+                    const float* krow = tile + r * ATT_D + 4 * c;
+                    if (has_pos && row0 + r == pos) krow = knew_s + 4 * c;
 #pragma unroll
-                    for (int g = 0; g < G; ++g) {
-                        float4 q4;
-                        if constexpr (G <= ATT_QREG_MAX) q4 = qreg[g][j];
-                        else q4 = *reinterpret_cast<const float4*>(&q_s[g][4 * (c8 + 8 * j)]);
-                        s[g] = fmaf(q4.x, k4.x, s[g]);
-                        s[g] = fmaf(q4.y, k4.y, s[g]);
-                        s[g] = fmaf(q4.z, k4.z, s[g]);
-                        s[g] = fmaf(q4.w, k4.w, s[g]);
+                    for (int j = 0; j < NJ; ++j) {
+                        const float4 k4 = *reinterpret_cast<const float4*>(krow + 4 * LPR * j);
+#pragma unroll
+                        for (int g = 0; g < G; ++g) {
+                            float4 q4;
+                            if constexpr (QREG) q4 = qreg[g][j];
+                            else q4 = *reinterpret_cast<const float4*>(&q_s[g][4 * (c + LPR * j)]);
+                            sv[g] = fmaf(q4.x, k4.x, sv[g]);
+                            sv[g] = fmaf(q4.y, k4.y, sv[g]);
+                            sv[g] = fmaf(q4.z, k4.z, sv[g]);
+                            sv[g] = fmaf(q4.w, k4.w, sv[g]);
+                        }
                     }
                 }
-            }
-            // reduce-scatter over the 8 lanes of the row (xor 4, 2, 1)
-            int n = G;
+                // reduce-scatter over the LPR lanes of the row (xor LPR/2 .. 1)
+                int n = G;
 #pragma unroll
-            for (int m = 4; m >= 1; m >>= 1) {
-                if (n >= 2) {
-                    const int hn = n >> 1;
-                    const bool upper = (c8 & m) != 0;
+                for (int m = LPR / 2; m >= 1; m >>= 1) {
+                    if (n >= 2) {
+                        const int hn = n >> 1;
+                        const bool upper = (c & m) != 0;
 #pragma unroll
-                    for (int i = 0; i < hn; ++i) {
-                        const float send = upper ? s[i] : s[i + hn];
-                        const float keep = upper ? s[i + hn] : s[i];
-                        s[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+                        for (int i = 0; i < hn; ++i) {
+                            const float send = upper ? sv[i] : sv[i + hn];
+                            const float keep = upper ? sv[i + hn] : sv[i];
+                            sv[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+                        }
+                        n = hn;
+                    } else {
+                        sv[0] += __shfl_xor_sync(0xffffffffu, sv[0], m);
                     }
-                    n = hn;
-                } else {
-                    s[0] += __shfl_xor_sync(0xffffffffu, s[0], m);
                 }
-            }
-            if (c8 % LPH == 0) {
-                const int col = sq.t * ATT_TILE + r_k;
-                const bool valid = r_k < nvalid;
+                if (c % LPH == 0) {
+                    const int col = cq.t * ATT_TILE + r;
+                    const bool valid = r < nvalid;
 #pragma unroll
-                for (int i = 0; i < HPL; ++i) sc_s[(h_lane + i) * ATT_SC_STRIDE + col] = valid ? s[i] * scale : -INFINITY;
+                    for (int i = 0; i < HPL; ++i)
+                        sc_s[(h_lane + i) * ATT_SC_STRIDE + col] = valid ? sv[i] * scale : -INFINITY;
+                }
             }
         } else {
-            if (sq.t == 0) {
+            if (cq.t == 0) {
                 // ---- softmax step over the super-chunk (every K tile done: barrier above)
-                const int rows_sc = min(ATT_SC, end - (start + sq.sc * ATT_SC));
+                const int rows_sc = min(ATT_SC, end - cq.sc_row0);
                 for (int g = warp; g < G; g += ATT_WARPS) {
                     float* srow = sc_s + g * ATT_SC_STRIDE;
                     float mx = -INFINITY;
@@ -352,28 +393,50 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
             }
             // ---- phase 2: P.V, warp rows rb .. rb + 3, lane dims 4*lane .. 4*lane + 3
             const int rb = 4 * warp;
-            if (rb < nvalid) {
-                float4 pv[G];
+            const float* prow = sc_s + cq.t * ATT_TILE + rb;
+            if (nvalid == ATT_TILE && !has_pos) {
+                float4 v4[4];
 #pragma unroll
-                for (int g = 0; g < G; ++g)
-                    pv[g] = *reinterpret_cast<const float4*>(sc_s + g * ATT_SC_STRIDE + sq.t * ATT_TILE + rb);
+                for (int rr = 0; rr < 4; ++rr) v4[rr] = *reinterpret_cast<const float4*>(tile + (rb + rr) * ATT_D + 4 * lane);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float4 pv = *reinterpret_cast<const float4*>(prow + g * ATT_SC_STRIDE);
+                    const float pr[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+                    for (int rr = 0; rr < 4; ++rr) {
+                        o[g].x = fmaf(pr[rr], v4[rr].x, o[g].x);
+                        o[g].y = fmaf(pr[rr], v4[rr].y, o[g].y);
+                        o[g].z = fmaf(pr[rr], v4[rr].z, o[g].z);
+                        o[g].w = fmaf(pr[rr], v4[rr].w, o[g].w);
+                    }
+                }
+            } else if (rb < nvalid) {
+                // partial tile or the tile holding `pos`: rows past the slice end
+                // were never copied (weight 0, zeros), row `pos` comes from vnew_s
+                float4 v4[4];
 #pragma unroll
                 for (int rr = 0; rr < 4; ++rr) {
-                    if (rb + rr < nvalid) {  // rows past the slice end were never copied
-                        const float* vrow = (sq.row0 + rb + rr == pos) ? vnew_s : tile + (rb + rr) * ATT_D;
-                        const float4 v4 = *reinterpret_cast<const float4*>(vrow + 4 * lane);
+                    const float* vrow = (row0 + rb + rr == pos) ? vnew_s : tile + (rb + rr) * ATT_D;
+                    v4[rr] = (rb + rr < nvalid) ? *reinterpret_cast<const float4*>(vrow + 4 * lane)
+                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
 #pragma unroll
-                        for (int g = 0; g < G; ++g) {
-                            const float pg = f4_get(pv[g], rr);
-                            o[g].x = fmaf(pg, v4.x, o[g].x);
-                            o[g].y = fmaf(pg, v4.y, o[g].y);
-                            o[g].z = fmaf(pg, v4.z, o[g].z);
-                            o[g].w = fmaf(pg, v4.w, o[g].w);
-                        }
+                for (int g = 0; g < G; ++g) {
+                    const float4 pv = *reinterpret_cast<const float4*>(prow + g * ATT_SC_STRIDE);
+                    const float pr[4] = {pv.x, rb + 1 < nvalid ? pv.y : 0.f, rb + 2 < nvalid ? pv.z : 0.f,
+                                         rb + 3 < nvalid ? pv.w : 0.f};
+#pragma unroll
+                    for (int rr = 0; rr < 4; ++rr) {
+                        o[g].x = fmaf(pr[rr], v4[rr].x, o[g].x);
+                        o[g].y = fmaf(pr[rr], v4[rr].y, o[g].y);
+                        o[g].z = fmaf(pr[rr], v4[rr].z, o[g].z);
+                        o[g].w = fmaf(pr[rr], v4[rr].w, o[g].w);
                     }
                 }
             }
         }
+        cq.advance(end);
+        cslot = (cslot + 1 == ATT_STAGES) ? 0 : cslot + 1;
     }
     cp_async_wait<0>();
 

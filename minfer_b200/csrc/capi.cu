@@ -226,7 +226,8 @@ int run_gemv(int dtype, int xm, int ym, mf::GemvParams& p, long long units, cuda
     choose_shape(p.K, dtype, ym, &T, &R);
     const void* fn = gemv_ptr(dtype, xm, ym, T, R);
     MF_REQUIRE(fn != nullptr, MF_E_UNSUPPORTED, "no GEMV kernel for dtype %d", dtype);
-    const size_t xfloats = (ym == mf::Y_MOE_DOWN) ? (size_t)p.K * p.n_slots : (size_t)p.K;
+    // X_NORM keeps the norm weights beside x
+    const size_t xfloats = (ym == mf::Y_MOE_DOWN) ? (size_t)p.K * p.n_slots : (size_t)p.K * (xm == mf::X_NORM ? 2 : 1);
     const size_t smem = xfloats * sizeof(float);
     MF_REQUIRE(smem <= 200 * 1024, MF_E_UNSUPPORTED, "activation vector of %zu floats exceeds shared memory", xfloats);
     int bps = 0;
@@ -665,7 +666,8 @@ size_t mf_attn_workspace_bytes(int n_heads, int n_kv_heads, int d_head, int n_sp
 int mf_attn_default_split(int n_kv_heads, int max_seq) {
     if (n_kv_heads <= 0) return 1;
     int sms = num_sms();
-    int s = sms * mf::ATT_CTAS_PER_SM / n_kv_heads;
+    static const int ctas_per_sm = env_int("MF_ATT_CTAS_PER_SM", mf::ATT_CTAS_PER_SM);
+    int s = sms * ctas_per_sm / n_kv_heads;
     if (s < 1) s = 1;
     const int max_useful = (max_seq + mf::ATT_MIN_CHUNK - 1) / mf::ATT_MIN_CHUNK;
     if (s > max_useful) s = max_useful;

@@ -17,7 +17,8 @@
 //    the next step's loads are issued before the current step is reduced
 //    (two register buffers).
 //  * The activation vector lives in shared memory (optionally RMS-normalised
-//    in the prologue, which fuses the reference's separate rmsnorm pass).
+//    in the prologue, which fuses the reference's separate rmsnorm pass; the
+//    norm weights are staged before the dependency wait, x is read once).
 //  * Programmatic dependent launch: dense weight loads are issued before
 //    griddepcontrol.wait, so they overlap the previous kernel's tail.
 //    Everything written by earlier kernels is read through L2 (ld.cg).
@@ -163,11 +164,17 @@ __global__ void __launch_bounds__(T, MF_GEMV_MIN_BLOCKS) gemv_kernel(const GemvP
     };
 
     uint4 bufA[R][PC], bufB[R][PC];
-    // Dense weights do not depend on earlier kernels: start streaming them
-    // before the dependency wait. Expert ids come from the router kernel.
+    // Dense weights and norm weights do not depend on earlier kernels: start
+    // streaming them before the dependency wait. Expert ids come from the
+    // router kernel.
     if (tid == 0)
         for (int t = 0; t <= pf_ahead; ++t) prefetch_tile(t);
     if (!indirect && nitems > 0) load(bufA, 0);
+    if (XM == X_NORM)
+        for (int i = tid; i < K; i += T) xs[K + i] = __ldg(p.nw + i);
+    // Triggering this early lets the next kernel's CTAs become resident and
+    // start their own weight loads while this one runs (measured faster than
+    // triggering after the last weight load).
     pdl_launch_dependents();
     pdl_wait();
     if (YM == Y_MOE_DOWN) {
@@ -181,12 +188,14 @@ __global__ void __launch_bounds__(T, MF_GEMV_MIN_BLOCKS) gemv_kernel(const GemvP
         float ss = 0.f;
         for (int i = tid; i < K; i += T) {
             const float v = __ldcg(p.x + i);
+            xs[i] = v;
             ss = fmaf(v, v, ss);
         }
         ss = block_sum(ss, scratch);
         // src/ops/kernels.cpp:355-363: rms = sqrtf(ss/dim + eps); inv = 1/rms; out = inv*x*w
+        // (each thread rescales the elements it stored itself)
         const float inv = 1.0f / sqrtf(ss / (float)K + p.eps);
-        for (int i = tid; i < K; i += T) xs[i] = (inv * __ldcg(p.x + i)) * __ldg(p.nw + i);
+        for (int i = tid; i < K; i += T) xs[i] = (inv * xs[i]) * xs[K + i];
     } else {
         const int xlen = (YM == Y_MOE_DOWN) ? K * p.n_slots : K;
         for (int i = tid * 4; i < xlen; i += T * 4) {
