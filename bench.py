@@ -18,8 +18,11 @@ needed between steps.
 `--impl reference` runs the reference's own CPU token loop (oracle/_ref, built
 from the reference sources; the oracle port if absent) on the host cores on a
 bounded sample of the same workload.
-Multi-GPU runs (torchrun) use one rank per GPU, each decoding its own copy
-("replicas"): no tensor parallelism yet.
+Multi-GPU runs (torchrun, one rank per GPU) decode the same single stream
+with tensor parallelism over the N GPUs (strong scaling): each rank holds a
+1/N shard of every projection, the two all-reduces per layer are fused into
+the GEMVs over NVLink peer memory. `value` is then the tokens/s of that one
+stream, timed on the device as the max over ranks.
 """
 from __future__ import annotations
 
@@ -226,7 +229,7 @@ def main():
     config = {"workload": f"{args.workload} greedy decode at batch 1 after a {args.context}-token prompt",
               "context": args.context, "batch": 1,
               "l2": "inputs larger than L2 (each step streams all weights and the KV cache)",
-              "parallelism": "single" if world == 1 else f"replicas{world}"}
+              "parallelism": "single" if world == 1 else f"tp{world}"}
 
     if args.impl == "reference":
         if rank != 0:
@@ -236,7 +239,7 @@ def main():
         cb = run_reference_cpu(path, args.context, args.steps, args.warmup, thr)
         line = {"metric": METRIC, "value": round(cb["value"], 4), "unit": "tokens/s", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 / cb["value"], 3),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": config, "impl": "reference", "cpu_baseline": cb,
                 "e2e": {"value": round(cb["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
@@ -254,6 +257,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local_rank))
     from minfer_b200 import model as mm
+    from minfer_b200 import tp
     from minfer_b200._lib import check, cuda_lib
 
     mm.init(1, [local_rank])
@@ -262,11 +266,13 @@ def main():
     ctx = args.context
     n_tok = args.warmup + 2 * args.steps + 4
     t_load = time.perf_counter()
-    m = mm.Qwen3Model(path, mm.RunParams(num_iters=n_tok, max_seq_len=ctx + n_tok + 2), device=local_rank)
+    m = mm.Qwen3Model(path, mm.RunParams(num_iters=n_tok, max_seq_len=ctx + n_tok + 2), device=local_rank,
+                      tp_rank=rank, tp_size=world)
     m.set_device("cuda")
+    tp.connect(m)
     t_load = time.perf_counter() - t_load
     info = m.info
-    prompt = mm.random_prompt(ctx, info.vocab_size, 30 + rank)
+    prompt = mm.random_prompt(ctx, info.vocab_size, 30)
 
     # prefill (token by token through the decode frames), timed on the device
     check(lib.mf_timer_start(0))
@@ -306,7 +312,7 @@ def main():
     barrier()
     dev_ms = max_over_ranks(ms.value)
     pos += args.steps
-    value = world * args.steps / (dev_ms / 1e3)
+    value = args.steps / (dev_ms / 1e3)
 
     # ---- e2e: one reference-facing call per token, host in the loop
     barrier()
@@ -317,12 +323,21 @@ def main():
     check(lib.mf_timer_stop(0, C.byref(ms)))
     barrier()
     e2e_ms = max_over_ranks(ms.value)
-    e2e = world * args.steps / (e2e_ms / 1e3)
+    e2e = args.steps / (e2e_ms / 1e3)
 
     peaks, peak_kind = load_peaks()
     ctx_mid = ctx + args.warmup + args.steps // 2
+    # bytes every rank reads per token, summed over ranks (the replicated
+    # norms and embedding row are a few KB per layer)
     tb = token_bytes(info, ctx_mid)
-    step_gbs = tb / (dev_ms / args.steps / 1e3) / 1e9
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([tb], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t)
+        tb = t.item()
+    step_gbs = tb / (dev_ms / args.steps / 1e3) / 1e9 / world  # per GPU
+    status = m.comm_status()
     roof = time_dominant_kernel(cfgshape, peaks) if rank == 0 else None
 
     if rank == 0:
@@ -336,7 +351,7 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "compute": "fp32 accumulate, fp32 activations/KV",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "compute": "fp32 accumulate, fp32 activations/KV",
             "data": "synthetic (seeded GGUF, random prompt ids)", "config": config,
             "e2e": {"value": round(e2e, 3), "unit": "tokens/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 16,
                     "ms_per_step": round(e2e_ms / args.steps, 4)},
@@ -348,6 +363,9 @@ def main():
                         "method": "token-by-token decode frames"},
             "cpu_baseline": cpu, "clocks": clk.summary(), "load_seconds": round(t_load, 2),
         }
+        if world > 1:
+            line["tp"] = {"size": world, "exchange_status": status,
+                          "note": "hbm_roofline.achieved_gbs is per GPU; bytes_per_token summed over ranks"}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

@@ -125,9 +125,14 @@ void* mf_stream(int rank);
  * start and stop (CUDA events; stop waits for the stop event). */
 int mf_timer_start(int rank);
 int mf_timer_stop(int rank, float* ms);
-/* Host-visible step record copied to the device at the start of every frame
- * launch: {token, pos, next_token, chain}. Returns a pinned host pointer and the
+/* Host-visible step record (MF_STEP_RECORD_BYTES) copied to the device at the
+ * start of every frame launch: int32 {token, pos, next_token, chain, frame,
+ * 0, 0, 0}. `frame` is a sequence number the caller advances for every frame
+ * (a chained lm_head advances it on the device); the tensor-parallel
+ * exchange tags its messages with it. Returns a pinned host pointer and the
  * matching device pointer. */
+#define MF_STEP_RECORD_BYTES 32
+#define MF_STEP_FRAME 4 /* index of the frame field */
 int mf_step_state(int rank, int32_t** host, void** device);
 
 /* ===================================================================== */
@@ -224,6 +229,76 @@ int mf_moe_down_residual(float* x, const float* h, const void* w_down_exps, int 
 size_t mf_lm_head_workspace_bytes(void);
 int mf_lm_head(float* logits, const float* x, const float* norm_w, float eps, const void* w, int dtype, int vocab,
                int d_model, int vocab_offset, void* step_state, void* workspace, void* stream);
+
+/* ===================================================================== */
+/* Tensor parallelism over NVLink / NVSwitch peer memory                 */
+/* ===================================================================== */
+/* No reference counterpart: the reference runs one device
+ * (src/base/model.cpp:36-59). These calls split each decoder layer over
+ * tp_size GPUs, one process per GPU: Q/K/V by KV-head group, O by input
+ * columns, gate/up by FFN rows, down by FFN columns, lm_head by vocabulary
+ * rows; embeddings and norms are replicated. The two all-reduces per layer
+ * are fused into the GEMVs around them: the O and down projections store
+ * their partial rows straight into every rank's receive slot
+ * (mf_matmul_push), and the next RMSNorm GEMV reads all ranks' partials in
+ * its prologue and sums them in rank order with the residual
+ * (mf_allreduce_*). Each value travels in one 64-bit store with a 32-bit tag
+ * (frame * 256 + seq, frame from the step record's MF_STEP_FRAME field), so
+ * no memory fence or flag round trip is needed; waits are bounded by
+ * MF_COMM_TIMEOUT_MS (default 1000) and a wait that gives up sets a bit
+ * readable with mf_comm_status. No TMA, no multicast.
+ *
+ * Setup: mf_comm_create on every rank, exchange the MF_COMM_HANDLE_BYTES
+ * handles (any host channel, e.g. torch.distributed), mf_comm_connect with
+ * all handles ordered by tp_rank. Every rank then issues the same sequence of
+ * frames and exchange calls. `seq` numbers the exchanges within one frame
+ * (0 .. 254; consecutive exchanges alternate its parity, e.g. 2*layer and
+ * 2*layer + 1), and the step record's frame field must advance between
+ * frames. */
+#define MF_TP_MAX 8
+#define MF_COMM_HANDLE_BYTES 64
+typedef struct mf_comm mf_comm;
+/* max_floats: longest all-reduced vector (d_model, multiple of 4);
+ * gather_floats: length of the full-logits gather buffer (vocabulary size, or 0). */
+int mf_comm_create(int rank, int tp_rank, int tp_size, int max_floats, int gather_floats, mf_comm** out);
+int mf_comm_handle(const mf_comm* c, void* out, size_t n);
+/* A rank's own handle in another rank's place maps that peer to this rank's
+ * region: a loopback in which that peer never sends (its waits time out). */
+int mf_comm_connect(mf_comm* c, const void* handles, size_t n);
+/* COMM status bits (1: an all-reduce wait gave up, 2: a greedy-id exchange
+ * gave up); clear != 0 resets them. Synchronises the rank's stream. */
+int mf_comm_status(mf_comm* c, int* status, int clear);
+/* Device address of this rank's full-logits buffer (mf_allreduce_lm_head with gather_logits). */
+int mf_comm_gather_ptr(const mf_comm* c, float** logits);
+void mf_comm_destroy(mf_comm* c);
+
+/* All-reduce send fused into a GEMV: the partial W·a of this rank (W holds
+ * this rank's input columns) goes to every rank as exchange `seq`. */
+int mf_matmul_push(const float* a, const void* w, int dtype, int d_out, int d_in, mf_comm* c, int seq,
+                   const void* step_state, void* stream);
+/* All-reduce receive fused into an RMSNorm GEMV: x = x_res + sum of every
+ * rank's partial of exchange `seq` (rank order), x_out = x (written once),
+ * y = W · rmsnorm(x) (W holds this rank's output rows). */
+int mf_allreduce_rmsnorm_matmul(float* y, const float* x_res, float* x_out, const float* norm_w, float eps,
+                                const void* w, int dtype, int d_out, int d_in, mf_comm* c, int seq,
+                                const void* step_state, void* stream);
+/* The same receive fused into the SwiGLU gate/up GEMV (d_ff = this rank's rows). */
+int mf_allreduce_swiglu_matmul(float* h, const float* x_res, float* x_out, const float* norm_w, float eps,
+                               const void* w_gate_up, int dtype, int d_ff, int d_in, mf_comm* c, int seq,
+                               const void* step_state, void* stream);
+/* The same receive fused into the vocabulary-split lm_head: logits rows
+ * [vocab_offset, vocab_offset + vocab) of this rank. The greedy id is agreed
+ * over all ranks (every rank writes the same id to its step record and, for
+ * a chained record, advances it); with gather_logits every rank also receives
+ * all ranks' logits in its gather buffer (mf_comm_gather_ptr), complete when
+ * the kernel ends. step_state and workspace are required. */
+int mf_allreduce_lm_head(float* logits, const float* x_res, float* x_out, const float* norm_w, float eps,
+                         const void* w, int dtype, int vocab, int d_model, int vocab_offset, void* step_state,
+                         void* workspace, int gather_logits, mf_comm* c, int seq, void* stream);
+/* Stand-alone all-reduce of n floats (one kernel): x_out = x_res + sum over
+ * ranks of `partial` (rank order). x_out may equal x_res. */
+int mf_allreduce(float* x_out, const float* x_res, const float* partial, int n, mf_comm* c, int seq,
+                 const void* step_state, void* stream);
 
 /* ===================================================================== */
 /* Single ops with the reference's CPU signatures                        */

@@ -52,7 +52,8 @@ typedef struct mf_model_info {
     float rms_norm_eps, freq_base;
     size_t read_bytes_logits;    /* weight bytes one forward with logits reads */
     size_t read_bytes_no_logits; /* ... without the lm_head */
-    size_t kv_bytes_per_pos;     /* 2 * n_layers * n_kv_heads * d_head * 4 */
+    size_t kv_bytes_per_pos;     /* 2 * n_layers * n_kv_heads * d_head * 4 (this rank's heads) */
+    int tp_rank, tp_size;        /* tensor-parallel position of this process */
 } mf_model_info;
 
 /* GenStats (include/minfer/base/stats.hpp:3-15) */
@@ -68,6 +69,22 @@ typedef struct mf_gen_stats {
 int mf_model_load(const char* gguf_path, const mf_run_params* rp, int rank, mf_model** out);
 /* BaseModel::set_device(DeviceType::CUDA): upload weights, allocate RunState. */
 int mf_model_to_cuda(mf_model* m);
+
+/* Tensor parallelism (no reference counterpart; the reference runs one
+ * device): rank tp_rank of tp_size loads its shard of the GGUF (Q/K/V by
+ * KV-head group, O and down by input columns, gate/up by FFN rows, lm_head
+ * by vocabulary rows; dense FFN models). After mf_model_to_cuda every rank
+ * exports MF_COMM_HANDLE_BYTES with mf_model_comm_handle; the caller
+ * exchanges them (e.g. torch.distributed all_gather) and passes all of them,
+ * ordered by tp_rank, to mf_model_comm_connect. From then on every rank runs
+ * the same calls (forward / generate / decode_chained) with the same tokens;
+ * greedy ids and sampled ids come out identical on every rank. */
+int mf_model_load_tp(const char* gguf_path, const mf_run_params* rp, int rank, int tp_rank, int tp_size,
+                     mf_model** out);
+int mf_model_comm_handle(const mf_model* m, void* out, size_t n);
+int mf_model_comm_connect(mf_model* m, const void* handles, size_t n);
+/* Exchange status bits since the last call (0: every wait succeeded); synchronises. */
+int mf_model_comm_status(mf_model* m, int* status);
 int mf_model_info_get(const mf_model* m, mf_model_info* out);
 void mf_model_free(mf_model* m);
 

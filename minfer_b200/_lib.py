@@ -24,6 +24,10 @@ MF_E_STATE = -6
 MF_E_IO = -7
 
 MF_F32, MF_F16, MF_BF16 = 0, 1, 2
+MF_TP_MAX = 8
+MF_COMM_HANDLE_BYTES = 64
+MF_STEP_RECORD_BYTES = 32
+MF_STEP_FRAME = 4
 MF_FRAME_RECORD, MF_FRAME_REPLAY = 0, 1
 MF_GEN_STOP_AT_EOS, MF_GEN_MARGINS = 1, 2
 
@@ -57,7 +61,7 @@ class mf_model_info(C.Structure):
                 ("weight_dtype", C.c_int), ("untied_head", C.c_int), ("eos_token_id", C.c_uint32),
                 ("rms_norm_eps", C.c_float), ("freq_base", C.c_float),
                 ("read_bytes_logits", C.c_size_t), ("read_bytes_no_logits", C.c_size_t),
-                ("kv_bytes_per_pos", C.c_size_t)]
+                ("kv_bytes_per_pos", C.c_size_t), ("tp_rank", C.c_int), ("tp_size", C.c_int)]
 
 
 class mf_gen_stats(C.Structure):
@@ -123,6 +127,17 @@ CUDA_API = {
     "mf_moe_down_residual": (I, [P, P, P, I, P, P, I, I, I, P]),
     "mf_lm_head_workspace_bytes": (SZ, []),
     "mf_lm_head": (I, [P, P, P, F, P, I, I, I, I, P, P, P]),
+    "mf_comm_create": (I, [I, I, I, I, I, P]),
+    "mf_comm_handle": (I, [P, P, SZ]),
+    "mf_comm_connect": (I, [P, P, SZ]),
+    "mf_comm_status": (I, [P, P, I]),
+    "mf_comm_gather_ptr": (I, [P, P]),
+    "mf_comm_destroy": (None, [P]),
+    "mf_matmul_push": (I, [P, P, I, I, I, P, I, P, P]),
+    "mf_allreduce_rmsnorm_matmul": (I, [P, P, P, P, F, P, I, I, I, P, I, P, P]),
+    "mf_allreduce_swiglu_matmul": (I, [P, P, P, P, F, P, I, I, I, P, I, P, P]),
+    "mf_allreduce_lm_head": (I, [P, P, P, P, F, P, I, I, I, I, P, P, I, P, I, P]),
+    "mf_allreduce": (I, [P, P, P, I, P, I, P, P]),
     "mf_matmul": (I, [P, P, P, I, SZ, I, I, P]),
     "mf_rmsnorm": (I, [P, P, P, I, F, I, P]),
     "mf_softmax": (I, [P, P, I, I, P]),
@@ -139,6 +154,10 @@ HOST_API = {
     "mf_host_last_error": (I, [C.c_char_p, SZ]),
     "mf_model_load": (I, [C.c_char_p, P, I, P]),
     "mf_model_to_cuda": (I, [P]),
+    "mf_model_load_tp": (I, [C.c_char_p, P, I, I, I, P]),
+    "mf_model_comm_handle": (I, [P, P, SZ]),
+    "mf_model_comm_connect": (I, [P, P, SZ]),
+    "mf_model_comm_status": (I, [P, P]),
     "mf_model_info_get": (I, [P, P]),
     "mf_model_free": (None, [P]),
     "mf_model_forward": (I, [P, U32, I, I, I]),

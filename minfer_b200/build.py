@@ -29,7 +29,8 @@ NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-
 CXX_FLAGS = ["-std=c++17", "-O3", "-march=x86-64-v3", "-fPIC", "-Wall", "-Wextra", "-Wno-unused-parameter",
              f"-I{INCLUDE}", f"-I{HOST}"]
 
-CUDA_SOURCES = ["capi.cu", "attention.cu", "attn_noalloc.cu", "gemv_f32.cu", "gemv_f16.cu", "gemv_bf16.cu"]
+CUDA_SOURCES = ["capi.cu", "attention.cu", "attn_noalloc.cu", "gemv_f32.cu", "gemv_f16.cu", "gemv_bf16.cu",
+                "gemv_tp_f32.cu", "gemv_tp_f16.cu", "gemv_tp_bf16.cu"]
 HOST_SOURCES = ["gguf.cpp", "sampler.cpp", "model.cpp", "capi_model.cpp"]
 
 LIBMFCUDA = LIB / "libmfcuda.so"

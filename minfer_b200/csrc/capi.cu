@@ -7,12 +7,15 @@
 // weight prefetch overlaps its predecessor's tail, inside captured graphs too.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <cstddef>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <set>
 #include <string>
@@ -27,6 +30,16 @@ struct mf_buf {
     void* ptr;
     size_t bytes;
     int rank;
+};
+
+// One tensor-parallel rank's exchange state (see comm.cuh).
+struct mf_comm {
+    int rank = 0;         // manager rank (device) this comm lives on
+    char* region = nullptr;
+    std::vector<void*> opened;  // peers' regions mapped through CUDA IPC
+    mf::CommDev dev = {};
+    mf::CommLayout layout = {};
+    bool connected = false;
 };
 
 namespace mf {
@@ -59,7 +72,7 @@ int fail(int code, const char* fmt, ...) {
 struct Rank {
     int device = 0;
     cudaStream_t stream = nullptr;
-    int32_t* h_step = nullptr;  // pinned {token, pos, next_token, pad}
+    int32_t* h_step = nullptr;  // pinned step record (MF_STEP_RECORD_BYTES)
     void* d_step = nullptr;
     std::map<int, cudaGraphExec_t> frames;
     cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
@@ -175,6 +188,14 @@ int prepare(const void* fn, int threads, size_t smem, int* blocks_per_sm) {
 }
 
 const void* gemv_ptr(int dtype, int xm, int ym, int T, int R) {
+    if (xm == mf::X_AR_NORM || ym == mf::Y_PUSH) {
+        switch (dtype) {
+            case MF_F32: return mf::gemv_tp_kernel_ptr_f32(xm, ym, T, R);
+            case MF_F16: return mf::gemv_tp_kernel_ptr_f16(xm, ym, T, R);
+            case MF_BF16: return mf::gemv_tp_kernel_ptr_bf16(xm, ym, T, R);
+            default: return nullptr;
+        }
+    }
     switch (dtype) {
         case MF_F32: return mf::gemv_kernel_ptr_f32(xm, ym, T, R);
         case MF_F16: return mf::gemv_kernel_ptr_f16(xm, ym, T, R);
@@ -227,7 +248,8 @@ int run_gemv(int dtype, int xm, int ym, mf::GemvParams& p, long long units, cuda
     const void* fn = gemv_ptr(dtype, xm, ym, T, R);
     MF_REQUIRE(fn != nullptr, MF_E_UNSUPPORTED, "no GEMV kernel for dtype %d", dtype);
     // X_NORM keeps the norm weights beside x
-    const size_t xfloats = (ym == mf::Y_MOE_DOWN) ? (size_t)p.K * p.n_slots : (size_t)p.K * (xm == mf::X_NORM ? 2 : 1);
+    const bool norm = xm == mf::X_NORM || xm == mf::X_AR_NORM;
+    const size_t xfloats = (ym == mf::Y_MOE_DOWN) ? (size_t)p.K * p.n_slots : (size_t)p.K * (norm ? 2 : 1);
     const size_t smem = xfloats * sizeof(float);
     MF_REQUIRE(smem <= 200 * 1024, MF_E_UNSUPPORTED, "activation vector of %zu floats exceeds shared memory", xfloats);
     int bps = 0;
@@ -295,10 +317,10 @@ int mf_init(int n_ranks, const int* devices) {
                    ndev);
         MF_CK(cudaSetDevice(r.device));
         MF_CK(cudaStreamCreateWithFlags(&r.stream, cudaStreamNonBlocking));
-        MF_CK(cudaHostAlloc((void**)&r.h_step, 16, cudaHostAllocDefault));
-        std::memset(r.h_step, 0, 16);
-        MF_CK(cudaMalloc(&r.d_step, 16));
-        MF_CK(cudaMemset(r.d_step, 0, 16));
+        MF_CK(cudaHostAlloc((void**)&r.h_step, MF_STEP_RECORD_BYTES, cudaHostAllocDefault));
+        std::memset(r.h_step, 0, MF_STEP_RECORD_BYTES);
+        MF_CK(cudaMalloc(&r.d_step, MF_STEP_RECORD_BYTES));
+        MF_CK(cudaMemset(r.d_step, 0, MF_STEP_RECORD_BYTES));
     }
     MF_CK(cudaSetDevice(g.ranks[0].device));
     g.inited = true;
@@ -501,7 +523,7 @@ int mf_begin_frame_ex(int rank, int frame_id, int flags) {
     r.recording = frame_id;
     cudaError_t e = (flags & MF_FRAME_NO_UPLOAD)
                         ? cudaSuccess
-                        : cudaMemcpyAsync(r.d_step, r.h_step, 16, cudaMemcpyHostToDevice, r.stream);
+                        : cudaMemcpyAsync(r.d_step, r.h_step, MF_STEP_RECORD_BYTES, cudaMemcpyHostToDevice, r.stream);
     if (e != cudaSuccess) {
         cudaGraph_t gr = nullptr;
         cudaStreamEndCapture(r.stream, &gr);
@@ -798,6 +820,244 @@ int mf_lm_head(float* logits, const float* x, const float* norm_w, float eps, co
         p.step = (int*)step_state;
     }
     return run_gemv(dtype, mf::X_NORM, mf::Y_STORE, p, vocab, resolve(stream), LMH_MAX_GRID);
+}
+
+// ===================================================================== tensor parallelism
+
+int mf_comm_create(int rank, int tp_rank, int tp_size, int max_floats, int gather_floats, mf_comm** out) {
+    MF_REQUIRE(out, MF_E_INVALID, "null output");
+    MF_REQUIRE(g.inited && rank >= 0 && rank < (int)g.ranks.size(), MF_E_STATE, "mf_init first (rank %d)", rank);
+    MF_REQUIRE(tp_size >= 1 && tp_size <= MF_TP_MAX && tp_rank >= 0 && tp_rank < tp_size, MF_E_INVALID,
+               "tp_rank %d / tp_size %d", tp_rank, tp_size);
+    MF_REQUIRE(max_floats > 0 && max_floats % 4 == 0 && gather_floats >= 0, MF_E_INVALID,
+               "max_floats must be a positive multiple of 4");
+    MF_CK(cudaSetDevice(g.ranks[rank].device));
+    auto c = std::make_unique<mf_comm>();
+    c->rank = rank;
+    c->layout = mf::comm_layout(max_floats, gather_floats);
+    MF_REQUIRE(c->layout.total < (1ull << 32), MF_E_INVALID, "exchange region too large");
+    MF_CK(cudaMalloc((void**)&c->region, c->layout.total));
+    cudaError_t e = cudaMemset(c->region, 0, c->layout.total);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(c->region);
+        return fail(MF_E_CUDA, "exchange region: %s", cudaGetErrorString(e));
+    }
+    mf::CommDev& d = c->dev;
+    d.tp_rank = tp_rank;
+    d.tp_size = tp_size;
+    d.max_floats = max_floats;
+    d.gather_floats = gather_floats;
+    // MF_COMM_TIMEOUT_MS: how long an exchange wait polls before giving up
+    d.timeout_ns = 1000000ull * (unsigned long long)std::max(1, env_int("MF_COMM_TIMEOUT_MS", 1000));
+    d.off_recv = (uint32_t)c->layout.recv;
+    d.off_best = (uint32_t)c->layout.best;
+    d.off_gather = (uint32_t)c->layout.gather;
+    d.off_local = (uint32_t)c->layout.local;
+    d.base[tp_rank] = c->region;
+    c->connected = tp_size == 1;
+    *out = c.release();
+    return MF_OK;
+}
+
+int mf_comm_handle(const mf_comm* c, void* out, size_t n) {
+    MF_REQUIRE(c && out && n >= MF_COMM_HANDLE_BYTES, MF_E_INVALID, "bad arguments");
+    static_assert(sizeof(cudaIpcMemHandle_t) <= MF_COMM_HANDLE_BYTES, "IPC handle size");
+    MF_CK(cudaSetDevice(g.ranks[c->rank].device));
+    cudaIpcMemHandle_t h;
+    MF_CK(cudaIpcGetMemHandle(&h, c->region));
+    std::memset(out, 0, MF_COMM_HANDLE_BYTES);
+    std::memcpy(out, &h, sizeof(h));
+    return MF_OK;
+}
+
+int mf_comm_connect(mf_comm* c, const void* handles, size_t n) {
+    MF_REQUIRE(c && handles, MF_E_INVALID, "null argument");
+    const int T = c->dev.tp_size;
+    MF_REQUIRE(n == (size_t)T * MF_COMM_HANDLE_BYTES, MF_E_INVALID, "expected %d handles", T);
+    MF_REQUIRE(!c->connected || T == 1, MF_E_STATE, "already connected");
+    MF_CK(cudaSetDevice(g.ranks[c->rank].device));
+    cudaIpcMemHandle_t own;
+    MF_CK(cudaIpcGetMemHandle(&own, c->region));
+    for (int r = 0; r < T; ++r) {
+        if (r == c->dev.tp_rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, (const char*)handles + (size_t)r * MF_COMM_HANDLE_BYTES, sizeof(h));
+        if (std::memcmp(&h, &own, sizeof(h)) == 0) {
+            // this rank's own handle in a peer's place: the peer slot maps to
+            // this region (a loopback whose peer never sends; exercises the
+            // waits' time limit)
+            c->dev.base[r] = c->region;
+            continue;
+        }
+        void* p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (void* q : c->opened) cudaIpcCloseMemHandle(q);
+            c->opened.clear();
+            return fail(MF_E_CUDA, "open peer %d exchange region: %s", r, cudaGetErrorString(e));
+        }
+        c->opened.push_back(p);
+        c->dev.base[r] = (char*)p;
+    }
+    c->connected = true;
+    return MF_OK;
+}
+
+int mf_comm_status(mf_comm* c, int* status, int clear) {
+    MF_REQUIRE(c && status, MF_E_INVALID, "null argument");
+    Rank& r = g.ranks[c->rank];
+    MF_CK(cudaSetDevice(r.device));
+    MF_CK(cudaStreamSynchronize(r.stream));
+    int* dst = (int*)(c->region + c->layout.local + offsetof(mf::CommLocal, status));
+    MF_CK(cudaMemcpy(status, dst, sizeof(int), cudaMemcpyDeviceToHost));
+    if (clear) MF_CK(cudaMemset(dst, 0, sizeof(int)));
+    return MF_OK;
+}
+
+int mf_comm_gather_ptr(const mf_comm* c, float** logits) {
+    MF_REQUIRE(c && logits && c->dev.gather_floats > 0, MF_E_INVALID, "no gather buffer");
+    *logits = (float*)(c->region + c->layout.gather);
+    return MF_OK;
+}
+
+void mf_comm_destroy(mf_comm* c) {
+    if (!c) return;
+    if (c->rank < (int)g.ranks.size()) {
+        cudaSetDevice(g.ranks[c->rank].device);
+        cudaDeviceSynchronize();
+    }
+    for (void* q : c->opened) cudaIpcCloseMemHandle(q);
+    cudaFree(c->region);
+    delete c;
+}
+
+namespace {
+int comm_ready(const mf_comm* c, int seq, const void* step_state) {
+    MF_REQUIRE(c && c->connected, MF_E_STATE, "exchange not connected (mf_comm_connect)");
+    MF_REQUIRE(seq >= 0 && seq < mf::COMM_SEQ_GREEDY, MF_E_INVALID, "exchange number %d outside [0, %d)", seq,
+               mf::COMM_SEQ_GREEDY);
+    MF_REQUIRE(step_state, MF_E_INVALID, "the exchange needs the step record (frame tag)");
+    return MF_OK;
+}
+}  // namespace
+
+int mf_matmul_push(const float* a, const void* w, int dtype, int d_out, int d_in, mf_comm* c, int seq,
+                   const void* step_state, void* stream) {
+    MF_REQUIRE(a && w, MF_E_INVALID, "null argument");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    int rc = comm_ready(c, seq, step_state);
+    if (rc) return rc;
+    MF_REQUIRE(d_out <= c->dev.max_floats, MF_E_INVALID, "d_out %d exceeds the exchange slot (%d)", d_out,
+               c->dev.max_floats);
+    mf::GemvParams p = {};
+    p.w = w;
+    p.x = a;
+    p.rows = d_out;
+    p.K = d_in;
+    p.comm = c->dev;
+    p.ar_seq = seq;
+    p.step = (int*)step_state;
+    return run_gemv(dtype, mf::X_PLAIN, mf::Y_PUSH, p, d_out, resolve(stream));
+}
+
+int mf_allreduce_rmsnorm_matmul(float* y, const float* x_res, float* x_out, const float* norm_w, float eps,
+                                const void* w, int dtype, int d_out, int d_in, mf_comm* c, int seq,
+                                const void* step_state, void* stream) {
+    MF_REQUIRE(y && x_res && x_out && norm_w && w, MF_E_INVALID, "null argument");
+    MF_REQUIRE(x_out != x_res, MF_E_INVALID, "x_out must differ from x_res (other CTAs still read it)");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    int rc = comm_ready(c, seq, step_state);
+    if (rc) return rc;
+    MF_REQUIRE(d_in <= c->dev.max_floats, MF_E_INVALID, "d_in %d exceeds the exchange slot", d_in);
+    mf::GemvParams p = {};
+    p.w = w;
+    p.x_res = x_res;
+    p.x_out = x_out;
+    p.nw = norm_w;
+    p.eps = eps;
+    p.y = y;
+    p.rows = d_out;
+    p.K = d_in;
+    p.comm = c->dev;
+    p.ar_seq = seq;
+    p.step = (int*)step_state;
+    return run_gemv(dtype, mf::X_AR_NORM, mf::Y_STORE, p, d_out, resolve(stream));
+}
+
+int mf_allreduce_swiglu_matmul(float* h, const float* x_res, float* x_out, const float* norm_w, float eps,
+                               const void* w_gate_up, int dtype, int d_ff, int d_in, mf_comm* c, int seq,
+                               const void* step_state, void* stream) {
+    MF_REQUIRE(h && x_res && x_out && norm_w && w_gate_up, MF_E_INVALID, "null argument");
+    MF_REQUIRE(x_out != x_res, MF_E_INVALID, "x_out must differ from x_res (other CTAs still read it)");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    int rc = comm_ready(c, seq, step_state);
+    if (rc) return rc;
+    MF_REQUIRE(d_in <= c->dev.max_floats, MF_E_INVALID, "d_in %d exceeds the exchange slot", d_in);
+    mf::GemvParams p = {};
+    p.w = w_gate_up;
+    p.x_res = x_res;
+    p.x_out = x_out;
+    p.nw = norm_w;
+    p.eps = eps;
+    p.y = h;
+    p.rows = 2 * d_ff;
+    p.K = d_in;
+    p.comm = c->dev;
+    p.ar_seq = seq;
+    p.step = (int*)step_state;
+    return run_gemv(dtype, mf::X_AR_NORM, mf::Y_SWIGLU, p, d_ff, resolve(stream));
+}
+
+int mf_allreduce_lm_head(float* logits, const float* x_res, float* x_out, const float* norm_w, float eps,
+                         const void* w, int dtype, int vocab, int d_model, int vocab_offset, void* step_state,
+                         void* workspace, int gather_logits, mf_comm* c, int seq, void* stream) {
+    MF_REQUIRE(logits && x_res && x_out && norm_w && w, MF_E_INVALID, "null argument");
+    MF_REQUIRE(x_out != x_res, MF_E_INVALID, "x_out must differ from x_res (other CTAs still read it)");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    MF_REQUIRE(!step_state || workspace, MF_E_INVALID, "argmax needs a workspace");
+    MF_REQUIRE(step_state && workspace, MF_E_INVALID, "the exchange needs the step record and the workspace");
+    int rc = comm_ready(c, seq, step_state);
+    if (rc) return rc;
+    MF_REQUIRE(d_model <= c->dev.max_floats, MF_E_INVALID, "d_model %d exceeds the exchange slot", d_model);
+    MF_REQUIRE(!gather_logits || (long long)vocab_offset + vocab <= c->dev.gather_floats, MF_E_INVALID,
+               "logits rows [%d, %d) outside the gather buffer (%d)", vocab_offset, vocab_offset + vocab,
+               c->dev.gather_floats);
+    mf::GemvParams p = {};
+    p.w = w;
+    p.x_res = x_res;
+    p.x_out = x_out;
+    p.nw = norm_w;
+    p.eps = eps;
+    p.y = logits;
+    p.rows = vocab;
+    p.K = d_model;
+    p.vocab_offset = vocab_offset;
+    p.comm = c->dev;
+    p.ar_seq = seq;
+    p.gather_logits = gather_logits ? 1 : 0;
+    {
+        char* ws = (char*)workspace;
+        p.counter = (int*)ws;
+        p.best_val = (float*)(ws + 256);
+        p.best_idx = (int*)(ws + 256 + (size_t)LMH_MAX_GRID * sizeof(float));
+        p.step = (int*)step_state;
+    }
+    return run_gemv(dtype, mf::X_AR_NORM, mf::Y_STORE, p, vocab, resolve(stream), LMH_MAX_GRID);
+}
+
+int mf_allreduce(float* x_out, const float* x_res, const float* partial, int n, mf_comm* c, int seq,
+                 const void* step_state, void* stream) {
+    MF_REQUIRE(x_out && x_res && partial && n > 0, MF_E_INVALID, "bad arguments");
+    int rc = comm_ready(c, seq, step_state);
+    if (rc) return rc;
+    MF_REQUIRE(n <= c->dev.max_floats, MF_E_INVALID, "n %d exceeds the exchange slot", n);
+    const void* fn = (const void*)&mf::allreduce_kernel;
+    mf::CommDev dev = c->dev;
+    const mf::StepState* st = (const mf::StepState*)step_state;
+    void* args[] = {(void*)&partial, (void*)&x_res, (void*)&x_out, (void*)&n, (void*)&dev, (void*)&seq, (void*)&st};
+    MF_CK(launch(fn, dim3(1), dim3(1024), 0, resolve(stream), args));
+    return MF_OK;
 }
 
 // ===================================================================== single ops

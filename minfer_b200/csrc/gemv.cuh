@@ -24,12 +24,17 @@
 //    Everything written by earlier kernels is read through L2 (ld.cg).
 #pragma once
 
+#include "comm.cuh"
 #include "mf_common.cuh"
 
 namespace mf {
 
-enum XMode { X_PLAIN = 0, X_NORM = 1 };
-enum YMode { Y_STORE = 0, Y_RESID = 1, Y_SWIGLU = 2, Y_MOE_DOWN = 3 };
+// X_AR_NORM: the activation is the residual plus every tensor-parallel rank's
+// partial vector of an all-reduce (waited for in the prologue), then RMSNorm.
+// Y_PUSH: the rows' partial sums are stored into every rank's receive slot of
+// an all-reduce instead of locally.
+enum XMode { X_PLAIN = 0, X_NORM = 1, X_AR_NORM = 2 };
+enum YMode { Y_STORE = 0, Y_RESID = 1, Y_SWIGLU = 2, Y_MOE_DOWN = 3, Y_PUSH = 4 };
 
 struct GemvParams {
     const void* w;        // weight rows, dtype given by the template
@@ -52,14 +57,23 @@ struct GemvParams {
     int* step;                  // device step record {token, pos, next_token, chain}
     int vocab_offset;           // index of row 0 (vocab-split lm_head)
     int pf_tiles;               // L2 prefetch depth in tiles (tiles <= 48 KB)
+    // tensor parallelism (X_AR_NORM, Y_PUSH, and the lm_head's cross-rank argmax)
+    CommDev comm;
+    int ar_seq;                 // exchange number within the frame (slot = ar_seq & 1); tag from step[frame]
+    const float* x_res;         // X_AR_NORM: residual before the all-reduce
+    float* x_out;               // X_AR_NORM: residual after it (written by CTA 0)
+    int gather_logits;          // Y_STORE + TP: also store rows into every rank's full-logits buffer
 };
 
 #ifndef MF_GEMV_MIN_BLOCKS
 #define MF_GEMV_MIN_BLOCKS 1
 #endif
 
+// The all-reduce receive prologue holds tagged words next to the first
+// weight loads: keep such kernels at two resident CTAs per SM.
 template <typename W, int T, int R, int PC, int XM, int YM>
-__global__ void __launch_bounds__(T, MF_GEMV_MIN_BLOCKS) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2) ? 2 : MF_GEMV_MIN_BLOCKS)
+    gemv_kernel(const GemvParams p) {
     constexpr int VEC = W::VEC;
     constexpr int NW = T / 32;
     constexpr int RU = (YM == Y_SWIGLU) ? 2 : 1;  // rows per unit
@@ -170,7 +184,7 @@ __global__ void __launch_bounds__(T, MF_GEMV_MIN_BLOCKS) gemv_kernel(const GemvP
     if (tid == 0)
         for (int t = 0; t <= pf_ahead; ++t) prefetch_tile(t);
     if (!indirect && nitems > 0) load(bufA, 0);
-    if (XM == X_NORM)
+    if (XM == X_NORM || XM == X_AR_NORM)
         for (int i = tid; i < K; i += T) xs[K + i] = __ldg(p.nw + i);
     // Triggering this early lets the next kernel's CTAs become resident and
     // start their own weight loads while this one runs (measured faster than
@@ -183,13 +197,33 @@ __global__ void __launch_bounds__(T, MF_GEMV_MIN_BLOCKS) gemv_kernel(const GemvP
     }
     if (indirect && nitems > 0) load(bufA, 0);
 
+    // tagged words of a push (tensor-parallel send)
+    uint32_t push_tag = 0;
+    if (YM == Y_PUSH) push_tag = comm_tag(__ldcg(p.step + MF_STEP_FRAME), p.ar_seq);
+
     // ---- prologue: activation vector(s) -> shared memory
-    if (XM == X_NORM) {
+    if (XM == X_NORM || XM == X_AR_NORM) {
         float ss = 0.f;
-        for (int i = tid; i < K; i += T) {
-            const float v = __ldcg(p.x + i);
-            xs[i] = v;
-            ss = fmaf(v, v, ss);
+        if (XM == X_AR_NORM) {
+            // all-reduce receive: x = residual + partial_0 + partial_1 + ...
+            // in rank order (identical on every rank), each partial element
+            // read once its tag shows it is this exchange's
+            const uint32_t tag = comm_tag(__ldcg(p.step + MF_STEP_FRAME), p.ar_seq);
+            const int slot = p.ar_seq & 1;
+            int* status = &p.comm.local()->status;
+            const unsigned long long deadline = globaltimer_ns() + p.comm.timeout_ns;
+            bool late = false;
+            recv_sum(p.comm, slot, tag, p.x_res, tid, T, K, deadline, &late, status, [&](int i, float v) {
+                xs[i] = v;
+                ss = fmaf(v, v, ss);
+                if (blockIdx.x == 0) p.x_out[i] = v;
+            });
+        } else {
+            for (int i = tid; i < K; i += T) {
+                const float v = __ldcg(p.x + i);
+                xs[i] = v;
+                ss = fmaf(v, v, ss);
+            }
         }
         ss = block_sum(ss, scratch);
         // src/ops/kernels.cpp:355-363: rms = sqrtf(ss/dim + eps); inv = 1/rms; out = inv*x*w
@@ -293,8 +327,14 @@ __global__ void __launch_bounds__(T, MF_GEMV_MIN_BLOCKS) gemv_kernel(const GemvP
                     for (int w2 = 0; w2 < NW; ++w2) s += red[par][w2][lane];
                     if (YM == Y_RESID) {
                         p.y[lr] = __ldcg(p.y + lr) + s;  // src/models/qwen3/module.cpp:238-240
+                    } else if (YM == Y_PUSH) {
+                        const unsigned long long w = tagged(s, push_tag);
+                        for (int r = 0; r < p.comm.tp_size; ++r)
+                            st_tagged(p.comm.recv(r, p.ar_seq & 1, p.comm.tp_rank) + lr, w);
                     } else {
                         p.y[lr] = s;
+                        if (YM == Y_STORE && p.gather_logits)
+                            for (int r = 0; r < p.comm.tp_size; ++r) p.comm.gather(r)[p.vocab_offset + lr] = s;
                     }
                 }
                 if (YM == Y_STORE && p.counter != nullptr) {
@@ -339,6 +379,7 @@ __global__ void __launch_bounds__(T, MF_GEMV_MIN_BLOCKS) gemv_kernel(const GemvP
 
     // ---- greedy argmax finisher: the last CTA reduces the per-CTA candidates
     if (YM == Y_STORE && p.counter != nullptr) {
+        if (p.gather_logits && warp == 0) __threadfence_system();  // logits rows stored on peers
         __syncthreads();
         if (tid == 0) {
             p.best_val[blockIdx.x] = cta_best_v;
@@ -376,12 +417,39 @@ __global__ void __launch_bounds__(T, MF_GEMV_MIN_BLOCKS) gemv_kernel(const GemvP
                 }
                 // no candidate (every logit NaN): std::max_element returns the first element
                 if (fi == 0x7fffffff) fi = p.vocab_offset;
+                if (p.comm.tp_size > 1) {
+                    // vocab split over ranks: exchange the per-rank maxima as
+                    // tagged words, then reduce them in rank order (every rank
+                    // picks the same id). In gather mode every CTA fenced its
+                    // logits stores before its ticket, so they are visible on
+                    // the peers before this rank's maximum is.
+                    const uint32_t tag = comm_tag(p.step[MF_STEP_FRAME], COMM_SEQ_GREEDY);
+                    const unsigned long long wv = tagged(fv, tag), wi = tagged(__int_as_float(fi), tag);
+                    for (int r = 0; r < p.comm.tp_size; ++r) {
+                        st_tagged(p.comm.best(r) + 2 * p.comm.tp_rank, wv);
+                        st_tagged(p.comm.best(r) + 2 * p.comm.tp_rank + 1, wi);
+                    }
+                    int* status = &p.comm.local()->status;
+                    const unsigned long long deadline = globaltimer_ns() + p.comm.timeout_ns;
+                    bool late = false;
+                    const unsigned long long* b = p.comm.best(p.comm.tp_rank);
+                    for (int r = 0; r < p.comm.tp_size; ++r) {
+                        const float v = recv_tagged(b + 2 * r, tag, deadline, &late, status, COMM_STATUS_LM_TIMEOUT);
+                        const int i = __float_as_int(
+                            recv_tagged(b + 2 * r + 1, tag, deadline, &late, status, COMM_STATUS_LM_TIMEOUT));
+                        if (r == 0 || better(v, i, fv, fi)) {
+                            fv = v;
+                            fi = i;
+                        }
+                    }
+                }
                 // greedy id -> next_token; a chained record also becomes the
                 // next step's input so decode can continue without the host
                 p.step[2] = fi;
                 if (p.step[3] != 0) {
                     p.step[0] = fi;
                     p.step[1] = p.step[1] + 1;
+                    p.step[MF_STEP_FRAME] = p.step[MF_STEP_FRAME] + 1;
                 }
                 *p.counter = 0;
             }

@@ -36,8 +36,20 @@ const void* gemv_kernel_ptr(int xm, int ym, int T, int R) {
     return nullptr;
 }
 
+// Tensor-parallel modes (all-reduce receive / send), compiled in gemv_tp_*.cu.
+template <typename W>
+const void* gemv_tp_kernel_ptr(int xm, int ym, int T, int R) {
+    if (xm == X_AR_NORM && ym == Y_STORE) return gemv_ptr_rpc<W, X_AR_NORM, Y_STORE>(T, R);
+    if (xm == X_AR_NORM && ym == Y_SWIGLU) return gemv_ptr_rpc<W, X_AR_NORM, Y_SWIGLU>(T, R);
+    if (xm == X_PLAIN && ym == Y_PUSH) return gemv_ptr_rpc<W, X_PLAIN, Y_PUSH>(T, R);
+    return nullptr;
+}
+
 const void* gemv_kernel_ptr_f32(int xm, int ym, int T, int R);
 const void* gemv_kernel_ptr_f16(int xm, int ym, int T, int R);
 const void* gemv_kernel_ptr_bf16(int xm, int ym, int T, int R);
+const void* gemv_tp_kernel_ptr_f32(int xm, int ym, int T, int R);
+const void* gemv_tp_kernel_ptr_f16(int xm, int ym, int T, int R);
+const void* gemv_tp_kernel_ptr_bf16(int xm, int ym, int T, int R);
 
 }  // namespace mf

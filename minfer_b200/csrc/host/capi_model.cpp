@@ -45,6 +45,11 @@ int mf_host_last_error(char* buf, size_t n) {
 }
 
 int mf_model_load(const char* gguf_path, const mf_run_params* rp, int rank, mf_model** out) {
+    return mf_model_load_tp(gguf_path, rp, rank, 0, 1, out);
+}
+
+int mf_model_load_tp(const char* gguf_path, const mf_run_params* rp, int rank, int tp_rank, int tp_size,
+                     mf_model** out) {
     if (!gguf_path || !rp || !out) return herr(MF_E_INVALID, "null argument");
     g_host_err[0] = 0;
     minfer::RunParams p;
@@ -59,7 +64,7 @@ int mf_model_load(const char* gguf_path, const mf_run_params* rp, int rank, mf_m
     MF_TRY({
         auto* h = new mf_model;
         try {
-            h->m = std::make_unique<minfer::Qwen3Model>(gguf_path, p, rank);
+            h->m = std::make_unique<minfer::Qwen3Model>(gguf_path, p, rank, tp_rank, tp_size);
         } catch (...) {
             delete h;
             throw;
@@ -74,6 +79,26 @@ int mf_model_to_cuda(mf_model* m) {
     g_host_err[0] = 0;
     MF_TRY(m->m->set_device(minfer::DeviceType::CUDA));
     return MF_OK;
+}
+
+int mf_model_comm_handle(const mf_model* m, void* out, size_t n) {
+    if (!m || !out) return herr(MF_E_INVALID, "null argument");
+    g_host_err[0] = 0;
+    MF_TRY(m->m->comm_handle(out, n));
+    return MF_OK;
+}
+
+int mf_model_comm_connect(mf_model* m, const void* handles, size_t n) {
+    if (!m || !handles) return herr(MF_E_INVALID, "null argument");
+    g_host_err[0] = 0;
+    MF_TRY(m->m->comm_connect(handles, n));
+    return MF_OK;
+}
+
+int mf_model_comm_status(mf_model* m, int* status) {
+    if (!m || !status) return herr(MF_E_INVALID, "null argument");
+    const int rc = m->m->comm_status(status);
+    return rc ? herr(rc, "exchange status read failed") : MF_OK;
 }
 
 int mf_model_info_get(const mf_model* m, mf_model_info* out) {
@@ -99,7 +124,9 @@ int mf_model_info_get(const mf_model* m, mf_model_info* out) {
         out->read_bytes_logits = m->m->read_bytes(true);
         out->read_bytes_no_logits = m->m->read_bytes(false);
     }
-    out->kv_bytes_per_pos = 2ull * c.n_layers * c.n_kv_heads * c.d_head * sizeof(float);
+    out->kv_bytes_per_pos = 2ull * c.n_layers * c.kv_heads_local() * c.d_head * sizeof(float);
+    out->tp_rank = c.tp_rank;
+    out->tp_size = c.tp_size;
     return MF_OK;
 }
 

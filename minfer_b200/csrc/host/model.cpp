@@ -43,6 +43,27 @@ void expect_shape(const TensorView& t, std::initializer_list<uint64_t> shape) {
     }
 }
 
+// Rows [r0, r0 + n) of a row-major tensor, uploaded as one contiguous buffer.
+mf_buf* upload_rows(const TensorView& t, size_t r0, size_t n, size_t row_bytes, int rank) {
+    if ((r0 + n) * row_bytes > t.bytes) throw std::runtime_error("row slice outside tensor " + t.name);
+    mf_buf* b = nullptr;
+    check(mf_upload((const char*)t.data + r0 * row_bytes, n * row_bytes, rank, &b), ("upload " + t.name).c_str());
+    return b;
+}
+
+// Columns [c0, c0 + nc) (in bytes: col0_bytes, width_bytes) of every row of a
+// row-major [rows, row_bytes] tensor, packed into a new [rows, width] buffer.
+mf_buf* upload_cols(const TensorView& t, size_t rows, size_t row_bytes, size_t col0_bytes, size_t width_bytes,
+                    int rank) {
+    if (rows * row_bytes != t.bytes || col0_bytes + width_bytes > row_bytes)
+        throw std::runtime_error("column slice outside tensor " + t.name);
+    mf_buf* b = nullptr;
+    check(mf_alloc(rows * width_bytes, rank, &b), ("alloc " + t.name).c_str());
+    check(mf_write_2d(b, 0, width_bytes, (const char*)t.data + col0_bytes, row_bytes, width_bytes, rows),
+          ("upload " + t.name).c_str());
+    return b;
+}
+
 void expect_f32(const TensorView& t) {
     // norms and the router are fp32 (src/base/module.cpp:64,88-93,130-134)
     if (t.dtype != DataType::F32) throw std::runtime_error("tensor " + t.name + " must be F32");
@@ -108,23 +129,39 @@ public:
         expect_f32(kn);
         expect_f32(an);
         dtype_ = mf_dtype(wq.dtype);
-        // fused [Wq; Wk; Wv] so one streaming pass computes q|k|v
-        check(mf_alloc(wq.bytes + wk.bytes + wv.bytes, rank, &wqkv_), "alloc qkv");
-        check(mf_write(wqkv_, 0, wq.data, wq.bytes), "upload q");
-        check(mf_write(wqkv_, wq.bytes, wk.data, wk.bytes), "upload k");
-        check(mf_write(wqkv_, wq.bytes + wk.bytes, wv.data, wv.bytes), "upload v");
+        // fused [Wq; Wk; Wv] so one streaming pass computes q|k|v; under
+        // tensor parallelism this rank's KV-head group: Q heads and K/V heads
+        // [t*H/T, (t+1)*H/T), and the matching input columns of Wo
+        const size_t esz = dtype_size(wq.dtype), rowb = d * esz, t = c_.tp_rank;
+        const size_t ql = (size_t)c_.heads_local() * c_.d_head, kvl = (size_t)c_.kv_heads_local() * c_.d_head;
+        const char* qsrc = (const char*)wq.data + t * ql * rowb;
+        const char* ksrc = (const char*)wk.data + t * kvl * rowb;
+        const char* vsrc = (const char*)wv.data + t * kvl * rowb;
+        check(mf_alloc((ql + 2 * kvl) * rowb, rank, &wqkv_), "alloc qkv");
+        check(mf_write(wqkv_, 0, qsrc, ql * rowb), "upload q");
+        check(mf_write(wqkv_, ql * rowb, ksrc, kvl * rowb), "upload k");
+        check(mf_write(wqkv_, (ql + kvl) * rowb, vsrc, kvl * rowb), "upload v");
         own(wqkv_);
-        own(wo_ = upload_tensor(wo, rank));
+        own(wo_ = c_.tp_size == 1 ? upload_tensor(wo, rank) : upload_cols(wo, d, q * esz, t * ql * esz, ql * esz, rank));
         own(qn_ = upload_tensor(qn, rank));
         own(kn_ = upload_tensor(kn, rank));
         own(an_ = upload_tensor(an, rank));
-        read_bytes_ = wq.bytes + wk.bytes + wv.bytes + wo.bytes + qn.bytes + kn.bytes + an.bytes;
+        read_bytes_ = (ql + 2 * kvl) * rowb + d * ql * esz + qn.bytes + kn.bytes + an.bytes;
     }
     void cuda_forward(RunState& rs) override {
-        const int d = c_.d_model, H = c_.n_heads, Hkv = c_.n_kv_heads, D = c_.d_head;
-        check(mf_rmsnorm_matmul((float*)mf_ptr(rs.qkv), (const float*)mf_ptr(rs.x), (const float*)mf_ptr(an_),
-                                c_.rms_norm_eps, mf_ptr(wqkv_), dtype_, (H + 2 * Hkv) * D, d, rs.stream),
-              "qkv projection");
+        const int d = c_.d_model, H = c_.heads_local(), Hkv = c_.kv_heads_local(), D = c_.d_head;
+        if (c_.tp_size == 1 || layer_ == 0) {
+            check(mf_rmsnorm_matmul((float*)mf_ptr(rs.qkv), (const float*)mf_ptr(rs.x), (const float*)mf_ptr(an_),
+                                    c_.rms_norm_eps, mf_ptr(wqkv_), dtype_, (H + 2 * Hkv) * D, d, rs.stream),
+                  "qkv projection");
+        } else {
+            // receive the previous layer's down-projection all-reduce
+            check(mf_allreduce_rmsnorm_matmul((float*)mf_ptr(rs.qkv), (const float*)mf_ptr(rs.xb[1]),
+                                              (float*)mf_ptr(rs.xb[0]), (const float*)mf_ptr(an_), c_.rms_norm_eps,
+                                              mf_ptr(wqkv_), dtype_, (H + 2 * Hkv) * D, d, rs.comm, 2 * layer_ - 1,
+                                              rs.d_step, rs.stream),
+                  "qkv projection (all-reduce)");
+        }
         mf_attn_desc a = {};
         a.qkv = (const float*)mf_ptr(rs.qkv);
         a.q_norm_w = (const float*)mf_ptr(qn_);
@@ -142,9 +179,15 @@ public:
         a.n_split = rs.attn_split;
         a.workspace = mf_ptr(rs.attn_ws);
         check(mf_attn_decode(&a, rs.stream), "attention");
-        check(mf_matmul_residual((float*)mf_ptr(rs.x), (const float*)mf_ptr(rs.att), mf_ptr(wo_), dtype_, d, H * D,
-                                 rs.stream),
-              "output projection");
+        if (c_.tp_size == 1) {
+            check(mf_matmul_residual((float*)mf_ptr(rs.x), (const float*)mf_ptr(rs.att), mf_ptr(wo_), dtype_, d,
+                                     H * D, rs.stream),
+                  "output projection");
+        } else {
+            check(mf_matmul_push((const float*)mf_ptr(rs.att), mf_ptr(wo_), dtype_, d, H * D, rs.comm, 2 * layer_,
+                                 rs.d_step, rs.stream),
+                  "output projection (all-reduce send)");
+        }
     }
 
 private:
@@ -182,16 +225,23 @@ public:
             throw std::runtime_error("FFN weights of layer " + std::to_string(layer_) + " differ in dtype");
         dtype_ = mf_dtype(wg.dtype);
         own(fn_ = upload_tensor(fn, rank));
-        // gate/up interleaved by row: row 2i = gate_i, 2i+1 = up_i (per expert)
-        const size_t row = (size_t)d * dtype_size(wg.dtype);
-        const size_t nrows = wg.numel / d;
-        check(mf_alloc(wg.bytes + wu.bytes, rank, &wgu_), "alloc gate/up");
-        check(mf_write_2d(wgu_, 0, 2 * row, wg.data, row, row, nrows), "upload gate");
-        check(mf_write_2d(wgu_, row, 2 * row, wu.data, row, row, nrows), "upload up");
+        // gate/up interleaved by row: row 2i = gate_i, 2i+1 = up_i (per expert);
+        // under tensor parallelism (dense) this rank's FFN rows
+        // [t*F/T, (t+1)*F/T) and the matching input columns of W_down
+        const size_t esz = dtype_size(wg.dtype), row = (size_t)d * esz;
+        const size_t Fl = moe ? F : (size_t)c_.ff_local(), t = moe ? 0 : c_.tp_rank;
+        const size_t nrows = moe ? wg.numel / d : Fl;
+        const char* gsrc = (const char*)wg.data + t * Fl * row;
+        const char* usrc = (const char*)wu.data + t * Fl * row;
+        check(mf_alloc(2 * nrows * row, rank, &wgu_), "alloc gate/up");
+        check(mf_write_2d(wgu_, 0, 2 * row, gsrc, row, row, nrows), "upload gate");
+        check(mf_write_2d(wgu_, row, 2 * row, usrc, row, row, nrows), "upload up");
         own(wgu_);
-        own(wd_ = upload_tensor(wd, rank));
+        own(wd_ = (moe || c_.tp_size == 1) ? upload_tensor(wd, rank)
+                                           : upload_cols(wd, d, F * esz, t * Fl * esz, Fl * esz, rank));
         const size_t k = moe ? (size_t)c_.n_active_experts : 1, ne = moe ? E : 1;
-        read_bytes_ = fn.bytes + (wg.bytes / ne + wu.bytes / ne + wd.bytes / ne) * k;
+        read_bytes_ = moe ? fn.bytes + (wg.bytes / ne + wu.bytes / ne + wd.bytes / ne) * k
+                          : fn.bytes + 2 * Fl * row + d * Fl * esz;
         if (moe) {
             const TensorView& wr = f.tensor(p + "ffn_gate_inp.weight");
             expect_shape(wr, {E, d});
@@ -204,6 +254,17 @@ public:
         const int d = c_.d_model, F = c_.d_ff;
         float* x = (float*)mf_ptr(rs.x);
         float* h = (float*)mf_ptr(rs.h);
+        if (c_.n_experts == 0 && c_.tp_size > 1) {
+            // receive the attention all-reduce (exchange 2l), send the FFN's (2l + 1)
+            const int Fl = c_.ff_local();
+            check(mf_allreduce_swiglu_matmul(h, (const float*)mf_ptr(rs.xb[0]), (float*)mf_ptr(rs.xb[1]),
+                                             (const float*)mf_ptr(fn_), c_.rms_norm_eps, mf_ptr(wgu_), dtype_, Fl, d,
+                                             rs.comm, 2 * layer_, rs.d_step, rs.stream),
+                  "gate/up projection (all-reduce)");
+            check(mf_matmul_push(h, mf_ptr(wd_), dtype_, d, Fl, rs.comm, 2 * layer_ + 1, rs.d_step, rs.stream),
+                  "down projection (all-reduce send)");
+            return;
+        }
         if (c_.n_experts == 0) {
             check(mf_swiglu_matmul(h, x, (const float*)mf_ptr(fn_), c_.rms_norm_eps, mf_ptr(wgu_), dtype_, F, d,
                                    rs.stream),
@@ -240,23 +301,39 @@ public:
         expect_shape(on, {(uint64_t)c_.d_model});
         expect_f32(on);
         own(on_ = upload_tensor(on, rank));
+        // under tensor parallelism this rank's vocabulary rows
+        const size_t V0 = c_.vocab_offset(), Vl = c_.vocab_local();
         if (c_.untied_head) {
             const TensorView& t = f.tensor("output.weight");
             expect_shape(t, {c_.vocab_size, (uint64_t)c_.d_model});
             dtype_ = mf_dtype(t.dtype);
-            own(w_ = upload_tensor(t, rank));
-            head_bytes_ = t.bytes;
+            const size_t rowb = t.bytes / c_.vocab_size;
+            own(w_ = c_.tp_size == 1 ? upload_tensor(t, rank) : upload_rows(t, V0, Vl, rowb, rank));
+            head_bytes_ = Vl * rowb;
         } else {
             const TensorView& t = f.tensor("token_embd.weight");
-            w_ = embed_->weight();  // tied (src/models/qwen3/model.cpp:79-85)
+            w_ = embed_->weight();  // tied (src/models/qwen3/model.cpp:79-85); the table stays whole
             dtype_ = embed_->dtype();
-            head_bytes_ = t.bytes;
+            const size_t rowb = t.bytes / c_.vocab_size;
+            w_off_ = V0 * rowb;
+            head_bytes_ = Vl * rowb;
         }
         norm_bytes_ = on.bytes;
         read_bytes_ = head_bytes_ + norm_bytes_;
     }
     void cuda_forward(RunState& rs) override {
         if (!rs.compute_logits) return;
+        if (c_.tp_size > 1) {
+            // receive the last down-projection all-reduce; greedy id agreed
+            // over ranks; full logits gathered when the host wants them
+            check(mf_allreduce_lm_head((float*)mf_ptr(rs.logits), (const float*)mf_ptr(rs.xb[1]),
+                                       (float*)mf_ptr(rs.xb[0]), (const float*)mf_ptr(on_), c_.rms_norm_eps,
+                                       (const char*)mf_ptr(w_) + w_off_, dtype_, (int)c_.vocab_local(), c_.d_model,
+                                       (int)c_.vocab_offset(), rs.d_step, mf_ptr(rs.lmh_ws), rs.host_logits ? 1 : 0,
+                                       rs.comm, 2 * c_.n_layers - 1, rs.stream),
+                  "lm_head (all-reduce)");
+            return;
+        }
         check(mf_lm_head((float*)mf_ptr(rs.logits), (const float*)mf_ptr(rs.x), (const float*)mf_ptr(on_),
                          c_.rms_norm_eps, mf_ptr(w_), dtype_, (int)c_.vocab_size, c_.d_model, 0, rs.d_step,
                          mf_ptr(rs.lmh_ws), rs.stream),
@@ -270,6 +347,7 @@ private:
     const Qwen3Embed* embed_;
     int dtype_ = MF_BF16;
     mf_buf *on_ = nullptr, *w_ = nullptr;
+    size_t w_off_ = 0;  // byte offset of this rank's first row in w_ (tied head)
     size_t head_bytes_ = 0, norm_bytes_ = 0;
 };
 
@@ -336,10 +414,21 @@ int next_frame_base() {
 }
 }  // namespace
 
-Qwen3Model::Qwen3Model(const std::string& path, const RunParams& rp, int rank)
+Qwen3Model::Qwen3Model(const std::string& path, const RunParams& rp, int rank, int tp_rank, int tp_size)
     : path_(path), rp_(rp), rank_(rank), frame_base_(next_frame_base()) {
     if (file_.open(path) != 0) throw std::runtime_error("failed to load model file " + path + ": " + file_.error());
     cfg_ = Config::from_gguf(file_, rp);
+    if (tp_size < 1 || tp_size > MF_TP_MAX || tp_rank < 0 || tp_rank >= tp_size)
+        throw std::invalid_argument("tp_rank/tp_size out of range");
+    if (tp_size > 1) {
+        if (cfg_.n_kv_heads % tp_size != 0)
+            throw std::invalid_argument("n_kv_heads is not divisible by the tensor-parallel size");
+        if (cfg_.n_experts > 0) throw std::invalid_argument("tensor parallelism covers dense FFN models");
+        if (cfg_.d_ff % tp_size != 0) throw std::invalid_argument("d_ff is not divisible by the tensor-parallel size");
+        if (2 * cfg_.n_layers > 255) throw std::invalid_argument("tensor parallelism supports up to 127 layers");
+    }
+    cfg_.tp_rank = tp_rank;
+    cfg_.tp_size = tp_size;
     reset_sampler();
     build_layers();
 }
@@ -349,6 +438,7 @@ Qwen3Model::~Qwen3Model() {
         mf_sync(rank_);
         mf_drop_frames(rank_, frame_base_, frame_base_ + kFrameKinds - 1);
     }
+    if (rs_.comm) mf_comm_destroy(rs_.comm);
     layers_.clear();
     for (mf_buf* b : state_bufs_) mf_release(b);
     if (rs_.h_logits) mf_host_free(rs_.h_logits);
@@ -398,15 +488,20 @@ void Qwen3Model::alloc_state() {
     };
     const size_t S = c.user_max_seq_len;
     const int k = std::max(c.n_active_experts, 1);
+    const int Hl = c.heads_local(), Hkvl = c.kv_heads_local();
     rs.x = alloc((size_t)c.d_model * 4, "x");
-    rs.qkv = alloc((size_t)(c.n_heads + 2 * c.n_kv_heads) * c.d_head * 4, "qkv");
-    rs.att = alloc((size_t)c.n_heads * c.d_head * 4, "att_out");
-    rs.h = alloc((size_t)c.d_ff * k * 4, "hidden");
+    if (c.tp_size > 1) {
+        rs.xb[0] = rs.x;
+        rs.xb[1] = alloc((size_t)c.d_model * 4, "x (all-reduce ping-pong)");
+    }
+    rs.qkv = alloc((size_t)(Hl + 2 * Hkvl) * c.d_head * 4, "qkv");
+    rs.att = alloc((size_t)Hl * c.d_head * 4, "att_out");
+    rs.h = alloc((size_t)(c.n_experts > 0 ? c.d_ff : c.ff_local()) * k * 4, "hidden");
     rs.logits = alloc(c.vocab_size * 4, "logits");
     rs.scores = alloc((size_t)std::max(c.n_experts, 1) * 4, "moe_scores");
     rs.expert_ids = alloc((size_t)c.n_layers * k * 4, "active_experts");
     rs.expert_w = alloc((size_t)c.n_layers * k * 4, "active_experts_weights");
-    rs.kv_layer_floats = (size_t)c.n_kv_heads * S * c.d_head;
+    rs.kv_layer_floats = (size_t)Hkvl * S * c.d_head;
     rs.k_cache = alloc(rs.kv_layer_floats * c.n_layers * 4, "k_cache");
     rs.v_cache = alloc(rs.kv_layer_floats * c.n_layers * 4, "v_cache");
     {
@@ -415,14 +510,35 @@ void Qwen3Model::alloc_state() {
         rs.rope = alloc(tab.size() * 4, "rope table");
         check(mf_write(rs.rope, 0, tab.data(), tab.size() * 4), "upload rope table");
     }
-    rs.attn_split = mf_attn_default_split(c.n_kv_heads, (int)S);
-    rs.attn_ws = alloc(mf_attn_workspace_bytes(c.n_heads, c.n_kv_heads, c.d_head, rs.attn_split), "attn workspace");
+    rs.attn_split = mf_attn_default_split(Hkvl, (int)S);
+    rs.attn_ws = alloc(mf_attn_workspace_bytes(Hl, Hkvl, c.d_head, rs.attn_split), "attn workspace");
     rs.lmh_ws = alloc(mf_lm_head_workspace_bytes(), "lm_head workspace");
     check(mf_step_state(rank_, &rs.h_step, &rs.d_step), "step state");
     void* hl = nullptr;
     check(mf_host_alloc(c.vocab_size * 4, &hl), "pinned logits");
     rs.h_logits = (float*)hl;
-    rs.kv_bytes_per_pos = 2ull * c.n_layers * c.n_kv_heads * c.d_head * sizeof(float);
+    rs.kv_bytes_per_pos = 2ull * c.n_layers * Hkvl * c.d_head * sizeof(float);
+    if (c.tp_size > 1)
+        check(mf_comm_create(rank_, c.tp_rank, c.tp_size, (c.d_model + 3) / 4 * 4, (int)c.vocab_size, &rs.comm),
+              "tensor-parallel exchange");
+}
+
+void Qwen3Model::comm_handle(void* out, size_t n) const {
+    if (!rs_.comm) throw std::runtime_error("no tensor-parallel exchange (tp_size 1, or set_device(CUDA) first)");
+    check(mf_comm_handle(rs_.comm, out, n), "exchange handle");
+}
+
+void Qwen3Model::comm_connect(const void* handles, size_t n) {
+    if (!rs_.comm) throw std::runtime_error("no tensor-parallel exchange (tp_size 1, or set_device(CUDA) first)");
+    check(mf_comm_connect(rs_.comm, handles, n), "exchange connect");
+}
+
+int Qwen3Model::comm_status(int* status) {
+    if (!rs_.comm) {
+        *status = 0;
+        return MF_OK;
+    }
+    return mf_comm_status(rs_.comm, status, 1);
 }
 
 size_t Qwen3Model::read_bytes(bool with_logits) const {
@@ -439,9 +555,15 @@ void Qwen3Model::issue_frame(bool readback) {
     // the step record (greedy id) comes back with every host-driven frame;
     // logits when asked
     if (readback) check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, 16, rs_.stream), "step readback");
-    if (rs_.compute_logits && rs_.host_logits)
-        check(mf_copy_to_host_async(rs_.h_logits, mf_ptr(rs_.logits), cfg_.vocab_size * 4, rs_.stream),
-              "logits readback");
+    if (rs_.compute_logits && rs_.host_logits) {
+        const void* src = mf_ptr(rs_.logits);
+        if (rs_.comm) {
+            float* g = nullptr;
+            check(mf_comm_gather_ptr(rs_.comm, &g), "gather buffer");
+            src = g;  // all ranks' rows, complete when the lm_head kernel ends
+        }
+        check(mf_copy_to_host_async(rs_.h_logits, src, cfg_.vocab_size * 4, rs_.stream), "logits readback");
+    }
 }
 
 void Qwen3Model::forward(uint32_t token, int pos, bool compute_logits, bool host_logits) {
@@ -455,6 +577,7 @@ void Qwen3Model::forward(uint32_t token, int pos, bool compute_logits, bool host
     rs_.h_step[0] = (int32_t)token;
     rs_.h_step[1] = pos;
     rs_.h_step[3] = 0;
+    rs_.h_step[MF_STEP_FRAME] += 1;  // every frame gets a new sequence number
     const int frame = frame_base_ + (compute_logits ? (host_logits ? 2 : 0) : 1);
     const int rc = mf_begin_frame(rank_, frame);
     if (rc < 0) check(rc, "begin_frame");
@@ -545,6 +668,7 @@ uint32_t Qwen3Model::decode_chained(uint32_t token, int start_pos, int n) {
     rs_.h_step[0] = (int32_t)token;
     rs_.h_step[1] = start_pos;
     rs_.h_step[3] = 1;
+    rs_.h_step[MF_STEP_FRAME] += 1;  // later frames advance it on the device
     for (int i = 0; i < n; ++i) {
         // frame kind 3 uploads the host record once; kind 4 continues from the
         // record the previous frame's lm_head advanced on the device
@@ -561,7 +685,8 @@ uint32_t Qwen3Model::decode_chained(uint32_t token, int start_pos, int n) {
         }
         check(mf_end_frame_async(rank_), "end_frame");
     }
-    check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, 16, rs_.stream), "step readback");
+    // the whole record: the frame number continues from the device's
+    check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, MF_STEP_RECORD_BYTES, rs_.stream), "step readback");
     check(mf_sync(rank_), "sync");
     const uint32_t last = (uint32_t)rs_.h_step[2];
     rs_.h_step[3] = 0;
@@ -578,6 +703,7 @@ int Qwen3Model::read_experts(int layer, int* ids, float* w) const {
 
 int Qwen3Model::read_kv(int layer, float* k, float* v, int n_pos) const {
     // returns rows [0, n_pos) in the reference's [pos][kv_head][d_head] order
+    // (this rank's KV heads under tensor parallelism)
     if (layer < 0 || layer >= cfg_.n_layers || n_pos < 0 || (size_t)n_pos > cfg_.user_max_seq_len) return MF_E_INVALID;
     const size_t D = cfg_.d_head, S = cfg_.user_max_seq_len;
     std::vector<float> tmp(rs_.kv_layer_floats);
@@ -588,8 +714,8 @@ int Qwen3Model::read_kv(int layer, float* k, float* v, int n_pos) const {
                          tmp.size() * 4);
         if (rc) return rc;
         for (int p = 0; p < n_pos; ++p)
-            for (int hh = 0; hh < cfg_.n_kv_heads; ++hh)
-                std::memcpy(dst + ((size_t)p * cfg_.n_kv_heads + hh) * D, tmp.data() + ((size_t)hh * S + p) * D,
+            for (int hh = 0; hh < cfg_.kv_heads_local(); ++hh)
+                std::memcpy(dst + ((size_t)p * cfg_.kv_heads_local() + hh) * D, tmp.data() + ((size_t)hh * S + p) * D,
                             D * 4);
     }
     return MF_OK;

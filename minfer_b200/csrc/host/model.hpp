@@ -5,6 +5,7 @@
 // BaseModel::forward becomes one frame (a captured CUDA graph per frame kind).
 #pragma once
 
+#include <algorithm>
 #include <cstddef>
 #include <cstdint>
 #include <functional>
@@ -47,6 +48,17 @@ struct Config {
     DataType weight_dtype = DataType::INVALID;  // projection weights
     DataType head_dtype = DataType::INVALID;    // lm_head weight
     bool untied_head = false;
+    // tensor parallelism: this process holds rank tp_rank of tp_size
+    int tp_rank = 0, tp_size = 1;
+
+    int heads_local() const { return n_heads / tp_size; }
+    int kv_heads_local() const { return n_kv_heads / tp_size; }
+    int ff_local() const { return d_ff / tp_size; }
+    // vocabulary rows [vocab_offset(), vocab_offset() + vocab_local()) of the lm_head
+    size_t vocab_local() const { return vocab_size / tp_size + ((size_t)tp_rank < vocab_size % tp_size ? 1 : 0); }
+    size_t vocab_offset() const {
+        return (size_t)tp_rank * (vocab_size / tp_size) + std::min<size_t>(tp_rank, vocab_size % tp_size);
+    }
 
     static Config from_gguf(const GGUFFile& f, const RunParams& rp);
 };
@@ -80,7 +92,11 @@ struct RunState {
     bool compute_logits = false;
     bool host_logits = false;
     size_t kv_bytes_per_pos = 0;
-    size_t kv_layer_floats = 0;  // n_kv_heads * max_seq * d_head
+    size_t kv_layer_floats = 0;  // this rank's n_kv_heads * max_seq * d_head
+    // tensor parallelism: exchange state and the two residual buffers the
+    // all-reduces alternate between (x aliases xb[0])
+    mf_comm* comm = nullptr;
+    mf_buf* xb[2] = {nullptr, nullptr};
 };
 
 class BaseLayer {
@@ -98,7 +114,7 @@ protected:
 
 class Qwen3Model {
 public:
-    Qwen3Model(const std::string& path, const RunParams& rp, int rank = 0);
+    Qwen3Model(const std::string& path, const RunParams& rp, int rank = 0, int tp_rank = 0, int tp_size = 1);
     ~Qwen3Model();
 
     void set_device(DeviceType d);  // CUDA: upload weights, allocate the run state
@@ -125,6 +141,12 @@ public:
     // of frame i-1 (chained step record), frames are queued back to back with
     // no host round trip. Returns the last greedy id; the caller times it.
     uint32_t decode_chained(uint32_t token, int start_pos, int n);
+
+    // Tensor parallelism: after set_device(CUDA), every rank exports its
+    // handle, and connects with all ranks' handles ordered by tp_rank.
+    void comm_handle(void* out, size_t n) const;
+    void comm_connect(const void* handles, size_t n);
+    int comm_status(int* status);
 
     // Test access
     int read_experts(int layer, int* ids, float* w) const;

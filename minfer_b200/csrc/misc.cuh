@@ -5,6 +5,7 @@
 
 #include <float.h>
 
+#include "comm.cuh"
 #include "mf_common.cuh"
 
 namespace mf {
@@ -15,8 +16,11 @@ struct StepState {
     int token;
     int pos;
     int next_token;  // greedy argmax of the last computed logits
-    int chain;       // non-zero: the lm_head advances the record (token = next_token, pos += 1)
+    int chain;       // non-zero: the lm_head advances the record (token = next_token, pos += 1, frame += 1)
+    int frame;       // frame sequence number (tags of the tensor-parallel exchange)
+    int pad[3];
 };
+static_assert(sizeof(StepState) == MF_STEP_RECORD_BYTES, "step record layout");
 
 // x = fp32(E[token]) (src/ops/kernels.cpp:153-187, src/base/types.cpp:14-38),
 // token read from the device step record.
@@ -255,6 +259,26 @@ __global__ void argmax_kernel(const float* logits, int n, int* out) {
         }
         *out = bi;
     }
+}
+
+// Stand-alone all-reduce of an n-float vector in one CTA: push `partial` as
+// tagged words into every rank's slot, then x_out = x_res + partial_0 +
+// partial_1 + ... (rank order) as the words arrive (bounded waits).
+__global__ void __launch_bounds__(1024) allreduce_kernel(const float* partial, const float* x_res, float* x_out, int n,
+                                                         const CommDev c, int seq, const StepState* st) {
+    const int tid = threadIdx.x;
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t tag = comm_tag(__ldcg(&st->frame), seq);
+    const int slot = seq & 1;
+    for (int i = tid; i < n; i += blockDim.x) {
+        const unsigned long long w = tagged(__ldcg(partial + i), tag);
+        for (int r = 0; r < c.tp_size; ++r) st_tagged(c.recv(r, slot, c.tp_rank) + i, w);
+    }
+    int* status = &c.local()->status;
+    const unsigned long long deadline = globaltimer_ns() + c.timeout_ns;
+    bool late = false;
+    recv_sum(c, slot, tag, x_res, tid, blockDim.x, n, deadline, &late, status, [&](int i, float v) { x_out[i] = v; });
 }
 
 }  // namespace mf

@@ -355,10 +355,18 @@ def write_qwen3_gguf(path: str | os.PathLike, cfg: Qwen3Shape, chunk_elems: int 
 
 
 def ensure_gguf(path: str | os.PathLike, cfg: Qwen3Shape) -> str:
-    """Write the file unless one with the expected size is already there."""
+    """Write the file unless it is already there. The file appears atomically
+    (written under a temporary name, then renamed), so processes that race to
+    create it never read a partial file."""
     path = os.fspath(path)
     if not os.path.exists(path):
-        write_qwen3_gguf(path, cfg)
+        tmp = f"{path}.tmp{os.getpid()}"
+        try:
+            write_qwen3_gguf(tmp, cfg)
+            os.replace(tmp, path)
+        finally:
+            if os.path.exists(tmp):
+                os.remove(tmp)
     return path
 
 

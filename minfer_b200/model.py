@@ -11,8 +11,8 @@ import dataclasses
 
 import numpy as np
 
-from ._lib import (MF_GEN_MARGINS, MF_GEN_STOP_AT_EOS, check, cuda_lib, host_lib, mf_gen_stats, mf_model_info,
-                   mf_run_params)
+from ._lib import (MF_COMM_HANDLE_BYTES, MF_GEN_MARGINS, MF_GEN_STOP_AT_EOS, check, cuda_lib, host_lib,
+                   mf_gen_stats, mf_model_info, mf_run_params)
 
 
 @dataclasses.dataclass
@@ -60,14 +60,20 @@ def init(n_ranks: int = 1, devices: list[int] | None = None) -> None:
 
 
 class Qwen3Model:
-    def __init__(self, model_file: str, run_params: RunParams, rank: int = 0, device: int | None = None):
+    """`tp_rank`/`tp_size` > 1 loads this process's tensor-parallel shard
+    (dense models); after `set_device("cuda")` connect the ranks with
+    `minfer_b200.tp.connect` (or comm_handle / comm_connect directly)."""
+
+    def __init__(self, model_file: str, run_params: RunParams, rank: int = 0, device: int | None = None,
+                 tp_rank: int = 0, tp_size: int = 1):
         if not _initialised:
             init(1, [device if device is not None else 0])
         self._lib = host_lib()
         self._h = C.c_void_p()
         self.run_params = run_params
         self._rp = run_params.to_c()
-        check(self._lib.mf_model_load(str(model_file).encode(), C.byref(self._rp), rank, C.byref(self._h)))
+        check(self._lib.mf_model_load_tp(str(model_file).encode(), C.byref(self._rp), rank, tp_rank, tp_size,
+                                         C.byref(self._h)))
         self.device = "cpu"
         self._refresh_info()
 
@@ -95,6 +101,24 @@ class Qwen3Model:
             self.close()
         except Exception:
             pass
+
+    # -- tensor parallelism
+    def comm_handle(self) -> bytes:
+        buf = (C.c_char * MF_COMM_HANDLE_BYTES)()
+        check(self._lib.mf_model_comm_handle(self._h, buf, MF_COMM_HANDLE_BYTES))
+        return bytes(buf)
+
+    def comm_connect(self, handles: list[bytes]) -> None:
+        blob = b"".join(handles)
+        if len(handles) != self.info.tp_size or len(blob) != len(handles) * MF_COMM_HANDLE_BYTES:
+            raise ValueError("need one handle of MF_COMM_HANDLE_BYTES per tensor-parallel rank")
+        buf = C.create_string_buffer(blob, len(blob))
+        check(self._lib.mf_model_comm_connect(self._h, buf, len(blob)))
+
+    def comm_status(self) -> int:
+        v = C.c_int()
+        check(self._lib.mf_model_comm_status(self._h, C.byref(v)))
+        return v.value
 
     # -- BaseModel::forward
     def forward(self, token: int, pos: int, compute_logits: bool = True, host_logits: bool = True):
@@ -144,7 +168,7 @@ class Qwen3Model:
         return ids, w
 
     def kv(self, layer: int, n_pos: int):
-        n = n_pos * self.info.n_kv_heads * self.info.d_head
+        n = n_pos * (self.info.n_kv_heads // self.info.tp_size) * self.info.d_head
         k = np.zeros(n, dtype=np.float32)
         v = np.zeros(n, dtype=np.float32)
         check(self._lib.mf_model_kv(self._h, layer, k.ctypes.data, v.ctypes.data, n_pos))

@@ -17,6 +17,8 @@ TINY = {
     "tiny-f16": Qwen3Shape(2, 256, 4, 2, 128, 512, 1024, "f16", True, seed=103),
     "tiny-gqa8": Qwen3Shape(2, 256, 16, 2, 128, 384, 1024, "bf16", False, seed=104),
     "tiny-moe": Qwen3Shape(2, 256, 4, 2, 128, 128, 1024, "bf16", False, 16, 4, seed=105),
+    # 8 KV heads: tensor-parallel splits up to 8 ranks
+    "tiny-tp8": Qwen3Shape(2, 512, 16, 8, 128, 1024, 2048, "bf16", False, seed=106),
 }
 
 

@@ -252,7 +252,7 @@ def test_lm_head_argmax(ops, orc, gpu):
     w[40001] = w[17]
     logits = torch.zeros(V, device=gpu)
     ws = torch.zeros(ops.lm_head_workspace_bytes() // 4 + 1, dtype=torch.int32, device=gpu)
-    st = torch.zeros(4, dtype=torch.int32, device=gpu)
+    st = torch.zeros(8, dtype=torch.int32, device=gpu)
     wt = T(w.ravel().view(np.int16), gpu)
     for rep in range(3):  # the workspace counter must come back to zero each call
         ops.lm_head(logits, T(x, gpu), T(nw, gpu), 1e-6, wt, V, d, step_state=st, workspace=ws, dtype="bf16")
@@ -306,7 +306,7 @@ def test_attn_decode(ops, orc, gpu, H, Hkv, pos, split):
     vc = T(np.ascontiguousarray(vc_hist.transpose(1, 0, 2)), gpu)
     n_split = ops.attn_default_split(Hkv, S) if split == "default" else split
     ws = torch.zeros(ops.attn_workspace_bytes(H, Hkv, D, n_split) // 4 + 1, dtype=torch.int32, device=gpu)
-    st = torch.tensor([0, pos, 0, 0], dtype=torch.int32, device=gpu)
+    st = torch.tensor([0, pos, 0, 0, 0, 0, 0, 0], dtype=torch.int32, device=gpu)
     out = torch.zeros(H * D, device=gpu)
     for rep in range(2):
         ops.attn_decode(T(qkv, gpu), T(qn, gpu), T(kn, gpu), 1e-6, rope.to(gpu), kc, vc, S, st, out, H, Hkv, D,
@@ -335,7 +335,7 @@ def test_attn_decode_position_out_of_range(ops, gpu):
     n_split = ops.attn_default_split(Hkv, S)
     ws = torch.zeros(ops.attn_workspace_bytes(H, Hkv, D, n_split) // 4 + 1, dtype=torch.int32, device=gpu)
     for pos in (S, S + 1000, -1):
-        st = torch.tensor([0, pos, 0, 0], dtype=torch.int32, device=gpu)
+        st = torch.tensor([0, pos, 0, 0, 0, 0, 0, 0], dtype=torch.int32, device=gpu)
         out = torch.full((H * D,), 7.0, device=gpu)
         ops.attn_decode(qkv, nw, nw, 1e-6, rope, kc, vc, S, st, out, H, Hkv, D, n_split, ws)
         torch.cuda.synchronize()
@@ -397,7 +397,7 @@ def test_embed(ops, orc, gpu):
         out = torch.zeros(d, device=gpu)
         ops.embed(out, T(w.view(np.int16) if dt else w, gpu), 123, d, dtype=DT_NAME[dt])
         np.testing.assert_array_equal(out.cpu().numpy(), orc.embed(w, dt, 123, d))
-        st = torch.tensor([77, 0, 0, 0], dtype=torch.int32, device=gpu)
+        st = torch.tensor([77, 0, 0, 0, 0, 0, 0, 0], dtype=torch.int32, device=gpu)
         ops.embed_step(out, T(w.view(np.int16) if dt else w, gpu), V, d, st, dtype=DT_NAME[dt])
         np.testing.assert_array_equal(out.cpu().numpy(), orc.embed(w, dt, 77, d))
 

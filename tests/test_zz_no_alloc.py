@@ -40,7 +40,7 @@ def test_noalloc_matches_workspace_variant(gpu, H, Hkv, pos):
     kc0 = torch.randn(Hkv * S * D, generator=g, device=gpu)
     vc0 = torch.randn(Hkv * S * D, generator=g, device=gpu)
     rope = ops.rope_table(S, D, 1e6).to(gpu)
-    st = torch.tensor([0, pos, 0, 0], dtype=torch.int32, device=gpu)
+    st = torch.tensor([0, pos, 0, 0, 0, 0, 0, 0], dtype=torch.int32, device=gpu)
     n_split = ops.attn_default_split(Hkv, S)
     stream = ops._stream()
 
@@ -72,7 +72,7 @@ def test_noalloc_rejects_oversized_request(gpu):
     lib = cuda_lib()
     H, Hkv, D, S = 64, 8, 128, 64
     t = torch.zeros(1 << 20, device=gpu)
-    st = torch.tensor([0, 3, 0, 0], dtype=torch.int32, device=gpu)
+    st = torch.tensor([0, 3, 0, 0, 0, 0, 0, 0], dtype=torch.int32, device=gpu)
     # 8 KV heads x 148 slices x 8 heads x 130 floats needs ~4.9 MB of scratch
     d = _desc(ops, (t, t, t, t, t, t, st, t), S, H, Hkv, D, 148, None)
     rc = lib.mf_attn_decode_noalloc(C.byref(d), ops._stream())
