@@ -301,6 +301,44 @@ int mf_allreduce(float* x_out, const float* x_res, const float* partial, int n, 
                  const void* step_state, void* stream);
 
 /* ===================================================================== */
+/* Batched prefill (tcgen05 tensor cores)                                */
+/* ===================================================================== */
+/* No reference counterpart: the reference prefills token by token
+ * (src/base/model.cpp:120-129). These calls process all n_tokens prompt
+ * tokens of a layer at once. Activations stay fp32 between calls; a GEMM
+ * operand is the fp32 activation split into two bf16 matrices hi + lo
+ * (hi = bf16(a), lo = bf16(a - hi)), so bf16 tensor cores reproduce the
+ * fp32-activation GEMV to ~1e-5 relative. bf16 matrices are row-major,
+ * 16-byte aligned, row length a multiple of 8. */
+#define MF_PREFILL_STORE 0  /* y[m*ldy + n] = C */
+#define MF_PREFILL_RESID 1  /* y[m*ldy + n] += C */
+#define MF_PREFILL_SWIGLU 2 /* C's columns 2i/2i+1 are gate_i/up_i: h = silu(g)*u as hi/lo [M][N/2] */
+/* C[M, N] = (a_hi + a_lo)[M, K] · w[N, K]^T with w bf16. */
+int mf_prefill_gemm(float* y, int ldy, const void* a_hi, const void* a_lo, const void* w, int M, int N, int K,
+                    int mode, void* h_hi, void* h_lo, void* stream);
+/* Row-wise RMSNorm (src/ops/kernels.cpp:351-365) of x [n_rows][d] split into
+ * bf16 hi/lo; xn (optional) receives the fp32 normalised rows. */
+int mf_prefill_norm_split(void* hi, void* lo, float* xn, const float* x, const float* norm_w, float eps, int d,
+                          int n_rows, void* stream);
+/* fp32 -> bf16 hi/lo split of n elements. */
+int mf_prefill_split(void* hi, void* lo, const float* x, size_t n, void* stream);
+/* x[t] = embedding row tokens[t] (device ids) for t < n_tokens. */
+int mf_prefill_embed(float* x, const void* emb, int dtype, int vocab, int d_model, const uint32_t* tokens,
+                     int n_tokens, void* stream);
+/* Per token t (position pos0 + t) of qkv [n_tokens][(Hq + 2 Hkv) * d_head]:
+ * Q/K RMSNorm + NeoX RoPE (as mf_attn_decode), q -> q_out [n_tokens][Hq * d_head],
+ * k/v -> cache row pos0 + t (caches [n_kv_heads][max_seq][d_head], this layer). */
+int mf_prefill_qkv_post(float* q_out, float* k_cache, float* v_cache, const float* qkv, const float* q_norm_w,
+                        const float* k_norm_w, float eps, const void* rope_table, int max_seq, int n_heads,
+                        int n_kv_heads, int d_head, int n_tokens, int pos0, void* stream);
+/* Causal GQA attention of the prompt tokens (token t sees cache rows
+ * [0, pos0 + t]), written as bf16 hi/lo [n_tokens][Hq * d_head]. */
+int mf_prefill_attention(void* out_hi, void* out_lo, const float* q, const float* k_cache, const float* v_cache,
+                         int max_seq, int n_tokens, int pos0, int n_heads, int n_kv_heads, int d_head, void* stream);
+/* Status bits of the prefill GEMM's bounded waits since the last clear (synchronises the device). */
+int mf_prefill_status(int* status, int clear);
+
+/* ===================================================================== */
 /* Single ops with the reference's CPU signatures                        */
 /* (include/minfer/ops/kernels.hpp:13-32) on device buffers.              */
 /* ===================================================================== */

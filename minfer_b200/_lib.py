@@ -28,6 +28,7 @@ MF_TP_MAX = 8
 MF_COMM_HANDLE_BYTES = 64
 MF_STEP_RECORD_BYTES = 32
 MF_STEP_FRAME = 4
+MF_PREFILL_STORE, MF_PREFILL_RESID, MF_PREFILL_SWIGLU = 0, 1, 2
 MF_FRAME_RECORD, MF_FRAME_REPLAY = 0, 1
 MF_GEN_STOP_AT_EOS, MF_GEN_MARGINS = 1, 2
 
@@ -138,6 +139,13 @@ CUDA_API = {
     "mf_allreduce_swiglu_matmul": (I, [P, P, P, P, F, P, I, I, I, P, I, P, P]),
     "mf_allreduce_lm_head": (I, [P, P, P, P, F, P, I, I, I, I, P, P, I, P, I, P]),
     "mf_allreduce": (I, [P, P, P, I, P, I, P, P]),
+    "mf_prefill_gemm": (I, [P, I, P, P, P, I, I, I, I, P, P, P]),
+    "mf_prefill_norm_split": (I, [P, P, P, P, P, F, I, I, P]),
+    "mf_prefill_split": (I, [P, P, P, SZ, P]),
+    "mf_prefill_embed": (I, [P, P, I, I, I, P, I, P]),
+    "mf_prefill_qkv_post": (I, [P, P, P, P, P, P, F, P, I, I, I, I, I, I, P]),
+    "mf_prefill_attention": (I, [P, P, P, P, P, I, I, I, I, I, I, P]),
+    "mf_prefill_status": (I, [P, I]),
     "mf_matmul": (I, [P, P, P, I, SZ, I, I, P]),
     "mf_rmsnorm": (I, [P, P, P, I, F, I, P]),
     "mf_softmax": (I, [P, P, I, I, P]),

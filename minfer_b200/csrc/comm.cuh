@@ -94,12 +94,6 @@ MF_DEVICE unsigned long long ld_tagged(const unsigned long long* p) {
     return w;
 }
 
-MF_DEVICE unsigned long long globaltimer_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
 constexpr long long COMM_MAX_POLLS = 1ll << 26;  // backstop: the time limit ends a wait first
 
 // Reads the tagged word at p once its tag is `tag`. Polls until `deadline`

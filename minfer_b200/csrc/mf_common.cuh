@@ -61,6 +61,13 @@ MF_DEVICE void prefetch_l2(const void* p, uint32_t bytes) {
 MF_DEVICE float ld_cg(const float* p) { return __ldcg(p); }
 MF_DEVICE int ld_cg(const int* p) { return __ldcg(p); }
 
+// Wall clock (ns) for bounded waits.
+MF_DEVICE unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 // ---------------------------------------------------------------- PDL
 // Programmatic dependent launch: the next kernel in the stream may start its
 // weight prefetch while this one drains; `wait` blocks until every

@@ -1,0 +1,182 @@
+"""Batched prefill kernels on the GPU against fp64 references.
+
+* the tcgen05 GEMM (fp32 activation as bf16 hi + lo, bf16 weights) in its
+  three modes, including partial M/N tiles: relative error <= 2e-5 of the
+  output scale, i.e. fp32-GEMV accuracy, not bf16's;
+* the per-token Q/K RMSNorm + RoPE + KV-cache write against the decode
+  kernel's norm/rope (bit-identical routine) via the oracle;
+* causal attention (fresh prompt and prompt after cache history) against a
+  float64 softmax-attention reference: max-abs <= 2e-5.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def P(t):
+    return C.c_void_p(t.data_ptr())
+
+
+def split(a: torch.Tensor):
+    hi = a.to(torch.bfloat16)
+    lo = (a - hi.float()).to(torch.bfloat16)
+    return hi.contiguous(), lo.contiguous()
+
+
+@pytest.fixture(scope="module")
+def lib(gpu):
+    from minfer_b200._lib import cuda_lib
+
+    return cuda_lib()
+
+
+def stream():
+    from minfer_b200 import ops
+
+    return C.c_void_p(ops._stream())
+
+
+def status_ok(lib):
+    from minfer_b200._lib import check
+
+    st = C.c_int()
+    check(lib.mf_prefill_status(C.byref(st), 1))
+    return st.value == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (200, 768, 256), (512, 1040, 1024), (37, 512, 4096)])
+def test_prefill_gemm_store_and_resid(lib, gpu, M, N, K):
+    from minfer_b200._lib import MF_PREFILL_RESID, MF_PREFILL_STORE, check
+
+    g = torch.Generator(device=gpu).manual_seed(M * 7 + N)
+    a = torch.randn(M, K, generator=g, device=gpu)
+    w = (torch.randn(N, K, generator=g, device=gpu) * 0.02).to(torch.bfloat16)
+    hi, lo = split(a)
+    ref = (hi.double() + lo.double()) @ w.double().t()
+    y = torch.full((M, N), 7.0, device=gpu)
+    check(lib.mf_prefill_gemm(P(y), N, P(hi), P(lo), P(w), M, N, K, MF_PREFILL_STORE, None, None, stream()))
+    torch.cuda.synchronize()
+    scale = ref.abs().max().item()
+    assert (y.double() - ref).abs().max().item() <= 2e-5 * scale
+    # the split keeps fp32-GEMV accuracy against the unsplit fp32 activation too
+    ref32 = a.double() @ w.double().t()
+    assert (y.double() - ref32).abs().max().item() <= 5e-5 * scale
+    base = torch.randn(M, N, generator=g, device=gpu)
+    y2 = base.clone()
+    check(lib.mf_prefill_gemm(P(y2), N, P(hi), P(lo), P(w), M, N, K, MF_PREFILL_RESID, None, None, stream()))
+    torch.cuda.synchronize()
+    assert (y2.double() - (base.double() + ref)).abs().max().item() <= 2e-5 * scale + 1e-6
+    assert status_ok(lib)
+
+
+@pytest.mark.parametrize("M,F,K", [(128, 128, 256), (300, 384, 512)])
+def test_prefill_gemm_swiglu(lib, gpu, M, F, K):
+    from minfer_b200._lib import MF_PREFILL_SWIGLU, check
+
+    g = torch.Generator(device=gpu).manual_seed(F + K)
+    a = torch.randn(M, K, generator=g, device=gpu)
+    w = (torch.randn(2 * F, K, generator=g, device=gpu) * 0.05).to(torch.bfloat16)  # rows 2i gate, 2i+1 up
+    hi, lo = split(a)
+    c = (hi.double() + lo.double()) @ w.double().t()
+    gate, up = c[:, 0::2], c[:, 1::2]
+    ref = gate / (1 + torch.exp(-gate)) * up
+    h_hi = torch.zeros(M, F, dtype=torch.bfloat16, device=gpu)
+    h_lo = torch.zeros(M, F, dtype=torch.bfloat16, device=gpu)
+    check(lib.mf_prefill_gemm(None, 0, P(hi), P(lo), P(w), M, 2 * F, K, MF_PREFILL_SWIGLU, P(h_hi), P(h_lo), stream()))
+    torch.cuda.synchronize()
+    got = h_hi.double() + h_lo.double()
+    assert (got - ref).abs().max().item() <= 3e-5 * ref.abs().max().item()
+    assert status_ok(lib)
+
+
+def test_prefill_norm_split(lib, gpu):
+    from minfer_b200._lib import check
+
+    M, d = 70, 1024
+    g = torch.Generator(device=gpu).manual_seed(3)
+    x = torch.randn(M, d, generator=g, device=gpu)
+    w = 1 + 0.1 * torch.randn(d, generator=g, device=gpu)
+    hi = torch.empty(M, d, dtype=torch.bfloat16, device=gpu)
+    lo = torch.empty_like(hi)
+    xn = torch.empty(M, d, device=gpu)
+    check(lib.mf_prefill_norm_split(P(hi), P(lo), P(xn), P(x), P(w), C.c_float(1e-6), d, M, stream()))
+    torch.cuda.synchronize()
+    ref = x.double() / torch.sqrt((x.double() ** 2).mean(1, keepdim=True) + 1e-6) * w.double()
+    assert (xn.double() - ref).abs().max().item() < 1e-5
+    h2, l2 = split(xn)
+    assert torch.equal(hi, h2) and torch.equal(lo, l2)
+
+
+def _attn_ref(q, kc, vc, pos0, Hq, Hkv):
+    """float64 causal attention: token t (position pos0 + t) over cache rows [0, pos0 + t]."""
+    T = q.shape[0]
+    G = Hq // Hkv
+    D = 128
+    out = torch.zeros(T, Hq * D, dtype=torch.float64)
+    q = q.double().cpu().view(T, Hq, D)
+    kc, vc = kc.double().cpu(), vc.double().cpu()
+    for h in range(Hq):
+        kvh = h // G
+        s = q[:, h, :] @ kc[kvh, : pos0 + T].t() / np.sqrt(D)
+        mask = torch.arange(pos0 + T)[None, :] > (pos0 + torch.arange(T))[:, None]
+        s[mask] = -np.inf
+        p = torch.softmax(s, dim=1)
+        out[:, h * D:(h + 1) * D] = p @ vc[kvh, : pos0 + T]
+    return out
+
+
+@pytest.mark.parametrize("Hq,Hkv,T,pos0", [(32, 8, 100, 0), (16, 2, 67, 0), (8, 8, 33, 40), (16, 1, 20, 5),
+                                           (64, 8, 130, 0)])
+def test_prefill_attention(lib, gpu, Hq, Hkv, T, pos0):
+    from minfer_b200._lib import check
+
+    S, D = 256, 128
+    g = torch.Generator(device=gpu).manual_seed(Hq + T)
+    q = torch.randn(T, Hq * D, generator=g, device=gpu)
+    kc = torch.randn(Hkv, S, D, generator=g, device=gpu)
+    vc = torch.randn(Hkv, S, D, generator=g, device=gpu)
+    hi = torch.empty(T, Hq * D, dtype=torch.bfloat16, device=gpu)
+    lo = torch.empty_like(hi)
+    check(lib.mf_prefill_attention(P(hi), P(lo), P(q), P(kc), P(vc), S, T, pos0, Hq, Hkv, D, stream()))
+    torch.cuda.synchronize()
+    ref = _attn_ref(q, kc, vc, pos0, Hq, Hkv)
+    got = (hi.double() + lo.double()).cpu()
+    assert (got - ref).abs().max().item() <= 2e-5
+
+
+def test_prefill_qkv_post_matches_decode_rotation(lib, gpu):
+    """Same per-head norm + RoPE as the decode kernel: compare with the oracle's restatement."""
+    from conftest import TINY  # noqa: F401
+    from minfer_b200 import ops
+    from minfer_b200._lib import check
+    from oracle.oracle_py import PortOps
+
+    Hq, Hkv, D, T, S, pos0 = 4, 2, 128, 9, 32, 3
+    rng = np.random.default_rng(5)
+    qkv = rng.standard_normal((T, (Hq + 2 * Hkv) * D)).astype(np.float32)
+    qn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    rope = ops.rope_table(S, D, 1e6).to(gpu)
+    qo = torch.zeros(T, Hq * D, device=gpu)
+    kc = torch.zeros(Hkv, S, D, device=gpu)
+    vc = torch.zeros(Hkv, S, D, device=gpu)
+    qkv_t, qn_t, kn_t = (torch.from_numpy(a).to(gpu) for a in (qkv, qn, kn))  # alive until the kernel ran
+    check(lib.mf_prefill_qkv_post(P(qo), P(kc), P(vc), P(qkv_t), P(qn_t), P(kn_t), C.c_float(1e-6), P(rope),
+                                  S, Hq, Hkv, D, T, pos0, stream()))
+    torch.cuda.synchronize()
+    po = PortOps()
+    for t in range(T):
+        for h in range(Hq):
+            x = po.rmsnorm(qkv[t, h * D:(h + 1) * D], qn, 1e-6)
+            exp = po.rope(x, 0, D, D, 1e6, pos0 + t)
+            np.testing.assert_allclose(qo[t, h * D:(h + 1) * D].cpu().numpy(), exp, rtol=2e-6, atol=2e-6)
+        for h in range(Hkv):
+            x = po.rmsnorm(qkv[t, (Hq + h) * D:(Hq + h + 1) * D], kn, 1e-6)
+            exp = po.rope(x, 0, D, D, 1e6, pos0 + t)
+            np.testing.assert_allclose(kc[h, pos0 + t].cpu().numpy(), exp, rtol=2e-6, atol=2e-6)
+            np.testing.assert_array_equal(vc[h, pos0 + t].cpu().numpy(), qkv[t, (Hq + Hkv + h) * D:(Hq + Hkv + h + 1) * D])
+    assert kc[:, :pos0].abs().sum().item() == 0 and kc[:, pos0 + T:].abs().sum().item() == 0
