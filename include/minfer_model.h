@@ -107,6 +107,15 @@ int mf_model_generate(mf_model* m, const uint32_t* prompt, size_t n_prompt, size
                       mf_gen_stats* stats);
 #define MF_GEN_STOP_AT_EOS 1
 #define MF_GEN_MARGINS 2
+#define MF_GEN_TOKEN_PREFILL 4 /* prefill token by token (the reference's loop) instead of batched */
+
+/* Batched prefill (no reference counterpart; the reference prefills token by
+ * token, src/base/model.cpp:120-129): tokens at positions [pos0, pos0 + n)
+ * go through every layer as tcgen05 GEMMs, filling the KV cache; with
+ * compute_logits the last token's logits / greedy id are then available as
+ * after mf_model_forward. bf16 dense models on one GPU; others return
+ * MF_E_UNSUPPORTED (use mf_model_forward per token). */
+int mf_model_prefill(mf_model* m, const uint32_t* tokens, size_t n, int pos0, int compute_logits, int host_logits);
 
 /* Greedy decode of n tokens with the device feeding itself (no host round
  * trip between tokens), starting with `token` at `start_pos`. Blocks until

@@ -30,7 +30,7 @@ MF_STEP_RECORD_BYTES = 32
 MF_STEP_FRAME = 4
 MF_PREFILL_STORE, MF_PREFILL_RESID, MF_PREFILL_SWIGLU = 0, 1, 2
 MF_FRAME_RECORD, MF_FRAME_REPLAY = 0, 1
-MF_GEN_STOP_AT_EOS, MF_GEN_MARGINS = 1, 2
+MF_GEN_STOP_AT_EOS, MF_GEN_MARGINS, MF_GEN_TOKEN_PREFILL = 1, 2, 4
 
 _STATUS = {
     MF_E_INVALID: "invalid argument",
@@ -163,6 +163,7 @@ HOST_API = {
     "mf_model_load": (I, [C.c_char_p, P, I, P]),
     "mf_model_to_cuda": (I, [P]),
     "mf_model_load_tp": (I, [C.c_char_p, P, I, I, I, P]),
+    "mf_model_prefill": (I, [P, P, SZ, I, I, I]),
     "mf_model_comm_handle": (I, [P, P, SZ]),
     "mf_model_comm_connect": (I, [P, P, SZ]),
     "mf_model_comm_status": (I, [P, P]),

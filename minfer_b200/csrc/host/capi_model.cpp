@@ -162,6 +162,7 @@ int mf_model_generate(mf_model* m, const uint32_t* prompt, size_t n_prompt, size
     MF_TRY({
         minfer::Qwen3Model::GenOptions o;
         o.stop_at_eos = (flags & MF_GEN_STOP_AT_EOS) != 0;
+        o.batched_prefill = (flags & MF_GEN_TOKEN_PREFILL) == 0;
         o.trace = (flags & MF_GEN_MARGINS) != 0;
         o.forced = forced;
         std::vector<uint32_t> pr(prompt, prompt + n_prompt);
@@ -182,6 +183,14 @@ int mf_model_generate(mf_model* m, const uint32_t* prompt, size_t n_prompt, size
         }
     });
     return MF_OK;
+}
+
+int mf_model_prefill(mf_model* m, const uint32_t* tokens, size_t n, int pos0, int compute_logits, int host_logits) {
+    if (!m || !tokens || n == 0) return herr(MF_E_INVALID, "bad arguments");
+    g_host_err[0] = 0;
+    bool ok = false;
+    MF_TRY(ok = m->m->prefill(tokens, (int)n, pos0, compute_logits != 0, host_logits != 0));
+    return ok ? MF_OK : herr(MF_E_UNSUPPORTED, "batched prefill needs a bf16 dense model on one GPU");
 }
 
 int mf_model_decode_chained(mf_model* m, uint32_t token, int start_pos, int n, uint32_t* last_id) {

@@ -3,6 +3,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 
@@ -92,6 +93,11 @@ public:
         check(mf_embed_step((float*)mf_ptr(rs.x), mf_ptr(w_), dtype_, (int)c_.vocab_size, c_.d_model, rs.d_step,
                             rs.stream),
               "embed");
+    }
+    void prefill_forward(RunState& rs, int n, int pos0) override {
+        check(mf_prefill_embed((float*)mf_ptr(rs.pf_x), mf_ptr(w_), dtype_, (int)c_.vocab_size, c_.d_model,
+                               (const uint32_t*)mf_ptr(rs.pf_tok), n, rs.stream),
+              "prefill embed");
     }
     mf_buf* weight() const { return w_; }
     int dtype() const { return dtype_; }
@@ -190,6 +196,30 @@ public:
         }
     }
 
+    // the same layer for n prompt tokens at once: pre-norm, QKV GEMM, Q/K norm
+    // + RoPE + KV write, causal attention, O GEMM + residual
+    void prefill_forward(RunState& rs, int n, int pos0) override {
+        const int d = c_.d_model, H = c_.n_heads, Hkv = c_.n_kv_heads, D = c_.d_head, Nqkv = (H + 2 * Hkv) * D;
+        const int S = (int)c_.user_max_seq_len;
+        float* X = (float*)mf_ptr(rs.pf_x);
+        void *hi = mf_ptr(rs.pf_hi), *lo = mf_ptr(rs.pf_lo);
+        float* kc = (float*)mf_ptr(rs.k_cache) + (size_t)layer_ * rs.kv_layer_floats;
+        float* vc = (float*)mf_ptr(rs.v_cache) + (size_t)layer_ * rs.kv_layer_floats;
+        check(mf_prefill_norm_split(hi, lo, nullptr, X, (const float*)mf_ptr(an_), c_.rms_norm_eps, d, n, rs.stream),
+              "prefill attn norm");
+        check(mf_prefill_gemm((float*)mf_ptr(rs.pf_qkv), Nqkv, hi, lo, mf_ptr(wqkv_), n, Nqkv, d, MF_PREFILL_STORE,
+                              nullptr, nullptr, rs.stream),
+              "prefill qkv projection");
+        check(mf_prefill_qkv_post((float*)mf_ptr(rs.pf_q), kc, vc, (const float*)mf_ptr(rs.pf_qkv),
+                                  (const float*)mf_ptr(qn_), (const float*)mf_ptr(kn_), c_.rms_norm_eps,
+                                  mf_ptr(rs.rope), S, H, Hkv, D, n, pos0, rs.stream),
+              "prefill q/k norm, rope, kv");
+        check(mf_prefill_attention(hi, lo, (const float*)mf_ptr(rs.pf_q), kc, vc, S, n, pos0, H, Hkv, D, rs.stream),
+              "prefill attention");
+        check(mf_prefill_gemm(X, d, hi, lo, mf_ptr(wo_), n, d, H * D, MF_PREFILL_RESID, nullptr, nullptr, rs.stream),
+              "prefill output projection");
+    }
+
 private:
     const Config& c_;
     int layer_;
@@ -284,6 +314,21 @@ public:
         check(mf_moe_down_residual(x, h, mf_ptr(wd_), dtype_, ids, w, k, d, F, rs.stream), "expert down");
     }
 
+    // dense FFN for n prompt tokens: pre-norm, gate/up GEMM with the SwiGLU
+    // epilogue, down GEMM + residual
+    void prefill_forward(RunState& rs, int n, int pos0) override {
+        if (c_.n_experts > 0) throw std::runtime_error("batched prefill covers dense FFN layers");
+        const int d = c_.d_model, F = c_.d_ff;
+        float* X = (float*)mf_ptr(rs.pf_x);
+        void *hi = mf_ptr(rs.pf_hi), *lo = mf_ptr(rs.pf_lo), *hhi = mf_ptr(rs.pf_hhi), *hlo = mf_ptr(rs.pf_hlo);
+        check(mf_prefill_norm_split(hi, lo, nullptr, X, (const float*)mf_ptr(fn_), c_.rms_norm_eps, d, n, rs.stream),
+              "prefill ffn norm");
+        check(mf_prefill_gemm(nullptr, 0, hi, lo, mf_ptr(wgu_), n, 2 * F, d, MF_PREFILL_SWIGLU, hhi, hlo, rs.stream),
+              "prefill gate/up projection");
+        check(mf_prefill_gemm(X, d, hhi, hlo, mf_ptr(wd_), n, d, F, MF_PREFILL_RESID, nullptr, nullptr, rs.stream),
+              "prefill down projection");
+    }
+
 private:
     const Config& c_;
     int layer_;
@@ -357,6 +402,8 @@ BaseLayer::~BaseLayer() {
     for (mf_buf* b : bufs_) mf_release(b);
 }
 
+void BaseLayer::prefill_forward(RunState&, int, int) {}  // layers without prefill work (the lm_head)
+
 Config Config::from_gguf(const GGUFFile& f, const RunParams& rp) {
     Config c;
     const std::string arch = f.get_string("general.architecture");
@@ -405,7 +452,7 @@ Config Config::from_gguf(const GGUFFile& f, const RunParams& rp) {
 namespace {
 // Frames are captured per manager rank; every model instance owns a disjoint
 // block of frame ids so two models on one device never replay each other's graphs.
-constexpr int kFrameKinds = 8;
+constexpr int kFrameKinds = 8;  // 0-2 forward, 3-4 chained decode, 5-6 logits after a batched prefill
 int next_frame_base() {
     static int next = 0;
     const int b = next;
@@ -541,6 +588,97 @@ int Qwen3Model::comm_status(int* status) {
     return mf_comm_status(rs_.comm, status, 1);
 }
 
+bool Qwen3Model::prefill_supported() const {
+    if (device_ != DeviceType::CUDA || cfg_.tp_size != 1 || cfg_.n_experts != 0) return false;
+    if (cfg_.weight_dtype != DataType::BF16 || cfg_.d_head != 128 || cfg_.d_model % 8 != 0 || cfg_.d_ff % 8 != 0)
+        return false;
+    const int G = cfg_.n_heads / cfg_.n_kv_heads;
+    return G == 1 || G == 2 || G == 4 || G == 8 || G == 16;
+}
+
+void Qwen3Model::alloc_prefill(int rows) {
+    if (rs_.pf_cap >= rows) return;
+    RunState& rs = rs_;
+    for (mf_buf** b : {&rs.pf_x, &rs.pf_hi, &rs.pf_lo, &rs.pf_hhi, &rs.pf_hlo, &rs.pf_qkv, &rs.pf_q, &rs.pf_tok}) {
+        if (*b) {
+            state_bufs_.erase(std::find(state_bufs_.begin(), state_bufs_.end(), *b));
+            mf_release(*b);
+            *b = nullptr;
+        }
+    }
+    const Config& c = cfg_;
+    auto alloc = [&](size_t bytes, const char* what) {
+        mf_buf* b = nullptr;
+        check(mf_alloc(bytes < 16 ? 16 : bytes, rank_, &b), what);
+        state_bufs_.push_back(b);
+        return b;
+    };
+    const size_t R = (size_t)rows, qd = (size_t)c.n_heads * c.d_head;
+    const size_t wide = std::max<size_t>({(size_t)c.d_model, qd});
+    rs.pf_x = alloc(R * c.d_model * 4, "prefill residual");
+    rs.pf_hi = alloc(R * wide * 2, "prefill operand hi");
+    rs.pf_lo = alloc(R * wide * 2, "prefill operand lo");
+    rs.pf_hhi = alloc(R * c.d_ff * 2, "prefill ffn hi");
+    rs.pf_hlo = alloc(R * c.d_ff * 2, "prefill ffn lo");
+    rs.pf_qkv = alloc(R * (qd + 2ull * c.n_kv_heads * c.d_head) * 4, "prefill qkv");
+    rs.pf_q = alloc(R * qd * 4, "prefill queries");
+    rs.pf_tok = alloc(R * 4, "prefill token ids");
+    rs.pf_cap = rows;
+}
+
+bool Qwen3Model::prefill(const uint32_t* tokens, int n, int pos0, bool compute_logits, bool host_logits) {
+    if (!prefill_supported()) return false;
+    if (n <= 0) throw std::invalid_argument("empty prompt");
+    if (pos0 < 0 || (size_t)pos0 + (size_t)n > cfg_.user_max_seq_len)
+        throw std::runtime_error("prompt runs past max_seq_len");
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] >= cfg_.vocab_size) throw std::runtime_error("token id outside the vocabulary");
+    // MF_PREFILL_CHUNK overrides the rows per pass (smaller chunks exercise the history path)
+    const char* ce = std::getenv("MF_PREFILL_CHUNK");
+    const size_t want = (ce && std::atoi(ce) > 0) ? (size_t)std::atoi(ce) : (size_t)kPrefillChunk;
+    const int chunk = (int)std::min<size_t>(cfg_.user_max_seq_len, want);
+    alloc_prefill(std::min(chunk, n));
+    int last_rows = 0;
+    for (int c0 = 0; c0 < n; c0 += rs_.pf_cap) {
+        const int nc = std::min(rs_.pf_cap, n - c0);
+        check(mf_write(rs_.pf_tok, 0, tokens + c0, (size_t)nc * 4), "prefill token ids");
+        for (size_t i = 0; i + 1 < layers_.size(); ++i) layers_[i]->prefill_forward(rs_, nc, pos0 + c0);
+        last_rows = nc;
+    }
+    int st = 0;
+    check(mf_prefill_status(&st, 1), "prefill status");
+    if (st) throw std::runtime_error("a prefill GEMM wait gave up (status " + std::to_string(st) + ")");
+    // the last token's residual row feeds the decode lm_head
+    check(mf_copy(rs_.x, 0, rs_.pf_x, (size_t)(last_rows - 1) * cfg_.d_model * 4, (size_t)cfg_.d_model * 4),
+          "prefill last row");
+    rs_.cur_pos = pos0 + n - 1;
+    rs_.token_id = tokens[n - 1];
+    if (!compute_logits) return true;
+    rs_.compute_logits = true;
+    rs_.host_logits = host_logits;
+    rs_.h_step[0] = (int32_t)tokens[n - 1];
+    rs_.h_step[1] = pos0 + n - 1;
+    rs_.h_step[3] = 0;
+    rs_.h_step[MF_STEP_FRAME] += 1;
+    const int frame = frame_base_ + (host_logits ? 6 : 5);
+    const int rc = mf_begin_frame(rank_, frame);
+    if (rc < 0) check(rc, "begin_frame");
+    if (rc == MF_FRAME_RECORD) {
+        try {
+            layers_.back()->cuda_forward(rs_);
+            check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, 16, rs_.stream), "step readback");
+            if (host_logits)
+                check(mf_copy_to_host_async(rs_.h_logits, mf_ptr(rs_.logits), cfg_.vocab_size * 4, rs_.stream),
+                      "logits readback");
+        } catch (...) {
+            mf_abort_frame(rank_);
+            throw;
+        }
+    }
+    check(mf_end_frame(rank_), "end_frame");
+    return true;
+}
+
 size_t Qwen3Model::read_bytes(bool with_logits) const {
     size_t b = 0;
     for (size_t i = 0; i + 1 < layers_.size(); ++i) b += layers_[i]->read_bytes();
@@ -601,10 +739,13 @@ std::vector<uint32_t> Qwen3Model::generate(const std::vector<uint32_t>& prompt, 
     GenStats st;
     size_t model_bytes = 0, kv_bytes = 0;
     const double t0 = now_s();
-    // prefill, token by token (src/base/model.cpp:120-129)
+    // prefill: batched on the tensor cores when the model allows it, else
+    // token by token as the reference does (src/base/model.cpp:120-129)
+    const bool batched = opt.batched_prefill && prompt.size() > 1 &&
+                         prefill(prompt.data(), (int)prompt.size(), 0, true, need_host);
     for (size_t i = 0; i < prompt.size(); ++i) {
         const bool last = i + 1 == prompt.size();
-        forward(prompt[i], (int)i, last, last && need_host);
+        if (!batched) forward(prompt[i], (int)i, last, last && need_host);
         model_bytes += read_bytes(last);
         kv_bytes += rs_.kv_bytes_per_pos * (i + 1);
     }

@@ -19,6 +19,8 @@
 
 namespace minfer {
 
+constexpr int kPrefillChunk = 4096;  // prompt tokens per batched-prefill pass
+
 // include/minfer/base/config.hpp:22 plus the CUDA device this runtime adds
 enum class DeviceType : int { CPU = 0, METAL = 1, CUDA = 2 };
 
@@ -97,12 +99,20 @@ struct RunState {
     // all-reduces alternate between (x aliases xb[0])
     mf_comm* comm = nullptr;
     mf_buf* xb[2] = {nullptr, nullptr};
+    // batched prefill (allocated on first use): residual rows, bf16 hi/lo
+    // GEMM operands (two pairs: a GEMM's input and its SwiGLU output), the
+    // fused QKV rows, normalised/rotated queries, token ids
+    int pf_cap = 0;  // rows per chunk
+    mf_buf *pf_x = nullptr, *pf_hi = nullptr, *pf_lo = nullptr, *pf_hhi = nullptr, *pf_hlo = nullptr;
+    mf_buf *pf_qkv = nullptr, *pf_q = nullptr, *pf_tok = nullptr;
 };
 
 class BaseLayer {
 public:
     virtual ~BaseLayer();
     virtual void cuda_forward(RunState& rs) = 0;
+    // Batched prefill of rows [0, n) of the prefill buffers at positions pos0.. (tcgen05 GEMMs).
+    virtual void prefill_forward(RunState& rs, int n, int pos0);
     virtual void upload(const GGUFFile& f, int rank) = 0;
     size_t read_bytes() const { return read_bytes_; }
 
@@ -127,11 +137,18 @@ public:
     uint32_t device_argmax() const { return (uint32_t)rs_.h_step[2]; }
     // Bytes the reference counts per forward (src/base/module.cpp read bytes).
     size_t read_bytes(bool with_logits) const;
+    // Batched prefill of `n` prompt tokens at positions [pos0, pos0 + n) in
+    // chunks (the reference's token-by-token prefill, src/base/model.cpp:120-129,
+    // as tensor-core GEMMs); leaves the last token's logits / greedy id like
+    // forward(). False when the model is not eligible (see prefill_supported).
+    bool prefill(const uint32_t* tokens, int n, int pos0, bool compute_logits, bool host_logits);
+    bool prefill_supported() const;
 
     struct GenOptions {
         bool stop_at_eos = false;
         const uint32_t* forced = nullptr;  // teacher forcing: feed forced[i] after step i
         bool trace = false;                // host logits every step (margins, callbacks)
+        bool batched_prefill = true;       // tensor-core prefill when supported (else token by token)
         std::function<void(size_t step, const float* logits, uint32_t picked)> on_step;
     };
     // BaseModel::generate without the tokenizer (src/base/model.cpp:99-186).
@@ -157,6 +174,7 @@ public:
 private:
     void build_layers();
     void alloc_state();
+    void alloc_prefill(int rows);
     void issue_frame(bool readback);
 
     std::string path_;

@@ -11,8 +11,8 @@ import dataclasses
 
 import numpy as np
 
-from ._lib import (MF_COMM_HANDLE_BYTES, MF_GEN_MARGINS, MF_GEN_STOP_AT_EOS, check, cuda_lib, host_lib,
-                   mf_gen_stats, mf_model_info, mf_run_params)
+from ._lib import (MF_COMM_HANDLE_BYTES, MF_E_UNSUPPORTED, MF_GEN_MARGINS, MF_GEN_STOP_AT_EOS, MF_GEN_TOKEN_PREFILL,
+                   MinferError, check, cuda_lib, host_lib, mf_gen_stats, mf_model_info, mf_run_params)
 
 
 @dataclasses.dataclass
@@ -134,14 +134,26 @@ class Qwen3Model:
         check(self._lib.mf_model_argmax(self._h, C.byref(v)))
         return v.value
 
+    # -- batched prefill (tensor cores); False when the model is not eligible
+    def prefill(self, tokens, pos0: int = 0, compute_logits: bool = True, host_logits: bool = True) -> bool:
+        tokens = np.ascontiguousarray(tokens, dtype=np.uint32)
+        rc = self._lib.mf_model_prefill(self._h, tokens.ctypes.data, tokens.size, int(pos0), int(compute_logits),
+                                        int(host_logits))
+        if rc == MF_E_UNSUPPORTED:
+            return False
+        check(rc)
+        return True
+
     # -- BaseModel::generate (ids in, ids out)
-    def generate(self, prompt, n_gen: int, stop_at_eos: bool = False, forced=None, margins: bool = False):
+    def generate(self, prompt, n_gen: int, stop_at_eos: bool = False, forced=None, margins: bool = False,
+                 token_prefill: bool = False):
         prompt = np.ascontiguousarray(prompt, dtype=np.uint32)
         out = np.zeros(n_gen, dtype=np.uint32)
         mg = np.zeros(n_gen, dtype=np.float32)
         n_out = C.c_size_t()
         st = mf_gen_stats()
-        flags = (MF_GEN_STOP_AT_EOS if stop_at_eos else 0) | (MF_GEN_MARGINS if margins else 0)
+        flags = ((MF_GEN_STOP_AT_EOS if stop_at_eos else 0) | (MF_GEN_MARGINS if margins else 0) |
+                 (MF_GEN_TOKEN_PREFILL if token_prefill else 0))
         forced_arr = None if forced is None else np.ascontiguousarray(forced, dtype=np.uint32)
         check(self._lib.mf_model_generate(self._h, prompt.ctypes.data, prompt.size, n_gen, flags,
                                           None if forced_arr is None else forced_arr.ctypes.data, out.ctypes.data,

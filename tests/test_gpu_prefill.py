@@ -180,3 +180,66 @@ def test_prefill_qkv_post_matches_decode_rotation(lib, gpu):
             np.testing.assert_allclose(kc[h, pos0 + t].cpu().numpy(), exp, rtol=2e-6, atol=2e-6)
             np.testing.assert_array_equal(vc[h, pos0 + t].cpu().numpy(), qkv[t, (Hq + Hkv + h) * D:(Hq + Hkv + h + 1) * D])
     assert kc[:, :pos0].abs().sum().item() == 0 and kc[:, pos0 + T:].abs().sum().item() == 0
+
+
+# ------------------------------------------------------------------ model level
+
+@pytest.mark.parametrize("name", ["tiny-bf16", "tiny-gqa8", "tiny-tp8"])
+@pytest.mark.parametrize("chunk", [None, 16])
+def test_model_prefill_vs_oracle(gpu, monkeypatch, name, chunk):
+    """Batched prefill (tensor cores) of a 40-token prompt: last-token logits,
+    greedy id and every KV row against the oracle's token-by-token prefill."""
+    from conftest import TINY, tiny_model
+    from minfer_b200.model import Qwen3Model, RunParams, random_prompt
+    from oracle.oracle_py import PortModel
+
+    if chunk:
+        monkeypatch.setenv("MF_PREFILL_CHUNK", str(chunk))
+    cfg = TINY[name]
+    path = tiny_model(name)
+    Pn = 40
+    prompt = random_prompt(Pn, cfg.vocab, 11)
+    m = Qwen3Model(path, RunParams(max_seq_len=Pn + 8)).set_device("cuda")
+    assert m.prefill(prompt, 0, True, True)
+    orc = PortModel(path, max_seq=Pn + 8)
+    for i, t in enumerate(prompt):
+        orc.forward(int(t), i, i == Pn - 1)
+    lo, lg = orc.logits(), m.logits()
+    assert np.max(np.abs(lo - lg)) <= 2e-3, np.max(np.abs(lo - lg))
+    assert m.argmax() == int(np.argmax(lg))
+    kvd = cfg.n_kv_heads * cfg.d_head
+    for layer in range(cfg.n_layers):
+        k, v = m.kv(layer, Pn)
+        ko, vo = orc.kv(layer, Pn, kvd)
+        np.testing.assert_allclose(k, ko, rtol=1e-4, atol=2e-5)
+        np.testing.assert_allclose(v, vo, rtol=1e-4, atol=2e-5)
+
+
+@pytest.mark.parametrize("name", ["tiny-bf16", "tiny-tp8"])
+def test_generate_batched_prefill_matches_token_prefill(gpu, name):
+    """generate(): batched prefill and the reference's token-by-token prefill
+    give the same greedy continuation (margin rule) and close margins."""
+    from conftest import TINY, tiny_model
+    from minfer_b200.model import Qwen3Model, RunParams, random_prompt
+
+    cfg = TINY[name]
+    path = tiny_model(name)
+    Pn, G = 64, 24
+    prompt = random_prompt(Pn, cfg.vocab, 21)
+    a = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=Pn + G + 1)).set_device("cuda")
+    ids_tok, mg_tok, _ = a.generate(prompt, G, margins=True, token_prefill=True)
+    b = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=Pn + G + 1)).set_device("cuda")
+    ids_b, mg_b, _ = b.generate(prompt, G, forced=ids_tok, margins=True)
+    for i in range(G):
+        if ids_b[i] != ids_tok[i]:
+            assert mg_tok[i] < 1e-3, (i, mg_tok[i])
+    np.testing.assert_allclose(mg_b, mg_tok, atol=2e-3)
+
+
+def test_prefill_not_eligible_falls_back(gpu):
+    from conftest import tiny_model
+    from minfer_b200.model import Qwen3Model, RunParams
+
+    for name in ("tiny-f32", "tiny-moe"):
+        m = Qwen3Model(tiny_model(name), RunParams(max_seq_len=32)).set_device("cuda")
+        assert m.prefill(np.arange(5, dtype=np.uint32)) is False
