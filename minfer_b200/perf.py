@@ -2,6 +2,7 @@
 
     python -m minfer_b200.perf gemv --rows 24576 --k 4096 --mode swiglu
     python -m minfer_b200.perf attn --hq 32 --hkv 8 --ctx 4096
+    python -m minfer_b200.perf gemm --m 4096 --n 24576 --k 4096 --mode swiglu
 
 Prints one JSON line per case: average device time per launch (CUDA events
 around a CUDA-graph replay of `--iters` launches on torch's stream, after
@@ -89,6 +90,34 @@ def attn(args) -> dict:
             "algo_bytes": algo, "gbs": round(algo / us / 1e3, 1)}
 
 
+def gemm(args) -> dict:
+    """The batched-prefill tcgen05 GEMM: M tokens x N outputs x K, bf16 hi/lo activations."""
+    import ctypes as C
+
+    from . import ops
+    from ._lib import MF_PREFILL_RESID, MF_PREFILL_STORE, MF_PREFILL_SWIGLU, check, cuda_lib
+
+    lib = cuda_lib()
+    M, N, K = args.m, args.n, args.k
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randn(M, K, generator=g, device="cuda")
+    hi = a.to(torch.bfloat16)
+    lo = (a - hi.float()).to(torch.bfloat16)
+    ws = [(torch.randn(N, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16) for _ in range(args.copies)]
+    mode = {"store": MF_PREFILL_STORE, "resid": MF_PREFILL_RESID, "swiglu": MF_PREFILL_SWIGLU}[args.mode]
+    y = torch.zeros(M, N, device="cuda") if mode != MF_PREFILL_SWIGLU else None
+    hh = torch.empty(M, N // 2, dtype=torch.bfloat16, device="cuda") if mode == MF_PREFILL_SWIGLU else None
+    hl = torch.empty_like(hh) if hh is not None else None
+    P = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None
+    # the stream is looked up per launch: inside the graph capture it is torch's capture stream
+    fn = lambda i: check(lib.mf_prefill_gemm(P(y), N if y is not None else 0, P(hi), P(lo), P(ws[i % len(ws)]), M, N,
+                                             K, mode, P(hh), P(hl), C.c_void_p(ops._stream())))
+    us = _time(fn, args.iters, args.warmup)
+    flops = 2.0 * M * N * K  # algorithmic (the hi/lo split executes twice this on the tensor cores)
+    return {"op": f"prefill-gemm-{args.mode}", "m": M, "n": N, "k": K, "us": round(us, 2),
+            "tflops": round(flops / us / 1e6, 1), "tensor_tflops": round(2 * flops / us / 1e6, 1)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -102,13 +131,18 @@ def main():
     b.add_argument("--hkv", type=int, default=8)
     b.add_argument("--ctx", type=int, default=4096)
     b.add_argument("--split", type=int, default=0)
-    for p in (a, b):
+    c = sub.add_parser("gemm")
+    c.add_argument("--m", type=int, default=4096)
+    c.add_argument("--n", type=int, default=24576)
+    c.add_argument("--k", type=int, default=4096)
+    c.add_argument("--mode", default="swiglu", choices=["store", "resid", "swiglu"])
+    for p in (a, b, c):
         p.add_argument("--iters", type=int, default=20)
         p.add_argument("--warmup", type=int, default=5)
         p.add_argument("--copies", type=int, default=2)
     args = ap.parse_args()
     mm.init(1, [torch.cuda.current_device()])
-    res = gemv(args) if args.what == "gemv" else attn(args)
+    res = {"gemv": gemv, "attn": attn, "gemm": gemm}[args.what](args)
     print(json.dumps(res), flush=True)
 
 
