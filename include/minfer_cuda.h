@@ -295,6 +295,18 @@ int mf_allreduce_swiglu_matmul(float* h, const float* x_res, float* x_out, const
 int mf_allreduce_lm_head(float* logits, const float* x_res, float* x_out, const float* norm_w, float eps,
                          const void* w, int dtype, int vocab, int d_model, int vocab_offset, void* step_state,
                          void* workspace, int gather_logits, mf_comm* c, int seq, void* stream);
+/* Expert parallelism (MoE): each rank stores experts [expert_lo,
+ * expert_lo + n_local) (expert e at local index e - expert_lo); the router
+ * runs on every rank, so all ranks hold the same ids. Slots routed to another
+ * rank's experts produce zeros here. mf_moe_swiglu_ep is mf_moe_swiglu over
+ * the local experts; mf_moe_down_push computes this rank's weighted sum of its
+ * experts' down projections (slot order) and sends it as exchange `seq`, to be
+ * received by the next mf_allreduce_* call (the residual add happens there). */
+int mf_moe_swiglu_ep(float* h, const float* x, const float* norm_w, float eps, const void* w_gate_up_local, int dtype,
+                     const int* ids, int k, int d_ff, int d_in, int expert_lo, int n_local, void* stream);
+int mf_moe_down_push(const float* h, const void* w_down_local, int dtype, const int* ids, const float* weights, int k,
+                     int d_model, int d_ff, int expert_lo, int n_local, mf_comm* c, int seq, const void* step_state,
+                     void* stream);
 /* Stand-alone all-reduce of n floats (one kernel): x_out = x_res + sum over
  * ranks of `partial` (rank order). x_out may equal x_res. */
 int mf_allreduce(float* x_out, const float* x_res, const float* partial, int n, mf_comm* c, int seq,

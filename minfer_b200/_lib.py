@@ -139,6 +139,8 @@ CUDA_API = {
     "mf_allreduce_swiglu_matmul": (I, [P, P, P, P, F, P, I, I, I, P, I, P, P]),
     "mf_allreduce_lm_head": (I, [P, P, P, P, F, P, I, I, I, I, P, P, I, P, I, P]),
     "mf_allreduce": (I, [P, P, P, I, P, I, P, P]),
+    "mf_moe_swiglu_ep": (I, [P, P, P, F, P, I, P, I, I, I, I, I, P]),
+    "mf_moe_down_push": (I, [P, P, I, P, P, I, I, I, I, I, P, I, P, P]),
     "mf_prefill_gemm": (I, [P, I, P, P, P, I, I, I, I, P, P, P]),
     "mf_prefill_norm_split": (I, [P, P, P, P, P, F, I, I, P]),
     "mf_prefill_split": (I, [P, P, P, SZ, P]),

@@ -188,7 +188,7 @@ int prepare(const void* fn, int threads, size_t smem, int* blocks_per_sm) {
 }
 
 const void* gemv_ptr(int dtype, int xm, int ym, int T, int R) {
-    if (xm == mf::X_AR_NORM || ym == mf::Y_PUSH) {
+    if (xm == mf::X_AR_NORM || ym == mf::Y_PUSH || ym == mf::Y_MOE_PUSH) {
         switch (dtype) {
             case MF_F32: return mf::gemv_tp_kernel_ptr_f32(xm, ym, T, R);
             case MF_F16: return mf::gemv_tp_kernel_ptr_f16(xm, ym, T, R);
@@ -217,7 +217,7 @@ void choose_shape(int K, int dtype, int ym, int* T_out, int* R_out) {
     for (int ti = 0; ti < 3; ++ti) {
         for (int ri = 0; ri < 3; ++ri) {
             const int T = Ts[ti], R = Rs[ri], PC = 8 / R;
-            if (ym == mf::Y_MOE_DOWN && R != 8) continue;
+            if ((ym == mf::Y_MOE_DOWN || ym == mf::Y_MOE_PUSH) && R != 8) continue;
             const long long step = (long long)PC * T * vec;
             const long long nsteps = (K + step - 1) / step;
             const double waste = (double)(nsteps * step) / K;
@@ -249,7 +249,8 @@ int run_gemv(int dtype, int xm, int ym, mf::GemvParams& p, long long units, cuda
     MF_REQUIRE(fn != nullptr, MF_E_UNSUPPORTED, "no GEMV kernel for dtype %d", dtype);
     // X_NORM keeps the norm weights beside x
     const bool norm = xm == mf::X_NORM || xm == mf::X_AR_NORM;
-    const size_t xfloats = (ym == mf::Y_MOE_DOWN) ? (size_t)p.K * p.n_slots : (size_t)p.K * (norm ? 2 : 1);
+    const bool moe_down = ym == mf::Y_MOE_DOWN || ym == mf::Y_MOE_PUSH;
+    const size_t xfloats = moe_down ? (size_t)p.K * p.n_slots : (size_t)p.K * (norm ? 2 : 1);
     const size_t smem = xfloats * sizeof(float);
     MF_REQUIRE(smem <= 200 * 1024, MF_E_UNSUPPORTED, "activation vector of %zu floats exceeds shared memory", xfloats);
     int bps = 0;
@@ -764,7 +765,7 @@ int mf_moe_swiglu(float* h, const float* x, const float* norm_w, float eps, cons
                   const int* ids, int k, int d_ff, int d_in, void* stream) {
     MF_REQUIRE(h && x && norm_w && w_gate_up_exps && ids, MF_E_INVALID, "null argument");
     MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
-    MF_REQUIRE(k >= 1 && d_ff > 0, MF_E_INVALID, "bad k/d_ff");
+    MF_REQUIRE(k >= 1 && k <= 32 && d_ff > 0, MF_E_INVALID, "bad k/d_ff (k must be 1..32)");
     mf::GemvParams p = {};
     p.w = w_gate_up_exps;
     p.x = x;
@@ -1044,6 +1045,54 @@ int mf_allreduce_lm_head(float* logits, const float* x_res, float* x_out, const 
         p.step = (int*)step_state;
     }
     return run_gemv(dtype, mf::X_AR_NORM, mf::Y_STORE, p, vocab, resolve(stream), LMH_MAX_GRID);
+}
+
+int mf_moe_swiglu_ep(float* h, const float* x, const float* norm_w, float eps, const void* w_gate_up_local, int dtype,
+                     const int* ids, int k, int d_ff, int d_in, int expert_lo, int n_local, void* stream) {
+    MF_REQUIRE(h && x && norm_w && w_gate_up_local && ids, MF_E_INVALID, "null argument");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    MF_REQUIRE(k >= 1 && k <= 32 && d_ff > 0 && expert_lo >= 0 && n_local >= 1, MF_E_INVALID,
+               "bad k/d_ff/expert range (k must be 1..32)");
+    mf::GemvParams p = {};
+    p.w = w_gate_up_local;
+    p.x = x;
+    p.nw = norm_w;
+    p.eps = eps;
+    p.y = h;
+    p.rows = 2 * d_ff * k;
+    p.K = d_in;
+    p.expert_ids = ids;
+    p.rows_per_expert = 2 * d_ff;
+    p.ep_lo = expert_lo;
+    p.ep_n = n_local;
+    return run_gemv(dtype, mf::X_NORM, mf::Y_SWIGLU, p, (long long)d_ff * k, resolve(stream));
+}
+
+int mf_moe_down_push(const float* h, const void* w_down_local, int dtype, const int* ids, const float* weights, int k,
+                     int d_model, int d_ff, int expert_lo, int n_local, mf_comm* c, int seq, const void* step_state,
+                     void* stream) {
+    MF_REQUIRE(h && w_down_local && ids && weights, MF_E_INVALID, "null argument");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    MF_REQUIRE(k >= 1 && k <= 8, MF_E_UNSUPPORTED, "k %d (grouped down projection supports 1..8)", k);
+    MF_REQUIRE(expert_lo >= 0 && n_local >= 1, MF_E_INVALID, "bad expert range");
+    int rc = comm_ready(c, seq, step_state);
+    if (rc) return rc;
+    MF_REQUIRE(d_model <= c->dev.max_floats, MF_E_INVALID, "d_model %d exceeds the exchange slot", d_model);
+    mf::GemvParams p = {};
+    p.w = w_down_local;
+    p.x = h;
+    p.rows = d_model;
+    p.K = d_ff;
+    p.expert_ids = ids;
+    p.expert_w = weights;
+    p.rows_per_expert = d_model;
+    p.n_slots = k;
+    p.ep_lo = expert_lo;
+    p.ep_n = n_local;
+    p.comm = c->dev;
+    p.ar_seq = seq;
+    p.step = (int*)step_state;
+    return run_gemv(dtype, mf::X_PLAIN, mf::Y_MOE_PUSH, p, d_model, resolve(stream));
 }
 
 int mf_allreduce(float* x_out, const float* x_res, const float* partial, int n, mf_comm* c, int seq,

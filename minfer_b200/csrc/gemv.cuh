@@ -34,7 +34,9 @@ namespace mf {
 // Y_PUSH: the rows' partial sums are stored into every rank's receive slot of
 // an all-reduce instead of locally.
 enum XMode { X_PLAIN = 0, X_NORM = 1, X_AR_NORM = 2 };
-enum YMode { Y_STORE = 0, Y_RESID = 1, Y_SWIGLU = 2, Y_MOE_DOWN = 3, Y_PUSH = 4 };
+// Y_MOE_PUSH: the grouped expert down projection of this rank's experts,
+// pushed as its partial of an all-reduce (expert parallelism).
+enum YMode { Y_STORE = 0, Y_RESID = 1, Y_SWIGLU = 2, Y_MOE_DOWN = 3, Y_PUSH = 4, Y_MOE_PUSH = 5 };
 
 struct GemvParams {
     const void* w;        // weight rows, dtype given by the template
@@ -49,7 +51,11 @@ struct GemvParams {
     const int* expert_ids;      // [k] device, or null for dense weights
     const float* expert_w;      // [k] device (Y_MOE_DOWN)
     int rows_per_expert;        // physical rows per expert matrix
-    int n_slots;                // k for Y_MOE_DOWN
+    int n_slots;                // k for Y_MOE_DOWN / Y_MOE_PUSH
+    // expert parallelism: only experts [ep_lo, ep_lo + ep_n) are stored here
+    // (expert e at local index e - ep_lo); slots routed elsewhere contribute
+    // nothing. ep_n == 0: every expert is local.
+    int ep_lo, ep_n;
     // greedy argmax finisher (Y_STORE only; counter may be null)
     float* best_val;            // [gridDim.x]
     int* best_idx;              // [gridDim.x]
@@ -71,9 +77,12 @@ struct GemvParams {
 
 // The all-reduce receive prologue holds tagged words next to the first
 // weight loads: keep such kernels at two resident CTAs per SM.
+MF_DEVICE bool expert_local(const GemvParams& p, int e) { return p.ep_n == 0 || (e >= p.ep_lo && e < p.ep_lo + p.ep_n); }
+
 template <typename W, int T, int R, int PC, int XM, int YM>
 __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2) ? 2 : MF_GEMV_MIN_BLOCKS)
     gemv_kernel(const GemvParams p) {
+    constexpr bool MOE_DOWN = (YM == Y_MOE_DOWN || YM == Y_MOE_PUSH);
     constexpr int VEC = W::VEC;
     constexpr int NW = T / 32;
     constexpr int RU = (YM == Y_SWIGLU) ? 2 : 1;  // rows per unit
@@ -85,6 +94,8 @@ __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2)
     __shared__ float red[2][NW][R];
     __shared__ float scratch[32];
     __shared__ int scratch_i[32];
+    __shared__ int ids_s[32];    // expert ids of the slots (indirect modes), read once per launch
+    __shared__ float ew_s[32];   // their routing weights (grouped down projection)
     __shared__ float cta_best_v;
     __shared__ int cta_best_i;
     __shared__ int is_last;
@@ -96,16 +107,28 @@ __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2)
     const size_t row_bytes = (size_t)K * esz;
 
     // ---- unit range of this CTA
-    const long long units = (YM == Y_MOE_DOWN) ? p.rows : p.rows / RU;
+    const long long units = MOE_DOWN ? p.rows : p.rows / RU;
     const long long u0 = (long long)blockIdx.x * units / gridDim.x;
     const long long u1 = (long long)(blockIdx.x + 1) * units / gridDim.x;
     const int rows0 = (int)(u0 * RU), rows1 = (int)(u1 * RU);
     // Y_MOE_DOWN: one output row per tile, tile row r = expert slot r.
-    const int ntiles = (YM == Y_MOE_DOWN) ? (rows1 - rows0) : (rows1 - rows0 + R - 1) / R;
+    const int ntiles = MOE_DOWN ? (rows1 - rows0) : (rows1 - rows0 + R - 1) / R;
     constexpr int STEP_COLS = PC * T * VEC;
     const int nsteps = (K + STEP_COLS - 1) / STEP_COLS;
     const int nitems = ntiles * nsteps;
-    const bool indirect = (YM == Y_MOE_DOWN) || (p.expert_ids != nullptr);
+    const bool indirect = MOE_DOWN || (p.expert_ids != nullptr);
+    const int n_ids = MOE_DOWN ? p.n_slots : (indirect ? p.rows / p.rows_per_expert : 0);
+    const int ep_base = p.ep_n ? p.ep_lo : 0;
+    // rows of the gate/up expert tile starting at logical row r0 lie in one
+    // local expert: its first physical row (or -1 when not, or when the
+    // slot's expert is stored on another rank)
+    auto expert_tile_row = [&](int r0) -> long long {
+        const int s0 = r0 / p.rows_per_expert;
+        if ((min(r0 + R, rows1) - 1) / p.rows_per_expert != s0) return -1;
+        const int e = ids_s[s0];
+        if (!expert_local(p, e)) return -1;
+        return (long long)(e - ep_base) * p.rows_per_expert + (r0 - s0 * p.rows_per_expert);
+    };
 
     int eid[R];
 #pragma unroll
@@ -142,17 +165,17 @@ __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2)
         for (int r = 0; r < R; ++r) {
             bool valid;
             long long phys;
-            if (YM == Y_MOE_DOWN) {
+            if (MOE_DOWN) {
                 const int j = rows0 + tile;
-                valid = r < p.n_slots;
-                phys = (long long)eid[r] * p.rows_per_expert + j;
+                valid = r < p.n_slots && expert_local(p, eid[r]);
+                phys = (long long)(eid[r] - (p.ep_n ? p.ep_lo : 0)) * p.rows_per_expert + j;
             } else {
                 const int lr = rows0 + tile * R + r;
                 valid = lr < rows1;
-                const int slot = lr / p.rows_per_expert;
-                phys = valid ? (long long)__ldcg(p.expert_ids + slot) * p.rows_per_expert +
-                                   (lr - slot * p.rows_per_expert)
-                             : 0;
+                const int slot = valid ? lr / p.rows_per_expert : 0;
+                const int e = ids_s[slot];
+                valid = valid && expert_local(p, e);
+                phys = valid ? (long long)(e - ep_base) * p.rows_per_expert + (lr - slot * p.rows_per_expert) : 0;
             }
             const char* rp = wbase + phys * row_bytes + coff;
 #pragma unroll
@@ -163,17 +186,41 @@ __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2)
             }
         }
     };
+    // gate/up over experts: a full tile inside one local expert is a
+    // contiguous run of rows, loaded like a dense tile
+    auto load_expert = [&](uint4 (&buf)[R][PC], int it) {
+        if (!MOE_DOWN && k_exact) {
+            const int tile = it / nsteps, step = it - tile * nsteps;
+            const int r0 = rows0 + tile * R;
+            const long long pr = (r0 + R <= rows1) ? expert_tile_row(r0) : -1;
+            if (pr >= 0) {
+                const size_t coff = ((size_t)(step * PC) * T + tid) * VEC * esz;
+                const char* tp = wbase + (size_t)pr * row_bytes + coff;
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+#pragma unroll
+                    for (int c = 0; c < PC; ++c) buf[r][c] = ld_stream(tp + r * row_bytes + c * CSTRIDE);
+                return;
+            }
+        }
+        load(buf, it);
+    };
 
     // L2 prefetch window (dense weights): the CTA's rows are one contiguous
     // byte range, so one bulk prefetch per tile keeps `pf_ahead` tiles in
     // flight ahead of the register loads without holding registers.
     const size_t tile_bytes = (size_t)R * row_bytes;
-    const int pf_ahead = indirect ? -1
+    const int pf_ahead = MOE_DOWN ? -1
                                   : (tile_bytes <= 48 * 1024 ? p.pf_tiles : (tile_bytes <= 128 * 1024 ? 1 : -1));
     auto prefetch_tile = [&](int t) {
         if (t >= ntiles) return;
         const int r0 = rows0 + t * R;
         const int r1 = min(r0 + R, rows1);
+        if (indirect) {
+            const long long pr = expert_tile_row(r0);
+            if (pr >= 0) prefetch_l2(wbase + (size_t)pr * row_bytes, (uint32_t)((size_t)(r1 - r0) * row_bytes));
+            return;
+        }
         prefetch_l2(wbase + (size_t)r0 * row_bytes, (uint32_t)((size_t)(r1 - r0) * row_bytes));
     };
 
@@ -181,7 +228,7 @@ __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2)
     // Dense weights and norm weights do not depend on earlier kernels: start
     // streaming them before the dependency wait. Expert ids come from the
     // router kernel.
-    if (tid == 0)
+    if (tid == 0 && !indirect)
         for (int t = 0; t <= pf_ahead; ++t) prefetch_tile(t);
     if (!indirect && nitems > 0) load(bufA, 0);
     if (XM == X_NORM || XM == X_AR_NORM)
@@ -191,15 +238,25 @@ __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2)
     // triggering after the last weight load).
     pdl_launch_dependents();
     pdl_wait();
-    if (YM == Y_MOE_DOWN) {
+    if (indirect) {
+        // expert ids (and weights) come from the router kernel: read them once
+        if (tid < 32) {
+            ids_s[tid] = tid < n_ids ? __ldcg(p.expert_ids + tid) : 0;
+            ew_s[tid] = (MOE_DOWN && tid < n_ids) ? __ldcg(p.expert_w + tid) : 0.f;
+        }
+        __syncthreads();
+        if (MOE_DOWN) {
 #pragma unroll
-        for (int r = 0; r < R; ++r) eid[r] = (r < p.n_slots) ? __ldcg(p.expert_ids + r) : 0;
+            for (int r = 0; r < R; ++r) eid[r] = (r < p.n_slots) ? ids_s[r] : 0;
+        }
+        if (tid == 0)
+            for (int t = 0; t <= pf_ahead; ++t) prefetch_tile(t);
+        if (nitems > 0) load_expert(bufA, 0);
     }
-    if (indirect && nitems > 0) load(bufA, 0);
 
     // tagged words of a push (tensor-parallel send)
     uint32_t push_tag = 0;
-    if (YM == Y_PUSH) push_tag = comm_tag(__ldcg(p.step + MF_STEP_FRAME), p.ar_seq);
+    if (YM == Y_PUSH || YM == Y_MOE_PUSH) push_tag = comm_tag(__ldcg(p.step + MF_STEP_FRAME), p.ar_seq);
 
     // ---- prologue: activation vector(s) -> shared memory
     if (XM == X_NORM || XM == X_AR_NORM) {
@@ -231,9 +288,21 @@ __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2)
         const float inv = 1.0f / sqrtf(ss / (float)K + p.eps);
         for (int i = tid; i < K; i += T) xs[i] = (inv * xs[i]) * xs[K + i];
     } else {
-        const int xlen = (YM == Y_MOE_DOWN) ? K * p.n_slots : K;
-        for (int i = tid * 4; i < xlen; i += T * 4) {
-            *reinterpret_cast<float4*>(xs + i) = __ldcg(reinterpret_cast<const float4*>(p.x + i));
+        // all of a thread's 16-byte loads of a batch are issued before any is stored
+        const int xlen = MOE_DOWN ? K * p.n_slots : K;
+        constexpr int XB = 8;
+        for (int i0 = tid * 4; i0 < xlen; i0 += T * 4 * XB) {
+            float4 v[XB];
+#pragma unroll
+            for (int u = 0; u < XB; ++u) {
+                const int i = i0 + u * T * 4;
+                if (i < xlen) v[u] = __ldcg(reinterpret_cast<const float4*>(p.x + i));
+            }
+#pragma unroll
+            for (int u = 0; u < XB; ++u) {
+                const int i = i0 + u * T * 4;
+                if (i < xlen) *reinterpret_cast<float4*>(xs + i) = v[u];
+            }
         }
     }
     if (tid == 0) {
@@ -247,13 +316,15 @@ __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2)
     for (int r = 0; r < R; ++r) acc[r] = 0.f;
     int par = 0;
 
+    float y_pre = 0.f;  // Y_MOE_DOWN: the residual of the tile's output row, fetched early
     auto consume = [&](const uint4 (&buf)[R][PC], int it) {
         const int tile = it / nsteps, step = it - tile * nsteps;
+        if (YM == Y_MOE_DOWN && step == 0 && tid == 0) y_pre = __ldcg(p.y + rows0 + tile);
 #pragma unroll
         for (int c = 0; c < PC; ++c) {
             const int col = ((step * PC + c) * T + tid) * VEC;
             if (col < K) {
-                if (YM == Y_MOE_DOWN) {
+                if (MOE_DOWN) {
 #pragma unroll
                     for (int r = 0; r < R; ++r) {
                         if (r >= p.n_slots) break;  // xs holds n_slots vectors only
@@ -300,13 +371,29 @@ __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2)
                 if (lane == 0) {
                     const int j = rows0 + tile;
                     // src/models/qwen3/module.cpp:471-474: x += expert_out * weight, one expert at a time
-                    float xo = __ldcg(p.y + j);
+                    float xo = y_pre;
                     for (int r = 0; r < p.n_slots; ++r) {
                         float s = 0.f;
                         for (int w2 = 0; w2 < NW; ++w2) s += red[par][w2][r];
-                        xo = fmaf(s, __ldcg(p.expert_w + r), xo);
+                        xo = fmaf(s, ew_s[r], xo);
                     }
                     p.y[j] = xo;
+                }
+            } else if (YM == Y_MOE_PUSH) {
+                if (lane == 0) {
+                    // this rank's experts only, in slot order; the receiver adds
+                    // the ranks' partials to the residual in rank order
+                    const int j = rows0 + tile;
+                    float part = 0.f;
+                    for (int r = 0; r < p.n_slots; ++r) {
+                        if (!expert_local(p, eid[r])) continue;
+                        float s = 0.f;
+                        for (int w2 = 0; w2 < NW; ++w2) s += red[par][w2][r];
+                        part = fmaf(s, ew_s[r], part);
+                    }
+                    const unsigned long long w = tagged(part, push_tag);
+                    for (int r = 0; r < p.comm.tp_size; ++r)
+                        st_tagged(p.comm.recv(r, p.ar_seq & 1, p.comm.tp_rank) + j, w);
                 }
             } else if (YM == Y_SWIGLU) {
                 const int lr = rows0 + tile * R + 2 * lane;
@@ -359,20 +446,24 @@ __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2)
     auto advance_prefetch = [&](int it) {
         if (pf_ahead >= 0 && tid == 0 && it % nsteps == 0) prefetch_tile(it / nsteps + pf_ahead + 1);
     };
+    auto load_any = [&](uint4 (&buf)[R][PC], int it) {
+        if (indirect) load_expert(buf, it);
+        else load(buf, it);
+    };
 #ifdef MF_GEMV_SINGLE_BUFFER
     for (int it = 0; it < nitems; ++it) {
         advance_prefetch(it);
-        if (it > 0) load(bufA, it);
+        if (it > 0) load_any(bufA, it);
         consume(bufA, it);
     }
 #else
     for (int it = 0; it < nitems; it += 2) {
         advance_prefetch(it);
-        if (it + 1 < nitems) load(bufB, it + 1);
+        if (it + 1 < nitems) load_any(bufB, it + 1);
         consume(bufA, it);
         if (it + 1 >= nitems) break;
         advance_prefetch(it + 1);
-        if (it + 2 < nitems) load(bufA, it + 2);
+        if (it + 2 < nitems) load_any(bufA, it + 2);
         consume(bufB, it + 1);
     }
 #endif

@@ -13,7 +13,7 @@ const void* gemv_ptr_rpc(int T, int R) {
 #define MF_GEMV_T(TT)                                                                        \
     if (T == TT) {                                                                           \
         if (R == 8) return (const void*)&gemv_kernel<W, TT, 8, 1, XM, YM>;                  \
-        if (YM != Y_MOE_DOWN) {                                                              \
+        if (YM != Y_MOE_DOWN && YM != Y_MOE_PUSH) {                                          \
             if (R == 4) return (const void*)&gemv_kernel<W, TT, 4, 2, XM, YM>;              \
             if (R == 2) return (const void*)&gemv_kernel<W, TT, 2, 4, XM, YM>;              \
         }                                                                                    \
@@ -42,6 +42,7 @@ const void* gemv_tp_kernel_ptr(int xm, int ym, int T, int R) {
     if (xm == X_AR_NORM && ym == Y_STORE) return gemv_ptr_rpc<W, X_AR_NORM, Y_STORE>(T, R);
     if (xm == X_AR_NORM && ym == Y_SWIGLU) return gemv_ptr_rpc<W, X_AR_NORM, Y_SWIGLU>(T, R);
     if (xm == X_PLAIN && ym == Y_PUSH) return gemv_ptr_rpc<W, X_PLAIN, Y_PUSH>(T, R);
+    if (xm == X_PLAIN && ym == Y_MOE_PUSH) return gemv_ptr_rpc<W, X_PLAIN, Y_MOE_PUSH>(T, R);
     return nullptr;
 }
 

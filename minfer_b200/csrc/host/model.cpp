@@ -138,7 +138,7 @@ public:
         // fused [Wq; Wk; Wv] so one streaming pass computes q|k|v; under
         // tensor parallelism this rank's KV-head group: Q heads and K/V heads
         // [t*H/T, (t+1)*H/T), and the matching input columns of Wo
-        const size_t esz = dtype_size(wq.dtype), rowb = d * esz, t = c_.tp_rank;
+        const size_t esz = dtype_size(wq.dtype), rowb = d * esz, t = c_.attn_split() ? c_.tp_rank : 0;
         const size_t ql = (size_t)c_.heads_local() * c_.d_head, kvl = (size_t)c_.kv_heads_local() * c_.d_head;
         const char* qsrc = (const char*)wq.data + t * ql * rowb;
         const char* ksrc = (const char*)wk.data + t * kvl * rowb;
@@ -148,18 +148,27 @@ public:
         check(mf_write(wqkv_, ql * rowb, ksrc, kvl * rowb), "upload k");
         check(mf_write(wqkv_, (ql + kvl) * rowb, vsrc, kvl * rowb), "upload v");
         own(wqkv_);
-        own(wo_ = c_.tp_size == 1 ? upload_tensor(wo, rank) : upload_cols(wo, d, q * esz, t * ql * esz, ql * esz, rank));
+        own(wo_ = !c_.attn_split() ? upload_tensor(wo, rank) : upload_cols(wo, d, q * esz, t * ql * esz, ql * esz, rank));
         own(qn_ = upload_tensor(qn, rank));
         own(kn_ = upload_tensor(kn, rank));
         own(an_ = upload_tensor(an, rank));
         read_bytes_ = (ql + 2 * kvl) * rowb + d * ql * esz + qn.bytes + kn.bytes + an.bytes;
+        if (c_.ep()) read_bytes_ /= c_.tp_size;  // replicated: each rank counts its share
     }
     void cuda_forward(RunState& rs) override {
         const int d = c_.d_model, H = c_.heads_local(), Hkv = c_.kv_heads_local(), D = c_.d_head;
+        // expert parallelism: the residual of layer l lives in xb[l & 1]; the
+        // previous layer's expert all-reduce (exchange l - 1) is received here
+        float* xres = c_.ep() ? (float*)mf_ptr(rs.xb[layer_ & 1]) : (float*)mf_ptr(rs.x);
         if (c_.tp_size == 1 || layer_ == 0) {
             check(mf_rmsnorm_matmul((float*)mf_ptr(rs.qkv), (const float*)mf_ptr(rs.x), (const float*)mf_ptr(an_),
                                     c_.rms_norm_eps, mf_ptr(wqkv_), dtype_, (H + 2 * Hkv) * D, d, rs.stream),
                   "qkv projection");
+        } else if (c_.ep()) {
+            check(mf_allreduce_rmsnorm_matmul((float*)mf_ptr(rs.qkv), (const float*)mf_ptr(rs.xb[(layer_ - 1) & 1]),
+                                              xres, (const float*)mf_ptr(an_), c_.rms_norm_eps, mf_ptr(wqkv_), dtype_,
+                                              (H + 2 * Hkv) * D, d, rs.comm, layer_ - 1, rs.d_step, rs.stream),
+                  "qkv projection (expert all-reduce)");
         } else {
             // receive the previous layer's down-projection all-reduce
             check(mf_allreduce_rmsnorm_matmul((float*)mf_ptr(rs.qkv), (const float*)mf_ptr(rs.xb[1]),
@@ -185,9 +194,8 @@ public:
         a.n_split = rs.attn_split;
         a.workspace = mf_ptr(rs.attn_ws);
         check(mf_attn_decode(&a, rs.stream), "attention");
-        if (c_.tp_size == 1) {
-            check(mf_matmul_residual((float*)mf_ptr(rs.x), (const float*)mf_ptr(rs.att), mf_ptr(wo_), dtype_, d,
-                                     H * D, rs.stream),
+        if (!c_.attn_split()) {
+            check(mf_matmul_residual(xres, (const float*)mf_ptr(rs.att), mf_ptr(wo_), dtype_, d, H * D, rs.stream),
                   "output projection");
         } else {
             check(mf_matmul_push((const float*)mf_ptr(rs.att), mf_ptr(wo_), dtype_, d, H * D, rs.comm, 2 * layer_,
@@ -260,24 +268,30 @@ public:
         // [t*F/T, (t+1)*F/T) and the matching input columns of W_down
         const size_t esz = dtype_size(wg.dtype), row = (size_t)d * esz;
         const size_t Fl = moe ? F : (size_t)c_.ff_local(), t = moe ? 0 : c_.tp_rank;
-        const size_t nrows = moe ? wg.numel / d : Fl;
-        const char* gsrc = (const char*)wg.data + t * Fl * row;
-        const char* usrc = (const char*)wu.data + t * Fl * row;
+        // MoE: this rank's experts [lo, lo + n) (all of them without expert parallelism)
+        const size_t e_lo = moe ? (size_t)c_.expert_lo() : 0, e_n = moe ? (size_t)c_.experts_local() : 1;
+        const size_t nrows = moe ? e_n * F : Fl;
+        const char* gsrc = (const char*)wg.data + (moe ? e_lo * F * row : t * Fl * row);
+        const char* usrc = (const char*)wu.data + (moe ? e_lo * F * row : t * Fl * row);
         check(mf_alloc(2 * nrows * row, rank, &wgu_), "alloc gate/up");
         check(mf_write_2d(wgu_, 0, 2 * row, gsrc, row, row, nrows), "upload gate");
         check(mf_write_2d(wgu_, row, 2 * row, usrc, row, row, nrows), "upload up");
         own(wgu_);
-        own(wd_ = (moe || c_.tp_size == 1) ? upload_tensor(wd, rank)
-                                           : upload_cols(wd, d, F * esz, t * Fl * esz, Fl * esz, rank));
+        if (moe)
+            own(wd_ = c_.ep() ? upload_rows(wd, e_lo * d, e_n * d, F * esz, rank) : upload_tensor(wd, rank));
+        else
+            own(wd_ = c_.tp_size == 1 ? upload_tensor(wd, rank)
+                                      : upload_cols(wd, d, F * esz, t * Fl * esz, Fl * esz, rank));
         const size_t k = moe ? (size_t)c_.n_active_experts : 1, ne = moe ? E : 1;
         read_bytes_ = moe ? fn.bytes + (wg.bytes / ne + wu.bytes / ne + wd.bytes / ne) * k
                           : fn.bytes + 2 * Fl * row + d * Fl * esz;
+        if (c_.ep()) read_bytes_ /= c_.tp_size;  // the k active experts are spread over the ranks
         if (moe) {
             const TensorView& wr = f.tensor(p + "ffn_gate_inp.weight");
             expect_shape(wr, {E, d});
             expect_f32(wr);
             own(wr_ = upload_tensor(wr, rank));
-            read_bytes_ += wr.bytes;
+            read_bytes_ += c_.ep() ? wr.bytes / c_.tp_size : wr.bytes;
         }
     }
     void cuda_forward(RunState& rs) override {
@@ -305,6 +319,21 @@ public:
         const int k = c_.n_active_experts;
         int* ids = (int*)mf_ptr(rs.expert_ids) + (size_t)layer_ * k;
         float* w = (float*)mf_ptr(rs.expert_w) + (size_t)layer_ * k;
+        if (c_.ep()) {
+            // router on every rank (identical ids); this rank's experts only; their
+            // weighted sum goes out as exchange `layer`, received by the next layer
+            float* xl = (float*)mf_ptr(rs.xb[layer_ & 1]);
+            check(mf_router_topk(ids, w, (float*)mf_ptr(rs.scores), xl, (const float*)mf_ptr(fn_), c_.rms_norm_eps,
+                                 (const float*)mf_ptr(wr_), d, c_.n_experts, k, rs.stream),
+                  "router");
+            check(mf_moe_swiglu_ep(h, xl, (const float*)mf_ptr(fn_), c_.rms_norm_eps, mf_ptr(wgu_), dtype_, ids, k, F,
+                                   d, c_.expert_lo(), c_.experts_local(), rs.stream),
+                  "expert gate/up (local experts)");
+            check(mf_moe_down_push(h, mf_ptr(wd_), dtype_, ids, w, k, d, F, c_.expert_lo(), c_.experts_local(),
+                                   rs.comm, layer_, rs.d_step, rs.stream),
+                  "expert down (all-reduce send)");
+            return;
+        }
         check(mf_router_topk(ids, w, (float*)mf_ptr(rs.scores), x, (const float*)mf_ptr(fn_), c_.rms_norm_eps,
                              (const float*)mf_ptr(wr_), d, c_.n_experts, k, rs.stream),
               "router");
@@ -369,13 +398,17 @@ public:
     void cuda_forward(RunState& rs) override {
         if (!rs.compute_logits) return;
         if (c_.tp_size > 1) {
-            // receive the last down-projection all-reduce; greedy id agreed
-            // over ranks; full logits gathered when the host wants them
-            check(mf_allreduce_lm_head((float*)mf_ptr(rs.logits), (const float*)mf_ptr(rs.xb[1]),
-                                       (float*)mf_ptr(rs.xb[0]), (const float*)mf_ptr(on_), c_.rms_norm_eps,
-                                       (const char*)mf_ptr(w_) + w_off_, dtype_, (int)c_.vocab_local(), c_.d_model,
-                                       (int)c_.vocab_offset(), rs.d_step, mf_ptr(rs.lmh_ws), rs.host_logits ? 1 : 0,
-                                       rs.comm, 2 * c_.n_layers - 1, rs.stream),
+            // receive the last all-reduce (the last layer's down projection or
+            // experts); greedy id agreed over ranks; full logits gathered when
+            // the host wants them
+            const int L = c_.n_layers;
+            const int seq = c_.ep() ? L - 1 : 2 * L - 1;
+            mf_buf* res = c_.ep() ? rs.xb[(L - 1) & 1] : rs.xb[1];
+            mf_buf* out = c_.ep() ? rs.xb[L & 1] : rs.xb[0];
+            check(mf_allreduce_lm_head((float*)mf_ptr(rs.logits), (const float*)mf_ptr(res), (float*)mf_ptr(out),
+                                       (const float*)mf_ptr(on_), c_.rms_norm_eps, (const char*)mf_ptr(w_) + w_off_,
+                                       dtype_, (int)c_.vocab_local(), c_.d_model, (int)c_.vocab_offset(), rs.d_step,
+                                       mf_ptr(rs.lmh_ws), rs.host_logits ? 1 : 0, rs.comm, seq, rs.stream),
                   "lm_head (all-reduce)");
             return;
         }
@@ -467,10 +500,13 @@ Qwen3Model::Qwen3Model(const std::string& path, const RunParams& rp, int rank, i
     cfg_ = Config::from_gguf(file_, rp);
     if (tp_size < 1 || tp_size > MF_TP_MAX || tp_rank < 0 || tp_rank >= tp_size)
         throw std::invalid_argument("tp_rank/tp_size out of range");
-    if (tp_size > 1) {
+    if (tp_size > 1 && cfg_.n_experts > 0) {
+        if (cfg_.n_experts % tp_size != 0)
+            throw std::invalid_argument("expert_count is not divisible by the expert-parallel size");
+        if (cfg_.n_layers > 255) throw std::invalid_argument("expert parallelism supports up to 255 layers");
+    } else if (tp_size > 1) {
         if (cfg_.n_kv_heads % tp_size != 0)
             throw std::invalid_argument("n_kv_heads is not divisible by the tensor-parallel size");
-        if (cfg_.n_experts > 0) throw std::invalid_argument("tensor parallelism covers dense FFN models");
         if (cfg_.d_ff % tp_size != 0) throw std::invalid_argument("d_ff is not divisible by the tensor-parallel size");
         if (2 * cfg_.n_layers > 255) throw std::invalid_argument("tensor parallelism supports up to 127 layers");
     }

@@ -53,9 +53,15 @@ struct Config {
     // tensor parallelism: this process holds rank tp_rank of tp_size
     int tp_rank = 0, tp_size = 1;
 
-    int heads_local() const { return n_heads / tp_size; }
-    int kv_heads_local() const { return n_kv_heads / tp_size; }
-    int ff_local() const { return d_ff / tp_size; }
+    // MoE models split their experts over the ranks (expert parallelism) and
+    // replicate attention; dense models split attention and FFN (tensor parallelism)
+    bool ep() const { return tp_size > 1 && n_experts > 0; }
+    bool attn_split() const { return tp_size > 1 && n_experts == 0; }
+    int heads_local() const { return attn_split() ? n_heads / tp_size : n_heads; }
+    int kv_heads_local() const { return attn_split() ? n_kv_heads / tp_size : n_kv_heads; }
+    int ff_local() const { return attn_split() ? d_ff / tp_size : d_ff; }
+    int experts_local() const { return ep() ? n_experts / tp_size : n_experts; }
+    int expert_lo() const { return ep() ? tp_rank * experts_local() : 0; }
     // vocabulary rows [vocab_offset(), vocab_offset() + vocab_local()) of the lm_head
     size_t vocab_local() const { return vocab_size / tp_size + ((size_t)tp_rank < vocab_size % tp_size ? 1 : 0); }
     size_t vocab_offset() const {

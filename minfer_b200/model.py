@@ -180,7 +180,9 @@ class Qwen3Model:
         return ids, w
 
     def kv(self, layer: int, n_pos: int):
-        n = n_pos * (self.info.n_kv_heads // self.info.tp_size) * self.info.d_head
+        # tensor parallelism splits the KV heads; expert parallelism (MoE) keeps them all
+        kvh = self.info.n_kv_heads if self.info.n_experts > 0 else self.info.n_kv_heads // self.info.tp_size
+        n = n_pos * kvh * self.info.d_head
         k = np.zeros(n, dtype=np.float32)
         v = np.zeros(n, dtype=np.float32)
         check(self._lib.mf_model_kv(self._h, layer, k.ctypes.data, v.ctypes.data, n_pos))

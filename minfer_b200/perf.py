@@ -118,6 +118,37 @@ def gemm(args) -> dict:
             "tflops": round(flops / us / 1e6, 1), "tensor_tflops": round(2 * flops / us / 1e6, 1)}
 
 
+def moe(args) -> dict:
+    """One MoE layer's expert path at batch 1: router + top-k, grouped gate/up +
+    SiLU over the k selected experts, grouped down + weighted residual. The
+    expert weights of `--copies` layers rotate so each launch streams from HBM."""
+    from . import ops
+
+    E, k, F, d = args.experts, args.k_active, args.ff, args.d
+    g = torch.Generator(device="cuda").manual_seed(0)
+    wr = torch.randn(E, d, generator=g, device="cuda") * 0.02
+    wgus = [(torch.randn(E * 2 * F, d, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+            for _ in range(args.copies)]
+    wds = [(torch.randn(E * d, F, generator=g, device="cuda") * 0.02).to(torch.bfloat16) for _ in range(args.copies)]
+    x = torch.randn(d, generator=g, device="cuda")
+    nw = torch.ones(d, device="cuda")
+    ids = torch.zeros(k, dtype=torch.int32, device="cuda")
+    w = torch.zeros(k, device="cuda")
+    scores = torch.zeros(E, device="cuda")
+    h = torch.zeros(k * F, device="cuda")
+    res = {}
+    res["router_us"] = round(_time(lambda i: ops.router_topk(ids, w, scores, x, nw, 1e-6, wr, d, E, k), args.iters,
+                                   args.warmup), 2)
+    res["gate_up_us"] = round(_time(lambda i: ops.moe_swiglu(h, x, nw, 1e-6, wgus[i % len(wgus)], ids, k, F, d),
+                                    args.iters, args.warmup), 2)
+    res["down_us"] = round(_time(lambda i: ops.moe_down_residual(x, h, wds[i % len(wds)], ids, w, k, d, F),
+                                 args.iters, args.warmup), 2)
+    gu_bytes, dn_bytes = k * 2 * F * d * 2, k * d * F * 2
+    res.update(op="moe-layer", experts=E, k=k, ff=F, d=d, gate_up_gbs=round(gu_bytes / res["gate_up_us"] / 1e3, 1),
+               down_gbs=round(dn_bytes / res["down_us"] / 1e3, 1), router_bytes=E * d * 4)
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -136,13 +167,18 @@ def main():
     c.add_argument("--n", type=int, default=24576)
     c.add_argument("--k", type=int, default=4096)
     c.add_argument("--mode", default="swiglu", choices=["store", "resid", "swiglu"])
-    for p in (a, b, c):
+    e = sub.add_parser("moe")
+    e.add_argument("--experts", type=int, default=128)
+    e.add_argument("--k-active", type=int, default=8)
+    e.add_argument("--ff", type=int, default=768)
+    e.add_argument("--d", type=int, default=2048)
+    for p in (a, b, c, e):
         p.add_argument("--iters", type=int, default=20)
         p.add_argument("--warmup", type=int, default=5)
         p.add_argument("--copies", type=int, default=2)
     args = ap.parse_args()
     mm.init(1, [torch.cuda.current_device()])
-    res = {"gemv": gemv, "attn": attn, "gemm": gemm}[args.what](args)
+    res = {"gemv": gemv, "attn": attn, "gemm": gemm, "moe": moe}[args.what](args)
     print(json.dumps(res), flush=True)
 
 

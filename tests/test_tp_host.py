@@ -100,7 +100,13 @@ def test_shard_load_splits(size):
     m = C.c_void_p()
     rc = host_lib().mf_model_load_tp(tiny_model("tiny-bf16").encode(), C.byref(rp), 0, 0, 4, C.byref(m))
     assert rc != MF_OK and "n_kv_heads" in last_error()
-    rc = host_lib().mf_model_load_tp(tiny_model("tiny-moe").encode(), C.byref(rp), 0, 0, 2, C.byref(m))
-    assert rc != MF_OK and "dense" in last_error()
+    # the MoE model splits its 16 experts instead (expert parallelism): 2 ranks load, 3 do not divide
+    rc = host_lib().mf_model_load_tp(tiny_model("tiny-moe").encode(), C.byref(rp), 0, 1, 2, C.byref(m))
+    assert rc == MF_OK, last_error()
+    info = mf_model_info()
+    assert host_lib().mf_model_info_get(m, C.byref(info)) == MF_OK and (info.tp_rank, info.tp_size) == (1, 2)
+    host_lib().mf_model_free(m)
+    rc = host_lib().mf_model_load_tp(tiny_model("tiny-moe").encode(), C.byref(rp), 0, 0, 3, C.byref(m))
+    assert rc != MF_OK and "expert_count" in last_error()
     rc = host_lib().mf_model_load_tp(tiny_model("tiny-bf16").encode(), C.byref(rp), 0, 2, 2, C.byref(m))
     assert rc != MF_OK

@@ -105,6 +105,20 @@ def check_model(name, rank, world):
         m.forward(int(t), i, i == P - 1, i == P - 1)
     err = np.max(np.abs(orc0.logits() - m.logits()))
     assert err <= logit_tol(cfg.dtype), f"{name}: step-0 logits max-abs {err}"
+    if cfg.n_experts > 0:
+        # the router runs on every rank: every rank's expert ids per layer match the oracle's
+        orc_e = PortModel(path, max_seq=P + 1)
+        orc_e.record_experts(True)
+        me = load()
+        for i, t in enumerate(prompt):
+            orc_e.forward(int(t), i, True)
+            me.forward(int(t), i, True, False)
+            ref_e, _ = orc_e.recorded_experts(cfg.n_active)
+            for layer in range(cfg.n_layers):
+                ids, _ = me.experts(layer)
+                assert list(ids) == list(ref_e[i * cfg.n_layers + layer]), f"{name}: experts differ at {i}/{layer}"
+        assert me.comm_status() == 0
+        me.close()
     assert m.argmax() == int(np.argmax(m.logits()))
     # teacher-forced greedy
     ids, mg, st = m.generate(prompt, G, forced=ref_ids, margins=True)
@@ -148,8 +162,10 @@ def main():
     torch.cuda.set_device(local)
     mm.init(1, [local])
     device = torch.device("cuda", local)
-    names = [n for n in TINY if TINY[n].n_experts == 0 and TINY[n].n_kv_heads % world == 0
-             and TINY[n].d_ff % world == 0]
+    # dense models split attention and FFN (tensor parallelism); MoE models split their experts
+    names = [n for n in TINY if (TINY[n].n_experts == 0 and TINY[n].n_kv_heads % world == 0
+                                 and TINY[n].d_ff % world == 0) or
+             (TINY[n].n_experts > 0 and TINY[n].n_experts % world == 0)]
     if rank == 0:
         for n in names:
             tiny_model(n)  # create the files once
