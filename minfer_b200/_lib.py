@@ -147,6 +147,8 @@ CUDA_API = {
     "mf_prefill_embed": (I, [P, P, I, I, I, P, I, P]),
     "mf_prefill_qkv_post": (I, [P, P, P, P, P, P, F, P, I, I, I, I, I, I, P]),
     "mf_prefill_attention": (I, [P, P, P, P, P, I, I, I, I, I, I, P]),
+    "mf_prefill_attention_scratch": (I, [I, I, I, I, P]),
+    "mf_prefill_attention_tc": (I, [P, P, P, P, P, I, I, I, I, I, I, P, SZ, P]),
     "mf_prefill_status": (I, [P, I]),
     "mf_matmul": (I, [P, P, P, I, SZ, I, I, P]),
     "mf_rmsnorm": (I, [P, P, P, I, F, I, P]),

@@ -222,8 +222,14 @@ public:
                                   (const float*)mf_ptr(qn_), (const float*)mf_ptr(kn_), c_.rms_norm_eps,
                                   mf_ptr(rs.rope), S, H, Hkv, D, n, pos0, rs.stream),
               "prefill q/k norm, rope, kv");
-        check(mf_prefill_attention(hi, lo, (const float*)mf_ptr(rs.pf_q), kc, vc, S, n, pos0, H, Hkv, D, rs.stream),
-              "prefill attention");
+        if (rs.pf_simt_attn)
+            check(mf_prefill_attention(hi, lo, (const float*)mf_ptr(rs.pf_q), kc, vc, S, n, pos0, H, Hkv, D,
+                                       rs.stream),
+                  "prefill attention");
+        else
+            check(mf_prefill_attention_tc(hi, lo, (const float*)mf_ptr(rs.pf_q), kc, vc, S, n, pos0, H, Hkv, D,
+                                          mf_ptr(rs.pf_att), rs.pf_att_bytes, rs.stream),
+                  "prefill attention");
         check(mf_prefill_gemm(X, d, hi, lo, mf_ptr(wo_), n, d, H * D, MF_PREFILL_RESID, nullptr, nullptr, rs.stream),
               "prefill output projection");
     }
@@ -635,7 +641,8 @@ bool Qwen3Model::prefill_supported() const {
 void Qwen3Model::alloc_prefill(int rows) {
     if (rs_.pf_cap >= rows) return;
     RunState& rs = rs_;
-    for (mf_buf** b : {&rs.pf_x, &rs.pf_hi, &rs.pf_lo, &rs.pf_hhi, &rs.pf_hlo, &rs.pf_qkv, &rs.pf_q, &rs.pf_tok}) {
+    for (mf_buf** b :
+         {&rs.pf_x, &rs.pf_hi, &rs.pf_lo, &rs.pf_hhi, &rs.pf_hlo, &rs.pf_qkv, &rs.pf_q, &rs.pf_tok, &rs.pf_att}) {
         if (*b) {
             state_bufs_.erase(std::find(state_bufs_.begin(), state_bufs_.end(), *b));
             mf_release(*b);
@@ -659,6 +666,15 @@ void Qwen3Model::alloc_prefill(int rows) {
     rs.pf_qkv = alloc(R * (qd + 2ull * c.n_kv_heads * c.d_head) * 4, "prefill qkv");
     rs.pf_q = alloc(R * qd * 4, "prefill queries");
     rs.pf_tok = alloc(R * 4, "prefill token ids");
+    const char* se = std::getenv("MF_PREFILL_SIMT_ATTN");
+    rs.pf_simt_attn = se && se[0] == '1';
+    if (!rs.pf_simt_attn) {
+        // sized for the longest history: keys up to max_seq_len
+        check(mf_prefill_attention_scratch(rows, (int)c.user_max_seq_len, c.n_heads, c.n_kv_heads,
+                                           &rs.pf_att_bytes),
+              "prefill attention scratch size");
+        rs.pf_att = alloc(rs.pf_att_bytes, "prefill attention operands");
+    }
     rs.pf_cap = rows;
 }
 
@@ -683,7 +699,7 @@ bool Qwen3Model::prefill(const uint32_t* tokens, int n, int pos0, bool compute_l
     }
     int st = 0;
     check(mf_prefill_status(&st, 1), "prefill status");
-    if (st) throw std::runtime_error("a prefill GEMM wait gave up (status " + std::to_string(st) + ")");
+    if (st) throw std::runtime_error("a prefill kernel wait gave up (status " + std::to_string(st) + ")");
     // the last token's residual row feeds the decode lm_head
     check(mf_copy(rs_.x, 0, rs_.pf_x, (size_t)(last_rows - 1) * cfg_.d_model * 4, (size_t)cfg_.d_model * 4),
           "prefill last row");

@@ -111,6 +111,9 @@ struct RunState {
     int pf_cap = 0;  // rows per chunk
     mf_buf *pf_x = nullptr, *pf_hi = nullptr, *pf_lo = nullptr, *pf_hhi = nullptr, *pf_hlo = nullptr;
     mf_buf *pf_qkv = nullptr, *pf_q = nullptr, *pf_tok = nullptr;
+    mf_buf* pf_att = nullptr;  // tensor-core attention operands (bf16 hi/lo Q, K, V^T)
+    size_t pf_att_bytes = 0;
+    bool pf_simt_attn = false;  // MF_PREFILL_SIMT_ATTN=1: the SIMT attention kernel instead
 };
 
 class BaseLayer {

@@ -13,6 +13,7 @@
 
 #include "minfer_cuda.h"
 #include "prefill_attn.cuh"
+#include "prefill_fa.cuh"
 #include "prefill_gemm.cuh"
 
 namespace mf {
@@ -60,16 +61,13 @@ int set_smem(const void* fn, size_t smem) {
     return e == cudaSuccess ? MF_OK : fail(MF_E_CUDA, cudaGetErrorString(e));
 }
 
-// 2-D bf16 tensor map over a row-major [rows, cols] matrix: 64-column
-// (128-byte) x box_rows boxes, 128-byte swizzle, zero fill out of bounds.
-int make_tmap(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
-    if (((uintptr_t)base & 15) != 0 || (cols * 2) % 16 != 0)
-        return fail(MF_E_INVALID, "bf16 operand must be 16-byte aligned with a row length multiple of 8");
-    // the driver entry point is looked up at run time, so the library loads
-    // (and its CPU-side checks run) on machines without a driver
-    using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// The driver entry point is looked up at run time, so the library loads (and
+// its CPU-side checks run) on machines without a driver.
+EncodeFn tmap_encoder() {
     static EncodeFn encode = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
@@ -79,15 +77,39 @@ int make_tmap(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, u
             q == cudaDriverEntryPointSuccess)
             encode = (EncodeFn)fn;
     });
+    return encode;
+}
+
+// bf16 tensor map of rank 2 or 3 (dims[0] innermost, strides in bytes of
+// dims 1..rank-1), 128-byte swizzle, zero fill out of bounds. The box's inner
+// extent is 64 elements (128 bytes).
+int make_tmap_nd(CUtensorMap* tm, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                 const uint32_t* box) {
+    if (((uintptr_t)base & 15) != 0) return fail(MF_E_INVALID, "bf16 operand must be 16-byte aligned");
+    for (int i = 0; i + 1 < rank; ++i)
+        if (strides[i] % 16 != 0) return fail(MF_E_INVALID, "bf16 operand strides must be multiples of 16 bytes");
+    EncodeFn encode = tmap_encoder();
     if (!encode) return fail(MF_E_CUDA, "cuTensorMapEncodeTiled is not available");
-    cuuint64_t dims[2] = {cols, rows};
-    cuuint64_t strides[1] = {cols * 2};
-    cuuint32_t box[2] = {64, box_rows};
-    cuuint32_t es[2] = {1, 1};
-    CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    cuuint64_t d[3], st[2];
+    cuuint32_t bx[3], es[3] = {1, 1, 1};
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        bx[i] = box[i];
+    }
+    for (int i = 0; i + 1 < rank; ++i) st[i] = strides[i];
+    CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx,
+                        es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? MF_OK : fail(MF_E_CUDA, "cuTensorMapEncodeTiled failed");
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix: 64-column
+// (128-byte) x box_rows boxes.
+int make_tmap(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    if ((cols * 2) % 16 != 0) return fail(MF_E_INVALID, "bf16 operand row length must be a multiple of 8");
+    const uint64_t dims[2] = {cols, rows}, strides[1] = {cols * 2};
+    const uint32_t box[2] = {64, box_rows};
+    return make_tmap_nd(tm, base, 2, dims, strides, box);
 }
 
 int* status_ptr() {
@@ -272,6 +294,116 @@ int mf_prefill_attention(void* out_hi, void* out_lo, const float* q, const float
                     (void*)&n_heads, (void*)&hi, (void*)&lo};
     cudaError_t e = launch(fn, dim3((n_tokens + QT - 1) / QT, n_kv_heads), dim3(mf::PA_THREADS), smem,
                            mf::resolve_stream(stream), args);
+    return e == cudaSuccess ? MF_OK : fail(MF_E_CUDA, cudaGetErrorString(e));
+}
+
+// Scratch of mf_prefill_attention_tc: Q hi/lo [Hkv][P*G][128], K hi/lo
+// [Hkv][ld][128], V^T hi/lo [Hkv][128][ld], ld = n_keys rounded up to 64,
+// each section 256-byte aligned.
+static size_t fa_layout(int n_tokens, int n_keys, int n_heads, int n_kv_heads, size_t off[6]) {
+    const size_t ld = ((size_t)n_keys + 63) / 64 * 64;
+    const size_t q = (size_t)n_tokens * n_heads * mf::ATT_D * 2, kv = (size_t)n_kv_heads * ld * mf::ATT_D * 2;
+    const size_t sz[6] = {q, q, kv, kv, kv, kv};
+    size_t o = 0;
+    for (int i = 0; i < 6; ++i) {
+        off[i] = o;
+        o += (sz[i] + 255) / 256 * 256;
+    }
+    return o;
+}
+
+int mf_prefill_attention_scratch(int n_tokens, int n_keys, int n_heads, int n_kv_heads, size_t* bytes) {
+    if (!bytes || n_tokens <= 0 || n_keys < n_tokens || n_heads <= 0 || n_kv_heads <= 0)
+        return fail(MF_E_INVALID, "bad arguments");
+    size_t off[6];
+    *bytes = fa_layout(n_tokens, n_keys, n_heads, n_kv_heads, off);
+    return MF_OK;
+}
+
+int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const float* k_cache, const float* v_cache,
+                            int max_seq, int n_tokens, int pos0, int n_heads, int n_kv_heads, int d_head,
+                            void* scratch, size_t scratch_bytes, void* stream) {
+    if (!out_hi || !out_lo || !q || !k_cache || !v_cache || !scratch || n_tokens <= 0 || pos0 < 0 ||
+        n_kv_heads <= 0 || n_heads % n_kv_heads != 0)
+        return fail(MF_E_INVALID, "bad arguments");
+    if (d_head != mf::ATT_D) return fail(MF_E_UNSUPPORTED, "d_head must be 128");
+    if (pos0 + n_tokens > max_seq) return fail(MF_E_INVALID, "prompt runs past max_seq");
+    if (((uintptr_t)scratch & 255) != 0) return fail(MF_E_INVALID, "scratch must be 256-byte aligned");
+    const int G = n_heads / n_kv_heads;
+    const void* fn = G == 1    ? (const void*)&mf::prefill_fa_kernel<1>
+                     : G == 2  ? (const void*)&mf::prefill_fa_kernel<2>
+                     : G == 4  ? (const void*)&mf::prefill_fa_kernel<4>
+                     : G == 8  ? (const void*)&mf::prefill_fa_kernel<8>
+                     : G == 16 ? (const void*)&mf::prefill_fa_kernel<16>
+                               : nullptr;
+    if (!fn) return fail(MF_E_UNSUPPORTED, "query heads per KV head must be 1, 2, 4, 8 or 16");
+    const int n_keys = pos0 + n_tokens;
+    size_t off[6];
+    if (fa_layout(n_tokens, n_keys, n_heads, n_kv_heads, off) > scratch_bytes)
+        return fail(MF_E_INVALID, "attention scratch too small");
+    const size_t ld = ((size_t)n_keys + 63) / 64 * 64;
+    uint8_t* base = (uint8_t*)scratch;
+    __nv_bfloat16 *qh = (__nv_bfloat16*)(base + off[0]), *ql = (__nv_bfloat16*)(base + off[1]);
+    __nv_bfloat16 *kh = (__nv_bfloat16*)(base + off[2]), *kl = (__nv_bfloat16*)(base + off[3]);
+    __nv_bfloat16 *vh = (__nv_bfloat16*)(base + off[4]), *vl = (__nv_bfloat16*)(base + off[5]);
+    CUtensorMap tq[2], tk[2], tv[2];
+    const uint64_t D = mf::ATT_D;
+    {
+        const uint64_t dims[2] = {D, (uint64_t)n_tokens * n_heads}, strides[1] = {D * 2};
+        const uint32_t box[2] = {64, mf::FA_BM};
+        int rc = make_tmap_nd(&tq[0], qh, 2, dims, strides, box);
+        if (!rc) rc = make_tmap_nd(&tq[1], ql, 2, dims, strides, box);
+        if (rc) return rc;
+    }
+    {
+        const uint64_t dims[3] = {D, (uint64_t)n_keys, (uint64_t)n_kv_heads}, strides[2] = {D * 2, ld * D * 2};
+        const uint32_t box[3] = {64, mf::FA_BN, 1};
+        int rc = make_tmap_nd(&tk[0], kh, 3, dims, strides, box);
+        if (!rc) rc = make_tmap_nd(&tk[1], kl, 3, dims, strides, box);
+        if (rc) return rc;
+    }
+    {
+        const uint64_t dims[3] = {(uint64_t)n_keys, D, (uint64_t)n_kv_heads}, strides[2] = {ld * 2, D * ld * 2};
+        const uint32_t box[3] = {64, (uint32_t)D, 1};
+        int rc = make_tmap_nd(&tv[0], vh, 3, dims, strides, box);
+        if (!rc) rc = make_tmap_nd(&tv[1], vl, 3, dims, strides, box);
+        if (rc) return rc;
+    }
+    int rc = set_smem(fn, mf::FA_SMEM_BYTES);
+    if (rc) return rc;
+    int* status = status_ptr();
+    if (!status) return fail(MF_E_CUDA, "prefill status symbol");
+    cudaStream_t st = mf::resolve_stream(stream);
+    // operands: Q and K rows split (one warp per 128-float row), V transposed in 64-key tiles
+    const int ldi = (int)ld;
+    {
+        const long long rows = (long long)n_tokens * n_heads + (long long)n_kv_heads * n_keys;
+        const int blocks = (int)std::min<long long>((rows + 7) / 8, 148LL * 16);
+        void* args[] = {(void*)&q, (void*)&k_cache, (void*)&n_tokens, (void*)&n_heads, (void*)&n_kv_heads,
+                        (void*)&max_seq, (void*)&n_keys, (void*)&ldi, (void*)&qh, (void*)&ql, (void*)&kh, (void*)&kl};
+        cudaError_t e = launch((const void*)&mf::fa_qk_split_kernel, dim3(blocks), dim3(256), 0, st, args);
+        if (e != cudaSuccess) return fail(MF_E_CUDA, cudaGetErrorString(e));
+    }
+    {
+        void* args[] = {(void*)&v_cache, (void*)&max_seq, (void*)&n_keys, (void*)&ldi, (void*)&vh, (void*)&vl};
+        cudaError_t e = launch((const void*)&mf::fa_v_split_kernel, dim3((n_keys + 63) / 64, n_kv_heads), dim3(256),
+                               0, st, args);
+        if (e != cudaSuccess) return fail(MF_E_CUDA, cudaGetErrorString(e));
+    }
+    mf::FaParams p;
+    p.P = n_tokens;
+    p.pos0 = pos0;
+    p.n_heads = n_heads;
+    p.n_keys_max = n_keys;
+    p.out_hi = (__nv_bfloat16*)out_hi;
+    p.out_lo = (__nv_bfloat16*)out_lo;
+    p.status = status;
+    p.timeout_ns = timeout_ns();
+    const int QT = mf::FA_BM / G;
+    void* args[] = {(void*)&tq[0], (void*)&tq[1], (void*)&tk[0], (void*)&tk[1], (void*)&tv[0], (void*)&tv[1],
+                    (void*)&p};
+    cudaError_t e = launch(fn, dim3((n_tokens + QT - 1) / QT, n_kv_heads), dim3(mf::FA_THREADS),
+                           mf::FA_SMEM_BYTES, st, args);
     return e == cudaSuccess ? MF_OK : fail(MF_E_CUDA, cudaGetErrorString(e));
 }
 

@@ -3,6 +3,7 @@
     python -m minfer_b200.perf gemv --rows 24576 --k 4096 --mode swiglu
     python -m minfer_b200.perf attn --hq 32 --hkv 8 --ctx 4096
     python -m minfer_b200.perf gemm --m 4096 --n 24576 --k 4096 --mode swiglu
+    python -m minfer_b200.perf pattn --p 4096 --pos0 0 --hq 32 --hkv 8 --kernel tc
 
 Prints one JSON line per case: average device time per launch (CUDA events
 around a CUDA-graph replay of `--iters` launches on torch's stream, after
@@ -118,6 +119,42 @@ def gemm(args) -> dict:
             "tflops": round(flops / us / 1e6, 1), "tensor_tflops": round(2 * flops / us / 1e6, 1)}
 
 
+def pattn(args) -> dict:
+    """Batched-prefill causal attention of P tokens after pos0 cached positions:
+    the tensor-core kernel (operand split included) or the SIMT kernel."""
+    import ctypes as C
+
+    from . import ops
+    from ._lib import check, cuda_lib
+
+    lib = cuda_lib()
+    Pn, pos0, Hq, Hkv, D = args.p, args.pos0, args.hq, args.hkv, 128
+    S = pos0 + Pn
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(Pn, Hq * D, generator=g, device="cuda")
+    kc = torch.randn(Hkv, S, D, generator=g, device="cuda")
+    vc = torch.randn(Hkv, S, D, generator=g, device="cuda")
+    hi = torch.empty(Pn, Hq * D, dtype=torch.bfloat16, device="cuda")
+    lo = torch.empty_like(hi)
+    need = C.c_size_t()
+    check(lib.mf_prefill_attention_scratch(Pn, S, Hq, Hkv, C.byref(need)))
+    scratch = torch.empty(need.value, dtype=torch.uint8, device="cuda")
+    P = lambda t: C.c_void_p(t.data_ptr())
+    if args.kernel == "tc":
+        fn = lambda i: check(lib.mf_prefill_attention_tc(P(hi), P(lo), P(q), P(kc), P(vc), S, Pn, pos0, Hq, Hkv, D,
+                                                         P(scratch), need.value, C.c_void_p(ops._stream())))
+    else:
+        fn = lambda i: check(lib.mf_prefill_attention(P(hi), P(lo), P(q), P(kc), P(vc), S, Pn, pos0, Hq, Hkv, D,
+                                                      C.c_void_p(ops._stream())))
+    us = _time(fn, args.iters, args.warmup)
+    st = C.c_int()
+    check(lib.mf_prefill_status(C.byref(st), 1))
+    # causal: token t attends to pos0 + t + 1 keys; 2 flops per multiply-add, QK^T and PV
+    flops = 4.0 * Hq * D * (Pn * pos0 + Pn * (Pn + 1) / 2)
+    return {"op": f"prefill-attn-{args.kernel}", "p": Pn, "pos0": pos0, "hq": Hq, "hkv": Hkv, "us": round(us, 2),
+            "tflops": round(flops / us / 1e6, 1), "status": st.value}
+
+
 def moe(args) -> dict:
     """One MoE layer's expert path at batch 1: router + top-k, grouped gate/up +
     SiLU over the k selected experts, grouped down + weighted residual. The
@@ -167,18 +204,24 @@ def main():
     c.add_argument("--n", type=int, default=24576)
     c.add_argument("--k", type=int, default=4096)
     c.add_argument("--mode", default="swiglu", choices=["store", "resid", "swiglu"])
+    f = sub.add_parser("pattn")
+    f.add_argument("--p", type=int, default=4096)
+    f.add_argument("--pos0", type=int, default=0)
+    f.add_argument("--hq", type=int, default=32)
+    f.add_argument("--hkv", type=int, default=8)
+    f.add_argument("--kernel", default="tc", choices=["tc", "simt"])
     e = sub.add_parser("moe")
     e.add_argument("--experts", type=int, default=128)
     e.add_argument("--k-active", type=int, default=8)
     e.add_argument("--ff", type=int, default=768)
     e.add_argument("--d", type=int, default=2048)
-    for p in (a, b, c, e):
+    for p in (a, b, c, e, f):
         p.add_argument("--iters", type=int, default=20)
         p.add_argument("--warmup", type=int, default=5)
         p.add_argument("--copies", type=int, default=2)
     args = ap.parse_args()
     mm.init(1, [torch.cuda.current_device()])
-    res = {"gemv": gemv, "attn": attn, "gemm": gemm, "moe": moe}[args.what](args)
+    res = {"gemv": gemv, "attn": attn, "gemm": gemm, "moe": moe, "pattn": pattn}[args.what](args)
     print(json.dumps(res), flush=True)
 
 

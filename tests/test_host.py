@@ -162,4 +162,18 @@ def test_ops_validate_before_touching_the_device():
     assert lib.mf_rmsnorm(None, None, None, 0, 1e-6, 1, None) == MF_E_INVALID
     assert lib.mf_attn_decode(None, None) == MF_E_INVALID
     assert lib.mf_attn_decode_noalloc(None, None) == MF_E_INVALID
+    # tensor-core prefill attention: scratch size and alignment are checked before any device call
+    need = C.c_size_t()
+    assert lib.mf_prefill_attention_scratch(100, 140, 32, 8, C.byref(need)) == MF_OK
+    ld = 192  # 140 keys rounded up to 64
+    assert need.value == 2 * 100 * 32 * 128 * 2 + 4 * 8 * ld * 128 * 2
+    assert lib.mf_prefill_attention_scratch(100, 99, 32, 8, C.byref(need)) == MF_E_INVALID
+    fake = C.c_void_p(1 << 20)
+    args = (fake, fake, fake, fake, fake, 256, 100, 40, 32, 8, 128)  # 40 + 100 = 140 keys
+    assert lib.mf_prefill_attention_tc(*args, fake, need.value - 1, None) == MF_E_INVALID
+    msg = C.create_string_buffer(256)
+    lib.mf_last_error(msg, 256)
+    assert b"scratch too small" in msg.value
+    assert lib.mf_prefill_attention_tc(*args, C.c_void_p((1 << 20) + 16), need.value, None) == MF_E_INVALID
+    assert lib.mf_prefill_attention_tc(*args[:6], 300, *args[7:], fake, need.value, None) == MF_E_INVALID
     assert lib.mf_lm_head(None, None, None, 1e-6, None, 2, 10, 16, 0, None, None, None) == MF_E_INVALID
