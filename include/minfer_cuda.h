@@ -347,17 +347,19 @@ int mf_prefill_qkv_post(float* q_out, float* k_cache, float* v_cache, const floa
  * [0, pos0 + t]), written as bf16 hi/lo [n_tokens][Hq * d_head]. */
 int mf_prefill_attention(void* out_hi, void* out_lo, const float* q, const float* k_cache, const float* v_cache,
                          int max_seq, int n_tokens, int pos0, int n_heads, int n_kv_heads, int d_head, void* stream);
-/* The same attention on the tensor cores (tcgen05): S = Q K^T and O += P V
- * with bf16 hi/lo operands (three products each, ~fp32 accuracy) in TMEM,
- * online softmax per query row. Needs device scratch of at least
+/* The same attention on the tensor cores (tcgen05): S = Q K^T with fp16 hi/lo
+ * operands and O += P V with bf16 hi/lo operands (three products each) in
+ * TMEM, online softmax per query row. Needs device scratch of at least
  * mf_prefill_attention_scratch(n_tokens, pos0 + n_tokens, ...) bytes,
- * 256-byte aligned. A wait that gives up sets status bit 2. */
+ * 256-byte aligned. A wait that gives up sets status bit 2; a q or k value
+ * outside the fp16 range (|x| >= 65504, or not finite) sets status bit 4. */
 int mf_prefill_attention_scratch(int n_tokens, int n_keys, int n_heads, int n_kv_heads, size_t* bytes);
 int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const float* k_cache, const float* v_cache,
                             int max_seq, int n_tokens, int pos0, int n_heads, int n_kv_heads, int d_head,
                             void* scratch, size_t scratch_bytes, void* stream);
-/* Status bits of the prefill kernels' bounded waits since the last clear
- * (1: GEMM, 2: tensor-core attention; synchronises the device). */
+/* Status bits of the prefill kernels since the last clear (1: a GEMM wait
+ * gave up, 2: an attention wait gave up, 4: attention q/k outside the fp16
+ * range; synchronises the device). */
 int mf_prefill_status(int* status, int clear);
 
 /* ===================================================================== */

@@ -152,6 +152,12 @@ public:
         own(qn_ = upload_tensor(qn, rank));
         own(kn_ = upload_tensor(kn, rank));
         own(an_ = upload_tensor(an, rank));
+        // normalised, rotated q/k elements are bounded by sqrt(2 * d_head) * max|norm weight|; the
+        // tensor-core prefill attention carries them as fp16 hi/lo, so it needs that bound below 65504
+        float wmax = 0.f;
+        for (const TensorView* tv : {&qn, &kn})
+            for (size_t i = 0; i < tv->numel; ++i) wmax = std::max(wmax, std::fabs(((const float*)tv->data)[i]));
+        tc_attn_ok_ = std::sqrt(2.0f * (float)c_.d_head) * wmax < 60000.f;
         read_bytes_ = (ql + 2 * kvl) * rowb + d * ql * esz + qn.bytes + kn.bytes + an.bytes;
         if (c_.ep()) read_bytes_ /= c_.tp_size;  // replicated: each rank counts its share
     }
@@ -222,7 +228,7 @@ public:
                                   (const float*)mf_ptr(qn_), (const float*)mf_ptr(kn_), c_.rms_norm_eps,
                                   mf_ptr(rs.rope), S, H, Hkv, D, n, pos0, rs.stream),
               "prefill q/k norm, rope, kv");
-        if (rs.pf_simt_attn)
+        if (rs.pf_simt_attn || !tc_attn_ok_)
             check(mf_prefill_attention(hi, lo, (const float*)mf_ptr(rs.pf_q), kc, vc, S, n, pos0, H, Hkv, D,
                                        rs.stream),
                   "prefill attention");
@@ -239,6 +245,7 @@ private:
     int layer_;
     int dtype_ = MF_BF16;
     mf_buf *wqkv_ = nullptr, *wo_ = nullptr, *qn_ = nullptr, *kn_ = nullptr, *an_ = nullptr;
+    bool tc_attn_ok_ = true;  // q/k fit the tensor-core attention's fp16 operands
 };
 
 // Qwen3MoE (src/models/qwen3/module.cpp:405-476): dense SwiGLU FFN when the

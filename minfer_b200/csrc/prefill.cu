@@ -80,14 +80,14 @@ EncodeFn tmap_encoder() {
     return encode;
 }
 
-// bf16 tensor map of rank 2 or 3 (dims[0] innermost, strides in bytes of
+// 16-bit (bf16 or fp16) tensor map of rank 2 or 3 (dims[0] innermost, strides in bytes of
 // dims 1..rank-1), 128-byte swizzle, zero fill out of bounds. The box's inner
 // extent is 64 elements (128 bytes).
 int make_tmap_nd(CUtensorMap* tm, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
-                 const uint32_t* box) {
-    if (((uintptr_t)base & 15) != 0) return fail(MF_E_INVALID, "bf16 operand must be 16-byte aligned");
+                 const uint32_t* box, CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
+    if (((uintptr_t)base & 15) != 0) return fail(MF_E_INVALID, "16-bit operand must be 16-byte aligned");
     for (int i = 0; i + 1 < rank; ++i)
-        if (strides[i] % 16 != 0) return fail(MF_E_INVALID, "bf16 operand strides must be multiples of 16 bytes");
+        if (strides[i] % 16 != 0) return fail(MF_E_INVALID, "16-bit operand strides must be multiples of 16 bytes");
     EncodeFn encode = tmap_encoder();
     if (!encode) return fail(MF_E_CUDA, "cuTensorMapEncodeTiled is not available");
     cuuint64_t d[3], st[2];
@@ -97,7 +97,7 @@ int make_tmap_nd(CUtensorMap* tm, const void* base, int rank, const uint64_t* di
         bx[i] = box[i];
     }
     for (int i = 0; i + 1 < rank; ++i) st[i] = strides[i];
-    CUresult r = encode(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx,
+    CUresult r = encode(tm, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx,
                         es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? MF_OK : fail(MF_E_CUDA, "cuTensorMapEncodeTiled failed");
@@ -297,9 +297,9 @@ int mf_prefill_attention(void* out_hi, void* out_lo, const float* q, const float
     return e == cudaSuccess ? MF_OK : fail(MF_E_CUDA, cudaGetErrorString(e));
 }
 
-// Scratch of mf_prefill_attention_tc: Q hi/lo [Hkv][P*G][128], K hi/lo
-// [Hkv][ld][128], V^T hi/lo [Hkv][128][ld], ld = n_keys rounded up to 64,
-// each section 256-byte aligned.
+// Scratch of mf_prefill_attention_tc: Q fp16 hi/lo [Hkv][P*G][128], K fp16
+// hi/lo [Hkv][ld][128], V^T bf16 hi/lo [Hkv][128][ld], ld = n_keys rounded up
+// to 64, each section 256-byte aligned.
 static size_t fa_layout(int n_tokens, int n_keys, int n_heads, int n_kv_heads, size_t off[6]) {
     const size_t ld = ((size_t)n_keys + 63) / 64 * 64;
     const size_t q = (size_t)n_tokens * n_heads * mf::ATT_D * 2, kv = (size_t)n_kv_heads * ld * mf::ATT_D * 2;
@@ -343,23 +343,23 @@ int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const fl
         return fail(MF_E_INVALID, "attention scratch too small");
     const size_t ld = ((size_t)n_keys + 63) / 64 * 64;
     uint8_t* base = (uint8_t*)scratch;
-    __nv_bfloat16 *qh = (__nv_bfloat16*)(base + off[0]), *ql = (__nv_bfloat16*)(base + off[1]);
-    __nv_bfloat16 *kh = (__nv_bfloat16*)(base + off[2]), *kl = (__nv_bfloat16*)(base + off[3]);
+    __half *qh = (__half*)(base + off[0]), *ql = (__half*)(base + off[1]);
+    __half *kh = (__half*)(base + off[2]), *kl = (__half*)(base + off[3]);
     __nv_bfloat16 *vh = (__nv_bfloat16*)(base + off[4]), *vl = (__nv_bfloat16*)(base + off[5]);
     CUtensorMap tq[2], tk[2], tv[2];
     const uint64_t D = mf::ATT_D;
     {
         const uint64_t dims[2] = {D, (uint64_t)n_tokens * n_heads}, strides[1] = {D * 2};
         const uint32_t box[2] = {64, mf::FA_BM};
-        int rc = make_tmap_nd(&tq[0], qh, 2, dims, strides, box);
-        if (!rc) rc = make_tmap_nd(&tq[1], ql, 2, dims, strides, box);
+        int rc = make_tmap_nd(&tq[0], qh, 2, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+        if (!rc) rc = make_tmap_nd(&tq[1], ql, 2, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
         if (rc) return rc;
     }
     {
         const uint64_t dims[3] = {D, (uint64_t)n_keys, (uint64_t)n_kv_heads}, strides[2] = {D * 2, ld * D * 2};
         const uint32_t box[3] = {64, mf::FA_BN, 1};
-        int rc = make_tmap_nd(&tk[0], kh, 3, dims, strides, box);
-        if (!rc) rc = make_tmap_nd(&tk[1], kl, 3, dims, strides, box);
+        int rc = make_tmap_nd(&tk[0], kh, 3, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+        if (!rc) rc = make_tmap_nd(&tk[1], kl, 3, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
         if (rc) return rc;
     }
     {
@@ -380,7 +380,8 @@ int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const fl
         const long long rows = (long long)n_tokens * n_heads + (long long)n_kv_heads * n_keys;
         const int blocks = (int)std::min<long long>((rows + 7) / 8, 148LL * 16);
         void* args[] = {(void*)&q, (void*)&k_cache, (void*)&n_tokens, (void*)&n_heads, (void*)&n_kv_heads,
-                        (void*)&max_seq, (void*)&n_keys, (void*)&ldi, (void*)&qh, (void*)&ql, (void*)&kh, (void*)&kl};
+                        (void*)&max_seq, (void*)&n_keys, (void*)&ldi, (void*)&qh, (void*)&ql, (void*)&kh, (void*)&kl,
+                        (void*)&status};
         cudaError_t e = launch((const void*)&mf::fa_qk_split_kernel, dim3(blocks), dim3(256), 0, st, args);
         if (e != cudaSuccess) return fail(MF_E_CUDA, cudaGetErrorString(e));
     }

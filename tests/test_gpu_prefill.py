@@ -7,7 +7,7 @@
   kernel's norm/rope (bit-identical routine) via the oracle;
 * causal attention (fresh prompt and prompt after cache history) against a
   float64 softmax-attention reference: max-abs <= 2e-5 for the fp32 SIMT
-  kernel, <= 5e-5 for the tensor-core kernel (bf16 hi/lo operands).
+  kernel, <= 2e-5 * max|V| for the tensor-core kernel (hi/lo operands).
 """
 import ctypes as C
 
@@ -149,18 +149,21 @@ def test_prefill_attention(lib, gpu, Hq, Hkv, T, pos0):
     assert (got - ref).abs().max().item() <= 2e-5
 
 
-@pytest.mark.parametrize("Hq,Hkv,T,pos0,S", [(32, 8, 100, 0, 256), (16, 2, 67, 0, 256), (8, 8, 33, 40, 256),
-                                             (16, 1, 20, 5, 256), (64, 8, 130, 0, 256), (8, 8, 300, 200, 512),
-                                             (32, 8, 257, 63, 384), (16, 4, 64, 64, 128)])
-def test_prefill_attention_tensor_cores(lib, gpu, Hq, Hkv, T, pos0, S):
-    """tcgen05 attention vs float64: max-abs <= 5e-5. Each operand is carried as
-    bf16 hi + lo (2^-17 relative) and the lo*lo product is dropped, so scores and
-    P*V carry ~1e-5 relative error per output (the fp32 SIMT kernel meets 2e-5)."""
+@pytest.mark.parametrize("Hq,Hkv,T,pos0,S,qs", [(32, 8, 100, 0, 256, 1), (16, 2, 67, 0, 256, 1),
+                                                (8, 8, 33, 40, 256, 1), (16, 1, 20, 5, 256, 1),
+                                                (64, 8, 130, 0, 256, 1), (8, 8, 300, 200, 512, 1),
+                                                (32, 8, 257, 63, 384, 1), (16, 4, 64, 64, 128, 1),
+                                                (16, 2, 150, 1100, 1280, 4), (8, 1, 90, 700, 800, 8)])
+def test_prefill_attention_tensor_cores(lib, gpu, Hq, Hkv, T, pos0, S, qs):
+    """tcgen05 attention vs float64: max-abs <= 2e-5 * max|V|. q/k are carried as
+    fp16 hi + lo (~2^-22 relative), P and V as bf16 hi + lo (~2^-17 relative each,
+    lo*lo dropped): an output dominated by one key carries up to ~1.5e-5 of that
+    key's |V| (the fp32 SIMT kernel meets 2e-5 absolute)."""
     from minfer_b200._lib import check
 
     D = 128
     g = torch.Generator(device=gpu).manual_seed(Hq + T + pos0)
-    q = torch.randn(T, Hq * D, generator=g, device=gpu)
+    q = torch.randn(T, Hq * D, generator=g, device=gpu) * qs  # qs > 1: peaked softmax, late max moves
     kc = torch.randn(Hkv, S, D, generator=g, device=gpu)
     vc = torch.randn(Hkv, S, D, generator=g, device=gpu)
     hi = torch.empty(T, Hq * D, dtype=torch.bfloat16, device=gpu)
@@ -174,7 +177,28 @@ def test_prefill_attention_tensor_cores(lib, gpu, Hq, Hkv, T, pos0, S):
     assert status_ok(lib)
     ref = _attn_ref(q, kc, vc, pos0, Hq, Hkv)
     got = (hi.double() + lo.double()).cpu()
-    assert (got - ref).abs().max().item() <= 5e-5
+    assert (got - ref).abs().max().item() <= 2e-5 * vc.abs().max().item()
+
+
+def test_prefill_attention_tensor_cores_flags_fp16_range(lib, gpu):
+    """A q value beyond fp16 sets status bit 4 (the result is not used)."""
+    from minfer_b200._lib import check
+
+    Hq, Hkv, T, S, D = 8, 8, 16, 64, 128
+    q = torch.randn(T, Hq * D, device=gpu)
+    q[3, 5] = 1e5
+    kc = torch.randn(Hkv, S, D, device=gpu)
+    vc = torch.randn(Hkv, S, D, device=gpu)
+    hi = torch.empty(T, Hq * D, dtype=torch.bfloat16, device=gpu)
+    lo = torch.empty_like(hi)
+    need = C.c_size_t()
+    check(lib.mf_prefill_attention_scratch(T, T, Hq, Hkv, C.byref(need)))
+    scratch = torch.empty(need.value, dtype=torch.uint8, device=gpu)
+    check(lib.mf_prefill_attention_tc(P(hi), P(lo), P(q), P(kc), P(vc), S, T, 0, Hq, Hkv, D, P(scratch), need.value,
+                                      stream()))
+    st = C.c_int()
+    check(lib.mf_prefill_status(C.byref(st), 1))
+    assert st.value == 4
 
 
 def test_prefill_qkv_post_matches_decode_rotation(lib, gpu):
