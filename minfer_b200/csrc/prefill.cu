@@ -297,17 +297,16 @@ int mf_prefill_attention(void* out_hi, void* out_lo, const float* q, const float
     return e == cudaSuccess ? MF_OK : fail(MF_E_CUDA, cudaGetErrorString(e));
 }
 
-// Scratch of mf_prefill_attention_tc: Q fp16 hi/lo [Hkv][P*G][128], K fp16
-// hi/lo [Hkv][ld][128], V^T bf16 hi/lo [Hkv][128][ld], ld = n_keys rounded up
-// to 64, each section 256-byte aligned.
-static size_t fa_layout(int n_tokens, int n_keys, int n_heads, int n_kv_heads, size_t off[6]) {
+// Scratch of mf_prefill_attention_tc: K fp16 hi/lo [Hkv][ld][128] and V^T
+// bf16 hi/lo [Hkv][128][ld], ld = n_keys rounded up to 64, each section
+// 256-byte aligned. (Q goes straight from the fp32 buffer into TMEM.)
+static size_t fa_layout(int n_keys, int n_kv_heads, size_t off[4]) {
     const size_t ld = ((size_t)n_keys + 63) / 64 * 64;
-    const size_t q = (size_t)n_tokens * n_heads * mf::ATT_D * 2, kv = (size_t)n_kv_heads * ld * mf::ATT_D * 2;
-    const size_t sz[6] = {q, q, kv, kv, kv, kv};
+    const size_t kv = (size_t)n_kv_heads * ld * mf::ATT_D * 2;
     size_t o = 0;
-    for (int i = 0; i < 6; ++i) {
+    for (int i = 0; i < 4; ++i) {
         off[i] = o;
-        o += (sz[i] + 255) / 256 * 256;
+        o += (kv + 255) / 256 * 256;
     }
     return o;
 }
@@ -315,8 +314,8 @@ static size_t fa_layout(int n_tokens, int n_keys, int n_heads, int n_kv_heads, s
 int mf_prefill_attention_scratch(int n_tokens, int n_keys, int n_heads, int n_kv_heads, size_t* bytes) {
     if (!bytes || n_tokens <= 0 || n_keys < n_tokens || n_heads <= 0 || n_kv_heads <= 0)
         return fail(MF_E_INVALID, "bad arguments");
-    size_t off[6];
-    *bytes = fa_layout(n_tokens, n_keys, n_heads, n_kv_heads, off);
+    size_t off[4];
+    *bytes = fa_layout(n_keys, n_kv_heads, off);
     return MF_OK;
 }
 
@@ -329,6 +328,7 @@ int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const fl
     if (d_head != mf::ATT_D) return fail(MF_E_UNSUPPORTED, "d_head must be 128");
     if (pos0 + n_tokens > max_seq) return fail(MF_E_INVALID, "prompt runs past max_seq");
     if (((uintptr_t)scratch & 255) != 0) return fail(MF_E_INVALID, "scratch must be 256-byte aligned");
+    if (((uintptr_t)q & 15) != 0) return fail(MF_E_INVALID, "q must be 16-byte aligned");
     const int G = n_heads / n_kv_heads;
     const void* fn = G == 1    ? (const void*)&mf::prefill_fa_kernel<1>
                      : G == 2  ? (const void*)&mf::prefill_fa_kernel<2>
@@ -338,23 +338,14 @@ int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const fl
                                : nullptr;
     if (!fn) return fail(MF_E_UNSUPPORTED, "query heads per KV head must be 1, 2, 4, 8 or 16");
     const int n_keys = pos0 + n_tokens;
-    size_t off[6];
-    if (fa_layout(n_tokens, n_keys, n_heads, n_kv_heads, off) > scratch_bytes)
-        return fail(MF_E_INVALID, "attention scratch too small");
+    size_t off[4];
+    if (fa_layout(n_keys, n_kv_heads, off) > scratch_bytes) return fail(MF_E_INVALID, "attention scratch too small");
     const size_t ld = ((size_t)n_keys + 63) / 64 * 64;
     uint8_t* base = (uint8_t*)scratch;
-    __half *qh = (__half*)(base + off[0]), *ql = (__half*)(base + off[1]);
-    __half *kh = (__half*)(base + off[2]), *kl = (__half*)(base + off[3]);
-    __nv_bfloat16 *vh = (__nv_bfloat16*)(base + off[4]), *vl = (__nv_bfloat16*)(base + off[5]);
-    CUtensorMap tq[2], tk[2], tv[2];
+    __half *kh = (__half*)(base + off[0]), *kl = (__half*)(base + off[1]);
+    __nv_bfloat16 *vh = (__nv_bfloat16*)(base + off[2]), *vl = (__nv_bfloat16*)(base + off[3]);
+    CUtensorMap tk[2], tv[2];
     const uint64_t D = mf::ATT_D;
-    {
-        const uint64_t dims[2] = {D, (uint64_t)n_tokens * n_heads}, strides[1] = {D * 2};
-        const uint32_t box[2] = {64, mf::FA_BM};
-        int rc = make_tmap_nd(&tq[0], qh, 2, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
-        if (!rc) rc = make_tmap_nd(&tq[1], ql, 2, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
-        if (rc) return rc;
-    }
     {
         const uint64_t dims[3] = {D, (uint64_t)n_keys, (uint64_t)n_kv_heads}, strides[2] = {D * 2, ld * D * 2};
         const uint32_t box[3] = {64, mf::FA_BN, 1};
@@ -374,15 +365,14 @@ int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const fl
     int* status = status_ptr();
     if (!status) return fail(MF_E_CUDA, "prefill status symbol");
     cudaStream_t st = mf::resolve_stream(stream);
-    // operands: Q and K rows split (one warp per 128-float row), V transposed in 64-key tiles
+    // operands: K rows split (one warp per 128-float row), V transposed in 64-key tiles
     const int ldi = (int)ld;
     {
-        const long long rows = (long long)n_tokens * n_heads + (long long)n_kv_heads * n_keys;
+        const long long rows = (long long)n_kv_heads * n_keys;
         const int blocks = (int)std::min<long long>((rows + 7) / 8, 148LL * 16);
-        void* args[] = {(void*)&q, (void*)&k_cache, (void*)&n_tokens, (void*)&n_heads, (void*)&n_kv_heads,
-                        (void*)&max_seq, (void*)&n_keys, (void*)&ldi, (void*)&qh, (void*)&ql, (void*)&kh, (void*)&kl,
-                        (void*)&status};
-        cudaError_t e = launch((const void*)&mf::fa_qk_split_kernel, dim3(blocks), dim3(256), 0, st, args);
+        void* args[] = {(void*)&k_cache, (void*)&n_kv_heads, (void*)&max_seq, (void*)&n_keys, (void*)&ldi,
+                        (void*)&kh, (void*)&kl, (void*)&status};
+        cudaError_t e = launch((const void*)&mf::fa_k_split_kernel, dim3(blocks), dim3(256), 0, st, args);
         if (e != cudaSuccess) return fail(MF_E_CUDA, cudaGetErrorString(e));
     }
     {
@@ -392,17 +382,16 @@ int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const fl
         if (e != cudaSuccess) return fail(MF_E_CUDA, cudaGetErrorString(e));
     }
     mf::FaParams p;
+    p.q = q;
     p.P = n_tokens;
     p.pos0 = pos0;
     p.n_heads = n_heads;
-    p.n_keys_max = n_keys;
     p.out_hi = (__nv_bfloat16*)out_hi;
     p.out_lo = (__nv_bfloat16*)out_lo;
     p.status = status;
     p.timeout_ns = timeout_ns();
     const int QT = mf::FA_BM / G;
-    void* args[] = {(void*)&tq[0], (void*)&tq[1], (void*)&tk[0], (void*)&tk[1], (void*)&tv[0], (void*)&tv[1],
-                    (void*)&p};
+    void* args[] = {(void*)&tk[0], (void*)&tk[1], (void*)&tv[0], (void*)&tv[1], (void*)&p};
     cudaError_t e = launch(fn, dim3((n_tokens + QT - 1) / QT, n_kv_heads), dim3(mf::FA_THREADS),
                            mf::FA_SMEM_BYTES, st, args);
     return e == cudaSuccess ? MF_OK : fail(MF_E_CUDA, cudaGetErrorString(e));
