@@ -43,6 +43,10 @@ constexpr int COMM_SEQ_GREEDY = 255;
 struct CommLocal {
     int status;  // COMM_STATUS_* bits; cleared by the host
     int pad[15];
+    // arrival counters of the receiving kernels' grid barrier, per slot:
+    // (tag << 32) | CTAs arrived (see grid_arrive_wait)
+    unsigned long long bar[2];
+    unsigned long long pad2[6];
 };
 
 struct CommLayout {
@@ -115,6 +119,40 @@ MF_DEVICE float recv_tagged(const unsigned long long* p, uint32_t tag, unsigned 
         atomicOr(status, bit);
     }
     return __uint_as_float((uint32_t)w);
+}
+
+// Grid barrier of one receiving kernel, on a counter word holding
+// (tag << 32) | arrivals: the first CTA of this exchange replaces a stale tag
+// (compare-and-swap), the others add one; then every CTA polls until all
+// `n_ctas` have arrived. Every CTA of the grid is resident (the grid is sized
+// to the SMs' capacity, and the dependent kernel launches only after all of
+// this grid's CTAs started), so the barrier completes; it is bounded by
+// `deadline` all the same (then it sets `bit` in *status and returns). The
+// slot is reused two exchanges later, after this kernel completed. Called by
+// one thread per CTA, after the CTA's writes were fenced.
+MF_DEVICE void grid_arrive_wait(unsigned long long* ctr, uint32_t tag, unsigned n_ctas, unsigned long long deadline,
+                                bool* late, int* status, int bit) {
+    unsigned long long old;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(old) : "l"(ctr) : "memory");
+    for (;;) {
+        if ((uint32_t)(old >> 32) == tag) {
+            atomicAdd(ctr, 1ull);
+            break;
+        }
+        const unsigned long long prev = atomicCAS(ctr, old, ((unsigned long long)tag << 32) | 1ull);
+        if (prev == old) break;
+        old = prev;
+    }
+    const unsigned long long target = ((unsigned long long)tag << 32) | n_ctas;
+    for (long long i = 0; i < COMM_MAX_POLLS; ++i) {
+        unsigned long long v;
+        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(ctr) : "memory");
+        if (v == target) return;
+        if (*late || globaltimer_ns() > deadline) break;
+        __nanosleep(20);
+    }
+    *late = true;
+    atomicOr(status, bit);
 }
 
 // x[i] = x_res[i] + partial_0[i] + ... + partial_{tp-1}[i] (rank order) for

@@ -264,17 +264,33 @@ __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2)
         if (XM == X_AR_NORM) {
             // all-reduce receive: x = residual + partial_0 + partial_1 + ...
             // in rank order (identical on every rank), each partial element
-            // read once its tag shows it is this exchange's
+            // read once its tag shows it is this exchange's. Each CTA reduces
+            // only its slice of x into x_out; after a grid barrier every CTA
+            // reads the whole reduced x_out (the partials cross L2 once, not
+            // once per CTA).
             const uint32_t tag = comm_tag(__ldcg(p.step + MF_STEP_FRAME), p.ar_seq);
             const int slot = p.ar_seq & 1;
             int* status = &p.comm.local()->status;
             const unsigned long long deadline = globaltimer_ns() + p.comm.timeout_ns;
             bool late = false;
-            recv_sum(p.comm, slot, tag, p.x_res, tid, T, K, deadline, &late, status, [&](int i, float v) {
-                xs[i] = v;
-                ss = fmaf(v, v, ss);
-                if (blockIdx.x == 0) p.x_out[i] = v;
-            });
+            const int e0 = (int)((long long)blockIdx.x * K / gridDim.x);
+            const int e1 = (int)((long long)(blockIdx.x + 1) * K / gridDim.x);
+            recv_sum(p.comm, slot, tag, p.x_res, e0 + tid, T, e1, deadline, &late, status,
+                     [&](int i, float v) { p.x_out[i] = v; });
+            __threadfence();
+            __syncthreads();
+            if (tid == 0)
+                grid_arrive_wait(&p.comm.local()->bar[slot], tag, gridDim.x, deadline, &late, status,
+                                 COMM_STATUS_AR_TIMEOUT);
+            __syncthreads();
+            for (int i = tid * 4; i < K; i += T * 4) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(p.x_out + i));
+                *reinterpret_cast<float4*>(xs + i) = v;
+                ss = fmaf(v.x, v.x, ss);
+                ss = fmaf(v.y, v.y, ss);
+                ss = fmaf(v.z, v.z, ss);
+                ss = fmaf(v.w, v.w, ss);
+            }
         } else {
             for (int i = tid; i < K; i += T) {
                 const float v = __ldcg(p.x + i);
@@ -282,7 +298,7 @@ __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2)
                 ss = fmaf(v, v, ss);
             }
         }
-        ss = block_sum(ss, scratch);
+        ss = block_sum(ss, scratch);  // (its barrier also publishes every thread's xs stores)
         // src/ops/kernels.cpp:355-363: rms = sqrtf(ss/dim + eps); inv = 1/rms; out = inv*x*w
         // (each thread rescales the elements it stored itself)
         const float inv = 1.0f / sqrtf(ss / (float)K + p.eps);
