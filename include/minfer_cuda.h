@@ -261,6 +261,10 @@ typedef struct mf_comm mf_comm;
 /* max_floats: longest all-reduced vector (d_model, multiple of 4);
  * gather_floats: length of the full-logits gather buffer (vocabulary size, or 0). */
 int mf_comm_create(int rank, int tp_rank, int tp_size, int max_floats, int gather_floats, mf_comm** out);
+/* The same with two bulk slots of bulk_floats fp32 each for batched-prefill
+ * exchanges of [rows, d] partials (mf_comm_bulk_ptr, mf_bulk_allreduce). */
+int mf_comm_create_ex(int rank, int tp_rank, int tp_size, int max_floats, int gather_floats, size_t bulk_floats,
+                      mf_comm** out);
 int mf_comm_handle(const mf_comm* c, void* out, size_t n);
 /* A rank's own handle in another rank's place maps that peer to this rank's
  * region: a loopback in which that peer never sends (its waits time out). */
@@ -270,6 +274,17 @@ int mf_comm_connect(mf_comm* c, const void* handles, size_t n);
 int mf_comm_status(mf_comm* c, int* status, int clear);
 /* Device address of this rank's full-logits buffer (mf_allreduce_lm_head with gather_logits). */
 int mf_comm_gather_ptr(const mf_comm* c, float** logits);
+/* This rank's bulk slot (0 or 1): where its partial of a batched-prefill
+ * exchange goes (for example as the output of mf_prefill_gemm). */
+int mf_comm_bulk_ptr(const mf_comm* c, int slot, float** out);
+/* Batched-prefill all-reduce (replaces minfer's per-token exchange-free CPU
+ * path, src/base/model.cpp:120-129, for tensor-parallel shards): after this
+ * rank's partial is complete in bulk slot `slot`, x[i] += partial_0[i] + ...
+ * + partial_{T-1}[i] in rank order on every rank. `epoch` numbers the
+ * exchanges (1, 2, ... identical on every rank); slots must alternate between
+ * consecutive exchanges. A wait that gives up sets mf_comm_status bit 1 and
+ * leaves x unchanged. */
+int mf_bulk_allreduce(float* x, size_t n, mf_comm* c, int slot, unsigned long long epoch, void* stream);
 void mf_comm_destroy(mf_comm* c);
 
 /* All-reduce send fused into a GEMV: the partial W·a of this rank (W holds
@@ -357,6 +372,19 @@ int mf_prefill_attention_scratch(int n_tokens, int n_keys, int n_heads, int n_kv
 int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const float* k_cache, const float* v_cache,
                             int max_seq, int n_tokens, int pos0, int n_heads, int n_kv_heads, int d_head,
                             void* scratch, size_t scratch_bytes, void* stream);
+/* ===================================================================== */
+/* Sampling on the device                                                */
+/* ===================================================================== */
+/* The k (<= 64) largest of x[0, n) and their indices, sorted by value,
+ * largest first (equal values: lower index first; NaN counts as -inf): the
+ * candidate list minfer's Sampler builds with nth_element + sort
+ * (src/base/sampler.cpp:40-50), so the host only needs k pairs instead of the
+ * whole vocabulary. The workspace (mf_topk_workspace_bytes, 16-byte aligned)
+ * must be zero before the first call; the kernel leaves it ready for the next. */
+size_t mf_topk_workspace_bytes(int n, int k);
+int mf_topk(const float* x, int n, int k, int* ids, float* vals, void* workspace, size_t workspace_bytes,
+            void* stream);
+
 /* Status bits of the prefill kernels since the last clear (1: a GEMM wait
  * gave up, 2: an attention wait gave up, 4: attention q/k outside the fp16
  * range; synchronises the device). */

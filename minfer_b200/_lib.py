@@ -129,10 +129,13 @@ CUDA_API = {
     "mf_lm_head_workspace_bytes": (SZ, []),
     "mf_lm_head": (I, [P, P, P, F, P, I, I, I, I, P, P, P]),
     "mf_comm_create": (I, [I, I, I, I, I, P]),
+    "mf_comm_create_ex": (I, [I, I, I, I, I, SZ, P]),
     "mf_comm_handle": (I, [P, P, SZ]),
     "mf_comm_connect": (I, [P, P, SZ]),
     "mf_comm_status": (I, [P, P, I]),
     "mf_comm_gather_ptr": (I, [P, P]),
+    "mf_comm_bulk_ptr": (I, [P, I, P]),
+    "mf_bulk_allreduce": (I, [P, SZ, P, I, C.c_ulonglong, P]),
     "mf_comm_destroy": (None, [P]),
     "mf_matmul_push": (I, [P, P, I, I, I, P, I, P, P]),
     "mf_allreduce_rmsnorm_matmul": (I, [P, P, P, P, F, P, I, I, I, P, I, P, P]),
@@ -150,6 +153,8 @@ CUDA_API = {
     "mf_prefill_attention_scratch": (I, [I, I, I, I, P]),
     "mf_prefill_attention_tc": (I, [P, P, P, P, P, I, I, I, I, I, I, P, SZ, P]),
     "mf_prefill_status": (I, [P, I]),
+    "mf_topk_workspace_bytes": (SZ, [I, I]),
+    "mf_topk": (I, [P, I, I, P, P, P, SZ, P]),
     "mf_matmul": (I, [P, P, P, I, SZ, I, I, P]),
     "mf_rmsnorm": (I, [P, P, P, I, F, I, P]),
     "mf_softmax": (I, [P, P, I, I, P]),

@@ -826,7 +826,13 @@ int mf_lm_head(float* logits, const float* x, const float* norm_w, float eps, co
 // ===================================================================== tensor parallelism
 
 int mf_comm_create(int rank, int tp_rank, int tp_size, int max_floats, int gather_floats, mf_comm** out) {
+    return mf_comm_create_ex(rank, tp_rank, tp_size, max_floats, gather_floats, 0, out);
+}
+
+int mf_comm_create_ex(int rank, int tp_rank, int tp_size, int max_floats, int gather_floats, size_t bulk_floats,
+                      mf_comm** out) {
     MF_REQUIRE(out, MF_E_INVALID, "null output");
+    MF_REQUIRE(bulk_floats % 4 == 0, MF_E_INVALID, "bulk_floats must be a multiple of 4");
     MF_REQUIRE(g.inited && rank >= 0 && rank < (int)g.ranks.size(), MF_E_STATE, "mf_init first (rank %d)", rank);
     MF_REQUIRE(tp_size >= 1 && tp_size <= MF_TP_MAX && tp_rank >= 0 && tp_rank < tp_size, MF_E_INVALID,
                "tp_rank %d / tp_size %d", tp_rank, tp_size);
@@ -835,7 +841,7 @@ int mf_comm_create(int rank, int tp_rank, int tp_size, int max_floats, int gathe
     MF_CK(cudaSetDevice(g.ranks[rank].device));
     auto c = std::make_unique<mf_comm>();
     c->rank = rank;
-    c->layout = mf::comm_layout(max_floats, gather_floats);
+    c->layout = mf::comm_layout(max_floats, gather_floats, bulk_floats);
     MF_REQUIRE(c->layout.total < (1ull << 32), MF_E_INVALID, "exchange region too large");
     MF_CK(cudaMalloc((void**)&c->region, c->layout.total));
     cudaError_t e = cudaMemset(c->region, 0, c->layout.total);
@@ -855,6 +861,9 @@ int mf_comm_create(int rank, int tp_rank, int tp_size, int max_floats, int gathe
     d.off_best = (uint32_t)c->layout.best;
     d.off_gather = (uint32_t)c->layout.gather;
     d.off_local = (uint32_t)c->layout.local;
+    d.off_flags = (uint32_t)c->layout.flags;
+    d.off_bulk = (uint32_t)c->layout.bulk;
+    d.bulk_floats = bulk_floats;
     d.base[tp_rank] = c->region;
     c->connected = tp_size == 1;
     *out = c.release();
@@ -913,6 +922,60 @@ int mf_comm_status(mf_comm* c, int* status, int clear) {
     int* dst = (int*)(c->region + c->layout.local + offsetof(mf::CommLocal, status));
     MF_CK(cudaMemcpy(status, dst, sizeof(int), cudaMemcpyDeviceToHost));
     if (clear) MF_CK(cudaMemset(dst, 0, sizeof(int)));
+    return MF_OK;
+}
+
+size_t mf_topk_workspace_bytes(int n, int k) {
+    if (n <= 0 || k <= 0) return 0;
+    const size_t grid = ((size_t)n + mf::TOPK_CHUNK - 1) / mf::TOPK_CHUNK;
+    return 256 + grid * (size_t)k * (sizeof(float) + sizeof(int));
+}
+
+int mf_topk(const float* x, int n, int k, int* ids, float* vals, void* workspace, size_t workspace_bytes,
+            void* stream) {
+    MF_REQUIRE(x && ids && vals && workspace, MF_E_INVALID, "null argument");
+    MF_REQUIRE(k >= 1 && k <= mf::TOPK_MAX && n >= k, MF_E_INVALID, "need 1 <= k <= %d and k <= n", mf::TOPK_MAX);
+    MF_REQUIRE(workspace_bytes >= mf_topk_workspace_bytes(n, k), MF_E_INVALID, "top-k workspace too small");
+    MF_REQUIRE(((uintptr_t)workspace & 15) == 0, MF_E_INVALID, "workspace must be 16-byte aligned");
+    const int grid = (n + mf::TOPK_CHUNK - 1) / mf::TOPK_CHUNK;
+    const size_t smem = 2 * (size_t)std::max(mf::TOPK_CHUNK, grid * k) * sizeof(float);
+    MF_REQUIRE(smem <= 200 * 1024, MF_E_UNSUPPORTED, "n * k too large for one merge CTA");
+    static std::mutex mu;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        MF_CK(cudaFuncSetAttribute((const void*)&mf::topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)smem));
+    }
+    unsigned int* counter = (unsigned int*)workspace;
+    float* cand_v = (float*)((char*)workspace + 256);
+    int* cand_i = (int*)(cand_v + (size_t)grid * k);
+    void* args[] = {(void*)&x, (void*)&n, (void*)&k, (void*)&ids, (void*)&vals, (void*)&cand_v, (void*)&cand_i,
+                    (void*)&counter};
+    MF_CK(launch((const void*)&mf::topk_kernel, dim3(grid), dim3(mf::TOPK_THREADS), smem,
+                 mf::resolve_stream(stream), args));
+    return MF_OK;
+}
+
+int mf_comm_bulk_ptr(const mf_comm* c, int slot, float** out) {
+    MF_REQUIRE(c && out && (slot == 0 || slot == 1), MF_E_INVALID, "bad arguments");
+    MF_REQUIRE(c->dev.bulk_floats > 0, MF_E_STATE, "exchange region has no bulk slots");
+    *out = (float*)(c->region + c->layout.bulk) + (size_t)slot * c->dev.bulk_floats;
+    return MF_OK;
+}
+
+int mf_bulk_allreduce(float* x, size_t n, mf_comm* c, int slot, unsigned long long epoch, void* stream) {
+    MF_REQUIRE(x && c && (slot == 0 || slot == 1) && epoch > 0, MF_E_INVALID, "bad arguments");
+    MF_REQUIRE(c->connected, MF_E_STATE, "mf_comm_connect first");
+    MF_REQUIRE(n > 0 && n % 4 == 0 && n <= c->dev.bulk_floats, MF_E_INVALID,
+               "n must be a positive multiple of 4 within the bulk slot (%zu floats)", c->dev.bulk_floats);
+    MF_REQUIRE(((uintptr_t)x & 15) == 0, MF_E_INVALID, "x must be 16-byte aligned");
+    const size_t n4 = n / 4;
+    long long grid = (long long)((n4 + 255) / 256);
+    grid = std::min<long long>(grid, (long long)num_sms() * 4);
+    const mf::CommDev dev = c->dev;
+    void* args[] = {(void*)&x, (void*)&n4, (void*)&dev, (void*)&slot, (void*)&epoch};
+    MF_CK(launch((const void*)&mf::bulk_allreduce_kernel, dim3((unsigned)grid), dim3(256), 0,
+                 mf::resolve_stream(stream), args));
     return MF_OK;
 }
 

@@ -20,6 +20,15 @@
 //   best    [MF_TP_MAX][2] u64                             per-rank lm_head maximum: value, index
 //   gather  [gather_floats] f32                            full logits (each rank writes its slice)
 //   local   CommLocal                                      this rank only: status
+//   flags   [MF_TP_MAX] u64                                batched-prefill exchange: sender's epoch
+//   bulk    [2 slots][bulk_floats] f32                     batched-prefill partials [rows][d]
+//
+// Batched prefill exchanges whole [rows, d] partials: each rank's GEMM writes
+// its partial into its own bulk slot, the exchange kernel raises this rank's
+// flag (a monotonic epoch) in every rank's region and, once every rank's flag
+// shows the epoch, adds all ranks' slots in rank order. Slots alternate; a
+// rank writes a slot again only after its next exchange, which needs every
+// rank's flag for that exchange, raised after that rank finished reading.
 //
 // Slot reuse: consecutive all-reduces alternate slots. A rank cannot send
 // into a slot again before every rank has read that slot's previous message:
@@ -50,18 +59,20 @@ struct CommLocal {
 };
 
 struct CommLayout {
-    size_t recv, best, gather, local, total;
+    size_t recv, best, gather, local, flags, bulk, total;
 };
 
 __host__ __device__ inline size_t comm_align(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline CommLayout comm_layout(int max_floats, int gather_floats) {
+__host__ __device__ inline CommLayout comm_layout(int max_floats, int gather_floats, size_t bulk_floats = 0) {
     CommLayout L;
     L.recv = 0;
     L.best = comm_align(L.recv + (size_t)2 * TP_MAX * max_floats * 8, 256);
     L.gather = comm_align(L.best + (size_t)TP_MAX * 2 * 8, 256);
     L.local = comm_align(L.gather + (size_t)gather_floats * sizeof(float), 256);
-    L.total = comm_align(L.local + sizeof(CommLocal), 256);
+    L.flags = comm_align(L.local + sizeof(CommLocal), 256);
+    L.bulk = comm_align(L.flags + (size_t)TP_MAX * 8, 256);
+    L.total = comm_align(L.bulk + 2 * bulk_floats * sizeof(float), 256);
     return L;
 }
 
@@ -71,7 +82,8 @@ struct CommDev {
     int tp_rank, tp_size;
     int max_floats, gather_floats;
     unsigned long long timeout_ns;  // how long a wait polls before it gives up
-    uint32_t off_recv, off_best, off_gather, off_local;
+    uint32_t off_recv, off_best, off_gather, off_local, off_flags, off_bulk;
+    size_t bulk_floats;
 
     MF_DEVICE unsigned long long* recv(int owner, int slot, int sender) const {
         return reinterpret_cast<unsigned long long*>(base[owner] + off_recv) +
@@ -82,6 +94,12 @@ struct CommDev {
     }
     MF_DEVICE float* gather(int owner) const { return reinterpret_cast<float*>(base[owner] + off_gather); }
     MF_DEVICE CommLocal* local() const { return reinterpret_cast<CommLocal*>(base[tp_rank] + off_local); }
+    MF_DEVICE unsigned long long* flags(int owner) const {
+        return reinterpret_cast<unsigned long long*>(base[owner] + off_flags);
+    }
+    MF_DEVICE float* bulk(int owner, int slot) const {
+        return reinterpret_cast<float*>(base[owner] + off_bulk) + (size_t)slot * bulk_floats;
+    }
 };
 
 MF_DEVICE uint32_t comm_tag(int frame, int seq) { return (uint32_t)frame * 256u + (uint32_t)seq; }

@@ -28,6 +28,19 @@ int mf_dtype(DataType t) {
     }
 }
 
+// Tensor-parallel batched prefill: a projection's partial goes into this
+// rank's next bulk slot (exchange rs.pf_epoch + 1, slots alternating), then
+// X += every rank's partial in rank order.
+float* prefill_exchange_slot(RunState& rs) {
+    float* p = nullptr;
+    check(mf_comm_bulk_ptr(rs.comm, (int)((rs.pf_epoch + 1) & 1), &p), "prefill exchange slot");
+    return p;
+}
+void prefill_exchange(RunState& rs, float* X, int n, int d) {
+    const unsigned long long ep = ++rs.pf_epoch;
+    check(mf_bulk_allreduce(X, (size_t)n * d, rs.comm, (int)(ep & 1), ep, rs.stream), "prefill all-reduce");
+}
+
 mf_buf* upload_tensor(const TensorView& t, int rank) {
     mf_buf* b = nullptr;
     check(mf_upload(t.data, t.bytes, rank, &b), ("upload " + t.name).c_str());
@@ -213,7 +226,8 @@ public:
     // the same layer for n prompt tokens at once: pre-norm, QKV GEMM, Q/K norm
     // + RoPE + KV write, causal attention, O GEMM + residual
     void prefill_forward(RunState& rs, int n, int pos0) override {
-        const int d = c_.d_model, H = c_.n_heads, Hkv = c_.n_kv_heads, D = c_.d_head, Nqkv = (H + 2 * Hkv) * D;
+        const int d = c_.d_model, H = c_.heads_local(), Hkv = c_.kv_heads_local(), D = c_.d_head;
+        const int Nqkv = (H + 2 * Hkv) * D;
         const int S = (int)c_.user_max_seq_len;
         float* X = (float*)mf_ptr(rs.pf_x);
         void *hi = mf_ptr(rs.pf_hi), *lo = mf_ptr(rs.pf_lo);
@@ -236,8 +250,17 @@ public:
             check(mf_prefill_attention_tc(hi, lo, (const float*)mf_ptr(rs.pf_q), kc, vc, S, n, pos0, H, Hkv, D,
                                           mf_ptr(rs.pf_att), rs.pf_att_bytes, rs.stream),
                   "prefill attention");
-        check(mf_prefill_gemm(X, d, hi, lo, mf_ptr(wo_), n, d, H * D, MF_PREFILL_RESID, nullptr, nullptr, rs.stream),
-              "prefill output projection");
+        if (c_.tp_size == 1) {
+            check(mf_prefill_gemm(X, d, hi, lo, mf_ptr(wo_), n, d, H * D, MF_PREFILL_RESID, nullptr, nullptr,
+                                  rs.stream),
+                  "prefill output projection");
+        } else {
+            float* part = prefill_exchange_slot(rs);
+            check(mf_prefill_gemm(part, d, hi, lo, mf_ptr(wo_), n, d, H * D, MF_PREFILL_STORE, nullptr, nullptr,
+                                  rs.stream),
+                  "prefill output projection (partial)");
+            prefill_exchange(rs, X, n, d);
+        }
     }
 
 private:
@@ -360,15 +383,24 @@ public:
     // epilogue, down GEMM + residual
     void prefill_forward(RunState& rs, int n, int pos0) override {
         if (c_.n_experts > 0) throw std::runtime_error("batched prefill covers dense FFN layers");
-        const int d = c_.d_model, F = c_.d_ff;
+        const int d = c_.d_model, F = c_.ff_local();
         float* X = (float*)mf_ptr(rs.pf_x);
         void *hi = mf_ptr(rs.pf_hi), *lo = mf_ptr(rs.pf_lo), *hhi = mf_ptr(rs.pf_hhi), *hlo = mf_ptr(rs.pf_hlo);
         check(mf_prefill_norm_split(hi, lo, nullptr, X, (const float*)mf_ptr(fn_), c_.rms_norm_eps, d, n, rs.stream),
               "prefill ffn norm");
         check(mf_prefill_gemm(nullptr, 0, hi, lo, mf_ptr(wgu_), n, 2 * F, d, MF_PREFILL_SWIGLU, hhi, hlo, rs.stream),
               "prefill gate/up projection");
-        check(mf_prefill_gemm(X, d, hhi, hlo, mf_ptr(wd_), n, d, F, MF_PREFILL_RESID, nullptr, nullptr, rs.stream),
-              "prefill down projection");
+        if (c_.tp_size == 1) {
+            check(mf_prefill_gemm(X, d, hhi, hlo, mf_ptr(wd_), n, d, F, MF_PREFILL_RESID, nullptr, nullptr,
+                                  rs.stream),
+                  "prefill down projection");
+        } else {
+            float* part = prefill_exchange_slot(rs);
+            check(mf_prefill_gemm(part, d, hhi, hlo, mf_ptr(wd_), n, d, F, MF_PREFILL_STORE, nullptr, nullptr,
+                                  rs.stream),
+                  "prefill down projection (partial)");
+            prefill_exchange(rs, X, n, d);
+        }
     }
 
 private:
@@ -498,7 +530,9 @@ Config Config::from_gguf(const GGUFFile& f, const RunParams& rp) {
 namespace {
 // Frames are captured per manager rank; every model instance owns a disjoint
 // block of frame ids so two models on one device never replay each other's graphs.
-constexpr int kFrameKinds = 8;  // 0-2 forward, 3-4 chained decode, 5-6 logits after a batched prefill
+// 0-2 forward, 3-4 chained decode, 5-6 logits after a batched prefill, 7-8 forward / prefill
+// logits read back as top-k candidates
+constexpr int kFrameKinds = 10;
 int next_frame_base() {
     static int next = 0;
     const int b = next;
@@ -538,6 +572,7 @@ Qwen3Model::~Qwen3Model() {
     layers_.clear();
     for (mf_buf* b : state_bufs_) mf_release(b);
     if (rs_.h_logits) mf_host_free(rs_.h_logits);
+    if (rs_.h_topk) mf_host_free(rs_.h_topk);
 }
 
 void Qwen3Model::reset_sampler() {
@@ -613,10 +648,21 @@ void Qwen3Model::alloc_state() {
     void* hl = nullptr;
     check(mf_host_alloc(c.vocab_size * 4, &hl), "pinned logits");
     rs.h_logits = (float*)hl;
+    rs.topk_ids = alloc(kTopkMax * 4, "top-k ids");
+    rs.topk_vals = alloc(kTopkMax * 4, "top-k logits");
+    rs.topk_ws_bytes = mf_topk_workspace_bytes((int)c.vocab_size, kTopkMax);
+    rs.topk_ws = alloc(rs.topk_ws_bytes, "top-k workspace");
+    check(mf_host_alloc(2 * kTopkMax * 4, &rs.h_topk), "pinned top-k");
     rs.kv_bytes_per_pos = 2ull * c.n_layers * Hkvl * c.d_head * sizeof(float);
-    if (c.tp_size > 1)
-        check(mf_comm_create(rank_, c.tp_rank, c.tp_size, (c.d_model + 3) / 4 * 4, (int)c.vocab_size, &rs.comm),
+    if (c.tp_size > 1) {
+        // dense models also get two bulk slots of [prompt chunk rows, d] for the batched prefill
+        rs.pf_bulk_rows = c.ep() ? 0 : (int)std::min<size_t>(c.user_max_seq_len, (size_t)kPrefillChunk);
+        const size_t bulk = (size_t)rs.pf_bulk_rows * ((c.d_model + 3) / 4 * 4);
+        check(mf_comm_create_ex(rank_, c.tp_rank, c.tp_size, (c.d_model + 3) / 4 * 4, (int)c.vocab_size, bulk,
+                                &rs.comm),
               "tensor-parallel exchange");
+        rs.zero_d = alloc((size_t)c.d_model * 4, "zero partial");
+    }
 }
 
 void Qwen3Model::comm_handle(void* out, size_t n) const {
@@ -638,7 +684,8 @@ int Qwen3Model::comm_status(int* status) {
 }
 
 bool Qwen3Model::prefill_supported() const {
-    if (device_ != DeviceType::CUDA || cfg_.tp_size != 1 || cfg_.n_experts != 0) return false;
+    if (device_ != DeviceType::CUDA || cfg_.n_experts != 0) return false;
+    if (cfg_.tp_size > 1 && (rs_.pf_bulk_rows <= 0 || !rs_.comm || cfg_.d_model % 4 != 0)) return false;
     if (cfg_.weight_dtype != DataType::BF16 || cfg_.d_head != 128 || cfg_.d_model % 8 != 0 || cfg_.d_ff % 8 != 0)
         return false;
     const int G = cfg_.n_heads / cfg_.n_kv_heads;
@@ -695,7 +742,8 @@ bool Qwen3Model::prefill(const uint32_t* tokens, int n, int pos0, bool compute_l
     // MF_PREFILL_CHUNK overrides the rows per pass (smaller chunks exercise the history path)
     const char* ce = std::getenv("MF_PREFILL_CHUNK");
     const size_t want = (ce && std::atoi(ce) > 0) ? (size_t)std::atoi(ce) : (size_t)kPrefillChunk;
-    const int chunk = (int)std::min<size_t>(cfg_.user_max_seq_len, want);
+    int chunk = (int)std::min<size_t>(cfg_.user_max_seq_len, want);
+    if (cfg_.tp_size > 1) chunk = std::min(chunk, rs_.pf_bulk_rows);  // rows one exchange slot holds
     alloc_prefill(std::min(chunk, n));
     int last_rows = 0;
     for (int c0 = 0; c0 < n; c0 += rs_.pf_cap) {
@@ -707,8 +755,14 @@ bool Qwen3Model::prefill(const uint32_t* tokens, int n, int pos0, bool compute_l
     int st = 0;
     check(mf_prefill_status(&st, 1), "prefill status");
     if (st) throw std::runtime_error("a prefill kernel wait gave up (status " + std::to_string(st) + ")");
-    // the last token's residual row feeds the decode lm_head
-    check(mf_copy(rs_.x, 0, rs_.pf_x, (size_t)(last_rows - 1) * cfg_.d_model * 4, (size_t)cfg_.d_model * 4),
+    if (rs_.comm) {
+        check(mf_comm_status(rs_.comm, &st, 0), "exchange status");
+        if (st) throw std::runtime_error("a prefill exchange wait gave up (status " + std::to_string(st) + ")");
+    }
+    // the last token's residual row feeds the decode lm_head (under tensor
+    // parallelism the lm_head adds an all-reduce to it: see below)
+    mf_buf* last = cfg_.tp_size > 1 ? rs_.xb[1] : rs_.x;
+    check(mf_copy(last, 0, rs_.pf_x, (size_t)(last_rows - 1) * cfg_.d_model * 4, (size_t)cfg_.d_model * 4),
           "prefill last row");
     rs_.cur_pos = pos0 + n - 1;
     rs_.token_id = tokens[n - 1];
@@ -719,16 +773,23 @@ bool Qwen3Model::prefill(const uint32_t* tokens, int n, int pos0, bool compute_l
     rs_.h_step[1] = pos0 + n - 1;
     rs_.h_step[3] = 0;
     rs_.h_step[MF_STEP_FRAME] += 1;
-    const int frame = frame_base_ + (host_logits ? 6 : 5);
+    const int frame = frame_base_ + (host_logits ? (rs_.topk_k > 0 ? 8 : 6) : 5);
     const int rc = mf_begin_frame(rank_, frame);
     if (rc < 0) check(rc, "begin_frame");
     if (rc == MF_FRAME_RECORD) {
         try {
+            if (cfg_.tp_size > 1) {
+                // the tensor-parallel lm_head receives the last layer's all-reduce
+                // (exchange 2L - 1) on top of its residual; the residual is already
+                // complete, so every rank sends a zero partial
+                check(mf_allreduce((float*)mf_ptr(rs_.xb[0]), (const float*)mf_ptr(rs_.xb[1]),
+                                   (const float*)mf_ptr(rs_.zero_d), cfg_.d_model, rs_.comm, 2 * cfg_.n_layers - 1,
+                                   rs_.d_step, rs_.stream),
+                      "prefill zero all-reduce");
+            }
             layers_.back()->cuda_forward(rs_);
             check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, 16, rs_.stream), "step readback");
-            if (host_logits)
-                check(mf_copy_to_host_async(rs_.h_logits, mf_ptr(rs_.logits), cfg_.vocab_size * 4, rs_.stream),
-                      "logits readback");
+            if (host_logits) read_back_logits();
         } catch (...) {
             mf_abort_frame(rank_);
             throw;
@@ -750,17 +811,31 @@ size_t Qwen3Model::read_bytes(bool with_logits) const {
 void Qwen3Model::issue_frame(bool readback) {
     for (auto& l : layers_) l->cuda_forward(rs_);
     // the step record (greedy id) comes back with every host-driven frame;
-    // logits when asked
+    // logits (or their top-k candidates) when asked
     if (readback) check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, 16, rs_.stream), "step readback");
-    if (rs_.compute_logits && rs_.host_logits) {
-        const void* src = mf_ptr(rs_.logits);
-        if (rs_.comm) {
-            float* g = nullptr;
-            check(mf_comm_gather_ptr(rs_.comm, &g), "gather buffer");
-            src = g;  // all ranks' rows, complete when the lm_head kernel ends
-        }
-        check(mf_copy_to_host_async(rs_.h_logits, src, cfg_.vocab_size * 4, rs_.stream), "logits readback");
+    if (rs_.compute_logits && rs_.host_logits) read_back_logits();
+}
+
+void Qwen3Model::read_back_logits() {
+    const float* src = (const float*)mf_ptr(rs_.logits);
+    if (rs_.comm) {
+        float* g = nullptr;
+        check(mf_comm_gather_ptr(rs_.comm, &g), "gather buffer");
+        src = g;  // all ranks' rows, complete when the lm_head kernel ends
     }
+    if (rs_.topk_k > 0) {
+        int* ids = (int*)mf_ptr(rs_.topk_ids);
+        float* vals = (float*)mf_ptr(rs_.topk_vals);
+        check(mf_topk(src, (int)cfg_.vocab_size, rs_.topk_k, ids, vals, mf_ptr(rs_.topk_ws), rs_.topk_ws_bytes,
+                      rs_.stream),
+              "top-k candidates");
+        char* h = (char*)rs_.h_topk;
+        check(mf_copy_to_host_async(h, ids, (size_t)rs_.topk_k * 4, rs_.stream), "top-k ids readback");
+        check(mf_copy_to_host_async(h + kTopkMax * 4, vals, (size_t)rs_.topk_k * 4, rs_.stream),
+              "top-k logits readback");
+        return;
+    }
+    check(mf_copy_to_host_async(rs_.h_logits, src, cfg_.vocab_size * 4, rs_.stream), "logits readback");
 }
 
 void Qwen3Model::forward(uint32_t token, int pos, bool compute_logits, bool host_logits) {
@@ -775,7 +850,7 @@ void Qwen3Model::forward(uint32_t token, int pos, bool compute_logits, bool host
     rs_.h_step[1] = pos;
     rs_.h_step[3] = 0;
     rs_.h_step[MF_STEP_FRAME] += 1;  // every frame gets a new sequence number
-    const int frame = frame_base_ + (compute_logits ? (host_logits ? 2 : 0) : 1);
+    const int frame = frame_base_ + (compute_logits ? (host_logits ? (rs_.topk_k > 0 ? 7 : 2) : 0) : 1);
     const int rc = mf_begin_frame(rank_, frame);
     if (rc < 0) check(rc, "begin_frame");
     if (rc == MF_FRAME_RECORD) {
@@ -795,6 +870,17 @@ std::vector<uint32_t> Qwen3Model::generate(const std::vector<uint32_t>& prompt, 
     if (prompt.size() > cfg_.user_max_seq_len) throw std::runtime_error("prompt longer than max_seq_len");
     const bool greedy = sampler_->greedy();
     const bool need_host = !greedy || opt.trace;
+    // sampling needs only the top-k (id, logit) list when nothing else reads the
+    // logits and there is no presence penalty (which changes the list with every
+    // token); MF_HOST_TOPK=1 keeps the whole-vocabulary readback
+    const char* ht = std::getenv("MF_HOST_TOPK");
+    const bool cand = !greedy && !opt.trace && !margins && !opt.on_step && sampler_->penalty_pres() == 0.0f &&
+                      sampler_->top_k() <= (size_t)kTopkMax && !(ht && ht[0] == '1');
+    rs_.topk_k = cand ? (int)sampler_->top_k() : 0;
+    struct TopkReset {
+        int& k;
+        ~TopkReset() { k = 0; }
+    } topk_reset{rs_.topk_k};
     GenStats st;
     size_t model_bytes = 0, kv_bytes = 0;
     const double t0 = now_s();
@@ -818,7 +904,13 @@ std::vector<uint32_t> Qwen3Model::generate(const std::vector<uint32_t>& prompt, 
         uint32_t next;
         if (need_host) {
             const float* lg = rs_.h_logits;
-            next = sampler_->sample(lg);
+            if (cand) {
+                const char* h = (const char*)rs_.h_topk;
+                next = sampler_->sample_candidates((const uint32_t*)h, (const float*)(h + kTopkMax * 4),
+                                                   (size_t)rs_.topk_k);
+            } else {
+                next = sampler_->sample(lg);
+            }
             if (margins) {
                 float v1 = -INFINITY, v2 = -INFINITY;
                 for (size_t i = 0; i < cfg_.vocab_size; ++i) {

@@ -20,6 +20,7 @@
 namespace minfer {
 
 constexpr int kPrefillChunk = 4096;  // prompt tokens per batched-prefill pass
+constexpr int kTopkMax = 64;         // largest top_k sampled from device candidates (mf_topk)
 
 // include/minfer/base/config.hpp:22 plus the CUDA device this runtime adds
 enum class DeviceType : int { CPU = 0, METAL = 1, CUDA = 2 };
@@ -94,6 +95,12 @@ struct RunState {
     int32_t* h_step = nullptr;  // pinned {token, pos, next_token, chain}
     void* d_step = nullptr;
     float* h_logits = nullptr;  // pinned copy of the last logits (host-logit frames)
+    // sampling from device top-k candidates: k > 0 while a frame reads back k
+    // (id, logit) pairs instead of the whole vocabulary
+    int topk_k = 0;
+    mf_buf *topk_ids = nullptr, *topk_vals = nullptr, *topk_ws = nullptr;
+    size_t topk_ws_bytes = 0;
+    void* h_topk = nullptr;  // pinned: kTopkMax ids, then kTopkMax logits
     int attn_split = 1;
     int cur_pos = 0;
     uint32_t token_id = 0;
@@ -114,6 +121,10 @@ struct RunState {
     mf_buf* pf_att = nullptr;  // tensor-core attention operands (bf16 hi/lo Q, K, V^T)
     size_t pf_att_bytes = 0;
     bool pf_simt_attn = false;  // MF_PREFILL_SIMT_ATTN=1: the SIMT attention kernel instead
+    // tensor parallelism: prompt rows one bulk exchange slot holds, exchanges so far, a zero partial
+    int pf_bulk_rows = 0;
+    unsigned long long pf_epoch = 0;
+    mf_buf* zero_d = nullptr;
 };
 
 class BaseLayer {
@@ -185,6 +196,7 @@ private:
     void alloc_state();
     void alloc_prefill(int rows);
     void issue_frame(bool readback);
+    void read_back_logits();  // logits, or their top-k candidates, to pinned host memory
 
     std::string path_;
     GGUFFile file_;

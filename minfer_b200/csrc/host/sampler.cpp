@@ -27,19 +27,33 @@ uint32_t Sampler::sample(const float* logits) {
     auto by_logit = [&](size_t a, size_t b) { return logits_[a] > logits_[b]; };
     std::nth_element(idx_.begin(), idx_.begin() + p_.top_k, idx_.end(), by_logit);
     std::sort(idx_.begin(), idx_.begin() + p_.top_k, by_logit);
+    for (size_t i = 0; i < p_.top_k; ++i) probs_[i] = logits_[idx_[i]];  // candidate logits, in order
+    return pick(idx_.data(), probs_.data(), p_.top_k);
+}
 
-    size_t cut = p_.top_k;
-    const float top = logits_[idx_[0]];
+uint32_t Sampler::sample_candidates(const uint32_t* ids, const float* logits, size_t k) {
+    if (k != p_.top_k || p_.penalty_pres != 0.0f) throw std::invalid_argument("candidate list does not match top_k");
+    if (p_.temp == 0.0f) return ids[0];
+    return pick(ids, logits, k);
+}
+
+// src/base/sampler.cpp:52-117 from the sorted top-k list: softmax over the
+// top-k, top-p cut, min-p cut, temperature softmax over the kept prefix, draw.
+uint32_t Sampler::pick(const uint32_t* ids, const float* lg, size_t k) {
+    std::vector<float>& pr = pick_probs_;
+    pr.resize(k);
+    size_t cut = k;
+    const float top = lg[0];
     float acc = 0.0f;
     for (size_t i = 0; i < cut; ++i) {
-        probs_[idx_[i]] = std::exp(logits_[idx_[i]] - top);
-        acc += probs_[idx_[i]];
+        pr[i] = std::exp(lg[i] - top);
+        acc += pr[i];
     }
-    for (size_t i = 0; i < cut; ++i) probs_[idx_[i]] /= acc;
+    for (size_t i = 0; i < cut; ++i) pr[i] /= acc;
 
     acc = 0.0f;
     for (size_t i = 0; i < cut; ++i) {
-        acc += probs_[idx_[i]];
+        acc += pr[i];
         if (acc >= p_.top_p) {
             cut = i + 1;
             break;
@@ -48,7 +62,7 @@ uint32_t Sampler::sample(const float* logits) {
     if (p_.min_p > 0.0f) {
         const float thr = top + std::log(p_.min_p);
         for (size_t i = 0; i < cut; ++i) {
-            if (logits_[idx_[i]] < thr) {
+            if (lg[i] < thr) {
                 cut = i;
                 break;
             }
@@ -58,18 +72,18 @@ uint32_t Sampler::sample(const float* logits) {
 
     acc = 0.0f;
     for (size_t i = 0; i < cut; ++i) {
-        probs_[idx_[i]] = std::exp((logits_[idx_[i]] - top) / p_.temp);
-        acc += probs_[idx_[i]];
+        pr[i] = std::exp((lg[i] - top) / p_.temp);
+        acc += pr[i];
     }
-    for (size_t i = 0; i < cut; ++i) probs_[idx_[i]] /= acc;
+    for (size_t i = 0; i < cut; ++i) pr[i] /= acc;
 
     const float r = dist_(rng_);
     acc = 0.0f;
     for (size_t i = 0; i < cut; ++i) {
-        acc += probs_[idx_[i]];
-        if (acc >= r) return idx_[i];
+        acc += pr[i];
+        if (acc >= r) return ids[i];
     }
-    return idx_[cut - 1];
+    return ids[cut - 1];
 }
 
 }  // namespace minfer

@@ -31,11 +31,21 @@ public:
     explicit Sampler(const SamplerParams& p);
     void add_token(uint32_t token);
     uint32_t sample(const float* logits);
+    // The same draw from the top-k candidates alone: ids[i], logits[i] sorted by
+    // logit, largest first (ties: lower id first), k == top_k. Valid when the
+    // presence penalty is 0 (the candidates are then exactly the list sample()
+    // builds); consumes one random number like sample().
+    uint32_t sample_candidates(const uint32_t* ids, const float* logits, size_t k);
     bool greedy() const { return p_.temp == 0.0f; }
+    size_t top_k() const { return p_.top_k; }
+    float penalty_pres() const { return p_.penalty_pres; }
 
 private:
+    // top-p / min-p cuts, temperature softmax and the draw over a sorted candidate list
+    uint32_t pick(const uint32_t* ids, const float* lg, size_t k);
+
     SamplerParams p_;
-    std::vector<float> logits_, probs_;
+    std::vector<float> logits_, probs_, pick_probs_;
     std::vector<uint32_t> idx_;
     std::unordered_set<uint32_t> seen_;
     std::mt19937_64 rng_;

@@ -281,4 +281,157 @@ __global__ void __launch_bounds__(1024) allreduce_kernel(const float* partial, c
     recv_sum(c, slot, tag, x_res, tid, blockDim.x, n, deadline, &late, status, [&](int i, float v) { x_out[i] = v; });
 }
 
+// Batched-prefill all-reduce: x[i] += bulk_0[i] + ... + bulk_{T-1}[i] (rank
+// order, the same sum on every rank) over n4 float4 groups. This rank's bulk
+// slot was written by the previous kernel; CTA 0 raises this rank's flag to
+// `epoch` in every rank's region, every CTA waits until all ranks' flags show
+// it (bounded: on timeout status bit COMM_STATUS_AR_TIMEOUT), then reads the
+// peers' slots over NVLink.
+__global__ void __launch_bounds__(256) bulk_allreduce_kernel(float* __restrict__ x, size_t n4, const CommDev c, int slot,
+                                                             unsigned long long epoch) {
+    __shared__ int ok;
+    pdl_launch_dependents();
+    pdl_wait();
+    int* status = &c.local()->status;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        __threadfence_system();
+        for (int r = 0; r < c.tp_size; ++r)
+            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(c.flags(r) + c.tp_rank), "l"(epoch) : "memory");
+    }
+    if (threadIdx.x == 0) {
+        const unsigned long long deadline = globaltimer_ns() + c.timeout_ns;
+        bool late = false;
+        for (int r = 0; r < c.tp_size && !late; ++r) {
+            for (long long i = 0;; ++i) {
+                unsigned long long v;
+                asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(c.flags(c.tp_rank) + r) : "memory");
+                if (v >= epoch) break;
+                if (i >= COMM_MAX_POLLS || globaltimer_ns() > deadline) {
+                    late = true;
+                    atomicOr(status, COMM_STATUS_AR_TIMEOUT);
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        ok = !late;
+    }
+    __syncthreads();
+    if (!ok) return;  // the partials are not all there: leave x as it is (status tells the host)
+    float4* x4 = reinterpret_cast<float4*>(x);
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        float4 a = x4[i];
+        for (int r = 0; r < c.tp_size; ++r) {
+            const float4 b = __ldcv(reinterpret_cast<const float4*>(c.bulk(r, slot)) + i);
+            a.x += b.x;
+            a.y += b.y;
+            a.z += b.z;
+            a.w += b.w;
+        }
+        x4[i] = a;
+    }
+}
+
+// ---- top-k candidates for the host sampler -------------------------------
+// The k largest of x[0, n) with their indices, sorted by value (largest
+// first, equal values: lower index first; NaN counts as -inf), i.e. the list
+// the reference's sampler builds with nth_element + sort before its top-p /
+// min-p / temperature steps (src/base/sampler.cpp:40-50). Phase 1: CTA b
+// takes x[b*TOPK_CHUNK, ...) into shared memory and extracts its k best by k
+// block-wide arg-max rounds; the last CTA to finish (ticket) merges the
+// grid's k-lists the same way.
+constexpr int TOPK_MAX = 64;
+constexpr int TOPK_CHUNK = 1024;
+constexpr int TOPK_THREADS = 256;
+
+// block-wide best (value, index) of this thread's candidate; all threads get it
+MF_DEVICE void block_best(float& v, int& i, float* sv, int* si) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+        if (better(ov, oi, v, i)) {
+            v = ov;
+            i = oi;
+        }
+    }
+    __syncthreads();
+    if (lane == 0) {
+        sv[warp] = v;
+        si[warp] = i;
+    }
+    __syncthreads();
+    v = sv[0];
+    i = si[0];
+    for (int w = 1; w < TOPK_THREADS / 32; ++w)
+        if (better(sv[w], si[w], v, i)) {
+            v = sv[w];
+            i = si[w];
+        }
+}
+
+// k rounds over the m (value, index) pairs in shared memory
+MF_DEVICE void extract_topk(float* vals, int* idx, int m, int k, float* out_v, int* out_i, float* sv, int* si) {
+    for (int r = 0; r < k; ++r) {
+        float v = -INFINITY;
+        int i = 0x7fffffff, pos = -1;
+        for (int e = threadIdx.x; e < m; e += TOPK_THREADS) {
+            const int id = idx[e];
+            if (better(vals[e], id, v, i)) {
+                v = vals[e];
+                i = id;
+                pos = e;
+            }
+        }
+        int mypos = pos;
+        const int myid = i;
+        block_best(v, i, sv, si);
+        if (mypos >= 0 && myid == i) {  // the winner leaves the pool (a sentinel never wins)
+            vals[mypos] = -INFINITY;
+            idx[mypos] = 0x7fffffff;
+        }
+        if (threadIdx.x == 0) {
+            out_v[r] = v;
+            out_i[r] = i;
+        }
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(const float* __restrict__ x, int n, int k, int* out_ids,
+                                                           float* out_vals, float* cand_v, int* cand_i,
+                                                           unsigned int* counter) {
+    extern __shared__ float tk_smem[];
+    __shared__ float sv[TOPK_THREADS / 32];
+    __shared__ int si[TOPK_THREADS / 32];
+    __shared__ int is_last;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int c0 = blockIdx.x * TOPK_CHUNK, m = min(TOPK_CHUNK, n - c0);
+    float* vals = tk_smem;  // [TOPK_CHUNK] in phase 1, [gridDim.x * k] in phase 2
+    int* ids = reinterpret_cast<int*>(tk_smem + max(TOPK_CHUNK, (int)gridDim.x * k));
+    for (int e = threadIdx.x; e < m; e += TOPK_THREADS) {
+        const float v = __ldcg(x + c0 + e);
+        vals[e] = v == v ? v : -INFINITY;
+        ids[e] = c0 + e;
+    }
+    __syncthreads();
+    extract_topk(vals, ids, m, k, cand_v + (size_t)blockIdx.x * k, cand_i + (size_t)blockIdx.x * k, sv, si);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const int mc = gridDim.x * k;
+    for (int e = threadIdx.x; e < mc; e += TOPK_THREADS) {
+        vals[e] = __ldcg(cand_v + e);
+        ids[e] = __ldcg(cand_i + e);
+    }
+    __syncthreads();
+    extract_topk(vals, ids, mc, k, out_vals, out_ids, sv, si);
+    if (threadIdx.x == 0) *counter = 0;  // ready for the next launch
+}
+
 }  // namespace mf

@@ -121,6 +121,31 @@ def test_sampled_vs_oracle(Model):
     assert len(set(ref_ids.tolist())) > 1  # really sampling
 
 
+def test_sampled_from_device_candidates(Model, monkeypatch):
+    """Sampling without margins reads back only the device top-k list: the ids
+    equal the oracle's and those of the whole-vocabulary readback."""
+    Qwen3Model, RunParams = Model
+    name = "tiny-bf16"
+    path = tiny_model(name)
+    cfg = TINY[name]
+    P, G = 16, 48
+    from minfer_b200.model import random_prompt
+
+    prompt = random_prompt(P, cfg.vocab, 42)
+    kw = dict(top_k=20, temp=0.7, top_p=0.9, seed=42)
+    orc = PortModel(path, max_seq=P + G + 1, **kw)
+    ref_ids, _ = orc.generate(prompt, G)
+    runs = []
+    for host in ("0", "1"):
+        monkeypatch.setenv("MF_HOST_TOPK", host)
+        m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=P + G + 1, **kw)).set_device("cuda")
+        ids, _, _ = m.generate(prompt, G, forced=ref_ids)  # teacher-forced: one draw per oracle step
+        runs.append(list(ids))
+    assert runs[0] == runs[1]
+    mism = [i for i in range(G) if runs[0][i] != ref_ids[i]]
+    assert len(mism) <= 1, mism
+
+
 def test_chained_matches_host_loop(Model):
     Qwen3Model, RunParams = Model
     path = tiny_model("tiny-bf16")

@@ -423,3 +423,32 @@ def test_error_status(ops, gpu):
     out = torch.zeros(16, device=gpu)
     with pytest.raises(MinferError):
         ops.matmul(out, torch.zeros(15, device=gpu), torch.zeros(16 * 15, device=gpu), 0, 16, 15)  # d_in % 16
+
+
+@pytest.mark.parametrize("n,k", [(151936, 20), (151936, 64), (100, 64), (1030, 20), (5000, 1)])
+def test_topk_candidates(gpu, n, k):
+    """Device top-k (the sampler's candidate list): same ids and logits as a sort,
+    largest first, equal values by lower index; NaN never wins; two calls in a row."""
+    import ctypes as C
+
+    from minfer_b200 import ops as O
+    from minfer_b200._lib import check, cuda_lib
+
+    lib = cuda_lib()
+    g = torch.Generator(device="cpu").manual_seed(n + k)
+    x = torch.randn(n, generator=g)
+    x[n // 3] = float("nan")
+    x[7] = x[11] = x.max() + 1.0  # a tie at the top: index 7 first
+    ws_bytes = lib.mf_topk_workspace_bytes(n, k)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=gpu)
+    ids = torch.empty(k, dtype=torch.int32, device=gpu)
+    vals = torch.empty(k, dtype=torch.float32, device=gpu)
+    xd = x.to(gpu)
+    key = torch.where(torch.isnan(x), torch.tensor(float("-inf")), x).double()
+    order = sorted(range(n), key=lambda i: (-key[i].item(), i))[:k]
+    for _ in range(2):
+        check(lib.mf_topk(C.c_void_p(xd.data_ptr()), n, k, C.c_void_p(ids.data_ptr()), C.c_void_p(vals.data_ptr()),
+                          C.c_void_p(ws.data_ptr()), ws_bytes, C.c_void_p(O._stream())))
+        torch.cuda.synchronize()
+        assert ids.cpu().tolist() == order
+        assert torch.equal(vals.cpu(), x[order])

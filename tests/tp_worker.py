@@ -120,6 +120,21 @@ def check_model(name, rank, world):
         assert me.comm_status() == 0
         me.close()
     assert m.argmax() == int(np.argmax(m.logits()))
+    if cfg.n_experts == 0 and cfg.dtype == "bf16":
+        # batched prefill on the tensor cores, partials exchanged per projection
+        # (one pass, and 5-row chunks: alternating slots and cached history)
+        for chunk in (None, "5"):
+            if chunk:
+                os.environ["MF_PREFILL_CHUNK"] = chunk
+            mp = load()
+            assert mp.prefill(prompt, 0, True, True), f"{name}: batched prefill not taken"
+            err = np.max(np.abs(orc0.logits() - mp.logits()))
+            assert err <= logit_tol(cfg.dtype), f"{name}: batched-prefill logits max-abs {err} (chunk {chunk})"
+            assert mp.argmax() == int(np.argmax(mp.logits()))
+            assert same_on_all_ranks([mp.argmax()]), f"{name}: ranks disagree after batched prefill"
+            assert mp.comm_status() == 0
+            mp.close()
+            os.environ.pop("MF_PREFILL_CHUNK", None)
     # teacher-forced greedy
     ids, mg, st = m.generate(prompt, G, forced=ref_ids, margins=True)
     events = [i for i in range(G) if ids[i] != ref_ids[i]]
