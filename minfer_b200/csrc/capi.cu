@@ -236,7 +236,7 @@ void choose_shape(int K, int dtype, int ym, int* T_out, int* R_out) {
 
 int run_gemv(int dtype, int xm, int ym, mf::GemvParams& p, long long units, cudaStream_t st, int max_grid = 0) {
     static const int cps_cap = env_int("MF_GEMV_CTAS_PER_SM", 0);
-    static const int pf_tiles = env_int("MF_GEMV_PF_TILES", 2);
+    static const int pf_tiles = env_int("MF_GEMV_PF_TILES", 1);
     p.pf_tiles = pf_tiles;
     MF_REQUIRE(p.K > 0 && p.K % 16 == 0, MF_E_INVALID, "d_in must be a positive multiple of 16 (got %d)", p.K);
     MF_REQUIRE(p.rows > 0, MF_E_INVALID, "d_out must be positive");
