@@ -279,8 +279,10 @@ int mf_comm_gather_ptr(const mf_comm* c, float** logits);
 int mf_comm_bulk_ptr(const mf_comm* c, int slot, float** out);
 /* Batched-prefill all-reduce (replaces minfer's per-token exchange-free CPU
  * path, src/base/model.cpp:120-129, for tensor-parallel shards): after this
- * rank's partial is complete in bulk slot `slot`, x[i] += partial_0[i] + ...
- * + partial_{T-1}[i] in rank order on every rank. `epoch` numbers the
+ * rank's partial is complete in bulk slot `slot`, x[i] += (partial_0[i] + ...
+ * + partial_{T-1}[i]) with the sum in rank order, the same on every rank
+ * (reduce-scatter into the slots, then all-gather; the slot's contents are
+ * consumed). `epoch` numbers the
  * exchanges (1, 2, ... identical on every rank); slots must alternate between
  * consecutive exchanges. A wait that gives up sets mf_comm_status bit 1 and
  * leaves x unchanged. */

@@ -973,9 +973,16 @@ int mf_bulk_allreduce(float* x, size_t n, mf_comm* c, int slot, unsigned long lo
     long long grid = (long long)((n4 + 255) / 256);
     grid = std::min<long long>(grid, (long long)num_sms() * 4);
     const mf::CommDev dev = c->dev;
-    void* args[] = {(void*)&x, (void*)&n4, (void*)&dev, (void*)&slot, (void*)&epoch};
-    MF_CK(launch((const void*)&mf::bulk_allreduce_kernel, dim3((unsigned)grid), dim3(256), 0,
-                 mf::resolve_stream(stream), args));
+    cudaStream_t st = mf::resolve_stream(stream);
+    // flags rise by two per exchange: partial complete, then reduced slice complete
+    unsigned long long f1 = 2 * epoch - 1, f2 = 2 * epoch;
+    {
+        const long long g1 = std::max<long long>(1, std::min<long long>(grid / dev.tp_size + 1, grid));
+        void* args[] = {(void*)&n4, (void*)&dev, (void*)&slot, (void*)&f1};
+        MF_CK(launch((const void*)&mf::bulk_reduce_kernel, dim3((unsigned)g1), dim3(256), 0, st, args));
+    }
+    void* args[] = {(void*)&x, (void*)&n4, (void*)&dev, (void*)&slot, (void*)&f2};
+    MF_CK(launch((const void*)&mf::bulk_gather_kernel, dim3((unsigned)grid), dim3(256), 0, st, args));
     return MF_OK;
 }
 

@@ -281,22 +281,24 @@ __global__ void __launch_bounds__(1024) allreduce_kernel(const float* partial, c
     recv_sum(c, slot, tag, x_res, tid, blockDim.x, n, deadline, &late, status, [&](int i, float v) { x_out[i] = v; });
 }
 
-// Batched-prefill all-reduce: x[i] += bulk_0[i] + ... + bulk_{T-1}[i] (rank
-// order, the same sum on every rank) over n4 float4 groups. This rank's bulk
-// slot was written by the previous kernel; CTA 0 raises this rank's flag to
-// `epoch` in every rank's region, every CTA waits until all ranks' flags show
-// it (bounded: on timeout status bit COMM_STATUS_AR_TIMEOUT), then reads the
-// peers' slots over NVLink.
-__global__ void __launch_bounds__(256) bulk_allreduce_kernel(float* __restrict__ x, size_t n4, const CommDev c, int slot,
-                                                             unsigned long long epoch) {
-    __shared__ int ok;
-    pdl_launch_dependents();
-    pdl_wait();
+// Batched-prefill all-reduce of the [rows, d] partials in the ranks' bulk
+// slots, as reduce-scatter + all-gather over NVLink (each rank reads
+// 2 (T-1)/T of a partial instead of T-1 partials):
+//  * bulk_reduce_kernel: rank r raises its flag to `flag` in every rank's
+//    region (its partial is complete: the previous kernel wrote it), waits
+//    for every rank's flag, then sums slice r of all ranks' partials in rank
+//    order into slice r of its own slot;
+//  * bulk_gather_kernel: raises its flag to `flag` again (its reduced slice is
+//    complete), waits for every rank's, then x += the reduced slices, each
+//    read from the rank that owns it. Every rank adds the same values.
+// Waits are bounded (on timeout: status bit COMM_STATUS_AR_TIMEOUT, and the
+// kernel leaves its output alone).
+MF_DEVICE bool bulk_signal_wait(const CommDev& c, unsigned long long flag, int* ok_s) {
     int* status = &c.local()->status;
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         __threadfence_system();
         for (int r = 0; r < c.tp_size; ++r)
-            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(c.flags(r) + c.tp_rank), "l"(epoch) : "memory");
+            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(c.flags(r) + c.tp_rank), "l"(flag) : "memory");
     }
     if (threadIdx.x == 0) {
         const unsigned long long deadline = globaltimer_ns() + c.timeout_ns;
@@ -305,7 +307,7 @@ __global__ void __launch_bounds__(256) bulk_allreduce_kernel(float* __restrict__
             for (long long i = 0;; ++i) {
                 unsigned long long v;
                 asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(c.flags(c.tp_rank) + r) : "memory");
-                if (v >= epoch) break;
+                if (v >= flag) break;
                 if (i >= COMM_MAX_POLLS || globaltimer_ns() > deadline) {
                     late = true;
                     atomicOr(status, COMM_STATUS_AR_TIMEOUT);
@@ -314,21 +316,61 @@ __global__ void __launch_bounds__(256) bulk_allreduce_kernel(float* __restrict__
                 __nanosleep(64);
             }
         }
-        ok = !late;
+        *ok_s = !late;
     }
     __syncthreads();
-    if (!ok) return;  // the partials are not all there: leave x as it is (status tells the host)
-    float4* x4 = reinterpret_cast<float4*>(x);
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
-        float4 a = x4[i];
-        for (int r = 0; r < c.tp_size; ++r) {
+    return *ok_s != 0;
+}
+
+// float4 groups [lo, hi) of rank r's slice
+MF_DEVICE void bulk_slice(size_t n4, int r, int T, size_t& lo, size_t& hi) {
+    lo = n4 * (size_t)r / (size_t)T;
+    hi = n4 * (size_t)(r + 1) / (size_t)T;
+}
+
+__global__ void __launch_bounds__(256) bulk_reduce_kernel(size_t n4, const CommDev c, int slot,
+                                                          unsigned long long flag) {
+    __shared__ int ok;
+    pdl_launch_dependents();
+    pdl_wait();
+    if (!bulk_signal_wait(c, flag, &ok)) return;
+    size_t lo, hi;
+    bulk_slice(n4, c.tp_rank, c.tp_size, lo, hi);
+    float4* own = reinterpret_cast<float4*>(c.bulk(c.tp_rank, slot));
+    for (size_t i = lo + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < hi; i += (size_t)gridDim.x * blockDim.x) {
+        float4 a = __ldcv(reinterpret_cast<const float4*>(c.bulk(0, slot)) + i);
+        for (int r = 1; r < c.tp_size; ++r) {
             const float4 b = __ldcv(reinterpret_cast<const float4*>(c.bulk(r, slot)) + i);
             a.x += b.x;
             a.y += b.y;
             a.z += b.z;
             a.w += b.w;
         }
-        x4[i] = a;
+        own[i] = a;
+    }
+}
+
+__global__ void __launch_bounds__(256) bulk_gather_kernel(float* __restrict__ x, size_t n4, const CommDev c, int slot,
+                                                          unsigned long long flag) {
+    __shared__ int ok;
+    pdl_launch_dependents();
+    pdl_wait();
+    if (!bulk_signal_wait(c, flag, &ok)) return;
+    float4* x4 = reinterpret_cast<float4*>(x);
+    for (int r = 0; r < c.tp_size; ++r) {
+        size_t lo, hi;
+        bulk_slice(n4, r, c.tp_size, lo, hi);
+        const float4* src = reinterpret_cast<const float4*>(c.bulk(r, slot));
+        for (size_t i = lo + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < hi;
+             i += (size_t)gridDim.x * blockDim.x) {
+            const float4 b = __ldcv(src + i);
+            float4 a = x4[i];
+            a.x += b.x;
+            a.y += b.y;
+            a.z += b.z;
+            a.w += b.w;
+            x4[i] = a;
+        }
     }
 }
 
