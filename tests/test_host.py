@@ -174,6 +174,15 @@ def test_ops_validate_before_touching_the_device():
     msg = C.create_string_buffer(256)
     lib.mf_last_error(msg, 256)
     assert b"scratch too small" in msg.value
+    # device top-k: k limits and workspace size are checked on the host
+    assert lib.mf_topk_workspace_bytes(151936, 20) == 256 + 149 * 20 * 8
+    assert lib.mf_topk(fake, 151936, 65, fake, fake, fake, 1 << 20, None) == MF_E_INVALID
+    assert lib.mf_topk(fake, 10, 20, fake, fake, fake, 1 << 20, None) == MF_E_INVALID
+    assert lib.mf_topk(fake, 151936, 20, fake, fake, fake, 100, None) == MF_E_INVALID
+    # bulk exchange: arguments checked before any device work
+    assert lib.mf_bulk_allreduce(None, 16, None, 0, 1, None) == MF_E_INVALID
+    assert lib.mf_bulk_allreduce(fake, 16, None, 2, 1, None) == MF_E_INVALID
+    assert lib.mf_comm_bulk_ptr(None, 0, C.byref(C.c_void_p())) == MF_E_INVALID
     assert lib.mf_prefill_attention_tc(*args, C.c_void_p((1 << 20) + 16), need.value, None) == MF_E_INVALID
     assert lib.mf_prefill_attention_tc(*args[:6], 300, *args[7:], fake, need.value, None) == MF_E_INVALID
     assert lib.mf_lm_head(None, None, None, 1e-6, None, 2, 10, 16, 0, None, None, None) == MF_E_INVALID
