@@ -17,6 +17,7 @@
 #include <map>
 #include <memory>
 #include <mutex>
+#include <thread>
 #include <set>
 #include <string>
 #include <vector>
@@ -78,6 +79,11 @@ struct Rank {
     cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
     int recording = -1;  // frame id being captured
     int pending = -1;    // frame id to launch at end_frame
+    // pinned staging ring for large host -> device copies (weights from the model file's mapping)
+    void* stage[4] = {};
+    cudaEvent_t stage_ev[4] = {};
+    bool stage_ready = false;
+    std::shared_ptr<std::mutex> stage_mu = std::make_shared<std::mutex>();
 };
 
 struct Ctx {
@@ -340,6 +346,10 @@ int mf_shutdown(void) {
         if (r.stream) cudaStreamDestroy(r.stream);
         if (r.h_step) cudaFreeHost(r.h_step);
         if (r.d_step) cudaFree(r.d_step);
+        for (int i = 0; i < 4; ++i) {
+            if (r.stage[i]) cudaFreeHost(r.stage[i]);
+            if (r.stage_ev[i]) cudaEventDestroy(r.stage_ev[i]);
+        }
     }
     for (mf_buf* b : g.bufs) {
         cudaSetDevice(g.ranks[b->rank].device);
@@ -381,13 +391,73 @@ int mf_alloc(size_t bytes, int rank, mf_buf** out) {
     return MF_OK;
 }
 
+// Host -> device copy of a large pageable range (typically a tensor inside the
+// model file's mapping) through a ring of pinned staging buffers: host threads
+// fill one buffer while the copy engine drains the previous ones, so reading
+// the mapping and the PCIe transfer overlap. Small copies go directly.
+constexpr size_t STAGE_BYTES = 32u << 20;
+constexpr int STAGE_SLOTS = 4;
+constexpr int STAGE_THREADS = 4;
+constexpr size_t STAGE_MIN = 8u << 20;
+
+static void parallel_memcpy(char* dst, const char* src, size_t n) {
+    const size_t part = (n + STAGE_THREADS - 1) / STAGE_THREADS;
+    std::thread th[STAGE_THREADS - 1];
+    int nt = 0;
+    for (int t = 1; t < STAGE_THREADS; ++t) {
+        const size_t o = (size_t)t * part;
+        if (o >= n) break;
+        const size_t len = std::min(part, n - o);
+        th[nt++] = std::thread([=] { std::memcpy(dst + o, src + o, len); });
+    }
+    std::memcpy(dst, src, std::min(part, n));
+    for (int t = 0; t < nt; ++t) th[t].join();
+}
+
+static int h2d(Rank& r, char* dst, const char* src, size_t bytes) {
+    if (bytes >= STAGE_MIN) {
+        std::lock_guard<std::mutex> lk(*r.stage_mu);
+        if (!r.stage_ready) {
+            bool ok = true;
+            for (int i = 0; i < STAGE_SLOTS && ok; ++i)
+                ok = cudaHostAlloc(&r.stage[i], STAGE_BYTES, cudaHostAllocPortable) == cudaSuccess &&
+                     cudaEventCreateWithFlags(&r.stage_ev[i], cudaEventDisableTiming) == cudaSuccess;
+            if (!ok) {
+                cudaGetLastError();
+                for (int i = 0; i < STAGE_SLOTS; ++i) {
+                    if (r.stage[i]) cudaFreeHost(r.stage[i]);
+                    if (r.stage_ev[i]) cudaEventDestroy(r.stage_ev[i]);
+                    r.stage[i] = nullptr;
+                    r.stage_ev[i] = nullptr;
+                }
+            }
+            r.stage_ready = ok;
+        }
+        if (r.stage_ready) {
+            size_t off = 0;
+            for (int k = 0; off < bytes; ++k) {
+                const size_t n = std::min(STAGE_BYTES, bytes - off);
+                const int slot = k % STAGE_SLOTS;
+                MF_CK(cudaEventSynchronize(r.stage_ev[slot]));  // this buffer's previous copy is done
+                parallel_memcpy((char*)r.stage[slot], src + off, n);
+                MF_CK(cudaMemcpyAsync(dst + off, r.stage[slot], n, cudaMemcpyHostToDevice, r.stream));
+                MF_CK(cudaEventRecord(r.stage_ev[slot], r.stream));
+                off += n;
+            }
+            MF_CK(cudaStreamSynchronize(r.stream));
+            return MF_OK;
+        }
+    }
+    MF_CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, r.stream));
+    MF_CK(cudaStreamSynchronize(r.stream));
+    return MF_OK;
+}
+
 int mf_upload(const void* host, size_t bytes, int rank, mf_buf** out) {
     MF_REQUIRE(host, MF_E_INVALID, "null host pointer");
     int rc = alloc_impl(bytes, rank, out);
     if (rc) return rc;
-    MF_CK(cudaMemcpyAsync((*out)->ptr, host, bytes, cudaMemcpyHostToDevice, g.ranks[rank].stream));
-    MF_CK(cudaStreamSynchronize(g.ranks[rank].stream));
-    return MF_OK;
+    return h2d(g.ranks[rank], (char*)(*out)->ptr, (const char*)host, bytes);
 }
 
 void mf_release(mf_buf* buf) {
@@ -417,9 +487,7 @@ int mf_write(mf_buf* buf, size_t offset, const void* host, size_t bytes) {
     MF_REQUIRE(offset + bytes <= buf->bytes, MF_E_INVALID, "write past the end of the buffer");
     Rank& r = g.ranks[buf->rank];
     MF_CK(cudaSetDevice(r.device));
-    MF_CK(cudaMemcpyAsync((char*)buf->ptr + offset, host, bytes, cudaMemcpyHostToDevice, r.stream));
-    MF_CK(cudaStreamSynchronize(r.stream));
-    return MF_OK;
+    return h2d(r, (char*)buf->ptr + offset, (const char*)host, bytes);
 }
 
 int mf_write_2d(mf_buf* buf, size_t offset, size_t dst_pitch, const void* host, size_t src_pitch, size_t width,
