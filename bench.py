@@ -172,7 +172,7 @@ def time_dominant_kernel(cfg, peaks, iters: int = 20) -> dict:
     prof = ROOT / "profiles" / "gemv_swiglu_qwen3-8b.txt"
     if prof.exists():
         for line in prof.read_text().splitlines():
-            if line.startswith("dram_bytes_per_launch:"):
+            if line.strip().startswith("dram_bytes_per_launch:"):
                 traffic = float(line.split(":")[1])
     return {"kernel": "gemv_kernel<W_BF16,...,X_NORM,Y_SWIGLU> (gate/up + SiLU, one layer)",
             "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -207,6 +207,7 @@ def run_reference_cpu(path: str, ctx: int, steps: int, warmup: int, threads: int
     from oracle import oracle_py
 
     with tempfile.TemporaryDirectory() as td:
+        arch = oracle_py.ref_binary()[1]
         if oracle_py.ref_available():
             res = oracle_py.run_reference(path, f"{td}/r", bench_context=ctx, bench_steps=steps,
                                           bench_warmup=warmup, threads=threads, timeout=1800)
@@ -221,17 +222,103 @@ def run_reference_cpu(path: str, ctx: int, steps: int, warmup: int, threads: int
                     ts.append(time.perf_counter() - t0)
             res = {"tok_per_s": len(ts) / sum(ts), "seconds": sum(ts)}
             kind = "port"
+            arch = "-march=x86-64-v3 (oracle restatement)"
     return {"value": res["tok_per_s"], "unit": "tokens/s", "cores": threads, "kind": kind,
             "sample": f"{steps} decode tokens (+{warmup} warm-up) at context {ctx} on the same GGUF, "
                       f"KV rows below the context zero-filled, OMP_NUM_THREADS={threads}",
-            "seconds": res["seconds"]}
+            "seconds": res["seconds"], "omp_num_threads": threads, "host": host_cpu(),
+            "build": f"g++ 13 -O3 {arch} -fopenmp; the reference's NEON GEMVs as 128-bit FMA/F16C/SSE ops"}
+
+
+PARITY_PROMPT = 64  # prompt tokens of the multi-GPU parity check
+PARITY_GEN = 16  # greedy ids compared
+MARGIN_TOL = 1e-4  # a step whose top-2 logit gap (single-GPU side) is below this may flip
+
+
+def tp_parity(m, path: str, prompt, info, rank: int, world: int, local_rank: int) -> dict:
+    """Greedy ids of the sharded model against a single-GPU run of the whole
+    model on rank 0's GPU, for the first PARITY_PROMPT prompt ids. Rank 0
+    decodes free-running (ids and top-2 logit margins); every rank then
+    decodes teacher-forced on those ids. An id may differ only where the
+    single-GPU margin is below MARGIN_TOL, and every rank must produce the
+    same ids. Runs after the timed regions (it rewrites the KV cache)."""
+    import torch.distributed as dist
+
+    from minfer_b200 import model as mm
+
+    p = prompt[:PARITY_PROMPT]
+    ref = [None, None]
+    if rank == 0:
+        single = mm.Qwen3Model(path, mm.RunParams(num_iters=PARITY_GEN, max_seq_len=len(p) + PARITY_GEN + 1),
+                               device=local_rank).set_device("cuda")
+        ids, mg, _ = single.generate(p, PARITY_GEN, margins=True)
+        ref = [[int(v) for v in ids], [float(v) for v in mg]]
+        single.close()
+        del single
+    box = [ref]
+    dist.broadcast_object_list(box, src=0)
+    ref_ids, ref_mg = box[0]
+    ids, _, _ = m.generate(p, PARITY_GEN, forced=np.array(ref_ids, np.uint32))
+    ids = [int(v) for v in ids]
+    every = [None] * world
+    dist.all_gather_object(every, ids)
+    same = all(e == every[0] for e in every)
+    events = [i for i, (a, b) in enumerate(zip(ids, ref_ids)) if a != b]
+    bad = [i for i in events if ref_mg[i] >= MARGIN_TOL]
+    return {"ok": same and not bad, "ids_same_on_all_ranks": same, "compared": len(ref_ids),
+            "prompt_tokens": len(p), "tolerance_events": events, "mismatches": bad,
+            "min_margin": round(min(ref_mg), 6) if ref_mg else None,
+            "ids": ids, "against": "single-GPU decode of the whole model (teacher-forced, margin rule)"}
+
+
+def host_cpu() -> dict:
+    """The host's CPU as lscpu reports it (model, sockets, physical cores,
+    logical CPUs), the CPUs this process may run on, the cgroup CPU quota and
+    the RAM. `threads` = physical cores, capped by the CPUs the process may use
+    (more OpenMP threads than usable CPUs only time-slice)."""
+    info = {"model": None, "sockets": None, "cores_per_socket": None, "threads_per_core": None, "logical": None}
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        keys = {"Model name": "model", "Socket(s)": "sockets", "Core(s) per socket": "cores_per_socket",
+                "Thread(s) per core": "threads_per_core", "CPU(s)": "logical"}
+        for line in out.splitlines():
+            k, _, v = line.partition(":")
+            if k.strip() in keys and info[keys[k.strip()]] is None:
+                v = v.strip()
+                info[keys[k.strip()]] = int(v) if v.isdigit() else v
+    except (OSError, subprocess.SubprocessError):
+        pass
+    phys = None
+    if isinstance(info["sockets"], int) and isinstance(info["cores_per_socket"], int):
+        phys = info["sockets"] * info["cores_per_socket"]
+    info["physical_cores"] = phys
+    try:
+        usable = len(os.sched_getaffinity(0))
+    except AttributeError:
+        usable = os.cpu_count() or 1
+    info["usable_cpus"] = usable
+    quota = None
+    try:
+        q, per = Path("/sys/fs/cgroup/cpu.max").read_text().split()
+        if q != "max":
+            quota = round(int(q) / int(per), 2)
+    except (OSError, ValueError):
+        pass
+    info["cgroup_cpu_quota"] = quota
+    try:
+        info["ram_gb"] = round(os.sysconf("SC_PAGE_SIZE") * os.sysconf("SC_PHYS_PAGES") / 1e9, 1)
+    except (ValueError, OSError):
+        info["ram_gb"] = None
+    t = phys or usable
+    t = min(t, usable)
+    if quota:
+        t = min(t, max(1, int(quota)))
+    info["threads"] = max(1, t)
+    return info
 
 
 def host_threads() -> int:
-    try:
-        return len(os.sched_getaffinity(0))
-    except AttributeError:
-        return os.cpu_count() or 1
+    return host_cpu()["threads"]
 
 
 def main():
@@ -243,7 +330,7 @@ def main():
     ap.add_argument("--workload", default="qwen3-8b-bf16", choices=sorted(CONFIGS))
     ap.add_argument("--context", type=int, default=4096, help="prompt tokens prefilled before decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-steps", type=int, default=6)
+    ap.add_argument("--cpu-steps", type=int, default=16)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local_rank = dist_env()
@@ -357,6 +444,11 @@ def main():
     e2e_ms = max_over_ranks(ms.value)
     e2e = args.steps / (e2e_ms / 1e3)
 
+    # ---- multi-GPU correctness: the sharded decode vs a single-GPU decode of
+    # the same prompt (margin rule), then every rank's exchange status
+    status = m.comm_status()
+    parity = tp_parity(m, path, prompt, info, rank, world, local_rank) if world > 1 else None
+
     peaks, peak_kind = load_peaks()
     prefill_max_s = max_over_ranks(prefill_s)
     ctx_mid = ctx + args.warmup + args.steps // 2
@@ -370,12 +462,18 @@ def main():
         dist.all_reduce(t)
         tb = t.item()
     step_gbs = tb / (dev_ms / args.steps / 1e3) / 1e9 / world  # per GPU
-    status = m.comm_status()
+    status = max(status, m.comm_status())
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([status], device="cuda", dtype=torch.int32)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        status = int(t.item())
     roof = time_dominant_kernel(cfgshape, peaks) if rank == 0 else None
 
     if rank == 0:
         cpu = None
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:  # rank 0 at N=1 only (other ranks would compete for cores)
             try:
                 cpu = run_reference_cpu(path, ctx, args.cpu_steps, 1, host_threads())
             except Exception as e:  # reported, not fatal
@@ -398,12 +496,18 @@ def main():
         if world > 1:
             line["tp"] = {"size": world, "exchange_status": status,
                           "note": "hbm_roofline.achieved_gbs is per GPU; bytes_per_token summed over ranks"}
+            line["parity_ok"] = bool(parity["ok"]) and status == 0
+            line["exchange_status"] = status
+            line["parity"] = parity
         print(json.dumps(line), flush=True)
+    failed = world > 1 and not (parity["ok"] and status == 0)
     if world > 1:
         import torch.distributed as dist
 
         dist.barrier()
         dist.destroy_process_group()
+    if failed:
+        sys.exit(3)
 
 
 if __name__ == "__main__":

@@ -133,6 +133,7 @@ int mf_timer_stop(int rank, float* ms);
  * matching device pointer. */
 #define MF_STEP_RECORD_BYTES 32
 #define MF_STEP_FRAME 4 /* index of the frame field */
+#define MF_STEP_STATUS 5 /* exchange status bits (mf_comm_status), written by the tensor-parallel lm_head */
 int mf_step_state(int rank, int32_t** host, void** device);
 
 /* ===================================================================== */

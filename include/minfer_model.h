@@ -105,6 +105,12 @@ int mf_model_argmax(const mf_model* m, uint32_t* out);
 int mf_model_generate(mf_model* m, const uint32_t* prompt, size_t n_prompt, size_t n_gen, int flags,
                       const uint32_t* forced, uint32_t* out_ids, size_t* n_out, float* margins,
                       mf_gen_stats* stats);
+/* The same, also copying the logits the id of step steps[i] was drawn from
+ * (step 0 = the first generated id) into logits_out[i * vocab_size ...] for
+ * i < n_steps (the logits are then read back every step). */
+int mf_model_generate_logits(mf_model* m, const uint32_t* prompt, size_t n_prompt, size_t n_gen, int flags,
+                             const uint32_t* forced, uint32_t* out_ids, size_t* n_out, float* margins,
+                             mf_gen_stats* stats, const size_t* steps, size_t n_steps, float* logits_out);
 #define MF_GEN_STOP_AT_EOS 1
 #define MF_GEN_MARGINS 2
 #define MF_GEN_TOKEN_PREFILL 4 /* prefill token by token (the reference's loop) instead of batched */
@@ -138,6 +144,15 @@ int mf_model_x(const mf_model* m, float* x);
  * advances between draws). No GPU involved. */
 int mf_sample(const float* logits, size_t vocab, const mf_run_params* rp, const uint32_t* seen, size_t n_seen,
               size_t n_draws, uint32_t* out);
+
+/* The draw generate() makes when a frame reads back only the device's top-k
+ * candidates (mf_topk: the top_k + 1 largest logits, largest first, equal
+ * values lower index first): Sampler::sample_candidates on that list, or the
+ * whole-vocabulary Sampler::sample when two of those values are equal (their
+ * order in the reference's nth_element + sort list is the library's). The
+ * candidate list is built here on the host in the device's order; n_draws
+ * draws, the RNG advancing between them; no presence penalty. No GPU involved. */
+int mf_sample_candidates(const float* logits, size_t vocab, const mf_run_params* rp, size_t n_draws, uint32_t* out);
 
 /* Prompt ids as BaseModel::benchmark draws them (src/base/model.cpp:189-193):
  * std::mt19937(seed) + std::uniform_int_distribution<>(0, vocab-1). */

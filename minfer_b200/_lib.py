@@ -182,6 +182,7 @@ HOST_API = {
     "mf_model_logits": (I, [P, P, SZ]),
     "mf_model_argmax": (I, [P, P]),
     "mf_model_generate": (I, [P, P, SZ, SZ, I, P, P, P, P, P]),
+    "mf_model_generate_logits": (I, [P, P, SZ, SZ, I, P, P, P, P, P, P, SZ, P]),
     "mf_model_decode_chained": (I, [P, U32, I, I, P]),
     "mf_model_reset_sampler": (I, [P]),
     "mf_model_experts": (I, [P, I, P, P]),
@@ -189,6 +190,7 @@ HOST_API = {
     "mf_model_x": (I, [P, P]),
     "mf_random_prompt": (I, [I, U32, SZ, P]),
     "mf_sample": (I, [P, SZ, P, P, SZ, SZ, P]),
+    "mf_sample_candidates": (I, [P, SZ, P, SZ, P]),
 }
 
 _cuda = None

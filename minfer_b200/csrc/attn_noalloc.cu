@@ -14,7 +14,10 @@
 // Properties a caller must know:
 //  * The first call on a device looks up the array's device address
 //    (cudaGetSymbolAddress, with that device current) and caches it; make that
-//    first call before any stream capture on the device.
+//    first call before any stream capture on the device. The cache is tied to
+//    the device's context: after the context is destroyed and re-created
+//    (cudaDeviceReset), the next call looks the address up again, so make
+//    that call, too, outside any stream capture.
 //  * The array is shared by every call. It keeps the last call's contents;
 //    the completion counters are cleared at the start of each call on the
 //    caller's stream. Calls whose executions overlap on the GPU (different
@@ -23,6 +26,7 @@
 //  * A request whose scratch would exceed MF_ATTN_NOALLOC_SCRATCH_BYTES is
 //    rejected with MF_E_UNSUPPORTED; nothing is launched.
 //  * It calls no cudaMalloc, cudaFree or other allocating routine.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -44,19 +48,39 @@ static __device__ __align__(256) unsigned char g_attn_scratch[MF_ATTN_NOALLOC_SC
 
 int noalloc_fail(int code, const char* msg) { return mf::record_error(code, msg); }
 
-// Device address of g_attn_scratch for the current device (looked up once).
+// Device address of g_attn_scratch for the current device, looked up once per
+// device and context: a context destroyed and re-created on the device (for
+// example after cudaDeviceReset) gets the array at a new address, so the cached
+// address is keyed on the context that was current when it was taken.
 int scratch_address(void** out) {
     static std::mutex mu;
     static void* addr[64] = {nullptr};
+    static CUcontext owner[64] = {nullptr};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return noalloc_fail(MF_E_CUDA, "no usable current device");
+    // the driver's cuCtxGetCurrent, a query (resolved through the runtime, so the
+    // library does not link the driver library directly)
+    static CUresult (*ctx_current)(CUcontext*) = nullptr;
     std::lock_guard<std::mutex> lk(mu);
-    if (!addr[dev]) {
+    if (!ctx_current) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+            return noalloc_fail(MF_E_CUDA, "cuCtxGetCurrent is not available");
+        ctx_current = (CUresult(*)(CUcontext*))fn;
+    }
+    // NULL before the runtime first touched the device on this thread
+    CUcontext ctx = nullptr;
+    if (ctx_current(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+    if (!addr[dev] || !ctx || owner[dev] != ctx) {
         void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_scratch);
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_scratch);  // makes the device's context current
         if (e != cudaSuccess) return noalloc_fail(MF_E_CUDA, cudaGetErrorString(e));
+        if (ctx_current(&ctx) != CUDA_SUCCESS || !ctx) return noalloc_fail(MF_E_CUDA, "no current CUDA context");
         addr[dev] = p;
+        owner[dev] = ctx;
     }
     *out = addr[dev];
     return MF_OK;

@@ -457,7 +457,12 @@ int mf_upload(const void* host, size_t bytes, int rank, mf_buf** out) {
     MF_REQUIRE(host, MF_E_INVALID, "null host pointer");
     int rc = alloc_impl(bytes, rank, out);
     if (rc) return rc;
-    return h2d(g.ranks[rank], (char*)(*out)->ptr, (const char*)host, bytes);
+    rc = h2d(g.ranks[rank], (char*)(*out)->ptr, (const char*)host, bytes);
+    if (rc) {  // the caller gets no buffer on failure: release it here
+        mf_release(*out);
+        *out = nullptr;
+    }
+    return rc;
 }
 
 void mf_release(mf_buf* buf) {
@@ -1008,12 +1013,11 @@ int mf_topk(const float* x, int n, int k, int* ids, float* vals, void* workspace
     const int grid = (n + mf::TOPK_CHUNK - 1) / mf::TOPK_CHUNK;
     const size_t smem = 2 * (size_t)std::max(mf::TOPK_CHUNK, grid * k) * sizeof(float);
     MF_REQUIRE(smem <= 200 * 1024, MF_E_UNSUPPORTED, "n * k too large for one merge CTA");
-    static std::mutex mu;
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        MF_CK(cudaFuncSetAttribute((const void*)&mf::topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)smem));
-    }
+    // the shared-memory opt-in only ever grows (per device), so a concurrent
+    // call with a smaller request cannot lower it under this launch
+    int bps = 0;
+    int rc = prepare((const void*)&mf::topk_kernel, mf::TOPK_THREADS, smem, &bps);
+    if (rc) return rc;
     unsigned int* counter = (unsigned int*)workspace;
     float* cand_v = (float*)((char*)workspace + 256);
     int* cand_i = (int*)(cand_v + (size_t)grid * k);

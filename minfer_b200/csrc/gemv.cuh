@@ -549,6 +549,10 @@ __global__ void __launch_bounds__(T, (XM == X_AR_NORM && MF_GEMV_MIN_BLOCKS < 2)
                             fi = i;
                         }
                     }
+                    // every wait of this frame is behind us (earlier kernels, this
+                    // kernel's CTAs before their tickets, the exchange above): the
+                    // host reads the sticky status bits with the step record
+                    p.step[MF_STEP_STATUS] = *(volatile int*)status;
                 }
                 // greedy id -> next_token; a chained record also becomes the
                 // next step's input so decode can continue without the host

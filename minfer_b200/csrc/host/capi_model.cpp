@@ -1,8 +1,10 @@
 // extern "C" surface of the host runtime (include/minfer_model.h).
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
 #include <random>
+#include <vector>
 #include <stdexcept>
 
 #include "minfer_model.h"
@@ -23,6 +25,8 @@ int herr(int code, const char* msg) {
 #define MF_TRY(body)                                   \
     try {                                              \
         body;                                          \
+    } catch (const minfer::WaitTimeout& e) {       \
+        return herr(MF_E_TIMEOUT, e.what());           \
     } catch (const std::bad_alloc&) {                  \
         return herr(MF_E_OOM, "host allocation failed"); \
     } catch (const std::invalid_argument& e) {         \
@@ -157,14 +161,29 @@ int mf_model_argmax(const mf_model* m, uint32_t* out) {
 int mf_model_generate(mf_model* m, const uint32_t* prompt, size_t n_prompt, size_t n_gen, int flags,
                       const uint32_t* forced, uint32_t* out_ids, size_t* n_out, float* margins,
                       mf_gen_stats* stats) {
+    return mf_model_generate_logits(m, prompt, n_prompt, n_gen, flags, forced, out_ids, n_out, margins, stats,
+                                    nullptr, 0, nullptr);
+}
+
+int mf_model_generate_logits(mf_model* m, const uint32_t* prompt, size_t n_prompt, size_t n_gen, int flags,
+                             const uint32_t* forced, uint32_t* out_ids, size_t* n_out, float* margins,
+                             mf_gen_stats* stats, const size_t* steps, size_t n_steps, float* logits_out) {
     if (!m || !prompt || !out_ids || !n_out) return herr(MF_E_INVALID, "null argument");
+    if (n_steps && (!steps || !logits_out)) return herr(MF_E_INVALID, "steps and logits_out are required");
     g_host_err[0] = 0;
     MF_TRY({
         minfer::Qwen3Model::GenOptions o;
         o.stop_at_eos = (flags & MF_GEN_STOP_AT_EOS) != 0;
         o.batched_prefill = (flags & MF_GEN_TOKEN_PREFILL) == 0;
-        o.trace = (flags & MF_GEN_MARGINS) != 0;
+        o.trace = (flags & MF_GEN_MARGINS) != 0 || n_steps > 0;
         o.forced = forced;
+        if (n_steps) {
+            const size_t V = m->m->config().vocab_size;
+            o.on_step = [=](size_t step, const float* lg, uint32_t) {
+                for (size_t i = 0; i < n_steps; ++i)
+                    if (steps[i] == step && lg) std::memcpy(logits_out + i * V, lg, V * sizeof(float));
+            };
+        }
         std::vector<uint32_t> pr(prompt, prompt + n_prompt);
         minfer::GenStats st;
         std::vector<float> mg;
@@ -241,6 +260,34 @@ int mf_sample(const float* logits, size_t vocab, const mf_run_params* rp, const 
         minfer::Sampler smp(sp);
         for (size_t i = 0; i < n_seen; ++i) smp.add_token(seen[i]);
         for (size_t i = 0; i < n_draws; ++i) out[i] = smp.sample(logits);
+    });
+    return MF_OK;
+}
+
+int mf_sample_candidates(const float* logits, size_t vocab, const mf_run_params* rp, size_t n_draws, uint32_t* out) {
+    if (!logits || !rp || !out || vocab == 0) return herr(MF_E_INVALID, "bad arguments");
+    if (rp->penalty_pres != 0.0f || rp->top_k + 1 > vocab) return herr(MF_E_INVALID, "needs top_k < vocab, no penalty");
+    MF_TRY({
+        minfer::SamplerParams sp;
+        sp.vocab_size = vocab;
+        sp.top_k = rp->top_k;
+        sp.temp = rp->temp;
+        sp.top_p = rp->top_p;
+        sp.min_p = rp->min_p;
+        sp.seed = rp->seed;
+        minfer::Sampler smp(sp);
+        // the device's list: value descending, equal values lower index first
+        const size_t n = rp->top_k + 1;
+        std::vector<uint32_t> idx(vocab);
+        for (size_t i = 0; i < vocab; ++i) idx[i] = (uint32_t)i;
+        std::partial_sort(idx.begin(), idx.begin() + n, idx.end(), [&](uint32_t a, uint32_t b) {
+            return logits[a] > logits[b] || (logits[a] == logits[b] && a < b);
+        });
+        std::vector<float> vals(n);
+        for (size_t i = 0; i < n; ++i) vals[i] = logits[idx[i]];
+        const bool decisive = minfer::Sampler::candidates_decisive(vals.data(), n);
+        for (size_t i = 0; i < n_draws; ++i)
+            out[i] = decisive ? smp.sample_candidates(idx.data(), vals.data(), rp->top_k) : smp.sample(logits);
     });
     return MF_OK;
 }

@@ -754,10 +754,10 @@ bool Qwen3Model::prefill(const uint32_t* tokens, int n, int pos0, bool compute_l
     }
     int st = 0;
     check(mf_prefill_status(&st, 1), "prefill status");
-    if (st) throw std::runtime_error("a prefill kernel wait gave up (status " + std::to_string(st) + ")");
+    if (st) throw WaitTimeout("a prefill kernel wait gave up (status " + std::to_string(st) + ")");
     if (rs_.comm) {
         check(mf_comm_status(rs_.comm, &st, 0), "exchange status");
-        if (st) throw std::runtime_error("a prefill exchange wait gave up (status " + std::to_string(st) + ")");
+        if (st) throw WaitTimeout("a prefill exchange wait gave up (status " + std::to_string(st) + ")");
     }
     // the last token's residual row feeds the decode lm_head (under tensor
     // parallelism the lm_head adds an all-reduce to it: see below)
@@ -788,7 +788,7 @@ bool Qwen3Model::prefill(const uint32_t* tokens, int n, int pos0, bool compute_l
                       "prefill zero all-reduce");
             }
             layers_.back()->cuda_forward(rs_);
-            check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, 16, rs_.stream), "step readback");
+            check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, kStepReadback, rs_.stream), "step readback");
             if (host_logits) read_back_logits();
         } catch (...) {
             mf_abort_frame(rank_);
@@ -796,6 +796,7 @@ bool Qwen3Model::prefill(const uint32_t* tokens, int n, int pos0, bool compute_l
         }
     }
     check(mf_end_frame(rank_), "end_frame");
+    check_exchange_status();
     return true;
 }
 
@@ -812,7 +813,7 @@ void Qwen3Model::issue_frame(bool readback) {
     for (auto& l : layers_) l->cuda_forward(rs_);
     // the step record (greedy id) comes back with every host-driven frame;
     // logits (or their top-k candidates) when asked
-    if (readback) check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, 16, rs_.stream), "step readback");
+    if (readback) check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, kStepReadback, rs_.stream), "step readback");
     if (rs_.compute_logits && rs_.host_logits) read_back_logits();
 }
 
@@ -836,6 +837,25 @@ void Qwen3Model::read_back_logits() {
         return;
     }
     check(mf_copy_to_host_async(rs_.h_logits, src, cfg_.vocab_size * 4, rs_.stream), "logits readback");
+}
+
+void Qwen3Model::check_exchange_status() const {
+    if (!rs_.comm) return;
+    const int st = rs_.h_step[MF_STEP_STATUS];
+    if (st != 0)
+        throw WaitTimeout("a tensor-parallel exchange wait gave up (status " + std::to_string(st) +
+                              "): a peer rank did not arrive in time; this frame's results are invalid");
+}
+
+void Qwen3Model::read_full_logits() {
+    const float* src = (const float*)mf_ptr(rs_.logits);
+    if (rs_.comm) {
+        float* g = nullptr;
+        check(mf_comm_gather_ptr(rs_.comm, &g), "gather buffer");
+        src = g;
+    }
+    check(mf_copy_to_host_async(rs_.h_logits, src, cfg_.vocab_size * 4, rs_.stream), "logits readback");
+    check(mf_sync(rank_), "sync");
 }
 
 void Qwen3Model::forward(uint32_t token, int pos, bool compute_logits, bool host_logits) {
@@ -862,6 +882,7 @@ void Qwen3Model::forward(uint32_t token, int pos, bool compute_logits, bool host
         }
     }
     check(mf_end_frame(rank_), "end_frame");
+    if (compute_logits) check_exchange_status();  // the tensor-parallel lm_head reports the frame's waits
 }
 
 std::vector<uint32_t> Qwen3Model::generate(const std::vector<uint32_t>& prompt, size_t n_gen, const GenOptions& opt,
@@ -875,8 +896,9 @@ std::vector<uint32_t> Qwen3Model::generate(const std::vector<uint32_t>& prompt, 
     // token); MF_HOST_TOPK=1 keeps the whole-vocabulary readback
     const char* ht = std::getenv("MF_HOST_TOPK");
     const bool cand = !greedy && !opt.trace && !margins && !opt.on_step && sampler_->penalty_pres() == 0.0f &&
-                      sampler_->top_k() <= (size_t)kTopkMax && !(ht && ht[0] == '1');
-    rs_.topk_k = cand ? (int)sampler_->top_k() : 0;
+                      sampler_->top_k() < (size_t)kTopkMax && !(ht && ht[0] == '1');
+    // one candidate beyond top_k shows whether the k-th logit is tied with the next
+    rs_.topk_k = cand ? (int)sampler_->top_k() + 1 : 0;
     struct TopkReset {
         int& k;
         ~TopkReset() { k = 0; }
@@ -906,8 +928,14 @@ std::vector<uint32_t> Qwen3Model::generate(const std::vector<uint32_t>& prompt, 
             const float* lg = rs_.h_logits;
             if (cand) {
                 const char* h = (const char*)rs_.h_topk;
-                next = sampler_->sample_candidates((const uint32_t*)h, (const float*)(h + kTopkMax * 4),
-                                                   (size_t)rs_.topk_k);
+                const float* vals = (const float*)(h + kTopkMax * 4);
+                if (Sampler::candidates_decisive(vals, (size_t)rs_.topk_k)) {
+                    next = sampler_->sample_candidates((const uint32_t*)h, vals, sampler_->top_k());
+                } else {
+                    // equal logits among the candidates: the whole vocabulary decides
+                    read_full_logits();
+                    next = sampler_->sample(lg);
+                }
             } else {
                 next = sampler_->sample(lg);
             }
@@ -982,6 +1010,7 @@ uint32_t Qwen3Model::decode_chained(uint32_t token, int start_pos, int n) {
     check(mf_sync(rank_), "sync");
     const uint32_t last = (uint32_t)rs_.h_step[2];
     rs_.h_step[3] = 0;
+    check_exchange_status();
     return last;
 }
 

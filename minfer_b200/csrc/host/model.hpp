@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <functional>
 #include <memory>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -21,6 +22,16 @@ namespace minfer {
 
 constexpr int kPrefillChunk = 4096;  // prompt tokens per batched-prefill pass
 constexpr int kTopkMax = 64;         // largest top_k sampled from device candidates (mf_topk)
+// step-record bytes read back after a host-driven frame: token, pos, next_token,
+// chain, frame and the exchange status (MF_STEP_STATUS)
+constexpr size_t kStepReadback = 24;
+
+// A bounded wait on the device gave up (a tensor-parallel exchange whose peer
+// did not arrive, or a prefill kernel's pipeline wait): the results of that
+// work are invalid. The C ABI reports it as MF_E_TIMEOUT.
+struct WaitTimeout : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
 
 // include/minfer/base/config.hpp:22 plus the CUDA device this runtime adds
 enum class DeviceType : int { CPU = 0, METAL = 1, CUDA = 2 };
@@ -197,6 +208,9 @@ private:
     void alloc_prefill(int rows);
     void issue_frame(bool readback);
     void read_back_logits();  // logits, or their top-k candidates, to pinned host memory
+    void read_full_logits();  // the last frame's logits to pinned host memory, synchronously
+    // throws WaitTimeout when the step record read back last carries exchange status bits
+    void check_exchange_status() const;
 
     std::string path_;
     GGUFFile file_;

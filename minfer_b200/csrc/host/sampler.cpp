@@ -37,6 +37,12 @@ uint32_t Sampler::sample_candidates(const uint32_t* ids, const float* logits, si
     return pick(ids, logits, k);
 }
 
+bool Sampler::candidates_decisive(const float* vals, size_t n) {
+    for (size_t i = 0; i + 1 < n; ++i)
+        if (!(vals[i] != vals[i + 1])) return false;  // equal (or NaN): order undefined
+    return true;
+}
+
 // src/base/sampler.cpp:52-117 from the sorted top-k list: softmax over the
 // top-k, top-p cut, min-p cut, temperature softmax over the kept prefix, draw.
 uint32_t Sampler::pick(const uint32_t* ids, const float* lg, size_t k) {

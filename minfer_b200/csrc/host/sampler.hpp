@@ -36,6 +36,13 @@ public:
     // presence penalty is 0 (the candidates are then exactly the list sample()
     // builds); consumes one random number like sample().
     uint32_t sample_candidates(const uint32_t* ids, const float* logits, size_t k);
+    // Whether a candidate list decides the draw on its own. `vals` holds the
+    // top_k + 1 largest logits, largest first. sample() orders equal logits
+    // the way nth_element + sort leaves them, which a list built with another
+    // tie rule need not reproduce; so any two equal values among them (inside
+    // the top-k, or the k-th equal to the next one, which makes the top-k set
+    // itself ambiguous) mean the whole-vocabulary sample() must decide.
+    static bool candidates_decisive(const float* vals, size_t n);
     bool greedy() const { return p_.temp == 0.0f; }
     size_t top_k() const { return p_.top_k; }
     float penalty_pres() const { return p_.penalty_pres; }

@@ -49,9 +49,20 @@ class Qwen3Shape:
     context_length: int = 40960
     seed: int = 0
     std: float = 0.02
+    # layers of the model whose random streams this file follows (0: n_layers).
+    # A file with n_layers < rng_layers is the depth-reduced prefix of that
+    # model: the same embedding, layers 0..n_layers-1 and lm_head weights.
+    rng_layers: int = 0
 
     def with_(self, **kw) -> "Qwen3Shape":
         return dataclasses.replace(self, **kw)
+
+    def prefix(self, n_layers: int) -> "Qwen3Shape":
+        """The first n_layers decoder layers of this model, with its embedding,
+        final norm and lm_head (the same weights, drawn from the same streams)."""
+        if not 1 <= n_layers <= self.n_layers:
+            raise ValueError("prefix depth outside [1, n_layers]")
+        return dataclasses.replace(self, n_layers=n_layers, rng_layers=self.rng_layers or self.n_layers)
 
     @property
     def moe(self) -> bool:
@@ -238,6 +249,17 @@ def tensor_plan(cfg: Qwen3Shape) -> list[tuple[str, tuple[int, ...], str]]:
     return plan
 
 
+def rng_index(cfg: Qwen3Shape, plan_index: int) -> int:
+    """Random-stream index of the tensor at plan_index: its index in the plan of
+    the model with rng_layers layers (tensors after the decoder layers shift)."""
+    full = cfg.rng_layers or cfg.n_layers
+    if full == cfg.n_layers:
+        return plan_index
+    per = (len(tensor_plan(cfg)) - 2 - (0 if cfg.tied else 1)) // cfg.n_layers
+    first_after = 1 + cfg.n_layers * per
+    return plan_index if plan_index < first_after else plan_index + (full - cfg.n_layers) * per
+
+
 def _is_norm(name: str) -> bool:
     return name.endswith("_norm.weight")
 
@@ -343,7 +365,7 @@ def write_qwen3_gguf(path: str | os.PathLike, cfg: Qwen3Shape, chunk_elems: int 
             esz = _DTYPE_SIZE[dt]
             for c_idx, start in enumerate(range(0, n, chunk_elems)):
                 m = min(chunk_elems, n - start)
-                jobs.append((fd, data0 + o + start * esz, cfg.seed, t_idx, c_idx, m, dt, cfg.std))
+                jobs.append((fd, data0 + o + start * esz, cfg.seed, rng_index(cfg, t_idx), c_idx, m, dt, cfg.std))
         nthreads = threads or min(32, os.cpu_count() or 4)
         with cf.ThreadPoolExecutor(max_workers=nthreads) as ex:
             for f in [ex.submit(_fill_chunk, *j) for j in jobs]:

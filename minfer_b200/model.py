@@ -146,7 +146,9 @@ class Qwen3Model:
 
     # -- BaseModel::generate (ids in, ids out)
     def generate(self, prompt, n_gen: int, stop_at_eos: bool = False, forced=None, margins: bool = False,
-                 token_prefill: bool = False):
+                 token_prefill: bool = False, logits_at=None):
+        """Ids (and margins, stats). With `logits_at` (a list of step numbers)
+        a fourth result holds the logits each of those steps drew from."""
         prompt = np.ascontiguousarray(prompt, dtype=np.uint32)
         out = np.zeros(n_gen, dtype=np.uint32)
         mg = np.zeros(n_gen, dtype=np.float32)
@@ -155,12 +157,18 @@ class Qwen3Model:
         flags = ((MF_GEN_STOP_AT_EOS if stop_at_eos else 0) | (MF_GEN_MARGINS if margins else 0) |
                  (MF_GEN_TOKEN_PREFILL if token_prefill else 0))
         forced_arr = None if forced is None else np.ascontiguousarray(forced, dtype=np.uint32)
-        check(self._lib.mf_model_generate(self._h, prompt.ctypes.data, prompt.size, n_gen, flags,
-                                          None if forced_arr is None else forced_arr.ctypes.data, out.ctypes.data,
-                                          C.byref(n_out), mg.ctypes.data, C.byref(st)))
+        steps = np.ascontiguousarray(logits_at if logits_at is not None else [], dtype=np.uintp)
+        lg = np.zeros((steps.size, self.vocab_size), dtype=np.float32)
+        check(self._lib.mf_model_generate_logits(self._h, prompt.ctypes.data, prompt.size, n_gen, flags,
+                                                 None if forced_arr is None else forced_arr.ctypes.data,
+                                                 out.ctypes.data, C.byref(n_out), mg.ctypes.data, C.byref(st),
+                                                 steps.ctypes.data if steps.size else None, steps.size,
+                                                 lg.ctypes.data if steps.size else None))
         n = n_out.value
         stats = GenStats(st.num_tokens_gen, st.ttft, st.throughput, st.prefill_time, st.bandwidth,
                          st.decode_seconds, st.bytes_read)
+        if logits_at is not None:
+            return out[:n], (mg[:n] if margins else None), stats, lg
         return out[:n], (mg[:n] if margins else None), stats
 
     def decode_chained(self, token: int, start_pos: int, n: int) -> int:

@@ -23,6 +23,8 @@ HERE = Path(__file__).resolve().parent
 PORT_LIB = HERE / "_build" / "liboracle.so"
 REF_OPS_LIB = HERE / "_ref" / "libminfer_ref_ops.so"
 REF_RUN = HERE / "_ref" / "minfer_ref_run"
+REF_RUN_NATIVE = HERE / "_ref" / "minfer_ref_run_native"  # -march=native of the build machine
+REF_NATIVE_FLAGS = HERE / "_ref" / "native_flags.txt"  # that machine's CPU flags
 
 P, I, U32, SZ, F = C.c_void_p, C.c_int, C.c_uint32, C.c_size_t, C.c_float
 
@@ -221,12 +223,32 @@ class PortModel:
         return out[:n], mg[:n]
 
 
+def ref_binary() -> tuple[Path, str]:
+    """The reference token-loop build to run here and its arch flags: the
+    -march=native build when this CPU has every flag of the machine it was
+    built on (so every instruction it may use exists here), else x86-64-v3."""
+    try:
+        want = set(REF_NATIVE_FLAGS.read_text().split())
+        have = set()
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    have = set(line.split(":", 1)[1].split())
+                    break
+        if REF_RUN_NATIVE.exists() and want and want <= have:
+            return REF_RUN_NATIVE, "-march=native (this CPU's flags include the build machine's)"
+    except OSError:
+        pass
+    return REF_RUN, "-march=x86-64-v3"
+
+
 def run_reference(model: str, out_prefix: str, *, prompt=None, random_prompt: int = 0, prompt_seed: int = 0,
                   gen: int = 8, max_seq: int = 0, temp: float = 0.0, top_k: int = 1, top_p: float = 1.0,
                   min_p: float = 0.0, pres: float = 0.0, seed: int = 0, dump_logits=(), threads: int | None = None,
                   bench_context: int = -1, bench_steps: int = 0, bench_warmup: int = 0, timeout: float = 3600):
     """Run the reference's own CPU token loop (minfer_ref_run) and load its dump."""
-    args = [str(REF_RUN), str(model), "--out", out_prefix, "--gen", str(gen), "--temp", str(temp), "--top-k",
+    binary, _ = ref_binary()
+    args = [str(binary), str(model), "--out", out_prefix, "--gen", str(gen), "--temp", str(temp), "--top-k",
             str(top_k), "--top-p", str(top_p), "--min-p", str(min_p), "--pres", str(pres), "--seed", str(seed)]
     if prompt is not None:
         pf = out_prefix + ".prompt.u32"

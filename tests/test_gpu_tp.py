@@ -76,3 +76,32 @@ def test_exchange_wait_times_out(gpu, monkeypatch):
         assert y == 3 * n
     finally:
         lib.mf_comm_destroy(comm)
+
+
+def test_model_timeout_is_an_error(gpu, monkeypatch):
+    """A model-level frame whose exchange wait gave up fails with MF_E_TIMEOUT
+    (forward, chained decode, generate) instead of returning ids: rank 0 of a
+    2-rank model is connected to a peer that never sends (its own handle in
+    the peer's place)."""
+    from conftest import tiny_model
+    from minfer_b200 import model as mm
+    from minfer_b200._lib import MF_E_TIMEOUT, MinferError
+
+    monkeypatch.setenv("MF_COMM_TIMEOUT_MS", "50")
+    m = mm.Qwen3Model(tiny_model("tiny-tp8"), mm.RunParams(num_iters=4, max_seq_len=16), tp_rank=0,
+                      tp_size=2).set_device("cuda")
+    h = m.comm_handle()
+    m.comm_connect([h, h])
+    with pytest.raises(MinferError) as e:
+        m.forward(3, 0, True, False)
+    assert e.value.code == MF_E_TIMEOUT, e.value
+    assert m.comm_status() != 0  # the bits stay readable (and are cleared by reading them)
+    with pytest.raises(MinferError) as e:
+        m.decode_chained(3, 1, 2)
+    assert e.value.code == MF_E_TIMEOUT, e.value
+    with pytest.raises(MinferError) as e:
+        m.generate(np.array([1, 2, 3], np.uint32), 2, token_prefill=True)
+    assert e.value.code == MF_E_TIMEOUT, e.value
+    m.close()
+    # the device is still usable
+    assert (torch.ones(8, device=gpu) * 2).sum().item() == 16

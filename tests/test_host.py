@@ -148,6 +148,60 @@ def test_sampler_matches_oracle(temp, top_k, top_p, min_p, pres):
         assert set(ref) == {5}  # first maximum
 
 
+@pytest.mark.parametrize("case", ["inside", "boundary", "none"])
+def test_candidate_sampling_with_tied_logits(case):
+    """generate() samples from the device's top-k list (equal logits lower id
+    first) only when no two of its top_k + 1 values are equal; otherwise the
+    whole-vocabulary sampler decides. Either way the ids equal the reference
+    sampler's (nth_element + sort) on the same logits."""
+    V, k = 1024, 20
+    rng = np.random.default_rng({"inside": 1, "boundary": 2, "none": 3}[case])
+    logits = (rng.standard_normal(V) * 2).astype(np.float32)
+    order = np.argsort(-logits, kind="stable")
+    if case == "inside":  # ties among the top-k: ids 900 and 3 share the 2nd value
+        logits[900] = logits[3] = logits[order[1]]
+    elif case == "boundary":  # the k-th and (k+1)-th logits are equal
+        logits[order[k]] = logits[order[k - 1]]
+    rp = mf_run_params(0, 64, k, 0.9, 0.95, 0.0, 0.0, 42)
+    n = 256
+    got = np.zeros(n, np.uint32)
+    assert host_lib().mf_sample_candidates(logits.ctypes.data, V, C.byref(rp), n, got.ctypes.data) == MF_OK
+    ref = np.zeros(n, np.uint32)
+    assert host_lib().mf_sample(logits.ctypes.data, V, C.byref(rp), None, 0, n, ref.ctypes.data) == MF_OK
+    assert got.tolist() == ref.tolist()
+
+
+def test_prefix_gguf_shares_the_full_models_weights(tmp_path):
+    """A depth-reduced prefix file holds the same embedding, layers and lm_head
+    as the first layers of the full model (same random streams)."""
+    from minfer_b200.gguf_synth import Qwen3Shape, write_qwen3_gguf
+
+    full = Qwen3Shape(4, 64, 2, 1, 32, 64, 300, "bf16", False, seed=5)
+    a = write_qwen3_gguf(tmp_path / "full.gguf", full)
+    b = write_qwen3_gguf(tmp_path / "pre.gguf", full.prefix(2))
+
+    # tensor data is the file's tail, tensors in plan order at ALIGN-aligned offsets
+    def raw(path, cfg):
+        from minfer_b200.gguf_synth import ALIGN, _DTYPE_SIZE, tensor_plan
+        data = open(path, "rb").read()
+        plan = tensor_plan(cfg)
+        sizes = [int(np.prod(sh)) * _DTYPE_SIZE[dt] for _, sh, dt in plan]
+        tail = 0
+        for sz in sizes:
+            tail = (tail + sz + ALIGN - 1) // ALIGN * ALIGN
+        data0 = len(data) - tail
+        out, off = {}, 0
+        for (name, _, _), sz in zip(plan, sizes):
+            out[name] = data[data0 + off:data0 + off + sz]
+            off = (off + sz + ALIGN - 1) // ALIGN * ALIGN
+        return out
+
+    ra, rb = raw(a, full), raw(b, full.prefix(2))
+    for name in rb:
+        assert ra[name] == rb[name], name
+    assert "blk.3.attn_q.weight" in ra and "blk.3.attn_q.weight" not in rb
+
+
 def test_sampler_rejects_bad_params():
     logits = np.zeros(16, np.float32)
     out = np.zeros(1, np.uint32)
