@@ -141,6 +141,17 @@ class RefOps(_Ops):
         return out
 
 
+def uniform_draws(seed: int, n: int) -> np.ndarray:
+    """The first n random numbers the reference's Sampler draws with this seed
+    (one per sampled token)."""
+    lib = C.CDLL(str(PORT_LIB))
+    lib.orc_uniform_draws.restype = None
+    lib.orc_uniform_draws.argtypes = [I, SZ, P]
+    out = np.zeros(n, np.float32)
+    lib.orc_uniform_draws(seed, n, _ptr(out))
+    return out
+
+
 def port_available() -> bool:
     return PORT_LIB.exists()
 

@@ -559,6 +559,15 @@ uint32_t orc_sample(orc_model* m, const float* logits) {
     return m->sidx[cut - 1];
 }
 
+// The first n numbers Sampler::sample draws: std::uniform_real_distribution<float>
+// (0, 1) over std::mt19937_64(seed), one per sampled token
+// (src/base/sampler.cpp:21-22, include/minfer/base/sampler.hpp:23-24).
+void orc_uniform_draws(int seed, size_t n, float* out) {
+    std::mt19937_64 rng(seed);
+    std::uniform_real_distribution<float> dist(0.0f, 1.0f);
+    for (size_t i = 0; i < n; ++i) out[i] = dist(rng);
+}
+
 // BaseModel::generate loop without the tokenizer (src/base/model.cpp:119-173),
 // EOS ignored. out_ids[n_gen]; margins[n_gen] (top-1 minus top-2 logit of the
 // logits each id was sampled from; may be NULL).

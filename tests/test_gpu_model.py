@@ -101,8 +101,37 @@ def test_logits_and_kv_vs_oracle(Model, name):
         np.testing.assert_allclose(v, vo, rtol=1e-4, atol=1e-5)
 
 
+def oracle_sampled(path, prompt, G, kw):
+    """The oracle's sampled ids and, per step, its top_k + 1 largest logits."""
+    from sampling_rule import top_candidates
+
+    P = len(prompt)
+    orc = PortModel(path, max_seq=P + G + 1, **kw)
+    for i, t in enumerate(prompt):
+        orc.forward(int(t), i, i == P - 1)
+    for t in prompt:
+        orc.add_token(int(t))
+    ids, cands = [], []
+    for g in range(G):
+        lg = orc.logits()
+        cands.append(top_candidates(lg, kw["top_k"] + 1))
+        nxt = orc.sample(lg)
+        ids.append(nxt)
+        orc.add_token(nxt)
+        orc.forward(nxt, P + g, True)
+    return np.array(ids, np.uint32), cands
+
+
+SAMPLED = dict(top_k=20, temp=0.7, top_p=0.9, seed=42)  # the sampled workload's settings
+
+
 def test_sampled_vs_oracle(Model):
-    """Temperature 0.7, top-k 20, top-p 0.9, seed 42 (the sampled workload's settings)."""
+    """Temperature 0.7, top-k 20, top-p 0.9, seed 42: teacher-forced on the
+    oracle's ids, every id equals the oracle's unless the flip rule
+    (tests/sampling_rule.py) explains it by the logits' error."""
+    from oracle.oracle_py import uniform_draws
+    from sampling_rule import check_sampled
+
     Qwen3Model, RunParams = Model
     name = "tiny-bf16"
     path = tiny_model(name)
@@ -111,19 +140,21 @@ def test_sampled_vs_oracle(Model):
     from minfer_b200.model import random_prompt
 
     prompt = random_prompt(P, cfg.vocab, 42)
-    kw = dict(top_k=20, temp=0.7, top_p=0.9, seed=42)
-    orc = PortModel(path, max_seq=P + G + 1, **kw)
-    ref_ids, ref_mg = orc.generate(prompt, G)
-    m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=P + G + 1, **kw)).set_device("cuda")
-    ids, mg, _ = m.generate(prompt, G, forced=ref_ids, margins=True)
-    mism = [i for i in range(G) if ids[i] != ref_ids[i]]
-    assert len(mism) <= 1, mism
+    ref_ids, cands = oracle_sampled(path, prompt, G, SAMPLED)
+    m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=P + G + 1, **SAMPLED)).set_device("cuda")
+    ids, _, _, lg = m.generate(prompt, G, forced=ref_ids, logits_at=list(range(G)))
+    flips = check_sampled(ids, ref_ids, cands, lg, 20, 0.7, 0.9, 0.0, uniform_draws(42, G), name)
+    assert len(flips) <= 1, flips
     assert len(set(ref_ids.tolist())) > 1  # really sampling
 
 
 def test_sampled_from_device_candidates(Model, monkeypatch):
-    """Sampling without margins reads back only the device top-k list: the ids
-    equal the oracle's and those of the whole-vocabulary readback."""
+    """Sampling without logits requested reads back only the device top-k
+    list: the ids equal those of the whole-vocabulary readback, and the
+    oracle's under the flip rule."""
+    from oracle.oracle_py import uniform_draws
+    from sampling_rule import check_sampled
+
     Qwen3Model, RunParams = Model
     name = "tiny-bf16"
     path = tiny_model(name)
@@ -132,18 +163,18 @@ def test_sampled_from_device_candidates(Model, monkeypatch):
     from minfer_b200.model import random_prompt
 
     prompt = random_prompt(P, cfg.vocab, 42)
-    kw = dict(top_k=20, temp=0.7, top_p=0.9, seed=42)
-    orc = PortModel(path, max_seq=P + G + 1, **kw)
-    ref_ids, _ = orc.generate(prompt, G)
+    ref_ids, cands = oracle_sampled(path, prompt, G, SAMPLED)
     runs = []
     for host in ("0", "1"):
         monkeypatch.setenv("MF_HOST_TOPK", host)
-        m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=P + G + 1, **kw)).set_device("cuda")
+        m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=P + G + 1, **SAMPLED)).set_device("cuda")
         ids, _, _ = m.generate(prompt, G, forced=ref_ids)  # teacher-forced: one draw per oracle step
         runs.append(list(ids))
     assert runs[0] == runs[1]
-    mism = [i for i in range(G) if runs[0][i] != ref_ids[i]]
-    assert len(mism) <= 1, mism
+    m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=P + G + 1, **SAMPLED)).set_device("cuda")
+    _, _, _, lg = m.generate(prompt, G, forced=ref_ids, logits_at=list(range(G)))
+    flips = check_sampled(runs[0], ref_ids, cands, lg, 20, 0.7, 0.9, 0.0, uniform_draws(42, G), name)
+    assert len(flips) <= 1, flips
 
 
 def test_chained_matches_host_loop(Model):

@@ -322,6 +322,32 @@ def test_attn_decode(ops, orc, gpu, H, Hkv, pos, split):
     assert ws[:Hkv].abs().sum().item() == 0  # counters back to zero
 
 
+@pytest.mark.parametrize("H,Hkv,pos", [(32, 8, 4095), (32, 8, 32767), (64, 8, 32767), (32, 4, 32767)])
+def test_attn_decode_long_context(ops, orc, gpu, H, Hkv, pos):
+    """Decode attention at the benchmarked contexts (the 8B shape at 4096, the
+    32B shape at a full 32K cache, the 30B-A3B head layout) against the oracle."""
+    D, S = 128, pos + 1
+    rng = np.random.default_rng(H * 7 + pos)
+    qkv = rng.standard_normal((H + 2 * Hkv) * D).astype(np.float32)
+    qn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    kc_hist = rng.standard_normal((S, Hkv, D), dtype=np.float32)
+    vc_hist = rng.standard_normal((S, Hkv, D), dtype=np.float32)
+    rope = ops.rope_table(S, D, 1e6)
+    kc = T(np.ascontiguousarray(kc_hist.transpose(1, 0, 2)), gpu)
+    vc = T(np.ascontiguousarray(vc_hist.transpose(1, 0, 2)), gpu)
+    n_split = ops.attn_default_split(Hkv, S)
+    ws = torch.zeros(ops.attn_workspace_bytes(H, Hkv, D, n_split) // 4 + 1, dtype=torch.int32, device=gpu)
+    st = torch.tensor([0, pos, 0, 0, 0, 0, 0, 0], dtype=torch.int32, device=gpu)
+    out = torch.zeros(H * D, device=gpu)
+    ops.attn_decode(T(qkv, gpu), T(qn, gpu), T(kn, gpu), 1e-6, rope.to(gpu), kc, vc, S, st, out, H, Hkv, D, n_split, ws)
+    ref, kref, vref = _attn_reference(orc, qkv, qn, kn, 1e-6, rope, kc_hist, vc_hist, pos, H, Hkv, D)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=2e-5, atol=2e-5)
+    np.testing.assert_allclose(kc[:, pos, :].cpu().numpy(), kref, rtol=2e-6, atol=2e-6)
+    np.testing.assert_array_equal(vc[:, pos, :].cpu().numpy(), vref)
+    assert ws[:Hkv].abs().sum().item() == 0
+
+
 def test_attn_decode_position_out_of_range(ops, gpu):
     # a step record whose position has no cache row: nothing is written, the output is zero
     D, S, H, Hkv = 128, 64, 8, 2

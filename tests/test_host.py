@@ -171,6 +171,25 @@ def test_candidate_sampling_with_tied_logits(case):
     assert got.tolist() == ref.tolist()
 
 
+def test_sampling_rule_rebuilds_the_reference_draw():
+    """The sampling distribution the flip rule of the GPU tests rebuilds
+    (tests/sampling_rule.py), with the reference's random numbers
+    (oracle uniform_draws), picks exactly the reference sampler's ids."""
+    from oracle.oracle_py import uniform_draws
+    from sampling_rule import pick, sampling_cdf
+
+    V, n = 4096, 200
+    for seed, (temp, top_k, top_p, min_p) in enumerate([(0.7, 20, 0.9, 0.0), (1.0, 40, 0.95, 0.05), (0.5, 5, 1.0, 0.0)]):
+        logits = (np.random.default_rng(seed).standard_normal(V) * 2).astype(np.float32)
+        rp = mf_run_params(0, 64, top_k, temp, top_p, min_p, 0.0, 42 + seed)
+        ref = np.zeros(n, np.uint32)
+        assert host_lib().mf_sample(logits.ctypes.data, V, C.byref(rp), None, 0, n, ref.ctypes.data) == MF_OK
+        order = np.argsort(-logits, kind="stable")[:top_k]
+        cdf, _, _ = sampling_cdf(logits[order], temp, top_p, min_p)
+        r = uniform_draws(42 + seed, n)
+        assert [pick(order, cdf, x) for x in r] == ref.tolist()
+
+
 def test_prefix_gguf_shares_the_full_models_weights(tmp_path):
     """A depth-reduced prefix file holds the same embedding, layers and lm_head
     as the first layers of the full model (same random streams)."""
