@@ -42,7 +42,7 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-from minfer_b200.gguf_synth import CONFIGS, ensure_gguf  # noqa: E402
+from minfer_b200.gguf_synth import CONFIGS, ensure_gguf, ensure_gguf_ranks  # noqa: E402
 
 METRIC = "decode tokens/s (batch 1) and % HBM roofline at 1/2/4/8 B200; prefill tok/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
@@ -77,14 +77,16 @@ def model_path(workload: str) -> Path:
 
 
 def prepare_model(workload: str, rank: int, world: int):
+    """The workload's synthetic GGUF (written once; with several ranks every
+    rank draws a share of the weights)."""
     path = model_path(workload)
     cfg = CONFIGS[workload]
-    if rank == 0:
-        ensure_gguf(path, cfg)
     if world > 1:
         import torch.distributed as dist
 
-        dist.barrier()
+        ensure_gguf_ranks(path, cfg, rank, world, dist.barrier)
+    else:
+        ensure_gguf(path, cfg)
     return str(path), cfg
 
 
@@ -271,6 +273,119 @@ def tp_parity(m, path: str, prompt, info, rank: int, world: int, local_rank: int
             "ids": ids, "against": "single-GPU decode of the whole model (teacher-forced, margin rule)"}
 
 
+def llama_bench_record(m, batched: bool) -> dict:
+    """BaseModel::benchmark's numbers (pp512 then tg128 of random ids, each
+    tg step one host-driven frame) from this runtime."""
+    st = m.benchmark(token_prefill=not batched)
+    return {"pp512_seconds": round(st.prefill_time, 4), "tg128_tok_per_s": round(st.throughput, 2),
+            "bandwidth_gbs": round(st.bandwidth, 1),
+            "prefill": "batched tensor-core prefill" if batched else "token by token, as the reference",
+            "note": "the reference's formula: bytes it counts (lm_head every step) / (pp + tg time)"}
+
+
+def llama_bench_main(args) -> None:
+    """The reference's own published loop (README tg128 rows) on one model:
+    this runtime (batched and token-by-token pp512) next to the reference's
+    CPU build running BaseModel::benchmark unchanged. Seed 30, 4096-token cache."""
+    import torch
+
+    from minfer_b200 import model as mm
+    from oracle import oracle_py
+
+    torch.cuda.set_device(0)
+    mm.init(1, [0])
+    path, cfg = prepare_model(args.workload, 0, 1)
+    rp = mm.RunParams(num_iters=128, max_seq_len=4096, seed=30)
+    m = mm.Qwen3Model(path, rp).set_device("cuda")
+    ours = llama_bench_record(m, True)
+    ours_tok = llama_bench_record(m, False)
+    line = {"metric": "tg128 tokens/s (BaseModel::benchmark: pp512 + tg128, seed 30)", "workload": args.workload,
+            "unit": "tokens/s", "value": ours["tg128_tok_per_s"], "minfer_b200": ours,
+            "minfer_b200_token_prefill": ours_tok}
+    if oracle_py.ref_available():
+        thr = host_threads()
+        with tempfile.TemporaryDirectory() as td:
+            r = oracle_py.run_reference(path, f"{td}/r", llama_bench=True, seed=30, max_seq=4096, threads=thr,
+                                        timeout=1800)
+        line["reference_cpu"] = {"pp512_seconds": round(r["prefill_time"], 3),
+                                 "tg128_tok_per_s": round(r["throughput"], 3), "bandwidth_gbs": round(r["bandwidth"], 2),
+                                 "omp_num_threads": thr, "build": oracle_py.ref_binary()[1]}
+    print(json.dumps(line), flush=True)
+
+
+def measure_long_context(workload: str, ctx: int, steps: int, warmup: int, rank: int, world: int, local_rank: int,
+                         peaks: dict) -> dict:
+    """Decode of a second workload at a long context, the same way as the main
+    line (batched prefill of a random prompt, chained greedy decode timed with
+    CUDA events, max over ranks): tokens/s and the HBM roofline fraction per
+    GPU, prefill tokens/s, exchange status."""
+    import torch
+
+    from minfer_b200 import model as mm
+    from minfer_b200 import tp
+    from minfer_b200._lib import check, cuda_lib
+
+    lib = cuda_lib()
+    t0 = time.perf_counter()
+    path, cfg = prepare_model(workload, rank, world)
+    t_gen = time.perf_counter() - t0
+    n_tok = warmup + steps + 4
+    t0 = time.perf_counter()
+    m = mm.Qwen3Model(path, mm.RunParams(num_iters=n_tok, max_seq_len=ctx + n_tok + 2), device=local_rank,
+                      tp_rank=rank, tp_size=world)
+    m.set_device("cuda")
+    tp.connect(m)
+    t_load = time.perf_counter() - t0
+    info = m.info
+    prompt = mm.random_prompt(ctx, info.vocab_size, 30)
+    ms = C.c_float()
+    check(lib.mf_timer_start(0))
+    if not m.prefill(prompt, 0, True, False):
+        raise RuntimeError("long-context workload needs the batched prefill")
+    check(lib.mf_timer_stop(0, C.byref(ms)))
+    prefill_s = ms.value / 1e3
+    tok = m.argmax()
+    tok = m.decode_chained(tok, ctx, warmup)
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        import torch.distributed as dist
+
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+    check(lib.mf_timer_start(0))
+    m.decode_chained(tok, ctx + warmup, steps)
+    check(lib.mf_timer_stop(0, C.byref(ms)))
+    dev_ms = max_over_ranks(ms.value)
+    prefill_s = max_over_ranks(prefill_s)
+    tb = token_bytes(info, ctx + warmup + steps // 2)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([tb], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t)
+        tb = t.item()
+    status = int(max_over_ranks(float(m.comm_status())))
+    m.close()
+    step_gbs = tb / (dev_ms / steps / 1e3) / 1e9 / world
+    return {"workload": f"{workload} greedy decode at batch 1 after a {ctx}-token prompt", "context": ctx,
+            "tok_per_s": round(steps / (dev_ms / 1e3), 2), "ms_per_step": round(dev_ms / steps, 3), "steps": steps,
+            "bytes_per_token": tb, "hbm_roofline": {"achieved_gbs_per_gpu": round(step_gbs, 1),
+                                                    "peak_gbs": peaks["hbm_gbs"],
+                                                    "frac": round(step_gbs / peaks["hbm_gbs"], 4)},
+            "prefill_tok_per_s": round(ctx / prefill_s, 1), "exchange_status": status,
+            "parallelism": "single" if world == 1 else f"tp{world}", "load_seconds": round(t_load, 1),
+            "file_seconds": round(t_gen, 1)}
+
+
 def host_cpu() -> dict:
     """The host's CPU as lscpu reports it (model, sockets, physical cores,
     logical CPUs), the CPUs this process may run on, the cgroup CPU quota and
@@ -331,6 +446,13 @@ def main():
     ap.add_argument("--context", type=int, default=4096, help="prompt tokens prefilled before decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=16)
+    ap.add_argument("--long-workload", default="qwen3-32b-bf16", choices=sorted(CONFIGS),
+                    help="second record: this model decoded after a long prompt (the scaling target)")
+    ap.add_argument("--long-context", type=int, default=32768)
+    ap.add_argument("--no-long", action="store_true", help="skip the long-context record")
+    ap.add_argument("--llama-bench", action="store_true",
+                    help="only the reference's benchmark loop (pp512 + tg128, seed 30) on --workload, this runtime "
+                         "and the reference CPU build side by side (one GPU)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local_rank = dist_env()
@@ -339,6 +461,10 @@ def main():
               "context": args.context, "batch": 1,
               "l2": "inputs larger than L2 (each step streams all weights and the KV cache)",
               "parallelism": "single" if world == 1 else f"tp{world}"}
+
+    if args.llama_bench:
+        llama_bench_main(args)
+        return
 
     if args.impl == "reference":
         if rank != 0:
@@ -463,6 +589,8 @@ def main():
         tb = t.item()
     step_gbs = tb / (dev_ms / args.steps / 1e3) / 1e9 / world  # per GPU
     status = max(status, m.comm_status())
+    # the reference's benchmark loop (pp512 + tg128) on the same model (N=1)
+    lb = llama_bench_record(m, batched) if world == 1 else None
     if world > 1:
         import torch.distributed as dist
 
@@ -470,6 +598,26 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         status = int(t.item())
     roof = time_dominant_kernel(cfgshape, peaks) if rank == 0 else None
+
+    # ---- the long-context record (the 32B-shaped model after a 32K prompt by default)
+    long_rec = None
+    if not args.no_long:
+        import shutil
+
+        lp = model_path(args.long_workload)
+        room = lp.exists() or shutil.disk_usage(lp.parent).free > CONFIGS[args.long_workload].weight_bytes() * 1.05
+        if world > 1:
+            import torch.distributed as dist
+
+            box = [room]
+            dist.broadcast_object_list(box, src=0)  # every rank takes the same branch
+            room = box[0]
+        if room:
+            m.close()
+            long_rec = measure_long_context(args.long_workload, args.long_context, args.steps, args.warmup, rank,
+                                            world, local_rank, peaks)
+        else:
+            long_rec = {"skipped": f"no room for the {args.long_workload} file under {lp.parent}"}
 
     if rank == 0:
         cpu = None
@@ -493,6 +641,10 @@ def main():
             "prefill": prefill_line(cfgshape, ctx, prefill_max_s, batched, peaks, world),
             "cpu_baseline": cpu, "clocks": clk.summary(), "load_seconds": round(t_load, 2),
         }
+        if lb:
+            line["llama_bench"] = lb
+        if long_rec:
+            line["long_context"] = long_rec
         if world > 1:
             line["tp"] = {"size": world, "exchange_status": status,
                           "note": "hbm_roofline.achieved_gbs is per GPU; bytes_per_token summed over ranks"}

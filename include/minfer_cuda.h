@@ -134,7 +134,12 @@ int mf_timer_stop(int rank, float* ms);
 #define MF_STEP_RECORD_BYTES 32
 #define MF_STEP_FRAME 4 /* index of the frame field */
 #define MF_STEP_STATUS 5 /* exchange status bits (mf_comm_status), written by the tensor-parallel lm_head */
+#define MF_STEP_DSTATUS 6 /* bit 1: a decode kernel's copy wait gave up (mf_decode_status) */
 int mf_step_state(int rank, int32_t** host, void** device);
+/* Decode-kernel status of a rank (the MF_STEP_DSTATUS field of its device
+ * step record, which the TMA-fed GEMVs set when a bounded copy wait gave up);
+ * clear != 0 resets it. Synchronises the rank's stream. */
+int mf_decode_status(int rank, int* status, int clear);
 
 /* ===================================================================== */
 /* Token-loop ops (fused). Each replaces a run of Metal dispatches of     */

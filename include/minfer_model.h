@@ -123,6 +123,15 @@ int mf_model_generate_logits(mf_model* m, const uint32_t* prompt, size_t n_promp
  * MF_E_UNSUPPORTED (use mf_model_forward per token). */
 int mf_model_prefill(mf_model* m, const uint32_t* tokens, size_t n, int pos0, int compute_logits, int host_logits);
 
+/* BaseModel::benchmark (src/base/model.cpp:188-236): pp512 (512 random ids
+ * from std::mt19937(seed), logits on the last) then tg128 (128 forwards of
+ * fresh random ids at positions 0..127); stats as the reference reports them
+ * (prefill_time = ttft, throughput = 128 / decode time, bandwidth = bytes the
+ * reference counts / total time). flags: MF_GEN_TOKEN_PREFILL runs the 512
+ * prompt ids as decode frames, as the reference does; otherwise the batched
+ * tensor-core prefill is used when the model supports it. */
+int mf_model_benchmark(mf_model* m, int flags, mf_gen_stats* stats);
+
 /* Greedy decode of n tokens with the device feeding itself (no host round
  * trip between tokens), starting with `token` at `start_pos`. Blocks until
  * done; returns the last greedy id. */

@@ -89,6 +89,7 @@ CUDA_API = {
     "mf_init": (I, [I, P]),
     "mf_shutdown": (I, []),
     "mf_device_count": (I, [P]),
+    "mf_decode_status": (I, [I, P, I]),
     "mf_last_error": (I, [C.c_char_p, SZ]),
     "mf_upload": (I, [P, SZ, I, P]),
     "mf_alloc": (I, [SZ, I, P]),
@@ -184,6 +185,7 @@ HOST_API = {
     "mf_model_generate": (I, [P, P, SZ, SZ, I, P, P, P, P, P]),
     "mf_model_generate_logits": (I, [P, P, SZ, SZ, I, P, P, P, P, P, P, SZ, P]),
     "mf_model_decode_chained": (I, [P, U32, I, I, P]),
+    "mf_model_benchmark": (I, [P, I, P]),
     "mf_model_reset_sampler": (I, [P]),
     "mf_model_experts": (I, [P, I, P, P]),
     "mf_model_kv": (I, [P, I, P, P, I]),

@@ -24,6 +24,7 @@
 
 #include "attention.cuh"
 #include "gemv_inst.cuh"
+#include "gemv_tma.cuh"
 #include "minfer_cuda.h"
 #include "misc.cuh"
 
@@ -240,6 +241,92 @@ void choose_shape(int K, int dtype, int ym, int* T_out, int* R_out) {
     *R_out = bR;
 }
 
+// The manager step record's decode-status field on the current device (the
+// TMA-fed kernels report a wait that gave up there).
+int* decode_status_ptr() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    for (auto& r : g.ranks)
+        if (r.device == dev) return (int*)r.d_step + MF_STEP_DSTATUS;
+    return nullptr;
+}
+
+const void* gemv_tma_fn(int dtype, int xm, int ym, int nwc, int j) {
+    switch (dtype) {
+        case MF_F32: return mf::gemv_tma_ptr_f32(xm, ym, nwc, j);
+        case MF_F16: return mf::gemv_tma_ptr_f16(xm, ym, nwc, j);
+        case MF_BF16: return mf::gemv_tma_ptr_bf16(xm, ym, nwc, j);
+        default: return nullptr;
+    }
+}
+
+// The TMA-fed dense GEMV (gemv_tma.cuh) for the plain and normalised store,
+// residual and SwiGLU forms: 1 when it launched, 0 when the shape is left to
+// the register-fed kernel (MF_GEMV_TMA=0 sends everything there), < 0 on error.
+int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_t st) {
+    static const int on = env_int("MF_GEMV_TMA", 0);
+    static const long long timeout_ms = env_int("MF_DECODE_TIMEOUT_MS", 1000);
+    if (!on) return 0;
+    if (!(xm == mf::X_PLAIN || xm == mf::X_NORM) || !(ym == mf::Y_STORE || ym == mf::Y_RESID || ym == mf::Y_SWIGLU))
+        return 0;
+    if (q.expert_ids || q.counter || q.gather_logits) return 0;
+    const int vec = vec_of(dtype);
+    const size_t esz = esz_of(dtype);
+    const int NV = q.K / vec;
+    int nwc = 8, j = (NV + 8 * 32 - 1) / (8 * 32);
+    if (j > 8) {
+        nwc = 16;
+        j = (NV + 16 * 32 - 1) / (16 * 32);
+        if (j > 8) return 0;
+        j = 8;
+    } else {
+        static const int js[] = {1, 2, 3, 4, 6, 8};
+        for (int c : js)
+            if (c >= j) {
+                j = c;
+                break;
+            }
+    }
+    const void* fn = gemv_tma_fn(dtype, xm, ym, nwc, j);
+    if (!fn) return 0;
+    const int RU = ym == mf::Y_SWIGLU ? 2 : 1;
+    const size_t row_bytes = (size_t)q.K * esz;
+    int rps = (int)(mf::GT_STAGE_TARGET / row_bytes) / RU * RU;
+    if (rps < RU) rps = RU;
+    const size_t stage_bytes = (size_t)rps * row_bytes;
+    if (stage_bytes > 2 * (size_t)mf::GT_STAGE_TARGET) return 0;  // rows too wide for the ring
+    int stages = (int)(mf::GT_RING_BYTES / stage_bytes);
+    stages = std::max(2, std::min(stages, mf::GT_MAX_STAGES));
+    const long long units = q.rows / RU;
+    long long grid = std::min<long long>(num_sms(), units);
+    if (grid < 1) grid = 1;
+    const size_t max_rows = (size_t)((units + grid - 1) / grid) * RU;
+    const size_t smem = (size_t)stages * stage_bytes + max_rows * nwc * sizeof(float);
+    if (smem > 200 * 1024) return 0;
+    int* status = decode_status_ptr();
+    if (!status) return 0;
+    int bps = 0;
+    int rc = prepare(fn, (nwc + 1) * 32, smem, &bps);
+    if (rc) return rc;
+    mf::GemvTmaParams p = {};
+    p.w = (const char*)q.w + q.w_offset * esz;
+    p.row_bytes = row_bytes;
+    p.rows = q.rows;
+    p.K = q.K;
+    p.x = q.x;
+    p.nw = q.nw;
+    p.eps = q.eps;
+    p.y = q.y;
+    p.rows_per_stage = rps;
+    p.stages = stages;
+    p.stage_bytes = (uint32_t)stage_bytes;
+    p.status = status;
+    p.timeout_ns = (unsigned long long)std::max(1ll, timeout_ms) * 1000000ull;
+    void* args[] = {&p};
+    MF_CK(launch(fn, dim3((unsigned)grid), dim3((nwc + 1) * 32), smem, st, args));
+    return 1;
+}
+
 int run_gemv(int dtype, int xm, int ym, mf::GemvParams& p, long long units, cudaStream_t st, int max_grid = 0) {
     static const int cps_cap = env_int("MF_GEMV_CTAS_PER_SM", 0);
     static const int pf_tiles = env_int("MF_GEMV_PF_TILES", 1);
@@ -249,6 +336,11 @@ int run_gemv(int dtype, int xm, int ym, mf::GemvParams& p, long long units, cuda
     MF_REQUIRE(((uintptr_t)p.w + p.w_offset * esz_of(dtype)) % 16 == 0, MF_E_INVALID,
                "weight rows must start 16-byte aligned");
     MF_REQUIRE(((uintptr_t)p.x) % 16 == 0, MF_E_INVALID, "activation vector must be 16-byte aligned");
+    if (max_grid == 0) {
+        const int tr = try_gemv_tma(dtype, xm, ym, p, st);
+        if (tr < 0) return tr;
+        if (tr == 1) return MF_OK;
+    }
     int T, R;
     choose_shape(p.K, dtype, ym, &T, &R);
     const void* fn = gemv_ptr(dtype, xm, ym, T, R);
@@ -548,6 +640,22 @@ int mf_step_state(int rank, int32_t** host, void** device) {
     MF_REQUIRE(rank >= 0 && rank < (int)g.ranks.size(), MF_E_INVALID, "rank %d out of range", rank);
     if (host) *host = g.ranks[rank].h_step;
     if (device) *device = g.ranks[rank].d_step;
+    return MF_OK;
+}
+
+int mf_decode_status(int rank, int* status, int clear) {
+    MF_REQUIRE(status, MF_E_INVALID, "null status");
+    MF_REQUIRE(g.inited && rank >= 0 && rank < (int)g.ranks.size(), MF_E_INVALID, "rank %d out of range", rank);
+    Rank& r = g.ranks[rank];
+    MF_CK(cudaSetDevice(r.device));
+    MF_CK(cudaStreamSynchronize(r.stream));
+    int v = 0;
+    MF_CK(cudaMemcpy(&v, (int*)r.d_step + MF_STEP_DSTATUS, sizeof(int), cudaMemcpyDeviceToHost));
+    *status = v;
+    if (clear) {
+        MF_CK(cudaMemset((int*)r.d_step + MF_STEP_DSTATUS, 0, sizeof(int)));
+        r.h_step[MF_STEP_DSTATUS] = 0;
+    }
     return MF_OK;
 }
 

@@ -1,0 +1,241 @@
+// Dense decode GEMV fed by 1-D TMA bulk copies: y = W x (optionally x
+// RMS-normalised first) with a store, residual-add or SwiGLU epilogue.
+//
+// Arithmetic follows the reference's matmul_{fp32,fp16,bf16}
+// (src/ops/kernels.cpp:211-343): weights widened exactly to fp32, fp32 FMAs,
+// one fp32 result per row (summation order differs: fp32 rounding level).
+//
+// Why TMA here: at batch 1 a GEMV is one pass over the weights, and the
+// register-fed kernel (gemv.cuh) keeps at most 8 x 16 bytes per thread in
+// flight, so each CTA walks its rows in latency-bound steps. Here one
+// producer lane streams the CTA's contiguous rows into a shared-memory ring
+// with cp.async.bulk (whole rows per copy, completion counted in bytes on a
+// "full" mbarrier per stage); the bytes in flight per SM are the ring size,
+// independent of registers.
+//
+// CTA layout: warps 0..NWC-1 consume, warp NWC produces. A CTA owns a
+// contiguous balanced range of units (rows, or gate/up row pairs). Consumer
+// warp w owns a fixed slice of the K columns for every row: its lanes hold
+// that slice of x (normalised, for X_NORM) in registers, read the weight
+// vectors of each staged row from shared memory, and reduce each row over
+// the warp; the per-warp partial of every row goes to shared memory and the
+// epilogue sums the NWC partials in a fixed order. A consumer warp arrives on
+// the stage's "empty" mbarrier when done with it; the producer refills the
+// stage once all NWC warps arrived.
+//
+// The ring is ~100 KB, so a CTA of the next kernel in the stream fits on the
+// SM beside this one (programmatic dependent launch) and starts its own
+// copies while this one drains. Every mbarrier wait is bounded by a
+// wall-clock deadline; on expiry the kernel records a status bit, stops
+// issuing copies, waits (bounded) for the copies it has in flight and returns.
+#pragma once
+
+#include "mbarrier.cuh"
+#include "mf_common.cuh"
+
+namespace mf {
+
+constexpr int GT_MAX_STAGES = 8;
+constexpr uint32_t GT_RING_BYTES = 100 * 1024;
+constexpr uint32_t GT_STAGE_TARGET = 32 * 1024;
+constexpr int GT_STATUS_TIMEOUT = 1;       // bit set in *status when a wait gave up
+
+struct GemvTmaParams {
+    const char* w;            // weight rows (dtype of the template), first row 16-byte aligned
+    unsigned long long row_bytes;
+    int rows;                 // rows of W (Y_SWIGLU: 2 x outputs, gate/up interleaved)
+    int K;
+    const float* x;
+    const float* nw;          // RMSNorm weight (X_NORM)
+    float eps;
+    float* y;
+    int rows_per_stage;       // a multiple of the unit size
+    int stages;
+    uint32_t stage_bytes;     // rows_per_stage * row_bytes (16-byte multiple)
+    int* status;              // timeout bit
+    unsigned long long timeout_ns;
+};
+
+// Dynamic shared memory: the ring, then the per-row partial sums [rows of this CTA][NWC].
+// J: 16-byte vectors per lane of a row (the warp's K slice is at most 32*J vectors).
+template <typename W, int NWC, int J, int XM, int YM>
+__global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvTmaParams p) {
+    constexpr int VEC = W::VEC;
+    constexpr int RU = (YM == Y_SWIGLU) ? 2 : 1;
+    extern __shared__ __align__(128) unsigned char gt_smem[];
+    __shared__ __align__(8) uint64_t full[GT_MAX_STAGES], empty[GT_MAX_STAGES];
+    __shared__ float ss_part[NWC];
+    __shared__ int abort_s;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const long long units = p.rows / RU;
+    const int r0 = (int)((long long)blockIdx.x * units / gridDim.x) * RU;
+    const int r1 = (int)((long long)(blockIdx.x + 1) * units / gridDim.x) * RU;
+    const int nrows = r1 - r0;
+    const int nchunks = (nrows + p.rows_per_stage - 1) / p.rows_per_stage;
+    const int S = p.stages;
+    float* part = reinterpret_cast<float*>(gt_smem + (size_t)S * p.stage_bytes);
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NWC);
+        }
+        abort_s = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const unsigned long long deadline = globaltimer_ns() + p.timeout_ns;
+
+    if (warp == NWC) {
+        // ---- producer: weights do not depend on earlier kernels, so the ring
+        // fills before the dependency wait
+        if (lane == 0) {
+            bool failed = false;
+            int c = 0;
+            for (; c < nchunks; ++c) {
+                const int s = c % S;
+                if (c >= S && !mbar_wait(&empty[s], (uint32_t)((c / S - 1) & 1), deadline, failed)) break;
+                if (*(volatile int*)&abort_s) break;
+                const int rr = min(p.rows_per_stage, nrows - c * p.rows_per_stage);
+                const uint32_t bytes = (uint32_t)(rr * p.row_bytes);
+                mbar_expect_tx(&full[s], bytes);
+                bulk_load(gt_smem + (size_t)s * p.stage_bytes, p.w + (size_t)(r0 + c * p.rows_per_stage) * p.row_bytes,
+                          bytes, &full[s]);
+            }
+            if (failed) {
+                atomicOr(p.status, GT_STATUS_TIMEOUT);
+                abort_s = 1;
+            }
+            // the CTA may only exit once every copy it issued has landed: wait
+            // (bounded) for the stages not yet known complete
+            bool drain_failed = false;
+            for (int d = max(0, c - S); d < c; ++d) mbar_wait(&full[d % S], (uint32_t)((d / S) & 1), deadline + p.timeout_ns, drain_failed);
+        }
+        pdl_launch_dependents();
+        return;
+    }
+
+    // ---- consumers: this warp's K slice [v0, v1) in 16-byte vectors
+    const int NV = p.K / VEC;
+    const int v0 = warp * NV / NWC, v1 = (warp + 1) * NV / NWC;
+    float xr[J][VEC];
+    pdl_launch_dependents();
+    pdl_wait();
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int v = v0 + lane + 32 * j;
+#pragma unroll
+        for (int e = 0; e < VEC; e += 4) {
+            float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (v < v1) t = __ldcg(reinterpret_cast<const float4*>(p.x + (size_t)v * VEC + e));
+            xr[j][e] = t.x; xr[j][e + 1] = t.y; xr[j][e + 2] = t.z; xr[j][e + 3] = t.w;
+            if (XM == X_NORM) {
+                ss = fmaf(t.x, t.x, ss);
+                ss = fmaf(t.y, t.y, ss);
+                ss = fmaf(t.z, t.z, ss);
+                ss = fmaf(t.w, t.w, ss);
+            }
+        }
+    }
+    if (XM == X_NORM) {
+        // src/ops/kernels.cpp:355-363: inv = 1/sqrtf(sum(x^2)/dim + eps); out = inv * x * w
+        ss = warp_sum(ss);
+        if (lane == 0) ss_part[warp] = ss;
+        asm volatile("bar.sync 1, %0;" ::"r"(NWC * 32) : "memory");
+        float tot = 0.f;
+        for (int i = 0; i < NWC; ++i) tot += ss_part[i];
+        const float inv = 1.0f / sqrtf(tot / (float)p.K + p.eps);
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            const int v = v0 + lane + 32 * j;
+            if (v < v1) {
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) xr[j][e] = (inv * xr[j][e]) * __ldg(p.nw + (size_t)v * VEC + e);
+            }
+        }
+    }
+
+    bool failed = false;
+    for (int c = 0; c < nchunks; ++c) {
+        const int s = c % S;
+        if (!mbar_wait(&full[s], (uint32_t)((c / S) & 1), deadline, failed)) break;
+        const unsigned char* st = gt_smem + (size_t)s * p.stage_bytes;
+        const int rr = min(p.rows_per_stage, nrows - c * p.rows_per_stage);
+        for (int r = 0; r < rr; ++r) {
+            const unsigned char* row = st + (size_t)r * p.row_bytes;
+            float acc = 0.f;
+#pragma unroll
+            for (int j = 0; j < J; ++j) {
+                const int v = v0 + lane + 32 * j;
+                if (v < v1) {
+                    const uint4 wv = *reinterpret_cast<const uint4*>(row + (size_t)v * 16);
+                    float wf[VEC];
+                    unpack16<W>(wv, wf);
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) acc = fmaf(xr[j][e], wf[e], acc);
+                }
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) part[(size_t)(c * p.rows_per_stage + r) * NWC + warp] = acc;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (failed && lane == 0) {
+        atomicOr(p.status, GT_STATUS_TIMEOUT);
+        abort_s = 1;
+    }
+    // every consumer warp reaches this barrier, failed or not (no wait is left
+    // unbounded); then all of them leave together when any gave up (the
+    // producer drains the copies in flight)
+    asm volatile("bar.sync 1, %0;" ::"r"(NWC * 32) : "memory");
+    if (*(volatile int*)&abort_s) return;
+
+    // ---- epilogue: fixed-order sum of the warp partials of every row
+    for (int u = tid; u < nrows / RU; u += NWC * 32) {
+        if (YM == Y_SWIGLU) {
+            float g = 0.f, up = 0.f;
+            for (int w2 = 0; w2 < NWC; ++w2) {
+                g += part[(size_t)(2 * u) * NWC + w2];
+                up += part[(size_t)(2 * u + 1) * NWC + w2];
+            }
+            p.y[(r0 >> 1) + u] = silu(g) * up;  // src/models/qwen3/module.cpp:466-468
+        } else {
+            float s2 = 0.f;
+            for (int w2 = 0; w2 < NWC; ++w2) s2 += part[(size_t)u * NWC + w2];
+            if (YM == Y_RESID) p.y[r0 + u] = __ldcg(p.y + r0 + u) + s2;  // src/models/qwen3/module.cpp:238-240
+            else p.y[r0 + u] = s2;
+        }
+    }
+}
+
+}  // namespace mf
+
+namespace mf {
+// Kernel pointer for (dtype, x mode, y mode, consumer warps, J); null when not built.
+template <typename W>
+const void* gemv_tma_ptr(int xm, int ym, int nwc, int j) {
+#define MF_GT(NW, JJ)                                                                                        \
+    if (nwc == NW && j == JJ) {                                                                              \
+        if (xm == X_NORM && ym == Y_STORE) return (const void*)&gemv_tma_kernel<W, NW, JJ, X_NORM, Y_STORE>; \
+        if (xm == X_PLAIN && ym == Y_STORE) return (const void*)&gemv_tma_kernel<W, NW, JJ, X_PLAIN, Y_STORE>; \
+        if (xm == X_PLAIN && ym == Y_RESID) return (const void*)&gemv_tma_kernel<W, NW, JJ, X_PLAIN, Y_RESID>; \
+        if (xm == X_NORM && ym == Y_SWIGLU) return (const void*)&gemv_tma_kernel<W, NW, JJ, X_NORM, Y_SWIGLU>; \
+        return nullptr;                                                                                       \
+    }
+    MF_GT(8, 1)
+    MF_GT(8, 2)
+    MF_GT(8, 3)
+    MF_GT(8, 4)
+    MF_GT(8, 6)
+    MF_GT(8, 8)
+    MF_GT(16, 8)
+#undef MF_GT
+    return nullptr;
+}
+const void* gemv_tma_ptr_f32(int xm, int ym, int nwc, int j);
+const void* gemv_tma_ptr_f16(int xm, int ym, int nwc, int j);
+const void* gemv_tma_ptr_bf16(int xm, int ym, int nwc, int j);
+}  // namespace mf

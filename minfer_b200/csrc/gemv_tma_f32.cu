@@ -1,0 +1,7 @@
+// TMA-fed dense GEMV instantiations for F32 weights.
+#include "gemv.cuh"
+#include "gemv_tma.cuh"
+
+namespace mf {
+const void* gemv_tma_ptr_f32(int xm, int ym, int nwc, int j) { return gemv_tma_ptr<W_F32>(xm, ym, nwc, j); }
+}  // namespace mf

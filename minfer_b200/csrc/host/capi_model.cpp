@@ -204,6 +204,22 @@ int mf_model_generate_logits(mf_model* m, const uint32_t* prompt, size_t n_promp
     return MF_OK;
 }
 
+int mf_model_benchmark(mf_model* m, int flags, mf_gen_stats* stats) {
+    if (!m || !stats) return herr(MF_E_INVALID, "null argument");
+    g_host_err[0] = 0;
+    MF_TRY({
+        const minfer::GenStats st = m->m->benchmark((flags & MF_GEN_TOKEN_PREFILL) == 0);
+        stats->num_tokens_gen = st.num_tokens_gen;
+        stats->ttft = st.ttft;
+        stats->throughput = st.throughput;
+        stats->prefill_time = st.prefill_time;
+        stats->bandwidth = st.bandwidth;
+        stats->decode_seconds = st.decode_seconds;
+        stats->bytes_read = st.bytes_read;
+    });
+    return MF_OK;
+}
+
 int mf_model_prefill(mf_model* m, const uint32_t* tokens, size_t n, int pos0, int compute_logits, int host_logits) {
     if (!m || !tokens || n == 0) return herr(MF_E_INVALID, "bad arguments");
     g_host_err[0] = 0;

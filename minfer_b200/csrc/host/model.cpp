@@ -5,6 +5,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <random>
 #include <stdexcept>
 
 namespace minfer {
@@ -840,11 +841,15 @@ void Qwen3Model::read_back_logits() {
 }
 
 void Qwen3Model::check_exchange_status() const {
+    const int ds = rs_.h_step[MF_STEP_DSTATUS];
+    if (ds != 0)
+        throw WaitTimeout("a decode kernel's copy wait gave up (status " + std::to_string(ds) +
+                          "); this frame's results are invalid");
     if (!rs_.comm) return;
     const int st = rs_.h_step[MF_STEP_STATUS];
     if (st != 0)
         throw WaitTimeout("a tensor-parallel exchange wait gave up (status " + std::to_string(st) +
-                              "): a peer rank did not arrive in time; this frame's results are invalid");
+                          "): a peer rank did not arrive in time; this frame's results are invalid");
 }
 
 void Qwen3Model::read_full_logits() {
@@ -882,7 +887,8 @@ void Qwen3Model::forward(uint32_t token, int pos, bool compute_logits, bool host
         }
     }
     check(mf_end_frame(rank_), "end_frame");
-    if (compute_logits) check_exchange_status();  // the tensor-parallel lm_head reports the frame's waits
+    // the decode kernels (and the tensor-parallel lm_head) report waits that gave up in the step record
+    check_exchange_status();
 }
 
 std::vector<uint32_t> Qwen3Model::generate(const std::vector<uint32_t>& prompt, size_t n_gen, const GenOptions& opt,
@@ -975,6 +981,39 @@ std::vector<uint32_t> Qwen3Model::generate(const std::vector<uint32_t>& prompt, 
     st.bandwidth = (float)(st.bytes_read / 1e9 / (dt + st.prefill_time));
     if (stats) *stats = st;
     return out;
+}
+
+GenStats Qwen3Model::benchmark(bool batched_prefill) {
+    constexpr size_t kPP = 512, kTG = 128;
+    if (cfg_.user_max_seq_len < kPP) throw std::runtime_error("benchmark needs max_seq_len >= 512");
+    std::mt19937 gen(cfg_.seed);
+    std::uniform_int_distribution<> distrib(0, (int)cfg_.vocab_size - 1);
+    GenStats st;
+    size_t model_bytes = 0, kv_bytes = 0;
+    std::vector<uint32_t> pp(kPP);
+    for (size_t i = 0; i < kPP; ++i) pp[i] = (uint32_t)distrib(gen);  // drawn in the loop's order
+    const double t0 = now_s();
+    const bool batched = batched_prefill && prefill(pp.data(), (int)kPP, 0, true, false);
+    for (size_t i = 0; i < kPP; ++i) {
+        if (!batched) forward(pp[i], (int)i, i == kPP - 1, false);
+        model_bytes += read_bytes(true);  // as the reference counts it (lm_head included every step)
+        kv_bytes += rs_.kv_bytes_per_pos * (i + 1);
+    }
+    st.prefill_time = (float)(now_s() - t0);
+    st.ttft = st.prefill_time;
+    const double t1 = now_s();
+    for (size_t i = 0; i < kTG; ++i) {
+        forward((uint32_t)distrib(gen), (int)i, true, false);
+        model_bytes += read_bytes(true);
+        kv_bytes += rs_.kv_bytes_per_pos * (i + 1);
+    }
+    const double dt = now_s() - t1;
+    st.num_tokens_gen = (int)kTG;
+    st.decode_seconds = dt;
+    st.throughput = (float)(kTG / dt);
+    st.bytes_read = (double)(model_bytes + kv_bytes);
+    st.bandwidth = (float)(st.bytes_read / 1e9 / (dt + st.prefill_time));
+    return st;
 }
 
 uint32_t Qwen3Model::decode_chained(uint32_t token, int start_pos, int n) {

@@ -23,8 +23,9 @@ namespace minfer {
 constexpr int kPrefillChunk = 4096;  // prompt tokens per batched-prefill pass
 constexpr int kTopkMax = 64;         // largest top_k sampled from device candidates (mf_topk)
 // step-record bytes read back after a host-driven frame: token, pos, next_token,
-// chain, frame and the exchange status (MF_STEP_STATUS)
-constexpr size_t kStepReadback = 24;
+// chain, frame, the exchange status (MF_STEP_STATUS) and the decode-kernel
+// status (MF_STEP_DSTATUS)
+constexpr size_t kStepReadback = 28;
 
 // A bounded wait on the device gave up (a tensor-parallel exchange whose peer
 // did not arrive, or a prefill kernel's pipeline wait): the results of that
@@ -185,6 +186,13 @@ public:
     // BaseModel::generate without the tokenizer (src/base/model.cpp:99-186).
     std::vector<uint32_t> generate(const std::vector<uint32_t>& prompt, size_t n_gen, const GenOptions& opt,
                                    GenStats* stats, std::vector<float>* margins);
+    // BaseModel::benchmark (src/base/model.cpp:188-236): 512 random prompt ids
+    // (std::mt19937(seed), uniform over the vocabulary) prefilled with logits
+    // on the last only ("pp512"), then 128 forwards of fresh random ids at
+    // positions 0..127 with logits ("tg128"); the same byte count and
+    // bandwidth formula. batched_prefill runs the 512 ids through the
+    // tensor-core prefill instead of 512 decode frames (when supported).
+    GenStats benchmark(bool batched_prefill);
     // Greedy decode with the device feeding itself: frame i embeds the argmax
     // of frame i-1 (chained step record), frames are queued back to back with
     // no host round trip. Returns the last greedy id; the caller times it.
@@ -209,7 +217,8 @@ private:
     void issue_frame(bool readback);
     void read_back_logits();  // logits, or their top-k candidates, to pinned host memory
     void read_full_logits();  // the last frame's logits to pinned host memory, synchronously
-    // throws WaitTimeout when the step record read back last carries exchange status bits
+    // throws WaitTimeout when the step record read back last carries exchange
+    // or decode-kernel status bits
     void check_exchange_status() const;
 
     std::string path_;

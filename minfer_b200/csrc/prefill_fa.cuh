@@ -78,9 +78,6 @@ MF_DEVICE void tma_load_3d(void* dst, const CUtensorMap* tm, uint64_t* bar, int 
         "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
         : "memory");
 }
-MF_DEVICE void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 // D (TMEM) (+)= A (TMEM) * B (shared-memory descriptor); no output lane disabled.
 MF_DEVICE void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc, uint32_t accumulate) {
     const uint32_t z = 0;

@@ -33,6 +33,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include "mbarrier.cuh"
 #include "mf_common.cuh"
 
 namespace mf {
@@ -57,39 +58,6 @@ struct PgParams {
     int* status;           // bit 1: a wait gave up
     unsigned long long timeout_ns;
 };
-
-MF_DEVICE uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-MF_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-MF_DEVICE void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-MF_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Wait for the phase of `parity` to complete, until `deadline` (and at most
-// 2^26 polls). Returns false, and sets `failed`, when it gives up; a caller
-// that already failed does not wait again.
-MF_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned long long deadline, bool& failed) {
-    if (failed) return false;
-    for (long long i = 0; i < (1ll << 26); ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 15) == 15 && globaltimer_ns() > deadline) break;
-    }
-    failed = true;
-    return false;
-}
 
 // 2-D TMA tile load (no multicast) into shared memory, completing on `bar`.
 // x (the inner, K coordinate) is always a multiple of 64 elements.

@@ -280,99 +280,150 @@ def _fill_chunk(fd: int, file_off: int, seed: int, t_idx: int, c_idx: int, n: in
         done += os.pwrite(fd, view[done:], file_off + done)
 
 
-def write_qwen3_gguf(path: str | os.PathLike, cfg: Qwen3Shape, chunk_elems: int = 1 << 22,
-                     threads: int | None = None) -> str:
-    """Write a seeded synthetic Qwen3 GGUF file; returns the path.
+def _layout(cfg: Qwen3Shape) -> tuple[bytes, list[tuple], list[int], int, int]:
+    """(header bytes up to the aligned data start, tensor plan, tensor offsets
+    relative to the data start, data start, data bytes) of the file for cfg."""
+    import io
 
-    Weights are N(0, cfg.std): tensor t is cut into chunks of `chunk_elems`
-    elements and chunk c is drawn from PCG64(SeedSequence([seed, t, c])), so the
-    file is identical for any thread count. Norm weights are 1.0.
-    """
-    import concurrent.futures as cf
-
-    path = os.fspath(path)
     plan = tensor_plan(cfg)
     toks, types, merges, eos, pad = synth_vocab(cfg.vocab, cfg.seed)
-    tmp = path + ".tmp"
-    with open(tmp, "wb") as fh:
-        w = _Writer(fh)
-        kvs: list[tuple] = []
-        arch = "qwen3"
-        kvs.append(("general.architecture", _STR, arch))
-        kvs.append(("general.name", _STR, "synthetic-qwen3"))
-        kvs.append(("general.alignment", _U32, ALIGN))
-        kvs.append((f"{arch}.context_length", _U32, cfg.context_length))
-        kvs.append((f"{arch}.embedding_length", _U32, cfg.d_model))
-        kvs.append((f"{arch}.block_count", _U32, cfg.n_layers))
-        kvs.append((f"{arch}.attention.head_count", _U32, cfg.n_heads))
-        kvs.append((f"{arch}.attention.head_count_kv", _U32, cfg.n_kv_heads))
-        kvs.append((f"{arch}.attention.key_length", _U32, cfg.d_head))
-        kvs.append((f"{arch}.attention.value_length", _U32, cfg.d_head))
-        if cfg.moe:
-            kvs.append((f"{arch}.expert_feed_forward_length", _U32, cfg.d_ff))
-            kvs.append((f"{arch}.feed_forward_length", _U32, cfg.d_ff))
-            kvs.append((f"{arch}.expert_count", _U32, cfg.n_experts))
-            kvs.append((f"{arch}.expert_used_count", _U32, cfg.n_active))
-        else:
-            kvs.append((f"{arch}.feed_forward_length", _U32, cfg.d_ff))
-        kvs.append((f"{arch}.attention.layer_norm_rms_epsilon", _F32, cfg.eps))
-        kvs.append((f"{arch}.rope.freq_base", _F32, cfg.rope_base))
-        kvs.append(("tokenizer.ggml.model", _STR, "gpt2"))
-        kvs.append(("tokenizer.ggml.pre", _STR, "qwen2"))
-        kvs.append(("tokenizer.ggml.eos_token_id", _U32, eos))
-        kvs.append(("tokenizer.ggml.padding_token_id", _U32, pad))
-        kvs.append(("tokenizer.ggml.bos_token_id", _U32, pad))
-        kvs.append(("tokenizer.ggml.add_bos_token", _BOOL, False))
-        kvs.append(("tokenizer.chat_template", _STR, CHAT_TEMPLATE))
-        n_kv = len(kvs) + 3
-        w.u32(MAGIC)
-        w.u32(3)
-        w.u64(len(plan))
-        w.u64(n_kv)
-        for k, t, v in kvs:
-            w.kv(k, t, v)
-        w.arr("tokenizer.ggml.tokens", _STR, toks)
-        w.arr("tokenizer.ggml.token_type", _I32, types)
-        w.arr("tokenizer.ggml.merges", _STR, merges)
-        off = 0
-        offsets = []
-        for name, shape, dt in plan:
-            nbytes = int(np.prod(shape)) * _DTYPE_SIZE[dt]
-            offsets.append(off)
-            w.s(name)
-            w.u32(len(shape))
-            for dim in reversed(shape):
-                w.u64(dim)
-            w.u32(_DTYPE_CODE[dt])
-            w.u64(off)
-            off = _align(off + nbytes)
-        pos = fh.tell()
-        fh.write(b"\0" * (_align(pos) - pos))
-        data0 = fh.tell()
-        # norms now; random tensors in parallel below
+    fh = io.BytesIO()
+    w = _Writer(fh)
+    kvs: list[tuple] = []
+    arch = "qwen3"
+    kvs.append(("general.architecture", _STR, arch))
+    kvs.append(("general.name", _STR, "synthetic-qwen3"))
+    kvs.append(("general.alignment", _U32, ALIGN))
+    kvs.append((f"{arch}.context_length", _U32, cfg.context_length))
+    kvs.append((f"{arch}.embedding_length", _U32, cfg.d_model))
+    kvs.append((f"{arch}.block_count", _U32, cfg.n_layers))
+    kvs.append((f"{arch}.attention.head_count", _U32, cfg.n_heads))
+    kvs.append((f"{arch}.attention.head_count_kv", _U32, cfg.n_kv_heads))
+    kvs.append((f"{arch}.attention.key_length", _U32, cfg.d_head))
+    kvs.append((f"{arch}.attention.value_length", _U32, cfg.d_head))
+    if cfg.moe:
+        kvs.append((f"{arch}.expert_feed_forward_length", _U32, cfg.d_ff))
+        kvs.append((f"{arch}.feed_forward_length", _U32, cfg.d_ff))
+        kvs.append((f"{arch}.expert_count", _U32, cfg.n_experts))
+        kvs.append((f"{arch}.expert_used_count", _U32, cfg.n_active))
+    else:
+        kvs.append((f"{arch}.feed_forward_length", _U32, cfg.d_ff))
+    kvs.append((f"{arch}.attention.layer_norm_rms_epsilon", _F32, cfg.eps))
+    kvs.append((f"{arch}.rope.freq_base", _F32, cfg.rope_base))
+    kvs.append(("tokenizer.ggml.model", _STR, "gpt2"))
+    kvs.append(("tokenizer.ggml.pre", _STR, "qwen2"))
+    kvs.append(("tokenizer.ggml.eos_token_id", _U32, eos))
+    kvs.append(("tokenizer.ggml.padding_token_id", _U32, pad))
+    kvs.append(("tokenizer.ggml.bos_token_id", _U32, pad))
+    kvs.append(("tokenizer.ggml.add_bos_token", _BOOL, False))
+    kvs.append(("tokenizer.chat_template", _STR, CHAT_TEMPLATE))
+    n_kv = len(kvs) + 3
+    w.u32(MAGIC)
+    w.u32(3)
+    w.u64(len(plan))
+    w.u64(n_kv)
+    for k, t, v in kvs:
+        w.kv(k, t, v)
+    w.arr("tokenizer.ggml.tokens", _STR, toks)
+    w.arr("tokenizer.ggml.token_type", _I32, types)
+    w.arr("tokenizer.ggml.merges", _STR, merges)
+    off = 0
+    offsets = []
+    for name, shape, dt in plan:
+        nbytes = int(np.prod(shape)) * _DTYPE_SIZE[dt]
+        offsets.append(off)
+        w.s(name)
+        w.u32(len(shape))
+        for dim in reversed(shape):
+            w.u64(dim)
+        w.u32(_DTYPE_CODE[dt])
+        w.u64(off)
+        off = _align(off + nbytes)
+    pos = fh.tell()
+    fh.write(b"\0" * (_align(pos) - pos))
+    return fh.getvalue(), plan, offsets, fh.tell(), off
+
+
+def _fill_jobs(cfg: Qwen3Shape, plan, offsets, data0: int) -> list[tuple]:
+    """The random tensors as chunk jobs (file offset, seed, stream index,
+    chunk index, elements, dtype, std); 2^22 elements per chunk."""
+    jobs = []
+    chunk_elems = 1 << 22
+    for t_idx, ((name, shape, dt), o) in enumerate(zip(plan, offsets)):
+        if _is_norm(name):
+            continue
+        n = int(np.prod(shape))
+        esz = _DTYPE_SIZE[dt]
+        for c_idx, start in enumerate(range(0, n, chunk_elems)):
+            m = min(chunk_elems, n - start)
+            jobs.append((data0 + o + start * esz, cfg.seed, rng_index(cfg, t_idx), c_idx, m, dt, cfg.std))
+    return jobs
+
+
+def _write_header(path: str, cfg: Qwen3Shape) -> list[tuple]:
+    """Writes the header and the norm weights of the file at `path` (sized to
+    its full length); returns the random-fill jobs."""
+    head, plan, offsets, data0, total = _layout(cfg)
+    with open(path, "wb") as fh:
+        fh.write(head)
         for (name, shape, dt), o in zip(plan, offsets):
             if _is_norm(name):
                 fh.seek(data0 + o)
                 np.ones(int(np.prod(shape)), dtype="<f4").tofile(fh)
-        fh.truncate(data0 + off)
-    fd = os.open(tmp, os.O_WRONLY)
+        fh.truncate(data0 + total)
+    return _fill_jobs(cfg, plan, offsets, data0)
+
+
+def _fill(path: str, jobs: list[tuple], threads: int | None = None) -> None:
+    import concurrent.futures as cf
+
+    fd = os.open(path, os.O_WRONLY)
     try:
-        jobs = []
-        for t_idx, ((name, shape, dt), o) in enumerate(zip(plan, offsets)):
-            if _is_norm(name):
-                continue
-            n = int(np.prod(shape))
-            esz = _DTYPE_SIZE[dt]
-            for c_idx, start in enumerate(range(0, n, chunk_elems)):
-                m = min(chunk_elems, n - start)
-                jobs.append((fd, data0 + o + start * esz, cfg.seed, rng_index(cfg, t_idx), c_idx, m, dt, cfg.std))
         nthreads = threads or min(32, os.cpu_count() or 4)
         with cf.ThreadPoolExecutor(max_workers=nthreads) as ex:
-            for f in [ex.submit(_fill_chunk, *j) for j in jobs]:
+            for f in [ex.submit(_fill_chunk, fd, *j) for j in jobs]:
                 f.result()
     finally:
         os.close(fd)
+
+
+def write_qwen3_gguf(path: str | os.PathLike, cfg: Qwen3Shape, threads: int | None = None) -> str:
+    """Write a seeded synthetic Qwen3 GGUF file; returns the path.
+
+    Weights are N(0, cfg.std): tensor t is cut into chunks of 2^22 elements
+    and chunk c is drawn from PCG64(SeedSequence([seed, t, c])), so the file
+    is identical for any thread or process count. Norm weights are 1.0.
+    """
+    path = os.fspath(path)
+    tmp = path + ".tmp"
+    jobs = _write_header(tmp, cfg)
+    _fill(tmp, jobs, threads)
     os.replace(tmp, path)
+    return path
+
+
+def ensure_gguf_ranks(path: str | os.PathLike, cfg: Qwen3Shape, rank: int, world: int, barrier) -> str:
+    """ensure_gguf shared by `world` processes (one per GPU): rank 0 writes
+    the header, every rank draws its share of the weight chunks, rank 0
+    renames the finished file. `barrier()` synchronises the processes; every
+    rank must call this with the same arguments."""
+    path = os.fspath(path)
+    tmp = path + ".ranks.tmp"
+    exists = os.path.exists(path)
+    barrier()
+    if exists:
+        return path
+    if rank == 0:
+        jobs = _write_header(tmp, cfg)
+    else:
+        _, plan, offsets, data0, _ = _layout(cfg)
+        jobs = _fill_jobs(cfg, plan, offsets, data0)
+    barrier()
+    _fill(tmp, jobs[rank::world])
+    barrier()
+    if rank == 0:
+        os.replace(tmp, path)
+    barrier()
     return path
 
 

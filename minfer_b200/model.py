@@ -171,6 +171,13 @@ class Qwen3Model:
             return out[:n], (mg[:n] if margins else None), stats, lg
         return out[:n], (mg[:n] if margins else None), stats
 
+    def benchmark(self, token_prefill: bool = False) -> GenStats:
+        """BaseModel::benchmark: pp512 then tg128 with random ids (seed from RunParams)."""
+        st = mf_gen_stats()
+        check(self._lib.mf_model_benchmark(self._h, MF_GEN_TOKEN_PREFILL if token_prefill else 0, C.byref(st)))
+        return GenStats(st.num_tokens_gen, st.ttft, st.throughput, st.prefill_time, st.bandwidth,
+                        st.decode_seconds, st.bytes_read)
+
     def decode_chained(self, token: int, start_pos: int, n: int) -> int:
         last = C.c_uint32()
         check(self._lib.mf_model_decode_chained(self._h, int(token), int(start_pos), int(n), C.byref(last)))

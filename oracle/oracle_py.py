@@ -256,7 +256,8 @@ def ref_binary() -> tuple[Path, str]:
 def run_reference(model: str, out_prefix: str, *, prompt=None, random_prompt: int = 0, prompt_seed: int = 0,
                   gen: int = 8, max_seq: int = 0, temp: float = 0.0, top_k: int = 1, top_p: float = 1.0,
                   min_p: float = 0.0, pres: float = 0.0, seed: int = 0, dump_logits=(), threads: int | None = None,
-                  bench_context: int = -1, bench_steps: int = 0, bench_warmup: int = 0, timeout: float = 3600):
+                  bench_context: int = -1, bench_steps: int = 0, bench_warmup: int = 0, llama_bench: bool = False,
+                  timeout: float = 3600):
     """Run the reference's own CPU token loop (minfer_ref_run) and load its dump."""
     binary, _ = ref_binary()
     args = [str(binary), str(model), "--out", out_prefix, "--gen", str(gen), "--temp", str(temp), "--top-k",
@@ -274,6 +275,8 @@ def run_reference(model: str, out_prefix: str, *, prompt=None, random_prompt: in
     if bench_context >= 0:
         args += ["--bench-context", str(bench_context), "--bench-steps", str(bench_steps), "--bench-warmup",
                  str(bench_warmup), "--prompt-seed", str(prompt_seed)]
+    if llama_bench:
+        args += ["--llama-bench"]
     env = dict(os.environ)
     if threads:
         env["OMP_NUM_THREADS"] = str(threads)

@@ -25,6 +25,7 @@
 #include "minfer/base/module.hpp"
 #include "minfer/base/config.hpp"
 #include "minfer/base/sampler.hpp"
+#include "minfer/base/stats.hpp"
 #include "minfer/base/tensor.hpp"
 #include "minfer/models/qwen3/module.hpp"
 
@@ -59,6 +60,7 @@ struct Options {
     std::vector<long> dump_steps;  // decode steps whose full logits are written; -1 = all
     long bench_context = -1;
     int bench_steps = 0, bench_warmup = 0;
+    bool llama_bench = false;  // run BaseModel::benchmark (pp512 + tg128) as it is
 };
 
 std::vector<long> parse_list(const std::string& s) {
@@ -132,6 +134,7 @@ public:
     Config& cfg() { return *config; }
     Sampler& sampler_ref() { return *sampler; }
     RunState& state() { return *run_state; }
+    const GenStats& gen_stats() const { return *stats; }
     bool untied() const { return untied_; }
 
     bool record_experts_ = true;
@@ -179,7 +182,7 @@ int usage() {
                  "usage: minfer_ref_run <model.gguf> [--prompt-file F | --random-prompt P --prompt-seed S]\n"
                  "  [--gen G] [--max-seq N] [--temp T --top-k K --top-p P --min-p M --pres X --seed S]\n"
                  "  [--stop-at-eos] [--tied-head] [--dump-logits a,b,...|-1] [--out PREFIX]\n"
-                 "  [--bench-context C --bench-steps K --bench-warmup W]\n");
+                 "  [--bench-context C --bench-steps K --bench-warmup W] [--llama-bench]\n");
     return 2;
 }
 
@@ -216,6 +219,7 @@ int main(int argc, char** argv) {
         else if (a == "--bench-context") o.bench_context = std::stol(next());
         else if (a == "--bench-steps") o.bench_steps = std::stoi(next());
         else if (a == "--bench-warmup") o.bench_warmup = std::stoi(next());
+        else if (a == "--llama-bench") o.llama_bench = true;
         else return usage();
     }
 
@@ -228,6 +232,7 @@ int main(int argc, char** argv) {
 
     size_t max_seq = o.max_seq;
     const bool bench = o.bench_context >= 0;
+    if (o.llama_bench && max_seq < 512) max_seq = 512;  // benchmark() prefills positions 0..511
     if (max_seq == 0) {
         max_seq = bench ? (size_t)o.bench_context + o.bench_steps + o.bench_warmup
                         : (o.random_prompt ? o.random_prompt : prompt.size()) + o.gen + 1;
@@ -249,6 +254,18 @@ int main(int argc, char** argv) {
 
     std::ofstream js(o.out + ".json");
     js.precision(9);
+
+    if (o.llama_bench) {
+        // the reference's own benchmark loop (src/base/model.cpp:188-236),
+        // unchanged; its stats are read back from the protected GenStats
+        m.record_experts_ = false;
+        m.benchmark();
+        const GenStats& st = m.gen_stats();
+        js << "{\"mode\":\"llama_bench\",\"num_tokens_gen\":" << st.num_tokens_gen << ",\"prefill_time\":"
+           << st.prefill_time << ",\"ttft\":" << st.ttft << ",\"throughput\":" << st.throughput
+           << ",\"bandwidth\":" << st.bandwidth << ",\"load_seconds\":" << t_load << "}\n";
+        return 0;
+    }
 
     if (bench) {
         // decode forwards at positions [C, C+W+K): the KV rows below C are
