@@ -65,7 +65,9 @@ def model_path(workload: str) -> Path:
     import shutil
 
     if os.environ.get("MF_MODEL_DIR"):
-        return Path(os.environ["MF_MODEL_DIR"]) / f"minfer_b200_{workload}.gguf"
+        d = Path(os.environ["MF_MODEL_DIR"])
+        d.mkdir(parents=True, exist_ok=True)
+        return d / f"minfer_b200_{workload}.gguf"
     need = CONFIGS[workload].weight_bytes() * 1.1 + (1 << 30)
     for d in ("/dev/shm", "/tmp"):
         p = Path(d) / f"minfer_b200_{workload}.gguf"

@@ -264,7 +264,7 @@ const void* gemv_tma_fn(int dtype, int xm, int ym, int nwc, int j) {
 // residual and SwiGLU forms: 1 when it launched, 0 when the shape is left to
 // the register-fed kernel (MF_GEMV_TMA=0 sends everything there), < 0 on error.
 int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_t st) {
-    static const int on = env_int("MF_GEMV_TMA", 0);
+    static const int on = env_int("MF_GEMV_TMA", 1);
     static const long long timeout_ms = env_int("MF_DECODE_TIMEOUT_MS", 1000);
     if (!on) return 0;
     if (!(xm == mf::X_PLAIN || xm == mf::X_NORM) || !(ym == mf::Y_STORE || ym == mf::Y_RESID || ym == mf::Y_SWIGLU))
@@ -289,16 +289,22 @@ int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_
     }
     const void* fn = gemv_tma_fn(dtype, xm, ym, nwc, j);
     if (!fn) return 0;
+    // ring geometry and CTAs per SM (MF_GEMV_TMA_STAGE_KB / _RING_KB / _CPS: tuning knobs)
+    static const size_t stage_target = (size_t)env_int("MF_GEMV_TMA_STAGE_KB", mf::GT_STAGE_TARGET / 1024) * 1024;
+    static const size_t ring_bytes = (size_t)env_int("MF_GEMV_TMA_RING_KB", mf::GT_RING_BYTES / 1024) * 1024;
+    static const int cps = std::max(1, env_int("MF_GEMV_TMA_CPS", 2));
     const int RU = ym == mf::Y_SWIGLU ? 2 : 1;
     const size_t row_bytes = (size_t)q.K * esz;
-    int rps = (int)(mf::GT_STAGE_TARGET / row_bytes) / RU * RU;
+    int rps = (int)(stage_target / row_bytes) / RU * RU;
     if (rps < RU) rps = RU;
     const size_t stage_bytes = (size_t)rps * row_bytes;
-    if (stage_bytes > 2 * (size_t)mf::GT_STAGE_TARGET) return 0;  // rows too wide for the ring
-    int stages = (int)(mf::GT_RING_BYTES / stage_bytes);
+    static const int max_row_kb = env_int("MF_GEMV_TMA_MAX_ROW_KB", 16);
+    if (row_bytes > (size_t)max_row_kb * 1024) return 0;  // wide rows: the register-fed kernel measured faster
+    if (stage_bytes > 2 * stage_target && stage_bytes > 2 * (size_t)mf::GT_STAGE_TARGET) return 0;
+    int stages = (int)(ring_bytes / stage_bytes);
     stages = std::max(2, std::min(stages, mf::GT_MAX_STAGES));
     const long long units = q.rows / RU;
-    long long grid = std::min<long long>(num_sms(), units);
+    long long grid = std::min<long long>((long long)num_sms() * cps, units);
     if (grid < 1) grid = 1;
     const size_t max_rows = (size_t)((units + grid - 1) / grid) * RU;
     const size_t smem = (size_t)stages * stage_bytes + max_rows * nwc * sizeof(float);
