@@ -165,6 +165,27 @@ cudaError_t launch(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStrea
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
+// Launch as clusters of `cluster` CTAs along x, with the programmatic-serialization attribute.
+cudaError_t launch_cluster(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args,
+                           int cluster) {
+    set_carveout_once(fn);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
 // Per-kernel one-time attribute setup + occupancy cache.
 struct KInfo {
     int max_smem_set = 0;
@@ -266,13 +287,32 @@ const void* gemv_tma_fn(int dtype, int xm, int ym, int nwc, int j) {
 int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_t st) {
     static const int on = env_int("MF_GEMV_TMA", 1);
     static const long long timeout_ms = env_int("MF_DECODE_TIMEOUT_MS", 1000);
+    // ring geometry and CTAs per SM (MF_GEMV_TMA_STAGE_KB / _RING_KB / _CPS: tuning knobs)
+    static const size_t stage_target = (size_t)env_int("MF_GEMV_TMA_STAGE_KB", mf::GT_STAGE_TARGET / 1024) * 1024;
+    static const size_t ring_bytes = (size_t)env_int("MF_GEMV_TMA_RING_KB", mf::GT_RING_BYTES / 1024) * 1024;
+    static const int cps = std::max(1, env_int("MF_GEMV_TMA_CPS", 2));
+    // rows up to 10 KB (K <= 5120 in bf16) run whole; wider rows of the plain
+    // store/residual forms are split over a cluster of CTAs (split-K, slices
+    // of at most 8 KB, reduced in distributed shared memory); MF_GEMV_TMA_SPLIT=0
+    // leaves those to the register-fed kernel
+    static const int max_row_kb = env_int("MF_GEMV_TMA_MAX_ROW_KB", 10);
+    static const int split_on = env_int("MF_GEMV_TMA_SPLIT", 1);
     if (!on) return 0;
     if (!(xm == mf::X_PLAIN || xm == mf::X_NORM) || !(ym == mf::Y_STORE || ym == mf::Y_RESID || ym == mf::Y_SWIGLU))
         return 0;
     if (q.expert_ids || q.counter || q.gather_logits) return 0;
     const int vec = vec_of(dtype);
     const size_t esz = esz_of(dtype);
-    const int NV = q.K / vec;
+    const size_t full_row = (size_t)q.K * esz;
+    int ks = 1;
+    if (full_row > (size_t)max_row_kb * 1024) {
+        if (!split_on || xm != mf::X_PLAIN || ym == mf::Y_SWIGLU) return 0;
+        for (int s = 2; s <= 8 && ks == 1; ++s)
+            if (q.K % s == 0 && (q.K / s) % (2 * vec) == 0 && (size_t)(q.K / s) * esz <= 8 * 1024) ks = s;
+        if (ks == 1) return 0;
+    }
+    const int Ks = q.K / ks;  // columns of this kernel's rows (a slice when split)
+    const int NV = Ks / vec;
     int nwc = 8, j = (NV + 8 * 32 - 1) / (8 * 32);
     if (j > 8) {
         nwc = 16;
@@ -289,24 +329,20 @@ int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_
     }
     const void* fn = gemv_tma_fn(dtype, xm, ym, nwc, j);
     if (!fn) return 0;
-    // ring geometry and CTAs per SM (MF_GEMV_TMA_STAGE_KB / _RING_KB / _CPS: tuning knobs)
-    static const size_t stage_target = (size_t)env_int("MF_GEMV_TMA_STAGE_KB", mf::GT_STAGE_TARGET / 1024) * 1024;
-    static const size_t ring_bytes = (size_t)env_int("MF_GEMV_TMA_RING_KB", mf::GT_RING_BYTES / 1024) * 1024;
-    static const int cps = std::max(1, env_int("MF_GEMV_TMA_CPS", 2));
     const int RU = ym == mf::Y_SWIGLU ? 2 : 1;
-    const size_t row_bytes = (size_t)q.K * esz;
+    const size_t row_bytes = (size_t)Ks * esz;
     int rps = (int)(stage_target / row_bytes) / RU * RU;
     if (rps < RU) rps = RU;
     const size_t stage_bytes = (size_t)rps * row_bytes;
-    static const int max_row_kb = env_int("MF_GEMV_TMA_MAX_ROW_KB", 16);
-    if (row_bytes > (size_t)max_row_kb * 1024) return 0;  // wide rows: the register-fed kernel measured faster
     if (stage_bytes > 2 * stage_target && stage_bytes > 2 * (size_t)mf::GT_STAGE_TARGET) return 0;
     int stages = (int)(ring_bytes / stage_bytes);
     stages = std::max(2, std::min(stages, mf::GT_MAX_STAGES));
     const long long units = q.rows / RU;
-    long long grid = std::min<long long>((long long)num_sms() * cps, units);
-    if (grid < 1) grid = 1;
-    const size_t max_rows = (size_t)((units + grid - 1) / grid) * RU;
+    // 16 consumer warps (rows wider than 256 vectors per warp) hold too many
+    // registers for two CTAs per SM: one CTA per SM then, in a single wave
+    long long nblk = std::min<long long>((long long)num_sms() * (nwc == 16 ? 1 : cps) / ks, units);
+    if (nblk < 1) nblk = 1;
+    const size_t max_rows = (size_t)((units + nblk - 1) / nblk) * RU;
     const size_t smem = (size_t)stages * stage_bytes + max_rows * nwc * sizeof(float);
     if (smem > 200 * 1024) return 0;
     int* status = decode_status_ptr();
@@ -318,7 +354,7 @@ int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_
     p.w = (const char*)q.w + q.w_offset * esz;
     p.row_bytes = row_bytes;
     p.rows = q.rows;
-    p.K = q.K;
+    p.K = Ks;
     p.x = q.x;
     p.nw = q.nw;
     p.eps = q.eps;
@@ -328,8 +364,11 @@ int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_
     p.stage_bytes = (uint32_t)stage_bytes;
     p.status = status;
     p.timeout_ns = (unsigned long long)std::max(1ll, timeout_ms) * 1000000ull;
+    p.ksplit = ks;
+    p.row_stride = full_row;
     void* args[] = {&p};
-    MF_CK(launch(fn, dim3((unsigned)grid), dim3((nwc + 1) * 32), smem, st, args));
+    if (ks == 1) MF_CK(launch(fn, dim3((unsigned)nblk), dim3((nwc + 1) * 32), smem, st, args));
+    else MF_CK(launch_cluster(fn, dim3((unsigned)(nblk * ks)), dim3((nwc + 1) * 32), smem, st, args, ks));
     return 1;
 }
 

@@ -25,8 +25,8 @@
 //
 // Two CTAs per SM with a 64 KB ring each (measured best in the 8B decode
 // step: 283 vs 277 tokens/s for the register-fed kernel alone); rows wider
-// than 16 KB (the K = 12288 down projection) stay on the register-fed kernel,
-// which measured faster there. Every mbarrier wait is bounded by a
+// than 10 KB (the K = 8192 / 12288 / 25600 projections) stay on the
+// register-fed kernel, which measured faster there. Every mbarrier wait is bounded by a
 // wall-clock deadline; on expiry the kernel records a status bit, stops
 // issuing copies, waits (bounded) for the copies it has in flight and returns.
 #pragma once
@@ -56,7 +56,29 @@ struct GemvTmaParams {
     uint32_t stage_bytes;     // rows_per_stage * row_bytes (16-byte multiple)
     int* status;              // timeout bit
     unsigned long long timeout_ns;
+    // split-K: a cluster of `ksplit` CTAs shares a row range, CTA rank r of the
+    // cluster takes columns [r*K, (r+1)*K) of rows `row_stride` bytes apart
+    // (K here is the slice width); rank 0 sums the ranks' partials through
+    // distributed shared memory. 1: no split (row_stride == row_bytes).
+    int ksplit;
+    unsigned long long row_stride;
 };
+
+MF_DEVICE uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+MF_DEVICE void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+MF_DEVICE float ld_cluster_f32(const float* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
 
 // Dynamic shared memory: the ring, then the per-row partial sums [rows of this CTA][NWC].
 // J: 16-byte vectors per lane of a row (the warp's K slice is at most 32*J vectors).
@@ -71,8 +93,13 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const long long units = p.rows / RU;
-    const int r0 = (int)((long long)blockIdx.x * units / gridDim.x) * RU;
-    const int r1 = (int)((long long)(blockIdx.x + 1) * units / gridDim.x) * RU;
+    const int ks = p.ksplit;
+    const uint32_t krank = ks > 1 ? cluster_rank() : 0u;
+    const int blk = blockIdx.x / ks, nblk = gridDim.x / ks;
+    const int r0 = (int)((long long)blk * units / nblk) * RU;
+    const int r1 = (int)((long long)(blk + 1) * units / nblk) * RU;
+    // this CTA's column slice starts kofs bytes into each row
+    const unsigned long long kofs = (unsigned long long)krank * p.row_bytes;
     const int nrows = r1 - r0;
     const int nchunks = (nrows + p.rows_per_stage - 1) / p.rows_per_stage;
     const int S = p.stages;
@@ -104,8 +131,14 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
                 const int rr = min(p.rows_per_stage, nrows - c * p.rows_per_stage);
                 const uint32_t bytes = (uint32_t)(rr * p.row_bytes);
                 mbar_expect_tx(&full[s], bytes);
-                bulk_load(gt_smem + (size_t)s * p.stage_bytes, p.w + (size_t)(r0 + c * p.rows_per_stage) * p.row_bytes,
-                          bytes, &full[s]);
+                const char* src = p.w + (size_t)(r0 + c * p.rows_per_stage) * p.row_stride + kofs;
+                if (ks == 1) {
+                    bulk_load(gt_smem + (size_t)s * p.stage_bytes, src, bytes, &full[s]);
+                } else {  // the slices of consecutive rows are row_stride apart: one copy per row
+                    for (int r = 0; r < rr; ++r)
+                        bulk_load(gt_smem + (size_t)s * p.stage_bytes + (size_t)r * p.row_bytes,
+                                  src + (size_t)r * p.row_stride, (uint32_t)p.row_bytes, &full[s]);
+                }
             }
             if (failed) {
                 atomicOr(p.status, GT_STATUS_TIMEOUT);
@@ -116,6 +149,12 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
             bool drain_failed = false;
             for (int d = max(0, c - S); d < c; ++d)
                 mbar_wait(&full[d % S], (uint32_t)((d / S) & 1), deadline + p.timeout_ns, drain_failed);
+        }
+        if (ks > 1) {
+            // the cluster barriers of the split-K epilogue count every thread
+            __syncwarp();
+            cluster_sync_all();
+            cluster_sync_all();
         }
         return;
     }
@@ -133,7 +172,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
 #pragma unroll
         for (int e = 0; e < VEC; e += 4) {
             float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (v < v1) t = __ldcg(reinterpret_cast<const float4*>(p.x + (size_t)v * VEC + e));
+            if (v < v1) t = __ldcg(reinterpret_cast<const float4*>(p.x + (size_t)krank * p.K + (size_t)v * VEC + e));
             xr[j][e] = t.x; xr[j][e + 1] = t.y; xr[j][e + 2] = t.z; xr[j][e + 3] = t.w;
             if (XM == X_NORM) {
                 ss = fmaf(t.x, t.x, ss);
@@ -235,6 +274,23 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
     // unbounded); then all of them leave together when any gave up (the
     // producer drains the copies in flight)
     asm volatile("bar.sync 1, %0;" ::"r"(NWC * 32) : "memory");
+    if (ks > 1) {
+        // split-K: rank 0 sums the cluster's partials (rank order, then warp
+        // order) and applies the epilogue; the second barrier keeps every
+        // rank's shared memory alive until rank 0 has read it
+        cluster_sync_all();
+        if (krank == 0 && !*(volatile int*)&abort_s) {
+            for (int u = tid; u < nrows; u += NWC * 32) {
+                float s2 = 0.f;
+                for (int kr = 0; kr < ks; ++kr)
+                    for (int w2 = 0; w2 < NWC; ++w2) s2 += ld_cluster_f32(part + (size_t)u * NWC + w2, (uint32_t)kr);
+                if (YM == Y_RESID) p.y[r0 + u] = __ldcg(p.y + r0 + u) + s2;
+                else p.y[r0 + u] = s2;
+            }
+        }
+        cluster_sync_all();
+        return;
+    }
     if (*(volatile int*)&abort_s) return;
 
     // ---- epilogue: fixed-order sum of the warp partials of every row

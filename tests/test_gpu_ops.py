@@ -219,6 +219,30 @@ def test_rmsnorm_matmul_and_residual(ops, orc, gpu, dt):
 
 
 @pytest.mark.parametrize("dt", [0, 1, 2])
+@pytest.mark.parametrize("d_out,d_in", [(4096, 12288), (5120, 25600), (1024, 3072), (3000, 8192)])
+def test_matmul_residual_wide_rows(ops, gpu, dt, d_out, d_in):
+    """The residual GEMV of the down projections (rows of 12-51 KB: split over
+    a cluster of CTAs, partials reduced in distributed shared memory) against
+    a float64 product, within an fp32 dot-product bound."""
+    if dt == 0 and d_in > 8192:
+        pytest.skip("fp32 case covered by the narrower shapes")
+    rng = np.random.default_rng(d_out + d_in + dt)
+    a = rng.standard_normal(d_in).astype(np.float32)
+    w = cast_weights(rng.standard_normal(d_out * d_in).astype(np.float32) * 0.02, DT_NAME[dt])
+    res = rng.standard_normal(d_out).astype(np.float32)
+    rt = T(res, gpu)
+    wt = T(w.view(np.int16) if dt else w, gpu)
+    for rep in range(2):  # twice: the second call starts from the first result
+        ops.matmul_residual(rt, T(a, gpu), wt, d_out, d_in, dtype=DT_NAME[dt])
+    W = widen(w, dt).reshape(d_out, d_in)
+    prod = W @ a.astype(np.float64)
+    exact = res.astype(np.float64) + 2 * prod
+    tol = 2 * dot_tol(np.abs(W) @ np.abs(a.astype(np.float64)), d_in) + 2 * EPS32 * np.abs(exact)
+    got = rt.cpu().numpy()
+    assert np.all(np.abs(got - exact) <= tol), np.max(np.abs(got - exact) / tol)
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2])
 def test_swiglu(ops, orc, gpu, dt):
     rng = np.random.default_rng(11 + dt)
     d_in, F = 1024, 1536
