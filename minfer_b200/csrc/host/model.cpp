@@ -773,7 +773,7 @@ bool Qwen3Model::prefill(const uint32_t* tokens, int n, int pos0, bool compute_l
     rs_.h_step[0] = (int32_t)tokens[n - 1];
     rs_.h_step[1] = pos0 + n - 1;
     rs_.h_step[3] = 0;
-    rs_.h_step[MF_STEP_FRAME] += 1;
+    rs_.h_step[MF_STEP_FRAME] = next_frame();
     const int frame = frame_base_ + (host_logits ? (rs_.topk_k > 0 ? 8 : 6) : 5);
     const int rc = mf_begin_frame(rank_, frame);
     if (rc < 0) check(rc, "begin_frame");
@@ -874,7 +874,7 @@ void Qwen3Model::forward(uint32_t token, int pos, bool compute_logits, bool host
     rs_.h_step[0] = (int32_t)token;
     rs_.h_step[1] = pos;
     rs_.h_step[3] = 0;
-    rs_.h_step[MF_STEP_FRAME] += 1;  // every frame gets a new sequence number
+    rs_.h_step[MF_STEP_FRAME] = next_frame();  // every frame gets a new sequence number
     const int frame = frame_base_ + (compute_logits ? (host_logits ? (rs_.topk_k > 0 ? 7 : 2) : 0) : 1);
     const int rc = mf_begin_frame(rank_, frame);
     if (rc < 0) check(rc, "begin_frame");
@@ -1027,7 +1027,7 @@ uint32_t Qwen3Model::decode_chained(uint32_t token, int start_pos, int n) {
     rs_.h_step[0] = (int32_t)token;
     rs_.h_step[1] = start_pos;
     rs_.h_step[3] = 1;
-    rs_.h_step[MF_STEP_FRAME] += 1;  // later frames advance it on the device
+    rs_.h_step[MF_STEP_FRAME] = next_frame();  // later frames advance it on the device
     for (int i = 0; i < n; ++i) {
         // frame kind 3 uploads the host record once; kind 4 continues from the
         // record the previous frame's lm_head advanced on the device
@@ -1049,6 +1049,7 @@ uint32_t Qwen3Model::decode_chained(uint32_t token, int start_pos, int n) {
     check(mf_sync(rank_), "sync");
     const uint32_t last = (uint32_t)rs_.h_step[2];
     rs_.h_step[3] = 0;
+    frame_seq_ = rs_.h_step[MF_STEP_FRAME];  // the chained lm_heads advanced it on the device
     check_exchange_status();
     return last;
 }

@@ -227,6 +227,12 @@ private:
     RunParams rp_;
     int rank_ = 0;
     int frame_base_ = 0;  // this model's frame ids: frame_base_ + kind
+    // Sequence number of this model's frames, written to the step record's
+    // frame field (tensor-parallel exchange tags derive from it). Kept per
+    // model: the step record is shared by every model on the device, and all
+    // ranks of a sharded model must count only that model's frames.
+    int32_t frame_seq_ = 0;
+    int32_t next_frame() { return ++frame_seq_; }
     DeviceType device_ = DeviceType::CPU;
     std::vector<std::unique_ptr<BaseLayer>> layers_;
     RunState rs_;

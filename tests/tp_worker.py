@@ -166,6 +166,17 @@ def check_model(name, rank, world):
     assert same_on_all_ranks(s_ids), f"{name}: ranks disagree on sampled ids"
     flips = check_sampled(s_ids, s_ref, cands, s_lg, 20, 0.7, 0.9, 0.0, uniform_draws(42, G), name)
     assert len(flips) <= 1, f"{name}: sampled flips {flips}"
+    # a single-GPU model on rank 0's device runs frames the other ranks never
+    # see; the sharded model's exchanges still line up (frame numbers are kept
+    # per model, not per device)
+    if rank == 0:
+        solo = mm.Qwen3Model(path, mm.RunParams(num_iters=4, max_seq_len=P + 5)).set_device("cuda")
+        solo.generate(prompt, 4)
+        solo.close()
+    dist.barrier()
+    again, _, _ = m.generate(prompt, G, forced=ref_ids)
+    assert list(again) == list(ids), f"{name}: decode after another model's frames differs"
+    assert same_on_all_ranks(again)
     for mod in (m, m2, m3, ms):
         assert mod.comm_status() == 0, f"{name}: an exchange wait gave up"
         mod.close()
