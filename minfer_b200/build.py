@@ -115,11 +115,20 @@ def build_oracle(reference: str | None = None) -> None:
     _run(["make", "-s", "-C", str(ORACLE), f"REF={ref}", *targets])
 
 
+def build_integration(reference: str | None = None) -> None:
+    """minfer's own host loop linked against the CUDA runtime
+    (integration/cuda_backend.cpp), where the reference sources are present."""
+    ref = reference or os.environ.get("MF_REFERENCE", "/root/reference")
+    if Path(ref, "src", "base", "model.cpp").exists():
+        _run(["make", "-s", "-C", str(ROOT / "integration"), f"REF={ref}"])
+
+
 def build_all(force: bool = False, oracle: bool = True) -> None:
     build_cuda(force)
     build_host(force)
     if oracle:
         build_oracle()
+        build_integration()
 
 
 if __name__ == "__main__":

@@ -297,8 +297,12 @@ int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_
     // leaves those to the register-fed kernel
     static const int max_row_kb = env_int("MF_GEMV_TMA_MAX_ROW_KB", 10);
     static const int split_on = env_int("MF_GEMV_TMA_SPLIT", 1);
+    static const int tp_on = env_int("MF_GEMV_TMA_TP", 1);  // the tensor-parallel receive/send forms
     if (!on) return 0;
-    if (!(xm == mf::X_PLAIN || xm == mf::X_NORM) || !(ym == mf::Y_STORE || ym == mf::Y_RESID || ym == mf::Y_SWIGLU))
+    const bool tp = xm == mf::X_AR_NORM || ym == mf::Y_PUSH;
+    if (tp && !tp_on) return 0;
+    if (!(xm == mf::X_PLAIN || xm == mf::X_NORM || xm == mf::X_AR_NORM) ||
+        !(ym == mf::Y_STORE || ym == mf::Y_RESID || ym == mf::Y_SWIGLU || ym == mf::Y_PUSH))
         return 0;
     if (q.expert_ids || q.counter || q.gather_logits) return 0;
     const int vec = vec_of(dtype);
@@ -338,18 +342,26 @@ int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_
     int stages = (int)(ring_bytes / stage_bytes);
     stages = std::max(2, std::min(stages, mf::GT_MAX_STAGES));
     const long long units = q.rows / RU;
-    // 16 consumer warps (rows wider than 256 vectors per warp) hold too many
-    // registers for two CTAs per SM: one CTA per SM then, in a single wave
-    long long nblk = std::min<long long>((long long)num_sms() * (nwc == 16 ? 1 : cps) / ks, units);
-    if (nblk < 1) nblk = 1;
-    const size_t max_rows = (size_t)((units + nblk - 1) / nblk) * RU;
-    const size_t smem = (size_t)stages * stage_bytes + max_rows * nwc * sizeof(float);
-    if (smem > 200 * 1024) return 0;
     int* status = decode_status_ptr();
     if (!status) return 0;
-    int bps = 0;
-    int rc = prepare(fn, (nwc + 1) * 32, smem, &bps);
-    if (rc) return rc;
+    // CTAs per SM: `cps` (one with 16 consumer warps), fewer when the
+    // occupancy calculation says they do not fit; the grid is one wave (all
+    // CTAs resident at once, which the all-reduce receive's grid barrier needs)
+    int want = nwc == 16 ? 1 : cps;
+    long long nblk = 1;
+    size_t smem = 0;
+    for (int attempt = 0;; ++attempt) {
+        nblk = std::max<long long>(1, std::min<long long>((long long)num_sms() * want / ks, units));
+        const size_t max_rows = (size_t)((units + nblk - 1) / nblk) * RU;
+        smem = (size_t)stages * stage_bytes + max_rows * nwc * sizeof(float);
+        if (smem > 200 * 1024) return 0;
+        int bps = 0;
+        int rc = prepare(fn, (nwc + 1) * 32, smem, &bps);
+        if (rc) return rc;
+        if (bps >= want) break;
+        if (bps < 1 || attempt > 0) return 0;
+        want = bps;
+    }
     mf::GemvTmaParams p = {};
     p.w = (const char*)q.w + q.w_offset * esz;
     p.row_bytes = row_bytes;
@@ -366,6 +378,14 @@ int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_
     p.timeout_ns = (unsigned long long)std::max(1ll, timeout_ms) * 1000000ull;
     p.ksplit = ks;
     p.row_stride = full_row;
+    if (tp) {
+        p.comm = q.comm;
+        p.ar_seq = q.ar_seq;
+        p.step = q.step;
+        p.x_res = q.x_res;
+        p.x_out = q.x_out;
+        if (xm == mf::X_AR_NORM) p.x = q.x_out;  // read after the receive and the grid barrier
+    }
     void* args[] = {&p};
     if (ks == 1) MF_CK(launch(fn, dim3((unsigned)nblk), dim3((nwc + 1) * 32), smem, st, args));
     else MF_CK(launch_cluster(fn, dim3((unsigned)(nblk * ks)), dim3((nwc + 1) * 32), smem, st, args, ks));

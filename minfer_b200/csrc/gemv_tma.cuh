@@ -31,6 +31,7 @@
 // issuing copies, waits (bounded) for the copies it has in flight and returns.
 #pragma once
 
+#include "comm.cuh"
 #include "mbarrier.cuh"
 #include "mf_common.cuh"
 
@@ -62,6 +63,13 @@ struct GemvTmaParams {
     // distributed shared memory. 1: no split (row_stride == row_bytes).
     int ksplit;
     unsigned long long row_stride;
+    // tensor parallelism (X_AR_NORM receive in the prologue, Y_PUSH send in
+    // the epilogue; the same exchange protocol as the register-fed kernel)
+    CommDev comm;
+    int ar_seq;
+    const int* step;        // device step record (frame number for the tags)
+    const float* x_res;     // X_AR_NORM: residual before the all-reduce (x is then x_out)
+    float* x_out;           // X_AR_NORM: residual after it
 };
 
 MF_DEVICE uint32_t cluster_rank() {
@@ -78,6 +86,13 @@ MF_DEVICE float ld_cluster_f32(const float* local, uint32_t rank) {
     float v;
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
     return v;
+}
+
+// Y_PUSH: row `row` of this rank's partial, as a tagged word into every
+// rank's receive slot of exchange ar_seq.
+MF_DEVICE void push_row(const GemvTmaParams& p, int row, float v) {
+    const unsigned long long w = tagged(v, comm_tag(__ldcg(p.step + MF_STEP_FRAME), p.ar_seq));
+    for (int r = 0; r < p.comm.tp_size; ++r) st_tagged(p.comm.recv(r, p.ar_seq & 1, p.comm.tp_rank) + row, w);
 }
 
 // Dynamic shared memory: the ring, then the per-row partial sums [rows of this CTA][NWC].
@@ -165,6 +180,26 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
     float xr[J][VEC];
     pdl_launch_dependents();
     pdl_wait();
+    if (XM == X_AR_NORM) {
+        // all-reduce receive: each CTA sums its slice of x = residual +
+        // partial_0 + ... (rank order) into x_out as the tagged words arrive;
+        // after a grid barrier (every CTA of the grid is resident: the grid
+        // fits the GPU and the next kernel launches only once all of these
+        // CTAs started) every consumer reads its K slice of the reduced x
+        const uint32_t tag = comm_tag(__ldcg(p.step + MF_STEP_FRAME), p.ar_seq);
+        const int slot = p.ar_seq & 1;
+        int* cst = &p.comm.local()->status;
+        const unsigned long long dl = globaltimer_ns() + p.comm.timeout_ns;
+        bool late = false;
+        const int e0 = (int)((long long)blockIdx.x * p.K / gridDim.x);
+        const int e1 = (int)((long long)(blockIdx.x + 1) * p.K / gridDim.x);
+        recv_sum(p.comm, slot, tag, p.x_res, e0 + tid, NWC * 32, e1, dl, &late, cst,
+                 [&](int i, float v) { p.x_out[i] = v; });
+        __threadfence();
+        asm volatile("bar.sync 1, %0;" ::"r"(NWC * 32) : "memory");
+        if (tid == 0) grid_arrive_wait(&p.comm.local()->bar[slot], tag, gridDim.x, dl, &late, cst, COMM_STATUS_AR_TIMEOUT);
+        asm volatile("bar.sync 1, %0;" ::"r"(NWC * 32) : "memory");
+    }
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
@@ -174,7 +209,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
             float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
             if (v < v1) t = __ldcg(reinterpret_cast<const float4*>(p.x + (size_t)krank * p.K + (size_t)v * VEC + e));
             xr[j][e] = t.x; xr[j][e + 1] = t.y; xr[j][e + 2] = t.z; xr[j][e + 3] = t.w;
-            if (XM == X_NORM) {
+            if (XM == X_NORM || XM == X_AR_NORM) {
                 ss = fmaf(t.x, t.x, ss);
                 ss = fmaf(t.y, t.y, ss);
                 ss = fmaf(t.z, t.z, ss);
@@ -182,7 +217,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
             }
         }
     }
-    if (XM == X_NORM) {
+    if (XM == X_NORM || XM == X_AR_NORM) {
         // src/ops/kernels.cpp:355-363: inv = 1/sqrtf(sum(x^2)/dim + eps); out = inv * x * w
         ss = warp_sum(ss);
         if (lane == 0) ss_part[warp] = ss;
@@ -285,6 +320,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
                 for (int kr = 0; kr < ks; ++kr)
                     for (int w2 = 0; w2 < NWC; ++w2) s2 += ld_cluster_f32(part + (size_t)u * NWC + w2, (uint32_t)kr);
                 if (YM == Y_RESID) p.y[r0 + u] = __ldcg(p.y + r0 + u) + s2;
+                else if (YM == Y_PUSH) push_row(p, r0 + u, s2);
                 else p.y[r0 + u] = s2;
             }
         }
@@ -306,6 +342,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
             float s2 = 0.f;
             for (int w2 = 0; w2 < NWC; ++w2) s2 += part[(size_t)u * NWC + w2];
             if (YM == Y_RESID) p.y[r0 + u] = __ldcg(p.y + r0 + u) + s2;  // src/models/qwen3/module.cpp:238-240
+            else if (YM == Y_PUSH) push_row(p, r0 + u, s2);
             else p.y[r0 + u] = s2;
         }
     }
@@ -323,6 +360,10 @@ const void* gemv_tma_ptr(int xm, int ym, int nwc, int j) {
         if (xm == X_PLAIN && ym == Y_STORE) return (const void*)&gemv_tma_kernel<W, NW, JJ, X_PLAIN, Y_STORE>; \
         if (xm == X_PLAIN && ym == Y_RESID) return (const void*)&gemv_tma_kernel<W, NW, JJ, X_PLAIN, Y_RESID>; \
         if (xm == X_NORM && ym == Y_SWIGLU) return (const void*)&gemv_tma_kernel<W, NW, JJ, X_NORM, Y_SWIGLU>; \
+        if (xm == X_AR_NORM && ym == Y_STORE) return (const void*)&gemv_tma_kernel<W, NW, JJ, X_AR_NORM, Y_STORE>; \
+        if (xm == X_AR_NORM && ym == Y_SWIGLU)                                                                \
+            return (const void*)&gemv_tma_kernel<W, NW, JJ, X_AR_NORM, Y_SWIGLU>;                            \
+        if (xm == X_PLAIN && ym == Y_PUSH) return (const void*)&gemv_tma_kernel<W, NW, JJ, X_PLAIN, Y_PUSH>; \
         return nullptr;                                                                                       \
     }
     MF_GT(8, 1)
