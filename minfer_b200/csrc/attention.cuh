@@ -52,6 +52,13 @@ constexpr int ATT_MAX_SPLIT = 128;  // merge tables live in the score area
 // merge, (m, l) and a scale factor per slice.
 constexpr int ATT_HEAD_AREA = ATT_SC_STRIDE > 3 * ATT_MAX_SPLIT ? ATT_SC_STRIDE : 3 * ATT_MAX_SPLIT;
 constexpr int ATT_PF_ROWS = 128;    // rows of K and of V prefetched into L2 before the dependency wait
+// A merging CTA pulls partials through its ring in batches of NB = ring /
+// (G * D) slices. More than two batches' worth of slices are merged in two
+// levels instead: the last CTA of each group of min(NB, 16) slices merges the
+// group, the last group merger merges the groups (a single CTA merging 128
+// slices of 8 heads took longer than streaming them).
+constexpr int ATT_MERGE_GROUP = 16;
+constexpr int ATT_MAX_GROUPS = 16;  // ATT_MAX_SPLIT / (smallest group, 10 slices for 16 heads), rounded up
 
 struct AttnParams {
     const float* qkv;        // [Hq*D | Hkv*D | Hkv*D] (this rank's heads)
@@ -66,7 +73,9 @@ struct AttnParams {
     float* out;              // [Hq*D]
     float* part_o;           // [Hkv][n_split][G][D]
     float* part_ml;          // [Hkv][n_split][G][2]
-    int* counters;           // [Hkv], zero-initialised, reset by the last CTA
+    int* counters;           // [Hkv] then [Hkv][ATT_MAX_GROUPS], zero-initialised, reset by the mergers
+    float* group_o;          // [Hkv][ATT_MAX_GROUPS][G][D] merged groups (two-level merge)
+    float* group_ml;         // [Hkv][ATT_MAX_GROUPS][G][2]
     int n_heads;
     int n_kv_heads;
     int n_split;
@@ -468,84 +477,127 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
         p.part_ml[(pbase + tid) * 2 + 1] = l_s[tid];
     }
 
-    // ---- the last CTA of this KV head merges the slices
+    // ---- merge: the last CTA of this KV head (or, with more than
+    // ATT_MERGE_GROUP slices, of this slice's group, then the last of the
+    // group mergers) combines partials with the (max, sum, vector) rescaling
+    constexpr int NB = (ATT_STAGES * ATT_TILE_FLOATS) / (G * ATT_D);
+    constexpr int MG = NB < ATT_MERGE_GROUP ? NB : ATT_MERGE_GROUP;
+    static_assert((ATT_MAX_SPLIT + MG - 1) / MG <= ATT_MAX_GROUPS, "merge groups");
+    const int ns = sl.eff;
+    const bool two = ns > 2 * NB;
+    const int grp = split / MG;
+    const int ngroups = (ns + MG - 1) / MG;
+    int* gcnt = p.counters + Hkv + (size_t)kvh * ATT_MAX_GROUPS + grp;
     __syncthreads();
     if (tid == 0) {
         __threadfence();
-        const int ticket = atomicAdd(p.counters + kvh, 1);
-        is_last = (ticket == sl.eff - 1);
+        const int gsz = two ? min(MG, ns - grp * MG) : ns;
+        const int ticket = atomicAdd(two ? gcnt : p.counters + kvh, 1);
+        is_last = (ticket == gsz - 1);
     }
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    const int ns = sl.eff;
-    const size_t hb = (size_t)kvh * p.n_split * G;
-    float* ml = sc_s;    // [ns][G][2], then the scale factors [ns][G] (ns <= ATT_MAX_SPLIT: both fit G * ATT_HEAD_AREA)
+    float* ml = sc_s;    // [n][G][2], then the scale factors [n][G] (n <= ATT_MAX_SPLIT: both fit G * ATT_HEAD_AREA)
     float* fs = sc_s + 2 * ATT_MAX_SPLIT * G;
     float* po = ring;    // a batch of partial outputs [nb][G][D]
-    constexpr int NB = (ATT_STAGES * ATT_TILE_FLOATS) / (G * ATT_D);
-    auto issue_batch = [&](int s0) {
-        const int nb = min(NB, ns - s0);
-        const float* src = p.part_o + (hb + (size_t)s0 * G) * ATT_D;
-        for (int i = tid; i < nb * G * ATT_D / 4; i += NT) cp_async16(po + 4 * i, src + 4 * i);
-        cp_async_commit();
-    };
-    issue_batch(0);
-    for (int i = tid; i < ns * G * 2; i += NT) ml[i] = __ldcg(p.part_ml + hb * 2 + i);
-    __syncthreads();
-    // per head: global max, per-slice factors, denominator (one warp per head)
-    for (int g = warp; g < G; g += ATT_WARPS) {
-        float M = -INFINITY;
-        for (int s0 = lane; s0 < ns; s0 += 32) M = fmaxf(M, ml[(s0 * G + g) * 2]);
-        M = warp_max(M);
-        float L = 0.f;
-        for (int s0 = lane; s0 < ns; s0 += 32) {
-            const float ms = ml[(s0 * G + g) * 2];
-            const float f = (ms == -INFINITY) ? 0.f : expf(ms - M);
-            fs[s0 * G + g] = f;
-            L = fmaf(f, ml[(s0 * G + g) * 2 + 1], L);
-        }
-        L = warp_sum(L);
-        if (lane == 0) a_s[g] = L;
-    }
-    // every thread owns float4 outputs idx4 = tid + k*NT of [G][D/4]
     constexpr int PER = (G * ATT_D / 4 + NT - 1) / NT;
-    float4 acc[PER];
-#pragma unroll
-    for (int k = 0; k < PER; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s0 = 0; s0 < ns; s0 += NB) {
-        cp_async_wait<0>();
+    // Merges n partials (src_o [n][G][D], src_ml [n][G][2]); final: writes the
+    // normalised output, else the merged partial (dst_o [G][D], dst_ml [G][2]).
+    auto merge = [&](const float* src_o, const float* src_ml, int n, bool final, float* dst_o, float* dst_ml) {
+        auto issue_batch = [&](int s0) {
+            const int nb = min(NB, n - s0);
+            const float* src = src_o + (size_t)s0 * G * ATT_D;
+            for (int i = tid; i < nb * G * ATT_D / 4; i += NT) cp_async16(po + 4 * i, src + 4 * i);
+            cp_async_commit();
+        };
+        issue_batch(0);
+        for (int i = tid; i < n * G * 2; i += NT) ml[i] = __ldcg(src_ml + i);
         __syncthreads();
-        const int nb = min(NB, ns - s0);
+        // per head: max, per-partial factors, denominator (one warp per head)
+        for (int g = warp; g < G; g += ATT_WARPS) {
+            float M = -INFINITY;
+            for (int s0 = lane; s0 < n; s0 += 32) M = fmaxf(M, ml[(s0 * G + g) * 2]);
+            M = warp_max(M);
+            float L = 0.f;
+            for (int s0 = lane; s0 < n; s0 += 32) {
+                const float ms = ml[(s0 * G + g) * 2];
+                const float f = (ms == -INFINITY) ? 0.f : expf(ms - M);
+                fs[s0 * G + g] = f;
+                L = fmaf(f, ml[(s0 * G + g) * 2 + 1], L);
+            }
+            L = warp_sum(L);
+            if (lane == 0) {
+                a_s[g] = L;
+                m_s[g] = M;
+            }
+        }
+        // every thread owns float4 outputs idx4 = tid + k*NT of [G][D/4]
+        float4 acc[PER];
+#pragma unroll
+        for (int k = 0; k < PER; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s0 = 0; s0 < n; s0 += NB) {
+            cp_async_wait<0>();
+            __syncthreads();
+            const int nb = min(NB, n - s0);
+#pragma unroll
+            for (int k = 0; k < PER; ++k) {
+                const int idx4 = tid + k * NT;
+                if (idx4 < G * ATT_D / 4) {
+                    const int g = idx4 / (ATT_D / 4);
+                    for (int b = 0; b < nb; ++b) {
+                        const float f = fs[(s0 + b) * G + g];
+                        const float4 v = reinterpret_cast<const float4*>(po + (size_t)b * G * ATT_D)[idx4];
+                        acc[k].x = fmaf(f, v.x, acc[k].x);
+                        acc[k].y = fmaf(f, v.y, acc[k].y);
+                        acc[k].z = fmaf(f, v.z, acc[k].z);
+                        acc[k].w = fmaf(f, v.w, acc[k].w);
+                    }
+                }
+            }
+            if (s0 + NB < n) {
+                __syncthreads();  // the batch buffer is refilled
+                issue_batch(s0 + NB);
+            }
+        }
 #pragma unroll
         for (int k = 0; k < PER; ++k) {
             const int idx4 = tid + k * NT;
             if (idx4 < G * ATT_D / 4) {
-                const int g = idx4 / (ATT_D / 4);
-                for (int b = 0; b < nb; ++b) {
-                    const float f = fs[(s0 + b) * G + g];
-                    const float4 v = reinterpret_cast<const float4*>(po + (size_t)b * G * ATT_D)[idx4];
-                    acc[k].x = fmaf(f, v.x, acc[k].x);
-                    acc[k].y = fmaf(f, v.y, acc[k].y);
-                    acc[k].z = fmaf(f, v.z, acc[k].z);
-                    acc[k].w = fmaf(f, v.w, acc[k].w);
-                }
+                const float L = a_s[idx4 / (ATT_D / 4)];
+                reinterpret_cast<float4*>(dst_o)[idx4] =
+                    final ? make_float4(acc[k].x / L, acc[k].y / L, acc[k].z / L, acc[k].w / L) : acc[k];
             }
         }
-        if (s0 + NB < ns) {
-            __syncthreads();  // the batch buffer is refilled
-            issue_batch(s0 + NB);
+        if (!final && tid < G) {
+            dst_ml[tid * 2 + 0] = m_s[tid];
+            dst_ml[tid * 2 + 1] = a_s[tid];
         }
+        __syncthreads();  // smem staging is reused by a following merge
+    };
+    const size_t hb = (size_t)kvh * p.n_split * G;
+    float* out = p.out + (size_t)kvh * G * ATT_D;
+    if (!two) {
+        merge(p.part_o + hb * ATT_D, p.part_ml + hb * 2, ns, true, out, nullptr);
+        if (tid == 0) p.counters[kvh] = 0;
+        return;
     }
-#pragma unroll
-    for (int k = 0; k < PER; ++k) {
-        const int idx4 = tid + k * NT;
-        if (idx4 < G * ATT_D / 4) {
-            const float L = a_s[idx4 / (ATT_D / 4)];
-            reinterpret_cast<float4*>(p.out + (size_t)kvh * G * ATT_D)[idx4] =
-                make_float4(acc[k].x / L, acc[k].y / L, acc[k].z / L, acc[k].w / L);
-        }
+    // level 1: this group's slices -> group partial
+    const size_t gb = ((size_t)kvh * ATT_MAX_GROUPS + grp) * G;
+    const int gs0 = grp * MG, gsz = min(MG, ns - gs0);
+    merge(p.part_o + (hb + (size_t)gs0 * G) * ATT_D, p.part_ml + (hb + (size_t)gs0 * G) * 2, gsz, false,
+          p.group_o + gb * ATT_D, p.group_ml + gb * 2);
+    if (tid == 0) {
+        *gcnt = 0;
+        __threadfence();
+        is_last = (atomicAdd(p.counters + kvh, 1) == ngroups - 1);
     }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    // level 2: the groups -> output
+    const size_t g0 = (size_t)kvh * ATT_MAX_GROUPS * G;
+    merge(p.group_o + g0 * ATT_D, p.group_ml + g0 * 2, ngroups, true, out, nullptr);
     if (tid == 0) p.counters[kvh] = 0;
 }
 
@@ -554,5 +606,24 @@ inline size_t attn_smem_bytes(int G) {
 }
 // Largest n_split the merge supports.
 inline int attn_max_split(int G) { return ATT_MAX_SPLIT; }
+
+// Workspace layout (byte offsets): counters | per-slice (m, l) | per-slice
+// outputs | per-group (m, l) | per-group outputs. Every part 256-byte aligned.
+struct AttnWsLayout {
+    size_t cnt, ml, o, gml, go, total;
+};
+inline AttnWsLayout attn_ws_layout(int n_kv_heads, int n_split, int G) {
+    auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+    AttnWsLayout L;
+    const size_t H = (size_t)n_kv_heads;
+    L.cnt = 0;
+    L.ml = al(H * (1 + ATT_MAX_GROUPS) * sizeof(int));
+    L.o = L.ml + al(H * n_split * G * 2 * sizeof(float));
+    L.gml = L.o + al(H * n_split * G * ATT_D * sizeof(float));
+    const bool two = n_split > 2 * ((ATT_STAGES * ATT_TILE_FLOATS) / (G * ATT_D));
+    L.go = L.gml + (two ? al(H * ATT_MAX_GROUPS * G * 2 * sizeof(float)) : 0);
+    L.total = L.go + (two ? al(H * ATT_MAX_GROUPS * G * ATT_D * sizeof(float)) : 0);
+    return L;
+}
 
 }  // namespace mf

@@ -43,7 +43,6 @@ cudaStream_t resolve_stream(void* stream);    // capi.cu: NULL -> manager stream
 
 namespace {
 
-constexpr size_t kCounterBytes = 256;  // room for 64 KV heads' counters
 static __device__ __align__(256) unsigned char g_attn_scratch[MF_ATTN_NOALLOC_SCRATCH_BYTES];
 
 int noalloc_fail(int code, const char* msg) { return mf::record_error(code, msg); }
@@ -100,10 +99,9 @@ extern "C" int mf_attn_decode_noalloc(const mf_attn_desc* d, void* stream) {
     const int G = d->n_heads / d->n_kv_heads;
     const void* fn = mf::attn_kernel_ptr(G);
     if (!fn) return noalloc_fail(MF_E_UNSUPPORTED, "query heads per KV head without a kernel");
-    // scratch layout: counters | (m, l) per split and head | partial outputs
-    const size_t pml = ((size_t)d->n_kv_heads * d->n_split * G * 2 * sizeof(float) + 255) / 256 * 256;
-    const size_t po = (size_t)d->n_kv_heads * d->n_split * G * mf::ATT_D * sizeof(float);
-    if ((size_t)d->n_kv_heads * sizeof(int) > kCounterBytes || kCounterBytes + pml + po > MF_ATTN_NOALLOC_SCRATCH_BYTES)
+    // scratch layout: counters | (m, l) per split and head | partial outputs | merged groups
+    const mf::AttnWsLayout L = mf::attn_ws_layout(d->n_kv_heads, d->n_split, G);
+    if (L.total > MF_ATTN_NOALLOC_SCRATCH_BYTES)
         return noalloc_fail(MF_E_UNSUPPORTED, "request needs more scratch than MF_ATTN_NOALLOC_SCRATCH_BYTES");
     if (d->n_split > mf::attn_max_split(G)) return noalloc_fail(MF_E_UNSUPPORTED, "n_split above the merge table size");
     void* base = nullptr;
@@ -112,7 +110,7 @@ extern "C" int mf_attn_decode_noalloc(const mf_attn_desc* d, void* stream) {
     cudaStream_t st = mf::resolve_stream(stream);
     char* ws = (char*)base;
     // the counters must start at zero; a previous call may have been cut short
-    cudaError_t e = cudaMemsetAsync(ws, 0, kCounterBytes, st);
+    cudaError_t e = cudaMemsetAsync(ws + L.cnt, 0, L.ml - L.cnt, st);
     if (e != cudaSuccess) return noalloc_fail(MF_E_CUDA, cudaGetErrorString(e));
     const size_t smem = mf::attn_smem_bytes(G);
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -128,9 +126,11 @@ extern "C" int mf_attn_decode_noalloc(const mf_attn_desc* d, void* stream) {
     p.max_seq = d->max_seq;
     p.pos_ptr = (const int*)d->step_state + 1;  // {token, pos, next_token, chain}
     p.out = d->out;
-    p.counters = (int*)ws;
-    p.part_ml = (float*)(ws + kCounterBytes);
-    p.part_o = (float*)(ws + kCounterBytes + pml);
+    p.counters = (int*)(ws + L.cnt);
+    p.part_ml = (float*)(ws + L.ml);
+    p.part_o = (float*)(ws + L.o);
+    p.group_ml = (float*)(ws + L.gml);
+    p.group_o = (float*)(ws + L.go);
     p.n_heads = d->n_heads;
     p.n_kv_heads = d->n_kv_heads;
     p.n_split = d->n_split;

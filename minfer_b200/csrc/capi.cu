@@ -925,11 +925,7 @@ int mf_swiglu_matmul(float* h, const float* x, const float* norm_w, float eps, c
 
 size_t mf_attn_workspace_bytes(int n_heads, int n_kv_heads, int d_head, int n_split) {
     if (n_kv_heads <= 0 || n_heads <= 0 || n_split <= 0) return 0;
-    const size_t G = (size_t)n_heads / n_kv_heads;
-    const size_t po = (size_t)n_kv_heads * n_split * G * d_head * sizeof(float);
-    const size_t pml = (size_t)n_kv_heads * n_split * G * 2 * sizeof(float);
-    const size_t cnt = (size_t)n_kv_heads * sizeof(int);
-    return ((cnt + 255) / 256 * 256) + ((pml + 255) / 256 * 256) + po;
+    return mf::attn_ws_layout(n_kv_heads, n_split, n_heads / n_kv_heads).total;
 }
 
 int mf_attn_default_split(int n_kv_heads, int max_seq) {
@@ -962,8 +958,7 @@ int mf_attn_decode(const mf_attn_desc* d, void* stream) {
     int rc = prepare(fn, mf::ATT_WARPS * 32, smem, &bps);
     if (rc) return rc;
     char* ws = (char*)d->workspace;
-    const size_t cnt = ((size_t)d->n_kv_heads * sizeof(int) + 255) / 256 * 256;
-    const size_t pml = ((size_t)d->n_kv_heads * d->n_split * G * 2 * sizeof(float) + 255) / 256 * 256;
+    const mf::AttnWsLayout L = mf::attn_ws_layout(d->n_kv_heads, d->n_split, G);
     mf::AttnParams p = {};
     p.qkv = d->qkv;
     p.q_norm_w = d->q_norm_w;
@@ -975,9 +970,11 @@ int mf_attn_decode(const mf_attn_desc* d, void* stream) {
     p.max_seq = d->max_seq;
     p.pos_ptr = &((const mf::StepState*)d->step_state)->pos;
     p.out = d->out;
-    p.counters = (int*)ws;
-    p.part_ml = (float*)(ws + cnt);
-    p.part_o = (float*)(ws + cnt + pml);
+    p.counters = (int*)(ws + L.cnt);
+    p.part_ml = (float*)(ws + L.ml);
+    p.part_o = (float*)(ws + L.o);
+    p.group_ml = (float*)(ws + L.gml);
+    p.group_o = (float*)(ws + L.go);
     p.n_heads = d->n_heads;
     p.n_kv_heads = d->n_kv_heads;
     p.n_split = d->n_split;
