@@ -384,7 +384,8 @@ def measure_long_context(workload: str, ctx: int, steps: int, warmup: int, rank:
                                                     "peak_gbs": peaks["hbm_gbs"],
                                                     "frac": round(step_gbs / peaks["hbm_gbs"], 4)},
             "prefill_tok_per_s": round(ctx / prefill_s, 1), "exchange_status": status,
-            "parallelism": "single" if world == 1 else f"tp{world}", "load_seconds": round(t_load, 1),
+            "parallelism": "single" if world == 1 else (f"ep{world}" if info.n_experts > 0 else f"tp{world}"),
+            "load_seconds": round(t_load, 1),
             "file_seconds": round(t_gen, 1)}
 
 
@@ -462,7 +463,8 @@ def main():
     config = {"workload": f"{args.workload} greedy decode at batch 1 after a {args.context}-token prompt",
               "context": args.context, "batch": 1,
               "l2": "inputs larger than L2 (each step streams all weights and the KV cache)",
-              "parallelism": "single" if world == 1 else f"tp{world}"}
+              "parallelism": "single" if world == 1 else
+              (f"ep{world}" if cfgshape.n_experts > 0 else f"tp{world}")}
 
     if args.llama_bench:
         llama_bench_main(args)

@@ -357,6 +357,11 @@ int mf_prefill_norm_split(void* hi, void* lo, float* xn, const float* x, const f
                           int n_rows, void* stream);
 /* fp32 -> bf16 hi/lo split of n elements. */
 int mf_prefill_split(void* hi, void* lo, const float* x, size_t n, void* stream);
+/* h = silu(g) * u (src/models/qwen3/module.cpp:466-468) of fp32 gate/up rows
+ * [n_rows][2 d_ff] (columns 2i, 2i+1 = g_i, u_i), as bf16 hi/lo [n_rows][d_ff]:
+ * the SwiGLU step of fp32-weight models, whose gate/up GEMM runs as two
+ * products (weights split into bf16 hi + lo) that are summed before it. */
+int mf_prefill_swiglu_split(void* h_hi, void* h_lo, const float* gate_up, int n_rows, int d_ff, void* stream);
 /* x[t] = embedding row tokens[t] (device ids) for t < n_tokens. */
 int mf_prefill_embed(float* x, const void* emb, int dtype, int vocab, int d_model, const uint32_t* tokens,
                      int n_tokens, void* stream);

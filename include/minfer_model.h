@@ -119,8 +119,9 @@ int mf_model_generate_logits(mf_model* m, const uint32_t* prompt, size_t n_promp
  * token, src/base/model.cpp:120-129): tokens at positions [pos0, pos0 + n)
  * go through every layer as tcgen05 GEMMs, filling the KV cache; with
  * compute_logits the last token's logits / greedy id are then available as
- * after mf_model_forward. bf16 dense models on one GPU; others return
- * MF_E_UNSUPPORTED (use mf_model_forward per token). */
+ * after mf_model_forward. Dense models with bf16 weights, or fp32 weights (kept
+ * as bf16 hi + lo copies for the GEMMs, two products each); others (f16
+ * weights, MoE) return MF_E_UNSUPPORTED (use mf_model_forward per token). */
 int mf_model_prefill(mf_model* m, const uint32_t* tokens, size_t n, int pos0, int compute_logits, int host_logits);
 
 /* BaseModel::benchmark (src/base/model.cpp:188-236): pp512 (512 random ids

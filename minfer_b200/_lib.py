@@ -148,6 +148,7 @@ CUDA_API = {
     "mf_prefill_gemm": (I, [P, I, P, P, P, I, I, I, I, P, P, P]),
     "mf_prefill_norm_split": (I, [P, P, P, P, P, F, I, I, P]),
     "mf_prefill_split": (I, [P, P, P, SZ, P]),
+    "mf_prefill_swiglu_split": (I, [P, P, P, I, I, P]),
     "mf_prefill_embed": (I, [P, P, I, I, I, P, I, P]),
     "mf_prefill_qkv_post": (I, [P, P, P, P, P, P, F, P, I, I, I, I, I, I, P]),
     "mf_prefill_attention": (I, [P, P, P, P, P, I, I, I, I, I, I, P]),

@@ -225,7 +225,7 @@ int mf_model_prefill(mf_model* m, const uint32_t* tokens, size_t n, int pos0, in
     g_host_err[0] = 0;
     bool ok = false;
     MF_TRY(ok = m->m->prefill(tokens, (int)n, pos0, compute_logits != 0, host_logits != 0));
-    return ok ? MF_OK : herr(MF_E_UNSUPPORTED, "batched prefill needs a bf16 dense model on one GPU");
+    return ok ? MF_OK : herr(MF_E_UNSUPPORTED, "batched prefill needs a dense model with bf16 or fp32 weights");
 }
 
 int mf_model_decode_chained(mf_model* m, uint32_t token, int start_pos, int n, uint32_t* last_id) {

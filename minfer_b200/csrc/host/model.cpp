@@ -42,6 +42,34 @@ void prefill_exchange(RunState& rs, float* X, int n, int d) {
     check(mf_bulk_allreduce(X, (size_t)n * d, rs.comm, (int)(ep & 1), ep, rs.stream), "prefill all-reduce");
 }
 
+// fp32 weights for the batched prefill: the tensor-core GEMM takes bf16
+// weights, so an fp32 matrix is kept as bf16 hi + lo (w = hi + lo to ~2^-17
+// relative) and multiplied as two products summed in fp32.
+struct SplitWeight {
+    mf_buf *hi = nullptr, *lo = nullptr;
+};
+SplitWeight split_weight(mf_buf* w, size_t n, int rank) {
+    SplitWeight s;
+    check(mf_alloc(n * 2, rank, &s.hi), "alloc weight hi");
+    check(mf_alloc(n * 2, rank, &s.lo), "alloc weight lo");
+    check(mf_prefill_split(mf_ptr(s.hi), mf_ptr(s.lo), (const float*)mf_ptr(w), n, mf_stream(rank)), "split weight");
+    check(mf_sync(rank), "sync");
+    return s;
+}
+
+// C = A · W^T for a prefill GEMM in `mode`, W bf16 or (fp32 models) a split
+// pair: the hi product in `mode`, then the lo product added (MF_PREFILL_RESID).
+void prefill_gemm(float* y, int ldy, void* a_hi, void* a_lo, const mf_buf* w, const SplitWeight& sw, int M, int N,
+                  int K, int mode, void* stream, const char* what) {
+    if (!sw.hi) {
+        check(mf_prefill_gemm(y, ldy, a_hi, a_lo, mf_ptr(w), M, N, K, mode, nullptr, nullptr, stream), what);
+        return;
+    }
+    check(mf_prefill_gemm(y, ldy, a_hi, a_lo, mf_ptr(sw.hi), M, N, K, mode, nullptr, nullptr, stream), what);
+    check(mf_prefill_gemm(y, ldy, a_hi, a_lo, mf_ptr(sw.lo), M, N, K, MF_PREFILL_RESID, nullptr, nullptr, stream),
+          what);
+}
+
 mf_buf* upload_tensor(const TensorView& t, int rank) {
     mf_buf* b = nullptr;
     check(mf_upload(t.data, t.bytes, rank, &b), ("upload " + t.name).c_str());
@@ -236,9 +264,8 @@ public:
         float* vc = (float*)mf_ptr(rs.v_cache) + (size_t)layer_ * rs.kv_layer_floats;
         check(mf_prefill_norm_split(hi, lo, nullptr, X, (const float*)mf_ptr(an_), c_.rms_norm_eps, d, n, rs.stream),
               "prefill attn norm");
-        check(mf_prefill_gemm((float*)mf_ptr(rs.pf_qkv), Nqkv, hi, lo, mf_ptr(wqkv_), n, Nqkv, d, MF_PREFILL_STORE,
-                              nullptr, nullptr, rs.stream),
-              "prefill qkv projection");
+        prefill_gemm((float*)mf_ptr(rs.pf_qkv), Nqkv, hi, lo, wqkv_, wqkv_s_, n, Nqkv, d, MF_PREFILL_STORE, rs.stream,
+                     "prefill qkv projection");
         check(mf_prefill_qkv_post((float*)mf_ptr(rs.pf_q), kc, vc, (const float*)mf_ptr(rs.pf_qkv),
                                   (const float*)mf_ptr(qn_), (const float*)mf_ptr(kn_), c_.rms_norm_eps,
                                   mf_ptr(rs.rope), S, H, Hkv, D, n, pos0, rs.stream),
@@ -252,16 +279,22 @@ public:
                                           mf_ptr(rs.pf_att), rs.pf_att_bytes, rs.stream),
                   "prefill attention");
         if (c_.tp_size == 1) {
-            check(mf_prefill_gemm(X, d, hi, lo, mf_ptr(wo_), n, d, H * D, MF_PREFILL_RESID, nullptr, nullptr,
-                                  rs.stream),
-                  "prefill output projection");
+            prefill_gemm(X, d, hi, lo, wo_, wo_s_, n, d, H * D, MF_PREFILL_RESID, rs.stream,
+                         "prefill output projection");
         } else {
             float* part = prefill_exchange_slot(rs);
-            check(mf_prefill_gemm(part, d, hi, lo, mf_ptr(wo_), n, d, H * D, MF_PREFILL_STORE, nullptr, nullptr,
-                                  rs.stream),
-                  "prefill output projection (partial)");
+            prefill_gemm(part, d, hi, lo, wo_, wo_s_, n, d, H * D, MF_PREFILL_STORE, rs.stream,
+                         "prefill output projection (partial)");
             prefill_exchange(rs, X, n, d);
         }
+    }
+    // fp32 weights: bf16 hi/lo copies for the batched prefill (made on first use)
+    void split_for_prefill(int rank) override {
+        if (dtype_ != MF_F32 || wqkv_s_.hi) return;
+        const size_t d = c_.d_model, ql = (size_t)c_.heads_local() * c_.d_head, kvl = (size_t)c_.kv_heads_local() * c_.d_head;
+        wqkv_s_ = split_weight(wqkv_, (ql + 2 * kvl) * d, rank);
+        wo_s_ = split_weight(wo_, d * ql, rank);
+        for (mf_buf* b : {wqkv_s_.hi, wqkv_s_.lo, wo_s_.hi, wo_s_.lo}) own(b);
     }
 
 private:
@@ -269,6 +302,7 @@ private:
     int layer_;
     int dtype_ = MF_BF16;
     mf_buf *wqkv_ = nullptr, *wo_ = nullptr, *qn_ = nullptr, *kn_ = nullptr, *an_ = nullptr;
+    SplitWeight wqkv_s_, wo_s_;  // fp32 models: prefill copies
     bool tc_attn_ok_ = true;  // q/k fit the tensor-core attention's fp16 operands
 };
 
@@ -389,19 +423,32 @@ public:
         void *hi = mf_ptr(rs.pf_hi), *lo = mf_ptr(rs.pf_lo), *hhi = mf_ptr(rs.pf_hhi), *hlo = mf_ptr(rs.pf_hlo);
         check(mf_prefill_norm_split(hi, lo, nullptr, X, (const float*)mf_ptr(fn_), c_.rms_norm_eps, d, n, rs.stream),
               "prefill ffn norm");
-        check(mf_prefill_gemm(nullptr, 0, hi, lo, mf_ptr(wgu_), n, 2 * F, d, MF_PREFILL_SWIGLU, hhi, hlo, rs.stream),
-              "prefill gate/up projection");
-        if (c_.tp_size == 1) {
-            check(mf_prefill_gemm(X, d, hhi, hlo, mf_ptr(wd_), n, d, F, MF_PREFILL_RESID, nullptr, nullptr,
+        if (!wgu_s_.hi) {
+            check(mf_prefill_gemm(nullptr, 0, hi, lo, mf_ptr(wgu_), n, 2 * F, d, MF_PREFILL_SWIGLU, hhi, hlo,
                                   rs.stream),
-                  "prefill down projection");
+                  "prefill gate/up projection");
+        } else {
+            // fp32 weights: both products summed in fp32 before the SwiGLU
+            float* gu = (float*)mf_ptr(rs.pf_gu);
+            prefill_gemm(gu, 2 * F, hi, lo, wgu_, wgu_s_, n, 2 * F, d, MF_PREFILL_STORE, rs.stream,
+                         "prefill gate/up projection");
+            check(mf_prefill_swiglu_split(hhi, hlo, gu, n, F, rs.stream), "prefill swiglu");
+        }
+        if (c_.tp_size == 1) {
+            prefill_gemm(X, d, hhi, hlo, wd_, wd_s_, n, d, F, MF_PREFILL_RESID, rs.stream, "prefill down projection");
         } else {
             float* part = prefill_exchange_slot(rs);
-            check(mf_prefill_gemm(part, d, hhi, hlo, mf_ptr(wd_), n, d, F, MF_PREFILL_STORE, nullptr, nullptr,
-                                  rs.stream),
-                  "prefill down projection (partial)");
+            prefill_gemm(part, d, hhi, hlo, wd_, wd_s_, n, d, F, MF_PREFILL_STORE, rs.stream,
+                         "prefill down projection (partial)");
             prefill_exchange(rs, X, n, d);
         }
+    }
+    void split_for_prefill(int rank) override {
+        if (dtype_ != MF_F32 || c_.n_experts > 0 || wgu_s_.hi) return;
+        const size_t d = c_.d_model, Fl = (size_t)c_.ff_local();
+        wgu_s_ = split_weight(wgu_, 2 * Fl * d, rank);
+        wd_s_ = split_weight(wd_, d * Fl, rank);
+        for (mf_buf* b : {wgu_s_.hi, wgu_s_.lo, wd_s_.hi, wd_s_.lo}) own(b);
     }
 
 private:
@@ -409,6 +456,7 @@ private:
     int layer_;
     int dtype_ = MF_BF16;
     mf_buf *fn_ = nullptr, *wgu_ = nullptr, *wd_ = nullptr, *wr_ = nullptr;
+    SplitWeight wgu_s_, wd_s_;  // fp32 models: prefill copies
 };
 
 // Qwen3FinalRMSNorm (module.cpp:105-138) + Qwen3LMHead (module.cpp:46-103):
@@ -687,7 +735,9 @@ int Qwen3Model::comm_status(int* status) {
 bool Qwen3Model::prefill_supported() const {
     if (device_ != DeviceType::CUDA || cfg_.n_experts != 0) return false;
     if (cfg_.tp_size > 1 && (rs_.pf_bulk_rows <= 0 || !rs_.comm || cfg_.d_model % 4 != 0)) return false;
-    if (cfg_.weight_dtype != DataType::BF16 || cfg_.d_head != 128 || cfg_.d_model % 8 != 0 || cfg_.d_ff % 8 != 0)
+    // bf16 weights directly; fp32 weights through bf16 hi/lo copies (two products per GEMM)
+    if ((cfg_.weight_dtype != DataType::BF16 && cfg_.weight_dtype != DataType::F32) || cfg_.d_head != 128 ||
+        cfg_.d_model % 8 != 0 || cfg_.d_ff % 8 != 0)
         return false;
     const int G = cfg_.n_heads / cfg_.n_kv_heads;
     return G == 1 || G == 2 || G == 4 || G == 8 || G == 16;
@@ -696,8 +746,8 @@ bool Qwen3Model::prefill_supported() const {
 void Qwen3Model::alloc_prefill(int rows) {
     if (rs_.pf_cap >= rows) return;
     RunState& rs = rs_;
-    for (mf_buf** b :
-         {&rs.pf_x, &rs.pf_hi, &rs.pf_lo, &rs.pf_hhi, &rs.pf_hlo, &rs.pf_qkv, &rs.pf_q, &rs.pf_tok, &rs.pf_att}) {
+    for (mf_buf** b : {&rs.pf_x, &rs.pf_hi, &rs.pf_lo, &rs.pf_hhi, &rs.pf_hlo, &rs.pf_qkv, &rs.pf_q, &rs.pf_tok,
+                       &rs.pf_att, &rs.pf_gu}) {
         if (*b) {
             state_bufs_.erase(std::find(state_bufs_.begin(), state_bufs_.end(), *b));
             mf_release(*b);
@@ -721,6 +771,10 @@ void Qwen3Model::alloc_prefill(int rows) {
     rs.pf_qkv = alloc(R * (qd + 2ull * c.n_kv_heads * c.d_head) * 4, "prefill qkv");
     rs.pf_q = alloc(R * qd * 4, "prefill queries");
     rs.pf_tok = alloc(R * 4, "prefill token ids");
+    if (c.weight_dtype == DataType::F32) {
+        rs.pf_gu = alloc(R * 2ull * c.ff_local() * 4, "prefill gate/up rows");
+        for (auto& l : layers_) l->split_for_prefill(rank_);
+    }
     const char* se = std::getenv("MF_PREFILL_SIMT_ATTN");
     rs.pf_simt_attn = se && se[0] == '1';
     if (!rs.pf_simt_attn) {

@@ -130,6 +130,7 @@ struct RunState {
     int pf_cap = 0;  // rows per chunk
     mf_buf *pf_x = nullptr, *pf_hi = nullptr, *pf_lo = nullptr, *pf_hhi = nullptr, *pf_hlo = nullptr;
     mf_buf *pf_qkv = nullptr, *pf_q = nullptr, *pf_tok = nullptr;
+    mf_buf* pf_gu = nullptr;  // fp32-weight models: gate/up rows before the SwiGLU [rows][2 d_ff]
     mf_buf* pf_att = nullptr;  // tensor-core attention operands (bf16 hi/lo Q, K, V^T)
     size_t pf_att_bytes = 0;
     bool pf_simt_attn = false;  // MF_PREFILL_SIMT_ATTN=1: the SIMT attention kernel instead
@@ -145,6 +146,8 @@ public:
     virtual void cuda_forward(RunState& rs) = 0;
     // Batched prefill of rows [0, n) of the prefill buffers at positions pos0.. (tcgen05 GEMMs).
     virtual void prefill_forward(RunState& rs, int n, int pos0);
+    // fp32-weight layers make the bf16 hi/lo weight copies the prefill GEMMs take.
+    virtual void split_for_prefill(int rank) {}
     virtual void upload(const GGUFFile& f, int rank) = 0;
     size_t read_bytes() const { return read_bytes_; }
 

@@ -172,9 +172,38 @@ __global__ void split_kernel(const float* __restrict__ x, size_t n, __nv_bfloat1
         split_bf16(x[i], hi[i], lo[i]);
 }
 
+// h = silu(g) * u of interleaved gate/up rows gu [n_rows][2 d_ff] (columns
+// 2i, 2i+1 = g_i, u_i), written as the down GEMM's bf16 hi/lo operands [n_rows][d_ff]
+__global__ void swiglu_split_kernel(const float* __restrict__ gu, size_t n_rows, int d_ff, __nv_bfloat16* hi,
+                                    __nv_bfloat16* lo) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const size_t n = n_rows * (size_t)d_ff;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float2 g_u = reinterpret_cast<const float2*>(gu)[i];
+        split_bf16(silu(g_u.x) * g_u.y, hi[i], lo[i]);  // src/models/qwen3/module.cpp:466-468
+    }
+}
+
 }  // namespace mf
 
 extern "C" {
+
+int mf_prefill_swiglu_split(void* h_hi, void* h_lo, const float* gate_up, int n_rows, int d_ff, void* stream) {
+    if (!h_hi || !h_lo || !gate_up || n_rows <= 0 || d_ff <= 0) return fail(MF_E_INVALID, "bad arguments");
+    if (((uintptr_t)gate_up & 7) != 0) return fail(MF_E_INVALID, "gate_up must be 8-byte aligned");
+    const float* g = gate_up;
+    size_t rows = (size_t)n_rows;
+    int F = d_ff;
+    __nv_bfloat16* h = (__nv_bfloat16*)h_hi;
+    __nv_bfloat16* l = (__nv_bfloat16*)h_lo;
+    void* args[] = {(void*)&g, (void*)&rows, (void*)&F, (void*)&h, (void*)&l};
+    const size_t n = rows * (size_t)d_ff;
+    const unsigned blocks = (unsigned)std::min<size_t>((n + 255) / 256, 148 * 8);
+    cudaError_t e = launch((const void*)&mf::swiglu_split_kernel, dim3(blocks), dim3(256), 0,
+                           mf::resolve_stream(stream), args);
+    return e == cudaSuccess ? MF_OK : fail(MF_E_CUDA, cudaGetErrorString(e));
+}
 
 int mf_prefill_gemm(float* y, int ldy, const void* a_hi, const void* a_lo, const void* w, int M, int N, int K,
                     int mode, void* h_hi, void* h_lo, void* stream) {

@@ -237,7 +237,7 @@ def test_prefill_qkv_post_matches_decode_rotation(lib, gpu):
 
 # ------------------------------------------------------------------ model level
 
-@pytest.mark.parametrize("name", ["tiny-bf16", "tiny-gqa8", "tiny-tp8"])
+@pytest.mark.parametrize("name", ["tiny-bf16", "tiny-gqa8", "tiny-tp8", "tiny-f32"])
 @pytest.mark.parametrize("chunk,simt", [(None, False), (16, False), (None, True)])
 def test_model_prefill_vs_oracle(gpu, monkeypatch, name, chunk, simt):
     """Batched prefill (tensor cores) of a 40-token prompt: last-token logits,
@@ -305,7 +305,7 @@ def test_model_prefill_long_prompt_vs_oracle(gpu, Pn):
     m.close()
 
 
-@pytest.mark.parametrize("name", ["tiny-bf16", "tiny-tp8"])
+@pytest.mark.parametrize("name", ["tiny-bf16", "tiny-tp8", "tiny-f32"])
 def test_generate_batched_prefill_matches_token_prefill(gpu, name):
     """generate(): batched prefill and the reference's token-by-token prefill
     give the same greedy continuation (margin rule) and close margins."""
@@ -330,6 +330,6 @@ def test_prefill_not_eligible_falls_back(gpu):
     from conftest import tiny_model
     from minfer_b200.model import Qwen3Model, RunParams
 
-    for name in ("tiny-f32", "tiny-moe"):
+    for name in ("tiny-f16", "tiny-moe"):
         m = Qwen3Model(tiny_model(name), RunParams(max_seq_len=32)).set_device("cuda")
         assert m.prefill(np.arange(5, dtype=np.uint32)) is False
