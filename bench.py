@@ -178,7 +178,8 @@ def time_dominant_kernel(cfg, peaks, iters: int = 20) -> dict:
         for line in prof.read_text().splitlines():
             if line.strip().startswith("dram_bytes_per_launch:"):
                 traffic = float(line.split(":")[1])
-    return {"kernel": "gemv_kernel<W_BF16,...,X_NORM,Y_SWIGLU> (gate/up + SiLU, one layer)",
+    return {"kernel": "gemv_tma_kernel<W_BF16, 8, 2, X_NORM, Y_SWIGLU> (RMSNorm + gate/up + SiLU over a "
+                      "TMA bulk-copy ring, one layer)",
             "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic, "algo_bytes": algo,
             "avg_launch_us": round(ms * 1e3, 2)}
