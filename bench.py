@@ -317,11 +317,12 @@ def llama_bench_main(args) -> None:
 
 
 def measure_long_context(workload: str, ctx: int, steps: int, warmup: int, rank: int, world: int, local_rank: int,
-                         peaks: dict) -> dict:
+                         peaks: dict, kv_dtype: str = "f32") -> dict:
     """Decode of a second workload at a long context, the same way as the main
     line (batched prefill of a random prompt, chained greedy decode timed with
     CUDA events, max over ranks): tokens/s and the HBM roofline fraction per
-    GPU, prefill tokens/s, exchange status."""
+    GPU, prefill tokens/s, exchange status. kv_dtype "bf16" runs it with the
+    opt-in bf16 KV cache (the reference's cache is fp32)."""
     import torch
 
     from minfer_b200 import model as mm
@@ -335,7 +336,7 @@ def measure_long_context(workload: str, ctx: int, steps: int, warmup: int, rank:
     n_tok = warmup + steps + 4
     t0 = time.perf_counter()
     m = mm.Qwen3Model(path, mm.RunParams(num_iters=n_tok, max_seq_len=ctx + n_tok + 2), device=local_rank,
-                      tp_rank=rank, tp_size=world)
+                      tp_rank=rank, tp_size=world, kv_dtype=kv_dtype)
     m.set_device("cuda")
     tp.connect(m)
     t_load = time.perf_counter() - t0
@@ -380,7 +381,7 @@ def measure_long_context(workload: str, ctx: int, steps: int, warmup: int, rank:
     m.close()
     step_gbs = tb / (dev_ms / steps / 1e3) / 1e9 / world
     return {"workload": f"{workload} greedy decode at batch 1 after a {ctx}-token prompt", "context": ctx,
-            "tok_per_s": round(steps / (dev_ms / 1e3), 2), "ms_per_step": round(dev_ms / steps, 3), "steps": steps,
+            "kv_dtype": kv_dtype, "tok_per_s": round(steps / (dev_ms / 1e3), 2), "ms_per_step": round(dev_ms / steps, 3), "steps": steps,
             "bytes_per_token": tb, "hbm_roofline": {"achieved_gbs_per_gpu": round(step_gbs, 1),
                                                     "peak_gbs": peaks["hbm_gbs"],
                                                     "frac": round(step_gbs / peaks["hbm_gbs"], 4)},
@@ -454,6 +455,8 @@ def main():
                     help="second record: this model decoded after a long prompt (the scaling target)")
     ap.add_argument("--long-context", type=int, default=32768)
     ap.add_argument("--no-long", action="store_true", help="skip the long-context record")
+    ap.add_argument("--no-long-kv-bf16", action="store_true",
+                    help="skip the long-context run with the opt-in bf16 KV cache")
     ap.add_argument("--llama-bench", action="store_true",
                     help="only the reference's benchmark loop (pp512 + tg128, seed 30) on --workload, this runtime "
                          "and the reference CPU build side by side (one GPU)")
@@ -621,6 +624,9 @@ def main():
             m.close()
             long_rec = measure_long_context(args.long_workload, args.long_context, args.steps, args.warmup, rank,
                                             world, local_rank, peaks)
+            if not args.no_long_kv_bf16:  # the same run with the opt-in bf16 KV cache
+                long_rec["kv_bf16"] = measure_long_context(args.long_workload, args.long_context, args.steps,
+                                                           args.warmup, rank, world, local_rank, peaks, "bf16")
         else:
             long_rec = {"skipped": f"no room for the {args.long_workload} file under {lp.parent}"}
 

@@ -182,8 +182,8 @@ typedef struct mf_attn_desc {
     const float* k_norm_w;
     float eps;
     const void* rope_table; /* mf_rope_table for >= max_seq positions (device) */
-    float* k_cache;
-    float* v_cache;
+    void* k_cache;         /* this layer's [Hkv][max_seq][D] rows of kv_dtype */
+    void* v_cache;
     int max_seq;
     const void* step_state; /* device step record (pos) */
     float* out;            /* [Hq*D] */
@@ -192,6 +192,8 @@ typedef struct mf_attn_desc {
     int d_head;
     int n_split;           /* position slices per KV head (mf_attn_default_split) */
     void* workspace;
+    int kv_dtype;          /* MF_F32 (the reference's cache; 0, the default) or MF_BF16
+                              (opt-in: rows rounded to nearest even at the append) */
 } mf_attn_desc;
 size_t mf_attn_workspace_bytes(int n_heads, int n_kv_heads, int d_head, int n_split);
 int mf_attn_default_split(int n_kv_heads, int max_seq);
@@ -367,14 +369,16 @@ int mf_prefill_embed(float* x, const void* emb, int dtype, int vocab, int d_mode
                      int n_tokens, void* stream);
 /* Per token t (position pos0 + t) of qkv [n_tokens][(Hq + 2 Hkv) * d_head]:
  * Q/K RMSNorm + NeoX RoPE (as mf_attn_decode), q -> q_out [n_tokens][Hq * d_head],
- * k/v -> cache row pos0 + t (caches [n_kv_heads][max_seq][d_head], this layer). */
-int mf_prefill_qkv_post(float* q_out, float* k_cache, float* v_cache, const float* qkv, const float* q_norm_w,
+ * k/v -> cache row pos0 + t (caches [n_kv_heads][max_seq][d_head] of kv_dtype,
+ * MF_F32 or MF_BF16, this layer). */
+int mf_prefill_qkv_post(float* q_out, void* k_cache, void* v_cache, const float* qkv, const float* q_norm_w,
                         const float* k_norm_w, float eps, const void* rope_table, int max_seq, int n_heads,
-                        int n_kv_heads, int d_head, int n_tokens, int pos0, void* stream);
+                        int n_kv_heads, int d_head, int n_tokens, int pos0, int kv_dtype, void* stream);
 /* Causal GQA attention of the prompt tokens (token t sees cache rows
  * [0, pos0 + t]), written as bf16 hi/lo [n_tokens][Hq * d_head]. */
-int mf_prefill_attention(void* out_hi, void* out_lo, const float* q, const float* k_cache, const float* v_cache,
-                         int max_seq, int n_tokens, int pos0, int n_heads, int n_kv_heads, int d_head, void* stream);
+int mf_prefill_attention(void* out_hi, void* out_lo, const float* q, const void* k_cache, const void* v_cache,
+                         int max_seq, int n_tokens, int pos0, int n_heads, int n_kv_heads, int d_head, int kv_dtype,
+                         void* stream);
 /* The same attention on the tensor cores (tcgen05): S = Q K^T with fp16 hi/lo
  * operands and O += P V with bf16 hi/lo operands (three products each) in
  * TMEM, online softmax per query row. Needs device scratch of at least
@@ -382,9 +386,9 @@ int mf_prefill_attention(void* out_hi, void* out_lo, const float* q, const float
  * 256-byte aligned. A wait that gives up sets status bit 2; a q or k value
  * outside the fp16 range (|x| >= 65504, or not finite) sets status bit 4. */
 int mf_prefill_attention_scratch(int n_tokens, int n_keys, int n_heads, int n_kv_heads, size_t* bytes);
-int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const float* k_cache, const float* v_cache,
+int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const void* k_cache, const void* v_cache,
                             int max_seq, int n_tokens, int pos0, int n_heads, int n_kv_heads, int d_head,
-                            void* scratch, size_t scratch_bytes, void* stream);
+                            void* scratch, size_t scratch_bytes, int kv_dtype, void* stream);
 /* ===================================================================== */
 /* Sampling on the device                                                */
 /* ===================================================================== */

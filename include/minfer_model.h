@@ -52,7 +52,8 @@ typedef struct mf_model_info {
     float rms_norm_eps, freq_base;
     size_t read_bytes_logits;    /* weight bytes one forward with logits reads */
     size_t read_bytes_no_logits; /* ... without the lm_head */
-    size_t kv_bytes_per_pos;     /* 2 * n_layers * n_kv_heads * d_head * 4 (this rank's heads) */
+    size_t kv_bytes_per_pos;     /* 2 * n_layers * n_kv_heads * d_head * (4, or 2 for a bf16 cache)
+                                    (this rank's heads) */
     int tp_rank, tp_size;        /* tensor-parallel position of this process */
 } mf_model_info;
 
@@ -67,6 +68,12 @@ typedef struct mf_gen_stats {
 /* Parse the GGUF file and build the layer list; rank selects the manager
  * rank (device) the model lives on. mf_init must have been called. */
 int mf_model_load(const char* gguf_path, const mf_run_params* rp, int rank, mf_model** out);
+/* KV cache element type (no reference counterpart: the reference keeps fp32):
+ * MF_F32 (default) or, opt-in, MF_BF16, which halves the cache's bytes and
+ * rounds every appended K/V row to nearest even (attention still computes in
+ * fp32 on the widened values; logits then differ from the reference's by the
+ * rounding's effect). Call before mf_model_to_cuda. */
+int mf_model_set_kv_dtype(mf_model* m, int dtype);
 /* BaseModel::set_device(DeviceType::CUDA): upload weights, allocate RunState. */
 int mf_model_to_cuda(mf_model* m);
 

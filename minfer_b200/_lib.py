@@ -75,7 +75,7 @@ class mf_attn_desc(C.Structure):
     _fields_ = [("qkv", C.c_void_p), ("q_norm_w", C.c_void_p), ("k_norm_w", C.c_void_p), ("eps", C.c_float),
                 ("rope_table", C.c_void_p), ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("max_seq", C.c_int),
                 ("step_state", C.c_void_p), ("out", C.c_void_p), ("n_heads", C.c_int), ("n_kv_heads", C.c_int),
-                ("d_head", C.c_int), ("n_split", C.c_int), ("workspace", C.c_void_p)]
+                ("d_head", C.c_int), ("n_split", C.c_int), ("workspace", C.c_void_p), ("kv_dtype", C.c_int)]
 
 
 P = C.c_void_p
@@ -150,10 +150,10 @@ CUDA_API = {
     "mf_prefill_split": (I, [P, P, P, SZ, P]),
     "mf_prefill_swiglu_split": (I, [P, P, P, I, I, P]),
     "mf_prefill_embed": (I, [P, P, I, I, I, P, I, P]),
-    "mf_prefill_qkv_post": (I, [P, P, P, P, P, P, F, P, I, I, I, I, I, I, P]),
-    "mf_prefill_attention": (I, [P, P, P, P, P, I, I, I, I, I, I, P]),
+    "mf_prefill_qkv_post": (I, [P, P, P, P, P, P, F, P, I, I, I, I, I, I, I, P]),
+    "mf_prefill_attention": (I, [P, P, P, P, P, I, I, I, I, I, I, I, P]),
     "mf_prefill_attention_scratch": (I, [I, I, I, I, P]),
-    "mf_prefill_attention_tc": (I, [P, P, P, P, P, I, I, I, I, I, I, P, SZ, P]),
+    "mf_prefill_attention_tc": (I, [P, P, P, P, P, I, I, I, I, I, I, P, SZ, I, P]),
     "mf_prefill_status": (I, [P, I]),
     "mf_topk_workspace_bytes": (SZ, [I, I]),
     "mf_topk": (I, [P, I, I, P, P, P, SZ, P]),
@@ -173,6 +173,7 @@ HOST_API = {
     "mf_host_last_error": (I, [C.c_char_p, SZ]),
     "mf_model_load": (I, [C.c_char_p, P, I, P]),
     "mf_model_to_cuda": (I, [P]),
+    "mf_model_set_kv_dtype": (I, [P, I]),
     "mf_model_load_tp": (I, [C.c_char_p, P, I, I, I, P]),
     "mf_model_prefill": (I, [P, P, SZ, I, I, I]),
     "mf_model_comm_handle": (I, [P, P, SZ]),

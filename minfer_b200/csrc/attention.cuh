@@ -1,5 +1,8 @@
 // Decode attention for one token: per-head Q/K RMSNorm + NeoX RoPE + KV-cache
-// append + GQA attention over the HBM-resident fp32 KV cache, as one kernel.
+// append + GQA attention over the HBM-resident KV cache, as one kernel. The
+// cache holds fp32 rows (the reference's format) or, opt-in, bf16 rows
+// (rounded to nearest even at the append; read back widened exactly, all
+// arithmetic in fp32).
 //
 // Reference semantics (src/models/qwen3/module.cpp:187-234, src/ops/kernels.cpp:31-110):
 //  * q_h <- rmsnorm(q_h, q_norm), k_h <- rmsnorm(k_h, k_norm) over d_head;
@@ -18,9 +21,10 @@
 //  * grid = (n_split, n_kv_heads), 8 warps per CTA, two CTAs per SM; each CTA
 //    serves ALL kv_mul query heads of its KV head over one contiguous slice of
 //    positions, so every K/V row is read from HBM exactly once per token.
-//  * The cache layout is [kv_head][position][d_head] (fp32): a slice is one
-//    contiguous run of rows, streamed as 32-row (16 KB) tiles through a
-//    5-stage CTA-wide cp.async ring with one barrier per tile.
+//  * The cache layout is [kv_head][position][d_head]: a slice is one
+//    contiguous run of rows, streamed as 32-row tiles (16 KB fp32, 8 KB
+//    bf16) through an 80 KB CTA-wide cp.async ring (5 or 10 stages) with one
+//    barrier per tile.
 //  * Two phases per 256-position super-chunk: (1) the K tiles -> scaled
 //    scores of every query head into shared memory (8 lanes per position,
 //    16 dims each, finished by a reduce-scatter over the 8 lanes); (2) one
@@ -66,8 +70,8 @@ struct AttnParams {
     const float* k_norm_w;   // [D]
     float eps;
     const float2* rope;      // [max_seq][D/2] (cos, sin) per position and pair
-    float* k_cache;          // this layer: [Hkv][max_seq][D]
-    float* v_cache;
+    void* k_cache;           // this layer: [Hkv][max_seq][D] of KV (float or bf16)
+    void* v_cache;
     int max_seq;
     const int* pos_ptr;      // current position (device)
     float* out;              // [Hq*D]
@@ -89,6 +93,31 @@ MF_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "me
 template <int N> MF_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 MF_DEVICE float f4_get(const float4& v, int i) { return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w)); }
+
+// Four consecutive cache elements widened to fp32 (bf16 -> fp32 is exact: the
+// 16 bits become the high half of the float), and their store.
+MF_DEVICE float4 kv_ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+MF_DEVICE float4 kv_ld4(const __nv_bfloat16* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xffff0000u));
+}
+MF_DEVICE void kv_ld16(const float* p, float4 (&o)[1]) { o[0] = *reinterpret_cast<const float4*>(p); }
+MF_DEVICE void kv_ld16(const __nv_bfloat16* p, float4 (&o)[2]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    o[0] = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xffff0000u));
+    o[1] = make_float4(__uint_as_float(u.z << 16), __uint_as_float(u.z & 0xffff0000u), __uint_as_float(u.w << 16),
+                       __uint_as_float(u.w & 0xffff0000u));
+}
+MF_DEVICE void kv_st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+MF_DEVICE void kv_st4(__nv_bfloat16* p, float4 v) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&a);
+    u.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = u;
+}
 
 // RMSNorm + NeoX RoPE of one 128-dim head held by a warp (lane owns dims 4l..4l+3).
 MF_DEVICE float4 norm_rope_head(float4 v, const float* nw, float eps, const float2* cs, int lane) {
@@ -166,15 +195,19 @@ struct AttnSeq {
 #define MF_ATT_QREG_FLOATS 64
 #endif
 
-template <int G>
+template <int G, typename KV>
 __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)) attn_decode_kernel(const AttnParams p) {
     static_assert(G >= 1 && G <= 16 && (G & (G - 1)) == 0, "power-of-two query groups");
     constexpr int NT = ATT_WARPS * 32;
+    constexpr int RB = ATT_D * (int)sizeof(KV);  // bytes per cache row
+    constexpr int TB = ATT_TILE * RB;            // bytes per tile
+    // the ring keeps the same bytes for either element type (5 fp32 or 10 bf16 tiles)
+    constexpr int STAGES = ATT_STAGES * ATT_TILE_FLOATS * (int)sizeof(float) / TB;
     extern __shared__ float4 att_smem4[];
-    float* ring = reinterpret_cast<float*>(att_smem4);      // [ATT_STAGES][ATT_TILE_FLOATS]
+    float* ring = reinterpret_cast<float*>(att_smem4);      // [STAGES][TB bytes]; later merge staging
     float* sc_s = ring + ATT_STAGES * ATT_TILE_FLOATS;       // [G][ATT_SC_STRIDE] within [G][ATT_HEAD_AREA]
     __shared__ __align__(16) float q_s[G][ATT_D];
-    __shared__ __align__(16) float knew_s[ATT_D], vnew_s[ATT_D];  // row `pos`, never re-read from HBM
+    __shared__ __align__(16) KV knew_s[ATT_D], vnew_s[ATT_D];  // row `pos` as stored, never re-read from HBM
     __shared__ float m_s[G], l_s[G], a_s[G];
     __shared__ int is_last;
 
@@ -182,8 +215,8 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
     const int split = blockIdx.x, kvh = blockIdx.y;
     const int Hq = p.n_heads, Hkv = p.n_kv_heads;
     const size_t head_stride = (size_t)p.max_seq * ATT_D;
-    const float* kc = p.k_cache + (size_t)kvh * head_stride;
-    const float* vc = p.v_cache + (size_t)kvh * head_stride;
+    const KV* kc = reinterpret_cast<const KV*>(p.k_cache) + (size_t)kvh * head_stride;
+    const KV* vc = reinterpret_cast<const KV*>(p.v_cache) + (size_t)kvh * head_stride;
 
     // Before the dependency wait nothing produced by earlier kernels may be
     // used; a possibly stale position only steers an L2 prefetch of cache rows
@@ -192,7 +225,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
         const int ps = min(max(__ldcg(p.pos_ptr), 0), p.max_seq - 1);
         const AttnSlice sl = attn_slice(ps + 1, p.n_split, split);
         if (split < sl.eff && sl.end > sl.start) {
-            const uint32_t nb = (uint32_t)min(sl.end - sl.start, ATT_PF_ROWS) * ATT_D * sizeof(float);
+            const uint32_t nb = (uint32_t)min(sl.end - sl.start, ATT_PF_ROWS) * RB;
             prefetch_l2(kc + (size_t)sl.start * ATT_D, nb);
             prefetch_l2(vc + (size_t)sl.start * ATT_D, nb);
         }
@@ -216,18 +249,20 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
     // its values are taken from shared memory, so it is never copied.
     const int copy_end = (end == len) ? end - 1 : end;
 
-    // Copy pieces: thread (warp, lane) moves the 16 bytes at column 4*lane of
-    // tile rows warp + 8*i, i < 4 (one 512-byte row per warp instruction).
-    constexpr int CP_ROWS = NT / 32;  // rows per copy instruction
-    const int toff = warp * ATT_D + 4 * lane;
+    // Copy pieces: LPRC threads move one row (16 bytes each); thread tid moves
+    // column chunk tid % LPRC of tile rows tid / LPRC + CP_ROWS * i.
+    constexpr int LPRC = RB / 16;
+    constexpr int CP_ROWS = NT / LPRC;  // rows per copy instruction
+    const int crow = tid / LPRC;
+    const int toff = crow * ATT_D + (tid % LPRC) * (16 / (int)sizeof(KV));
     AttnSeq ps;  // producer position
     ps.init(start, end);
     int pslot = 0;
     auto issue = [&](int q) {
         if (q < nseq) {
             const int row0 = ps.row0();
-            float* dst = ring + pslot * ATT_TILE_FLOATS + toff;
-            const float* src = (ps.is_v ? vc : kc) + (size_t)row0 * ATT_D + toff;
+            KV* dst = reinterpret_cast<KV*>(ring) + pslot * (TB / (int)sizeof(KV)) + toff;
+            const KV* src = (ps.is_v ? vc : kc) + (size_t)row0 * ATT_D + toff;
             const int ncopy = copy_end - row0;
             if (ncopy >= ATT_TILE) {
 #pragma unroll
@@ -236,15 +271,15 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
             } else {
 #pragma unroll
                 for (int i = 0; i < ATT_TILE / CP_ROWS; ++i)
-                    if (warp + i * CP_ROWS < ncopy) cp_async16(dst + i * CP_ROWS * ATT_D, src + (size_t)i * CP_ROWS * ATT_D);
+                    if (crow + i * CP_ROWS < ncopy) cp_async16(dst + i * CP_ROWS * ATT_D, src + (size_t)i * CP_ROWS * ATT_D);
             }
             ps.advance(end);
         }
         cp_async_commit();  // one group per sequence slot, empty groups included
-        pslot = (pslot + 1 == ATT_STAGES) ? 0 : pslot + 1;
+        pslot = (pslot + 1 == STAGES) ? 0 : pslot + 1;
     };
 #pragma unroll 1
-    for (int q = 0; q < ATT_STAGES - 1; ++q) issue(q);
+    for (int q = 0; q < STAGES - 1; ++q) issue(q);
 
     // ---- prologue: normalised + rotated queries; the KV append
     for (int g = warp; g < G; g += ATT_WARPS) {
@@ -258,10 +293,11 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
         const float4 k = norm_rope_head(__ldcg(reinterpret_cast<const float4*>(kraw) + lane), p.k_norm_w, p.eps,
                                         cs, lane);
         const float4 v = __ldcg(reinterpret_cast<const float4*>(vraw) + lane);
-        reinterpret_cast<float4*>(p.k_cache + (size_t)kvh * head_stride + (size_t)pos * ATT_D)[lane] = k;
-        reinterpret_cast<float4*>(p.v_cache + (size_t)kvh * head_stride + (size_t)pos * ATT_D)[lane] = v;
-        reinterpret_cast<float4*>(knew_s)[lane] = k;
-        reinterpret_cast<float4*>(vnew_s)[lane] = v;
+        const size_t row = (size_t)kvh * head_stride + (size_t)pos * ATT_D + 4 * lane;
+        kv_st4(reinterpret_cast<KV*>(p.k_cache) + row, k);
+        kv_st4(reinterpret_cast<KV*>(p.v_cache) + row, v);
+        kv_st4(knew_s + 4 * lane, k);
+        kv_st4(vnew_s + 4 * lane, v);
     }
     if (tid < G) {
         m_s[tid] = -INFINITY;
@@ -272,19 +308,25 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
     const float scale = 1.0f / sqrtf((float)ATT_D);  // src/ops/kernels.cpp:88
     // score mapping: LPR lanes per tile row, each summing DPL dims
     // {4*(c + LPR*j) + e}; a quarter-warp reads 128 contiguous bytes of one row
+    // (each lane loads 16 bytes of a row at a time: EPL elements = NQ4 float4s)
     constexpr int LPR = G >= 8 ? 16 : 8;
-    constexpr int NJ = ATT_D / 4 / LPR;  // float4 chunks per lane
-    constexpr int RPP = NT / LPR;        // rows per pass
-    constexpr int NP = ATT_TILE / RPP;   // passes per tile
+    constexpr int EPL = 16 / (int)sizeof(KV);
+    constexpr int NQ4 = EPL / 4;
+    constexpr int NJ = ATT_D / EPL / LPR;  // 16-byte loads per lane and row
+    constexpr int RPP = NT / LPR;          // rows per pass
+    constexpr int NP = ATT_TILE / RPP;     // passes per tile
     const int r_k = tid / LPR, c = tid % LPR;
-    constexpr bool QREG = G * NJ * 4 <= MF_ATT_QREG_FLOATS;
+    constexpr bool QREG = G * NJ * EPL <= MF_ATT_QREG_FLOATS;
     constexpr int QG = QREG ? G : 1;
-    float4 qreg[QG][NJ];
+    float4 qreg[QG][NJ * NQ4];
     if constexpr (QREG) {
 #pragma unroll
         for (int g = 0; g < G; ++g)
 #pragma unroll
-            for (int j = 0; j < NJ; ++j) qreg[g][j] = *reinterpret_cast<const float4*>(&q_s[g][4 * (c + LPR * j)]);
+            for (int j = 0; j < NJ; ++j)
+#pragma unroll
+                for (int u = 0; u < NQ4; ++u)
+                    qreg[g][j * NQ4 + u] = *reinterpret_cast<const float4*>(&q_s[g][EPL * (c + LPR * j) + 4 * u]);
     }
     // after the reduce-scatter a lane holds the sums of heads h_lane .. h_lane + HPL - 1
     constexpr int HPL = G >= LPR ? G / LPR : 1;
@@ -309,10 +351,10 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
     int cslot = 0;
 #pragma unroll 1
     for (int q = 0; q < nseq; ++q) {
-        cp_async_wait<ATT_STAGES - 2>();
+        cp_async_wait<STAGES - 2>();
         __syncthreads();  // tile q landed for every thread; slot (q - 1) is free
-        issue(q + ATT_STAGES - 1);
-        const float* tile = ring + cslot * ATT_TILE_FLOATS;
+        issue(q + STAGES - 1);
+        const KV* tile = reinterpret_cast<const KV*>(ring) + cslot * (TB / (int)sizeof(KV));
         const int row0 = cq.row0();
         const int nvalid = min(ATT_TILE, end - row0);  // rows of the slice in this tile
         const bool has_pos = pos < row0 + ATT_TILE && pos >= row0;
@@ -325,21 +367,24 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
 #pragma unroll
                 for (int g = 0; g < G; ++g) sv[g] = 0.f;
                 if (r < nvalid) {
-                    const float* krow = tile + r * ATT_D + 4 * c;
-                    if (has_pos && row0 + r == pos) krow = knew_s + 4 * c;
+                    const KV* krow = tile + r * ATT_D + EPL * c;
+                    if (has_pos && row0 + r == pos) krow = knew_s + EPL * c;
 #pragma unroll
                     for (int j = 0; j < NJ; ++j) {
-                        const float4 k4 = *reinterpret_cast<const float4*>(krow + 4 * LPR * j);
+                        float4 k4[NQ4];
+                        kv_ld16(krow + EPL * LPR * j, k4);
 #pragma unroll
-                        for (int g = 0; g < G; ++g) {
-                            float4 q4;
-                            if constexpr (QREG) q4 = qreg[g][j];
-                            else q4 = *reinterpret_cast<const float4*>(&q_s[g][4 * (c + LPR * j)]);
-                            sv[g] = fmaf(q4.x, k4.x, sv[g]);
-                            sv[g] = fmaf(q4.y, k4.y, sv[g]);
-                            sv[g] = fmaf(q4.z, k4.z, sv[g]);
-                            sv[g] = fmaf(q4.w, k4.w, sv[g]);
-                        }
+                        for (int u = 0; u < NQ4; ++u)
+#pragma unroll
+                            for (int g = 0; g < G; ++g) {
+                                float4 q4;
+                                if constexpr (QREG) q4 = qreg[g][j * NQ4 + u];
+                                else q4 = *reinterpret_cast<const float4*>(&q_s[g][EPL * (c + LPR * j) + 4 * u]);
+                                sv[g] = fmaf(q4.x, k4[u].x, sv[g]);
+                                sv[g] = fmaf(q4.y, k4[u].y, sv[g]);
+                                sv[g] = fmaf(q4.z, k4[u].z, sv[g]);
+                                sv[g] = fmaf(q4.w, k4[u].w, sv[g]);
+                            }
                     }
                 }
                 // reduce-scatter over the LPR lanes of the row (xor LPR/2 .. 1)
@@ -406,7 +451,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
             if (nvalid == ATT_TILE && !has_pos) {
                 float4 v4[4];
 #pragma unroll
-                for (int rr = 0; rr < 4; ++rr) v4[rr] = *reinterpret_cast<const float4*>(tile + (rb + rr) * ATT_D + 4 * lane);
+                for (int rr = 0; rr < 4; ++rr) v4[rr] = kv_ld4(tile + (rb + rr) * ATT_D + 4 * lane);
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
                     const float4 pv = *reinterpret_cast<const float4*>(prow + g * ATT_SC_STRIDE);
@@ -425,9 +470,8 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
                 float4 v4[4];
 #pragma unroll
                 for (int rr = 0; rr < 4; ++rr) {
-                    const float* vrow = (row0 + rb + rr == pos) ? vnew_s : tile + (rb + rr) * ATT_D;
-                    v4[rr] = (rb + rr < nvalid) ? *reinterpret_cast<const float4*>(vrow + 4 * lane)
-                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+                    const KV* vrow = (row0 + rb + rr == pos) ? vnew_s : tile + (rb + rr) * ATT_D;
+                    v4[rr] = (rb + rr < nvalid) ? kv_ld4(vrow + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
@@ -445,7 +489,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, (G <= 8 ? ATT_CTAS_PER_SM : 1)
             }
         }
         cq.advance(end);
-        cslot = (cslot + 1 == ATT_STAGES) ? 0 : cslot + 1;
+        cslot = (cslot + 1 == STAGES) ? 0 : cslot + 1;
     }
     cp_async_wait<0>();
 

@@ -36,7 +36,7 @@
 #include "minfer_cuda.h"
 
 namespace mf {
-const void* attn_kernel_ptr(int group);
+const void* attn_kernel_ptr(int group, int kv_dtype);
 int record_error(int code, const char* msg);  // capi.cu: message for mf_last_error
 cudaStream_t resolve_stream(void* stream);    // capi.cu: NULL -> manager stream of the current device
 }
@@ -97,7 +97,8 @@ extern "C" int mf_attn_decode_noalloc(const mf_attn_desc* d, void* stream) {
         return noalloc_fail(MF_E_INVALID, "n_heads must be a multiple of n_kv_heads");
     if (d->n_split < 1 || d->max_seq < 1) return noalloc_fail(MF_E_INVALID, "bad n_split/max_seq");
     const int G = d->n_heads / d->n_kv_heads;
-    const void* fn = mf::attn_kernel_ptr(G);
+    if (d->kv_dtype != MF_F32 && d->kv_dtype != MF_BF16) return noalloc_fail(MF_E_UNSUPPORTED, "KV cache dtype");
+    const void* fn = mf::attn_kernel_ptr(G, d->kv_dtype);
     if (!fn) return noalloc_fail(MF_E_UNSUPPORTED, "query heads per KV head without a kernel");
     // scratch layout: counters | (m, l) per split and head | partial outputs | merged groups
     const mf::AttnWsLayout L = mf::attn_ws_layout(d->n_kv_heads, d->n_split, G);

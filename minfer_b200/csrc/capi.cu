@@ -45,7 +45,7 @@ struct mf_comm {
 };
 
 namespace mf {
-const void* attn_kernel_ptr(int group);
+const void* attn_kernel_ptr(int group, int kv_dtype);
 }
 
 namespace {
@@ -949,7 +949,9 @@ int mf_attn_decode(const mf_attn_desc* d, void* stream) {
     MF_REQUIRE(d->n_kv_heads > 0 && d->n_heads % d->n_kv_heads == 0, MF_E_INVALID, "n_heads %% n_kv_heads != 0");
     MF_REQUIRE(d->n_split >= 1 && d->max_seq >= 1, MF_E_INVALID, "bad n_split/max_seq");
     const int G = d->n_heads / d->n_kv_heads;
-    const void* fn = mf::attn_kernel_ptr(G);
+    MF_REQUIRE(d->kv_dtype == MF_F32 || d->kv_dtype == MF_BF16, MF_E_UNSUPPORTED, "KV cache dtype %d (f32 or bf16)",
+               d->kv_dtype);
+    const void* fn = mf::attn_kernel_ptr(G, d->kv_dtype);
     MF_REQUIRE(fn, MF_E_UNSUPPORTED, "%d query heads per KV head has no kernel", G);
     MF_REQUIRE(d->n_split <= mf::attn_max_split(G), MF_E_UNSUPPORTED, "n_split %d above %d", d->n_split,
                mf::attn_max_split(G));

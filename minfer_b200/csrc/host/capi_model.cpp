@@ -78,6 +78,13 @@ int mf_model_load_tp(const char* gguf_path, const mf_run_params* rp, int rank, i
     return MF_OK;
 }
 
+int mf_model_set_kv_dtype(mf_model* m, int dtype) {
+    if (!m) return herr(MF_E_INVALID, "null model");
+    g_host_err[0] = 0;
+    MF_TRY(m->m->set_kv_dtype(dtype));
+    return MF_OK;
+}
+
 int mf_model_to_cuda(mf_model* m) {
     if (!m) return herr(MF_E_INVALID, "null model");
     g_host_err[0] = 0;
@@ -128,7 +135,7 @@ int mf_model_info_get(const mf_model* m, mf_model_info* out) {
         out->read_bytes_logits = m->m->read_bytes(true);
         out->read_bytes_no_logits = m->m->read_bytes(false);
     }
-    out->kv_bytes_per_pos = 2ull * c.n_layers * c.kv_heads_local() * c.d_head * sizeof(float);
+    out->kv_bytes_per_pos = 2ull * c.n_layers * c.kv_heads_local() * c.d_head * (m->m->kv_dtype() == MF_BF16 ? 2 : 4);
     out->tp_rank = c.tp_rank;
     out->tp_size = c.tp_size;
     return MF_OK;

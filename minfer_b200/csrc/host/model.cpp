@@ -231,8 +231,9 @@ public:
         a.k_norm_w = (const float*)mf_ptr(kn_);
         a.eps = c_.rms_norm_eps;
         a.rope_table = mf_ptr(rs.rope);
-        a.k_cache = (float*)mf_ptr(rs.k_cache) + (size_t)layer_ * rs.kv_layer_floats;
-        a.v_cache = (float*)mf_ptr(rs.v_cache) + (size_t)layer_ * rs.kv_layer_floats;
+        a.k_cache = rs.kv_layer(rs.k_cache, layer_);
+        a.v_cache = rs.kv_layer(rs.v_cache, layer_);
+        a.kv_dtype = rs.kv_dtype;
         a.max_seq = (int)c_.user_max_seq_len;
         a.step_state = rs.d_step;
         a.out = (float*)mf_ptr(rs.att);
@@ -260,23 +261,23 @@ public:
         const int S = (int)c_.user_max_seq_len;
         float* X = (float*)mf_ptr(rs.pf_x);
         void *hi = mf_ptr(rs.pf_hi), *lo = mf_ptr(rs.pf_lo);
-        float* kc = (float*)mf_ptr(rs.k_cache) + (size_t)layer_ * rs.kv_layer_floats;
-        float* vc = (float*)mf_ptr(rs.v_cache) + (size_t)layer_ * rs.kv_layer_floats;
+        void* kc = rs.kv_layer(rs.k_cache, layer_);
+        void* vc = rs.kv_layer(rs.v_cache, layer_);
         check(mf_prefill_norm_split(hi, lo, nullptr, X, (const float*)mf_ptr(an_), c_.rms_norm_eps, d, n, rs.stream),
               "prefill attn norm");
         prefill_gemm((float*)mf_ptr(rs.pf_qkv), Nqkv, hi, lo, wqkv_, wqkv_s_, n, Nqkv, d, MF_PREFILL_STORE, rs.stream,
                      "prefill qkv projection");
         check(mf_prefill_qkv_post((float*)mf_ptr(rs.pf_q), kc, vc, (const float*)mf_ptr(rs.pf_qkv),
                                   (const float*)mf_ptr(qn_), (const float*)mf_ptr(kn_), c_.rms_norm_eps,
-                                  mf_ptr(rs.rope), S, H, Hkv, D, n, pos0, rs.stream),
+                                  mf_ptr(rs.rope), S, H, Hkv, D, n, pos0, rs.kv_dtype, rs.stream),
               "prefill q/k norm, rope, kv");
         if (rs.pf_simt_attn || !tc_attn_ok_)
             check(mf_prefill_attention(hi, lo, (const float*)mf_ptr(rs.pf_q), kc, vc, S, n, pos0, H, Hkv, D,
-                                       rs.stream),
+                                       rs.kv_dtype, rs.stream),
                   "prefill attention");
         else
             check(mf_prefill_attention_tc(hi, lo, (const float*)mf_ptr(rs.pf_q), kc, vc, S, n, pos0, H, Hkv, D,
-                                          mf_ptr(rs.pf_att), rs.pf_att_bytes, rs.stream),
+                                          mf_ptr(rs.pf_att), rs.pf_att_bytes, rs.kv_dtype, rs.stream),
                   "prefill attention");
         if (c_.tp_size == 1) {
             prefill_gemm(X, d, hi, lo, wo_, wo_s_, n, d, H * D, MF_PREFILL_RESID, rs.stream,
@@ -655,6 +656,12 @@ void Qwen3Model::set_device(DeviceType d) {
     device_ = d;
 }
 
+void Qwen3Model::set_kv_dtype(int dtype) {
+    if (dtype != MF_F32 && dtype != MF_BF16) throw std::invalid_argument("KV cache dtype must be f32 or bf16");
+    if (device_ == DeviceType::CUDA) throw std::logic_error("set the KV cache dtype before moving the model to CUDA");
+    kv_dtype_ = dtype;
+}
+
 void Qwen3Model::alloc_state() {
     const Config& c = cfg_;
     RunState& rs = rs_;
@@ -681,9 +688,11 @@ void Qwen3Model::alloc_state() {
     rs.scores = alloc((size_t)std::max(c.n_experts, 1) * 4, "moe_scores");
     rs.expert_ids = alloc((size_t)c.n_layers * k * 4, "active_experts");
     rs.expert_w = alloc((size_t)c.n_layers * k * 4, "active_experts_weights");
-    rs.kv_layer_floats = (size_t)Hkvl * S * c.d_head;
-    rs.k_cache = alloc(rs.kv_layer_floats * c.n_layers * 4, "k_cache");
-    rs.v_cache = alloc(rs.kv_layer_floats * c.n_layers * 4, "v_cache");
+    rs.kv_dtype = kv_dtype_;
+    rs.kv_elem = kv_dtype_ == MF_BF16 ? 2 : 4;
+    rs.kv_layer_elems = (size_t)Hkvl * S * c.d_head;
+    rs.k_cache = alloc(rs.kv_layer_elems * c.n_layers * rs.kv_elem, "k_cache");
+    rs.v_cache = alloc(rs.kv_layer_elems * c.n_layers * rs.kv_elem, "v_cache");
     {
         std::vector<float> tab(S * (size_t)c.d_rotary);
         check(mf_rope_table(tab.data(), (int)S, c.d_rotary, c.freq_base), "rope table");
@@ -702,7 +711,7 @@ void Qwen3Model::alloc_state() {
     rs.topk_ws_bytes = mf_topk_workspace_bytes((int)c.vocab_size, kTopkMax);
     rs.topk_ws = alloc(rs.topk_ws_bytes, "top-k workspace");
     check(mf_host_alloc(2 * kTopkMax * 4, &rs.h_topk), "pinned top-k");
-    rs.kv_bytes_per_pos = 2ull * c.n_layers * Hkvl * c.d_head * sizeof(float);
+    rs.kv_bytes_per_pos = 2ull * c.n_layers * Hkvl * c.d_head * rs.kv_elem;
     if (c.tp_size > 1) {
         // dense models also get two bulk slots of [prompt chunk rows, d] for the batched prefill
         rs.pf_bulk_rows = c.ep() ? 0 : (int)std::min<size_t>(c.user_max_seq_len, (size_t)kPrefillChunk);
@@ -1120,18 +1129,29 @@ int Qwen3Model::read_kv(int layer, float* k, float* v, int n_pos) const {
     // returns rows [0, n_pos) in the reference's [pos][kv_head][d_head] order
     // (this rank's KV heads under tensor parallelism)
     if (layer < 0 || layer >= cfg_.n_layers || n_pos < 0 || (size_t)n_pos > cfg_.user_max_seq_len) return MF_E_INVALID;
-    const size_t D = cfg_.d_head, S = cfg_.user_max_seq_len;
-    std::vector<float> tmp(rs_.kv_layer_floats);
+    // (a bf16 cache is widened to fp32, exactly)
+    const size_t D = cfg_.d_head, S = cfg_.user_max_seq_len, es = rs_.kv_elem;
+    std::vector<uint8_t> tmp(rs_.kv_layer_elems * es);
     for (int which = 0; which < 2; ++which) {
         float* dst = which == 0 ? k : v;
         if (!dst) continue;
-        int rc = mf_read(which == 0 ? rs_.k_cache : rs_.v_cache, (size_t)layer * rs_.kv_layer_floats * 4, tmp.data(),
-                         tmp.size() * 4);
+        int rc = mf_read(which == 0 ? rs_.k_cache : rs_.v_cache, (size_t)layer * tmp.size(), tmp.data(), tmp.size());
         if (rc) return rc;
         for (int p = 0; p < n_pos; ++p)
-            for (int hh = 0; hh < cfg_.kv_heads_local(); ++hh)
-                std::memcpy(dst + ((size_t)p * cfg_.kv_heads_local() + hh) * D, tmp.data() + ((size_t)hh * S + p) * D,
-                            D * 4);
+            for (int hh = 0; hh < cfg_.kv_heads_local(); ++hh) {
+                float* out = dst + ((size_t)p * cfg_.kv_heads_local() + hh) * D;
+                const uint8_t* src = tmp.data() + ((size_t)hh * S + p) * D * es;
+                if (es == 4) {
+                    std::memcpy(out, src, D * 4);
+                } else {
+                    for (size_t i = 0; i < D; ++i) {
+                        uint16_t b;
+                        std::memcpy(&b, src + 2 * i, 2);
+                        const uint32_t u = (uint32_t)b << 16;
+                        std::memcpy(out + i, &u, 4);
+                    }
+                }
+            }
     }
     return MF_OK;
 }

@@ -96,7 +96,8 @@ struct GenStats {
 };
 
 // Device-resident run state (include/minfer/base/config.hpp:77-102). The KV
-// cache layout is [layer][kv_head][position][d_head] fp32.
+// cache layout is [layer][kv_head][position][d_head], fp32 as the reference
+// keeps it, or bf16 when the model was set to a bf16 cache.
 struct RunState {
     int rank = 0;
     void* stream = nullptr;
@@ -119,7 +120,12 @@ struct RunState {
     bool compute_logits = false;
     bool host_logits = false;
     size_t kv_bytes_per_pos = 0;
-    size_t kv_layer_floats = 0;  // this rank's n_kv_heads * max_seq * d_head
+    size_t kv_layer_elems = 0;  // this rank's n_kv_heads * max_seq * d_head
+    int kv_dtype = MF_F32;      // MF_F32 or MF_BF16
+    size_t kv_elem = 4;         // bytes per cache element
+    void* kv_layer(const mf_buf* cache, int layer) const {
+        return (char*)mf_ptr(cache) + (size_t)layer * kv_layer_elems * kv_elem;
+    }
     // tensor parallelism: exchange state and the two residual buffers the
     // all-reduces alternate between (x aliases xb[0])
     mf_comm* comm = nullptr;
@@ -163,6 +169,10 @@ public:
     ~Qwen3Model();
 
     void set_device(DeviceType d);  // CUDA: upload weights, allocate the run state
+    // KV cache element type (MF_F32, the reference's, or MF_BF16); set before
+    // set_device(CUDA). A bf16 cache rounds every appended row to nearest even.
+    void set_kv_dtype(int dtype);
+    int kv_dtype() const { return kv_dtype_; }
     DeviceType device() const { return device_; }
     const Config& config() const { return cfg_; }
 
@@ -237,6 +247,7 @@ private:
     int32_t frame_seq_ = 0;
     int32_t next_frame() { return ++frame_seq_; }
     DeviceType device_ = DeviceType::CPU;
+    int kv_dtype_ = MF_F32;
     std::vector<std::unique_ptr<BaseLayer>> layers_;
     RunState rs_;
     std::unique_ptr<Sampler> sampler_;

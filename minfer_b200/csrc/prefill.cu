@@ -282,36 +282,47 @@ int mf_prefill_embed(float* x, const void* emb, int dtype, int vocab, int d_mode
     return e == cudaSuccess ? MF_OK : fail(MF_E_CUDA, cudaGetErrorString(e));
 }
 
-int mf_prefill_qkv_post(float* q_out, float* k_cache, float* v_cache, const float* qkv, const float* q_norm_w,
+int mf_prefill_qkv_post(float* q_out, void* k_cache, void* v_cache, const float* qkv, const float* q_norm_w,
                         const float* k_norm_w, float eps, const void* rope_table, int max_seq, int n_heads,
-                        int n_kv_heads, int d_head, int n_tokens, int pos0, void* stream) {
+                        int n_kv_heads, int d_head, int n_tokens, int pos0, int kv_dtype, void* stream) {
     if (!q_out || !k_cache || !v_cache || !qkv || !q_norm_w || !k_norm_w || !rope_table || n_tokens <= 0 || pos0 < 0)
         return fail(MF_E_INVALID, "bad arguments");
     if (d_head != mf::ATT_D) return fail(MF_E_UNSUPPORTED, "d_head must be 128");
+    if (kv_dtype != MF_F32 && kv_dtype != MF_BF16) return fail(MF_E_UNSUPPORTED, "KV cache dtype (f32 or bf16)");
     if (pos0 + n_tokens > max_seq) return fail(MF_E_INVALID, "prompt runs past max_seq");
     const float2* rope = (const float2*)rope_table;
     void* args[] = {(void*)&qkv, (void*)&q_norm_w, (void*)&k_norm_w, (void*)&eps, (void*)&rope, (void*)&q_out,
                     (void*)&k_cache, (void*)&v_cache, (void*)&max_seq, (void*)&n_heads, (void*)&n_kv_heads,
                     (void*)&pos0};
-    cudaError_t e = launch((const void*)&mf::prefill_qkv_post_kernel, dim3(n_tokens, n_heads + n_kv_heads), dim3(32),
-                           0, mf::resolve_stream(stream), args);
+    const void* fn = kv_dtype == MF_F32 ? (const void*)&mf::prefill_qkv_post_kernel<float>
+                                        : (const void*)&mf::prefill_qkv_post_kernel<__nv_bfloat16>;
+    cudaError_t e = launch(fn, dim3(n_tokens, n_heads + n_kv_heads), dim3(32), 0, mf::resolve_stream(stream), args);
     return e == cudaSuccess ? MF_OK : fail(MF_E_CUDA, cudaGetErrorString(e));
 }
 
-int mf_prefill_attention(void* out_hi, void* out_lo, const float* q, const float* k_cache, const float* v_cache,
-                         int max_seq, int n_tokens, int pos0, int n_heads, int n_kv_heads, int d_head, void* stream) {
+extern "C++" {
+template <typename KV>
+static const void* prefill_attn_ptr(int G) {
+    return G == 1    ? (const void*)&mf::prefill_attn_kernel<1, KV>
+           : G == 2  ? (const void*)&mf::prefill_attn_kernel<2, KV>
+           : G == 4  ? (const void*)&mf::prefill_attn_kernel<4, KV>
+           : G == 8  ? (const void*)&mf::prefill_attn_kernel<8, KV>
+           : G == 16 ? (const void*)&mf::prefill_attn_kernel<16, KV>
+                     : nullptr;
+}
+}
+
+int mf_prefill_attention(void* out_hi, void* out_lo, const float* q, const void* k_cache, const void* v_cache,
+                         int max_seq, int n_tokens, int pos0, int n_heads, int n_kv_heads, int d_head, int kv_dtype,
+                         void* stream) {
     if (!out_hi || !out_lo || !q || !k_cache || !v_cache || n_tokens <= 0 || pos0 < 0 || n_kv_heads <= 0 ||
         n_heads % n_kv_heads != 0)
         return fail(MF_E_INVALID, "bad arguments");
     if (d_head != mf::ATT_D) return fail(MF_E_UNSUPPORTED, "d_head must be 128");
+    if (kv_dtype != MF_F32 && kv_dtype != MF_BF16) return fail(MF_E_UNSUPPORTED, "KV cache dtype (f32 or bf16)");
     if (pos0 + n_tokens > max_seq) return fail(MF_E_INVALID, "prompt runs past max_seq");
     const int G = n_heads / n_kv_heads;
-    const void* fn = G == 1    ? (const void*)&mf::prefill_attn_kernel<1>
-                     : G == 2  ? (const void*)&mf::prefill_attn_kernel<2>
-                     : G == 4  ? (const void*)&mf::prefill_attn_kernel<4>
-                     : G == 8  ? (const void*)&mf::prefill_attn_kernel<8>
-                     : G == 16 ? (const void*)&mf::prefill_attn_kernel<16>
-                               : nullptr;
+    const void* fn = kv_dtype == MF_F32 ? prefill_attn_ptr<float>(G) : prefill_attn_ptr<__nv_bfloat16>(G);
     if (!fn) return fail(MF_E_UNSUPPORTED, "query heads per KV head must be 1, 2, 4, 8 or 16");
     const size_t smem = mf::pa_smem_bytes();
     int rc = set_smem(fn, smem);
@@ -348,13 +359,14 @@ int mf_prefill_attention_scratch(int n_tokens, int n_keys, int n_heads, int n_kv
     return MF_OK;
 }
 
-int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const float* k_cache, const float* v_cache,
+int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const void* k_cache, const void* v_cache,
                             int max_seq, int n_tokens, int pos0, int n_heads, int n_kv_heads, int d_head,
-                            void* scratch, size_t scratch_bytes, void* stream) {
+                            void* scratch, size_t scratch_bytes, int kv_dtype, void* stream) {
     if (!out_hi || !out_lo || !q || !k_cache || !v_cache || !scratch || n_tokens <= 0 || pos0 < 0 ||
         n_kv_heads <= 0 || n_heads % n_kv_heads != 0)
         return fail(MF_E_INVALID, "bad arguments");
     if (d_head != mf::ATT_D) return fail(MF_E_UNSUPPORTED, "d_head must be 128");
+    if (kv_dtype != MF_F32 && kv_dtype != MF_BF16) return fail(MF_E_UNSUPPORTED, "KV cache dtype (f32 or bf16)");
     if (pos0 + n_tokens > max_seq) return fail(MF_E_INVALID, "prompt runs past max_seq");
     if (((uintptr_t)scratch & 255) != 0) return fail(MF_E_INVALID, "scratch must be 256-byte aligned");
     if (((uintptr_t)q & 15) != 0) return fail(MF_E_INVALID, "q must be 16-byte aligned");
@@ -401,13 +413,16 @@ int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const fl
         const int blocks = (int)std::min<long long>((rows + 7) / 8, 148LL * 16);
         void* args[] = {(void*)&k_cache, (void*)&n_kv_heads, (void*)&max_seq, (void*)&n_keys, (void*)&ldi,
                         (void*)&kh, (void*)&kl, (void*)&status};
-        cudaError_t e = launch((const void*)&mf::fa_k_split_kernel, dim3(blocks), dim3(256), 0, st, args);
+        const void* kfn = kv_dtype == MF_F32 ? (const void*)&mf::fa_k_split_kernel<float>
+                                             : (const void*)&mf::fa_k_split_kernel<__nv_bfloat16>;
+        cudaError_t e = launch(kfn, dim3(blocks), dim3(256), 0, st, args);
         if (e != cudaSuccess) return fail(MF_E_CUDA, cudaGetErrorString(e));
     }
     {
         void* args[] = {(void*)&v_cache, (void*)&max_seq, (void*)&n_keys, (void*)&ldi, (void*)&vh, (void*)&vl};
-        cudaError_t e = launch((const void*)&mf::fa_v_split_kernel, dim3((n_keys + 63) / 64, n_kv_heads), dim3(256),
-                               0, st, args);
+        const void* vfn = kv_dtype == MF_F32 ? (const void*)&mf::fa_v_split_kernel<float>
+                                             : (const void*)&mf::fa_v_split_kernel<__nv_bfloat16>;
+        cudaError_t e = launch(vfn, dim3((n_keys + 63) / 64, n_kv_heads), dim3(256), 0, st, args);
         if (e != cudaSuccess) return fail(MF_E_CUDA, cudaGetErrorString(e));
     }
     mf::FaParams p;

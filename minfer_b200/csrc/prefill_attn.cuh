@@ -29,10 +29,12 @@
 namespace mf {
 
 // qkv: [P][(Hq + 2 Hkv) * D] (projection output); Q out: [P][Hq * D];
-// caches: this layer's [Hkv][max_seq][D]. Positions are pos0 + token.
+// caches: this layer's [Hkv][max_seq][D] of KV (float, or bf16 rounded to
+// nearest even). Positions are pos0 + token.
+template <typename KV>
 __global__ void __launch_bounds__(32) prefill_qkv_post_kernel(const float* __restrict__ qkv, const float* q_norm_w,
                                                               const float* k_norm_w, float eps, const float2* rope,
-                                                              float* q_out, float* k_cache, float* v_cache,
+                                                              float* q_out, KV* k_cache, KV* v_cache,
                                                               int max_seq, int n_heads, int n_kv_heads, int pos0) {
     pdl_launch_dependents();
     pdl_wait();
@@ -50,9 +52,9 @@ __global__ void __launch_bounds__(32) prefill_qkv_post_kernel(const float* __res
         const int kh = h - Hq;
         const float4 k = reinterpret_cast<const float4*>(qkv + row + (size_t)(Hq + kh) * ATT_D)[lane];
         const float4 v = reinterpret_cast<const float4*>(qkv + row + (size_t)(Hq + Hkv + kh) * ATT_D)[lane];
-        const size_t c = ((size_t)kh * max_seq + pos) * ATT_D;
-        reinterpret_cast<float4*>(k_cache + c)[lane] = norm_rope_head(k, k_norm_w, eps, cs, lane);
-        reinterpret_cast<float4*>(v_cache + c)[lane] = v;
+        const size_t c = ((size_t)kh * max_seq + pos) * ATT_D + 4 * lane;
+        kv_st4(k_cache + c, norm_rope_head(k, k_norm_w, eps, cs, lane));
+        kv_st4(v_cache + c, v);
     }
 }
 
@@ -68,10 +70,11 @@ inline size_t pa_smem_bytes() {
 
 // Q: [P][Hq * D] (normed, rotated); caches [Hkv][max_seq][D] holding rows
 // pos0 .. pos0 + P - 1 (and the history before pos0); out: bf16 hi/lo [P][Hq * D].
-template <int G>
+// bf16 cache rows are widened into the fp32 tiles with plain loads.
+template <int G, typename KV>
 __global__ void __launch_bounds__(PA_THREADS, 2)
-    prefill_attn_kernel(const float* __restrict__ Q, const float* __restrict__ k_cache,
-                        const float* __restrict__ v_cache, int max_seq, int P, int pos0, int n_heads,
+    prefill_attn_kernel(const float* __restrict__ Q, const KV* __restrict__ k_cache,
+                        const KV* __restrict__ v_cache, int max_seq, int P, int pos0, int n_heads,
                         __nv_bfloat16* out_hi, __nv_bfloat16* out_lo) {
     constexpr int QT = PA_ROWS / G;  // tokens per CTA
     extern __shared__ float4 pa_smem4[];
@@ -86,8 +89,8 @@ __global__ void __launch_bounds__(PA_THREADS, 2)
     const int Hq = n_heads;
     const int t0 = qt * QT;                      // first token of this tile
     const int t_last = min(t0 + QT, P) - 1;
-    const float* kc = k_cache + (size_t)kvh * max_seq * ATT_D;
-    const float* vc = v_cache + (size_t)kvh * max_seq * ATT_D;
+    const KV* kc = k_cache + (size_t)kvh * max_seq * ATT_D;
+    const KV* vc = v_cache + (size_t)kvh * max_seq * ATT_D;
 
     pdl_launch_dependents();
     pdl_wait();
@@ -111,8 +114,15 @@ __global__ void __launch_bounds__(PA_THREADS, 2)
             for (int i = tid; i < PA_KT * ATT_D / 4; i += PA_THREADS) {
                 const int r = i / (ATT_D / 4), c4 = i % (ATT_D / 4);
                 if (k0 + r < n_keys) {
-                    cp_async16(ks + r * PA_KS + 4 * c4, kc + (size_t)(k0 + r) * ATT_D + 4 * c4);
-                    cp_async16(vs + r * PA_KS + 4 * c4, vc + (size_t)(k0 + r) * ATT_D + 4 * c4);
+                    if constexpr (sizeof(KV) == sizeof(float)) {
+                        cp_async16(ks + r * PA_KS + 4 * c4, kc + (size_t)(k0 + r) * ATT_D + 4 * c4);
+                        cp_async16(vs + r * PA_KS + 4 * c4, vc + (size_t)(k0 + r) * ATT_D + 4 * c4);
+                    } else {
+                        *reinterpret_cast<float4*>(ks + r * PA_KS + 4 * c4) =
+                            kv_ld4(kc + (size_t)(k0 + r) * ATT_D + 4 * c4);
+                        *reinterpret_cast<float4*>(vs + r * PA_KS + 4 * c4) =
+                            kv_ld4(vc + (size_t)(k0 + r) * ATT_D + 4 * c4);
+                    }
                 }
             }
         }

@@ -469,9 +469,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     }
 }
 
-// K cache rows [0, n_keys) of [Hkv][max_seq][128] -> fp16 hi/lo [Hkv][ld][128],
-// one warp per 128-float row. A value outside the fp16 range sets status bit 4.
-__global__ void __launch_bounds__(256) fa_k_split_kernel(const float* __restrict__ k_cache, int Hkv, int max_seq,
+// K cache rows [0, n_keys) of [Hkv][max_seq][128] (float or bf16) -> fp16 hi/lo
+// [Hkv][ld][128], one warp per row. A value outside the fp16 range sets status bit 4.
+template <typename KV>
+__global__ void __launch_bounds__(256) fa_k_split_kernel(const KV* __restrict__ k_cache, int Hkv, int max_seq,
                                                          int n_keys, int ld, __half* kh, __half* kl, int* status) {
     pdl_launch_dependents();
     pdl_wait();
@@ -481,7 +482,7 @@ __global__ void __launch_bounds__(256) fa_k_split_kernel(const float* __restrict
     bool bad = false;
     for (long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < rows; w += warps) {
         const int h = (int)(w / n_keys), key = (int)(w % n_keys);
-        const float4 v = reinterpret_cast<const float4*>(k_cache + ((size_t)h * max_seq + key) * ATT_D)[lane];
+        const float4 v = kv_ld4(k_cache + ((size_t)h * max_seq + key) * ATT_D + 4 * lane);
         const size_t dst = ((size_t)h * ld + key) * ATT_D + 4 * lane;
         __half h0, h1, h2, h3, l0, l1, l2, l3;
         split_f16(v.x, h0, l0, bad);
@@ -494,9 +495,11 @@ __global__ void __launch_bounds__(256) fa_k_split_kernel(const float* __restrict
     if (bad) atomicOr(status, 4);
 }
 
-// V cache rows [0, n_keys) of [Hkv][max_seq][128] -> V^T bf16 hi/lo [Hkv][128][ld]
-// (tiles of 64 keys x 128 dims through shared memory; grid (ceil(n_keys/64), Hkv)).
-__global__ void __launch_bounds__(256) fa_v_split_kernel(const float* __restrict__ v_cache, int max_seq, int n_keys,
+// V cache rows [0, n_keys) of [Hkv][max_seq][128] (float or bf16) -> V^T bf16 hi/lo
+// [Hkv][128][ld] (tiles of 64 keys x 128 dims through shared memory; grid
+// (ceil(n_keys/64), Hkv)). A bf16 row splits into itself and zero.
+template <typename KV>
+__global__ void __launch_bounds__(256) fa_v_split_kernel(const KV* __restrict__ v_cache, int max_seq, int n_keys,
                                                          int ld, __nv_bfloat16* vh, __nv_bfloat16* vl) {
     __shared__ float tile[64][ATT_D + 1];
     pdl_launch_dependents();
@@ -504,7 +507,7 @@ __global__ void __launch_bounds__(256) fa_v_split_kernel(const float* __restrict
     const int k0 = blockIdx.x * 64, h = blockIdx.y;
     for (int i = threadIdx.x; i < 64 * ATT_D; i += blockDim.x) {
         const int kk = i / ATT_D, d = i % ATT_D;
-        tile[kk][d] = (k0 + kk < n_keys) ? v_cache[((size_t)h * max_seq + k0 + kk) * ATT_D + d] : 0.f;
+        tile[kk][d] = (k0 + kk < n_keys) ? (float)v_cache[((size_t)h * max_seq + k0 + kk) * ATT_D + d] : 0.f;
     }
     __syncthreads();
     for (int i = threadIdx.x; i < 64 * ATT_D; i += blockDim.x) {

@@ -11,8 +11,8 @@ import dataclasses
 
 import numpy as np
 
-from ._lib import (MF_COMM_HANDLE_BYTES, MF_E_UNSUPPORTED, MF_GEN_MARGINS, MF_GEN_STOP_AT_EOS, MF_GEN_TOKEN_PREFILL,
-                   MinferError, check, cuda_lib, host_lib, mf_gen_stats, mf_model_info, mf_run_params)
+from ._lib import (MF_BF16, MF_COMM_HANDLE_BYTES, MF_E_UNSUPPORTED, MF_GEN_MARGINS, MF_GEN_STOP_AT_EOS,
+                   MF_GEN_TOKEN_PREFILL, MinferError, check, cuda_lib, host_lib, mf_gen_stats, mf_model_info, mf_run_params)
 
 
 @dataclasses.dataclass
@@ -62,10 +62,12 @@ def init(n_ranks: int = 1, devices: list[int] | None = None) -> None:
 class Qwen3Model:
     """`tp_rank`/`tp_size` > 1 loads this process's tensor-parallel shard
     (dense models); after `set_device("cuda")` connect the ranks with
-    `minfer_b200.tp.connect` (or comm_handle / comm_connect directly)."""
+    `minfer_b200.tp.connect` (or comm_handle / comm_connect directly).
+    `kv_dtype` "bf16" opts into a bf16 KV cache (the reference keeps fp32):
+    half the cache bytes, every appended row rounded to nearest even."""
 
     def __init__(self, model_file: str, run_params: RunParams, rank: int = 0, device: int | None = None,
-                 tp_rank: int = 0, tp_size: int = 1):
+                 tp_rank: int = 0, tp_size: int = 1, kv_dtype: str = "f32"):
         if not _initialised:
             init(1, [device if device is not None else 0])
         self._lib = host_lib()
@@ -74,6 +76,11 @@ class Qwen3Model:
         self._rp = run_params.to_c()
         check(self._lib.mf_model_load_tp(str(model_file).encode(), C.byref(self._rp), rank, tp_rank, tp_size,
                                          C.byref(self._h)))
+        if kv_dtype not in ("f32", "bf16"):
+            raise ValueError(f"kv_dtype {kv_dtype!r}: f32 or bf16")
+        if kv_dtype != "f32":
+            check(self._lib.mf_model_set_kv_dtype(self._h, MF_BF16))
+        self.kv_dtype = kv_dtype
         self.device = "cpu"
         self._refresh_info()
 

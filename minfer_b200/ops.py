@@ -133,8 +133,10 @@ def attn_default_split(n_kv_heads: int, max_seq: int) -> int:
 
 def attn_decode(qkv, q_norm_w, k_norm_w, eps: float, rope_table, k_cache, v_cache, max_seq: int, step_state, out,
                 n_heads: int, n_kv_heads: int, d_head: int, n_split: int, workspace):
+    """The cache element type follows k_cache's dtype (float32 or bfloat16)."""
     d = mf_attn_desc(_ptr(qkv), _ptr(q_norm_w), _ptr(k_norm_w), eps, _ptr(rope_table), _ptr(k_cache), _ptr(v_cache),
-                     max_seq, _ptr(step_state), _ptr(out), n_heads, n_kv_heads, d_head, n_split, _ptr(workspace))
+                     max_seq, _ptr(step_state), _ptr(out), n_heads, n_kv_heads, d_head, n_split, _ptr(workspace),
+                     dtype_code(k_cache))
     check(_lib.mf_attn_decode(C.byref(d), _stream()))
 
 

@@ -74,8 +74,9 @@ def attn(args) -> dict:
     H, Hkv, D, ctx = args.hq, args.hkv, 128, args.ctx
     S = ctx + 16
     g = torch.Generator(device="cuda").manual_seed(0)
-    kcs = [torch.randn(Hkv * S * D, generator=g, device="cuda") for _ in range(args.copies)]
-    vcs = [torch.randn(Hkv * S * D, generator=g, device="cuda") for _ in range(args.copies)]
+    kvt = torch.bfloat16 if args.kv == "bf16" else torch.float32
+    kcs = [torch.randn(Hkv * S * D, generator=g, device="cuda").to(kvt) for _ in range(args.copies)]
+    vcs = [torch.randn(Hkv * S * D, generator=g, device="cuda").to(kvt) for _ in range(args.copies)]
     qkv = torch.randn((H + 2 * Hkv) * D, generator=g, device="cuda")
     nw = torch.ones(D, device="cuda")
     rope = ops.rope_table(S, D, 1e6).cuda()
@@ -86,8 +87,8 @@ def attn(args) -> dict:
     fn = lambda i: ops.attn_decode(qkv, nw, nw, 1e-6, rope, kcs[i % len(kcs)], vcs[i % len(vcs)], S, st, out, H,
                                    Hkv, D, split, wsp)
     us = _time(fn, args.iters, args.warmup)
-    algo = 2 * Hkv * (ctx + 1) * D * 4 + (H + 2 * Hkv) * D * 4 + H * D * 4
-    return {"op": "attn-decode", "hq": H, "hkv": Hkv, "ctx": ctx, "split": split, "us": round(us, 2),
+    algo = 2 * Hkv * (ctx + 1) * D * (2 if args.kv == "bf16" else 4) + (H + 2 * Hkv) * D * 4 + H * D * 4
+    return {"op": "attn-decode", "kv": args.kv, "hq": H, "hkv": Hkv, "ctx": ctx, "split": split, "us": round(us, 2),
             "algo_bytes": algo, "gbs": round(algo / us / 1e3, 1)}
 
 
@@ -142,9 +143,9 @@ def pattn(args) -> dict:
     P = lambda t: C.c_void_p(t.data_ptr())
     if args.kernel == "tc":
         fn = lambda i: check(lib.mf_prefill_attention_tc(P(hi), P(lo), P(q), P(kc), P(vc), S, Pn, pos0, Hq, Hkv, D,
-                                                         P(scratch), need.value, C.c_void_p(ops._stream())))
+                                                         P(scratch), need.value, 0, C.c_void_p(ops._stream())))
     else:
-        fn = lambda i: check(lib.mf_prefill_attention(P(hi), P(lo), P(q), P(kc), P(vc), S, Pn, pos0, Hq, Hkv, D,
+        fn = lambda i: check(lib.mf_prefill_attention(P(hi), P(lo), P(q), P(kc), P(vc), S, Pn, pos0, Hq, Hkv, D, 0,
                                                       C.c_void_p(ops._stream())))
     us = _time(fn, args.iters, args.warmup)
     st = C.c_int()
@@ -199,6 +200,7 @@ def main():
     b.add_argument("--hkv", type=int, default=8)
     b.add_argument("--ctx", type=int, default=4096)
     b.add_argument("--split", type=int, default=0)
+    b.add_argument("--kv", default="f32", choices=["f32", "bf16"], help="KV cache element type")
     c = sub.add_parser("gemm")
     c.add_argument("--m", type=int, default=4096)
     c.add_argument("--n", type=int, default=24576)

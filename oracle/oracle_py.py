@@ -164,7 +164,9 @@ class PortModel:
     """The oracle token loop (restatement) over a GGUF file."""
 
     def __init__(self, path: str, max_seq: int, top_k: int = 1, temp: float = 0.0, top_p: float = 1.0,
-                 min_p: float = 0.0, pres: float = 0.0, seed: int = 0):
+                 min_p: float = 0.0, pres: float = 0.0, seed: int = 0, kv_bf16: bool = False):
+        """kv_bf16 emulates the CUDA runtime's opt-in bf16 KV cache (appended
+        rows rounded to bf16, nearest even); the reference has no such option."""
         lib = C.CDLL(str(PORT_LIB))
         lib.orc_model_open.restype = P
         lib.orc_model_open.argtypes = [C.c_char_p, SZ, SZ, F, F, F, F, I]
@@ -188,6 +190,9 @@ class PortModel:
         if not self.h:
             raise RuntimeError(f"oracle could not open {path}")
         self.vocab = lib.orc_model_vocab(self.h)
+        if kv_bf16:
+            lib.orc_model_set_kv_bf16.argtypes = [P, I]
+            lib.orc_model_set_kv_bf16(self.h, 1)
 
     def close(self):
         if self.h:

@@ -44,6 +44,16 @@ float bf16_to_f32(uint16_t b) {
     return f;
 }
 
+// fp32 -> nearest bf16 (ties to even) -> fp32; finite inputs
+float round_bf16(float x) {
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    u = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
+    float r;
+    std::memcpy(&r, &u, 4);
+    return r;
+}
+
 float f16_to_f32(uint16_t h) {
     // exact IEEE binary16 -> binary32
     const uint32_t sign = (uint32_t)(h >> 15) << 31;
@@ -350,6 +360,9 @@ struct orc_model {
     std::vector<int> rec_ids;
     std::vector<float> rec_w;
     bool record = false;
+    // Emulation of the CUDA runtime's opt-in bf16 KV cache (the reference has
+    // none): appended K/V rows rounded to bf16, nearest even, before use.
+    bool kv_bf16 = false;
     // sampler state (src/base/sampler.cpp)
     size_t top_k;
     float temp, top_p, min_p, pres;
@@ -414,6 +427,8 @@ void orc_model_close(orc_model* m) { delete m; }
 
 int orc_model_vocab(const orc_model* m) { return m->V; }
 
+void orc_model_set_kv_bf16(orc_model* m, int on) { m->kv_bf16 = on != 0; }
+
 void orc_model_record_experts(orc_model* m, int on) {
     m->record = on != 0;
     m->rec_ids.clear();
@@ -451,8 +466,8 @@ void orc_model_forward(orc_model* m, uint32_t token, int pos, int compute_logits
         for (int h = 0; h < Hkv; ++h) orc_neox_rope(m->k.data(), m->k.data(), h, D, D, m->base, pos);
         const size_t co = (size_t)l * m->S * kvd + (size_t)pos * kvd;
         for (int i = 0; i < kvd; ++i) {
-            m->kc[co + i] = m->k[i];
-            m->vc[co + i] = m->v[i];
+            m->kc[co + i] = m->kv_bf16 ? round_bf16(m->k[i]) : m->k[i];
+            m->vc[co + i] = m->kv_bf16 ? round_bf16(m->v[i]) : m->v[i];
         }
         const int kv_mul = H / Hkv;
 #pragma omp parallel for

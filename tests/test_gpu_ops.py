@@ -372,6 +372,52 @@ def test_attn_decode_long_context(ops, orc, gpu, H, Hkv, pos):
     assert ws[:Hkv].abs().sum().item() == 0
 
 
+def _bf16(a: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 (round to nearest even) -> fp32."""
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(torch.bfloat16).float().numpy()
+
+
+@pytest.mark.parametrize("H,Hkv,pos", [(32, 8, 4095), (32, 8, 32767), (64, 8, 300), (16, 1, 2049), (8, 8, 17),
+                                       (32, 4, 32767)])
+def test_attn_decode_bf16_cache(ops, orc, gpu, H, Hkv, pos):
+    """Opt-in bf16 KV cache: the history rows as stored (bf16, widened exactly),
+    the appended K/V row rounded to nearest even and used rounded. Compared
+    with the oracle on those same values: the rounded k may differ from the
+    oracle's by one bf16 step where the fp32 values differ in their last bits."""
+    D, S = 128, pos + 1
+    rng = np.random.default_rng(H * 11 + pos)
+    qkv = rng.standard_normal((H + 2 * Hkv) * D).astype(np.float32)
+    qn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    kc_hist = _bf16(rng.standard_normal((S, Hkv, D), dtype=np.float32))
+    vc_hist = _bf16(rng.standard_normal((S, Hkv, D), dtype=np.float32))
+    rope = ops.rope_table(S, D, 1e6)
+    kc = T(np.ascontiguousarray(kc_hist.transpose(1, 0, 2)), gpu).to(torch.bfloat16)
+    vc = T(np.ascontiguousarray(vc_hist.transpose(1, 0, 2)), gpu).to(torch.bfloat16)
+    n_split = ops.attn_default_split(Hkv, S)
+    ws = torch.zeros(ops.attn_workspace_bytes(H, Hkv, D, n_split) // 4 + 1, dtype=torch.int32, device=gpu)
+    st = torch.tensor([0, pos, 0, 0, 0, 0, 0, 0], dtype=torch.int32, device=gpu)
+    out = torch.zeros(H * D, device=gpu)
+    ops.attn_decode(T(qkv, gpu), T(qn, gpu), T(kn, gpu), 1e-6, rope.to(gpu), kc, vc, S, st, out, H, Hkv, D, n_split, ws)
+    _, kref, vref = _attn_reference(orc, qkv, qn, kn, 1e-6, rope, kc_hist, vc_hist, pos, H, Hkv, D)
+    krow = kc[:, pos, :].float().cpu().numpy()
+    np.testing.assert_allclose(krow, _bf16(kref), rtol=2 ** -7, atol=0)
+    np.testing.assert_array_equal(vc[:, pos, :].float().cpu().numpy(), _bf16(vref))
+    # the oracle's attention over exactly the rows the cache holds (history + the stored row)
+    kh, vh = kc_hist.copy(), vc_hist.copy()
+    kh[pos], vh[pos] = krow, _bf16(vref)
+    ref = np.zeros(H * D, np.float32)
+    G = H // Hkv
+    for h in range(H):
+        qh = orc.rope(orc.rmsnorm(qkv[h * D:(h + 1) * D], qn, 1e-6), 0, D, D, 1e6, pos)
+        kvh = h // G
+        _, o = orc.attn(qh, np.ascontiguousarray(kh[:, kvh, :]).ravel(), np.ascontiguousarray(vh[:, kvh, :]).ravel(),
+                        pos + 1, D, D)
+        ref[h * D:(h + 1) * D] = o
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=2e-5, atol=2e-5)
+    assert ws[:Hkv].abs().sum().item() == 0
+
+
 def test_attn_decode_position_out_of_range(ops, gpu):
     # a step record whose position has no cache row: nothing is written, the output is zero
     D, S, H, Hkv = 128, 64, 8, 2

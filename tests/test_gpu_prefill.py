@@ -17,6 +17,9 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
+KV_DT = {"f32": torch.float32, "bf16": torch.bfloat16}
+KV_CODE = {"f32": 0, "bf16": 2}  # MF_F32, MF_BF16
+
 
 def P(t):
     return C.c_void_p(t.data_ptr())
@@ -130,31 +133,35 @@ def _attn_ref(q, kc, vc, pos0, Hq, Hkv):
     return out
 
 
-@pytest.mark.parametrize("Hq,Hkv,T,pos0", [(32, 8, 100, 0), (16, 2, 67, 0), (8, 8, 33, 40), (16, 1, 20, 5),
-                                           (64, 8, 130, 0)])
-def test_prefill_attention(lib, gpu, Hq, Hkv, T, pos0):
+@pytest.mark.parametrize("Hq,Hkv,T,pos0,kv", [(32, 8, 100, 0, "f32"), (16, 2, 67, 0, "f32"), (8, 8, 33, 40, "f32"),
+                                              (16, 1, 20, 5, "f32"), (64, 8, 130, 0, "f32"), (32, 8, 100, 0, "bf16"),
+                                              (8, 8, 33, 40, "bf16")])
+def test_prefill_attention(lib, gpu, Hq, Hkv, T, pos0, kv):
+    """SIMT kernel vs float64 on the cache as stored (a bf16 cache is widened exactly)."""
     from minfer_b200._lib import check
 
     S, D = 256, 128
     g = torch.Generator(device=gpu).manual_seed(Hq + T)
     q = torch.randn(T, Hq * D, generator=g, device=gpu)
-    kc = torch.randn(Hkv, S, D, generator=g, device=gpu)
-    vc = torch.randn(Hkv, S, D, generator=g, device=gpu)
+    kc = torch.randn(Hkv, S, D, generator=g, device=gpu).to(KV_DT[kv])
+    vc = torch.randn(Hkv, S, D, generator=g, device=gpu).to(KV_DT[kv])
     hi = torch.empty(T, Hq * D, dtype=torch.bfloat16, device=gpu)
     lo = torch.empty_like(hi)
-    check(lib.mf_prefill_attention(P(hi), P(lo), P(q), P(kc), P(vc), S, T, pos0, Hq, Hkv, D, stream()))
+    check(lib.mf_prefill_attention(P(hi), P(lo), P(q), P(kc), P(vc), S, T, pos0, Hq, Hkv, D, KV_CODE[kv], stream()))
     torch.cuda.synchronize()
-    ref = _attn_ref(q, kc, vc, pos0, Hq, Hkv)
+    ref = _attn_ref(q, kc.float(), vc.float(), pos0, Hq, Hkv)
     got = (hi.double() + lo.double()).cpu()
     assert (got - ref).abs().max().item() <= 2e-5
 
 
-@pytest.mark.parametrize("Hq,Hkv,T,pos0,S,qs", [(32, 8, 100, 0, 256, 1), (16, 2, 67, 0, 256, 1),
-                                                (8, 8, 33, 40, 256, 1), (16, 1, 20, 5, 256, 1),
-                                                (64, 8, 130, 0, 256, 1), (8, 8, 300, 200, 512, 1),
-                                                (32, 8, 257, 63, 384, 1), (16, 4, 64, 64, 128, 1),
-                                                (16, 2, 150, 1100, 1280, 4), (8, 1, 90, 700, 800, 8)])
-def test_prefill_attention_tensor_cores(lib, gpu, Hq, Hkv, T, pos0, S, qs):
+@pytest.mark.parametrize("Hq,Hkv,T,pos0,S,qs,kv", [(32, 8, 100, 0, 256, 1, "f32"), (16, 2, 67, 0, 256, 1, "f32"),
+                                                   (8, 8, 33, 40, 256, 1, "f32"), (16, 1, 20, 5, 256, 1, "f32"),
+                                                   (64, 8, 130, 0, 256, 1, "f32"), (8, 8, 300, 200, 512, 1, "f32"),
+                                                   (32, 8, 257, 63, 384, 1, "f32"), (16, 4, 64, 64, 128, 1, "f32"),
+                                                   (16, 2, 150, 1100, 1280, 4, "f32"), (8, 1, 90, 700, 800, 8, "f32"),
+                                                   (32, 8, 257, 63, 384, 1, "bf16"),
+                                                   (16, 2, 150, 1100, 1280, 4, "bf16")])
+def test_prefill_attention_tensor_cores(lib, gpu, Hq, Hkv, T, pos0, S, qs, kv):
     """tcgen05 attention vs float64: max-abs <= 2e-5 * max|V|. q/k are carried as
     fp16 hi + lo (~2^-22 relative), P and V as bf16 hi + lo (~2^-17 relative each,
     lo*lo dropped): an output dominated by one key carries up to ~1.5e-5 of that
@@ -164,20 +171,20 @@ def test_prefill_attention_tensor_cores(lib, gpu, Hq, Hkv, T, pos0, S, qs):
     D = 128
     g = torch.Generator(device=gpu).manual_seed(Hq + T + pos0)
     q = torch.randn(T, Hq * D, generator=g, device=gpu) * qs  # qs > 1: peaked softmax, late max moves
-    kc = torch.randn(Hkv, S, D, generator=g, device=gpu)
-    vc = torch.randn(Hkv, S, D, generator=g, device=gpu)
+    kc = torch.randn(Hkv, S, D, generator=g, device=gpu).to(KV_DT[kv])
+    vc = torch.randn(Hkv, S, D, generator=g, device=gpu).to(KV_DT[kv])
     hi = torch.empty(T, Hq * D, dtype=torch.bfloat16, device=gpu)
     lo = torch.empty_like(hi)
     need = C.c_size_t()
     check(lib.mf_prefill_attention_scratch(T, pos0 + T, Hq, Hkv, C.byref(need)))
     scratch = torch.full((need.value,), 255, dtype=torch.uint8, device=gpu)  # NaN-patterned leftovers
     check(lib.mf_prefill_attention_tc(P(hi), P(lo), P(q), P(kc), P(vc), S, T, pos0, Hq, Hkv, D, P(scratch),
-                                      need.value, stream()))
+                                      need.value, KV_CODE[kv], stream()))
     torch.cuda.synchronize()
     assert status_ok(lib)
-    ref = _attn_ref(q, kc, vc, pos0, Hq, Hkv)
+    ref = _attn_ref(q, kc.float(), vc.float(), pos0, Hq, Hkv)
     got = (hi.double() + lo.double()).cpu()
-    assert (got - ref).abs().max().item() <= 2e-5 * vc.abs().max().item()
+    assert (got - ref).abs().max().item() <= 2e-5 * vc.float().abs().max().item()
 
 
 def test_prefill_attention_tensor_cores_flags_fp16_range(lib, gpu):
@@ -195,14 +202,17 @@ def test_prefill_attention_tensor_cores_flags_fp16_range(lib, gpu):
     check(lib.mf_prefill_attention_scratch(T, T, Hq, Hkv, C.byref(need)))
     scratch = torch.empty(need.value, dtype=torch.uint8, device=gpu)
     check(lib.mf_prefill_attention_tc(P(hi), P(lo), P(q), P(kc), P(vc), S, T, 0, Hq, Hkv, D, P(scratch), need.value,
-                                      stream()))
+                                      0, stream()))
     st = C.c_int()
     check(lib.mf_prefill_status(C.byref(st), 1))
     assert st.value == 4
 
 
-def test_prefill_qkv_post_matches_decode_rotation(lib, gpu):
-    """Same per-head norm + RoPE as the decode kernel: compare with the oracle's restatement."""
+@pytest.mark.parametrize("kv", ["f32", "bf16"])
+def test_prefill_qkv_post_matches_decode_rotation(lib, gpu, kv):
+    """Same per-head norm + RoPE as the decode kernel: compare with the oracle's
+    restatement (a bf16 cache row holds the restatement's value rounded to
+    nearest even)."""
     from conftest import TINY  # noqa: F401
     from minfer_b200 import ops
     from minfer_b200._lib import check
@@ -215,12 +225,15 @@ def test_prefill_qkv_post_matches_decode_rotation(lib, gpu):
     kn = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
     rope = ops.rope_table(S, D, 1e6).to(gpu)
     qo = torch.zeros(T, Hq * D, device=gpu)
-    kc = torch.zeros(Hkv, S, D, device=gpu)
-    vc = torch.zeros(Hkv, S, D, device=gpu)
+    kc = torch.zeros(Hkv, S, D, device=gpu, dtype=KV_DT[kv])
+    vc = torch.zeros(Hkv, S, D, device=gpu, dtype=KV_DT[kv])
     qkv_t, qn_t, kn_t = (torch.from_numpy(a).to(gpu) for a in (qkv, qn, kn))  # alive until the kernel ran
     check(lib.mf_prefill_qkv_post(P(qo), P(kc), P(vc), P(qkv_t), P(qn_t), P(kn_t), C.c_float(1e-6), P(rope),
-                                  S, Hq, Hkv, D, T, pos0, stream()))
+                                  S, Hq, Hkv, D, T, pos0, KV_CODE[kv], stream()))
     torch.cuda.synchronize()
+    rnd = (lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(torch.bfloat16).float().numpy()) if kv == "bf16" \
+        else (lambda a: a)
+    kc, vc = kc.float(), vc.float()
     po = PortOps()
     for t in range(T):
         for h in range(Hq):
@@ -230,8 +243,12 @@ def test_prefill_qkv_post_matches_decode_rotation(lib, gpu):
         for h in range(Hkv):
             x = po.rmsnorm(qkv[t, (Hq + h) * D:(Hq + h + 1) * D], kn, 1e-6)
             exp = po.rope(x, 0, D, D, 1e6, pos0 + t)
-            np.testing.assert_allclose(kc[h, pos0 + t].cpu().numpy(), exp, rtol=2e-6, atol=2e-6)
-            np.testing.assert_array_equal(vc[h, pos0 + t].cpu().numpy(), qkv[t, (Hq + Hkv + h) * D:(Hq + Hkv + h + 1) * D])
+            got = kc[h, pos0 + t].cpu().numpy()
+            if kv == "f32":
+                np.testing.assert_allclose(got, exp, rtol=2e-6, atol=2e-6)
+            else:  # the rounding may differ only where the fp32 values differ (one bf16 step)
+                np.testing.assert_allclose(got, rnd(exp), rtol=2 ** -7, atol=1e-30)
+            np.testing.assert_array_equal(vc[h, pos0 + t].cpu().numpy(), rnd(qkv[t, (Hq + Hkv + h) * D:(Hq + Hkv + h + 1) * D]))
     assert kc[:, :pos0].abs().sum().item() == 0 and kc[:, pos0 + T:].abs().sum().item() == 0
 
 

@@ -12,8 +12,8 @@ import numpy as np
 import pytest
 
 from conftest import TINY, tiny_model
-from minfer_b200._lib import (HOST_API, CUDA_API, MF_E_INVALID, MF_OK, cuda_lib, host_lib, last_error,
-                              mf_model_info, mf_run_params)
+from minfer_b200._lib import (HOST_API, CUDA_API, MF_E_INVALID, MF_E_UNSUPPORTED, MF_OK, cuda_lib, host_lib,
+                              last_error, mf_model_info, mf_run_params)
 from minfer_b200.gguf_synth import Qwen3Shape, random_prompt, write_qwen3_gguf
 from oracle.oracle_py import PortModel, PortOps
 
@@ -243,7 +243,7 @@ def test_ops_validate_before_touching_the_device():
     assert lib.mf_prefill_attention_scratch(100, 99, 32, 8, C.byref(need)) == MF_E_INVALID
     fake = C.c_void_p(1 << 20)
     args = (fake, fake, fake, fake, fake, 256, 100, 40, 32, 8, 128)  # 40 + 100 = 140 keys
-    assert lib.mf_prefill_attention_tc(*args, fake, need.value - 1, None) == MF_E_INVALID
+    assert lib.mf_prefill_attention_tc(*args, fake, need.value - 1, 0, None) == MF_E_INVALID
     msg = C.create_string_buffer(256)
     lib.mf_last_error(msg, 256)
     assert b"scratch too small" in msg.value
@@ -256,6 +256,7 @@ def test_ops_validate_before_touching_the_device():
     assert lib.mf_bulk_allreduce(None, 16, None, 0, 1, None) == MF_E_INVALID
     assert lib.mf_bulk_allreduce(fake, 16, None, 2, 1, None) == MF_E_INVALID
     assert lib.mf_comm_bulk_ptr(None, 0, C.byref(C.c_void_p())) == MF_E_INVALID
-    assert lib.mf_prefill_attention_tc(*args, C.c_void_p((1 << 20) + 16), need.value, None) == MF_E_INVALID
-    assert lib.mf_prefill_attention_tc(*args[:6], 300, *args[7:], fake, need.value, None) == MF_E_INVALID
+    assert lib.mf_prefill_attention_tc(*args, C.c_void_p((1 << 20) + 16), need.value, 0, None) == MF_E_INVALID
+    assert lib.mf_prefill_attention_tc(*args[:6], 300, *args[7:], fake, need.value, 0, None) == MF_E_INVALID
+    assert lib.mf_prefill_attention_tc(*args, fake, need.value, 1, None) == MF_E_UNSUPPORTED  # f16 cache
     assert lib.mf_lm_head(None, None, None, 1e-6, None, 2, 10, 16, 0, None, None, None) == MF_E_INVALID

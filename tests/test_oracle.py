@@ -162,3 +162,28 @@ def test_golden_logits_step0():
 def test_tolerances_sane():
     # the parity tests' fp32 dot bound is loose enough for a 16-lane vs CTA-wide sum
     assert 8 * math.sqrt(4096) * 2.0 ** -24 < 1e-4
+
+
+def test_kv_bf16_emulation_rounds_to_nearest_even():
+    """The oracle's emulation of the runtime's opt-in bf16 KV cache: the first
+    token's layer-0 K/V rows are the fp32 run's rows rounded to bf16, nearest
+    even (numpy bit arithmetic as the check); later rows differ because the
+    attention then reads rounded history."""
+    cfg = TINY["tiny-bf16"]
+    path = tiny_model("tiny-bf16")
+    kvd = cfg.n_kv_heads * cfg.d_head
+    a = PortModel(path, max_seq=4)
+    b = PortModel(path, max_seq=4, kv_bf16=True)
+    for m in (a, b):
+        m.forward(5, 0, True)
+    k32, v32 = a.kv(0, 1, kvd)
+    k16, v16 = b.kv(0, 1, kvd)
+
+    def rne(x):
+        u = x.view(np.uint32).astype(np.uint64)
+        u = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+        return u.view(np.float32)
+
+    assert np.array_equal(k16, rne(k32)) and np.array_equal(v16, rne(v32))
+    assert not np.array_equal(k16, k32)
+    assert np.abs(b.logits() - a.logits()).max() > 0
