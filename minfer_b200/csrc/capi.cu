@@ -298,16 +298,24 @@ int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_
     static const int max_row_kb = env_int("MF_GEMV_TMA_MAX_ROW_KB", 10);
     static const int split_on = env_int("MF_GEMV_TMA_SPLIT", 1);
     static const int tp_on = env_int("MF_GEMV_TMA_TP", 1);  // the tensor-parallel receive/send forms
+    static const int moe_on = env_int("MF_GEMV_TMA_MOE", 1);  // the grouped-expert gate/up form
     if (!on) return 0;
     const bool tp = xm == mf::X_AR_NORM || ym == mf::Y_PUSH;
     if (tp && !tp_on) return 0;
     if (!(xm == mf::X_PLAIN || xm == mf::X_NORM || xm == mf::X_AR_NORM) ||
         !(ym == mf::Y_STORE || ym == mf::Y_RESID || ym == mf::Y_SWIGLU || ym == mf::Y_PUSH))
         return 0;
-    if (q.expert_ids || q.counter || q.gather_logits) return 0;
+    if (q.counter || q.gather_logits) return 0;
+    // grouped experts: the SwiGLU form over every selected expert stored here
+    const bool grouped = q.expert_ids != nullptr;
+    if (grouped && !(moe_on && xm == mf::X_NORM && ym == mf::Y_SWIGLU && q.ep_n == 0 && q.rows_per_expert > 0 &&
+                     q.rows_per_expert % 2 == 0 && q.rows % q.rows_per_expert == 0 &&
+                     q.rows / q.rows_per_expert <= 32))
+        return 0;
     const int vec = vec_of(dtype);
     const size_t esz = esz_of(dtype);
     const size_t full_row = (size_t)q.K * esz;
+    if (grouped && full_row > (size_t)max_row_kb * 1024) return 0;
     int ks = 1;
     if (full_row > (size_t)max_row_kb * 1024) {
         if (!split_on || xm != mf::X_PLAIN || ym == mf::Y_SWIGLU) return 0;
@@ -386,9 +394,75 @@ int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_
         p.x_out = q.x_out;
         if (xm == mf::X_AR_NORM) p.x = q.x_out;  // read after the receive and the grid barrier
     }
+    if (grouped) {
+        p.expert_ids = q.expert_ids;
+        p.rows_per_expert = q.rows_per_expert;
+        p.expert_bytes = (unsigned long long)q.rows_per_expert * row_bytes;
+    }
     void* args[] = {&p};
     if (ks == 1) MF_CK(launch(fn, dim3((unsigned)nblk), dim3((nwc + 1) * 32), smem, st, args));
     else MF_CK(launch_cluster(fn, dim3((unsigned)(nblk * ks)), dim3((nwc + 1) * 32), smem, st, args, ks));
+    return 1;
+}
+
+// The TMA-fed grouped expert down projection (moe_down_tma_kernel): 1 when it
+// launched, 0 when left to the register-fed kernel (MF_GEMV_TMA_MOE=0, expert
+// parallelism, rows wider than 10 KB or K beyond 8 vectors per lane), < 0 on error.
+int try_moe_down_tma(int dtype, const mf::GemvParams& q, cudaStream_t st) {
+    static const int on = env_int("MF_GEMV_TMA", 1) && env_int("MF_GEMV_TMA_MOE", 1);
+    static const long long timeout_ms = env_int("MF_DECODE_TIMEOUT_MS", 1000);
+    static const size_t stage_target = (size_t)env_int("MF_MOE_TMA_STAGE_KB", 16) * 1024;
+    static const size_t ring_bytes = (size_t)env_int("MF_GEMV_TMA_RING_KB", mf::GT_RING_BYTES / 1024) * 1024;
+    if (!on || q.ep_n != 0 || q.n_slots < 1 || q.n_slots > mf::MD_WARPS) return 0;
+    const int vec = vec_of(dtype);
+    const size_t row_bytes = (size_t)q.K * esz_of(dtype);
+    if (row_bytes > 10 * 1024 || row_bytes % 16 != 0) return 0;
+    const int NV = q.K / vec;
+    int j = (NV + 31) / 32;
+    static const int js[] = {1, 2, 3, 4, 6, 8};
+    int jj = 0;
+    for (int c : js)
+        if (c >= j) {
+            jj = c;
+            break;
+        }
+    if (!jj) return 0;
+    const void* fn = dtype == MF_F32   ? mf::moe_down_tma_ptr_f32(jj)
+                     : dtype == MF_F16 ? mf::moe_down_tma_ptr_f16(jj)
+                                       : mf::moe_down_tma_ptr_bf16(jj);
+    if (!fn) return 0;
+    const size_t slot_bytes = (size_t)q.n_slots * row_bytes;  // one output row of every slot
+    int R = (int)std::max<size_t>(1, stage_target / slot_bytes);
+    const size_t stage_bytes = (size_t)R * slot_bytes;
+    int stages = (int)std::max<size_t>(2, std::min<size_t>(ring_bytes / stage_bytes, mf::GT_MAX_STAGES));
+    int* status = decode_status_ptr();
+    if (!status) return 0;
+    const long long nblk = std::max<long long>(1, std::min<long long>((long long)num_sms() * 2, q.rows));
+    const size_t max_rows = (size_t)((q.rows + nblk - 1) / nblk);
+    const size_t smem = (size_t)stages * stage_bytes + max_rows * q.n_slots * sizeof(float);
+    if (smem > 200 * 1024) return 0;
+    int bps = 0;
+    int rc = prepare(fn, (mf::MD_WARPS + 1) * 32, smem, &bps);
+    if (rc) return rc;
+    if (bps < 1) return 0;
+    mf::MoeDownTmaParams p = {};
+    p.w = (const char*)q.w + q.w_offset * esz_of(dtype);
+    p.row_bytes = row_bytes;
+    p.expert_bytes = (unsigned long long)q.rows_per_expert * row_bytes;
+    p.rows = q.rows;
+    p.K = q.K;
+    p.k = q.n_slots;
+    p.h = q.x;
+    p.ids = q.expert_ids;
+    p.ew = q.expert_w;
+    p.x = q.y;
+    p.rows_per_stage = R;
+    p.stages = stages;
+    p.stage_bytes = (uint32_t)stage_bytes;
+    p.status = status;
+    p.timeout_ns = (unsigned long long)std::max(1ll, timeout_ms) * 1000000ull;
+    void* args[] = {&p};
+    MF_CK(launch(fn, dim3((unsigned)nblk), dim3((mf::MD_WARPS + 1) * 32), smem, st, args));
     return 1;
 }
 
@@ -1039,6 +1113,12 @@ int mf_moe_down_residual(float* x, const float* h, const void* w_down_exps, int 
     p.expert_w = weights;
     p.rows_per_expert = d_model;
     p.n_slots = k;
+    MF_REQUIRE(d_ff > 0 && d_ff % 16 == 0 && d_model > 0, MF_E_INVALID, "bad d_ff/d_model");
+    MF_REQUIRE(((uintptr_t)w_down_exps) % 16 == 0 && ((uintptr_t)h) % 16 == 0, MF_E_INVALID,
+               "weights and h must be 16-byte aligned");
+    const int tr = try_moe_down_tma(dtype, p, resolve(stream));
+    if (tr < 0) return tr;
+    if (tr == 1) return MF_OK;
     return run_gemv(dtype, mf::X_PLAIN, mf::Y_MOE_DOWN, p, d_model, resolve(stream));
 }
 

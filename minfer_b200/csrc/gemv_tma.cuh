@@ -70,6 +70,13 @@ struct GemvTmaParams {
     const int* step;        // device step record (frame number for the tags)
     const float* x_res;     // X_AR_NORM: residual before the all-reduce (x is then x_out)
     float* x_out;           // X_AR_NORM: residual after it
+    // grouped experts (Y_SWIGLU over the k selected experts): logical row r is
+    // row r % rows_per_expert of expert expert_ids[r / rows_per_expert], whose
+    // matrix starts expert_bytes * id into w. The ids come from the router
+    // kernel, so the producer copies only after the dependency wait.
+    const int* expert_ids;  // [rows / rows_per_expert] device, or null (dense)
+    int rows_per_expert;
+    unsigned long long expert_bytes;
 };
 
 MF_DEVICE uint32_t cluster_rank() {
@@ -105,6 +112,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
     __shared__ __align__(8) uint64_t full[GT_MAX_STAGES], empty[GT_MAX_STAGES];
     __shared__ float ss_part[NWC];
     __shared__ int abort_s;
+    __shared__ int eid_s[32];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const long long units = p.rows / RU;
@@ -137,6 +145,13 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
         // (its CTAs fit beside this one and fill their own rings meanwhile).
         pdl_launch_dependents();
         if (lane == 0) {
+            const bool grouped = p.expert_ids != nullptr;
+            if (grouped) {
+                // the expert ids are the router kernel's output (read from L2)
+                pdl_wait();
+                const int n_ids = p.rows / p.rows_per_expert;
+                for (int i = 0; i < n_ids && i < 32; ++i) eid_s[i] = __ldcg(p.expert_ids + i);
+            }
             bool failed = false;
             int c = 0;
             for (; c < nchunks; ++c) {
@@ -147,7 +162,18 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
                 const uint32_t bytes = (uint32_t)(rr * p.row_bytes);
                 mbar_expect_tx(&full[s], bytes);
                 const char* src = p.w + (size_t)(r0 + c * p.rows_per_stage) * p.row_stride + kofs;
-                if (ks == 1) {
+                if (grouped) {  // one copy per run of rows inside one expert
+                    int r = 0;
+                    while (r < rr) {
+                        const int lr = r0 + c * p.rows_per_stage + r;
+                        const int slot = lr / p.rows_per_expert, er = lr - slot * p.rows_per_expert;
+                        const int n = min(rr - r, p.rows_per_expert - er);
+                        bulk_load(gt_smem + (size_t)s * p.stage_bytes + (size_t)r * p.row_bytes,
+                                  p.w + (size_t)eid_s[slot] * p.expert_bytes + (size_t)er * p.row_bytes,
+                                  (uint32_t)(n * p.row_bytes), &full[s]);
+                        r += n;
+                    }
+                } else if (ks == 1) {
                     bulk_load(gt_smem + (size_t)s * p.stage_bytes, src, bytes, &full[s]);
                 } else {  // the slices of consecutive rows are row_stride apart: one copy per row
                     for (int r = 0; r < rr; ++r)
@@ -348,6 +374,184 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
     }
 }
 
+// Grouped expert down projection + weighted residual (MoE, batch 1), fed by
+// TMA bulk copies: x[j] += sum over slots s in order of w_s * (W_down[ids[s]]
+// row j . h_s) (src/models/qwen3/module.cpp:469-474, one expert at a time).
+//
+// A CTA owns a contiguous range of output rows j; a ring stage holds the same
+// R rows of every selected expert ([slot][R rows], one copy per slot). Eight
+// consumer warps: warp s computes slot s's dot products over the whole K (its
+// lanes hold slot s's h vector in registers); the epilogue adds the slots in
+// order into the residual. The ids come from the router, so the producer
+// copies only after the dependency wait.
+struct MoeDownTmaParams {
+    const char* w;                     // [E][rows][K] expert matrices
+    unsigned long long row_bytes;      // K * sizeof(W)
+    unsigned long long expert_bytes;   // rows * row_bytes
+    int rows;                          // d_model
+    int K;                             // d_ff
+    int k;                             // slots (1..8)
+    const float* h;                    // [k][K]
+    const int* ids;                    // [k]
+    const float* ew;                   // [k]
+    float* x;                          // [rows] residual, updated in place
+    int rows_per_stage;                // output rows per stage
+    int stages;
+    uint32_t stage_bytes;              // k * rows_per_stage * row_bytes
+    int* status;
+    unsigned long long timeout_ns;
+};
+
+constexpr int MD_WARPS = 8;  // consumer warps = the most slots
+
+template <typename W, int J>
+__global__ void __launch_bounds__((MD_WARPS + 1) * 32, 1) moe_down_tma_kernel(const MoeDownTmaParams p) {
+    constexpr int VEC = W::VEC;
+    extern __shared__ __align__(128) unsigned char gt_smem[];
+    __shared__ __align__(8) uint64_t full[GT_MAX_STAGES], empty[GT_MAX_STAGES];
+    __shared__ int eid_s[MD_WARPS];
+    __shared__ int abort_s;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int r0 = (int)((long long)blockIdx.x * p.rows / gridDim.x);
+    const int r1 = (int)((long long)(blockIdx.x + 1) * p.rows / gridDim.x);
+    const int nrows = r1 - r0, R = p.rows_per_stage, S = p.stages;
+    const int nchunks = (nrows + R - 1) / R;
+    float* ys = reinterpret_cast<float*>(gt_smem + (size_t)S * p.stage_bytes);  // [k][nrows]
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], MD_WARPS);
+        }
+        abort_s = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const unsigned long long deadline = globaltimer_ns() + p.timeout_ns;
+
+    if (warp == MD_WARPS) {
+        pdl_launch_dependents();
+        if (lane == 0) {
+            pdl_wait();
+            for (int i = 0; i < p.k; ++i) eid_s[i] = __ldcg(p.ids + i);
+            bool failed = false;
+            int c = 0;
+            for (; c < nchunks; ++c) {
+                const int s = c % S;
+                if (c >= S && !mbar_wait(&empty[s], (uint32_t)((c / S - 1) & 1), deadline, failed)) break;
+                if (*(volatile int*)&abort_s) break;
+                const int rr = min(R, nrows - c * R);
+                const uint32_t bytes = (uint32_t)(rr * p.row_bytes);
+                mbar_expect_tx(&full[s], bytes * (uint32_t)p.k);
+                for (int sl = 0; sl < p.k; ++sl)
+                    bulk_load(gt_smem + (size_t)s * p.stage_bytes + (size_t)sl * R * p.row_bytes,
+                              p.w + (size_t)eid_s[sl] * p.expert_bytes + (size_t)(r0 + c * R) * p.row_bytes, bytes,
+                              &full[s]);
+            }
+            if (failed) {
+                atomicOr(p.status, GT_STATUS_TIMEOUT);
+                abort_s = 1;
+            }
+            bool drain_failed = false;
+            for (int d = max(0, c - S); d < c; ++d)
+                mbar_wait(&full[d % S], (uint32_t)((d / S) & 1), deadline + p.timeout_ns, drain_failed);
+        }
+        return;
+    }
+
+    // ---- consumer warp `warp` = slot `warp` (warps past k only release stages)
+    const bool active = warp < p.k;
+    const int NV = p.K / VEC;
+    float xr[J][VEC];
+    pdl_launch_dependents();
+    pdl_wait();
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int v = lane + 32 * j;
+#pragma unroll
+        for (int e = 0; e < VEC; e += 4) {
+            float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (active && v < NV) t = __ldcg(reinterpret_cast<const float4*>(p.h + (size_t)warp * p.K + (size_t)v * VEC + e));
+            xr[j][e] = t.x; xr[j][e + 1] = t.y; xr[j][e + 2] = t.z; xr[j][e + 3] = t.w;
+        }
+    }
+    bool failed = false;
+    for (int c = 0; c < nchunks; ++c) {
+        const int s = c % S;
+        if (!mbar_wait(&full[s], (uint32_t)((c / S) & 1), deadline, failed)) break;
+        if (active) {
+            const unsigned char* st = gt_smem + (size_t)s * p.stage_bytes + (size_t)warp * R * p.row_bytes;
+            const int rr = min(R, nrows - c * R);
+            int rg = 0;
+            for (; rg + GT_RG <= rr; rg += GT_RG) {
+                uint4 wv[GT_RG][J];
+#pragma unroll
+                for (int r = 0; r < GT_RG; ++r)
+#pragma unroll
+                    for (int j = 0; j < J; ++j) {
+                        const int v = lane + 32 * j;
+                        wv[r][j] = v < NV ? *reinterpret_cast<const uint4*>(st + (size_t)(rg + r) * p.row_bytes + (size_t)v * 16)
+                                          : make_uint4(0u, 0u, 0u, 0u);
+                    }
+                float acc[GT_RG];
+#pragma unroll
+                for (int r = 0; r < GT_RG; ++r) {
+                    acc[r] = 0.f;
+#pragma unroll
+                    for (int j = 0; j < J; ++j) {
+                        float wf[VEC];
+                        unpack16<W>(wv[r][j], wf);
+#pragma unroll
+                        for (int e = 0; e < VEC; ++e) acc[r] = fmaf(xr[j][e], wf[e], acc[r]);
+                    }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                    for (int r = 0; r < GT_RG; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+                if (lane < GT_RG) {
+                    float a = acc[0];
+#pragma unroll
+                    for (int r = 1; r < GT_RG; ++r)
+                        if (lane == r) a = acc[r];
+                    ys[(size_t)warp * nrows + c * R + rg + lane] = a;
+                }
+            }
+            for (; rg < rr; ++rg) {
+                float acc = 0.f;
+#pragma unroll
+                for (int j = 0; j < J; ++j) {
+                    const int v = lane + 32 * j;
+                    if (v < NV) {
+                        const uint4 wv = *reinterpret_cast<const uint4*>(st + (size_t)rg * p.row_bytes + (size_t)v * 16);
+                        float wf[VEC];
+                        unpack16<W>(wv, wf);
+#pragma unroll
+                        for (int e = 0; e < VEC; ++e) acc = fmaf(xr[j][e], wf[e], acc);
+                    }
+                }
+                acc = warp_sum(acc);
+                if (lane == 0) ys[(size_t)warp * nrows + c * R + rg] = acc;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (failed && lane == 0) {
+        atomicOr(p.status, GT_STATUS_TIMEOUT);
+        abort_s = 1;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(MD_WARPS * 32) : "memory");
+    if (*(volatile int*)&abort_s) return;
+    // src/models/qwen3/module.cpp:471-474: x += expert_out * weight, one expert at a time
+    for (int u = tid; u < nrows; u += MD_WARPS * 32) {
+        float xo = __ldcg(p.x + r0 + u);
+        for (int sl = 0; sl < p.k; ++sl) xo = fmaf(ys[(size_t)sl * nrows + u], __ldcg(p.ew + sl), xo);
+        p.x[r0 + u] = xo;
+    }
+}
+
 }  // namespace mf
 
 namespace mf {
@@ -376,7 +580,22 @@ const void* gemv_tma_ptr(int xm, int ym, int nwc, int j) {
 #undef MF_GT
     return nullptr;
 }
+template <typename W>
+const void* moe_down_tma_ptr(int j) {
+    switch (j) {
+        case 1: return (const void*)&moe_down_tma_kernel<W, 1>;
+        case 2: return (const void*)&moe_down_tma_kernel<W, 2>;
+        case 3: return (const void*)&moe_down_tma_kernel<W, 3>;
+        case 4: return (const void*)&moe_down_tma_kernel<W, 4>;
+        case 6: return (const void*)&moe_down_tma_kernel<W, 6>;
+        case 8: return (const void*)&moe_down_tma_kernel<W, 8>;
+        default: return nullptr;
+    }
+}
 const void* gemv_tma_ptr_f32(int xm, int ym, int nwc, int j);
 const void* gemv_tma_ptr_f16(int xm, int ym, int nwc, int j);
 const void* gemv_tma_ptr_bf16(int xm, int ym, int nwc, int j);
+const void* moe_down_tma_ptr_f32(int j);
+const void* moe_down_tma_ptr_f16(int j);
+const void* moe_down_tma_ptr_bf16(int j);
 }  // namespace mf

@@ -181,9 +181,17 @@ def moe(args) -> dict:
                                     args.iters, args.warmup), 2)
     res["down_us"] = round(_time(lambda i: ops.moe_down_residual(x, h, wds[i % len(wds)], ids, w, k, d, F),
                                  args.iters, args.warmup), 2)
+    # the whole expert path as the model runs it: router + top-k, grouped gate/up, grouped down
+    def layer(i):
+        ops.router_topk(ids, w, scores, x, nw, 1e-6, wr, d, E, k)
+        ops.moe_swiglu(h, x, nw, 1e-6, wgus[i % len(wgus)], ids, k, F, d)
+        ops.moe_down_residual(x, h, wds[i % len(wds)], ids, w, k, d, F)
+
+    res["layer_us"] = round(_time(layer, args.iters, args.warmup), 2)
     gu_bytes, dn_bytes = k * 2 * F * d * 2, k * d * F * 2
     res.update(op="moe-layer", experts=E, k=k, ff=F, d=d, gate_up_gbs=round(gu_bytes / res["gate_up_us"] / 1e3, 1),
-               down_gbs=round(dn_bytes / res["down_us"] / 1e3, 1), router_bytes=E * d * 4)
+               down_gbs=round(dn_bytes / res["down_us"] / 1e3, 1), router_bytes=E * d * 4,
+               layer_gbs=round((gu_bytes + dn_bytes + E * d * 4) / res["layer_us"] / 1e3, 1))
     return res
 
 

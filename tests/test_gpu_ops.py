@@ -442,9 +442,14 @@ def test_attn_decode_position_out_of_range(ops, gpu):
 
 # ------------------------------------------------------------------ MoE
 
-def test_router_topk_and_experts(ops, orc, gpu):
+@pytest.mark.parametrize("dt,E", [(2, 128), (1, 16), (0, 16)])
+def test_router_topk_and_experts(ops, orc, gpu, dt, E):
+    """Router + top-k, grouped gate/up + SiLU and grouped down + weighted
+    residual at the 30B-A3B layer shape (d 2048, k 8 of E, d_ff 768) in each
+    weight dtype (the TMA-fed grouped kernels)."""
     rng = np.random.default_rng(3)
-    d, E, k, F = 2048, 128, 8, 768
+    d, k, F = 2048, 8, 768
+    name = DT_NAME[dt]
     x = rng.standard_normal(d).astype(np.float32)
     nw = np.ones(d, np.float32)
     wr = (rng.standard_normal(E * d) * 0.02).astype(np.float32)
@@ -460,27 +465,28 @@ def test_router_topk_and_experts(ops, orc, gpu):
     assert ids.cpu().tolist() == rid.tolist()
     np.testing.assert_allclose(wts.cpu().numpy(), rw, rtol=1e-5, atol=1e-6)
     # grouped expert SwiGLU + weighted down projection with residual
-    g = cast_weights(rng.standard_normal(E * F * d).astype(np.float32) * 0.02, "bf16").reshape(E, F, d)
-    u = cast_weights(rng.standard_normal(E * F * d).astype(np.float32) * 0.02, "bf16").reshape(E, F, d)
-    dn = cast_weights(rng.standard_normal(E * d * F).astype(np.float32) * 0.02, "bf16").reshape(E, d, F)
-    gu = np.empty((E, 2 * F, d), np.uint16)
+    g = cast_weights(rng.standard_normal(E * F * d).astype(np.float32) * 0.02, name).reshape(E, F, d)
+    u = cast_weights(rng.standard_normal(E * F * d).astype(np.float32) * 0.02, name).reshape(E, F, d)
+    dn = cast_weights(rng.standard_normal(E * d * F).astype(np.float32) * 0.02, name).reshape(E, d, F)
+    gu = np.empty((E, 2 * F, d), g.dtype)
     gu[:, 0::2] = g
     gu[:, 1::2] = u
+    dev = (lambda a: T(a.view(np.int16), gpu)) if dt else (lambda a: T(a, gpu))
+    gu_d, dn_d = dev(gu), dev(dn)
     h = torch.zeros(k * F, device=gpu)
-    ops.moe_swiglu(h, xt, T(nw, gpu), 1e-6, T(gu.view(np.int16), gpu), ids, k, F, d, dtype="bf16")
+    ops.moe_swiglu(h, xt, T(nw, gpu), 1e-6, gu_d, ids, k, F, d, dtype=name)
     hr = np.zeros((k, F), np.float32)
     for sidx, e in enumerate(rid):
-        gr = orc.matmul(xn, g.ravel(), 2, e * F * d, F, d)
-        ur = orc.matmul(xn, u.ravel(), 2, e * F * d, F, d)
+        gr = orc.matmul(xn, g.ravel(), dt, e * F * d, F, d)
+        ur = orc.matmul(xn, u.ravel(), dt, e * F * d, F, d)
         hr[sidx] = np.array([orc.silu(float(a)) for a in gr], np.float32) * ur
     np.testing.assert_allclose(h.cpu().numpy().reshape(k, F), hr, rtol=3e-5, atol=3e-6)
     res = rng.standard_normal(d).astype(np.float32)
     rt = T(res, gpu)
-    ops.moe_down_residual(rt, T(hr.ravel(), gpu), T(dn.view(np.int16), gpu), ids, T(rw, gpu), k, d, F,
-                          dtype="bf16")
+    ops.moe_down_residual(rt, T(hr.ravel(), gpu), dn_d, ids, T(rw, gpu), k, d, F, dtype=name)
     ref = res.copy()
     for sidx, e in enumerate(rid):
-        o = orc.matmul(hr[sidx], dn.ravel(), 2, e * d * F, d, F)
+        o = orc.matmul(hr[sidx], dn.ravel(), dt, e * d * F, d, F)
         ref = (ref + o * rw[sidx]).astype(np.float32)
     np.testing.assert_allclose(rt.cpu().numpy(), ref, rtol=2e-5, atol=2e-6)
 
