@@ -187,14 +187,18 @@ def time_dominant_kernel(cfg, peaks, iters: int = 20) -> dict:
 
 def prefill_line(cfg, ctx: int, seconds: float, batched: bool, peaks, world: int = 1) -> dict:
     """Prefill tok/s and its tensor roofline. Algorithmic FLOPs of the prompt:
-    2 x linear params x tokens (Q/K/V/O, gate/up/down per layer; the lm_head
-    runs once) + causal attention 4 x L x Hq x D x (sum of context lengths).
-    The hi/lo operand split executes the linear part twice."""
+    2 x linear params each token uses x tokens (Q/K/V/O, gate/up/down per
+    layer: for MoE the router and the k selected experts; the lm_head runs
+    once) + causal attention 4 x L x Hq x D x (sum of context lengths). The
+    hi/lo operand split executes the linear part twice."""
     L, d, Hq, Hkv, D, F = cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.d_head, cfg.d_ff
-    lin = 2.0 * L * (d * (Hq + 2 * Hkv) * D + Hq * D * d + 3 * d * F) * ctx
+    ffn = 3 * d * F * (cfg.n_active if cfg.n_experts else 1) + (d * cfg.n_experts if cfg.n_experts else 0)
+    lin = 2.0 * L * (d * (Hq + 2 * Hkv) * D + Hq * D * d + ffn) * ctx
     att = 4.0 * L * Hq * D * (ctx * (ctx + 1) / 2)
     out = {"tokens": ctx, "seconds": round(seconds, 4), "tok_per_s": round(ctx / seconds, 1),
            "method": ("batched: tcgen05 GEMMs on fp32 activations split into bf16 hi+lo, tcgen05 causal attention"
+                      + ("; MoE: fp32 router, tokens grouped by expert, grouped expert GEMMs" if cfg.n_experts
+                         else "")
                       + (f", tensor-parallel over {world} GPUs (partials exchanged per projection)" if world > 1
                          else "") if batched else "token-by-token decode frames")}
     if batched:
@@ -317,12 +321,14 @@ def llama_bench_main(args) -> None:
 
 
 def measure_long_context(workload: str, ctx: int, steps: int, warmup: int, rank: int, world: int, local_rank: int,
-                         peaks: dict, kv_dtype: str = "f32") -> dict:
-    """Decode of a second workload at a long context, the same way as the main
-    line (batched prefill of a random prompt, chained greedy decode timed with
-    CUDA events, max over ranks): tokens/s and the HBM roofline fraction per
-    GPU, prefill tokens/s, exchange status. kv_dtype "bf16" runs it with the
-    opt-in bf16 KV cache (the reference's cache is fp32)."""
+                         peaks: dict, kv_dtype: str = "f32", parity: bool = False) -> dict:
+    """Decode of a second workload, the same way as the main line (prefill of
+    a random prompt: batched on the tensor cores when the model allows it,
+    else token by token; chained greedy decode timed with CUDA events, max
+    over ranks): tokens/s and the HBM roofline fraction per GPU, prefill
+    tokens/s, exchange status. kv_dtype "bf16" runs it with the opt-in bf16
+    KV cache (the reference's cache is fp32). parity (N > 1): the sharded
+    model's greedy ids against a single-GPU decode on rank 0 (margin rule)."""
     import torch
 
     from minfer_b200 import model as mm
@@ -344,8 +350,10 @@ def measure_long_context(workload: str, ctx: int, steps: int, warmup: int, rank:
     prompt = mm.random_prompt(ctx, info.vocab_size, 30)
     ms = C.c_float()
     check(lib.mf_timer_start(0))
-    if not m.prefill(prompt, 0, True, False):
-        raise RuntimeError("long-context workload needs the batched prefill")
+    batched = m.prefill(prompt, 0, True, False)
+    if not batched:
+        for i, t in enumerate(prompt):
+            m.forward(int(t), i, i == ctx - 1, False)
     check(lib.mf_timer_stop(0, C.byref(ms)))
     prefill_s = ms.value / 1e3
     tok = m.argmax()
@@ -378,6 +386,7 @@ def measure_long_context(workload: str, ctx: int, steps: int, warmup: int, rank:
         dist.all_reduce(t)
         tb = t.item()
     status = int(max_over_ranks(float(m.comm_status())))
+    par = tp_parity(m, path, prompt, info, rank, world, local_rank) if parity and world > 1 else None
     m.close()
     step_gbs = tb / (dev_ms / steps / 1e3) / 1e9 / world
     return {"workload": f"{workload} greedy decode at batch 1 after a {ctx}-token prompt", "context": ctx,
@@ -385,7 +394,9 @@ def measure_long_context(workload: str, ctx: int, steps: int, warmup: int, rank:
             "bytes_per_token": tb, "hbm_roofline": {"achieved_gbs_per_gpu": round(step_gbs, 1),
                                                     "peak_gbs": peaks["hbm_gbs"],
                                                     "frac": round(step_gbs / peaks["hbm_gbs"], 4)},
-            "prefill_tok_per_s": round(ctx / prefill_s, 1), "exchange_status": status,
+            "prefill_tok_per_s": round(ctx / prefill_s, 1),
+            "prefill": "batched (tensor cores)" if batched else "token by token",
+            **({"parity_ok": par["ok"], "parity": par} if par else {}), "exchange_status": status,
             "parallelism": "single" if world == 1 else (f"ep{world}" if info.n_experts > 0 else f"tp{world}"),
             "load_seconds": round(t_load, 1),
             "file_seconds": round(t_gen, 1)}
@@ -457,6 +468,9 @@ def main():
     ap.add_argument("--no-long", action="store_true", help="skip the long-context record")
     ap.add_argument("--no-long-kv-bf16", action="store_true",
                     help="skip the long-context run with the opt-in bf16 KV cache")
+    ap.add_argument("--moe-workload", default="qwen3-30b-a3b-bf16", choices=sorted(CONFIGS))
+    ap.add_argument("--moe-context", type=int, default=1024)
+    ap.add_argument("--no-moe", action="store_true", help="skip the MoE record")
     ap.add_argument("--llama-bench", action="store_true",
                     help="only the reference's benchmark loop (pp512 + tg128, seed 30) on --workload, this runtime "
                          "and the reference CPU build side by side (one GPU)")
@@ -598,7 +612,8 @@ def main():
     step_gbs = tb / (dev_ms / args.steps / 1e3) / 1e9 / world  # per GPU
     status = max(status, m.comm_status())
     # the reference's benchmark loop (pp512 + tg128) on the same model (N=1)
-    lb = llama_bench_record(m, batched) if world == 1 else None
+    # (the reference's pp512 + tg128 loop needs a cache of at least 512 positions)
+    lb = llama_bench_record(m, batched) if world == 1 and ctx + n_tok + 2 >= 512 else None
     if world > 1:
         import torch.distributed as dist
 
@@ -630,6 +645,25 @@ def main():
         else:
             long_rec = {"skipped": f"no room for the {args.long_workload} file under {lp.parent}"}
 
+    # ---- the MoE record (the 30B-A3B shape; expert parallelism at N > 1)
+    moe_rec = None
+    if not args.no_moe and args.moe_workload != args.workload:
+        import shutil
+
+        mp = model_path(args.moe_workload)
+        room = mp.exists() or shutil.disk_usage(mp.parent).free > CONFIGS[args.moe_workload].weight_bytes() * 1.05
+        if world > 1:
+            import torch.distributed as dist
+
+            box = [room]
+            dist.broadcast_object_list(box, src=0)
+            room = box[0]
+        if room:
+            moe_rec = measure_long_context(args.moe_workload, args.moe_context, args.steps, args.warmup, rank, world,
+                                           local_rank, peaks, parity=True)
+        else:
+            moe_rec = {"skipped": f"no room for the {args.moe_workload} file under {mp.parent}"}
+
     if rank == 0:
         cpu = None
         if not args.no_cpu_baseline and world == 1:  # rank 0 at N=1 only (other ranks would compete for cores)
@@ -637,7 +671,8 @@ def main():
                 cpu = run_reference_cpu(path, ctx, args.cpu_steps, 1, host_threads())
             except Exception as e:  # reported, not fatal
                 cpu = {"value": None, "error": str(e)[:200]}
-        launches_per_step = 2 + 5 * info.n_layers if info.n_experts == 0 else 2 + 6 * info.n_layers
+        # embed + lm_head, and per layer QKV, attention, O, gate/up, down (+ router GEMV and top-k for MoE)
+        launches_per_step = 2 + 5 * info.n_layers if info.n_experts == 0 else 2 + 7 * info.n_layers
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True,
@@ -656,6 +691,8 @@ def main():
             line["llama_bench"] = lb
         if long_rec:
             line["long_context"] = long_rec
+        if moe_rec:
+            line["moe"] = moe_rec
         if world > 1:
             line["tp"] = {"size": world, "exchange_status": status,
                           "note": "hbm_roofline.achieved_gbs is per GPU; bytes_per_token summed over ranks"}
@@ -663,7 +700,8 @@ def main():
             line["exchange_status"] = status
             line["parity"] = parity
         print(json.dumps(line), flush=True)
-    failed = world > 1 and not (parity["ok"] and status == 0)
+    moe_bad = bool(moe_rec) and (moe_rec.get("parity_ok") is False or moe_rec.get("exchange_status", 0) != 0)
+    failed = world > 1 and (not (parity["ok"] and status == 0) or moe_bad)
     if world > 1:
         import torch.distributed as dist
 

@@ -353,6 +353,31 @@ int mf_allreduce(float* x_out, const float* x_res, const float* partial, int n, 
 /* C[M, N] = (a_hi + a_lo)[M, K] · w[N, K]^T with w bf16. */
 int mf_prefill_gemm(float* y, int ldy, const void* a_hi, const void* a_lo, const void* w, int M, int N, int K,
                     int mode, void* h_hi, void* h_lo, void* stream);
+/* Grouped form (MoE experts): n_groups problems C_g = A_g · w_g^T, where A_g
+ * is rows [grp_rows[g], grp_rows[g+1]) of a_hi/a_lo [rows_cap][K], w_g the
+ * g-th [N][K] matrix of w, and group g's 128-row tiles are numbered from
+ * grp_tiles[g] (grp_rows / grp_tiles: device arrays of n_groups + 1 entries,
+ * e.g. from mf_prefill_moe_group). C rows keep A's row numbers. */
+int mf_prefill_gemm_grouped(float* y, int ldy, const void* a_hi, const void* a_lo, const void* w, int n_groups,
+                            int rows_cap, int N, int K, const int* grp_rows, const int* grp_tiles, int mode,
+                            void* h_hi, void* h_lo, void* stream);
+/* MoE layer prefill pieces (src/models/qwen3/module.cpp:440-476 for n tokens):
+ * route: fp32 router scores of the normalised rows xn [n_tokens][d_model]
+ *   against w_router [n_experts][d_model] and the reference's top-k + softmax
+ *   per token -> ids / weights [n_tokens][k] (n_experts a multiple of 4, <= 256);
+ * group: counting sort of the n_tokens*k (token, slot) pairs by expert: rows /
+ *   tiles [n_experts + 1] (first grouped row / 128-row tile of each expert) and
+ *   pos [n_tokens*k] (the grouped row of pair t*k + s);
+ * gather: token t's row of xn split into bf16 hi/lo at its k grouped rows;
+ * combine: x[t] += weights[t][s] * y[pos[t*k + s]] for s = 0..k-1 in order. */
+int mf_prefill_moe_route(int* ids, float* weights, const float* xn, const float* w_router, int n_tokens, int d_model,
+                         int n_experts, int k, void* stream);
+int mf_prefill_moe_group(const int* ids, int n_tokens, int k, int n_experts, int* rows, int* tiles, int* pos,
+                         void* stream);
+int mf_prefill_moe_gather(void* a_hi, void* a_lo, const float* xn, const int* pos, int n_tokens, int k, int d_model,
+                          void* stream);
+int mf_prefill_moe_combine(float* x, const float* y, const int* pos, const float* weights, int n_tokens, int k,
+                           int d_model, void* stream);
 /* Row-wise RMSNorm (src/ops/kernels.cpp:351-365) of x [n_rows][d] split into
  * bf16 hi/lo; xn (optional) receives the fp32 normalised rows. */
 int mf_prefill_norm_split(void* hi, void* lo, float* xn, const float* x, const float* norm_w, float eps, int d,

@@ -152,6 +152,10 @@ int mf_model_reset_sampler(mf_model* m);
  * weights), the KV rows [0, n_pos) of `layer` in the reference's
  * [pos][kv_head][d_head] order, and the residual stream x. */
 int mf_model_experts(const mf_model* m, int layer, int* ids, float* weights);
+/* The expert ids / weights ([n_tokens][k] each) the last batched prefill
+ * (mf_model_prefill) chose at `layer` for its first n_tokens tokens (MoE
+ * models; a prefill of several chunks keeps the last chunk's). */
+int mf_model_prefill_experts(const mf_model* m, int layer, int* ids, float* weights, int n_tokens);
 int mf_model_kv(const mf_model* m, int layer, float* k, float* v, int n_pos);
 int mf_model_x(const mf_model* m, float* x);
 

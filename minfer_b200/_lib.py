@@ -146,6 +146,11 @@ CUDA_API = {
     "mf_moe_swiglu_ep": (I, [P, P, P, F, P, I, P, I, I, I, I, I, P]),
     "mf_moe_down_push": (I, [P, P, I, P, P, I, I, I, I, I, P, I, P, P]),
     "mf_prefill_gemm": (I, [P, I, P, P, P, I, I, I, I, P, P, P]),
+    "mf_prefill_gemm_grouped": (I, [P, I, P, P, P, I, I, I, I, P, P, I, P, P, P]),
+    "mf_prefill_moe_route": (I, [P, P, P, P, I, I, I, I, P]),
+    "mf_prefill_moe_group": (I, [P, I, I, I, P, P, P, P]),
+    "mf_prefill_moe_gather": (I, [P, P, P, P, I, I, I, P]),
+    "mf_prefill_moe_combine": (I, [P, P, P, P, I, I, I, P]),
     "mf_prefill_norm_split": (I, [P, P, P, P, P, F, I, I, P]),
     "mf_prefill_split": (I, [P, P, P, SZ, P]),
     "mf_prefill_swiglu_split": (I, [P, P, P, I, I, P]),
@@ -190,6 +195,7 @@ HOST_API = {
     "mf_model_benchmark": (I, [P, I, P]),
     "mf_model_reset_sampler": (I, [P]),
     "mf_model_experts": (I, [P, I, P, P]),
+    "mf_model_prefill_experts": (I, [P, I, P, P, I]),
     "mf_model_kv": (I, [P, I, P, P, I]),
     "mf_model_x": (I, [P, P]),
     "mf_random_prompt": (I, [I, U32, SZ, P]),

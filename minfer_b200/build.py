@@ -31,7 +31,7 @@ CXX_FLAGS = ["-std=c++17", "-O3", "-march=x86-64-v3", "-fPIC", "-Wall", "-Wextra
 
 CUDA_SOURCES = ["capi.cu", "attention.cu", "attn_noalloc.cu", "gemv_f32.cu", "gemv_f16.cu", "gemv_bf16.cu",
                 "gemv_tma_f32.cu", "gemv_tma_f16.cu", "gemv_tma_bf16.cu",
-                "gemv_tp_f32.cu", "gemv_tp_f16.cu", "gemv_tp_bf16.cu", "prefill.cu"]
+                "gemv_tp_f32.cu", "gemv_tp_f16.cu", "gemv_tp_bf16.cu", "prefill.cu", "prefill_moe.cu"]
 HOST_SOURCES = ["gguf.cpp", "sampler.cpp", "model.cpp", "capi_model.cpp"]
 
 LIBMFCUDA = LIB / "libmfcuda.so"

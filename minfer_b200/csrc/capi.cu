@@ -1064,6 +1064,7 @@ int mf_router_topk(int* ids, float* weights, float* scores, const float* x, cons
     MF_REQUIRE(ids && weights && scores && x && norm_w && w_router, MF_E_INVALID, "null argument");
     MF_REQUIRE(n_experts >= 1 && n_experts <= 256, MF_E_UNSUPPORTED, "n_experts %d (1..256)", n_experts);
     MF_REQUIRE(k >= 1 && k <= n_experts && k <= 32, MF_E_INVALID, "k %d", k);
+    MF_REQUIRE(d_model > 0 && d_model % 16 == 0, MF_E_INVALID, "d_model must be a positive multiple of 16");
     cudaStream_t st = resolve(stream);
     mf::GemvParams p = {};
     p.w = w_router;

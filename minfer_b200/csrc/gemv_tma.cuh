@@ -79,22 +79,6 @@ struct GemvTmaParams {
     unsigned long long expert_bytes;
 };
 
-MF_DEVICE uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-MF_DEVICE void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-MF_DEVICE float ld_cluster_f32(const float* local, uint32_t rank) {
-    uint32_t remote;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-    return v;
-}
-
 // Y_PUSH: row `row` of this rank's partial, as a tagged word into every
 // rank's receive slot of exchange ar_seq.
 MF_DEVICE void push_row(const GemvTmaParams& p, int row, float v) {

@@ -257,6 +257,12 @@ int mf_model_experts(const mf_model* m, int layer, int* ids, float* weights) {
     return rc ? herr(rc, "no experts at this layer") : MF_OK;
 }
 
+int mf_model_prefill_experts(const mf_model* m, int layer, int* ids, float* weights, int n_tokens) {
+    if (!m) return herr(MF_E_INVALID, "null model");
+    const int rc = m->m->read_prefill_experts(layer, ids, weights, n_tokens);
+    return rc ? herr(rc, "no prefill routing at this layer") : MF_OK;
+}
+
 int mf_model_kv(const mf_model* m, int layer, float* k, float* v, int n_pos) {
     if (!m) return herr(MF_E_INVALID, "null model");
     const int rc = m->m->read_kv(layer, k, v, n_pos);

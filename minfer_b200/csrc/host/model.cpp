@@ -418,7 +418,10 @@ public:
     // dense FFN for n prompt tokens: pre-norm, gate/up GEMM with the SwiGLU
     // epilogue, down GEMM + residual
     void prefill_forward(RunState& rs, int n, int pos0) override {
-        if (c_.n_experts > 0) throw std::runtime_error("batched prefill covers dense FFN layers");
+        if (c_.n_experts > 0) {
+            moe_prefill(rs, n);
+            return;
+        }
         const int d = c_.d_model, F = c_.ff_local();
         float* X = (float*)mf_ptr(rs.pf_x);
         void *hi = mf_ptr(rs.pf_hi), *lo = mf_ptr(rs.pf_lo), *hhi = mf_ptr(rs.pf_hhi), *hlo = mf_ptr(rs.pf_hlo);
@@ -443,6 +446,43 @@ public:
                          "prefill down projection (partial)");
             prefill_exchange(rs, X, n, d);
         }
+    }
+    // MoE FFN for n prompt tokens (module.cpp:440-476 per token): fp32 router
+    // + top-k per token, tokens grouped by expert, grouped tcgen05 GEMMs
+    // (gate/up with the SwiGLU epilogue, down), then every token adds its
+    // experts' outputs in slot order
+    void moe_prefill(RunState& rs, int n) {
+        const int d = c_.d_model, F = c_.d_ff, E = c_.n_experts, k = c_.n_active_experts;
+        float* X = (float*)mf_ptr(rs.pf_x);
+        float* xn = (float*)mf_ptr(rs.pf_xn);
+        int* ids = (int*)mf_ptr(rs.pf_ids) + (size_t)layer_ * rs.pf_cap * k;
+        float* wts = (float*)mf_ptr(rs.pf_wts) + (size_t)layer_ * rs.pf_cap * k;
+        int* grows = (int*)mf_ptr(rs.pf_grows);
+        int* gtiles = (int*)mf_ptr(rs.pf_gtiles);
+        int* pos = (int*)mf_ptr(rs.pf_pos);
+        check(mf_prefill_norm_split(mf_ptr(rs.pf_hi), mf_ptr(rs.pf_lo), xn, X, (const float*)mf_ptr(fn_),
+                                    c_.rms_norm_eps, d, n, rs.stream),
+              "prefill ffn norm");
+        check(mf_prefill_moe_route(ids, wts, xn, (const float*)mf_ptr(wr_), n, d, E, k, rs.stream), "prefill router");
+        check(mf_prefill_moe_group(ids, n, k, E, grows, gtiles, pos, rs.stream), "prefill expert grouping");
+        check(mf_prefill_moe_gather(mf_ptr(rs.pf_ghi), mf_ptr(rs.pf_glo), xn, pos, n, k, d, rs.stream),
+              "prefill expert operands");
+        check(mf_prefill_gemm_grouped(nullptr, 0, mf_ptr(rs.pf_ghi), mf_ptr(rs.pf_glo), mf_ptr(wgu_), E, n * k, 2 * F,
+                                      d, grows, gtiles, MF_PREFILL_SWIGLU, mf_ptr(rs.pf_mhi), mf_ptr(rs.pf_mlo),
+                                      rs.stream),
+              "prefill expert gate/up");
+        check(mf_prefill_gemm_grouped((float*)mf_ptr(rs.pf_y), d, mf_ptr(rs.pf_mhi), mf_ptr(rs.pf_mlo), mf_ptr(wd_),
+                                      E, n * k, d, F, grows, gtiles, MF_PREFILL_STORE, nullptr, nullptr, rs.stream),
+              "prefill expert down");
+        check(mf_prefill_moe_combine(X, (const float*)mf_ptr(rs.pf_y), pos, wts, n, k, d, rs.stream),
+              "prefill expert combine");
+        // the last prompt token's routing, where the decode step keeps it
+        check(mf_copy(rs.expert_ids, (size_t)layer_ * k * 4, rs.pf_ids,
+                      ((size_t)layer_ * rs.pf_cap + (size_t)(n - 1)) * k * 4, (size_t)k * 4),
+              "prefill expert ids");
+        check(mf_copy(rs.expert_w, (size_t)layer_ * k * 4, rs.pf_wts,
+                      ((size_t)layer_ * rs.pf_cap + (size_t)(n - 1)) * k * 4, (size_t)k * 4),
+              "prefill expert weights");
     }
     void split_for_prefill(int rank) override {
         if (dtype_ != MF_F32 || c_.n_experts > 0 || wgu_s_.hi) return;
@@ -742,7 +782,11 @@ int Qwen3Model::comm_status(int* status) {
 }
 
 bool Qwen3Model::prefill_supported() const {
-    if (device_ != DeviceType::CUDA || cfg_.n_experts != 0) return false;
+    if (device_ != DeviceType::CUDA) return false;
+    // MoE: one GPU, bf16 experts, up to 256 experts (a multiple of 4), k <= 32
+    if (cfg_.n_experts != 0 && (cfg_.tp_size > 1 || cfg_.weight_dtype != DataType::BF16 || cfg_.n_experts % 4 != 0 ||
+                                cfg_.n_experts > 256 || cfg_.n_active_experts > 32))
+        return false;
     if (cfg_.tp_size > 1 && (rs_.pf_bulk_rows <= 0 || !rs_.comm || cfg_.d_model % 4 != 0)) return false;
     // bf16 weights directly; fp32 weights through bf16 hi/lo copies (two products per GEMM)
     if ((cfg_.weight_dtype != DataType::BF16 && cfg_.weight_dtype != DataType::F32) || cfg_.d_head != 128 ||
@@ -756,7 +800,8 @@ void Qwen3Model::alloc_prefill(int rows) {
     if (rs_.pf_cap >= rows) return;
     RunState& rs = rs_;
     for (mf_buf** b : {&rs.pf_x, &rs.pf_hi, &rs.pf_lo, &rs.pf_hhi, &rs.pf_hlo, &rs.pf_qkv, &rs.pf_q, &rs.pf_tok,
-                       &rs.pf_att, &rs.pf_gu}) {
+                       &rs.pf_att, &rs.pf_gu, &rs.pf_xn, &rs.pf_ids, &rs.pf_wts, &rs.pf_grows, &rs.pf_gtiles,
+                       &rs.pf_pos, &rs.pf_ghi, &rs.pf_glo, &rs.pf_mhi, &rs.pf_mlo, &rs.pf_y}) {
         if (*b) {
             state_bufs_.erase(std::find(state_bufs_.begin(), state_bufs_.end(), *b));
             mf_release(*b);
@@ -780,6 +825,20 @@ void Qwen3Model::alloc_prefill(int rows) {
     rs.pf_qkv = alloc(R * (qd + 2ull * c.n_kv_heads * c.d_head) * 4, "prefill qkv");
     rs.pf_q = alloc(R * qd * 4, "prefill queries");
     rs.pf_tok = alloc(R * 4, "prefill token ids");
+    if (c.n_experts > 0) {
+        const size_t k = c.n_active_experts, E = c.n_experts;
+        rs.pf_xn = alloc(R * c.d_model * 4, "prefill normalised rows");
+        rs.pf_ids = alloc((size_t)c.n_layers * R * k * 4, "prefill expert ids");
+        rs.pf_wts = alloc((size_t)c.n_layers * R * k * 4, "prefill expert weights");
+        rs.pf_grows = alloc((E + 1) * 4, "prefill expert rows");
+        rs.pf_gtiles = alloc((E + 1) * 4, "prefill expert tiles");
+        rs.pf_pos = alloc(R * k * 4, "prefill grouped rows");
+        rs.pf_ghi = alloc(R * k * c.d_model * 2, "prefill expert operands hi");
+        rs.pf_glo = alloc(R * k * c.d_model * 2, "prefill expert operands lo");
+        rs.pf_mhi = alloc(R * k * c.d_ff * 2, "prefill expert swiglu hi");
+        rs.pf_mlo = alloc(R * k * c.d_ff * 2, "prefill expert swiglu lo");
+        rs.pf_y = alloc(R * k * c.d_model * 4, "prefill expert outputs");
+    }
     if (c.weight_dtype == DataType::F32) {
         rs.pf_gu = alloc(R * 2ull * c.ff_local() * 4, "prefill gate/up rows");
         for (auto& l : layers_) l->split_for_prefill(rank_);
@@ -1122,6 +1181,15 @@ int Qwen3Model::read_experts(int layer, int* ids, float* w) const {
     const size_t k = cfg_.n_active_experts;
     int rc = mf_read(rs_.expert_ids, (size_t)layer * k * 4, ids, k * 4);
     if (rc == MF_OK && w) rc = mf_read(rs_.expert_w, (size_t)layer * k * 4, w, k * 4);
+    return rc;
+}
+
+int Qwen3Model::read_prefill_experts(int layer, int* ids, float* w, int n) const {
+    if (cfg_.n_experts == 0 || layer < 0 || layer >= cfg_.n_layers || !rs_.pf_ids || n < 0 || n > rs_.pf_cap)
+        return MF_E_INVALID;
+    const size_t k = cfg_.n_active_experts, off = (size_t)layer * rs_.pf_cap * k * 4;
+    int rc = ids ? mf_read(rs_.pf_ids, off, ids, (size_t)n * k * 4) : MF_OK;
+    if (rc == MF_OK && w) rc = mf_read(rs_.pf_wts, off, w, (size_t)n * k * 4);
     return rc;
 }
 

@@ -137,6 +137,15 @@ struct RunState {
     mf_buf *pf_x = nullptr, *pf_hi = nullptr, *pf_lo = nullptr, *pf_hhi = nullptr, *pf_hlo = nullptr;
     mf_buf *pf_qkv = nullptr, *pf_q = nullptr, *pf_tok = nullptr;
     mf_buf* pf_gu = nullptr;  // fp32-weight models: gate/up rows before the SwiGLU [rows][2 d_ff]
+    // MoE layers: normalised rows [rows][d] (fp32, the router's input), per
+    // layer the prompt's expert ids / weights [L][rows][k], the grouping
+    // (expert row and tile offsets [E + 1], grouped row of each (token, slot)
+    // [rows * k]), the grouped operands [rows * k][d] (bf16 hi/lo), the
+    // grouped SwiGLU outputs [rows * k][d_ff] (bf16 hi/lo) and down outputs
+    // [rows * k][d] (fp32)
+    mf_buf *pf_xn = nullptr, *pf_ids = nullptr, *pf_wts = nullptr, *pf_grows = nullptr, *pf_gtiles = nullptr;
+    mf_buf *pf_pos = nullptr, *pf_ghi = nullptr, *pf_glo = nullptr, *pf_mhi = nullptr, *pf_mlo = nullptr;
+    mf_buf* pf_y = nullptr;
     mf_buf* pf_att = nullptr;  // tensor-core attention operands (bf16 hi/lo Q, K, V^T)
     size_t pf_att_bytes = 0;
     bool pf_simt_attn = false;  // MF_PREFILL_SIMT_ATTN=1: the SIMT attention kernel instead
@@ -219,6 +228,9 @@ public:
 
     // Test access
     int read_experts(int layer, int* ids, float* w) const;
+    // the expert ids / weights the last batched prefill chose for its first
+    // n tokens at `layer` ([n][k] each)
+    int read_prefill_experts(int layer, int* ids, float* w, int n) const;
     int read_kv(int layer, float* k, float* v, int n_pos) const;
     int read_x(float* x) const;
     void reset_sampler();

@@ -72,6 +72,27 @@ MF_DEVICE unsigned long long globaltimer_ns() {
 // Programmatic dependent launch: the next kernel in the stream may start its
 // weight prefetch while this one drains; `wait` blocks until every
 // prerequisite grid has completed and flushed its writes.
+// Thread-block clusters: this CTA's rank, a full-cluster barrier (every
+// thread of every CTA arrives), and a float read from a peer CTA's shared
+// memory at the address `local` has in this CTA.
+MF_DEVICE uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+MF_DEVICE void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+MF_DEVICE float ld_cluster_f32(const float* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                 : "=r"(remote)
+                 : "r"((uint32_t)__cvta_generic_to_shared(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
 MF_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 MF_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

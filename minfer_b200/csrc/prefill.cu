@@ -245,6 +245,54 @@ int mf_prefill_gemm(float* y, int ldy, const void* a_hi, const void* a_lo, const
     return e == cudaSuccess ? MF_OK : fail(MF_E_CUDA, cudaGetErrorString(e));
 }
 
+int mf_prefill_gemm_grouped(float* y, int ldy, const void* a_hi, const void* a_lo, const void* w, int n_groups,
+                            int rows_cap, int N, int K, const int* grp_rows, const int* grp_tiles, int mode, void* h_hi,
+                            void* h_lo, void* stream) {
+    if (!a_hi || !a_lo || !w || !grp_rows || !grp_tiles || n_groups <= 0 || rows_cap <= 0 || N <= 0 || K <= 0)
+        return fail(MF_E_INVALID, "bad grouped GEMM arguments");
+    if (K % 8 != 0) return fail(MF_E_INVALID, "K must be a multiple of 8");
+    if ((long long)n_groups * N > (1ll << 31) - 1) return fail(MF_E_INVALID, "n_groups * N too large");
+    if (mode == mf::PG_SWIGLU_SPLIT) {
+        if (!h_hi || !h_lo || N % 2 != 0) return fail(MF_E_INVALID, "SwiGLU mode needs hi/lo outputs and even N");
+    } else if (mode == mf::PG_STORE || mode == mf::PG_RESID) {
+        if (!y || ldy < N || ((uintptr_t)y & 15) != 0 || ldy % 4 != 0)
+            return fail(MF_E_INVALID, "output must be 16-byte aligned with ldy >= N, ldy % 4 == 0");
+    } else {
+        return fail(MF_E_INVALID, "unknown GEMM mode");
+    }
+    int* status = status_ptr();
+    if (!status) return fail(MF_E_CUDA, "prefill status symbol");
+    CUtensorMap ta_hi, ta_lo, tw;
+    int rc = make_tmap(&ta_hi, a_hi, (uint64_t)rows_cap, (uint64_t)K, mf::PG_BM);
+    if (!rc) rc = make_tmap(&ta_lo, a_lo, (uint64_t)rows_cap, (uint64_t)K, mf::PG_BM);
+    if (!rc) rc = make_tmap(&tw, w, (uint64_t)n_groups * (uint64_t)N, (uint64_t)K, mf::PG_BN);
+    if (rc) return rc;
+    mf::PgParams p = {};
+    p.M = rows_cap;
+    p.N = N;
+    p.K = K;
+    p.grp_rows = grp_rows;
+    p.grp_tiles = grp_tiles;
+    p.n_groups = n_groups;
+    p.y = y;
+    p.ldy = ldy;
+    p.h_hi = (__nv_bfloat16*)h_hi;
+    p.h_lo = (__nv_bfloat16*)h_lo;
+    p.status = status;
+    p.timeout_ns = timeout_ns();
+    const void* fn = mode == mf::PG_STORE  ? (const void*)&mf::prefill_gemm_kernel<mf::PG_STORE>
+                     : mode == mf::PG_RESID ? (const void*)&mf::prefill_gemm_kernel<mf::PG_RESID>
+                                            : (const void*)&mf::prefill_gemm_kernel<mf::PG_SWIGLU_SPLIT>;
+    rc = set_smem(fn, mf::PG_SMEM_BYTES);
+    if (rc) return rc;
+    void* args[] = {&ta_hi, &ta_lo, &tw, &p};
+    // every group's tiles fit in ceil(rows / BM) + n_groups CTA rows; the
+    // CTAs past the last tile leave at once
+    const dim3 grid((N + mf::PG_BN - 1) / mf::PG_BN, (rows_cap + mf::PG_BM - 1) / mf::PG_BM + n_groups);
+    cudaError_t e = launch(fn, grid, dim3(mf::PG_THREADS), mf::PG_SMEM_BYTES, mf::resolve_stream(stream), args);
+    return e == cudaSuccess ? MF_OK : fail(MF_E_CUDA, cudaGetErrorString(e));
+}
+
 int mf_prefill_norm_split(void* hi, void* lo, float* xn, const float* x, const float* norm_w, float eps, int d,
                           int n_rows, void* stream) {
     if (!hi || !lo || !x || !norm_w || d <= 0 || n_rows <= 0) return fail(MF_E_INVALID, "bad arguments");

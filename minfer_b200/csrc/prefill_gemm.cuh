@@ -51,6 +51,15 @@ enum PgMode { PG_STORE = 0, PG_RESID = 1, PG_SWIGLU_SPLIT = 2 };
 
 struct PgParams {
     int M, N, K;
+    // grouped mode (MoE experts; grp_rows == nullptr: one plain GEMM): A holds
+    // the rows of every group back to back, group g at rows [grp_rows[g],
+    // grp_rows[g + 1]); W holds n_groups matrices of N rows each. CTA row
+    // blockIdx.y is tile blockIdx.y - grp_tiles[g] of the group g with
+    // grp_tiles[g] <= blockIdx.y < grp_tiles[g + 1] (the tables come from the
+    // previous kernel); rows past the group's end are computed but not stored.
+    const int* grp_rows;   // [n_groups + 1]
+    const int* grp_tiles;  // [n_groups + 1]
+    int n_groups;
     float* y;              // PG_STORE: y[m*ldy + n] = C; PG_RESID: y[m*ldy + n] += C
     int ldy;
     __nv_bfloat16* h_hi;   // PG_SWIGLU_SPLIT: h = silu(C[:, 2i]) * C[:, 2i+1] as hi/lo [M][N/2]
@@ -134,7 +143,23 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     __shared__ uint32_t tmem_base_s;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * PG_BN, m0 = blockIdx.y * PG_BM;
+    const int n0 = blockIdx.x * PG_BN;
+    int m0 = blockIdx.y * PG_BM, m_end = p.M, w_row0 = n0;
+    if (p.grp_rows) {
+        // the group tables are the previous kernel's output
+        pdl_wait();
+        const int y = blockIdx.y;
+        if (y >= __ldcg(p.grp_tiles + p.n_groups)) return;  // past the last tile: the whole CTA leaves
+        int lo = 0, hi = p.n_groups - 1;  // the group g with grp_tiles[g] <= y < grp_tiles[g + 1]
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (__ldcg(p.grp_tiles + mid) <= y) lo = mid;
+            else hi = mid - 1;
+        }
+        m0 = __ldcg(p.grp_rows + lo) + (y - __ldcg(p.grp_tiles + lo)) * PG_BM;
+        m_end = __ldcg(p.grp_rows + lo + 1);
+        w_row0 = lo * p.N + n0;
+    }
     const int KB = (p.K + PG_BK - 1) / PG_BK;
 
     if (threadIdx.x == 0) {
@@ -173,7 +198,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
                 mbar_expect_tx(&full_bar[s], PG_STAGE_BYTES);
                 tma_load_2d(st, &tm_ahi, &full_bar[s], kb * PG_BK, m0);
                 tma_load_2d(st + PG_A_BYTES, &tm_alo, &full_bar[s], kb * PG_BK, m0);
-                tma_load_2d(st + 2 * PG_A_BYTES, &tm_w, &full_bar[s], kb * PG_BK, n0);
+                tma_load_2d(st + 2 * PG_A_BYTES, &tm_w, &full_bar[s], kb * PG_BK, w_row0);
                 issued = kb + 1;
             }
             if (failed) {
@@ -215,7 +240,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
             uint32_t r[32];
             tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
             const int col = n0 + c0;
-            if (failed || row >= p.M || col >= p.N) continue;
+            if (failed || row >= m_end || col >= p.N) continue;
             const bool full = col + 32 <= p.N;
             if (MODE == PG_SWIGLU_SPLIT) {
                 // columns 2i / 2i+1 are gate_i / up_i (src/models/qwen3/module.cpp:466-468)

@@ -201,6 +201,14 @@ class Qwen3Model:
         check(self._lib.mf_model_experts(self._h, layer, ids.ctypes.data, w.ctypes.data))
         return ids, w
 
+    def prefill_experts(self, layer: int, n_tokens: int):
+        """Expert ids / weights ([n_tokens][k]) the last batched prefill chose at `layer`."""
+        k = self.info.n_active_experts
+        ids = np.zeros((n_tokens, k), dtype=np.int32)
+        w = np.zeros((n_tokens, k), dtype=np.float32)
+        check(self._lib.mf_model_prefill_experts(self._h, layer, ids.ctypes.data, w.ctypes.data, n_tokens))
+        return ids, w
+
     def kv(self, layer: int, n_pos: int):
         # tensor parallelism splits the KV heads; expert parallelism (MoE) keeps them all
         kvh = self.info.n_kv_heads if self.info.n_experts > 0 else self.info.n_kv_heads // self.info.tp_size

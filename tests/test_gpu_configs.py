@@ -154,3 +154,31 @@ def test_moe_expert_ids_at_workload_shape(mm):
     print(f"c3: {P + G} forwards x {L} layers of expert ids identical; logit max-abs {worst:.3g}")
     m.close()
     m2.close()
+
+
+def test_moe_batched_prefill_at_workload_shape(mm):
+    """c3 through the batched MoE prefill (fp32 router + top-k per token,
+    grouped tcgen05 expert GEMMs): the 8 expert ids of every prompt token at
+    every layer are the reference's, bit-exact; the logits after the prompt
+    match the reference's sample."""
+    g, path = load_case("c3")
+    P = len(g["prompt"])
+    m = mm.Qwen3Model(path, mm.RunParams(max_seq_len=P + 1)).set_device("cuda")
+    assert m.prefill(np.array(g["prompt"], np.uint32), 0, True, True)
+    mism = []
+    for layer in range(g["layers"]):
+        ids, _ = m.prefill_experts(layer, P)
+        for f in range(P):
+            if list(ids[f]) != g["experts"][f][layer]:
+                mism.append((f, layer, list(ids[f]), g["experts"][f][layer]))
+    assert not mism, f"expert ids differ: {mism[:4]}"
+    lg = m.logits()
+    worst = 0.0
+    for smp in g["logit_samples"]:
+        if smp["step"] == 0:  # the logits of the last prompt token
+            worst = float(np.abs(lg[np.array(smp["idx"])] - np.array(smp["val"], np.float32)).max())
+            assert worst <= logit_tol(g["dtype"]), f"c3 prefill logits differ by {worst}"
+    print(f"c3 batched prefill: {P} tokens x {g['layers']} layers of expert ids identical; logits after the prompt "
+          f"max-abs {worst}")
+    m.close()
+

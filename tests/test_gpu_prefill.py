@@ -97,6 +97,109 @@ def test_prefill_gemm_swiglu(lib, gpu, M, F, K):
     assert status_ok(lib)
 
 
+@pytest.mark.parametrize("counts,N,K", [([0, 130, 5, 0, 256, 1], 512, 256), ([300, 0, 77], 1536, 2048),
+                                        ([1, 1, 1, 1], 2048, 768)])
+def test_prefill_gemm_grouped(lib, gpu, counts, N, K):
+    """Grouped tcgen05 GEMM (MoE experts): groups of any size (empty, 1 row,
+    partial and several 128-row tiles) against float64, per group; the rows
+    of one group never see another group's weights."""
+    from minfer_b200._lib import MF_PREFILL_STORE, MF_PREFILL_SWIGLU, check
+
+    G = len(counts)
+    rows = int(sum(counts))
+    g = torch.Generator(device=gpu).manual_seed(rows + N)
+    a = torch.randn(rows, K, generator=g, device=gpu)
+    w = (torch.randn(G * N, K, generator=g, device=gpu) * 0.03).to(torch.bfloat16)
+    hi, lo = split(a)
+    off = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    tiles = np.concatenate([[0], np.cumsum([(c + 127) // 128 for c in counts])]).astype(np.int32)
+    grows, gtiles = torch.from_numpy(off).to(gpu), torch.from_numpy(tiles).to(gpu)
+    ref = torch.zeros(rows, N, dtype=torch.float64, device=gpu)
+    for e in range(G):
+        r0, r1 = off[e], off[e + 1]
+        if r1 > r0:
+            ref[r0:r1] = (hi[r0:r1].double() + lo[r0:r1].double()) @ w[e * N:(e + 1) * N].double().t()
+    y = torch.full((rows, N), 7.0, device=gpu)
+    check(lib.mf_prefill_gemm_grouped(P(y), N, P(hi), P(lo), P(w), G, rows, N, K, P(grows), P(gtiles),
+                                      MF_PREFILL_STORE, None, None, stream()))
+    torch.cuda.synchronize()
+    assert status_ok(lib)
+    scale = ref.abs().max().item()
+    assert (y.double() - ref).abs().max().item() <= 2e-5 * scale
+    # SwiGLU epilogue on interleaved gate/up columns
+    gate, up = ref[:, 0::2], ref[:, 1::2]
+    sw = gate / (1 + torch.exp(-gate)) * up
+    h_hi = torch.zeros(rows, N // 2, dtype=torch.bfloat16, device=gpu)
+    h_lo = torch.zeros_like(h_hi)
+    check(lib.mf_prefill_gemm_grouped(None, 0, P(hi), P(lo), P(w), G, rows, N, K, P(grows), P(gtiles),
+                                      MF_PREFILL_SWIGLU, P(h_hi), P(h_lo), stream()))
+    torch.cuda.synchronize()
+    assert status_ok(lib)
+    assert ((h_hi.double() + h_lo.double()) - sw).abs().max().item() <= 3e-5 * sw.abs().max().item()
+
+
+def test_prefill_moe_route_group_gather_combine(lib, gpu):
+    """MoE prefill pieces at the 30B-A3B layer shape (d 2048, 128 experts,
+    k 8) for 300 tokens: the router's ids / weights per token against the
+    oracle's route; the grouping is a permutation consistent with the ids;
+    the gathered operands are each token's row; the combine adds the slots in
+    order."""
+    from minfer_b200._lib import check
+    from oracle.oracle_py import PortOps
+
+    orc_ops = PortOps()
+    n, d, E, k = 300, 2048, 128, 8
+    rng = np.random.default_rng(17)
+    xn = rng.standard_normal((n, d)).astype(np.float32)
+    wr = (rng.standard_normal((E, d)) * 0.02).astype(np.float32)
+    xt, wt = torch.from_numpy(xn).to(gpu), torch.from_numpy(wr).to(gpu)
+    ids = torch.zeros(n, k, dtype=torch.int32, device=gpu)
+    wts = torch.zeros(n, k, device=gpu)
+    check(lib.mf_prefill_moe_route(P(ids), P(wts), P(xt), P(wt), n, d, E, k, stream()))
+    torch.cuda.synchronize()
+    ids_c, wts_c = ids.cpu().numpy(), wts.cpu().numpy()
+    near = 0
+    for t in range(n):
+        rid, rw, rs = orc_ops.route(xn[t], wr.ravel(), E, k)
+        srt = np.sort(rs)[::-1]
+        if srt[k - 1] - srt[k] < 1e-4:  # a near tie at the k-th place may order either way
+            near += 1
+            continue
+        assert ids_c[t].tolist() == rid.tolist(), f"token {t}"
+        np.testing.assert_allclose(wts_c[t], rw, rtol=1e-5, atol=1e-6)
+    assert near < n // 10
+    rows = torch.zeros(E + 1, dtype=torch.int32, device=gpu)
+    tiles = torch.zeros(E + 1, dtype=torch.int32, device=gpu)
+    pos = torch.full((n * k,), -1, dtype=torch.int32, device=gpu)
+    check(lib.mf_prefill_moe_group(P(ids), n, k, E, P(rows), P(tiles), P(pos), stream()))
+    torch.cuda.synchronize()
+    r, tl, ps = rows.cpu().numpy(), tiles.cpu().numpy(), pos.cpu().numpy()
+    cnt = np.bincount(ids_c.ravel(), minlength=E)
+    assert r[0] == 0 and r[E] == n * k and np.array_equal(np.diff(r), cnt)
+    assert np.array_equal(np.diff(tl), (cnt + 127) // 128)
+    assert sorted(ps.tolist()) == list(range(n * k))
+    for i, p_ in enumerate(ps):  # each pair lies in its expert's rows
+        e = ids_c.ravel()[i]
+        assert r[e] <= p_ < r[e + 1]
+    ahi = torch.zeros(n * k, d, dtype=torch.bfloat16, device=gpu)
+    alo = torch.zeros_like(ahi)
+    check(lib.mf_prefill_moe_gather(P(ahi), P(alo), P(xt), P(pos), n, k, d, stream()))
+    torch.cuda.synchronize()
+    hi, lo = split(xt)
+    for s_ in range(k):
+        rr = pos.view(n, k)[:, s_].long()
+        assert torch.equal(ahi[rr], hi) and torch.equal(alo[rr], lo)
+    y = torch.randn(n * k, d, device=gpu)
+    x0 = torch.randn(n, d, device=gpu)
+    x = x0.clone()
+    check(lib.mf_prefill_moe_combine(P(x), P(y), P(pos), P(wts), n, k, d, stream()))
+    torch.cuda.synchronize()
+    ref = x0.clone()
+    for s_ in range(k):
+        ref = torch.addcmul(ref, y[pos.view(n, k)[:, s_].long()], wts[:, s_:s_ + 1])
+    assert (x - ref).abs().max().item() <= 1e-5
+
+
 def test_prefill_norm_split(lib, gpu):
     from minfer_b200._lib import check
 
@@ -287,6 +390,50 @@ def test_model_prefill_vs_oracle(gpu, monkeypatch, name, chunk, simt):
         # rows of layers >= 1 carry the attention error of the layers below (<= 5e-5, tensor-core kernel)
         np.testing.assert_allclose(k, ko, rtol=1e-4, atol=5e-5)
         np.testing.assert_allclose(v, vo, rtol=1e-4, atol=5e-5)
+
+
+@pytest.mark.parametrize("chunk", [None, 16])
+def test_model_prefill_moe_vs_oracle(gpu, monkeypatch, chunk):
+    """Batched MoE prefill (fp32 router + top-k per token, grouped tcgen05
+    expert GEMMs, slot-ordered combine) of a 40-token prompt against the
+    oracle's token-by-token prefill: every token's expert ids at every layer,
+    every KV row, the last token's logits and greedy id."""
+    from conftest import TINY, tiny_model
+    from minfer_b200.model import Qwen3Model, RunParams, random_prompt
+    from oracle.oracle_py import PortModel
+
+    if chunk:
+        monkeypatch.setenv("MF_PREFILL_CHUNK", str(chunk))
+    name = "tiny-moe"
+    cfg = TINY[name]
+    path = tiny_model(name)
+    Pn = 40
+    prompt = random_prompt(Pn, cfg.vocab, 23)
+    m = Qwen3Model(path, RunParams(max_seq_len=Pn + 8)).set_device("cuda")
+    assert m.prefill(prompt, 0, True, True)
+    orc = PortModel(path, max_seq=Pn + 8)
+    orc.record_experts(True)
+    for i, t in enumerate(prompt):
+        orc.forward(int(t), i, i == Pn - 1)
+    ref_ids, _ = orc.recorded_experts(cfg.n_active)  # [Pn * L][k], token-major
+    ref_ids = ref_ids.reshape(Pn, cfg.n_layers, cfg.n_active)
+    last = Pn - (Pn // chunk) * chunk if chunk and Pn % chunk else (chunk or Pn)
+    first = Pn - last  # the readback holds the last chunk's tokens
+    for layer in range(cfg.n_layers):
+        ids, _ = m.prefill_experts(layer, last)
+        assert np.array_equal(ids, ref_ids[first:, layer]), f"layer {layer}"
+        e, _ = m.experts(layer)
+        assert list(e) == list(ref_ids[Pn - 1, layer])
+    lo, lg = orc.logits(), m.logits()
+    assert np.max(np.abs(lo - lg)) <= 2e-3, np.max(np.abs(lo - lg))
+    assert m.argmax() == int(np.argmax(lg))
+    kvd = cfg.n_kv_heads * cfg.d_head
+    for layer in range(cfg.n_layers):
+        k, v = m.kv(layer, Pn)
+        ko, vo = orc.kv(layer, Pn, kvd)
+        np.testing.assert_allclose(k, ko, rtol=1e-4, atol=5e-5)
+        np.testing.assert_allclose(v, vo, rtol=1e-4, atol=5e-5)
+    m.close()
 
 
 @pytest.mark.parametrize("Pn", [512, 4096])
