@@ -226,6 +226,14 @@ int mf_moe_swiglu(float* h, const float* x, const float* norm_w, float eps, cons
  * x[j] += sum over slots s in order of w_s * (W_down[ids[s]] · h_s)[j]. */
 int mf_moe_down_residual(float* x, const float* h, const void* w_down_exps, int dtype, const int* ids,
                          const float* weights, int k, int d_model, int d_ff, void* stream);
+/* The whole MoE FFN of one token (module.cpp:440-476): router + top-k
+ * (scores, ids, weights: scratch outputs [n_experts], [k], [k]), the selected
+ * experts' SwiGLU into h [k][d_ff], and the weighted down projection added to
+ * x. Same results as the three calls above; launched as one chain, the down
+ * projection's weight copies start while the gate/up kernel still runs. */
+int mf_moe_ffn(float* x, float* h, const float* norm_w, float eps, const float* w_router, const void* w_gate_up_exps,
+               const void* w_down_exps, int dtype, float* scores, int* ids, float* weights, int d_model, int d_ff,
+               int n_experts, int k, void* stream);
 
 /* Final RMSNorm + lm_head (module.cpp:54-79,113-126): logits = W · rmsnorm(x).
  * When step_state (a device step record) is non-NULL the greedy id (first

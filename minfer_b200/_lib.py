@@ -127,6 +127,7 @@ CUDA_API = {
     "mf_router_topk": (I, [P, P, P, P, P, F, P, I, I, I, P]),
     "mf_moe_swiglu": (I, [P, P, P, F, P, I, P, I, I, I, P]),
     "mf_moe_down_residual": (I, [P, P, P, I, P, P, I, I, I, P]),
+    "mf_moe_ffn": (I, [P, P, P, F, P, P, P, I, P, P, P, I, I, I, I, P]),
     "mf_lm_head_workspace_bytes": (SZ, []),
     "mf_lm_head": (I, [P, P, P, F, P, I, I, I, I, P, P, P]),
     "mf_comm_create": (I, [I, I, I, I, I, P]),

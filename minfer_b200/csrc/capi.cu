@@ -408,7 +408,7 @@ int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_
 // The TMA-fed grouped expert down projection (moe_down_tma_kernel): 1 when it
 // launched, 0 when left to the register-fed kernel (MF_GEMV_TMA_MOE=0, expert
 // parallelism, rows wider than 10 KB or K beyond 8 vectors per lane), < 0 on error.
-int try_moe_down_tma(int dtype, const mf::GemvParams& q, cudaStream_t st) {
+int try_moe_down_tma(int dtype, const mf::GemvParams& q, cudaStream_t st, bool ids_early) {
     static const int on = env_int("MF_GEMV_TMA", 1) && env_int("MF_GEMV_TMA_MOE", 1);
     static const long long timeout_ms = env_int("MF_DECODE_TIMEOUT_MS", 1000);
     static const size_t stage_target = (size_t)env_int("MF_MOE_TMA_STAGE_KB", 16) * 1024;
@@ -461,6 +461,7 @@ int try_moe_down_tma(int dtype, const mf::GemvParams& q, cudaStream_t st) {
     p.stage_bytes = (uint32_t)stage_bytes;
     p.status = status;
     p.timeout_ns = (unsigned long long)std::max(1ll, timeout_ms) * 1000000ull;
+    p.ids_early = ids_early ? 1 : 0;
     void* args[] = {&p};
     MF_CK(launch(fn, dim3((unsigned)nblk), dim3((mf::MD_WARPS + 1) * 32), smem, st, args));
     return 1;
@@ -1117,10 +1118,58 @@ int mf_moe_down_residual(float* x, const float* h, const void* w_down_exps, int 
     MF_REQUIRE(d_ff > 0 && d_ff % 16 == 0 && d_model > 0, MF_E_INVALID, "bad d_ff/d_model");
     MF_REQUIRE(((uintptr_t)w_down_exps) % 16 == 0 && ((uintptr_t)h) % 16 == 0, MF_E_INVALID,
                "weights and h must be 16-byte aligned");
-    const int tr = try_moe_down_tma(dtype, p, resolve(stream));
+    const int tr = try_moe_down_tma(dtype, p, resolve(stream), false);
     if (tr < 0) return tr;
     if (tr == 1) return MF_OK;
     return run_gemv(dtype, mf::X_PLAIN, mf::Y_MOE_DOWN, p, d_model, resolve(stream));
+}
+
+int mf_moe_ffn(float* x, float* h, const float* norm_w, float eps, const float* w_router, const void* w_gate_up_exps,
+               const void* w_down_exps, int dtype, float* scores, int* ids, float* weights, int d_model, int d_ff,
+               int n_experts, int k, void* stream) {
+    MF_REQUIRE(x && h && norm_w && w_router && w_gate_up_exps && w_down_exps && scores && ids && weights, MF_E_INVALID,
+               "null argument");
+    MF_REQUIRE(valid_dtype(dtype), MF_E_INVALID, "bad dtype %d", dtype);
+    MF_REQUIRE(k >= 1 && k <= 8 && d_ff > 0 && d_ff % 16 == 0 && d_model > 0 && d_model % 16 == 0, MF_E_INVALID,
+               "bad k/d_ff/d_model (k 1..8, sizes multiples of 16)");
+    MF_REQUIRE(((uintptr_t)w_gate_up_exps | (uintptr_t)w_down_exps | (uintptr_t)x | (uintptr_t)h) % 16 == 0,
+               MF_E_INVALID, "operands must be 16-byte aligned");
+    cudaStream_t st = resolve(stream);
+    int rc = mf_router_topk(ids, weights, scores, x, norm_w, eps, w_router, d_model, n_experts, k, st);
+    if (rc) return rc;
+    mf::GemvParams g = {};
+    g.w = w_gate_up_exps;
+    g.x = x;
+    g.nw = norm_w;
+    g.eps = eps;
+    g.y = h;
+    g.rows = 2 * d_ff * k;
+    g.K = d_model;
+    g.expert_ids = ids;
+    g.rows_per_expert = 2 * d_ff;
+    // the down projection may read the ids before its dependency wait only
+    // behind the grouped TMA gate/up kernel (which waits for the router
+    // before letting it launch)
+    const int tg = try_gemv_tma(dtype, mf::X_NORM, mf::Y_SWIGLU, g, st);
+    if (tg < 0) return tg;
+    if (tg == 0) {
+        rc = run_gemv(dtype, mf::X_NORM, mf::Y_SWIGLU, g, (long long)d_ff * k, st);
+        if (rc) return rc;
+    }
+    mf::GemvParams q = {};
+    q.w = w_down_exps;
+    q.x = h;
+    q.y = x;
+    q.rows = d_model;
+    q.K = d_ff;
+    q.expert_ids = ids;
+    q.expert_w = weights;
+    q.rows_per_expert = d_model;
+    q.n_slots = k;
+    const int td = try_moe_down_tma(dtype, q, st, tg == 1);
+    if (td < 0) return td;
+    if (td == 1) return MF_OK;
+    return run_gemv(dtype, mf::X_PLAIN, mf::Y_MOE_DOWN, q, d_model, st);
 }
 
 size_t mf_lm_head_workspace_bytes(void) { return 256 + (size_t)LMH_MAX_GRID * (sizeof(float) + sizeof(int)); }

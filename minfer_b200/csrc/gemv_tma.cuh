@@ -127,12 +127,15 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
         // ---- producer: weights do not depend on earlier kernels, so the ring
         // fills before the dependency wait. The next kernel may launch at once
         // (its CTAs fit beside this one and fill their own rings meanwhile).
+        const bool grouped = p.expert_ids != nullptr;
+        // grouped: the expert ids are the router's output, so this kernel lets
+        // its dependents launch only after its own dependency wait (every
+        // thread waits first): a kernel launched after it may then read the
+        // ids before its own wait
+        if (grouped) pdl_wait();
         pdl_launch_dependents();
         if (lane == 0) {
-            const bool grouped = p.expert_ids != nullptr;
             if (grouped) {
-                // the expert ids are the router kernel's output (read from L2)
-                pdl_wait();
                 const int n_ids = p.rows / p.rows_per_expert;
                 for (int i = 0; i < n_ids && i < 32; ++i) eid_s[i] = __ldcg(p.expert_ids + i);
             }
@@ -188,8 +191,13 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
     const int NV = p.K / VEC;
     const int v0 = warp * NV / NWC, v1 = (warp + 1) * NV / NWC;
     float xr[J][VEC];
-    pdl_launch_dependents();
-    pdl_wait();
+    if (p.expert_ids) {
+        pdl_wait();
+        pdl_launch_dependents();
+    } else {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
     if (XM == X_AR_NORM) {
         // all-reduce receive: each CTA sums its slice of x = residual +
         // partial_0 + ... (rank order) into x_out as the tagged words arrive;
@@ -384,6 +392,11 @@ struct MoeDownTmaParams {
     uint32_t stage_bytes;              // k * rows_per_stage * row_bytes
     int* status;
     unsigned long long timeout_ns;
+    // 1: the ids are read before the dependency wait, so the weight copies
+    // overlap the previous kernel. Only for a previous kernel that let its
+    // dependents launch after it had waited for the router (the grouped
+    // gate/up GEMV does), so the router's ids are complete here.
+    int ids_early;
 };
 
 constexpr int MD_WARPS = 8;  // consumer warps = the most slots
@@ -417,8 +430,8 @@ __global__ void __launch_bounds__((MD_WARPS + 1) * 32, 1) moe_down_tma_kernel(co
     if (warp == MD_WARPS) {
         pdl_launch_dependents();
         if (lane == 0) {
-            pdl_wait();
-            for (int i = 0; i < p.k; ++i) eid_s[i] = __ldcg(p.ids + i);
+            if (!p.ids_early) pdl_wait();
+            for (int i = 0; i < p.k; ++i) eid_s[i] = __ldcg(p.ids + i);  // from L2: written by the router
             bool failed = false;
             int c = 0;
             for (; c < nchunks; ++c) {

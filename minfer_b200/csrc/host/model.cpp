@@ -406,13 +406,9 @@ public:
                   "expert down (all-reduce send)");
             return;
         }
-        check(mf_router_topk(ids, w, (float*)mf_ptr(rs.scores), x, (const float*)mf_ptr(fn_), c_.rms_norm_eps,
-                             (const float*)mf_ptr(wr_), d, c_.n_experts, k, rs.stream),
-              "router");
-        check(mf_moe_swiglu(h, x, (const float*)mf_ptr(fn_), c_.rms_norm_eps, mf_ptr(wgu_), dtype_, ids, k, F, d,
-                            rs.stream),
-              "expert gate/up");
-        check(mf_moe_down_residual(x, h, mf_ptr(wd_), dtype_, ids, w, k, d, F, rs.stream), "expert down");
+        check(mf_moe_ffn(x, h, (const float*)mf_ptr(fn_), c_.rms_norm_eps, (const float*)mf_ptr(wr_), mf_ptr(wgu_),
+                         mf_ptr(wd_), dtype_, (float*)mf_ptr(rs.scores), ids, w, d, F, c_.n_experts, k, rs.stream),
+              "router + experts");
     }
 
     // dense FFN for n prompt tokens: pre-norm, gate/up GEMM with the SwiGLU

@@ -156,6 +156,14 @@ def moe_down_residual(x, h, w_down_exps, ids, weights, k: int, d_model: int, d_f
                                     _ptr(weights), k, d_model, d_ff, _stream()))
 
 
+def moe_ffn(x, h, norm_w, eps: float, w_router, w_gate_up_exps, w_down_exps, scores, ids, weights, d_model: int,
+            d_ff: int, n_experts: int, k: int, dtype: str | None = None):
+    """router_topk + moe_swiglu + moe_down_residual as one launch chain."""
+    check(_lib.mf_moe_ffn(_ptr(x), _ptr(h), _ptr(norm_w), eps, _ptr(w_router), _ptr(w_gate_up_exps),
+                          _ptr(w_down_exps), dtype_code(w_gate_up_exps, dtype), _ptr(scores), _ptr(ids), _ptr(weights),
+                          d_model, d_ff, n_experts, k, _stream()))
+
+
 def lm_head_workspace_bytes() -> int:
     return int(_lib.mf_lm_head_workspace_bytes())
 

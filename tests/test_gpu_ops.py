@@ -489,6 +489,21 @@ def test_router_topk_and_experts(ops, orc, gpu, dt, E):
         o = orc.matmul(hr[sidx], dn.ravel(), dt, e * d * F, d, F)
         ref = (ref + o * rw[sidx]).astype(np.float32)
     np.testing.assert_allclose(rt.cpu().numpy(), ref, rtol=2e-5, atol=2e-6)
+    # the same FFN as one launch chain (the down projection's copies start
+    # during the gate/up kernel): identical results to the separate calls.
+    # Inputs alternate between chains, so a down kernel that read the previous
+    # chain's expert ids would give a different residual.
+    nwt, wrt = T(nw, gpu), T(wr, gpu)
+    inputs = [rng.standard_normal(d).astype(np.float32) for _ in range(4)]
+    ids_ch, wts_ch, h_ch = torch.zeros_like(ids), torch.zeros_like(wts), torch.zeros(k * F, device=gpu)
+    for xi in inputs:
+        x_sep, h_sep = T(xi, gpu), torch.zeros(k * F, device=gpu)
+        ops.router_topk(ids, wts, scores, x_sep, nwt, 1e-6, wrt, d, E, k)
+        ops.moe_swiglu(h_sep, x_sep, nwt, 1e-6, gu_d, ids, k, F, d, dtype=name)
+        ops.moe_down_residual(x_sep, h_sep, dn_d, ids, wts, k, d, F, dtype=name)
+        x_ch = T(xi, gpu)
+        ops.moe_ffn(x_ch, h_ch, nwt, 1e-6, wrt, gu_d, dn_d, scores, ids_ch, wts_ch, d, F, E, k, dtype=name)
+        assert torch.equal(ids_ch, ids) and torch.equal(h_ch, h_sep) and torch.equal(x_ch, x_sep)
 
 
 def test_embed(ops, orc, gpu):
