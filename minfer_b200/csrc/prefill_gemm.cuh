@@ -247,11 +247,31 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
                 const int F = p.N >> 1;
                 __nv_bfloat16* hh = p.h_hi + (size_t)row * F + (col >> 1);
                 __nv_bfloat16* hl = p.h_lo + (size_t)row * F + (col >> 1);
+                if (full && (F & 7) == 0) {
+                    // 16 outputs of this row: packed into two 16-byte stores per operand
+                    // (col / 2 is a multiple of 16, so both are 16-byte aligned)
+                    uint32_t ph[8], pl[8];
 #pragma unroll
-                for (int j = 0; j < 32; j += 2) {
-                    if (!full && col + j + 1 >= p.N) break;
-                    const float h = silu(__uint_as_float(r[j])) * __uint_as_float(r[j + 1]);
-                    split_bf16(h, hh[j >> 1], hl[j >> 1]);
+                    for (int j = 0; j < 32; j += 4) {
+                        __nv_bfloat16 h0, l0, h1, l1;
+                        split_bf16(silu(__uint_as_float(r[j])) * __uint_as_float(r[j + 1]), h0, l0);
+                        split_bf16(silu(__uint_as_float(r[j + 2])) * __uint_as_float(r[j + 3]), h1, l1);
+                        ph[j >> 2] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+                        pl[j >> 2] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+                    }
+                    uint4* dh = reinterpret_cast<uint4*>(hh);
+                    uint4* dl = reinterpret_cast<uint4*>(hl);
+                    dh[0] = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+                    dh[1] = make_uint4(ph[4], ph[5], ph[6], ph[7]);
+                    dl[0] = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+                    dl[1] = make_uint4(pl[4], pl[5], pl[6], pl[7]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        if (!full && col + j + 1 >= p.N) break;
+                        const float h = silu(__uint_as_float(r[j])) * __uint_as_float(r[j + 1]);
+                        split_bf16(h, hh[j >> 1], hl[j >> 1]);
+                    }
                 }
             } else {
                 float* yr = p.y + (size_t)row * p.ldy + col;
