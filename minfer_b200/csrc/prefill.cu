@@ -128,21 +128,53 @@ namespace mf {
 
 // out = rmsnorm(x) * w split into bf16 hi/lo, one CTA per row
 // (src/ops/kernels.cpp:351-365: inv = 1/sqrtf(sum(x^2)/n + eps); out = inv*x*w).
+// Rows of a multiple of 4 elements go 16 bytes at a time (float4 loads,
+// 8-byte stores of four bf16); other widths element by element.
 __global__ void __launch_bounds__(256) norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                          float eps, int d, __nv_bfloat16* hi, __nv_bfloat16* lo,
                                                          float* xn) {
     __shared__ float scratch[32];
     pdl_launch_dependents();
     pdl_wait();
-    const float* xr = x + (size_t)blockIdx.x * d;
+    const size_t r0 = (size_t)blockIdx.x * d;
+    const float* xr = x + r0;
+    const bool vec = (d & 3) == 0;
     float ss = 0.f;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    if (vec) {
+        for (int i = 4 * threadIdx.x; i < d; i += 4 * blockDim.x) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + i);
+            ss = fmaf(v.x, v.x, ss);
+            ss = fmaf(v.y, v.y, ss);
+            ss = fmaf(v.z, v.z, ss);
+            ss = fmaf(v.w, v.w, ss);
+        }
+    } else {
+        for (int i = threadIdx.x; i < d; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    }
     ss = block_sum(ss, scratch);
     const float inv = 1.0f / sqrtf(ss / (float)d + eps);
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        const float v = (inv * xr[i]) * w[i];
-        if (xn) xn[(size_t)blockIdx.x * d + i] = v;
-        split_bf16(v, hi[(size_t)blockIdx.x * d + i], lo[(size_t)blockIdx.x * d + i]);
+    if (vec) {
+        for (int i = 4 * threadIdx.x; i < d; i += 4 * blockDim.x) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + i);
+            const float4 g = *reinterpret_cast<const float4*>(w + i);
+            const float o[4] = {(inv * v.x) * g.x, (inv * v.y) * g.y, (inv * v.z) * g.z, (inv * v.w) * g.w};
+            if (xn) *reinterpret_cast<float4*>(xn + r0 + i) = make_float4(o[0], o[1], o[2], o[3]);
+            __nv_bfloat16 h[4], l[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) split_bf16(o[e], h[e], l[e]);
+            *reinterpret_cast<uint2*>(hi + r0 + i) =
+                make_uint2((uint32_t)__bfloat16_as_ushort(h[0]) | ((uint32_t)__bfloat16_as_ushort(h[1]) << 16),
+                           (uint32_t)__bfloat16_as_ushort(h[2]) | ((uint32_t)__bfloat16_as_ushort(h[3]) << 16));
+            *reinterpret_cast<uint2*>(lo + r0 + i) =
+                make_uint2((uint32_t)__bfloat16_as_ushort(l[0]) | ((uint32_t)__bfloat16_as_ushort(l[1]) << 16),
+                           (uint32_t)__bfloat16_as_ushort(l[2]) | ((uint32_t)__bfloat16_as_ushort(l[3]) << 16));
+        }
+    } else {
+        for (int i = threadIdx.x; i < d; i += blockDim.x) {
+            const float v = (inv * xr[i]) * w[i];
+            if (xn) xn[r0 + i] = v;
+            split_bf16(v, hi[r0 + i], lo[r0 + i]);
+        }
     }
 }
 
@@ -296,6 +328,8 @@ int mf_prefill_gemm_grouped(float* y, int ldy, const void* a_hi, const void* a_l
 int mf_prefill_norm_split(void* hi, void* lo, float* xn, const float* x, const float* norm_w, float eps, int d,
                           int n_rows, void* stream) {
     if (!hi || !lo || !x || !norm_w || d <= 0 || n_rows <= 0) return fail(MF_E_INVALID, "bad arguments");
+    if ((d & 3) == 0 && (((uintptr_t)hi | (uintptr_t)lo) & 7 || ((uintptr_t)x | (uintptr_t)norm_w | (uintptr_t)xn) & 15))
+        return fail(MF_E_INVALID, "rows of a multiple of 4 need 16-byte aligned x/norm_w/xn and 8-byte aligned hi/lo");
     const float* xa = x;
     const float* wa = norm_w;
     __nv_bfloat16* h = (__nv_bfloat16*)hi;
@@ -344,7 +378,8 @@ int mf_prefill_qkv_post(float* q_out, void* k_cache, void* v_cache, const float*
                     (void*)&pos0};
     const void* fn = kv_dtype == MF_F32 ? (const void*)&mf::prefill_qkv_post_kernel<float>
                                         : (const void*)&mf::prefill_qkv_post_kernel<__nv_bfloat16>;
-    cudaError_t e = launch(fn, dim3(n_tokens, n_heads + n_kv_heads), dim3(32), 0, mf::resolve_stream(stream), args);
+    const unsigned hy = (unsigned)((n_heads + n_kv_heads + mf::QP_WARPS - 1) / mf::QP_WARPS);
+    cudaError_t e = launch(fn, dim3(n_tokens, hy), dim3(mf::QP_WARPS * 32), 0, mf::resolve_stream(stream), args);
     return e == cudaSuccess ? MF_OK : fail(MF_E_CUDA, cudaGetErrorString(e));
 }
 

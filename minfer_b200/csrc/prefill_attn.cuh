@@ -8,7 +8,8 @@
 // (RMSNorm, the fused rotation, max-subtracted softmax) is the same, the
 // softmax is evaluated online over 32-key tiles.
 //
-//  * prefill_qkv_post_kernel: one warp per (token, head): norm + RoPE of q
+//  * prefill_qkv_post_kernel: one warp per (token, head), eight heads per
+//    CTA: norm + RoPE of q
 //    (-> Q buffer), of k (-> K cache row), v copied to the V cache row.
 //  * prefill_attn_kernel: CTA = 64 query rows (QT tokens x G heads of one
 //    KV head, QT = 64 / G) x one KV head; 256 threads. K/V tiles of 32 rows
@@ -31,14 +32,17 @@ namespace mf {
 // qkv: [P][(Hq + 2 Hkv) * D] (projection output); Q out: [P][Hq * D];
 // caches: this layer's [Hkv][max_seq][D] of KV (float, or bf16 rounded to
 // nearest even). Positions are pos0 + token.
+// One warp per (token, head): CTA (t, y) serves token t, heads 8y .. 8y + 7.
+constexpr int QP_WARPS = 8;
 template <typename KV>
-__global__ void __launch_bounds__(32) prefill_qkv_post_kernel(const float* __restrict__ qkv, const float* q_norm_w,
-                                                              const float* k_norm_w, float eps, const float2* rope,
-                                                              float* q_out, KV* k_cache, KV* v_cache,
-                                                              int max_seq, int n_heads, int n_kv_heads, int pos0) {
+__global__ void __launch_bounds__(QP_WARPS * 32) prefill_qkv_post_kernel(const float* __restrict__ qkv,
+                                                                        const float* q_norm_w, const float* k_norm_w,
+                                                                        float eps, const float2* rope, float* q_out,
+                                                                        KV* k_cache, KV* v_cache, int max_seq,
+                                                                        int n_heads, int n_kv_heads, int pos0) {
     pdl_launch_dependents();
     pdl_wait();
-    const int t = blockIdx.x, h = blockIdx.y, lane = threadIdx.x;
+    const int t = blockIdx.x, h = blockIdx.y * QP_WARPS + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     const int Hq = n_heads, Hkv = n_kv_heads;
     const int pos = pos0 + t;
     if (pos >= max_seq) return;
