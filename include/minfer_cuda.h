@@ -373,19 +373,22 @@ int mf_prefill_gemm_grouped(float* y, int ldy, const void* a_hi, const void* a_l
  * route: fp32 router scores of the normalised rows xn [n_tokens][d_model]
  *   against w_router [n_experts][d_model] and the reference's top-k + softmax
  *   per token -> ids / weights [n_tokens][k] (n_experts a multiple of 4, <= 256);
- * group: counting sort of the n_tokens*k (token, slot) pairs by expert: rows /
- *   tiles [n_experts + 1] (first grouped row / 128-row tile of each expert) and
- *   pos [n_tokens*k] (the grouped row of pair t*k + s);
- * gather: token t's row of xn split into bf16 hi/lo at its k grouped rows;
- * combine: x[t] += weights[t][s] * y[pos[t*k + s]] for s = 0..k-1 in order. */
+ * group: counting sort of the n_tokens*k (token, slot) pairs by expert, over
+ *   the experts [expert_lo, expert_lo + n_local) stored here: rows / tiles
+ *   [n_local + 1] (first grouped row / 128-row tile of each local expert) and
+ *   pos [n_tokens*k] (the grouped row of pair t*k + s, -1 for an expert
+ *   stored elsewhere);
+ * gather: token t's row of xn split into bf16 hi/lo at its grouped rows;
+ * combine: x_out[t] = x_in[t] (0 when x_in is null) + weights[t][s] *
+ *   y[pos[t*k + s]] for s = 0..k-1 in order, slots with pos -1 skipped. */
 int mf_prefill_moe_route(int* ids, float* weights, const float* xn, const float* w_router, int n_tokens, int d_model,
                          int n_experts, int k, void* stream);
-int mf_prefill_moe_group(const int* ids, int n_tokens, int k, int n_experts, int* rows, int* tiles, int* pos,
-                         void* stream);
+int mf_prefill_moe_group(const int* ids, int n_tokens, int k, int expert_lo, int n_local, int* rows, int* tiles,
+                         int* pos, void* stream);
 int mf_prefill_moe_gather(void* a_hi, void* a_lo, const float* xn, const int* pos, int n_tokens, int k, int d_model,
                           void* stream);
-int mf_prefill_moe_combine(float* x, const float* y, const int* pos, const float* weights, int n_tokens, int k,
-                           int d_model, void* stream);
+int mf_prefill_moe_combine(float* x_out, const float* x_in, const float* y, const int* pos, const float* weights,
+                           int n_tokens, int k, int d_model, void* stream);
 /* Row-wise RMSNorm (src/ops/kernels.cpp:351-365) of x [n_rows][d] split into
  * bf16 hi/lo; xn (optional) receives the fp32 normalised rows. */
 int mf_prefill_norm_split(void* hi, void* lo, float* xn, const float* x, const float* norm_w, float eps, int d,

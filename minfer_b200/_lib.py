@@ -149,9 +149,9 @@ CUDA_API = {
     "mf_prefill_gemm": (I, [P, I, P, P, P, I, I, I, I, P, P, P]),
     "mf_prefill_gemm_grouped": (I, [P, I, P, P, P, I, I, I, I, P, P, I, P, P, P]),
     "mf_prefill_moe_route": (I, [P, P, P, P, I, I, I, I, P]),
-    "mf_prefill_moe_group": (I, [P, I, I, I, P, P, P, P]),
+    "mf_prefill_moe_group": (I, [P, I, I, I, I, P, P, P, P]),
     "mf_prefill_moe_gather": (I, [P, P, P, P, I, I, I, P]),
-    "mf_prefill_moe_combine": (I, [P, P, P, P, I, I, I, P]),
+    "mf_prefill_moe_combine": (I, [P, P, P, P, P, I, I, I, P]),
     "mf_prefill_norm_split": (I, [P, P, P, P, P, F, I, I, P]),
     "mf_prefill_split": (I, [P, P, P, SZ, P]),
     "mf_prefill_swiglu_split": (I, [P, P, P, I, I, P]),

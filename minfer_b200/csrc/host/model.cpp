@@ -279,7 +279,7 @@ public:
             check(mf_prefill_attention_tc(hi, lo, (const float*)mf_ptr(rs.pf_q), kc, vc, S, n, pos0, H, Hkv, D,
                                           mf_ptr(rs.pf_att), rs.pf_att_bytes, rs.kv_dtype, rs.stream),
                   "prefill attention");
-        if (c_.tp_size == 1) {
+        if (!c_.attn_split()) {  // one GPU, or expert parallelism (attention replicated)
             prefill_gemm(X, d, hi, lo, wo_, wo_s_, n, d, H * D, MF_PREFILL_RESID, rs.stream,
                          "prefill output projection");
         } else {
@@ -449,6 +449,7 @@ public:
     // experts' outputs in slot order
     void moe_prefill(RunState& rs, int n) {
         const int d = c_.d_model, F = c_.d_ff, E = c_.n_experts, k = c_.n_active_experts;
+        const int El = c_.experts_local();  // under expert parallelism this rank's experts only
         float* X = (float*)mf_ptr(rs.pf_x);
         float* xn = (float*)mf_ptr(rs.pf_xn);
         int* ids = (int*)mf_ptr(rs.pf_ids) + (size_t)layer_ * rs.pf_cap * k;
@@ -460,18 +461,29 @@ public:
                                     c_.rms_norm_eps, d, n, rs.stream),
               "prefill ffn norm");
         check(mf_prefill_moe_route(ids, wts, xn, (const float*)mf_ptr(wr_), n, d, E, k, rs.stream), "prefill router");
-        check(mf_prefill_moe_group(ids, n, k, E, grows, gtiles, pos, rs.stream), "prefill expert grouping");
+        check(mf_prefill_moe_group(ids, n, k, c_.expert_lo(), El, grows, gtiles, pos, rs.stream),
+              "prefill expert grouping");
         check(mf_prefill_moe_gather(mf_ptr(rs.pf_ghi), mf_ptr(rs.pf_glo), xn, pos, n, k, d, rs.stream),
               "prefill expert operands");
-        check(mf_prefill_gemm_grouped(nullptr, 0, mf_ptr(rs.pf_ghi), mf_ptr(rs.pf_glo), mf_ptr(wgu_), E, n * k, 2 * F,
-                                      d, grows, gtiles, MF_PREFILL_SWIGLU, mf_ptr(rs.pf_mhi), mf_ptr(rs.pf_mlo),
-                                      rs.stream),
+        check(mf_prefill_gemm_grouped(nullptr, 0, mf_ptr(rs.pf_ghi), mf_ptr(rs.pf_glo), mf_ptr(wgu_), El, n * k,
+                                      2 * F, d, grows, gtiles, MF_PREFILL_SWIGLU, mf_ptr(rs.pf_mhi),
+                                      mf_ptr(rs.pf_mlo), rs.stream),
               "prefill expert gate/up");
         check(mf_prefill_gemm_grouped((float*)mf_ptr(rs.pf_y), d, mf_ptr(rs.pf_mhi), mf_ptr(rs.pf_mlo), mf_ptr(wd_),
-                                      E, n * k, d, F, grows, gtiles, MF_PREFILL_STORE, nullptr, nullptr, rs.stream),
+                                      El, n * k, d, F, grows, gtiles, MF_PREFILL_STORE, nullptr, nullptr, rs.stream),
               "prefill expert down");
-        check(mf_prefill_moe_combine(X, (const float*)mf_ptr(rs.pf_y), pos, wts, n, k, d, rs.stream),
-              "prefill expert combine");
+        if (!c_.ep()) {
+            check(mf_prefill_moe_combine(X, X, (const float*)mf_ptr(rs.pf_y), pos, wts, n, k, d, rs.stream),
+                  "prefill expert combine");
+        } else {
+            // this rank's slots from zero into the exchange slot; the ranks'
+            // partials are summed into the residual (rank order)
+            float* part = prefill_exchange_slot(rs);
+            check(mf_prefill_moe_combine(part, nullptr, (const float*)mf_ptr(rs.pf_y), pos, wts, n, k, d, rs.stream),
+                  "prefill expert combine (partial)");
+            prefill_exchange(rs, X, n, d);
+        }
+        (void)E;
         // the last prompt token's routing, where the decode step keeps it
         check(mf_copy(rs.expert_ids, (size_t)layer_ * k * 4, rs.pf_ids,
                       ((size_t)layer_ * rs.pf_cap + (size_t)(n - 1)) * k * 4, (size_t)k * 4),
@@ -750,7 +762,7 @@ void Qwen3Model::alloc_state() {
     rs.kv_bytes_per_pos = 2ull * c.n_layers * Hkvl * c.d_head * rs.kv_elem;
     if (c.tp_size > 1) {
         // dense models also get two bulk slots of [prompt chunk rows, d] for the batched prefill
-        rs.pf_bulk_rows = c.ep() ? 0 : (int)std::min<size_t>(c.user_max_seq_len, (size_t)kPrefillChunk);
+        rs.pf_bulk_rows = (int)std::min<size_t>(c.user_max_seq_len, (size_t)kPrefillChunk);
         const size_t bulk = (size_t)rs.pf_bulk_rows * ((c.d_model + 3) / 4 * 4);
         check(mf_comm_create_ex(rank_, c.tp_rank, c.tp_size, (c.d_model + 3) / 4 * 4, (int)c.vocab_size, bulk,
                                 &rs.comm),
@@ -779,8 +791,9 @@ int Qwen3Model::comm_status(int* status) {
 
 bool Qwen3Model::prefill_supported() const {
     if (device_ != DeviceType::CUDA) return false;
-    // MoE: one GPU, bf16 experts, up to 256 experts (a multiple of 4), k <= 32
-    if (cfg_.n_experts != 0 && (cfg_.tp_size > 1 || cfg_.weight_dtype != DataType::BF16 || cfg_.n_experts % 4 != 0 ||
+    // MoE: bf16 experts, up to 256 experts (a multiple of 4), k <= 32; one GPU
+    // or expert parallelism
+    if (cfg_.n_experts != 0 && (cfg_.weight_dtype != DataType::BF16 || cfg_.n_experts % 4 != 0 ||
                                 cfg_.n_experts > 256 || cfg_.n_active_experts > 32))
         return false;
     if (cfg_.tp_size > 1 && (rs_.pf_bulk_rows <= 0 || !rs_.comm || cfg_.d_model % 4 != 0)) return false;
@@ -880,7 +893,8 @@ bool Qwen3Model::prefill(const uint32_t* tokens, int n, int pos0, bool compute_l
     }
     // the last token's residual row feeds the decode lm_head (under tensor
     // parallelism the lm_head adds an all-reduce to it: see below)
-    mf_buf* last = cfg_.tp_size > 1 ? rs_.xb[1] : rs_.x;
+    const int L = cfg_.n_layers;
+    mf_buf* last = cfg_.tp_size == 1 ? rs_.x : (cfg_.ep() ? rs_.xb[(L - 1) & 1] : rs_.xb[1]);
     check(mf_copy(last, 0, rs_.pf_x, (size_t)(last_rows - 1) * cfg_.d_model * 4, (size_t)cfg_.d_model * 4),
           "prefill last row");
     rs_.cur_pos = pos0 + n - 1;
@@ -898,11 +912,13 @@ bool Qwen3Model::prefill(const uint32_t* tokens, int n, int pos0, bool compute_l
     if (rc == MF_FRAME_RECORD) {
         try {
             if (cfg_.tp_size > 1) {
-                // the tensor-parallel lm_head receives the last layer's all-reduce
-                // (exchange 2L - 1) on top of its residual; the residual is already
-                // complete, so every rank sends a zero partial
-                check(mf_allreduce((float*)mf_ptr(rs_.xb[0]), (const float*)mf_ptr(rs_.xb[1]),
-                                   (const float*)mf_ptr(rs_.zero_d), cfg_.d_model, rs_.comm, 2 * cfg_.n_layers - 1,
+                // the sharded lm_head receives the last layer's all-reduce
+                // (exchange 2L - 1, or L - 1 under expert parallelism) on top of
+                // its residual; the residual is already complete, so every rank
+                // sends a zero partial
+                const bool ep = cfg_.ep();
+                check(mf_allreduce((float*)mf_ptr(ep ? rs_.xb[L & 1] : rs_.xb[0]), (const float*)mf_ptr(last),
+                                   (const float*)mf_ptr(rs_.zero_d), cfg_.d_model, rs_.comm, ep ? L - 1 : 2 * L - 1,
                                    rs_.d_step, rs_.stream),
                       "prefill zero all-reduce");
             }

@@ -9,8 +9,9 @@
 //                             the selection must see fp32 scores) and the
 //                             reference's top-k + softmax per token;
 //   2. mf_prefill_moe_group   a counting sort of the n*k (token, slot) pairs
-//                             by expert: per expert its rows [rows[e], rows[e+1])
-//                             of the grouped buffers and its GEMM tiles;
+//                             by expert (the experts stored here): per expert
+//                             its rows [rows[e], rows[e+1]) of the grouped
+//                             buffers and its GEMM tiles;
 //   3. mf_prefill_moe_gather  each token's normalised row, split into bf16
 //                             hi/lo, written to its k grouped rows;
 //   4. mf_prefill_gemm_grouped (prefill.cu) gate/up with the SwiGLU epilogue
@@ -18,6 +19,10 @@
 //                             (expert, 128 rows, 256 columns);
 //   5. mf_prefill_moe_combine x[t] += w_s * y[row(t, s)] for s = 0..k-1 in
 //                             slot order (the reference's order).
+// Under expert parallelism every rank holds every token's row (attention is
+// replicated), routes them all identically, runs only its experts, combines
+// its slots into a partial from zero, and the ranks' partials are summed into
+// the residual by the bulk all-reduce of the dense tensor-parallel prefill.
 // Rows of one expert are independent in the GEMMs, so the order the counting
 // sort assigns within an expert does not change any result.
 #include <cuda_runtime.h>
@@ -111,39 +116,42 @@ __global__ void __launch_bounds__(256) moe_route_prefill_kernel(const float* __r
     (void)lane;
 }
 
-// Counting sort of the n*k (token, slot) pairs by expert, one CTA.
-// rows[e]: first grouped row of expert e (rows[E] = n*k); tiles[e]: first
-// 128-row GEMM tile of expert e; pos[t*k + s]: the grouped row of (t, s).
-__global__ void __launch_bounds__(1024) moe_group_kernel(const int* __restrict__ ids, int nk, int n_experts,
+// Counting sort of the n*k (token, slot) pairs by expert, one CTA, over the
+// experts stored here: [e_lo, e_lo + n_local) (all of them on one GPU; a
+// rank's share under expert parallelism). rows[e]: first grouped row of local
+// expert e (rows[n_local] = the pairs routed here); tiles[e]: its first
+// 128-row GEMM tile; pos[t*k + s]: the grouped row of (t, s), -1 when its
+// expert is stored elsewhere.
+__global__ void __launch_bounds__(1024) moe_group_kernel(const int* __restrict__ ids, int nk, int e_lo, int n_local,
                                                          int* __restrict__ rows, int* __restrict__ tiles,
                                                          int* __restrict__ pos) {
     __shared__ int cnt[MR_MAXE], cur[MR_MAXE];
     pdl_launch_dependents();
     pdl_wait();
     const int tid = threadIdx.x;
-    for (int e = tid; e < n_experts; e += blockDim.x) cnt[e] = 0;
+    for (int e = tid; e < n_local; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     for (int i = tid; i < nk; i += blockDim.x) {
-        const int e = ids[i];
-        if (e >= 0 && e < n_experts) atomicAdd(&cnt[e], 1);
+        const int e = ids[i] - e_lo;
+        if (e >= 0 && e < n_local) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
     if (tid == 0) {
         int r = 0, tl = 0;
-        for (int e = 0; e < n_experts; ++e) {
+        for (int e = 0; e < n_local; ++e) {
             rows[e] = r;
             tiles[e] = tl;
             cur[e] = r;
             r += cnt[e];
             tl += (cnt[e] + PG_BM - 1) / PG_BM;
         }
-        rows[n_experts] = r;
-        tiles[n_experts] = tl;
+        rows[n_local] = r;
+        tiles[n_local] = tl;
     }
     __syncthreads();
     for (int i = tid; i < nk; i += blockDim.x) {
-        const int e = ids[i];
-        pos[i] = (e >= 0 && e < n_experts) ? atomicAdd(&cur[e], 1) : 0;
+        const int e = ids[i] - e_lo;
+        pos[i] = (e >= 0 && e < n_local) ? atomicAdd(&cur[e], 1) : -1;
     }
 }
 
@@ -160,27 +168,30 @@ __global__ void __launch_bounds__(256) moe_gather_split_kernel(const float* __re
         __nv_bfloat16 h, l;
         split_bf16(xr[i], h, l);
         for (int s = 0; s < k; ++s) {
-            const size_t r = (size_t)pos[(size_t)t * k + s];
-            hi[r * d + i] = h;
-            lo[r * d + i] = l;
+            const int r = pos[(size_t)t * k + s];
+            if (r < 0) continue;  // expert stored on another rank
+            hi[(size_t)r * d + i] = h;
+            lo[(size_t)r * d + i] = l;
         }
     }
 }
 
-// x[t] += w[t][s] * y[pos(t, s)] for s = 0..k-1 in order
+// x_out[t] = x_in[t] (or 0) + w[t][s] * y[pos(t, s)] for s = 0..k-1 in order,
+// skipping slots whose expert is stored elsewhere
 // (src/models/qwen3/module.cpp:471-474: x += expert_out * weight, one expert at a time).
-__global__ void __launch_bounds__(256) moe_combine_kernel(float* __restrict__ x, const float* __restrict__ y,
-                                                          const int* __restrict__ pos,
+__global__ void __launch_bounds__(256) moe_combine_kernel(float* x_out, const float* x_in,
+                                                          const float* __restrict__ y, const int* __restrict__ pos,
                                                           const float* __restrict__ weights, int k, int d) {
     pdl_launch_dependents();
     pdl_wait();
     const int t = blockIdx.x;
-    float* xr = x + (size_t)t * d;
     for (int j = threadIdx.x; j < d; j += blockDim.x) {
-        float acc = xr[j];
-        for (int s = 0; s < k; ++s)
-            acc = fmaf(y[(size_t)pos[(size_t)t * k + s] * d + j], weights[(size_t)t * k + s], acc);
-        xr[j] = acc;
+        float acc = x_in ? x_in[(size_t)t * d + j] : 0.f;
+        for (int s = 0; s < k; ++s) {
+            const int r = pos[(size_t)t * k + s];
+            if (r >= 0) acc = fmaf(y[(size_t)r * d + j], weights[(size_t)t * k + s], acc);
+        }
+        x_out[(size_t)t * d + j] = acc;
     }
 }
 
@@ -221,12 +232,13 @@ int mf_prefill_moe_route(int* ids, float* weights, const float* xn, const float*
                      dim3(256), mf::resolve_stream(stream), args));
 }
 
-int mf_prefill_moe_group(const int* ids, int n_tokens, int k, int n_experts, int* rows, int* tiles, int* pos,
-                         void* stream) {
-    if (!ids || !rows || !tiles || !pos || n_tokens <= 0 || k <= 0) return fail(MF_E_INVALID, "bad arguments");
-    if (n_experts < 1 || n_experts > mf::MR_MAXE) return fail(MF_E_UNSUPPORTED, "n_experts above 256");
+int mf_prefill_moe_group(const int* ids, int n_tokens, int k, int expert_lo, int n_local, int* rows, int* tiles,
+                         int* pos, void* stream) {
+    if (!ids || !rows || !tiles || !pos || n_tokens <= 0 || k <= 0 || expert_lo < 0)
+        return fail(MF_E_INVALID, "bad arguments");
+    if (n_local < 1 || n_local > mf::MR_MAXE) return fail(MF_E_UNSUPPORTED, "local experts must be 1..256");
     int nk = n_tokens * k;
-    void* args[] = {(void*)&ids, &nk, &n_experts, &rows, &tiles, &pos};
+    void* args[] = {(void*)&ids, &nk, &expert_lo, &n_local, &rows, &tiles, &pos};
     return ck(launch((const void*)&mf::moe_group_kernel, dim3(1), dim3(1024), mf::resolve_stream(stream), args));
 }
 
@@ -241,11 +253,11 @@ int mf_prefill_moe_gather(void* a_hi, void* a_lo, const float* xn, const int* po
                      mf::resolve_stream(stream), args));
 }
 
-int mf_prefill_moe_combine(float* x, const float* y, const int* pos, const float* weights, int n_tokens, int k,
-                           int d_model, void* stream) {
-    if (!x || !y || !pos || !weights || n_tokens <= 0 || k <= 0 || d_model <= 0)
+int mf_prefill_moe_combine(float* x_out, const float* x_in, const float* y, const int* pos, const float* weights,
+                           int n_tokens, int k, int d_model, void* stream) {
+    if (!x_out || !y || !pos || !weights || n_tokens <= 0 || k <= 0 || d_model <= 0)
         return fail(MF_E_INVALID, "bad arguments");
-    void* args[] = {(void*)&x, (void*)&y, (void*)&pos, (void*)&weights, &k, &d_model};
+    void* args[] = {(void*)&x_out, (void*)&x_in, (void*)&y, (void*)&pos, (void*)&weights, &k, &d_model};
     return ck(launch((const void*)&mf::moe_combine_kernel, dim3(n_tokens), dim3(256), mf::resolve_stream(stream),
                      args));
 }

@@ -171,7 +171,7 @@ def test_prefill_moe_route_group_gather_combine(lib, gpu):
     rows = torch.zeros(E + 1, dtype=torch.int32, device=gpu)
     tiles = torch.zeros(E + 1, dtype=torch.int32, device=gpu)
     pos = torch.full((n * k,), -1, dtype=torch.int32, device=gpu)
-    check(lib.mf_prefill_moe_group(P(ids), n, k, E, P(rows), P(tiles), P(pos), stream()))
+    check(lib.mf_prefill_moe_group(P(ids), n, k, 0, E, P(rows), P(tiles), P(pos), stream()))
     torch.cuda.synchronize()
     r, tl, ps = rows.cpu().numpy(), tiles.cpu().numpy(), pos.cpu().numpy()
     cnt = np.bincount(ids_c.ravel(), minlength=E)
@@ -181,6 +181,16 @@ def test_prefill_moe_route_group_gather_combine(lib, gpu):
     for i, p_ in enumerate(ps):  # each pair lies in its expert's rows
         e = ids_c.ravel()[i]
         assert r[e] <= p_ < r[e + 1]
+    # a rank's share under expert parallelism: experts [32, 64) only
+    rows2 = torch.zeros(33, dtype=torch.int32, device=gpu)
+    tiles2 = torch.zeros(33, dtype=torch.int32, device=gpu)
+    pos2 = torch.zeros(n * k, dtype=torch.int32, device=gpu)
+    check(lib.mf_prefill_moe_group(P(ids), n, k, 32, 32, P(rows2), P(tiles2), P(pos2), stream()))
+    torch.cuda.synchronize()
+    loc = (ids_c.ravel() >= 32) & (ids_c.ravel() < 64)
+    p2 = pos2.cpu().numpy()
+    assert np.all(p2[~loc] == -1) and sorted(p2[loc].tolist()) == list(range(int(loc.sum())))
+    assert rows2.cpu().numpy()[32] == int(loc.sum())
     ahi = torch.zeros(n * k, d, dtype=torch.bfloat16, device=gpu)
     alo = torch.zeros_like(ahi)
     check(lib.mf_prefill_moe_gather(P(ahi), P(alo), P(xt), P(pos), n, k, d, stream()))
@@ -192,7 +202,7 @@ def test_prefill_moe_route_group_gather_combine(lib, gpu):
     y = torch.randn(n * k, d, device=gpu)
     x0 = torch.randn(n, d, device=gpu)
     x = x0.clone()
-    check(lib.mf_prefill_moe_combine(P(x), P(y), P(pos), P(wts), n, k, d, stream()))
+    check(lib.mf_prefill_moe_combine(P(x), P(x), P(y), P(pos), P(wts), n, k, d, stream()))
     torch.cuda.synchronize()
     ref = x0.clone()
     for s_ in range(k):

@@ -108,6 +108,7 @@ def check_model(name, rank, world):
         m.forward(int(t), i, i == P - 1, i == P - 1)
     err = np.max(np.abs(orc0.logits() - m.logits()))
     assert err <= logit_tol(cfg.dtype), f"{name}: step-0 logits max-abs {err}"
+    ref_e = None
     if cfg.n_experts > 0:
         # the router runs on every rank: every rank's expert ids per layer match the oracle's
         orc_e = PortModel(path, max_seq=P + 1)
@@ -123,9 +124,10 @@ def check_model(name, rank, world):
         assert me.comm_status() == 0
         me.close()
     assert m.argmax() == int(np.argmax(m.logits()))
-    if cfg.n_experts == 0 and cfg.dtype == "bf16":
+    if cfg.dtype == "bf16":
         # batched prefill on the tensor cores, partials exchanged per projection
-        # (one pass, and 5-row chunks: alternating slots and cached history)
+        # (dense) or per layer's experts (MoE, expert parallelism); one pass, and
+        # 5-row chunks: alternating slots and cached history
         for chunk in (None, "5"):
             if chunk:
                 os.environ["MF_PREFILL_CHUNK"] = chunk
@@ -135,6 +137,12 @@ def check_model(name, rank, world):
             assert err <= logit_tol(cfg.dtype), f"{name}: batched-prefill logits max-abs {err} (chunk {chunk})"
             assert mp.argmax() == int(np.argmax(mp.logits()))
             assert same_on_all_ranks([mp.argmax()]), f"{name}: ranks disagree after batched prefill"
+            if ref_e is not None:  # every rank routed the prompt like the oracle
+                n_last = P if not chunk else P - (P - 1) // int(chunk) * int(chunk)
+                want = ref_e.reshape(P, cfg.n_layers, cfg.n_active)[P - n_last:]
+                for layer in range(cfg.n_layers):
+                    got, _ = mp.prefill_experts(layer, n_last)
+                    assert np.array_equal(got, want[:, layer]), f"{name}: prefill experts differ at layer {layer}"
             assert mp.comm_status() == 0
             mp.close()
             os.environ.pop("MF_PREFILL_CHUNK", None)
