@@ -135,6 +135,7 @@ int mf_timer_stop(int rank, float* ms);
 #define MF_STEP_FRAME 4 /* index of the frame field */
 #define MF_STEP_STATUS 5 /* exchange status bits (mf_comm_status), written by the tensor-parallel lm_head */
 #define MF_STEP_DSTATUS 6 /* bit 1: a decode kernel's copy wait gave up (mf_decode_status) */
+#define MF_STEP_SAMPLE 7  /* index of the next device-sampled token (mf_sample_step) */
 int mf_step_state(int rank, int32_t** host, void** device);
 /* Decode-kernel status of a rank (the MF_STEP_DSTATUS field of its device
  * step record, which the TMA-fed GEMVs set when a bounded copy wait gave up);
@@ -437,6 +438,17 @@ int mf_prefill_attention_tc(void* out_hi, void* out_lo, const float* q, const vo
 size_t mf_topk_workspace_bytes(int n, int k);
 int mf_topk(const float* x, int n, int k, int* ids, float* vals, void* workspace, size_t workspace_bytes,
             void* stream);
+/* One sampled token on the device from a top-k candidate list (top_k + 1
+ * entries from mf_topk, so equal logits at the cut are seen): the reference's
+ * Sampler::sample after its top-k (softmax, top-p, min-p, temperature softmax,
+ * the first candidate whose cumulative probability reaches draws[i], i = the
+ * step record's MF_STEP_SAMPLE field). The chosen id is written to out_ids[i]
+ * and becomes the record's token; position, frame and sample index advance,
+ * so a captured frame can feed the next one. flags: bit 1 equal logits among
+ * the candidates, bit 2 sample index outside [0, n_draws), bit 4 every
+ * candidate filtered out. No presence penalty (it changes the list). */
+int mf_sample_step(const int* cand_ids, const float* cand_vals, int top_k, float temp, float top_p, float min_p,
+                   const float* draws, int n_draws, void* step_state, int* out_ids, int* flags, void* stream);
 
 /* Status bits of the prefill kernels since the last clear (1: a GEMM wait
  * gave up, 2: an attention wait gave up, 4: attention q/k outside the fp16

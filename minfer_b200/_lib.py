@@ -163,6 +163,7 @@ CUDA_API = {
     "mf_prefill_status": (I, [P, I]),
     "mf_topk_workspace_bytes": (SZ, [I, I]),
     "mf_topk": (I, [P, I, I, P, P, P, SZ, P]),
+    "mf_sample_step": (I, [P, P, I, F, F, F, P, I, P, P, P, P]),
     "mf_matmul": (I, [P, P, P, I, SZ, I, I, P]),
     "mf_rmsnorm": (I, [P, P, P, I, F, I, P]),
     "mf_softmax": (I, [P, P, I, I, P]),

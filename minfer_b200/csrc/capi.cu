@@ -1330,6 +1330,20 @@ int mf_topk(const float* x, int n, int k, int* ids, float* vals, void* workspace
     return MF_OK;
 }
 
+int mf_sample_step(const int* cand_ids, const float* cand_vals, int top_k, float temp, float top_p, float min_p,
+                   const float* draws, int n_draws, void* step_state, int* out_ids, int* flags, void* stream) {
+    MF_REQUIRE(cand_ids && cand_vals && draws && step_state && out_ids && flags, MF_E_INVALID, "null argument");
+    MF_REQUIRE(top_k >= 1 && top_k + 1 <= mf::TOPK_MAX && top_k <= mf::SAMPLE_MAX_K, MF_E_INVALID,
+               "top_k must leave room for top_k + 1 candidates");
+    MF_REQUIRE(temp > 0.f && top_p >= 0.f && top_p <= 1.f && min_p >= 0.f && min_p <= 1.f && n_draws > 0,
+               MF_E_INVALID, "bad sampling parameters");
+    mf::StepState* st = (mf::StepState*)step_state;
+    void* args[] = {(void*)&cand_ids, (void*)&cand_vals, &top_k, &temp, &top_p, &min_p, (void*)&draws, &n_draws,
+                    &st, &out_ids, &flags};
+    MF_CK(launch((const void*)&mf::sample_step_kernel, dim3(1), dim3(32), 0, resolve(stream), args));
+    return MF_OK;
+}
+
 int mf_comm_bulk_ptr(const mf_comm* c, int slot, float** out) {
     MF_REQUIRE(c && out && (slot == 0 || slot == 1), MF_E_INVALID, "bad arguments");
     MF_REQUIRE(c->dev.bulk_floats > 0, MF_E_STATE, "exchange region has no bulk slots");

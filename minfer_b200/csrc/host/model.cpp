@@ -630,7 +630,7 @@ namespace {
 // block of frame ids so two models on one device never replay each other's graphs.
 // 0-2 forward, 3-4 chained decode, 5-6 logits after a batched prefill, 7-8 forward / prefill
 // logits read back as top-k candidates
-constexpr int kFrameKinds = 10;
+constexpr int kFrameKinds = 12;  // kinds 10 / 11: sampled chains (first frame uploads the record)
 int next_frame_base() {
     static int next = 0;
     const int b = next;
@@ -758,6 +758,9 @@ void Qwen3Model::alloc_state() {
     rs.topk_vals = alloc(kTopkMax * 4, "top-k logits");
     rs.topk_ws_bytes = mf_topk_workspace_bytes((int)c.vocab_size, kTopkMax);
     rs.topk_ws = alloc(rs.topk_ws_bytes, "top-k workspace");
+    rs.smp_draws = alloc((S + 1) * 4, "sampling draws");
+    rs.smp_ids = alloc((S + 1) * 4, "sampled ids");
+    rs.smp_flags = alloc(16, "sampling flags");
     check(mf_host_alloc(2 * kTopkMax * 4, &rs.h_topk), "pinned top-k");
     rs.kv_bytes_per_pos = 2ull * c.n_layers * Hkvl * c.d_head * rs.kv_elem;
     if (c.tp_size > 1) {
@@ -946,6 +949,26 @@ size_t Qwen3Model::read_bytes(bool with_logits) const {
 
 void Qwen3Model::issue_frame(bool readback) {
     for (auto& l : layers_) l->cuda_forward(rs_);
+    if (rs_.device_sample) {
+        // top_k + 1 candidates of the (gathered) logits, then the draw: the
+        // record carries the sampled id into the next frame
+        const float* src = (const float*)mf_ptr(rs_.logits);
+        if (rs_.comm) {
+            float* g = nullptr;
+            check(mf_comm_gather_ptr(rs_.comm, &g), "gather buffer");
+            src = g;
+        }
+        int* ids = (int*)mf_ptr(rs_.topk_ids);
+        float* vals = (float*)mf_ptr(rs_.topk_vals);
+        check(mf_topk(src, (int)cfg_.vocab_size, rs_.smp_top_k + 1, ids, vals, mf_ptr(rs_.topk_ws),
+                      rs_.topk_ws_bytes, rs_.stream),
+              "top-k candidates");
+        check(mf_sample_step(ids, vals, rs_.smp_top_k, rs_.smp_temp, rs_.smp_top_p, rs_.smp_min_p,
+                             (const float*)mf_ptr(rs_.smp_draws), rs_.smp_n_draws, rs_.d_step,
+                             (int*)mf_ptr(rs_.smp_ids), (int*)mf_ptr(rs_.smp_flags), rs_.stream),
+              "device sampling");
+        return;
+    }
     // the step record (greedy id) comes back with every host-driven frame;
     // logits (or their top-k candidates) when asked
     if (readback) check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, kStepReadback, rs_.stream), "step readback");
@@ -1039,6 +1062,10 @@ std::vector<uint32_t> Qwen3Model::generate(const std::vector<uint32_t>& prompt, 
                       sampler_->top_k() < (size_t)kTopkMax && !(ht && ht[0] == '1');
     // one candidate beyond top_k shows whether the k-th logit is tied with the next
     rs_.topk_k = cand ? (int)sampler_->top_k() + 1 : 0;
+    // after the first token, sampled decode can run as a device chain (no host
+    // round trip per token; one GPU); MF_DEVICE_SAMPLE=0 keeps the host loop
+    const char* dsm = std::getenv("MF_DEVICE_SAMPLE");
+    const bool dev_smp = cand && !opt.forced && cfg_.tp_size == 1 && !(dsm && dsm[0] == '0');
     struct TopkReset {
         int& k;
         ~TopkReset() { k = 0; }
@@ -1103,6 +1130,34 @@ std::vector<uint32_t> Qwen3Model::generate(const std::vector<uint32_t>& prompt, 
         generated++;
         if (generated == 1) st.ttft = st.prefill_time + (float)(now_s() - t1);
         if (opt.stop_at_eos && fed == cfg_.eos_token_id) break;
+        if (dev_smp && generated == 1 && generated < num_iters) {
+            // the rest as one device chain: frame j forwards the last id and samples
+            // the next with draw j; one frame more than tokens, as the host loop
+            // also forwards the last token. Equal logits among a step's candidates
+            // fall back to the host loop from here (nothing consumed yet).
+            const size_t rest = num_iters - generated;
+            bool tie = false;
+            const std::vector<uint32_t> ids = decode_sampled_chained(fed, (int)tokens.size() - 1, (int)rest + 1,
+                                                                     sampler_->peek_draws(rest + 1), &tie);
+            if (!tie) {
+                size_t used = 0;
+                for (size_t j = 0; j < rest; ++j) {
+                    const uint32_t t = ids[j];
+                    model_bytes += read_bytes(true);
+                    kv_bytes += rs_.kv_bytes_per_pos * tokens.size();
+                    out.push_back(t);
+                    sampler_->add_token(t);
+                    tokens.push_back(t);
+                    generated++;
+                    used++;
+                    if (opt.stop_at_eos && t == cfg_.eos_token_id) break;
+                }
+                sampler_->skip_draws(used);
+                model_bytes += read_bytes(true);
+                kv_bytes += rs_.kv_bytes_per_pos * tokens.size();
+                break;
+            }
+        }
         forward(fed, (int)tokens.size() - 1, true, need_host);
         model_bytes += read_bytes(true);
         kv_bytes += rs_.kv_bytes_per_pos * tokens.size();
@@ -1148,6 +1203,67 @@ GenStats Qwen3Model::benchmark(bool batched_prefill) {
     st.bytes_read = (double)(model_bytes + kv_bytes);
     st.bandwidth = (float)(st.bytes_read / 1e9 / (dt + st.prefill_time));
     return st;
+}
+
+std::vector<uint32_t> Qwen3Model::decode_sampled_chained(uint32_t token, int start_pos, int n,
+                                                        const std::vector<float>& draws, bool* tie) {
+    if (device_ != DeviceType::CUDA) throw std::runtime_error("call set_device(CUDA) first");
+    std::vector<uint32_t> out;
+    if (n <= 0) return out;
+    if (token >= cfg_.vocab_size) throw std::runtime_error("token id outside the vocabulary");
+    if (start_pos < 0 || (size_t)(start_pos + n) > cfg_.user_max_seq_len)
+        throw std::runtime_error("chained decode runs past max_seq_len");
+    if (draws.size() < (size_t)n || draws.size() > cfg_.user_max_seq_len + 1)
+        throw std::invalid_argument("one draw per sampled token");
+    if (sampler_->greedy() || sampler_->penalty_pres() != 0.0f || sampler_->top_k() + 1 > (size_t)kTopkMax)
+        throw std::invalid_argument("device sampling needs temperature > 0, no presence penalty, top_k < 64");
+    check(mf_write(rs_.smp_draws, 0, draws.data(), draws.size() * 4), "upload draws");
+    const int zero[4] = {0, 0, 0, 0};
+    check(mf_write(rs_.smp_flags, 0, zero, sizeof(zero)), "clear sampling flags");
+    rs_.device_sample = true;
+    rs_.smp_top_k = (int)sampler_->top_k();
+    rs_.smp_temp = rp_.temp;
+    rs_.smp_top_p = rp_.top_p;
+    rs_.smp_min_p = rp_.min_p;
+    rs_.smp_n_draws = (int)draws.size();
+    struct Reset {
+        RunState& rs;
+        ~Reset() { rs.device_sample = false; }
+    } reset{rs_};
+    rs_.compute_logits = true;
+    rs_.host_logits = true;  // under tensor parallelism the lm_head gathers every rank's logits
+    rs_.h_step[0] = (int32_t)token;
+    rs_.h_step[1] = start_pos;
+    rs_.h_step[3] = 0;  // the lm_head does not advance the record; the sampling kernel does
+    rs_.h_step[MF_STEP_FRAME] = next_frame();
+    rs_.h_step[MF_STEP_SAMPLE] = 0;
+    for (int i = 0; i < n; ++i) {
+        const int frame = frame_base_ + (i == 0 ? 10 : 11);
+        const int rc = mf_begin_frame_ex(rank_, frame, i == 0 ? 0 : MF_FRAME_NO_UPLOAD);
+        if (rc < 0) check(rc, "begin_frame");
+        if (rc == MF_FRAME_RECORD) {
+            try {
+                issue_frame(false);
+            } catch (...) {
+                mf_abort_frame(rank_);
+                throw;
+            }
+        }
+        check(mf_end_frame_async(rank_), "end_frame");
+    }
+    std::vector<int32_t> ids((size_t)n);
+    int flags[4] = {0, 0, 0, 0};
+    check(mf_copy_to_host_async(ids.data(), mf_ptr(rs_.smp_ids), (size_t)n * 4, rs_.stream), "sampled ids");
+    check(mf_copy_to_host_async(flags, mf_ptr(rs_.smp_flags), sizeof(flags), rs_.stream), "sampling flags");
+    check(mf_copy_to_host_async(rs_.h_step, rs_.d_step, MF_STEP_RECORD_BYTES, rs_.stream), "step readback");
+    check(mf_sync(rank_), "sync");
+    frame_seq_ = rs_.h_step[MF_STEP_FRAME];  // the sampling kernels advanced it on the device
+    rs_.h_step[MF_STEP_SAMPLE] = 0;
+    check_exchange_status();
+    if (flags[0] & 6) throw std::runtime_error("device sampling failed (flags " + std::to_string(flags[0]) + ")");
+    if (tie) *tie = (flags[0] & 1) != 0;
+    out.assign(ids.begin(), ids.end());
+    return out;
 }
 
 uint32_t Qwen3Model::decode_chained(uint32_t token, int start_pos, int n) {

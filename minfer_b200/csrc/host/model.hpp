@@ -114,6 +114,12 @@ struct RunState {
     mf_buf *topk_ids = nullptr, *topk_vals = nullptr, *topk_ws = nullptr;
     size_t topk_ws_bytes = 0;
     void* h_topk = nullptr;  // pinned: kTopkMax ids, then kTopkMax logits
+    // sampling on the device (chained sampled frames): the draws of the run
+    // [max_seq + 1], the sampled ids [max_seq + 1], flags (mf_sample_step)
+    bool device_sample = false;
+    float smp_temp = 0.f, smp_top_p = 1.f, smp_min_p = 0.f;
+    int smp_top_k = 0, smp_n_draws = 0;
+    mf_buf *smp_draws = nullptr, *smp_ids = nullptr, *smp_flags = nullptr;
     int attn_split = 1;
     int cur_pos = 0;
     uint32_t token_id = 0;
@@ -219,6 +225,12 @@ public:
     // of frame i-1 (chained step record), frames are queued back to back with
     // no host round trip. Returns the last greedy id; the caller times it.
     uint32_t decode_chained(uint32_t token, int start_pos, int n);
+    // Sampled decode with the device feeding itself: frame i forwards the id
+    // frame i-1 sampled on the device (mf_sample_step with draws[i]), no host
+    // round trip. Returns the n sampled ids; *tie is set when equal logits
+    // among a step's candidates made the order of equal values decide.
+    std::vector<uint32_t> decode_sampled_chained(uint32_t token, int start_pos, int n, const std::vector<float>& draws,
+                                                 bool* tie);
 
     // Tensor parallelism: after set_device(CUDA), every rank exports its
     // handle, and connects with all ranks' handles ordered by tp_rank.

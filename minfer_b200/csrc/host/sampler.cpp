@@ -18,6 +18,18 @@ Sampler::Sampler(const SamplerParams& p)
 
 void Sampler::add_token(uint32_t token) { seen_.insert(token); }
 
+std::vector<float> Sampler::peek_draws(size_t n) const {
+    std::mt19937_64 rng = rng_;
+    std::uniform_real_distribution<float> dist = dist_;
+    std::vector<float> out(n);
+    for (float& r : out) r = dist(rng);
+    return out;
+}
+
+void Sampler::skip_draws(size_t n) {
+    for (size_t i = 0; i < n; ++i) (void)dist_(rng_);
+}
+
 uint32_t Sampler::sample(const float* logits) {
     const size_t V = p_.vocab_size;
     if (p_.temp == 0.0f) return (uint32_t)(std::max_element(logits, logits + V) - logits);

@@ -43,6 +43,10 @@ public:
     // the top-k, or the k-th equal to the next one, which makes the top-k set
     // itself ambiguous) mean the whole-vocabulary sample() must decide.
     static bool candidates_decisive(const float* vals, size_t n);
+    // the next n draws of the random stream, without consuming them
+    std::vector<float> peek_draws(size_t n) const;
+    // consume n draws (as n sample() calls would)
+    void skip_draws(size_t n);
     bool greedy() const { return p_.temp == 0.0f; }
     size_t top_k() const { return p_.top_k; }
     float penalty_pres() const { return p_.penalty_pres; }

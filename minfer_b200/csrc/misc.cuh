@@ -44,6 +44,84 @@ __global__ void embed_kernel(float* __restrict__ x, const void* __restrict__ emb
     }
 }
 
+// One sampled token on the device, from the candidate list the top-k kernel
+// left (ids / logits sorted by logit, largest first, ties: lower id first):
+// the reference's Sampler::sample after its top-k (src/base/sampler.cpp:52-117):
+// softmax over the top_k, top-p cut, min-p cut, temperature softmax over the
+// kept prefix, then the first candidate whose cumulative probability reaches
+// the draw r = draws[i], i = the record's sample index. The chosen id becomes
+// the record's token (the next frame embeds it); position, frame number and
+// sample index advance. Equal logits among the top_k + 1 candidates (an order
+// the reference's nth_element + sort may not share) set bit 1 of *flags; a
+// sample index outside the draws sets bit 2 and leaves the record as it is.
+constexpr int SAMPLE_MAX_K = 64;
+__global__ void sample_step_kernel(const int* __restrict__ cand_ids, const float* __restrict__ cand_vals, int top_k,
+                                   float temp, float top_p, float min_p, const float* __restrict__ draws,
+                                   int n_draws, StepState* st, int* __restrict__ out_ids, int* flags) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (threadIdx.x != 0) return;
+    const int idx = st->pad[2];
+    if (idx < 0 || idx >= n_draws || top_k < 1 || top_k > SAMPLE_MAX_K) {
+        atomicOr(flags, 2);
+        return;
+    }
+    for (int i = 0; i < top_k; ++i)  // the list holds top_k + 1 candidates
+        if (!(cand_vals[i] != cand_vals[i + 1])) atomicOr(flags, 1);
+    float pr[SAMPLE_MAX_K];
+    const float top = cand_vals[0];
+    int cut = top_k;
+    float acc = 0.f;
+    for (int i = 0; i < cut; ++i) {
+        pr[i] = expf(cand_vals[i] - top);
+        acc += pr[i];
+    }
+    for (int i = 0; i < cut; ++i) pr[i] /= acc;
+    acc = 0.f;
+    for (int i = 0; i < cut; ++i) {
+        acc += pr[i];
+        if (acc >= top_p) {
+            cut = i + 1;
+            break;
+        }
+    }
+    if (min_p > 0.f) {
+        const float thr = top + logf(min_p);
+        for (int i = 0; i < cut; ++i)
+            if (cand_vals[i] < thr) {
+                cut = i;
+                break;
+            }
+    }
+    int id = cand_ids[0];
+    if (cut > 0) {
+        acc = 0.f;
+        for (int i = 0; i < cut; ++i) {
+            pr[i] = expf((cand_vals[i] - top) / temp);
+            acc += pr[i];
+        }
+        for (int i = 0; i < cut; ++i) pr[i] /= acc;
+        const float r = draws[idx];
+        id = cand_ids[cut - 1];
+        acc = 0.f;
+        for (int i = 0; i < cut; ++i) {
+            acc += pr[i];
+            if (acc >= r) {
+                id = cand_ids[i];
+                break;
+            }
+        }
+    } else {
+        atomicOr(flags, 4);  // the filters removed every candidate (the reference throws)
+    }
+    out_ids[idx] = id;
+    st->token = id;
+    st->next_token = id;
+    st->pos += 1;
+    st->frame += 1;
+    st->pad[2] = idx + 1;
+}
+
 __global__ void topk_softmax_kernel(const float* __restrict__ scores, int n_experts, int k, int* __restrict__ ids,
                                     float* __restrict__ weights) {
     pdl_launch_dependents();

@@ -123,6 +123,29 @@ def test_sampled_at_workload_shape(mm):
     m.close()
 
 
+def test_device_sampling_at_workload_shape(mm, monkeypatch):
+    """c1 free-running (no teacher forcing): the device-sampled chain gives the
+    host loop's 64 ids; the agreement with the reference's free-running ids is
+    printed (they may part at a flip the teacher-forced test above explains)."""
+    g, path = load_case("c1")
+    P, G = len(g["prompt"]), len(g["ids"])
+    sp = g["sampler"]
+    prompt = np.array(g["prompt"], np.uint32)
+    rp = mm.RunParams(num_iters=G, max_seq_len=P + G + 2, top_k=sp["top_k"], temp=sp["temp"], top_p=sp["top_p"],
+                      min_p=sp["min_p"], seed=sp["seed"])
+    got = {}
+    for mode in ("device", "host"):
+        if mode == "host":
+            monkeypatch.setenv("MF_DEVICE_SAMPLE", "0")
+        m = mm.Qwen3Model(path, rp).set_device("cuda")
+        ids, _, _ = m.generate(prompt, G)
+        got[mode] = [int(v) for v in ids]
+        m.close()
+    assert got["device"] == got["host"]
+    same = next((i for i, (a, b) in enumerate(zip(got["device"], g["ids"])) if a != b), G)
+    print(f"c1 free-running: device == host for {G} ids; equal to the reference's for the first {same}")
+
+
 def test_moe_expert_ids_at_workload_shape(mm):
     """c3: the 8 expert ids of every layer at every forward (prompt and decode,
     teacher-forced) are the reference's, bit-exact; greedy ids and logits as above."""

@@ -211,3 +211,33 @@ def test_golden_fixtures(Model):
                                 margins=True)
         check_ids(ids, g["ids"], g["margins"], f.name)
         np.testing.assert_allclose(mg, g["margins"], atol=logit_tol(cfg.dtype))
+
+
+@pytest.mark.parametrize("name,kw", [("tiny-bf16", dict(top_k=20, temp=0.7, top_p=0.9, seed=42)),
+                                     ("tiny-f32", dict(top_k=40, temp=1.2, top_p=0.95, min_p=0.05, seed=7)),
+                                     ("tiny-moe", dict(top_k=8, temp=0.9, top_p=1.0, seed=3))])
+def test_device_sampling_matches_host_loop(Model, monkeypatch, name, kw):
+    """Free-running sampled generate: the device chain (top-k candidates,
+    softmax / top-p / min-p / temperature and the draw in a kernel, the id fed
+    to the next frame on the device) gives the host loop's ids, with the same
+    random stream; a second run continues the stream identically."""
+    Qwen3Model, RunParams = Model
+    from minfer_b200.model import random_prompt
+
+    cfg = TINY[name]
+    path = tiny_model(name)
+    P, G = 12, 40
+    prompt = random_prompt(P, cfg.vocab, 17)
+    runs = {}
+    for mode in ("device", "host"):
+        if mode == "host":
+            monkeypatch.setenv("MF_DEVICE_SAMPLE", "0")
+        m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=2 * (P + G) + 2, **kw)).set_device("cuda")
+        first, _, st = m.generate(prompt, G)
+        second, _, _ = m.generate(prompt, G)  # continues the random stream
+        assert st.num_tokens_gen == G
+        runs[mode] = (list(first), list(second))
+        m.close()
+    assert runs["device"] == runs["host"], f"{name}: device {runs['device']} vs host {runs['host']}"
+    assert runs["device"][0] != runs["device"][1]  # the stream moved on
+
