@@ -402,6 +402,35 @@ def measure_long_context(workload: str, ctx: int, steps: int, warmup: int, rank:
             "file_seconds": round(t_gen, 1)}
 
 
+def measure_sampled(workload: str, ctx: int, gen: int, local_rank: int) -> dict:
+    """Sampled decode through the public generate call (the 1.7B workload's
+    sampler: top-k 20, temperature 0.7, top-p 0.9, seed 42) after a ctx-token
+    prompt: tokens/s of the decode loop with the draws on the device (chained
+    frames) and with the host loop (MF_DEVICE_SAMPLE=0); both must give the
+    same ids."""
+    from minfer_b200 import model as mm
+
+    path, _ = prepare_model(workload, 0, 1)
+    rp = mm.RunParams(num_iters=gen, max_seq_len=ctx + gen + 2, top_k=20, temp=0.7, top_p=0.9, seed=42)
+    out = {"workload": f"{workload}, {ctx}-token prompt, {gen} sampled tokens (top-k 20, T 0.7, top-p 0.9)"}
+    ids = {}
+    for mode in ("device", "host"):
+        if mode == "host":
+            os.environ["MF_DEVICE_SAMPLE"] = "0"
+        try:
+            m = mm.Qwen3Model(path, rp, device=local_rank).set_device("cuda")
+            prompt = mm.random_prompt(ctx, m.info.vocab_size, 42)
+            m.generate(prompt[:64], 8)  # warm-up (graphs captured)
+            got, _, st = m.generate(prompt, gen)
+            ids[mode] = [int(v) for v in got]
+            out[f"{mode}_tok_per_s"] = round(st.throughput, 1)
+            m.close()
+        finally:
+            os.environ.pop("MF_DEVICE_SAMPLE", None)
+    out["same_ids"] = ids["device"] == ids["host"]
+    return out
+
+
 def host_cpu() -> dict:
     """The host's CPU as lscpu reports it (model, sockets, physical cores,
     logical CPUs), the CPUs this process may run on, the cgroup CPU quota and
@@ -471,6 +500,7 @@ def main():
     ap.add_argument("--moe-workload", default="qwen3-30b-a3b-bf16", choices=sorted(CONFIGS))
     ap.add_argument("--moe-context", type=int, default=1024)
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE record")
+    ap.add_argument("--no-sampled", action="store_true", help="skip the sampled-decode record")
     ap.add_argument("--llama-bench", action="store_true",
                     help="only the reference's benchmark loop (pp512 + tg128, seed 30) on --workload, this runtime "
                          "and the reference CPU build side by side (one GPU)")
@@ -664,6 +694,13 @@ def main():
         else:
             moe_rec = {"skipped": f"no room for the {args.moe_workload} file under {mp.parent}"}
 
+    sampled = None
+    if world == 1 and not args.no_sampled:
+        try:
+            sampled = measure_sampled("qwen3-1.7b-bf16", 512, 256, local_rank)
+        except Exception as e:  # reported, not fatal
+            sampled = {"error": str(e)[:200]}
+
     if rank == 0:
         cpu = None
         if not args.no_cpu_baseline and world == 1:  # rank 0 at N=1 only (other ranks would compete for cores)
@@ -693,6 +730,8 @@ def main():
             line["long_context"] = long_rec
         if moe_rec:
             line["moe"] = moe_rec
+        if sampled:
+            line["sampled"] = sampled
         if world > 1:
             line["tp"] = {"size": world, "exchange_status": status,
                           "note": "hbm_roofline.achieved_gbs is per GPU; bytes_per_token summed over ranks"}

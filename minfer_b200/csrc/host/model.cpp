@@ -1225,7 +1225,9 @@ std::vector<uint32_t> Qwen3Model::decode_sampled_chained(uint32_t token, int sta
     rs_.smp_temp = rp_.temp;
     rs_.smp_top_p = rp_.top_p;
     rs_.smp_min_p = rp_.min_p;
-    rs_.smp_n_draws = (int)draws.size();
+    // the frames are captured once and replayed: their kernel arguments must
+    // not change between calls, so the bound is the buffer's capacity
+    rs_.smp_n_draws = (int)cfg_.user_max_seq_len + 1;
     struct Reset {
         RunState& rs;
         ~Reset() { rs.device_sample = false; }

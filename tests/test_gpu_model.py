@@ -235,8 +235,9 @@ def test_device_sampling_matches_host_loop(Model, monkeypatch, name, kw):
         m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=2 * (P + G) + 2, **kw)).set_device("cuda")
         first, _, st = m.generate(prompt, G)
         second, _, _ = m.generate(prompt, G)  # continues the random stream
+        third, _, _ = m.generate(prompt[:5], G // 2)  # another length: the replayed frames serve it too
         assert st.num_tokens_gen == G
-        runs[mode] = (list(first), list(second))
+        runs[mode] = (list(first), list(second), list(third))
         m.close()
     assert runs["device"] == runs["host"], f"{name}: device {runs['device']} vs host {runs['host']}"
     assert runs["device"][0] != runs["device"][1]  # the stream moved on
