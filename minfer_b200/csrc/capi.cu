@@ -308,7 +308,7 @@ int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_
     if (q.counter || q.gather_logits) return 0;
     // grouped experts: the SwiGLU form over every selected expert stored here
     const bool grouped = q.expert_ids != nullptr;
-    if (grouped && !(moe_on && xm == mf::X_NORM && ym == mf::Y_SWIGLU && q.ep_n == 0 && q.rows_per_expert > 0 &&
+    if (grouped && !(moe_on && xm == mf::X_NORM && ym == mf::Y_SWIGLU && q.rows_per_expert > 0 &&
                      q.rows_per_expert % 2 == 0 && q.rows % q.rows_per_expert == 0 &&
                      q.rows / q.rows_per_expert <= 32))
         return 0;
@@ -398,6 +398,8 @@ int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_
         p.expert_ids = q.expert_ids;
         p.rows_per_expert = q.rows_per_expert;
         p.expert_bytes = (unsigned long long)q.rows_per_expert * row_bytes;
+        p.ep_lo = q.ep_lo;
+        p.ep_n = q.ep_n;
     }
     void* args[] = {&p};
     if (ks == 1) MF_CK(launch(fn, dim3((unsigned)nblk), dim3((nwc + 1) * 32), smem, st, args));
@@ -408,12 +410,12 @@ int try_gemv_tma(int dtype, int xm, int ym, const mf::GemvParams& q, cudaStream_
 // The TMA-fed grouped expert down projection (moe_down_tma_kernel): 1 when it
 // launched, 0 when left to the register-fed kernel (MF_GEMV_TMA_MOE=0, expert
 // parallelism, rows wider than 10 KB or K beyond 8 vectors per lane), < 0 on error.
-int try_moe_down_tma(int dtype, const mf::GemvParams& q, cudaStream_t st, bool ids_early) {
+int try_moe_down_tma(int dtype, const mf::GemvParams& q, cudaStream_t st, bool ids_early, bool push = false) {
     static const int on = env_int("MF_GEMV_TMA", 1) && env_int("MF_GEMV_TMA_MOE", 1);
     static const long long timeout_ms = env_int("MF_DECODE_TIMEOUT_MS", 1000);
     static const size_t stage_target = (size_t)env_int("MF_MOE_TMA_STAGE_KB", 16) * 1024;
     static const size_t ring_bytes = (size_t)env_int("MF_GEMV_TMA_RING_KB", mf::GT_RING_BYTES / 1024) * 1024;
-    if (!on || q.ep_n != 0 || q.n_slots < 1 || q.n_slots > mf::MD_WARPS) return 0;
+    if (!on || q.n_slots < 1 || q.n_slots > mf::MD_WARPS) return 0;
     const int vec = vec_of(dtype);
     const size_t row_bytes = (size_t)q.K * esz_of(dtype);
     if (row_bytes > 10 * 1024 || row_bytes % 16 != 0) return 0;
@@ -462,6 +464,14 @@ int try_moe_down_tma(int dtype, const mf::GemvParams& q, cudaStream_t st, bool i
     p.status = status;
     p.timeout_ns = (unsigned long long)std::max(1ll, timeout_ms) * 1000000ull;
     p.ids_early = ids_early ? 1 : 0;
+    p.ep_lo = q.ep_lo;
+    p.ep_n = q.ep_n;
+    if (push) {
+        p.push = 1;
+        p.comm = q.comm;
+        p.ar_seq = q.ar_seq;
+        p.step = q.step;
+    }
     void* args[] = {&p};
     MF_CK(launch(fn, dim3((unsigned)nblk), dim3((mf::MD_WARPS + 1) * 32), smem, st, args));
     return 1;
@@ -1550,6 +1560,11 @@ int mf_moe_down_push(const float* h, const void* w_down_local, int dtype, const 
     p.comm = c->dev;
     p.ar_seq = seq;
     p.step = (int*)step_state;
+    MF_REQUIRE(d_ff % 16 == 0 && ((uintptr_t)w_down_local | (uintptr_t)h) % 16 == 0, MF_E_INVALID,
+               "d_ff must be a multiple of 16, weights and h 16-byte aligned");
+    const int tr = try_moe_down_tma(dtype, p, resolve(stream), false, true);
+    if (tr < 0) return tr;
+    if (tr == 1) return MF_OK;
     return run_gemv(dtype, mf::X_PLAIN, mf::Y_MOE_PUSH, p, d_model, resolve(stream));
 }
 

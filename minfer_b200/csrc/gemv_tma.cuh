@@ -77,6 +77,10 @@ struct GemvTmaParams {
     const int* expert_ids;  // [rows / rows_per_expert] device, or null (dense)
     int rows_per_expert;
     unsigned long long expert_bytes;
+    // expert parallelism: only experts [ep_lo, ep_lo + ep_n) are stored here
+    // (expert e at local index e - ep_lo); rows of slots routed elsewhere are
+    // not copied and their outputs are left unused. ep_n == 0: all local.
+    int ep_lo, ep_n;
 };
 
 // Y_PUSH: row `row` of this rank's partial, as a tagged word into every
@@ -146,23 +150,35 @@ __global__ void __launch_bounds__((NWC + 1) * 32, 1) gemv_tma_kernel(const GemvT
                 if (c >= S && !mbar_wait(&empty[s], (uint32_t)((c / S - 1) & 1), deadline, failed)) break;
                 if (*(volatile int*)&abort_s) break;
                 const int rr = min(p.rows_per_stage, nrows - c * p.rows_per_stage);
-                const uint32_t bytes = (uint32_t)(rr * p.row_bytes);
-                mbar_expect_tx(&full[s], bytes);
                 const char* src = p.w + (size_t)(r0 + c * p.rows_per_stage) * p.row_stride + kofs;
-                if (grouped) {  // one copy per run of rows inside one expert
-                    int r = 0;
-                    while (r < rr) {
-                        const int lr = r0 + c * p.rows_per_stage + r;
-                        const int slot = lr / p.rows_per_expert, er = lr - slot * p.rows_per_expert;
-                        const int n = min(rr - r, p.rows_per_expert - er);
-                        bulk_load(gt_smem + (size_t)s * p.stage_bytes + (size_t)r * p.row_bytes,
-                                  p.w + (size_t)eid_s[slot] * p.expert_bytes + (size_t)er * p.row_bytes,
-                                  (uint32_t)(n * p.row_bytes), &full[s]);
-                        r += n;
+                if (grouped) {
+                    // one copy per run of rows inside one expert stored here (the
+                    // bytes announced first: runs of other ranks' experts are skipped)
+                    uint32_t bytes = 0;
+                    for (int pass = 0; pass < 2; ++pass) {
+                        if (pass == 1) mbar_expect_tx(&full[s], bytes);
+                        int r = 0;
+                        while (r < rr) {
+                            const int lr = r0 + c * p.rows_per_stage + r;
+                            const int slot = lr / p.rows_per_expert, er = lr - slot * p.rows_per_expert;
+                            const int n = min(rr - r, p.rows_per_expert - er);
+                            const int e = eid_s[slot] - (p.ep_n ? p.ep_lo : 0);
+                            if (p.ep_n == 0 || (e >= 0 && e < p.ep_n)) {
+                                if (pass == 0) bytes += (uint32_t)(n * p.row_bytes);
+                                else
+                                    bulk_load(gt_smem + (size_t)s * p.stage_bytes + (size_t)r * p.row_bytes,
+                                              p.w + (size_t)e * p.expert_bytes + (size_t)er * p.row_bytes,
+                                              (uint32_t)(n * p.row_bytes), &full[s]);
+                            }
+                            r += n;
+                        }
                     }
                 } else if (ks == 1) {
+                    const uint32_t bytes = (uint32_t)(rr * p.row_bytes);
+                    mbar_expect_tx(&full[s], bytes);
                     bulk_load(gt_smem + (size_t)s * p.stage_bytes, src, bytes, &full[s]);
                 } else {  // the slices of consecutive rows are row_stride apart: one copy per row
+                    mbar_expect_tx(&full[s], (uint32_t)(rr * p.row_bytes));
                     for (int r = 0; r < rr; ++r)
                         bulk_load(gt_smem + (size_t)s * p.stage_bytes + (size_t)r * p.row_bytes,
                                   src + (size_t)r * p.row_stride, (uint32_t)p.row_bytes, &full[s]);
@@ -397,9 +413,20 @@ struct MoeDownTmaParams {
     // dependents launch after it had waited for the router (the grouped
     // gate/up GEMV does), so the router's ids are complete here.
     int ids_early;
+    // expert parallelism: experts [ep_lo, ep_lo + ep_n) are stored here
+    // (ep_n == 0: all). With push, this rank's slots are summed from zero in
+    // slot order and the partial row is sent as tagged words to every rank's
+    // receive slot of exchange ar_seq (the next layer's receive adds the
+    // ranks' partials to the residual); x is then not touched.
+    int ep_lo, ep_n;
+    int push;
+    CommDev comm;
+    int ar_seq;
+    const int* step;
 };
 
 constexpr int MD_WARPS = 8;  // consumer warps = the most slots
+MF_DEVICE bool md_local(const MoeDownTmaParams& p, int e) { return p.ep_n == 0 || (e >= p.ep_lo && e < p.ep_lo + p.ep_n); }
 
 template <typename W, int J>
 __global__ void __launch_bounds__((MD_WARPS + 1) * 32, 1) moe_down_tma_kernel(const MoeDownTmaParams p) {
@@ -431,7 +458,12 @@ __global__ void __launch_bounds__((MD_WARPS + 1) * 32, 1) moe_down_tma_kernel(co
         pdl_launch_dependents();
         if (lane == 0) {
             if (!p.ids_early) pdl_wait();
-            for (int i = 0; i < p.k; ++i) eid_s[i] = __ldcg(p.ids + i);  // from L2: written by the router
+            uint32_t n_loc = 0;
+            for (int i = 0; i < p.k; ++i) {
+                eid_s[i] = __ldcg(p.ids + i);  // from L2: written by the router
+                n_loc += md_local(p, eid_s[i]) ? 1u : 0u;
+            }
+            const int ebase = p.ep_n ? p.ep_lo : 0;
             bool failed = false;
             int c = 0;
             for (; c < nchunks; ++c) {
@@ -440,11 +472,13 @@ __global__ void __launch_bounds__((MD_WARPS + 1) * 32, 1) moe_down_tma_kernel(co
                 if (*(volatile int*)&abort_s) break;
                 const int rr = min(R, nrows - c * R);
                 const uint32_t bytes = (uint32_t)(rr * p.row_bytes);
-                mbar_expect_tx(&full[s], bytes * (uint32_t)p.k);
+                mbar_expect_tx(&full[s], bytes * n_loc);
                 for (int sl = 0; sl < p.k; ++sl)
-                    bulk_load(gt_smem + (size_t)s * p.stage_bytes + (size_t)sl * R * p.row_bytes,
-                              p.w + (size_t)eid_s[sl] * p.expert_bytes + (size_t)(r0 + c * R) * p.row_bytes, bytes,
-                              &full[s]);
+                    if (md_local(p, eid_s[sl]))
+                        bulk_load(gt_smem + (size_t)s * p.stage_bytes + (size_t)sl * R * p.row_bytes,
+                                  p.w + (size_t)(eid_s[sl] - ebase) * p.expert_bytes +
+                                      (size_t)(r0 + c * R) * p.row_bytes,
+                                  bytes, &full[s]);
             }
             if (failed) {
                 atomicOr(p.status, GT_STATUS_TIMEOUT);
@@ -457,12 +491,13 @@ __global__ void __launch_bounds__((MD_WARPS + 1) * 32, 1) moe_down_tma_kernel(co
         return;
     }
 
-    // ---- consumer warp `warp` = slot `warp` (warps past k only release stages)
-    const bool active = warp < p.k;
+    // ---- consumer warp `warp` = slot `warp` (warps past k, and slots whose
+    // expert is stored on another rank, only release stages)
     const int NV = p.K / VEC;
     float xr[J][VEC];
     pdl_launch_dependents();
     pdl_wait();
+    const bool active = warp < p.k && md_local(p, __ldcg(p.ids + warp));
 #pragma unroll
     for (int j = 0; j < J; ++j) {
         const int v = lane + 32 * j;
@@ -542,6 +577,19 @@ __global__ void __launch_bounds__((MD_WARPS + 1) * 32, 1) moe_down_tma_kernel(co
     asm volatile("bar.sync 1, %0;" ::"r"(MD_WARPS * 32) : "memory");
     if (*(volatile int*)&abort_s) return;
     // src/models/qwen3/module.cpp:471-474: x += expert_out * weight, one expert at a time
+    if (p.push) {
+        // this rank's slots only, in slot order, from zero; the receiver adds
+        // the ranks' partials to the residual in rank order
+        const uint32_t tag = comm_tag(__ldcg(p.step + MF_STEP_FRAME), p.ar_seq);
+        for (int u = tid; u < nrows; u += MD_WARPS * 32) {
+            float part = 0.f;
+            for (int sl = 0; sl < p.k; ++sl)
+                if (md_local(p, __ldcg(p.ids + sl))) part = fmaf(ys[(size_t)sl * nrows + u], __ldcg(p.ew + sl), part);
+            const unsigned long long w = tagged(part, tag);
+            for (int r = 0; r < p.comm.tp_size; ++r) st_tagged(p.comm.recv(r, p.ar_seq & 1, p.comm.tp_rank) + r0 + u, w);
+        }
+        return;
+    }
     for (int u = tid; u < nrows; u += MD_WARPS * 32) {
         float xo = __ldcg(p.x + r0 + u);
         for (int sl = 0; sl < p.k; ++sl) xo = fmaf(ys[(size_t)sl * nrows + u], __ldcg(p.ew + sl), xo);
