@@ -397,7 +397,7 @@ def measure_long_context(workload: str, ctx: int, steps: int, warmup: int, rank:
             "prefill_tok_per_s": round(ctx / prefill_s, 1),
             "prefill": "batched (tensor cores)" if batched else "token by token",
             **({"parity_ok": par["ok"], "parity": par} if par else {}), "exchange_status": status,
-            "parallelism": "single" if world == 1 else (f"ep{world}" if info.n_experts > 0 else f"tp{world}"),
+            "parallelism": "single" if world == 1 else (f"ep{world}" if info.expert_parallel else f"tp{world}"),
             "load_seconds": round(t_load, 1),
             "file_seconds": round(t_gen, 1)}
 
@@ -512,7 +512,8 @@ def main():
               "context": args.context, "batch": 1,
               "l2": "inputs larger than L2 (each step streams all weights and the KV cache)",
               "parallelism": "single" if world == 1 else
-              (f"ep{world}" if cfgshape.n_experts > 0 else f"tp{world}")}
+              (f"ep{world}" if cfgshape.n_experts > 0 and (cfgshape.n_kv_heads % world or
+                                                          os.environ.get("MF_MOE_EP") == "1") else f"tp{world}")}
 
     if args.llama_bench:
         llama_bench_main(args)

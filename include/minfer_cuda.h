@@ -329,10 +329,19 @@ int mf_allreduce_swiglu_matmul(float* h, const float* x_res, float* x_out, const
 int mf_allreduce_lm_head(float* logits, const float* x_res, float* x_out, const float* norm_w, float eps,
                          const void* w, int dtype, int vocab, int d_model, int vocab_offset, void* step_state,
                          void* workspace, int gather_logits, mf_comm* c, int seq, void* stream);
+/* Tensor-parallel MoE layer (no reference counterpart): receive the
+ * attention all-reduce (exchange seq) into x_out (as mf_allreduce_rmsnorm_matmul),
+ * then the router GEMV over rmsnorm(x_out) and the top-k as mf_router_topk.
+ * The experts then run on this rank's slice of their FFN rows
+ * (mf_moe_swiglu on x_out, then mf_moe_down_push with every expert local). */
+int mf_allreduce_router_topk(int* ids, float* weights, float* scores, const float* x_res, float* x_out,
+                             const float* norm_w, float eps, const float* w_router, int d_model, int n_experts, int k,
+                             mf_comm* c, int seq, const void* step_state, void* stream);
 /* Expert parallelism (MoE): each rank stores experts [expert_lo,
  * expert_lo + n_local) (expert e at local index e - expert_lo); the router
- * runs on every rank, so all ranks hold the same ids. Slots routed to another
- * rank's experts produce zeros here. mf_moe_swiglu_ep is mf_moe_swiglu over
+ * runs on every rank, so all ranks hold the same ids. h of slots routed to
+ * another rank's experts is left undefined here (the down projection skips
+ * those slots). mf_moe_swiglu_ep is mf_moe_swiglu over
  * the local experts; mf_moe_down_push computes this rank's weighted sum of its
  * experts' down projections (slot order) and sends it as exchange `seq`, to be
  * received by the next mf_allreduce_* call (the residual add happens there). */

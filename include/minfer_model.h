@@ -55,6 +55,8 @@ typedef struct mf_model_info {
     size_t kv_bytes_per_pos;     /* 2 * n_layers * n_kv_heads * d_head * (4, or 2 for a bf16 cache)
                                     (this rank's heads) */
     int tp_rank, tp_size;        /* tensor-parallel position of this process */
+    int expert_parallel;         /* 1: a MoE model split by experts (attention replicated);
+                                    0: one GPU, or rows split (tensor parallelism) */
 } mf_model_info;
 
 /* GenStats (include/minfer/base/stats.hpp:3-15) */

@@ -62,7 +62,8 @@ class mf_model_info(C.Structure):
                 ("weight_dtype", C.c_int), ("untied_head", C.c_int), ("eos_token_id", C.c_uint32),
                 ("rms_norm_eps", C.c_float), ("freq_base", C.c_float),
                 ("read_bytes_logits", C.c_size_t), ("read_bytes_no_logits", C.c_size_t),
-                ("kv_bytes_per_pos", C.c_size_t), ("tp_rank", C.c_int), ("tp_size", C.c_int)]
+                ("kv_bytes_per_pos", C.c_size_t), ("tp_rank", C.c_int), ("tp_size", C.c_int),
+                ("expert_parallel", C.c_int)]
 
 
 class mf_gen_stats(C.Structure):
@@ -144,6 +145,7 @@ CUDA_API = {
     "mf_allreduce_swiglu_matmul": (I, [P, P, P, P, F, P, I, I, I, P, I, P, P]),
     "mf_allreduce_lm_head": (I, [P, P, P, P, F, P, I, I, I, I, P, P, I, P, I, P]),
     "mf_allreduce": (I, [P, P, P, I, P, I, P, P]),
+    "mf_allreduce_router_topk": (I, [P, P, P, P, P, P, F, P, I, I, I, P, I, P, P]),
     "mf_moe_swiglu_ep": (I, [P, P, P, F, P, I, P, I, I, I, I, I, P]),
     "mf_moe_down_push": (I, [P, P, I, P, P, I, I, I, I, I, P, I, P, P]),
     "mf_prefill_gemm": (I, [P, I, P, P, P, I, I, I, I, P, P, P]),

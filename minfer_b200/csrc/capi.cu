@@ -1092,6 +1092,20 @@ int mf_router_topk(int* ids, float* weights, float* scores, const float* x, cons
     return MF_OK;
 }
 
+int mf_allreduce_router_topk(int* ids, float* weights, float* scores, const float* x_res, float* x_out,
+                             const float* norm_w, float eps, const float* w_router, int d_model, int n_experts, int k,
+                             mf_comm* c, int seq, const void* step_state, void* stream) {
+    MF_REQUIRE(ids && weights && scores, MF_E_INVALID, "null argument");
+    MF_REQUIRE(n_experts >= 1 && n_experts <= 256, MF_E_UNSUPPORTED, "n_experts %d (1..256)", n_experts);
+    MF_REQUIRE(k >= 1 && k <= n_experts && k <= 32, MF_E_INVALID, "k %d", k);
+    int rc = mf_allreduce_rmsnorm_matmul(scores, x_res, x_out, norm_w, eps, w_router, MF_F32, n_experts, d_model, c,
+                                         seq, step_state, stream);
+    if (rc) return rc;
+    void* args[] = {(void*)&scores, &n_experts, &k, &ids, &weights};
+    MF_CK(launch((const void*)&mf::topk_softmax_kernel, dim3(1), dim3(32), 0, resolve(stream), args));
+    return MF_OK;
+}
+
 int mf_moe_swiglu(float* h, const float* x, const float* norm_w, float eps, const void* w_gate_up_exps, int dtype,
                   const int* ids, int k, int d_ff, int d_in, void* stream) {
     MF_REQUIRE(h && x && norm_w && w_gate_up_exps && ids, MF_E_INVALID, "null argument");

@@ -138,6 +138,7 @@ int mf_model_info_get(const mf_model* m, mf_model_info* out) {
     out->kv_bytes_per_pos = 2ull * c.n_layers * c.kv_heads_local() * c.d_head * (m->m->kv_dtype() == MF_BF16 ? 2 : 4);
     out->tp_rank = c.tp_rank;
     out->tp_size = c.tp_size;
+    out->expert_parallel = c.ep() ? 1 : 0;
     return MF_OK;
 }
 

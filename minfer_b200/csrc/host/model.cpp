@@ -339,31 +339,49 @@ public:
         // under tensor parallelism (dense) this rank's FFN rows
         // [t*F/T, (t+1)*F/T) and the matching input columns of W_down
         const size_t esz = dtype_size(wg.dtype), row = (size_t)d * esz;
-        const size_t Fl = moe ? F : (size_t)c_.ff_local(), t = moe ? 0 : c_.tp_rank;
-        // MoE: this rank's experts [lo, lo + n) (all of them without expert parallelism)
-        const size_t e_lo = moe ? (size_t)c_.expert_lo() : 0, e_n = moe ? (size_t)c_.experts_local() : 1;
-        const size_t nrows = moe ? e_n * F : Fl;
-        const char* gsrc = (const char*)wg.data + (moe ? e_lo * F * row : t * Fl * row);
-        const char* usrc = (const char*)wu.data + (moe ? e_lo * F * row : t * Fl * row);
-        check(mf_alloc(2 * nrows * row, rank, &wgu_), "alloc gate/up");
-        check(mf_write_2d(wgu_, 0, 2 * row, gsrc, row, row, nrows), "upload gate");
-        check(mf_write_2d(wgu_, row, 2 * row, usrc, row, row, nrows), "upload up");
-        own(wgu_);
-        if (moe)
-            own(wd_ = c_.ep() ? upload_rows(wd, e_lo * d, e_n * d, F * esz, rank) : upload_tensor(wd, rank));
-        else
-            own(wd_ = c_.tp_size == 1 ? upload_tensor(wd, rank)
-                                      : upload_cols(wd, d, F * esz, t * Fl * esz, Fl * esz, rank));
+        const size_t Fl = (size_t)c_.ff_local(), t = c_.attn_split() ? c_.tp_rank : 0;
+        if (moe && c_.moe_tp) {
+            // every expert's FFN rows [t*Fl, (t+1)*Fl) (gate/up interleaved per
+            // expert) and the matching input columns of its down matrix
+            check(mf_alloc(2 * E * Fl * row, rank, &wgu_), "alloc gate/up");
+            check(mf_alloc(E * d * Fl * esz, rank, &wd_), "alloc down");
+            for (size_t e = 0; e < E; ++e) {
+                const size_t src = (e * F + t * Fl) * row, dst = e * 2 * Fl * row;
+                check(mf_write_2d(wgu_, dst, 2 * row, (const char*)wg.data + src, row, row, Fl), "upload gate");
+                check(mf_write_2d(wgu_, dst + row, 2 * row, (const char*)wu.data + src, row, row, Fl), "upload up");
+                check(mf_write_2d(wd_, e * d * Fl * esz, Fl * esz, (const char*)wd.data + (e * d * F + t * Fl) * esz,
+                                  F * esz, Fl * esz, d),
+                      "upload down");
+            }
+            own(wgu_);
+            own(wd_);
+        } else {
+            // MoE: this rank's experts [lo, lo + n) (all of them without expert parallelism)
+            const size_t e_lo = moe ? (size_t)c_.expert_lo() : 0, e_n = moe ? (size_t)c_.experts_local() : 1;
+            const size_t nrows = moe ? e_n * F : Fl;
+            const char* gsrc = (const char*)wg.data + (moe ? e_lo * F * row : t * Fl * row);
+            const char* usrc = (const char*)wu.data + (moe ? e_lo * F * row : t * Fl * row);
+            check(mf_alloc(2 * nrows * row, rank, &wgu_), "alloc gate/up");
+            check(mf_write_2d(wgu_, 0, 2 * row, gsrc, row, row, nrows), "upload gate");
+            check(mf_write_2d(wgu_, row, 2 * row, usrc, row, row, nrows), "upload up");
+            own(wgu_);
+            if (moe)
+                own(wd_ = c_.ep() ? upload_rows(wd, e_lo * d, e_n * d, F * esz, rank) : upload_tensor(wd, rank));
+            else
+                own(wd_ = c_.tp_size == 1 ? upload_tensor(wd, rank)
+                                          : upload_cols(wd, d, F * esz, t * Fl * esz, Fl * esz, rank));
+        }
         const size_t k = moe ? (size_t)c_.n_active_experts : 1, ne = moe ? E : 1;
         read_bytes_ = moe ? fn.bytes + (wg.bytes / ne + wu.bytes / ne + wd.bytes / ne) * k
                           : fn.bytes + 2 * Fl * row + d * Fl * esz;
-        if (c_.ep()) read_bytes_ /= c_.tp_size;  // the k active experts are spread over the ranks
+        // the k active experts are spread over the ranks (expert parallelism) or split in their rows
+        if (moe && c_.tp_size > 1) read_bytes_ /= c_.tp_size;
         if (moe) {
             const TensorView& wr = f.tensor(p + "ffn_gate_inp.weight");
             expect_shape(wr, {E, d});
             expect_f32(wr);
             own(wr_ = upload_tensor(wr, rank));
-            read_bytes_ += c_.ep() ? wr.bytes / c_.tp_size : wr.bytes;
+            read_bytes_ += c_.tp_size > 1 ? wr.bytes / c_.tp_size : wr.bytes;  // replicated: each rank a share
         }
     }
     void cuda_forward(RunState& rs) override {
@@ -391,6 +409,23 @@ public:
         const int k = c_.n_active_experts;
         int* ids = (int*)mf_ptr(rs.expert_ids) + (size_t)layer_ * k;
         float* w = (float*)mf_ptr(rs.expert_w) + (size_t)layer_ * k;
+        if (c_.moe_tp) {
+            // receive the attention all-reduce (exchange 2l) in the router GEMV;
+            // every expert on this rank's FFN rows; its partial goes out as 2l + 1
+            const int Fl = c_.ff_local();
+            float* xo = (float*)mf_ptr(rs.xb[1]);
+            check(mf_allreduce_router_topk(ids, w, (float*)mf_ptr(rs.scores), (const float*)mf_ptr(rs.xb[0]), xo,
+                                           (const float*)mf_ptr(fn_), c_.rms_norm_eps, (const float*)mf_ptr(wr_), d,
+                                           c_.n_experts, k, rs.comm, 2 * layer_, rs.d_step, rs.stream),
+                  "router (all-reduce)");
+            check(mf_moe_swiglu(h, xo, (const float*)mf_ptr(fn_), c_.rms_norm_eps, mf_ptr(wgu_), dtype_, ids, k, Fl, d,
+                                rs.stream),
+                  "expert gate/up (rows of this rank)");
+            check(mf_moe_down_push(h, mf_ptr(wd_), dtype_, ids, w, k, d, Fl, 0, c_.n_experts, rs.comm,
+                                   2 * layer_ + 1, rs.d_step, rs.stream),
+                  "expert down (all-reduce send)");
+            return;
+        }
         if (c_.ep()) {
             // router on every rank (identical ids); this rank's experts only; their
             // weighted sum goes out as exchange `layer`, received by the next layer
@@ -448,7 +483,8 @@ public:
     // (gate/up with the SwiGLU epilogue, down), then every token adds its
     // experts' outputs in slot order
     void moe_prefill(RunState& rs, int n) {
-        const int d = c_.d_model, F = c_.d_ff, E = c_.n_experts, k = c_.n_active_experts;
+        // (F: this rank's rows of every expert under tensor parallelism)
+        const int d = c_.d_model, F = c_.ff_local(), E = c_.n_experts, k = c_.n_active_experts;
         const int El = c_.experts_local();  // under expert parallelism this rank's experts only
         float* X = (float*)mf_ptr(rs.pf_x);
         float* xn = (float*)mf_ptr(rs.pf_xn);
@@ -472,7 +508,7 @@ public:
         check(mf_prefill_gemm_grouped((float*)mf_ptr(rs.pf_y), d, mf_ptr(rs.pf_mhi), mf_ptr(rs.pf_mlo), mf_ptr(wd_),
                                       El, n * k, d, F, grows, gtiles, MF_PREFILL_STORE, nullptr, nullptr, rs.stream),
               "prefill expert down");
-        if (!c_.ep()) {
+        if (c_.tp_size == 1) {
             check(mf_prefill_moe_combine(X, X, (const float*)mf_ptr(rs.pf_y), pos, wts, n, k, d, rs.stream),
                   "prefill expert combine");
         } else {
@@ -646,7 +682,12 @@ Qwen3Model::Qwen3Model(const std::string& path, const RunParams& rp, int rank, i
     if (tp_size < 1 || tp_size > MF_TP_MAX || tp_rank < 0 || tp_rank >= tp_size)
         throw std::invalid_argument("tp_rank/tp_size out of range");
     if (tp_size > 1 && cfg_.n_experts > 0) {
-        if (cfg_.n_experts % tp_size != 0)
+        // tensor parallelism inside every expert when the KV heads and the
+        // expert FFN rows divide over the ranks (MF_MOE_EP=1: expert parallelism)
+        const char* ep_env = std::getenv("MF_MOE_EP");
+        cfg_.moe_tp = !(ep_env && ep_env[0] == '1') && cfg_.n_kv_heads % tp_size == 0 &&
+                      cfg_.d_ff % tp_size == 0 && (cfg_.d_ff / tp_size) % 16 == 0 && 2 * cfg_.n_layers <= 255;
+        if (!cfg_.moe_tp && cfg_.n_experts % tp_size != 0)
             throw std::invalid_argument("expert_count is not divisible by the expert-parallel size");
         if (cfg_.n_layers > 255) throw std::invalid_argument("expert parallelism supports up to 255 layers");
     } else if (tp_size > 1) {

@@ -66,10 +66,13 @@ struct Config {
     // tensor parallelism: this process holds rank tp_rank of tp_size
     int tp_rank = 0, tp_size = 1;
 
-    // MoE models split their experts over the ranks (expert parallelism) and
-    // replicate attention; dense models split attention and FFN (tensor parallelism)
-    bool ep() const { return tp_size > 1 && n_experts > 0; }
-    bool attn_split() const { return tp_size > 1 && n_experts == 0; }
+    // Dense models split attention and FFN (tensor parallelism). MoE models
+    // do the same when the KV heads divide over the ranks (every expert's FFN
+    // rows split like a dense FFN: moe_tp), else they split their experts over
+    // the ranks and replicate attention (expert parallelism).
+    bool moe_tp = false;
+    bool ep() const { return tp_size > 1 && n_experts > 0 && !moe_tp; }
+    bool attn_split() const { return tp_size > 1 && (n_experts == 0 || moe_tp); }
     int heads_local() const { return attn_split() ? n_heads / tp_size : n_heads; }
     int kv_heads_local() const { return attn_split() ? n_kv_heads / tp_size : n_kv_heads; }
     int ff_local() const { return attn_split() ? d_ff / tp_size : d_ff; }

@@ -211,7 +211,7 @@ class Qwen3Model:
 
     def kv(self, layer: int, n_pos: int):
         # tensor parallelism splits the KV heads; expert parallelism (MoE) keeps them all
-        kvh = self.info.n_kv_heads if self.info.n_experts > 0 else self.info.n_kv_heads // self.info.tp_size
+        kvh = self.info.n_kv_heads if self.info.expert_parallel else self.info.n_kv_heads // self.info.tp_size
         n = n_pos * kvh * self.info.d_head
         k = np.zeros(n, dtype=np.float32)
         v = np.zeros(n, dtype=np.float32)

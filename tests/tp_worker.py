@@ -211,6 +211,13 @@ def main():
         ev = check_model(n, rank, world)
         if rank == 0:
             print(f"tp{world} {n}: ok ({ev} tolerance events)", flush=True)
+        if TINY[n].n_experts > 0 and TINY[n].n_kv_heads % world == 0:
+            # the same MoE model split by experts instead of by rows
+            os.environ["MF_MOE_EP"] = "1"
+            ev = check_model(n, rank, world)
+            os.environ.pop("MF_MOE_EP", None)
+            if rank == 0:
+                print(f"ep{world} {n}: ok ({ev} tolerance events)", flush=True)
     dist.barrier()
     dist.destroy_process_group()
 
