@@ -181,6 +181,43 @@ int mf_sample_candidates(const float* logits, size_t vocab, const mf_run_params*
  * std::mt19937(seed) + std::uniform_int_distribution<>(0, vocab-1). */
 int mf_random_prompt(int seed, uint32_t vocab, size_t n, uint32_t* out);
 
+/* ---- tokenizer (Qwen3Tokenizer, include/minfer/models/qwen3/tokenizer.hpp;
+ * src/models/qwen3/tokenizer.cpp). Host only, no GPU involved. Functions that
+ * return bytes or ids write at most `cap` of them and set *n to the full count
+ * (call again with a larger buffer when *n > cap). */
+typedef struct mf_tokenizer mf_tokenizer;
+
+/* Qwen3Tokenizer::Qwen3Tokenizer (tokenizer.cpp:12-41) from the GGUF keys
+ * tokenizer.ggml.{tokens, merges, token_type, eos_token_id,
+ * padding_token_id} and tokenizer.chat_template (the keys the reference's
+ * tokenizer test reads, tests/src/qwen3/tokenizer/tokenizer.cpp:20-25). */
+int mf_tokenizer_load(const char* gguf_path, mf_tokenizer** out);
+/* The same from arrays: tokens[i] has token_lens[i] bytes (byte form), merges
+ * are "left right" byte strings. MF_E_INVALID for mismatched lengths or a
+ * merge without a space (tokenizer.cpp:28-30,124-128). */
+int mf_tokenizer_create(const char* const* tokens, const size_t* token_lens, const uint32_t* token_types,
+                        size_t n_tokens, const char* const* merges, const size_t* merge_lens, size_t n_merges,
+                        const char* chat_template, uint32_t eos_id, uint32_t pad_id, mf_tokenizer** out);
+void mf_tokenizer_free(mf_tokenizer* t);
+int mf_tokenizer_info(const mf_tokenizer* t, size_t* vocab_size, uint32_t* eos_id, uint32_t* pad_id);
+/* encode (tokenizer.cpp:45-62). MF_E_INVALID when the vocabulary lacks a byte
+ * or merged string the text needs (the reference throws there). */
+int mf_tokenizer_encode(const mf_tokenizer* t, const char* text, size_t len, uint32_t* ids, size_t cap, size_t* n);
+/* decode (tokenizer.cpp:76-87): unused tokens decode as "<UNK>";
+ * MF_E_INVALID for an id past the vocabulary. */
+int mf_tokenizer_decode(const mf_tokenizer* t, const uint32_t* ids, size_t n_ids, char* out, size_t cap, size_t* n);
+/* The pieces encode splits the text into (regex_split, tokenizer.cpp:176-226):
+ * ends[i] = byte offset one past piece i. */
+int mf_tokenizer_pre_split(const mf_tokenizer* t, const char* text, size_t len, size_t* ends, size_t cap, size_t* n);
+/* apply_chat_template (tokenizer.cpp:291-335): messages_json is a JSON array
+ * of {"role", "content", "reasoning_content"?, "tool_calls"?: [{"name",
+ * "arguments"}]}, tools_json a JSON array of {"name", "description",
+ * "parameters"} (or NULL for none), the objects the reference builds from its
+ * Message/Tool structs. MF_E_STATE for errors the template raises,
+ * MF_E_UNSUPPORTED for template constructs or polyfills not built. */
+int mf_tokenizer_apply_chat_template(const mf_tokenizer* t, const char* messages_json, const char* tools_json,
+                                     int add_generation_prompt, char* out, size_t cap, size_t* n);
+
 #ifdef __cplusplus
 }
 #endif

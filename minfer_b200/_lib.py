@@ -203,6 +203,14 @@ HOST_API = {
     "mf_model_kv": (I, [P, I, P, P, I]),
     "mf_model_x": (I, [P, P]),
     "mf_random_prompt": (I, [I, U32, SZ, P]),
+    "mf_tokenizer_load": (I, [C.c_char_p, P]),
+    "mf_tokenizer_create": (I, [P, P, P, SZ, P, P, SZ, C.c_char_p, U32, U32, P]),
+    "mf_tokenizer_free": (None, [P]),
+    "mf_tokenizer_info": (I, [P, P, P, P]),
+    "mf_tokenizer_encode": (I, [P, C.c_char_p, SZ, P, SZ, P]),
+    "mf_tokenizer_decode": (I, [P, P, SZ, C.c_char_p, SZ, P]),
+    "mf_tokenizer_pre_split": (I, [P, C.c_char_p, SZ, P, SZ, P]),
+    "mf_tokenizer_apply_chat_template": (I, [P, C.c_char_p, C.c_char_p, I, C.c_char_p, SZ, P]),
     "mf_sample": (I, [P, SZ, P, P, SZ, SZ, P]),
     "mf_sample_candidates": (I, [P, SZ, P, SZ, P]),
 }

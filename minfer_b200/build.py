@@ -32,7 +32,7 @@ CXX_FLAGS = ["-std=c++17", "-O3", "-march=x86-64-v3", "-fPIC", "-Wall", "-Wextra
 CUDA_SOURCES = ["capi.cu", "attention.cu", "attn_noalloc.cu", "gemv_f32.cu", "gemv_f16.cu", "gemv_bf16.cu",
                 "gemv_tma_f32.cu", "gemv_tma_f16.cu", "gemv_tma_bf16.cu",
                 "gemv_tp_f32.cu", "gemv_tp_f16.cu", "gemv_tp_bf16.cu", "prefill.cu", "prefill_moe.cu"]
-HOST_SOURCES = ["gguf.cpp", "sampler.cpp", "model.cpp", "capi_model.cpp"]
+HOST_SOURCES = ["gguf.cpp", "sampler.cpp", "model.cpp", "capi_model.cpp", "tokenizer.cpp", "chat_template.cpp"]
 
 LIBMFCUDA = LIB / "libmfcuda.so"
 LIBHOST = LIB / "libminfer_host.so"
@@ -89,7 +89,7 @@ def build_cuda(force: bool = False, jobs: int = 8) -> Path:
 
 def build_host(force: bool = False, jobs: int = 8) -> Path:
     OBJ.mkdir(exist_ok=True)
-    hdrs = sorted(HOST.glob("*.hpp")) + sorted(INCLUDE.glob("*.h"))
+    hdrs = sorted(HOST.glob("*.hpp")) + sorted(HOST.glob("*.inc")) + sorted(INCLUDE.glob("*.h"))
     todo, objs = [], []
     for src in HOST_SOURCES:
         s = HOST / src

@@ -9,9 +9,13 @@
 
 #include "minfer_model.h"
 #include "model.hpp"
+#include "tokenizer.hpp"
 
 struct mf_model {
     std::unique_ptr<minfer::Qwen3Model> m;
+};
+struct mf_tokenizer {
+    std::unique_ptr<minfer::Qwen3Tokenizer> t;
 };
 
 namespace {
@@ -327,6 +331,112 @@ int mf_random_prompt(int seed, uint32_t vocab, size_t n, uint32_t* out) {
     std::mt19937 gen(seed);
     std::uniform_int_distribution<> distrib(0, (int)vocab - 1);
     for (size_t i = 0; i < n; ++i) out[i] = (uint32_t)distrib(gen);
+    return MF_OK;
+}
+
+// ---- tokenizer
+
+#define TOK_TRY(...)                                    \
+    try {                                               \
+        g_host_err[0] = 0;                              \
+        __VA_ARGS__;                                    \
+    } catch (const std::domain_error& e) {              \
+        return herr(MF_E_UNSUPPORTED, e.what());        \
+    } catch (const std::invalid_argument& e) {          \
+        return herr(MF_E_INVALID, e.what());            \
+    } catch (const std::out_of_range& e) {              \
+        return herr(MF_E_INVALID, e.what());            \
+    } catch (const std::bad_alloc&) {                   \
+        return herr(MF_E_OOM, "host allocation failed"); \
+    } catch (const std::exception& e) {                 \
+        return herr(MF_E_STATE, e.what());              \
+    }
+
+namespace {
+size_t put_bytes(const std::string& s, char* out, size_t cap) {
+    if (out) std::memcpy(out, s.data(), std::min(s.size(), cap));
+    return s.size();
+}
+}  // namespace
+
+int mf_tokenizer_load(const char* gguf_path, mf_tokenizer** out) {
+    if (!gguf_path || !out) return herr(MF_E_INVALID, "null argument");
+    TOK_TRY({
+        minfer::GGUFFile f;
+        if (f.open(gguf_path) != 0) return herr(MF_E_INVALID, f.error().c_str());
+        auto t = std::make_unique<mf_tokenizer>();
+        t->t = minfer::Qwen3Tokenizer::from_gguf(f);
+        *out = t.release();
+    });
+    return MF_OK;
+}
+
+int mf_tokenizer_create(const char* const* tokens, const size_t* token_lens, const uint32_t* token_types,
+                        size_t n_tokens, const char* const* merges, const size_t* merge_lens, size_t n_merges,
+                        const char* chat_template, uint32_t eos_id, uint32_t pad_id, mf_tokenizer** out) {
+    if (!out || (n_tokens && (!tokens || !token_lens || !token_types)) || (n_merges && (!merges || !merge_lens)))
+        return herr(MF_E_INVALID, "null argument");
+    TOK_TRY({
+        std::vector<std::string> tk(n_tokens), mg(n_merges);
+        for (size_t i = 0; i < n_tokens; ++i) tk[i].assign(tokens[i], token_lens[i]);
+        for (size_t i = 0; i < n_merges; ++i) mg[i].assign(merges[i], merge_lens[i]);
+        std::vector<uint32_t> ty(token_types, token_types + n_tokens);
+        auto t = std::make_unique<mf_tokenizer>();
+        t->t = std::make_unique<minfer::Qwen3Tokenizer>(tk, mg, ty, chat_template ? chat_template : "", eos_id, pad_id);
+        *out = t.release();
+    });
+    return MF_OK;
+}
+
+void mf_tokenizer_free(mf_tokenizer* t) { delete t; }
+
+int mf_tokenizer_info(const mf_tokenizer* t, size_t* vocab_size, uint32_t* eos_id, uint32_t* pad_id) {
+    if (!t) return herr(MF_E_INVALID, "null tokenizer");
+    if (vocab_size) *vocab_size = t->t->vocab_size();
+    if (eos_id) *eos_id = t->t->eos_id();
+    if (pad_id) *pad_id = t->t->pad_id();
+    return MF_OK;
+}
+
+int mf_tokenizer_encode(const mf_tokenizer* t, const char* text, size_t len, uint32_t* ids, size_t cap, size_t* n) {
+    if (!t || !n || (len && !text) || (cap && !ids)) return herr(MF_E_INVALID, "null argument");
+    TOK_TRY({
+        std::vector<uint32_t> v;
+        try {
+            v = t->t->encode(std::string(text ? text : "", len));
+        } catch (const std::runtime_error& e) {  // a byte or merged string missing from the vocabulary
+            return herr(MF_E_INVALID, e.what());
+        }
+        std::copy(v.begin(), v.begin() + (long)std::min(v.size(), cap), ids);
+        *n = v.size();
+    });
+    return MF_OK;
+}
+
+int mf_tokenizer_decode(const mf_tokenizer* t, const uint32_t* ids, size_t n_ids, char* out, size_t cap, size_t* n) {
+    if (!t || !n || (n_ids && !ids) || (cap && !out)) return herr(MF_E_INVALID, "null argument");
+    TOK_TRY({ *n = put_bytes(t->t->decode(std::vector<uint32_t>(ids, ids + n_ids)), out, cap); });
+    return MF_OK;
+}
+
+int mf_tokenizer_pre_split(const mf_tokenizer* t, const char* text, size_t len, size_t* ends, size_t cap, size_t* n) {
+    if (!t || !n || (len && !text) || (cap && !ends)) return herr(MF_E_INVALID, "null argument");
+    TOK_TRY({
+        const auto v = t->t->pre_split(std::string(text ? text : "", len));
+        for (size_t i = 0; i < v.size() && i < cap; ++i) ends[i] = v[i].second;
+        *n = v.size();
+    });
+    return MF_OK;
+}
+
+int mf_tokenizer_apply_chat_template(const mf_tokenizer* t, const char* messages_json, const char* tools_json,
+                                     int add_generation_prompt, char* out, size_t cap, size_t* n) {
+    if (!t || !messages_json || !n || (cap && !out)) return herr(MF_E_INVALID, "null argument");
+    TOK_TRY({
+        *n = put_bytes(t->t->apply_chat_template_json(messages_json, tools_json ? tools_json : "",
+                                                      add_generation_prompt != 0),
+                       out, cap);
+    });
     return MF_OK;
 }
 

@@ -1,0 +1,224 @@
+"""The host tokenizer (no GPU) against the reference's own tokenizer.
+
+Golden vectors (tests/golden/tokenizer_cases.json, made by
+tests/golden/make_tokenizer_golden.py from the reference's tokenizer.cpp
+compiled with its vendored chat-template engine): for every text the pieces of
+the pre-split and the ids; for every chat case the rendered prompt. Where the
+reference build is present (oracle/_ref/libtokenizer_ref.so) seeded random
+texts are compared live as well. The reference's own test is the
+encode -> decode round trip (tests/src/qwen3/tokenizer/tokenizer.cpp:45-67),
+run here over every text.
+"""
+import json
+import random
+from pathlib import Path
+
+import pytest
+
+from oracle import tokenizer_ref
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(scope="module")
+def vocab():
+    return json.loads((GOLDEN / "tokenizer_vocab.json").read_text())
+
+
+@pytest.fixture(scope="module")
+def cases():
+    return json.loads((GOLDEN / "tokenizer_cases.json").read_text())
+
+
+def _args(v):
+    return ([bytes.fromhex(t) for t in v["tokens"]], [bytes.fromhex(m) for m in v["merges"]], v["types"])
+
+
+@pytest.fixture(scope="module")
+def toks(vocab):
+    from minfer_b200.tokenizer import Qwen3Tokenizer
+
+    tokens, merges, types = _args(vocab)
+    return {name: Qwen3Tokenizer.from_vocab(tokens, merges, types, tmpl, vocab["eos"], vocab["pad"])
+            for name, tmpl in vocab["templates"].items()}
+
+
+def _chat_inputs(c):
+    # the JSON the reference builds from its Message/Tool structs
+    msgs = []
+    for m in c["messages"]:
+        d = {k: v for k, v in m.items() if k != "tool_calls"}
+        if "tool_calls" in m:
+            d["tool_calls"] = [{"name": n, "arguments": json.loads(a)} for n, a in m["tool_calls"]]
+        msgs.append(d)
+    tools = [dict(t, parameters=json.loads(t["parameters"])) for t in c["tools"]]
+    return msgs, tools
+
+
+def test_golden_pieces_and_ids(toks, cases):
+    t = toks["chatml_min"]
+    for c in cases["texts"]:
+        b = bytes.fromhex(c["text"])
+        assert [len(p) for p in t.pre_split(b)] == c["pieces"], b
+        assert t.encode(b) == c["ids"], b
+
+
+def test_round_trip(toks, cases):
+    t = toks["chatml_min"]
+    for c in cases["texts"]:
+        b = bytes.fromhex(c["text"])
+        assert t.decode(t.encode(b)) == b
+    assert t.encode("") == [] and t.decode([]) == b""
+
+
+def test_golden_chat_templates(toks, cases):
+    for c in cases["chats"]:
+        msgs, tools = _chat_inputs(c)
+        assert toks[c["template"]].apply_chat_template(msgs, tools, c["add_generation_prompt"]) == c["expected"], c
+
+
+def test_message_structs(toks, cases):
+    """The Message/Tool mirror builds the same JSON as the reference."""
+    from minfer_b200.tokenizer import Message, Tool
+
+    c = next(c for c in cases["chats"] if c["template"] == "chatml_tools" and c["tools"] and
+             any("tool_calls" in m for m in c["messages"]))
+    msgs = [Message(m["role"], m["content"], m.get("reasoning_content", ""), [tuple(x) for x in m.get("tool_calls", [])])
+            for m in c["messages"]]
+    tools = [Tool(t["name"], t["description"], t["parameters"]) for t in c["tools"]]
+    assert toks["chatml_tools"].apply_chat_template(msgs, tools, c["add_generation_prompt"]) == c["expected"]
+
+
+def _random_texts(seed, n):
+    rng = random.Random(seed)
+    blocks = [(0x20, 0x7E), (0xA0, 0x24F), (0x370, 0x3FF), (0x400, 0x4FF), (0x600, 0x6FF), (0x900, 0x97F),
+              (0x3040, 0x30FF), (0x4E00, 0x4FFF), (0xAC00, 0xAD00), (0x2000, 0x206F), (0x1F300, 0x1F64F),
+              (0xFF00, 0xFFEF), (0x660, 0x669), (0x2160, 0x2188)]
+    specials = ["<|im_start|>", "<|im_end|>", "<think>", "</tool_call>", "<|unused_1|>"]
+    out = []
+    for _ in range(n):
+        parts = []
+        for _ in range(rng.randint(1, 30)):
+            r = rng.random()
+            if r < 0.35:
+                parts.append(rng.choice(" \t\n\r  \n\n'sSdllve"))
+            elif r < 0.4:
+                parts.append(rng.choice(specials))
+            else:
+                lo, hi = rng.choice(blocks)
+                parts.append(chr(rng.randint(lo, hi)))
+        b = "".join(parts).encode("utf-8", "surrogatepass")
+        if rng.random() < 0.1:
+            i = rng.randint(0, len(b))
+            b = b[:i] + bytes([rng.choice([0x80, 0xBF, 0xC2, 0xE0, 0xED, 0xF0, 0xF5, 0xFF])]) + b[i:]
+        out.append(b)
+    return out
+
+
+@pytest.mark.skipif(not tokenizer_ref.available(), reason="the reference tokenizer build (oracle/_ref) is absent")
+def test_live_reference_random_texts(vocab, toks):
+    tokens, merges, types = _args(vocab)
+    ref = tokenizer_ref.RefTokenizer(tokens, types, merges, vocab["templates"]["chatml_min"], vocab["eos"],
+                                     vocab["pad"])
+    t = toks["chatml_min"]
+    for b in _random_texts(2024, 600):
+        assert [len(p) for p in t.pre_split(b)] == ref.split(b), b
+        assert t.encode(b) == ref.encode(b), b
+
+
+@pytest.mark.skipif(not tokenizer_ref.available(), reason="the reference tokenizer build (oracle/_ref) is absent")
+def test_live_reference_random_chats(vocab, toks):
+    from minfer_b200._lib import MinferError
+
+    tokens, merges, types = _args(vocab)
+    rng = random.Random(5)
+    words = ["hi", "Oslo", "2+2", "it's", "世界", "", " ", "\n", "<b>&'\"", "x" * 30]
+    for name in ("chatml_min", "chatml_tools", "exprs"):
+        ref = tokenizer_ref.RefTokenizer(tokens, types, merges, vocab["templates"][name], vocab["eos"], vocab["pad"])
+        for _ in range(25):
+            msgs = []
+            for _ in range(rng.randint(1, 5)):
+                role = rng.choice(["system", "user", "assistant", "user"])
+                m = {"role": role, "content": " ".join(rng.choice(words) for _ in range(rng.randint(0, 4)))}
+                if role == "assistant" and rng.random() < 0.4:
+                    m["reasoning_content"] = rng.choice(words) + "\n"
+                msgs.append(m)
+            gen = rng.random() < 0.5
+            try:
+                expected = ref.chat(msgs, [], gen)
+            except RuntimeError:  # the template fails on these messages (an empty content's [-3:]): so does ours
+                with pytest.raises(MinferError):
+                    toks[name].apply_chat_template(msgs, [], gen)
+                continue
+            assert toks[name].apply_chat_template(msgs, [], gen) == expected, (name, msgs)
+
+
+def test_reference_error_behaviour(vocab):
+    from minfer_b200._lib import MF_E_INVALID, MinferError
+    from minfer_b200.tokenizer import Qwen3Tokenizer
+
+    tokens, merges, types = _args(vocab)
+    with pytest.raises(MinferError) as e:  # token and type arrays of different lengths
+        Qwen3Tokenizer.from_vocab(tokens, merges, types[:-1])
+    assert e.value.code == MF_E_INVALID
+    with pytest.raises(MinferError):  # a merge rule without a space
+        Qwen3Tokenizer.from_vocab(tokens, merges + [b"ab"], types)
+    t = Qwen3Tokenizer.from_vocab(tokens, merges, types, "", vocab["eos"], vocab["pad"])
+    with pytest.raises(MinferError):  # an id past the vocabulary
+        t.decode([len(tokens)])
+    unused = types.index(5)
+    assert t.decode_token(unused) == b"<UNK>"
+    assert t.decode_token(vocab["eos"]) == b"<|im_end|>"
+    # a vocabulary without the byte the text needs: the reference throws
+    no_z = Qwen3Tokenizer.from_vocab([b"a", b"b"], [], [1, 1])
+    assert no_z.encode("abba") == [0, 1, 1, 0]
+    with pytest.raises(MinferError) as e:
+        no_z.encode("abz")
+    assert e.value.code == MF_E_INVALID
+
+
+def test_template_errors(vocab):
+    from minfer_b200._lib import MF_E_STATE, MF_E_UNSUPPORTED, MinferError
+    from minfer_b200.tokenizer import Qwen3Tokenizer
+
+    tokens, merges, types = _args(vocab)
+    raising = "{{ raise_exception('too many messages') if messages | length > 2 else 'ok' }}"
+    t = Qwen3Tokenizer.from_vocab(tokens, merges, types, raising)
+    assert t.apply_chat_template([{"role": "user", "content": "x"}]) == "ok"
+    with pytest.raises(MinferError) as e:
+        t.apply_chat_template([{"role": "user", "content": "x"}] * 3)
+    assert e.value.code == MF_E_STATE and "too many messages" in str(e.value)
+    macro = "{% macro f(x) %}{{ x }}{% endmacro %}{{ f(1) }}"
+    with pytest.raises(MinferError) as e:
+        Qwen3Tokenizer.from_vocab(tokens, merges, types, macro).apply_chat_template([{"role": "user", "content": "x"}])
+    assert e.value.code in (MF_E_UNSUPPORTED, MF_E_STATE)
+    # a template that cannot show tools needs the tools polyfill: refused, not rendered differently
+    plain = "{% for m in messages %}{{ m.role }}: {{ m.content }}\n{% endfor %}"
+    with pytest.raises(MinferError) as e:
+        Qwen3Tokenizer.from_vocab(tokens, merges, types, plain).apply_chat_template(
+            [{"role": "user", "content": "x"}], [{"name": "f", "description": "d", "parameters": {}}])
+    assert e.value.code == MF_E_UNSUPPORTED
+
+
+def test_load_from_gguf_model():
+    """mf_tokenizer_load reads the tokenizer keys of a model file (the tiny
+    synthetic models carry a printable-ASCII vocabulary whose other bytes are
+    spelled <0xNN>, so text with those bytes cannot be encoded, by the
+    reference either)."""
+    from conftest import TINY, tiny_model
+    from minfer_b200._lib import MinferError
+    from minfer_b200.gguf_synth import synth_vocab
+    from minfer_b200.tokenizer import Qwen3Tokenizer
+
+    cfg = TINY["tiny-bf16"]
+    t = Qwen3Tokenizer.from_gguf(tiny_model("tiny-bf16"))
+    toks, types, merges, eos, pad = synth_vocab(cfg.vocab, cfg.seed)
+    assert (t.vocab_size, t.eos_id, t.pad_id) == (cfg.vocab, eos, pad)
+    ids = t.encode("Hello!")
+    assert t.decode(ids) == b"Hello!"
+    with pytest.raises(MinferError):
+        t.encode("two words")
+    if tokenizer_ref.available():
+        ref = tokenizer_ref.RefTokenizer(toks, types, merges, "", eos, pad)
+        for s in [b"Hello!", b"a1b2c3", b"<|special_0|>xyz", b"(((!!!)))"]:
+            assert t.encode(s) == ref.encode(s)
