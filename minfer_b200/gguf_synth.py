@@ -53,6 +53,11 @@ class Qwen3Shape:
     # A file with n_layers < rng_layers is the depth-reduced prefix of that
     # model: the same embedding, layers 0..n_layers-1 and lm_head weights.
     rng_layers: int = 0
+    # vocabulary: False = printable-ASCII placeholder strings (ids-only
+    # workloads); True = a byte-level BPE vocabulary (all 256 bytes, merges
+    # whose results are vocabulary entries, and the Qwen3 chat specials), so
+    # the file's tokenizer encodes any text
+    byte_vocab: bool = False
 
     def with_(self, **kw) -> "Qwen3Shape":
         return dataclasses.replace(self, **kw)
@@ -121,12 +126,15 @@ def cast_weights(a: np.ndarray, dtype: str) -> np.ndarray:
     raise ValueError(dtype)
 
 
-def synth_vocab(n_vocab: int, seed: int) -> tuple[list[bytes], list[int], list[bytes], int, int]:
+def synth_vocab(n_vocab: int, seed: int, byte_vocab: bool = False) -> tuple[list[bytes], list[int], list[bytes], int, int]:
     """Byte tokens + seeded random merges + special tokens.
 
     Returns (tokens, token_types, merges, eos_id, pad_id). Token strings are
-    printable ASCII so every metadata string is valid UTF-8.
+    printable ASCII so every metadata string is valid UTF-8 (byte_vocab:
+    raw bytes, see synth_byte_vocab).
     """
+    if byte_vocab:
+        return synth_byte_vocab(n_vocab, seed)
     rng = np.random.Generator(np.random.PCG64(seed ^ 0x5EED))
     toks: list[bytes] = []
     for b in range(256):
@@ -155,6 +163,39 @@ def synth_vocab(n_vocab: int, seed: int) -> tuple[list[bytes], list[int], list[b
         toks.append(b"<|pad_%d|>" % len(toks))
         types.append(5)
     return toks[:n_vocab], types[:n_vocab], merges, eos, pad
+
+
+def synth_byte_vocab(n_vocab: int, seed: int) -> tuple[list[bytes], list[int], list[bytes], int, int]:
+    """A byte-level BPE vocabulary in the byte form the reference reads: the
+    256 single bytes, seeded merges of two existing entries (mostly letters,
+    digits and a leading space) whose results are new entries, then the
+    specials <|endoftext|> (pad), <|im_start|>, <|im_end|> (eos) as control
+    tokens and unused padding ids."""
+    rng = np.random.Generator(np.random.PCG64(seed ^ 0xB17E))
+    toks = [bytes([b]) for b in range(256)]
+    seen = set(toks)
+    alpha = [bytes([c]) for c in b"etaoinshrdlucmfwypvbgkqjxz ETAOINSHRD0123456789.,"]
+    specials = [b"<|endoftext|>", b"<|im_start|>", b"<|im_end|>"]
+    n_normal = n_vocab - len(specials) - max(2, n_vocab // 64)
+    merges: list[bytes] = []
+    while len(toks) < n_normal:
+        pool = alpha if rng.random() < 0.5 else toks[256:] or alpha
+        a = pool[int(rng.integers(len(pool)))]
+        b = alpha[int(rng.integers(len(alpha)))] if rng.random() < 0.7 else toks[int(rng.integers(256, len(toks)))] if len(toks) > 256 else alpha[0]
+        m = a + b
+        if m in seen or len(m) > 8:
+            continue
+        seen.add(m)
+        toks.append(m)
+        merges.append(a + b" " + b)
+    types = [1] * len(toks)
+    for sp in specials:
+        toks.append(sp)
+        types.append(3)
+    while len(toks) < n_vocab:
+        toks.append(b"<|unused_%d|>" % len(toks))
+        types.append(5)
+    return toks, types, merges, toks.index(b"<|im_end|>"), toks.index(b"<|endoftext|>")
 
 
 class _Writer:
@@ -286,7 +327,7 @@ def _layout(cfg: Qwen3Shape) -> tuple[bytes, list[tuple], list[int], int, int]:
     import io
 
     plan = tensor_plan(cfg)
-    toks, types, merges, eos, pad = synth_vocab(cfg.vocab, cfg.seed)
+    toks, types, merges, eos, pad = synth_vocab(cfg.vocab, cfg.seed, cfg.byte_vocab)
     fh = io.BytesIO()
     w = _Writer(fh)
     kvs: list[tuple] = []

@@ -59,6 +59,15 @@ def init(n_ranks: int = 1, devices: list[int] | None = None) -> None:
     _initialised.add(key)
 
 
+@dataclasses.dataclass
+class TextResult:
+    formatted: str          # the chat-template prompt
+    prompt_ids: list[int]
+    ids: list[int]          # generated ids (EOS included when reached)
+    text: bytes             # the generated ids decoded
+    stats: "GenStats"
+
+
 class Qwen3Model:
     """`tp_rank`/`tp_size` > 1 loads this process's tensor-parallel shard
     (dense models); after `set_device("cuda")` connect the ranks with
@@ -72,6 +81,8 @@ class Qwen3Model:
             init(1, [device if device is not None else 0])
         self._lib = host_lib()
         self._h = C.c_void_p()
+        self.model_file = str(model_file)
+        self._tokenizer = None
         self.run_params = run_params
         self._rp = run_params.to_c()
         check(self._lib.mf_model_load_tp(str(model_file).encode(), C.byref(self._rp), rank, tp_rank, tp_size,
@@ -177,6 +188,28 @@ class Qwen3Model:
         if logits_at is not None:
             return out[:n], (mg[:n] if margins else None), stats, lg
         return out[:n], (mg[:n] if margins else None), stats
+
+    # -- BaseModel::generate(std::string&) (src/base/model.cpp:99-186)
+    def generate_text(self, text: str, n_gen: int | None = None) -> "TextResult":
+        """One user message through the model file's chat template
+        (add_generation_prompt), encoded by its tokenizer, then the token loop
+        until EOS or min(num_iters, max_seq_len - prompt length) tokens, as
+        the reference's generate does; the output keeps the EOS token. The
+        tokenizer runs on the host (minfer_b200.tokenizer)."""
+        from .tokenizer import Qwen3Tokenizer
+
+        if getattr(self, "_tokenizer", None) is None:
+            self._tokenizer = Qwen3Tokenizer.from_gguf(self.model_file)
+        tok = self._tokenizer
+        formatted = tok.apply_chat_template([{"role": "user", "content": text}], [], True)
+        prompt = tok.encode(formatted)
+        max_seq = self.run_params.max_seq_len
+        if len(prompt) > max_seq:
+            raise ValueError(f"{len(prompt)} prompt tokens exceed max_seq_len {max_seq}")
+        n = min(self.run_params.num_iters, max_seq - len(prompt)) if n_gen is None else n_gen
+        ids, _, stats = self.generate(prompt, n, stop_at_eos=True)
+        ids = [int(i) for i in ids]
+        return TextResult(formatted, prompt, ids, tok.decode(ids), stats)
 
     def benchmark(self, token_prefill: bool = False) -> GenStats:
         """BaseModel::benchmark: pp512 then tg128 with random ids (seed from RunParams)."""

@@ -22,6 +22,15 @@ TINY = {
 }
 
 
+# a tiny model whose GGUF carries a byte-level BPE vocabulary and the ChatML
+# template: text prompts run end to end (tokenizer -> GPU decode -> text)
+TEXT_MODEL = Qwen3Shape(2, 256, 4, 2, 128, 512, 1024, "bf16", True, seed=107, byte_vocab=True)
+
+
+def text_model() -> str:
+    return ensure_gguf(model_dir() / "tiny-text.gguf", TEXT_MODEL)
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200)")
     config.addinivalue_line("markers", "slow: long-running parity case")

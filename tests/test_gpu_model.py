@@ -242,3 +242,36 @@ def test_device_sampling_matches_host_loop(Model, monkeypatch, name, kw):
     assert runs["device"] == runs["host"], f"{name}: device {runs['device']} vs host {runs['host']}"
     assert runs["device"][0] != runs["device"][1]  # the stream moved on
 
+
+
+def test_generate_text_vs_oracle(Model):
+    """BaseModel::generate(std::string&): chat template -> tokenizer -> GPU
+    token loop -> decoded text, on a model file with a byte-level vocabulary.
+    The ids must be the oracle's greedy ids for the same encoded prompt (cut
+    after the first EOS, which ends the loop), up to a tolerance event."""
+    from conftest import TEXT_MODEL, text_model
+    from minfer_b200.tokenizer import Qwen3Tokenizer
+
+    Qwen3Model, RunParams = Model
+    path = text_model()
+    G = 48
+    text = "Hello, world! It's 2 + 2 = 4; 世界\n"
+    m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=256)).set_device("cuda")
+    res = m.generate_text(text)
+    tok = Qwen3Tokenizer.from_gguf(path)
+    assert res.formatted == f"<|im_start|>user\n{text}<|im_end|>\n<|im_start|>assistant\n"
+    assert res.prompt_ids == tok.encode(res.formatted)
+    assert tok.decode(res.prompt_ids) == res.formatted.encode()
+    orc = PortModel(path, max_seq=len(res.prompt_ids) + G + 1)
+    ref_ids, ref_mg = orc.generate(np.array(res.prompt_ids, np.uint32), G)
+    ref = [int(i) for i in ref_ids]
+    if tok.eos_id in ref:
+        cut = ref.index(tok.eos_id) + 1
+        ref, ref_mg = ref[:cut], ref_mg[:cut]
+    ev = check_ids(res.ids, ref, ref_mg, "tiny-text")
+    first = ev[0] if ev else len(ref)
+    assert res.ids[:first] == ref[:first]
+    if not ev:
+        assert res.ids == ref and res.stats.num_tokens_gen == len(ref)
+    assert res.text == tok.decode(res.ids)
+    assert TEXT_MODEL.vocab == m.vocab_size
