@@ -179,9 +179,9 @@ def synth_byte_vocab(n_vocab: int, seed: int) -> tuple[list[bytes], list[int], l
     n_normal = n_vocab - len(specials) - max(2, n_vocab // 64)
     merges: list[bytes] = []
     while len(toks) < n_normal:
-        pool = alpha if rng.random() < 0.5 else toks[256:] or alpha
-        a = pool[int(rng.integers(len(pool)))]
-        b = alpha[int(rng.integers(len(alpha)))] if rng.random() < 0.7 else toks[int(rng.integers(256, len(toks)))] if len(toks) > 256 else alpha[0]
+        grown = len(toks) > 256
+        a = toks[int(rng.integers(256, len(toks)))] if grown and rng.random() >= 0.5 else alpha[int(rng.integers(len(alpha)))]
+        b = toks[int(rng.integers(256, len(toks)))] if grown and rng.random() >= 0.7 else alpha[int(rng.integers(len(alpha)))]
         m = a + b
         if m in seen or len(m) > 8:
             continue
