@@ -213,8 +213,10 @@ int mf_tokenizer_pre_split(const mf_tokenizer* t, const char* text, size_t len, 
  * of {"role", "content", "reasoning_content"?, "tool_calls"?: [{"name",
  * "arguments"}]}, tools_json a JSON array of {"name", "description",
  * "parameters"} (or NULL for none), the objects the reference builds from its
- * Message/Tool structs. MF_E_STATE for errors the template raises,
- * MF_E_UNSUPPORTED for template constructs or polyfills not built. */
+ * Message/Tool structs (any JSON messages are accepted, e.g. OpenAI-shaped
+ * tool calls). MF_E_STATE for errors the template raises, MF_E_UNSUPPORTED
+ * for template constructs not built (macros, call/filter blocks, recursive
+ * loops). */
 int mf_tokenizer_apply_chat_template(const mf_tokenizer* t, const char* messages_json, const char* tools_json,
                                      int add_generation_prompt, char* out, size_t cap, size_t* n);
 

@@ -84,6 +84,14 @@ const Value* Value::find(const std::string& key) const {
         if (kv.first == key) return &kv.second;
     return nullptr;
 }
+void Value::erase(const std::string& key) {
+    auto& o = obj();
+    for (size_t i = 0; i < o.size(); ++i)
+        if (o[i].first == key) {
+            o.erase(o.begin() + (long)i);
+            return;
+        }
+}
 size_t Value::size() const {
     switch (k_) {
         case OBJ: return o_->size();
@@ -237,6 +245,51 @@ void Value::dump_to(std::string& out, int indent, int level, bool json) const {
             break;
         case FUNC: throw std::runtime_error("Cannot dump callable to JSON");
     }
+}
+
+std::string Value::json_text(int indent) const {
+    std::string out;
+    std::function<void(const Value&, int)> put = [&](const Value& v, int level) {
+        auto pad = [&](int lv) {
+            out += '\n';
+            out.append((size_t)lv * indent, ' ');
+        };
+        switch (v.k_) {
+            case ARR:
+                if (v.a_->empty()) {
+                    out += "[]";
+                    return;
+                }
+                out += '[';
+                for (size_t i = 0; i < v.a_->size(); ++i) {
+                    if (i) out += ',';
+                    if (indent >= 0) pad(level + 1);
+                    put((*v.a_)[i], level + 1);
+                }
+                if (indent >= 0) pad(level);
+                out += ']';
+                return;
+            case OBJ:
+                if (v.o_->empty()) {
+                    out += "{}";
+                    return;
+                }
+                out += '{';
+                for (size_t i = 0; i < v.o_->size(); ++i) {
+                    if (i) out += ',';
+                    if (indent >= 0) pad(level + 1);
+                    out += json_quote((*v.o_)[i].first);
+                    out += indent >= 0 ? ": " : ":";
+                    put((*v.o_)[i].second, level + 1);
+                }
+                if (indent >= 0) pad(level);
+                out += '}';
+                return;
+            default: v.dump_to(out, -1, 0, true);
+        }
+    };
+    put(*this, 0);
+    return out;
 }
 
 std::string Value::dump(int indent, bool json) const {
@@ -2018,6 +2071,42 @@ ChatTemplate::ChatTemplate(const std::string& source, std::string bos_token, std
             try_raw_render(Value::array({user, calls_msg(Value::array({call("test_tool1", args)})), r2}), nullptr),
             "Some response!");
     }
+    // A template that cannot show tools gets them described in a system
+    // message, with an example call inferred from what the template renders
+    // for one: the text a tool-call turn adds after a plain prompt.
+    if (!caps_.supports_tools) {
+        try {
+            const Value user_msg = msg("user", Value("Hey"));
+            Value targs = Value::object();
+            targs.set("arg1", Value("some_value"));
+            Value f = Value::object();
+            f.set("name", Value("tool_name"));
+            f.set("arguments", caps_.requires_object_arguments ? targs : Value(targs.dump(-1, true)));
+            Value tc = Value::object();
+            tc.set("id", Value("call_1___"));
+            tc.set("type", Value("function"));
+            tc.set("function", f);
+            Value tcm = msg("assistant", caps_.requires_non_null_content ? Value("") : Value());
+            tcm.set("tool_calls", Value::array({tc}));
+            const std::string prefix = render(Value::array({user_msg}), Value(), true);
+            std::string full = render(Value::array({user_msg, tcm}), Value(), false);
+            const size_t eos_last = full.rfind(eos_);
+            if (eos_last == prefix.size() - eos_.size() ||
+                (!full.empty() && full.back() == '\n' && eos_last == full.size() - eos_.size() - 1))
+                full = full.substr(0, eos_last);
+            size_t common = 0;
+            for (size_t i = 0; i < prefix.size() && i < full.size(); ++i) {
+                if (prefix[i] != full[i]) break;
+                if (prefix[i] == '<') continue;  // (a divergence at a tag keeps the tag's '<')
+                common = i + 1;
+            }
+            const std::string example = full.substr(common);
+            if (example.find("tool_name") != std::string::npos || example.find("some_value") != std::string::npos)
+                tool_call_example_ = example;
+        } catch (const std::exception&) {
+            // no example: the tools are described without one
+        }
+    }
 }
 
 ChatTemplate::~ChatTemplate() = default;
@@ -2058,6 +2147,7 @@ std::string ChatTemplate::try_raw_render(const Value& messages, const Value* too
 
 std::string ChatTemplate::render(const Value& messages, const Value& tools, bool add_generation_prompt) const {
     if (!root_) throw std::runtime_error("chat template does not parse: " + parse_error_);
+    const Value* tools_var = tools.is_null() ? nullptr : &tools;
     const bool has_tools = tools.is_array() && !tools.arr().empty();
     bool has_tool_calls = false, has_tool_responses = false, has_string_content = false;
     for (const Value& m : messages.arr()) {
@@ -2075,11 +2165,19 @@ std::string ChatTemplate::render(const Value& messages, const Value& tools, bool
     const bool poly_obj_args = has_tool_calls && caps_.requires_object_arguments;
     const bool poly_typed = has_string_content && caps_.requires_typed_content;
     if (!(poly_system || poly_tools || poly_calls || poly_responses || poly_obj_args || poly_typed))
-        return raw_render(messages, &tools, add_generation_prompt);
-    if (poly_tools || poly_calls || poly_responses || poly_obj_args)
-        throw std::domain_error("chat template needs the tool polyfills, which are not supported");
+        return raw_render(messages, tools_var, add_generation_prompt);
 
-    // the system-role and typed-content polyfills
+    auto copy_obj = [](const Value& o) {
+        Value c = Value::object();
+        for (const auto& kv : o.obj()) c.set(kv.first, kv.second);
+        return c;
+    };
+    auto role_of = [](const Value& m) -> std::string {
+        const Value* r = m.find("role");
+        if (!r) throw std::out_of_range("key 'role' not found");
+        if (!r->is_string()) throw std::runtime_error("role must be a string");
+        return r->str();
+    };
     Value actual = Value::array();
     auto add = [&](const Value& m) {
         const Value* c = m.find("content");
@@ -2088,7 +2186,9 @@ std::string ChatTemplate::render(const Value& messages, const Value& tools, bool
             part.set("type", Value("text"));
             part.set("text", *c);
             Value nm = Value::object();
-            nm.set("role", m.find("role") ? *m.find("role") : Value());
+            const Value* r = m.find("role");
+            if (!r) throw std::out_of_range("key 'role' not found");
+            nm.set("role", *r);
             nm.set("content", Value::array({part}));
             actual.push(nm);
         } else {
@@ -2104,15 +2204,111 @@ std::string ChatTemplate::render(const Value& messages, const Value& tools, bool
         add(m);
         pending.clear();
     };
-    for (const Value& m0 : messages.arr()) {
+
+    // the tools, described in the (first) system message
+    Value msgs = messages;
+    if (poly_tools) {
+        std::string prompt =
+            "You can call any of the following tools to satisfy the user's requests: " + tools.dump(2, true);
+        if (!tool_call_example_.empty()) prompt += "\n\nExample tool call syntax:\n\n" + tool_call_example_ + "\n\n";
+        Value adj = Value::array();
+        for (const Value& m : messages.arr()) adj.push(m);
+        Value sys = Value::object();
+        sys.set("role", Value("system"));
+        const Value* r0 = adj.arr().empty() ? nullptr : adj.arr()[0].find("role");
+        if (!adj.arr().empty() && !r0) throw std::out_of_range("key 'role' not found");
+        if (r0 && r0->is_string() && r0->str() == "system") {
+            const Value* c = adj.arr()[0].find("content");
+            if (!c || !c->is_string()) throw std::runtime_error("system content must be a string");
+            sys.set("content", Value(c->str() + "\n\n" + prompt));
+            adj.arr()[0] = sys;
+        } else {
+            sys.set("content", Value(prompt));
+            adj.arr().insert(adj.arr().begin(), sys);
+        }
+        msgs = adj;
+    }
+
+    for (const Value& m0 : msgs.arr()) {
         if (!m0.is_object() || !m0.find("role") || (!m0.find("content") && !m0.find("tool_calls")))
-            throw std::runtime_error("message must have 'role' and one of 'content' or 'tool_calls' fields: " + m0.dump());
-        Value m = Value::object();
-        for (const auto& kv : m0.obj()) m.set(kv.first, kv.second);
-        const std::string role = m.find("role")->str();
-        if (!m.find("content")) m.set("content", Value());
+            throw std::runtime_error("message must have 'role' and one of 'content' or 'tool_calls' fields: " +
+                                     m0.json_text());
+        // a deep enough copy: the message and its tool calls are rewritten
+        Value m = copy_obj(m0);
+        const std::string role = role_of(m);
+        if (const Value* tcs0 = m.find("tool_calls")) {
+            if (poly_obj_args || poly_calls) {
+                if (!tcs0->is_array()) throw std::runtime_error("tool_calls must be an array");
+                Value tcs = Value::array();
+                for (const Value& tc0 : tcs0->arr()) {
+                    Value tc = tc0.is_object() ? copy_obj(tc0) : tc0;
+                    if (tc.is_object()) {
+                        if (!tc.find("type")) tc.set("type", Value());  // (a lookup that adds the key)
+                        const Value* ty = tc.find("type");
+                        if (ty->is_string() && ty->str() == "function") {
+                            const Value* f0 = tc.find("function");
+                            if (!f0) throw std::out_of_range("key 'function' not found");
+                            Value f = f0->is_object() ? copy_obj(*f0) : *f0;
+                            const Value* a = f.find("arguments");
+                            if (!a) throw std::out_of_range("key 'arguments' not found");
+                            if (a->is_string()) {
+                                try {
+                                    f.set("arguments", parse_json(a->str()));
+                                } catch (const std::invalid_argument&) {
+                                    // not JSON: the text stays
+                                }
+                            }
+                            tc.set("function", f);
+                        }
+                    }
+                    tcs.push(tc);
+                }
+                m.set("tool_calls", tcs);
+            }
+            if (poly_calls) {
+                Value calls = Value::array();
+                for (const Value& tc : m.find("tool_calls")->arr()) {
+                    const Value* ty = tc.find("type");
+                    if (!ty) throw std::out_of_range("key 'type' not found");
+                    if (!(ty->is_string() && ty->str() == "function")) continue;
+                    const Value* f = tc.find("function");
+                    if (!f || !f->find("name") || !f->find("arguments"))
+                        throw std::out_of_range("tool call function needs name and arguments");
+                    Value c = Value::object();
+                    c.set("name", *f->find("name"));
+                    c.set("arguments", *f->find("arguments"));
+                    if (const Value* id = tc.find("id")) c.set("id", *id);
+                    calls.push(c);
+                }
+                Value o = Value::object();
+                o.set("tool_calls", calls);
+                if (const Value* c = m.find("content")) {
+                    // (JSON emptiness: null, [] and {} are empty; "" is not)
+                    const bool empty = c->is_null() || (c->is_array() && c->arr().empty()) ||
+                                       (c->is_object() && c->obj().empty());
+                    if (!empty) o.set("content", *c);
+                }
+                m.set("content", Value(o.json_text(2)));
+                m.erase("tool_calls");
+            }
+        }
+        if (poly_responses && role == "tool") {
+            m.set("role", Value("user"));
+            Value r = Value::object();
+            if (const Value* n = m.find("name")) r.set("tool", *n);
+            const Value* c = m.find("content");
+            if (!c) throw std::out_of_range("key 'content' not found");
+            r.set("content", *c);
+            if (const Value* id = m.find("tool_call_id")) r.set("tool_call_id", *id);
+            Value o = Value::object();
+            o.set("tool_response", r);
+            m.set("content", Value(o.json_text(2)));
+            m.erase("name");
+        }
+        if (!m.find("content")) m.set("content", Value());  // (a lookup that adds the key)
         const Value content = *m.find("content");
         if (!content.is_null() && poly_system) {
+            if (!content.is_string()) throw std::runtime_error("content must be a string");
             const std::string& text = content.str();
             if (role == "system") {
                 if (!pending.empty()) pending += "\n";
@@ -2131,7 +2327,7 @@ std::string ChatTemplate::render(const Value& messages, const Value& tools, bool
         add(m);
     }
     flush();
-    return raw_render(actual, &tools, add_generation_prompt);
+    return raw_render(actual, tools_var, add_generation_prompt);
 }
 
 }  // namespace minfer

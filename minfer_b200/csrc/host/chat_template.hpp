@@ -10,10 +10,10 @@
 // block set), break/continue, generation blocks; the expression grammar with
 // minja's precedence, its value semantics (byte strings, integer division of
 // integers, objects always true, ...) and its filters/methods; the capability
-// probes and the system-role / typed-content polyfills of its chat_template.
-// Not built (rendering raises std::domain_error): macros, call and filter
-// blocks, recursive loops, and the tool / tool-call / tool-response polyfills
-// minja applies to templates that cannot render those itself.
+// probes and every polyfill of its chat_template (system role, typed content,
+// tools with an inferred tool-call example, tool calls, tool responses,
+// object arguments). Not built (rendering raises std::domain_error): macros,
+// call and filter blocks, recursive loops.
 #pragma once
 
 #include <cstdint>
@@ -69,11 +69,15 @@ public:
     void push(Value v);
     void set(const std::string& key, Value v);
     const Value* find(const std::string& key) const;
+    void erase(const std::string& key);
     size_t size() const;
 
     bool truthy() const;
     std::string to_str() const;                   // minja to_str: strings raw, floats %f, None/True/False
     std::string dump(int indent = -1, bool json = false) const;  // Python repr, or JSON with json=true
+    // plain JSON text: compact without spaces (indent < 0), or pretty with
+    // `indent` spaces per level and empty containers as [] / {}
+    std::string json_text(int indent = -1) const;
     bool equals(const Value& o) const;
 
 private:
@@ -102,9 +106,9 @@ public:
                           std::string eos_token = "<|im_end|>");
     ~ChatTemplate();
     // messages / tools: JSON arrays as the reference's apply_chat_template
-    // builds them. Throws std::runtime_error from the template
-    // (raise_exception, type errors) and std::domain_error for constructs
-    // and polyfills that are not built.
+    // builds them (tools null: no `tools` variable). Throws
+    // std::runtime_error from the template (raise_exception, type errors) and
+    // std::domain_error for constructs that are not built.
     std::string render(const Value& messages, const Value& tools, bool add_generation_prompt) const;
 
     struct Caps {
@@ -121,6 +125,7 @@ private:
     std::string parse_error_;
     std::string bos_, eos_;
     Caps caps_;
+    std::string tool_call_example_;
 };
 
 }  // namespace minfer

@@ -12,6 +12,9 @@
 #include <string>
 #include <vector>
 
+#include <chrono>
+
+#include "extern/minja/chat-template.hpp"
 #include "extern/nlohmann/json.hpp"
 #define private public
 #include "minfer/models/qwen3/tokenizer.hpp"
@@ -137,6 +140,26 @@ int tref_chat(void* t, const char* messages_json, const char* tools_json, int ad
                              x.at("parameters").get<std::string>()});
         *n_bytes = put(static_cast<Qwen3Tokenizer*>(t)->apply_chat_template(msgs, tools, add_generation_prompt != 0),
                        out, cap);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+// The chat-template engine the tokenizer holds, given any JSON messages and
+// tools (tools_json NULL: no tools value, as the probes render), the way
+// apply_chat_template calls it (tokenizer.cpp:328-334).
+int tref_chat_json(void* t, const char* messages_json, const char* tools_json, int add_generation_prompt, char* out,
+                   size_t cap, size_t* n_bytes) {
+    try {
+        using nlohmann::ordered_json;
+        minja::chat_template_inputs inputs;
+        inputs.messages = ordered_json::parse(messages_json);
+        inputs.tools = tools_json ? ordered_json::parse(tools_json) : ordered_json();
+        inputs.add_generation_prompt = add_generation_prompt != 0;
+        inputs.extra_context = ordered_json{};
+        inputs.now = std::chrono::system_clock::now();
+        *n_bytes = put(static_cast<Qwen3Tokenizer*>(t)->_chat_template->apply(inputs, {}), out, cap);
         return 0;
     } catch (const std::exception& e) {
         return fail(e);

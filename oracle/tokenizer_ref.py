@@ -44,6 +44,8 @@ class RefTokenizer:
                                     C.POINTER(C.c_size_t)]
         lib.tref_chat.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_int, C.c_char_p, C.c_size_t,
                                   C.POINTER(C.c_size_t)]
+        lib.tref_chat_json.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_int, C.c_char_p, C.c_size_t,
+                                       C.POINTER(C.c_size_t)]
         self.lib = lib
         blob = _blob(tokens, types, merges, template, eos, pad)
         self.h = lib.tref_create(blob, len(blob))
@@ -90,5 +92,16 @@ class RefTokenizer:
         n = C.c_size_t()
         if self.lib.tref_chat(self.h, json.dumps(messages).encode(), json.dumps(tools).encode(),
                               int(add_generation_prompt), out, cap, C.byref(n)):
+            raise self._err()
+        return out.raw[: n.value].decode(errors="surrogateescape")
+
+    def chat_json(self, messages, tools, add_generation_prompt: bool) -> str:
+        """The chat-template engine on any JSON messages/tools (tools None: unset)."""
+        cap = 1 << 20
+        out = C.create_string_buffer(cap)
+        n = C.c_size_t()
+        tj = None if tools is None else json.dumps(tools).encode()
+        if self.lib.tref_chat_json(self.h, json.dumps(messages).encode(), tj, int(add_generation_prompt), out, cap,
+                                   C.byref(n)):
             raise self._err()
         return out.raw[: n.value].decode(errors="surrogateescape")

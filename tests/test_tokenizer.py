@@ -192,12 +192,11 @@ def test_template_errors(vocab):
     with pytest.raises(MinferError) as e:
         Qwen3Tokenizer.from_vocab(tokens, merges, types, macro).apply_chat_template([{"role": "user", "content": "x"}])
     assert e.value.code in (MF_E_UNSUPPORTED, MF_E_STATE)
-    # a template that cannot show tools needs the tools polyfill: refused, not rendered differently
+    # a template that cannot show tools gets them in a system message (the tools polyfill)
     plain = "{% for m in messages %}{{ m.role }}: {{ m.content }}\n{% endfor %}"
-    with pytest.raises(MinferError) as e:
-        Qwen3Tokenizer.from_vocab(tokens, merges, types, plain).apply_chat_template(
-            [{"role": "user", "content": "x"}], [{"name": "f", "description": "d", "parameters": {}}])
-    assert e.value.code == MF_E_UNSUPPORTED
+    out = Qwen3Tokenizer.from_vocab(tokens, merges, types, plain).apply_chat_template(
+        [{"role": "user", "content": "x"}], [{"name": "f", "description": "d", "parameters": {}}])
+    assert out.startswith("system: You can call any of the following tools to satisfy the user's requests: [")
 
 
 def test_load_from_gguf_model():
@@ -244,3 +243,73 @@ def test_qwen3_sized_vocabulary_vs_reference():
     assert ids == ref.encode(text) and t.decode(ids) == text
     for b in _random_texts(99, 20):
         assert t.encode(b) == ref.encode(b), b
+
+
+POLYFILL_TEMPLATES = {
+    # shows roles and contents only: tools, tool calls and tool responses need polyfills
+    "plain": "{% for m in messages %}{{ m.role }}: {{ m.content }}\n{% endfor %}"
+             "{% if add_generation_prompt %}assistant: {% endif %}",
+    # refuses system messages: they are merged into the next user message
+    "no_system": "{% for m in messages %}{% if m.role == 'system' %}{{ raise_exception('no system role') }}{% endif %}"
+                 "<{{ m.role }}>{{ m.content }}</{{ m.role }}>{% endfor %}",
+    # reads content as a list of typed parts
+    "typed": "{% for m in messages %}{{ m.role }}:{% for p in m.content %}{{ p.text }}{% endfor %}\n{% endfor %}",
+    # renders tools and calls, but call arguments only as a mapping
+    "object_args": "{% if tools %}{% for t in tools %}{{ t | tojson }}\n{% endfor %}{% endif %}"
+                   "{% for m in messages %}[{{ m.role }}] {{ m.content if m.content is string else '' }}"
+                   "{% if m.tool_calls %}{% for tc in m.tool_calls %}<call {{ tc.function.name }}>"
+                   "{% for k, v in tc.function.arguments | items %}<parameter={{ k }}>{{ v }}{% endfor %}"
+                   "</call>{% endfor %}{% endif %}\n{% endfor %}",
+}
+
+
+def _openai_messages():
+    call = {"id": "call_7", "type": "function",
+            "function": {"name": "get_weather", "arguments": "{\"city\": \"Oslo\", \"days\": 2}"}}
+    call_obj = {"id": "call_8", "type": "function", "function": {"name": "calc", "arguments": {"expr": "2+2"}}}
+    return [
+        [{"role": "user", "content": "hi"}],
+        [{"role": "system", "content": "Be terse."}, {"role": "system", "content": "Use metric."},
+         {"role": "user", "content": "weather?"}, {"role": "assistant", "content": "Sunny."},
+         {"role": "user", "content": ""}],
+        [{"role": "system", "content": "sys"}, {"role": "user", "content": "weather in Oslo?"},
+         {"role": "assistant", "content": None, "tool_calls": [call]},
+         {"role": "tool", "name": "get_weather", "content": "{\"temp\": -3}", "tool_call_id": "call_7"},
+         {"role": "assistant", "content": "", "tool_calls": [call_obj, {"type": "other", "x": 1}]},
+         {"role": "tool", "content": "4"}, {"role": "assistant", "content": "Cold."}],
+    ]
+
+
+@pytest.mark.skipif(not tokenizer_ref.available(), reason="the reference tokenizer build (oracle/_ref) is absent")
+def test_polyfills_vs_reference(vocab):
+    """Templates that cannot render system messages, tools, tool calls, tool
+    responses or string contents themselves: the reference's chat-template
+    engine rewrites the conversation first (and infers a tool-call example
+    from the template); the renders must be identical, or both must fail."""
+    from minfer_b200._lib import MinferError
+    from minfer_b200.tokenizer import Qwen3Tokenizer
+
+    tokens, merges, types = _args(vocab)
+    tools = [{"type": "function", "function": {"name": "get_weather", "description": "Weather <now>.",
+                                               "parameters": {"type": "object",
+                                                              "properties": {"city": {"type": "string"}},
+                                                              "required": ["city"]}}}]
+    templates = dict(POLYFILL_TEMPLATES, chatml_tools=vocab["templates"]["chatml_tools"],
+                     chatml_min=vocab["templates"]["chatml_min"], exprs=vocab["templates"]["exprs"])
+    n_ok = n_err = 0
+    for name, tmpl in templates.items():
+        t = Qwen3Tokenizer.from_vocab(tokens, merges, types, tmpl, vocab["eos"], vocab["pad"])
+        ref = tokenizer_ref.RefTokenizer(tokens, types, merges, tmpl, vocab["eos"], vocab["pad"])
+        for msgs in _openai_messages():
+            for tl in ([], tools):
+                for gen in (True, False):
+                    try:
+                        expected = ref.chat_json(msgs, tl, gen)
+                    except RuntimeError:
+                        with pytest.raises(MinferError):
+                            t.apply_chat_template(msgs, tl, gen)
+                        n_err += 1
+                        continue
+                    assert t.apply_chat_template(msgs, tl, gen) == expected, (name, msgs, tl, gen)
+                    n_ok += 1
+    assert n_ok > 3 * n_err
