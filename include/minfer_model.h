@@ -6,8 +6,8 @@
  * It exposes what the reference's apps and tests reach through BaseModel
  * (include/minfer/base/model.hpp:17-41): construction from a GGUF file
  * (Qwen3Model::Qwen3Model, src/models/qwen3/model.cpp:9-86), set_device,
- * forward, generate and benchmark — with token ids instead of text, since the
- * tokenizer is not part of this path.
+ * forward, generate and benchmark on token ids, and the tokenizer with its
+ * chat template (Qwen3Tokenizer) for text, on the host (mf_tokenizer_*).
  *
  * Status codes are the MF_* codes of minfer_cuda.h; mf_last_error() returns
  * the message of the last failure (host-runtime failures included).
@@ -129,8 +129,9 @@ int mf_model_generate_logits(mf_model* m, const uint32_t* prompt, size_t n_promp
  * go through every layer as tcgen05 GEMMs, filling the KV cache; with
  * compute_logits the last token's logits / greedy id are then available as
  * after mf_model_forward. Dense models with bf16 weights, or fp32 weights (kept
- * as bf16 hi + lo copies for the GEMMs, two products each); others (f16
- * weights, MoE) return MF_E_UNSUPPORTED (use mf_model_forward per token). */
+ * as bf16 hi + lo copies for the GEMMs, two products each), and MoE models
+ * with bf16 experts (tokens grouped by expert, grouped GEMMs); f16 weights
+ * return MF_E_UNSUPPORTED (use mf_model_forward per token). */
 int mf_model_prefill(mf_model* m, const uint32_t* tokens, size_t n, int pos0, int compute_logits, int host_logits);
 
 /* BaseModel::benchmark (src/base/model.cpp:188-236): pp512 (512 random ids
