@@ -41,16 +41,14 @@ int64_t Value::i() const {
     switch (k_) {
         case INT: return i_;
         case FLOAT: return (int64_t)f_;
-        case BOOL: return b_ ? 1 : 0;
-        default: throw std::runtime_error("not a number: " + dump());
+        default: throw std::runtime_error("type must be number: " + dump());
     }
 }
 double Value::f() const {
     switch (k_) {
         case INT: return (double)i_;
         case FLOAT: return f_;
-        case BOOL: return b_ ? 1.0 : 0.0;
-        default: throw std::runtime_error("not a number: " + dump());
+        default: throw std::runtime_error("type must be number: " + dump());
     }
 }
 const std::string& Value::str() const {
@@ -950,13 +948,23 @@ struct Tok {
     enum K { ID, NUM, STR, OP, END } k;
     std::string s;
     Value v;
+    size_t at = 0;  // offset in the expression source
 };
 
 std::vector<Tok> lex(const std::string& src) {
     std::vector<Tok> out;
     size_t p = 0;
     const size_t n = src.size();
+    size_t marked = 0, start = 0;  // tokens whose offset is set; where the last one began
+    auto mark = [&]() {
+        if (marked < out.size()) {
+            out.back().at = start;
+            marked = out.size();
+        }
+    };
     while (p < n) {
+        mark();
+        start = p;
         const char c = src[p];
         if (std::isspace((unsigned char)c)) {
             ++p;
@@ -970,24 +978,43 @@ std::vector<Tok> lex(const std::string& src) {
             continue;
         }
         if (std::isdigit((unsigned char)c)) {
+            // the longest run of digits, one '.' and one e/E (no sign), which
+            // must then read as a JSON number ("7." and "2.5e-3" do not)
             size_t q = p;
-            bool fl = false;
-            while (q < n && std::isdigit((unsigned char)src[q])) ++q;
-            if (q + 1 < n && src[q] == '.' && std::isdigit((unsigned char)src[q + 1])) {
-                fl = true;
-                ++q;
-                while (q < n && std::isdigit((unsigned char)src[q])) ++q;
-            }
-            if (q < n && (src[q] == 'e' || src[q] == 'E')) {
-                size_t r = q + 1;
-                if (r < n && (src[r] == '+' || src[r] == '-')) ++r;
-                if (r < n && std::isdigit((unsigned char)src[r])) {
-                    fl = true;
-                    q = r;
-                    while (q < n && std::isdigit((unsigned char)src[q])) ++q;
+            bool dot = false, ex = false;
+            while (q < n) {
+                const char d = src[q];
+                if (std::isdigit((unsigned char)d)) {
+                    ++q;
+                } else if (d == '.') {
+                    if (dot) throw std::runtime_error("Multiple decimal points");
+                    dot = true;
+                    ++q;
+                } else if (d == 'e' || d == 'E') {
+                    if (ex) throw std::runtime_error("Multiple exponents");
+                    ex = true;
+                    ++q;
+                } else {
+                    break;
                 }
             }
             const std::string t = src.substr(p, q - p);
+            // JSON: (0 | [1-9][0-9]*) (. [0-9]+)? ([eE] [0-9]+)?
+            size_t k = 0;
+            bool good = t[0] != '0' || t.size() == 1 || !std::isdigit((unsigned char)t[1]);
+            while (k < t.size() && std::isdigit((unsigned char)t[k])) ++k;
+            if (good && k < t.size() && t[k] == '.') {
+                const size_t b = ++k;
+                while (k < t.size() && std::isdigit((unsigned char)t[k])) ++k;
+                good = k > b;
+            }
+            if (good && k < t.size() && (t[k] == 'e' || t[k] == 'E')) {
+                const size_t b = ++k;
+                while (k < t.size() && std::isdigit((unsigned char)t[k])) ++k;
+                good = k > b;
+            }
+            if (!good || k != t.size()) throw std::runtime_error("Failed to parse number: '" + t + "'");
+            const bool fl = dot || ex;
             out.push_back({Tok::NUM, t,
                            fl ? Value(std::strtod(t.c_str(), nullptr)) : Value((int64_t)std::strtoll(t.c_str(), nullptr, 10))});
             p = q;
@@ -1035,7 +1062,8 @@ std::vector<Tok> lex(const std::string& src) {
         }
         throw std::runtime_error(std::string("unexpected character '") + c + "' in expression");
     }
-    out.push_back({Tok::END, "", Value()});
+    mark();
+    out.push_back({Tok::END, "", Value(), n});
     return out;
 }
 
@@ -1213,6 +1241,19 @@ struct ExprParser {
     }
     ExprP primary() {
         const Tok& k = peek();
+        if (k.k == Tok::OP && (k.s == "-" || k.s == "+")) {
+            // a sign where a value starts belongs to a number literal (the
+            // unary operator has taken the first one): "-3" right after it
+            // reads as -3, anything else is not a number
+            const Tok& nx = peek(1);
+            if (k.s == "-" && nx.k == Tok::NUM && nx.at == k.at + 1) {
+                p += 2;
+                auto e = mk(Expr::LIT);
+                e->lit = nx.v.kind() == Value::INT ? Value(-nx.v.i()) : Value(-nx.v.f());
+                return e;
+            }
+            throw std::runtime_error("Failed to parse number: '" + k.s + (nx.k == Tok::NUM && nx.at == k.at + 1 ? nx.s : "") + "'");
+        }
         if (k.k == Tok::NUM || k.k == Tok::STR) {
             ++p;
             auto e = mk(Expr::LIT);
@@ -1851,7 +1892,8 @@ Ctx builtins() {
             const long long x = std::strtoll(v.str().c_str(), &end, 10);
             return Value((int64_t)(end == v.str().c_str() ? 0 : x));
         }
-        if (v.kind() == Value::BOOL || v.is_number()) return Value(v.i());
+        if (v.kind() == Value::BOOL) return Value((int64_t)(v.b() ? 1 : 0));
+        if (v.is_number()) return Value(v.i());
         return Value((int64_t)0);
     });
     def("list", [](CallArgs& a) {
@@ -1867,9 +1909,13 @@ Ctx builtins() {
         if (!v.is_array()) throw std::runtime_error("object is not iterable");
         Value r = Value::array();
         for (const Value& x : v.arr()) {
+            // a hash set of scalars: containers cannot be hashed, and values
+            // of different JSON types (1 and 1.0) never collide
+            if (x.is_array() || x.is_object() || x.is_callable())
+                throw std::runtime_error("Unsupported type for hashing: " + x.dump());
             bool seen = false;
             for (const Value& y : r.arr())
-                if (y.equals(x) || (x.is_null() && y.is_null())) seen = true;
+                if (y.kind() == x.kind() && (x.is_null() || y.equals(x))) seen = true;
             if (!seen) r.push(x);
         }
         return r;

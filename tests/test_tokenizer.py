@@ -313,3 +313,153 @@ def test_polyfills_vs_reference(vocab):
                     assert t.apply_chat_template(msgs, tl, gen) == expected, (name, msgs, tl, gen)
                     n_ok += 1
     assert n_ok > 3 * n_err
+
+
+_TESTS = ["defined", "none", "string", "number", "integer", "float", "mapping", "iterable", "sequence", "boolean",
+          "true", "false"]
+_SUBSCRIPTS = ["0", "1", "-1", ":2", "1:", "::-1", "::2", "'k'", "-2:", "1:3"]
+
+
+def _random_expression(rng, d=0):
+    """A random expression over literals, the render's variables, operators,
+    filters, methods, subscripts, slices, tests and conditionals."""
+    atoms = ["1", "2", "0", "-3", "2.5", "0.1", "'ab'", "'a b c'", "''", "\"x'y\"", "true", "false", "none",
+             "[1, 2, 3]", "[]", "['x', 'y']", "{'k': 1, 'j': 'v'}", "{}", "messages", "messages[0]",
+             "messages[0].content", "messages[-1].role", "add_generation_prompt", "bos_token", "undefined_thing",
+             "(1, 'a')", "[none, 0, '']", "'  pad\\n'", "'A-b-C'", "10", "7", "3.0"]
+    if d > 3 or rng.random() < 0.3:
+        return rng.choice(atoms)
+    r = rng.random()
+    a = _random_expression(rng, d + 1)
+    if r < 0.3:
+        op = rng.choice(["+", "-", "*", "**", "~", "==", "!=", "<", ">", "<=", ">=", "and", "or", "in", "not in"])
+        return f"({a} {op} {_random_expression(rng, d + 1)})"
+    if r < 0.45:
+        f = rng.choice(["length", "trim", "tojson", "upper", "lower", "list", "unique", "last", "count", "string", "int",
+                        "items", "dictsort", "safe", "escape", "join(',')", "default('dflt')", "default('d', true)",
+                        "map(attribute='role')", "selectattr('role')", "select('equalto', 1)", "reject('equalto', 1)",
+                        "tojson(indent=2)", "join", "first"])
+        return f"({a} | {f})"
+    if r < 0.6:
+        m = rng.choice(["strip()", "strip('a')", "lstrip()", "rstrip('\\n')", "split(' ')", "split('-')", "upper()",
+                        "lower()", "title()", "capitalize()", "startswith('a')", "endswith('c')",
+                        "replace('a', 'Z')", "replace('a', 'Z', 1)", "items()", "keys()", "get('k')", "get('q', 5)",
+                        "append(4)", "pop()"])
+        return f"{a}.{m}"
+    if r < 0.7:
+        return f"{a}[{rng.choice(_SUBSCRIPTS)}]"
+    if r < 0.8:
+        return f"({a} is {rng.choice(_TESTS)})"
+    if r < 0.87:
+        return f"(not {a})"
+    if r < 0.94:
+        return f"({a} if {_random_expression(rng, d + 1)} else {_random_expression(rng, d + 1)})"
+    return f"(-{a})"
+
+
+@pytest.mark.skipif(not tokenizer_ref.available(), reason="the reference tokenizer build (oracle/_ref) is absent")
+def test_random_expressions_vs_reference(vocab):
+    """Seeded random expressions (literals, operators, filters, methods,
+    subscripts, slices, tests, conditionals) as one-tag templates: the render
+    is the reference engine's, or both fail. (Integer division and modulo are
+    left out: the reference divides integers unchecked, and a zero divisor
+    kills its process with SIGFPE; ours raises an error.)"""
+    from minfer_b200._lib import MinferError
+    from minfer_b200.tokenizer import Qwen3Tokenizer
+
+    tokens, merges, types = _args(vocab)
+    msgs = [{"role": "user", "content": "Hello world"}, {"role": "assistant", "content": "a-b-c"}]
+    rng = random.Random(11)
+    ok = 0
+    for _ in range(500):
+        tmpl = "{{ " + _random_expression(rng) + " }}"
+        ours = Qwen3Tokenizer.from_vocab(tokens, merges, types, tmpl)
+        try:  # (a template the reference cannot parse fails its constructor; ours fails at render)
+            ref = tokenizer_ref.RefTokenizer(tokens, types, merges, tmpl, vocab["eos"], vocab["pad"])
+            expected = ref.chat_json(msgs, [], True)
+        except RuntimeError:
+            with pytest.raises(MinferError):
+                ours.apply_chat_template(msgs, [], True)
+            continue
+        assert ours.apply_chat_template(msgs, [], True) == expected, tmpl
+        ok += 1
+    assert ok > 150
+
+
+
+# random templates: text with spaces/newlines around nested for/if/set blocks,
+# loop variables, namespaces, break/continue and '-' trim markers
+_WS = ["", " ", "  ", "\n", "\n  ", "  \n", "\t", "\n\n", " x ", "text\n", "\n    "]
+_EXPRS = ["m.role", "m.content", "loop.index", "loop.first", "loop.last", "loop.length", "loop.revindex",
+          "ns.n", "x", "messages | length", "m.content[:3]", "bos_token", "loop.index0 ~ '/' ~ loop.length",
+          "loop.previtem.role if loop.previtem else 'none'", "loop.cycle('a', 'b')", "y"]
+_CONDS = ["loop.first", "m.role == 'user'", "not loop.last", "x", "ns.n > 1", "m.content", "add_generation_prompt",
+          "'o' in m.content", "y is defined"]
+_OUTER_EXPRS = ["x", "ns.n", "messages | length", "bos_token", "y", "add_generation_prompt"]
+_OUTER_CONDS = ["x", "ns.n > 1", "add_generation_prompt", "y is defined"]
+_SETS = ["set x = x ~ 'a'", "set ns.n = ns.n + 1", "set y = 3", "set x, y = ['p', 'q']"]
+
+
+def _tag(rng, body, kind="%"):
+    left = "-" if rng.random() < 0.3 else ""
+    right = "-" if rng.random() < 0.3 else ""
+    open_, close = {"%": ("{%", "%}"), "{": ("{{", "}}"), "#": ("{#", "#}")}[kind]
+    return f"{open_}{left} {body} {right}{close}"
+
+
+def _body(rng, depth, in_loop):
+    parts = []
+    for _ in range(rng.randint(1, 4)):
+        r = rng.random()
+        parts.append(rng.choice(_WS))
+        if r < 0.3 or depth > 2:
+            parts.append(_tag(rng, rng.choice(_EXPRS if in_loop else _OUTER_EXPRS), "{"))
+        elif r < 0.5:
+            cond = " if m.role != 'system'" if rng.random() < 0.3 else ""
+            parts.append(_tag(rng, "for m in messages" + cond))
+            parts.append(_body(rng, depth + 1, True))
+            if rng.random() < 0.2:
+                parts.append(_tag(rng, "else"))
+                parts.append(_body(rng, depth + 1, False))
+            parts.append(_tag(rng, "endfor"))
+        elif r < 0.7:
+            parts.append(_tag(rng, "if " + rng.choice(_CONDS if in_loop else _OUTER_CONDS)))
+            parts.append(_body(rng, depth + 1, in_loop))
+            if rng.random() < 0.4:
+                parts.append(_tag(rng, "elif " + rng.choice(["x", "true", "false"])))
+                parts.append(_body(rng, depth + 1, in_loop))
+            if rng.random() < 0.4:
+                parts.append(_tag(rng, "else"))
+                parts.append(_body(rng, depth + 1, in_loop))
+            parts.append(_tag(rng, "endif"))
+        elif r < 0.8:
+            parts.append(_tag(rng, rng.choice(_SETS)))
+        elif r < 0.86:
+            parts.append(_tag(rng, "set z"))
+            parts.append(_body(rng, depth + 1, in_loop))
+            parts.append(_tag(rng, "endset"))
+            parts.append(_tag(rng, "z", "{"))
+        elif r < 0.9 and in_loop:
+            parts.append(_tag(rng, rng.choice(["break", "continue"])))
+        else:
+            parts.append(_tag(rng, "comment", "#"))
+        parts.append(rng.choice(_WS))
+    return "".join(parts)
+
+
+@pytest.mark.skipif(not tokenizer_ref.available(), reason="the reference tokenizer build (oracle/_ref) is absent")
+def test_random_templates_vs_reference(vocab):
+    """Seeded random templates exercise the whitespace rules (trim_blocks,
+    lstrip_blocks, '-' markers, trailing newline), scoping and loop state:
+    every render identical to the reference engine's."""
+    from minfer_b200.tokenizer import Qwen3Tokenizer
+
+    tokens, merges, types = _args(vocab)
+    msgs = [{"role": "system", "content": "sys"}, {"role": "user", "content": "Hello world"},
+            {"role": "assistant", "content": "a-b-c"}, {"role": "user", "content": "foo"}]
+    rng = random.Random(3)
+    for _ in range(300):
+        tmpl = _tag(rng, "set ns = namespace(n=0)") + _tag(rng, "set x = 'v'") + _body(rng, 0, False)
+        ref = tokenizer_ref.RefTokenizer(tokens, types, merges, tmpl, vocab["eos"], vocab["pad"])
+        ours = Qwen3Tokenizer.from_vocab(tokens, merges, types, tmpl)
+        assert ours.apply_chat_template(msgs, [], True) == ref.chat_json(msgs, [], True), tmpl
