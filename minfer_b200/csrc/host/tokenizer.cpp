@@ -297,42 +297,66 @@ std::vector<std::pair<size_t, size_t>> Qwen3Tokenizer::pre_split(const std::stri
 }
 
 std::vector<uint32_t> Qwen3Tokenizer::bpe(const char* p, size_t n) const {
-    std::vector<int32_t> w(n);
-    for (size_t i = 0; i < n; ++i) w[i] = (uint8_t)p[i];
     // The reference walks the rules in rank order and applies each to the
-    // whole word once; the rules that change anything are, in turn, the
-    // lowest-ranked one above the last applied whose pair occurs in the word.
-    int64_t last = -1;
-    std::vector<int32_t> nw;
-    nw.reserve(n);
-    while (w.size() > 1) {
-        int64_t best = INT64_MAX;
-        for (size_t i = 0; i + 1 < w.size(); ++i) {
-            auto it = pair_ranks_.find(pair_key(w[i], w[i + 1]));
-            if (it == pair_ranks_.end()) continue;
-            auto r = std::upper_bound(it->second.begin(), it->second.end(), last);
-            if (r != it->second.end() && *r < best) best = *r;
+    // whole word once, left to right (tokenizer.cpp:251-275). The rules that
+    // change anything are, in turn, the lowest-ranked rule above the last one
+    // applied whose pair occurs in the word; a pass never creates a pair of its
+    // own rule. So: the word as a linked list, a min-heap of (rank, position)
+    // holding for every adjacent pair its lowest rank above the last applied
+    // rule, and one pass per popped rank, left to right over that rank's
+    // positions. O(n log n) in the piece's bytes.
+    struct Node {
+        int32_t sym, prev, next;
+    };
+    std::vector<Node> w(n);
+    for (size_t i = 0; i < n; ++i) w[i] = {(uint8_t)p[i], (int32_t)i - 1, i + 1 < n ? (int32_t)(i + 1) : -1};
+    using Entry = std::pair<int32_t, int32_t>;  // (rank, position of the pair's left symbol)
+    std::vector<Entry> heap;
+    auto push = [&](int32_t i, int64_t after) {
+        if (i < 0 || w[i].next < 0) return;
+        auto it = pair_ranks_.find(pair_key(w[i].sym, w[w[i].next].sym));
+        if (it == pair_ranks_.end()) return;
+        auto r = std::upper_bound(it->second.begin(), it->second.end(), after);
+        if (r == it->second.end()) return;
+        heap.emplace_back(*r, i);
+        std::push_heap(heap.begin(), heap.end(), std::greater<Entry>());
+    };
+    for (size_t i = 0; i + 1 < n; ++i) push((int32_t)i, -1);
+    std::vector<int32_t> at, merged;
+    while (!heap.empty()) {
+        const int32_t rank = heap.front().first;
+        at.clear();
+        while (!heap.empty() && heap.front().first == rank) {  // the pass's positions, left to right
+            at.push_back(heap.front().second);
+            std::pop_heap(heap.begin(), heap.end(), std::greater<Entry>());
+            heap.pop_back();
         }
-        if (best == INT64_MAX) break;
-        const Rule& rule = rules_[(size_t)best];
-        nw.clear();
-        for (size_t i = 0; i < w.size(); ++i) {
-            if (i + 1 < w.size() && w[i] == rule.left && w[i + 1] == rule.right) {
-                nw.push_back(rule.merged);
-                ++i;
-            } else {
-                nw.push_back(w[i]);
-            }
+        std::sort(at.begin(), at.end());
+        const Rule& rule = rules_[(size_t)rank];
+        merged.clear();
+        int32_t prev_merged = -1;
+        for (int32_t i : at) {
+            // stale entries (a symbol merged since) no longer show the rule's pair
+            const int32_t j = w[i].next;
+            if (i == prev_merged || j < 0 || w[i].sym != rule.left || w[j].sym != rule.right) continue;
+            w[i].sym = rule.merged;
+            w[i].next = w[j].next;
+            if (w[j].next >= 0) w[w[j].next].prev = i;
+            w[j].sym = -1;  // (removed)
+            merged.push_back(i);
+            prev_merged = i;
         }
-        w.swap(nw);
-        last = best;
+        // the pairs the merges made, at their lowest rank above this one
+        for (int32_t i : merged) {
+            push(w[i].prev, rank);
+            push(i, rank);
+        }
     }
     std::vector<uint32_t> ids;
-    ids.reserve(w.size());
-    for (int32_t sym : w) {
-        const int64_t id = sym_vocab_[(size_t)sym];
+    for (int32_t i = n ? 0 : -1; i >= 0; i = w[i].next) {
+        const int64_t id = sym_vocab_[(size_t)w[i].sym];
         if (id < 0)
-            throw std::runtime_error(std::string(n <= 1 ? "Byte" : "BPE") + " token '" + syms_[(size_t)sym] +
+            throw std::runtime_error(std::string(n <= 1 ? "Byte" : "BPE") + " token '" + syms_[(size_t)w[i].sym] +
                                      "' not found in vocab to id map");
         ids.push_back((uint32_t)id);
     }
