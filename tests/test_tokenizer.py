@@ -463,3 +463,20 @@ def test_random_templates_vs_reference(vocab):
         ref = tokenizer_ref.RefTokenizer(tokens, types, merges, tmpl, vocab["eos"], vocab["pad"])
         ours = Qwen3Tokenizer.from_vocab(tokens, merges, types, tmpl)
         assert ours.apply_chat_template(msgs, [], True) == ref.chat_json(msgs, [], True), tmpl
+
+
+@pytest.mark.skipif(not tokenizer_ref.available(), reason="the reference tokenizer build (oracle/_ref) is absent")
+def test_long_pieces_vs_reference(vocab):
+    """Single pieces of up to 20000 letters (one pre-split match each): the
+    heap-driven merges give the reference's ids."""
+    from minfer_b200.tokenizer import Qwen3Tokenizer
+
+    tokens, merges, types = _args(vocab)
+    t = Qwen3Tokenizer.from_vocab(tokens, merges, types, "", vocab["eos"], vocab["pad"])
+    ref = tokenizer_ref.RefTokenizer(tokens, types, merges, "", vocab["eos"], vocab["pad"])
+    rng = random.Random(4)
+    for n in (2, 3, 17, 200, 3000, 20000):
+        for alphabet in ("aaab", "etaoinshrdlu", "ab"):
+            s = "".join(rng.choice(alphabet) for _ in range(n)).encode()
+            assert len(t.pre_split(s)) == 1
+            assert t.encode(s) == ref.encode(s), (n, alphabet)
