@@ -19,6 +19,12 @@
  *       (the tokenizer is not part of this path): prompt forwards, then the
  *       reference's Sampler::sample on each step's logits, EOS ignored;
  *       prints the ids as one JSON line.
+ *   minfer_cuda_app text MODEL --prompt TEXT --gen G [--max-seq N ...]
+ *       BaseModel::generate(std::string&) (src/base/model.cpp:99-186) as
+ *       shipped, text in: the model's BaseTokenizer is CudaTokenizer below, the
+ *       reference's tokenizer interface (include/minfer/base/tokenizer.hpp)
+ *       over this runtime's tokenizer (mf_tokenizer_*), in place of the
+ *       PCRE2/minja Qwen3Tokenizer; the loop prints what the reference prints.
  *
  * The layers are assembled as src/models/qwen3/model.cpp:9-86 does (views of
  * the mapped file, never run here) so BaseModel::get_read_bytes reports the
@@ -30,8 +36,10 @@
 #include "minfer/base/sampler.hpp"
 #include "minfer/base/stats.hpp"
 #include "minfer/base/tensor.hpp"
+#include "minfer/base/tokenizer.hpp"
 #include "minfer/models/qwen3/module.hpp"
 #include "minfer_model.h"
+#include "nlohmann/json.hpp"
 
 #include <cstdio>
 #include <cstdlib>
@@ -51,6 +59,72 @@ void ck(int rc, const char* what) {
         throw std::runtime_error(std::string(what) + ": " + msg);
     }
 }
+
+// BaseTokenizer over mf_tokenizer_*: what the reference's generate(std::string&)
+// calls (apply_chat_template, encode, decode_token, get_eos_id).
+class CudaTokenizer : public BaseTokenizer {
+public:
+    CudaTokenizer(const std::string& gguf_path, uint32_t eos, uint32_t pad) : BaseTokenizer(eos, pad) {
+        ck(mf_tokenizer_load(gguf_path.c_str(), &t_), "mf_tokenizer_load");
+    }
+    ~CudaTokenizer() override { mf_tokenizer_free(t_); }
+
+    std::vector<uint32_t> encode(const std::string& text) override {
+        std::vector<uint32_t> ids(text.size() + 1);  // (every id covers at least one byte)
+        size_t n = 0;
+        ck(mf_tokenizer_encode(t_, text.data(), text.size(), ids.data(), ids.size(), &n), "mf_tokenizer_encode");
+        ids.resize(n);
+        return ids;
+    }
+    std::string decode(const std::vector<uint32_t>& ids) override { return bytes(ids.data(), ids.size()); }
+    std::string decode_token(uint32_t id) override { return bytes(&id, 1); }
+    std::string apply_chat_template(const std::vector<Message>& messages, const std::vector<Tool>& tools,
+                                    bool add_generation_prompt) override {
+        // the JSON the reference's Qwen3Tokenizer builds from these structs
+        nlohmann::ordered_json msgs = nlohmann::ordered_json::array(), tl = nlohmann::ordered_json::array();
+        for (const auto& m : messages) {
+            nlohmann::ordered_json j;
+            j["role"] = m.role;
+            j["content"] = m.content;
+            if (!m.reasoning_content.empty()) j["reasoning_content"] = m.reasoning_content;
+            if (!m.tool_calls.empty()) {
+                j["tool_calls"] = nlohmann::ordered_json::array();
+                for (const auto& tc : m.tool_calls)
+                    j["tool_calls"].push_back({{"name", tc.first}, {"arguments", nlohmann::ordered_json::parse(tc.second)}});
+            }
+            msgs.push_back(j);
+        }
+        for (const auto& t : tools)
+            tl.push_back({{"name", t.name}, {"description", t.description},
+                          {"parameters", nlohmann::ordered_json::parse(t.parameters)}});
+        const std::string mj = msgs.dump(), tj = tl.dump();
+        std::string out(4096, '\0');
+        size_t n = 0;
+        for (int pass = 0; pass < 2; ++pass) {
+            ck(mf_tokenizer_apply_chat_template(t_, mj.c_str(), tj.c_str(), add_generation_prompt, &out[0], out.size(),
+                                                &n),
+               "mf_tokenizer_apply_chat_template");
+            if (n <= out.size()) break;
+            out.resize(n);
+        }
+        out.resize(n);
+        return out;
+    }
+
+private:
+    std::string bytes(const uint32_t* ids, size_t k) {
+        std::string out(16 * k + 16, '\0');
+        size_t n = 0;
+        for (int pass = 0; pass < 2; ++pass) {
+            ck(mf_tokenizer_decode(t_, ids, k, &out[0], out.size(), &n), "mf_tokenizer_decode");
+            if (n <= out.size()) break;
+            out.resize(n);
+        }
+        out.resize(n);
+        return out;
+    }
+    mf_tokenizer* t_ = nullptr;
+};
 
 class CudaQwen3 : public BaseModel {
 public:
@@ -81,6 +155,7 @@ public:
         ck(mf_init(1, &dev), "mf_init");
         ck(mf_model_load(path.c_str(), &mp, 0, &m_), "mf_model_load");
         ck(mf_model_to_cuda(m_), "mf_model_to_cuda");
+        tokenizer = std::make_unique<CudaTokenizer>(path, config->eos_token_id, config->padding_token_id);
     }
     ~CudaQwen3() override {
         if (m_) mf_model_free(m_);
@@ -128,7 +203,8 @@ int usage() {
     std::fprintf(stderr,
                  "usage: minfer_cuda_app bench MODEL [--seed S] [--max-seq N]\n"
                  "       minfer_cuda_app generate MODEL --prompt-file F --gen G [--max-seq N]\n"
-                 "           [--temp T --top-k K --top-p P --min-p M --pres X --seed S]\n");
+                 "           [--temp T --top-k K --top-p P --min-p M --pres X --seed S]\n"
+                 "       minfer_cuda_app text MODEL --prompt TEXT --gen G [--max-seq N] [sampler flags]\n");
     return 2;
 }
 
@@ -137,7 +213,7 @@ int usage() {
 int main(int argc, char** argv) {
     if (argc < 3) return usage();
     const std::string mode = argv[1], model = argv[2];
-    std::string prompt_file;
+    std::string prompt_file, prompt_text;
     size_t gen = 16, max_seq = 0, top_k = 1;
     float temp = 0.f, top_p = 1.f, min_p = 0.f, pres = 0.f;
     int seed = 0;
@@ -146,6 +222,7 @@ int main(int argc, char** argv) {
         if (i + 1 >= argc) return usage();
         const std::string v = argv[++i];
         if (a == "--prompt-file") prompt_file = v;
+        else if (a == "--prompt") prompt_text = v;
         else if (a == "--gen") gen = std::stoul(v);
         else if (a == "--max-seq") max_seq = std::stoul(v);
         else if (a == "--temp") temp = std::stof(v);
@@ -167,6 +244,8 @@ int main(int argc, char** argv) {
             if (max_seq == 0) max_seq = prompt.size() + gen + 1;
         } else if (mode == "bench") {
             if (max_seq == 0) max_seq = 4096;
+        } else if (mode == "text") {
+            if (max_seq == 0) max_seq = 1024;
         } else {
             return usage();
         }
@@ -179,6 +258,13 @@ int main(int argc, char** argv) {
             std::printf("{\"mode\":\"bench\",\"num_tokens_gen\":%d,\"prefill_time\":%.6f,\"ttft\":%.6f,"
                         "\"throughput\":%.3f,\"bandwidth\":%.3f}\n",
                         st.num_tokens_gen, st.prefill_time, st.ttft, st.throughput, st.bandwidth);
+            return 0;
+        }
+        if (mode == "text") {
+            m.generate(prompt_text);  // the reference's text loop, unchanged (it prints its own output)
+            const GenStats& st = m.gen_stats();
+            std::printf("{\"mode\":\"text\",\"num_tokens_gen\":%d,\"throughput\":%.3f}\n", st.num_tokens_gen,
+                        st.throughput);
             return 0;
         }
         const std::vector<uint32_t> ids = m.generate_ids(prompt, gen);

@@ -53,3 +53,34 @@ def test_reference_benchmark_on_cuda(gpu):
     out = run_app("bench", tiny_model("tiny-bf16"), "--seed", 30, "--max-seq", 1024)
     assert out["num_tokens_gen"] == 128
     assert out["throughput"] > 0 and out["prefill_time"] > 0 and out["bandwidth"] > 0
+
+
+def test_reference_text_loop_on_cuda(gpu):
+    """The reference's BaseModel::generate(std::string&), unchanged, with this
+    runtime's tokenizer behind its BaseTokenizer interface and this runtime's
+    forward: it prints the chat-template prompt, the token count and the
+    generated text that the Python runtime produces for the same prompt
+    (token-by-token prefill on both sides, so the logits are the same)."""
+    from conftest import text_model
+    from minfer_b200.model import Qwen3Model, RunParams
+    from minfer_b200.tokenizer import Qwen3Tokenizer
+
+    path = text_model()
+    text = "Hello, world! It's 2 + 2 = 4"
+    G = 24
+    assert APP.exists(), "integration/_build/minfer_cuda_app was not built (make -C integration)"
+    r = subprocess.run([str(APP), "text", path, "--prompt", text, "--gen", str(G), "--max-seq", "256"],
+                       capture_output=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    out = r.stdout
+    tok = Qwen3Tokenizer.from_gguf(path)
+    formatted = tok.apply_chat_template([{"role": "user", "content": text}], [], True)
+    prompt = tok.encode(formatted)
+    assert b"Formatted message:\n" + formatted.encode() + b"\n" in out
+    assert b"Number of tokens: %d\n" % len(prompt) in out
+    m = Qwen3Model(path, RunParams(num_iters=G, max_seq_len=256)).set_device("cuda")
+    ids, _, _ = m.generate(prompt, G, stop_at_eos=True, token_prefill=True)
+    n = len(prompt)
+    assert b"Prefill progress: %d/%d\r\n" % (n, n) + tok.decode(ids) + b"\n\n" in out
+    summary = json.loads([ln for ln in out.decode(errors="replace").splitlines() if ln.startswith("{")][-1])
+    assert summary["num_tokens_gen"] == len(ids)
