@@ -105,32 +105,39 @@ def build_host(force: bool = False, jobs: int = 8) -> Path:
     return LIBHOST
 
 
+def _reference(reference: str | None) -> str | None:
+    # the reference checkout: the argument, else $MF_REFERENCE; none by default
+    return reference or os.environ.get("MF_REFERENCE") or None
+
+
 def build_oracle(reference: str | None = None) -> None:
-    """The oracle restatement always; the reference's own CPU path when its
-    sources are present (development container only)."""
+    """The oracle restatement always; the reference's own CPU path when a
+    reference checkout is given (argument or $MF_REFERENCE) and present."""
     targets = ["port"]
-    ref = reference or os.environ.get("MF_REFERENCE", "/root/reference")
-    if Path(ref, "src", "ops", "kernels.cpp").exists():
+    ref = _reference(reference)
+    if ref and Path(ref, "src", "ops", "kernels.cpp").exists():
         targets.append("ref")
-    _run(["make", "-s", "-C", str(ORACLE), f"REF={ref}", *targets])
+    _run(["make", "-s", "-C", str(ORACLE), *([f"REF={ref}"] if ref else []), *targets])
 
 
 def build_integration(reference: str | None = None) -> None:
     """minfer's own host loop linked against the CUDA runtime
-    (integration/cuda_backend.cpp), where the reference sources are present."""
-    ref = reference or os.environ.get("MF_REFERENCE", "/root/reference")
-    if Path(ref, "src", "base", "model.cpp").exists():
+    (integration/cuda_backend.cpp), where a reference checkout is given."""
+    ref = _reference(reference)
+    if ref and Path(ref, "src", "base", "model.cpp").exists():
         _run(["make", "-s", "-C", str(ROOT / "integration"), f"REF={ref}"])
 
 
-def build_all(force: bool = False, oracle: bool = True) -> None:
+def build_all(force: bool = False, oracle: bool = True, reference: str | None = None) -> None:
     build_cuda(force)
     build_host(force)
     if oracle:
-        build_oracle()
-        build_integration()
+        build_oracle(reference)
+        build_integration(reference)
 
 
 if __name__ == "__main__":
-    build_all(force="--force" in sys.argv, oracle="--no-oracle" not in sys.argv)
+    # python -m minfer_b200.build [--force] [--no-oracle] [--reference DIR]
+    ref = sys.argv[sys.argv.index("--reference") + 1] if "--reference" in sys.argv else None
+    build_all(force="--force" in sys.argv, oracle="--no-oracle" not in sys.argv, reference=ref)
     print("built", LIBMFCUDA, LIBHOST)

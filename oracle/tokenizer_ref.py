@@ -1,5 +1,5 @@
 """ctypes access to the reference's own tokenizer (oracle/_ref/libtokenizer_ref.so,
-built by `make -C oracle tokenizer` from src/models/qwen3/tokenizer.cpp and the
+built by `make -C oracle REF=<reference checkout> tokenizer` from src/models/qwen3/tokenizer.cpp and the
 vendored minja/nlohmann headers, against the system PCRE2 runtime).
 
 Test infrastructure: the tokenizer golden vectors come from here, and the

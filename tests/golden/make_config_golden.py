@@ -113,7 +113,7 @@ def make(name: str, model_dir: Path) -> dict:
 
 def main(argv: list[str]) -> None:
     if not oracle_py.ref_available():
-        sys.exit("oracle/_ref is not built (make -C oracle ref)")
+        sys.exit("oracle/_ref is not built (make -C oracle REF=<reference checkout> ref)")
     names = argv or list(CASES)
     model_dir = Path(os.environ.get("MF_MODEL_DIR", "/dev/shm/minfer_b200_cfg"))
     model_dir.mkdir(parents=True, exist_ok=True)

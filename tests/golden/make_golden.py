@@ -35,7 +35,7 @@ CASES = [
 
 def main():
     if not ref_available():
-        sys.exit("oracle/_ref is not built (make -C oracle ref)")
+        sys.exit("oracle/_ref is not built (make -C oracle REF=<reference checkout> ref)")
     for model, P, pseed, G, smp in CASES:
         path = tiny_model(model)
         prompt = random_prompt(P, TINY[model].vocab, pseed)

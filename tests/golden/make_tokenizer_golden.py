@@ -10,7 +10,7 @@
   prompt of its chat template path (minja).
 
 Run from the repository root in the development container, after
-`make -C oracle tokenizer`:
+`make -C oracle REF=<reference checkout> tokenizer`:
     python tests/golden/make_tokenizer_golden.py
 """
 import json
@@ -248,7 +248,7 @@ def chat_cases():
 
 def main():
     if not tokenizer_ref.available():
-        sys.exit("oracle/_ref/libtokenizer_ref.so is not built (make -C oracle tokenizer)")
+        sys.exit("oracle/_ref/libtokenizer_ref.so is not built (make -C oracle REF=<reference checkout> tokenizer)")
     tokens, types, merges, eos, pad = build_vocab()
     vocab = {"tokens": [t.hex() for t in tokens], "types": types, "merges": [m.hex() for m in merges],
              "eos": eos, "pad": pad, "templates": TEMPLATES}

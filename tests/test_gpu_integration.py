@@ -29,7 +29,7 @@ MARGIN_TOL = 1e-4
 
 
 def run_app(*args) -> dict:
-    assert APP.exists(), "integration/_build/minfer_cuda_app was not built (make -C integration)"
+    assert APP.exists(), "integration/_build/minfer_cuda_app was not built (make -C integration REF=<reference checkout>)"
     r = subprocess.run([str(APP), *map(str, args)], capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
     return json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("{")][-1])
@@ -68,7 +68,7 @@ def test_reference_text_loop_on_cuda(gpu):
     path = text_model()
     text = "Hello, world! It's 2 + 2 = 4"
     G = 24
-    assert APP.exists(), "integration/_build/minfer_cuda_app was not built (make -C integration)"
+    assert APP.exists(), "integration/_build/minfer_cuda_app was not built (make -C integration REF=<reference checkout>)"
     r = subprocess.run([str(APP), "text", path, "--prompt", text, "--gen", str(G), "--max-seq", "256"],
                        capture_output=True, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
