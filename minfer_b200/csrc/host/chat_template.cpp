@@ -1763,6 +1763,16 @@ const Value& need(CallArgs& a, size_t i, const char* pname, const char* fname) {
         if (kv.first == pname) return kv.second;
     throw std::runtime_error(std::string(fname) + ": missing argument '" + pname + "'");
 }
+// Builtins with named parameters take them by position or by name; extra
+// positional arguments and unknown names are errors.
+void params(const CallArgs& a, const char* fname, std::initializer_list<const char*> names) {
+    if (a.pos.size() > names.size()) throw std::runtime_error(std::string("Too many positional params for ") + fname);
+    for (const auto& kv : a.kw) {
+        bool known = false;
+        for (const char* n : names) known = known || kv.first == n;
+        if (!known) throw std::runtime_error("Unknown argument " + kv.first + " for function " + fname);
+    }
+}
 const Value* opt(CallArgs& a, size_t i, const char* pname) {
     if (i < a.pos.size()) return &a.pos[i];
     for (auto& kv : a.kw)
@@ -1789,13 +1799,16 @@ Ctx builtins() {
     auto g = std::make_shared<Context>();
     auto def = [&](const char* name, Value::Fn f) { g->set(name, Value::function(std::move(f))); };
     def("raise_exception", [](CallArgs& a) -> Value {
+        params(a, "raise_exception", {"message"});
         throw std::runtime_error(need(a, 0, "message", "raise_exception").str());
     });
     def("tojson", [](CallArgs& a) {
+        params(a, "tojson", {"value", "indent"});
         const Value* ind = opt(a, 1, "indent");
         return Value(need(a, 0, "value", "tojson").dump(ind ? (int)ind->i() : -1, true));
     });
     def("items", [](CallArgs& a) {
+        params(a, "items", {"object"});
         const Value& o = need(a, 0, "object", "items");
         if (!o.is_object()) throw std::runtime_error("Can only get item pairs from a mapping");
         Value r = Value::array();
@@ -1803,17 +1816,20 @@ Ctx builtins() {
         return r;
     });
     def("last", [](CallArgs& a) {
+        params(a, "last", {"items"});
         const Value& v = need(a, 0, "items", "last");
         if (!v.is_array()) throw std::runtime_error("object is not a list");
         return v.arr().empty() ? Value() : v.arr().back();
     });
     def("trim", [](CallArgs& a) {
+        params(a, "trim", {"text"});
         const Value& v = need(a, 0, "text", "trim");
         return v.is_null() ? v : Value(strip_chars(v.str(), "", true, true));
     });
     for (const char* nm : {"lower", "upper"}) {
         const bool up = nm[0] == 'u';
         def(nm, [up](CallArgs& a) {
+            params(a, up ? "upper" : "lower", {"text"});
             const Value& v = need(a, 0, "text", up ? "upper" : "lower");
             if (v.is_null()) return v;
             std::string s = v.str();
@@ -1831,10 +1847,14 @@ Ctx builtins() {
         const Value &v = a.pos[0], &d = a.pos[1];
         return boolean ? (v.truthy() ? v : d) : (v.is_null() ? d : v);
     });
-    auto esc = [](CallArgs& a) { return Value(html_escape(need(a, 0, "text", "escape").str())); };
+    auto esc = [](CallArgs& a) {
+        params(a, "escape", {"text"});
+        return Value(html_escape(need(a, 0, "text", "escape").str()));
+    };
     def("e", esc);
     def("escape", esc);
     def("joiner", [](CallArgs& a) {
+        params(a, "joiner", {"sep"});
         const Value* s = opt(a, 0, "sep");
         const std::string sep = s ? s->str() : "";
         auto first = std::make_shared<bool>(true);
@@ -1846,8 +1866,12 @@ Ctx builtins() {
             return Value(sep);
         });
     });
-    def("count", [](CallArgs& a) { return Value((int64_t)need(a, 0, "items", "count").size()); });
+    def("count", [](CallArgs& a) {
+        params(a, "count", {"items"});
+        return Value((int64_t)need(a, 0, "items", "count").size());
+    });
     def("dictsort", [](CallArgs& a) {
+        params(a, "dictsort", {"value"});
         if (a.pos.size() + a.kw.size() != 1) throw std::runtime_error("dictsort expects exactly 1 argument");
         const Value& v = need(a, 0, "value", "dictsort");
         std::vector<std::string> keys;
@@ -1858,6 +1882,7 @@ Ctx builtins() {
         return r;
     });
     def("join", [](CallArgs& a) {
+        params(a, "join", {"items", "d"});
         const Value* d = opt(a, 1, "d");
         const std::string sep = d ? d->str() : "";
         const Value* items = opt(a, 0, "items");
@@ -1877,14 +1902,25 @@ Ctx builtins() {
         return ns;
     });
     auto equalto = [](CallArgs& a) {
+        params(a, "equalto", {"expected", "actual"});
         return Value(need(a, 1, "actual", "equalto").equals(need(a, 0, "expected", "equalto")));
     };
     def("equalto", equalto);
     def("==", equalto);
-    def("length", [](CallArgs& a) { return Value((int64_t)need(a, 0, "items", "length").size()); });
-    def("safe", [](CallArgs& a) { return Value(need(a, 0, "value", "safe").to_str()); });
-    def("string", [](CallArgs& a) { return Value(need(a, 0, "value", "string").to_str()); });
+    def("length", [](CallArgs& a) {
+        params(a, "length", {"items"});
+        return Value((int64_t)need(a, 0, "items", "length").size());
+    });
+    def("safe", [](CallArgs& a) {
+        params(a, "safe", {"value"});
+        return Value(need(a, 0, "value", "safe").to_str());
+    });
+    def("string", [](CallArgs& a) {
+        params(a, "string", {"value"});
+        return Value(need(a, 0, "value", "string").to_str());
+    });
     def("int", [](CallArgs& a) {
+        params(a, "int", {"value"});
         const Value& v = need(a, 0, "value", "int");
         if (v.is_null()) return Value((int64_t)0);
         if (v.is_string()) {
@@ -1897,14 +1933,17 @@ Ctx builtins() {
         return Value((int64_t)0);
     });
     def("list", [](CallArgs& a) {
+        params(a, "list", {"items"});
         const Value& v = need(a, 0, "items", "list");
         if (!v.is_array()) throw std::runtime_error("object is not iterable");
         return v;
     });
     def("in", [](CallArgs& a) {
+        params(a, "in", {"item", "items"});
         return Value(contains_value(need(a, 0, "item", "in"), need(a, 1, "items", "in")));
     });
     def("unique", [](CallArgs& a) {
+        params(a, "unique", {"items"});
         const Value& v = need(a, 0, "items", "unique");
         if (!v.is_array()) throw std::runtime_error("object is not iterable");
         Value r = Value::array();
@@ -1919,6 +1958,31 @@ Ctx builtins() {
             if (!seen) r.push(x);
         }
         return r;
+    });
+    def("indent", [](CallArgs& a) {
+        params(a, "indent", {"text", "indent", "first"});
+        const std::string text = need(a, 0, "text", "indent").str();
+        const Value* w = opt(a, 1, "indent");
+        const Value* f = opt(a, 2, "first");
+        if (f && f->kind() != Value::BOOL) throw std::runtime_error("indent: first must be a boolean");
+        const bool first = f && f->b();
+        const std::string pad(w ? (size_t)std::max<int64_t>(0, w->i()) : 0, ' ');
+        // lines split at '\n' (a final newline ends the last line), each indented
+        // but the first unless `first`; a final newline is kept
+        std::string out;
+        size_t b = 0;
+        bool is_first = true;
+        while (b < text.size()) {
+            size_t e = text.find('\n', b);
+            if (e == std::string::npos) e = text.size();
+            if (!is_first) out += '\n';
+            if (!is_first || first) out += pad;
+            out.append(text, b, e - b);
+            is_first = false;
+            b = e + 1;
+        }
+        if (!text.empty() && text.back() == '\n') out += '\n';
+        return Value(out);
     });
     def("range", [](CallArgs& a) {
         int64_t v[3] = {0, 0, 1};

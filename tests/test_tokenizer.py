@@ -326,7 +326,8 @@ def _random_expression(rng, d=0):
     atoms = ["1", "2", "0", "-3", "2.5", "0.1", "'ab'", "'a b c'", "''", "\"x'y\"", "true", "false", "none",
              "[1, 2, 3]", "[]", "['x', 'y']", "{'k': 1, 'j': 'v'}", "{}", "messages", "messages[0]",
              "messages[0].content", "messages[-1].role", "add_generation_prompt", "bos_token", "undefined_thing",
-             "(1, 'a')", "[none, 0, '']", "'  pad\\n'", "'A-b-C'", "10", "7", "3.0"]
+             "(1, 'a')", "[none, 0, '']", "'  pad\\n'", "'A-b-C'", "10", "7", "3.0", "'l1\\nl2\\n\\nl4'",
+             "'\\n'"]
     if d > 3 or rng.random() < 0.3:
         return rng.choice(atoms)
     r = rng.random()
@@ -338,7 +339,8 @@ def _random_expression(rng, d=0):
         f = rng.choice(["length", "trim", "tojson", "upper", "lower", "list", "unique", "last", "count", "string", "int",
                         "items", "dictsort", "safe", "escape", "join(',')", "default('dflt')", "default('d', true)",
                         "map(attribute='role')", "selectattr('role')", "select('equalto', 1)", "reject('equalto', 1)",
-                        "tojson(indent=2)", "join", "first"])
+                        "tojson(indent=2)", "join", "first", "indent(2)", "indent(3, true)", "indent(first=true)",
+                        "length(1)", "tojson(bogus=1)", "trim('x')", "string"])
         return f"({a} | {f})"
     if r < 0.6:
         m = rng.choice(["strip()", "strip('a')", "lstrip()", "rstrip('\\n')", "split(' ')", "split('-')", "upper()",
