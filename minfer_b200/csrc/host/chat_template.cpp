@@ -572,6 +572,15 @@ struct Expr {
 
 Value eval(const Expr& e, const Ctx& ctx);
 
+// The context of the expression that calls a callable (a macro evaluates
+// its parameters' defaults there).
+thread_local const Ctx* g_caller = nullptr;
+struct CallerScope {
+    const Ctx* saved;
+    explicit CallerScope(const Ctx& c) : saved(g_caller) { g_caller = &c; }
+    ~CallerScope() { g_caller = saved; }
+};
+
 Value::Arr::size_type wrap_index(int64_t i, size_t n) { return (size_t)(i < 0 ? i + (int64_t)n : i); }
 
 bool contains_value(const Value& item, const Value& container) {
@@ -889,12 +898,14 @@ Value eval(const Expr& e, const Ctx& ctx) {
         case Expr::ATTR_CALL: {
             Value o = eval(*e.a, ctx);
             CallArgs a = eval_args(e, ctx);
+            CallerScope cs(ctx);
             return method_call(o, e.name, a);
         }
         case Expr::CALL: {
             Value f = eval(*e.a, ctx);
             if (!f.is_callable()) throw std::runtime_error("Object is not callable: " + f.dump(2));
             CallArgs a = eval_args(e, ctx);
+            CallerScope cs(ctx);
             return f.call(a);
         }
         case Expr::FILTER: {
@@ -910,6 +921,7 @@ Value eval(const Expr& e, const Ctx& ctx) {
                     f = eval(p, ctx);
                 }
                 a.pos.insert(a.pos.begin(), r);
+                CallerScope cs(ctx);
                 r = f.call(a);
             }
             return r;
@@ -1390,7 +1402,7 @@ ExprP parse_expression(const std::string& src) {
 // template nodes
 
 struct TemplateNode {
-    enum Kind { SEQ, TEXT, OUT, IF, FOR, SET, SET_BLOCK, BREAK, CONTINUE } kind;
+    enum Kind { SEQ, TEXT, OUT, IF, FOR, SET, SET_BLOCK, BREAK, CONTINUE, MACRO, FILTER_BLOCK } kind;
     std::string text;                                  // TEXT
     ExprP expr;                                        // OUT, SET value, FOR iterable
     ExprP cond;                                        // FOR filter
@@ -1398,7 +1410,8 @@ struct TemplateNode {
     std::string ns;                                    // SET namespace
     std::vector<std::pair<ExprP, std::shared_ptr<TemplateNode>>> branches;  // IF (null cond: else)
     std::vector<std::shared_ptr<TemplateNode>> kids;   // SEQ
-    std::shared_ptr<TemplateNode> body, else_body;     // FOR, SET_BLOCK
+    std::shared_ptr<TemplateNode> body, else_body;     // FOR, SET_BLOCK, MACRO, FILTER_BLOCK
+    std::vector<std::pair<std::string, ExprP>> params; // MACRO parameters (default or null)
     explicit TemplateNode(Kind k) : kind(k) {}
 };
 
@@ -1507,6 +1520,53 @@ void render_node(const TemplateNode& n, const Ctx& ctx, std::string& out) {
             std::string s;
             render_node(*n.body, ctx, s);
             ctx->set(n.names[0], Value(s));
+            return;
+        }
+        case TemplateNode::MACRO: {
+            // a callable in the defining scope; a call binds its arguments in
+            // that same scope (they stay set there), evaluates the defaults of
+            // the parameters not passed in the caller's scope, and returns the
+            // body's text
+            const TemplateNode* node = &n;
+            std::weak_ptr<Context> def = ctx;
+            ctx->set(n.names[0], Value::function([node, def](CallArgs& a) {
+                         Ctx c = def.lock();
+                         if (!c) throw std::runtime_error("macro called outside its template");
+                         const auto& ps = node->params;
+                         std::vector<bool> given(ps.size(), false);
+                         for (size_t i = 0; i < a.pos.size(); ++i) {
+                             if (i >= ps.size())
+                                 throw std::runtime_error("Too many positional arguments for macro " + node->names[0]);
+                             c->set(ps[i].first, a.pos[i]);
+                             given[i] = true;
+                         }
+                         for (auto& kv : a.kw) {
+                             size_t k = 0;
+                             while (k < ps.size() && ps[k].first != kv.first) ++k;
+                             if (k == ps.size())
+                                 throw std::runtime_error("Unknown parameter name for macro " + node->names[0] + ": " +
+                                                          kv.first);
+                             c->set(kv.first, kv.second);
+                             given[k] = true;
+                         }
+                         const Ctx& caller = g_caller ? *g_caller : c;
+                         for (size_t i = 0; i < ps.size(); ++i)
+                             if (!given[i] && ps[i].second) c->set(ps[i].first, eval(*ps[i].second, caller));
+                         std::string body;
+                         render_node(*node->body, c, body);
+                         return Value(body);
+                     }));
+            return;
+        }
+        case TemplateNode::FILTER_BLOCK: {
+            Value f = eval(*n.expr, ctx);
+            if (!f.is_callable()) throw std::runtime_error("Filter must be a callable: " + f.dump());
+            std::string body;
+            render_node(*n.body, ctx, body);
+            CallArgs a;
+            a.pos.emplace_back(body);
+            CallerScope cs(ctx);
+            out += f.call(a).to_str();
             return;
         }
         case TemplateNode::BREAK: throw LoopControl{true};
@@ -1749,6 +1809,42 @@ struct TreeBuilder {
             NodeP body = sequence({"endgeneration"});
             expect_end("endgeneration");
             return body;
+        }
+        if (w == "macro") {
+            auto n = std::make_shared<TemplateNode>(TemplateNode::MACRO);
+            ExprParser ep{lex(t.rest)};
+            if (ep.peek().k != Tok::ID || is_reserved(ep.peek().s)) throw std::runtime_error("Expected macro name in macro block");
+            n->names = {ep.peek().s};
+            ++ep.p;
+            ep.need_op("(");
+            if (!ep.eat_op(")")) {
+                while (true) {
+                    if (ep.peek().k != Tok::ID || is_reserved(ep.peek().s))
+                        throw std::domain_error("macro parameters other than names are not supported");
+                    std::string pname = ep.peek().s;
+                    ++ep.p;
+                    ExprP dflt;
+                    if (ep.eat_op("=")) dflt = ep.expression();
+                    n->params.emplace_back(pname, dflt);
+                    if (ep.eat_op(",")) {
+                        if (ep.eat_op(")")) break;
+                        continue;
+                    }
+                    ep.need_op(")");
+                    break;
+                }
+            }
+            if (!ep.at_end()) throw std::runtime_error("unexpected tokens in macro statement");
+            n->body = sequence({"endmacro"});
+            expect_end("endmacro");
+            return n;
+        }
+        if (w == "filter") {
+            auto n = std::make_shared<TemplateNode>(TemplateNode::FILTER_BLOCK);
+            n->expr = parse_expression(t.rest);
+            n->body = sequence({"endfilter"});
+            expect_end("endfilter");
+            return n;
         }
         throw std::domain_error("unsupported template statement: {% " + w + " %}");
     }
@@ -2104,6 +2200,10 @@ ChatTemplate::ChatTemplate(const std::string& source, std::string bos_token, std
         apply_whitespace(toks);
         TreeBuilder tb{toks};
         root_ = tb.sequence({});
+    } catch (const std::domain_error& e) {  // a construct that is not built
+        parse_error_ = e.what();
+        parse_unsupported_ = true;
+        return;
     } catch (const std::exception& e) {
         parse_error_ = e.what();
         return;
@@ -2221,8 +2321,14 @@ ChatTemplate::ChatTemplate(const std::string& source, std::string bos_token, std
 
 ChatTemplate::~ChatTemplate() = default;
 
+void ChatTemplate::check_parsed() const {
+    if (root_) return;
+    if (parse_unsupported_) throw std::domain_error("chat template uses " + parse_error_);
+    throw std::runtime_error("chat template does not parse: " + parse_error_);
+}
+
 std::string ChatTemplate::raw_render(const Value& messages, const Value* tools, bool add_generation_prompt) const {
-    if (!root_) throw std::runtime_error("chat template does not parse: " + parse_error_);
+    check_parsed();
     Ctx g = builtins();
     add_lookup_filters(g);
     auto ctx = std::make_shared<Context>();
@@ -2256,7 +2362,7 @@ std::string ChatTemplate::try_raw_render(const Value& messages, const Value* too
 }
 
 std::string ChatTemplate::render(const Value& messages, const Value& tools, bool add_generation_prompt) const {
-    if (!root_) throw std::runtime_error("chat template does not parse: " + parse_error_);
+    check_parsed();
     const Value* tools_var = tools.is_null() ? nullptr : &tools;
     const bool has_tools = tools.is_array() && !tools.arr().empty();
     bool has_tool_calls = false, has_tool_responses = false, has_string_content = false;

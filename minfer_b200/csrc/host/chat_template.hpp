@@ -7,13 +7,15 @@
 // trim_blocks + lstrip_blocks + no trailing newline (the options the
 // reference's chat_template parses with); if/elif/else, for (tuple targets,
 // inline `if` filter, else, loop.*), set (names, tuples, namespace attributes,
-// block set), break/continue, generation blocks; the expression grammar with
+// block set), macros (parameters with defaults), filter blocks,
+// break/continue, generation blocks; the expression grammar with
 // minja's precedence, its value semantics (byte strings, integer division of
 // integers, objects always true, ...) and its filters/methods; the capability
 // probes and every polyfill of its chat_template (system role, typed content,
 // tools with an inferred tool-call example, tool calls, tool responses,
-// object arguments). Not built (rendering raises std::domain_error): macros,
-// call and filter blocks, recursive loops.
+// object arguments). Not built (rendering raises std::domain_error): call
+// blocks (the reference's engine has none either), recursive loops, and
+// argument expansion (*args / **kwargs) in calls.
 #pragma once
 
 #include <cstdint>
@@ -121,6 +123,8 @@ public:
 private:
     std::string raw_render(const Value& messages, const Value* tools, bool add_generation_prompt) const;
     std::string try_raw_render(const Value& messages, const Value* tools) const;
+    void check_parsed() const;  // throws the parse error, if any
+    bool parse_unsupported_ = false;
     std::shared_ptr<TemplateNode> root_;
     std::string parse_error_;
     std::string bos_, eos_;

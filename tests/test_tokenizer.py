@@ -188,10 +188,13 @@ def test_template_errors(vocab):
     with pytest.raises(MinferError) as e:
         t.apply_chat_template([{"role": "user", "content": "x"}] * 3)
     assert e.value.code == MF_E_STATE and "too many messages" in str(e.value)
-    macro = "{% macro f(x) %}{{ x }}{% endmacro %}{{ f(1) }}"
+    macro = "{% macro f(x, y='!') %}<{{ x }}{{ y }}>{% endmacro %}{{ f(1) }}{{ f('a', y='?') }}"
+    assert Qwen3Tokenizer.from_vocab(tokens, merges, types, macro).apply_chat_template(
+        [{"role": "user", "content": "x"}]) == "<1!><a?>"
+    call = "{% call f() %}x{% endcall %}"  # (call blocks: the reference's engine has none either)
     with pytest.raises(MinferError) as e:
-        Qwen3Tokenizer.from_vocab(tokens, merges, types, macro).apply_chat_template([{"role": "user", "content": "x"}])
-    assert e.value.code in (MF_E_UNSUPPORTED, MF_E_STATE)
+        Qwen3Tokenizer.from_vocab(tokens, merges, types, call).apply_chat_template([{"role": "user", "content": "x"}])
+    assert e.value.code == MF_E_UNSUPPORTED
     # a template that cannot show tools gets them in a system message (the tools polyfill)
     plain = "{% for m in messages %}{{ m.role }}: {{ m.content }}\n{% endfor %}"
     out = Qwen3Tokenizer.from_vocab(tokens, merges, types, plain).apply_chat_template(
@@ -390,7 +393,8 @@ def test_random_expressions_vs_reference(vocab):
 
 
 # random templates: text with spaces/newlines around nested for/if/set blocks,
-# loop variables, namespaces, break/continue and '-' trim markers
+# filter blocks and macros, loop variables, namespaces, break/continue and
+# '-' trim markers
 _WS = ["", " ", "  ", "\n", "\n  ", "  \n", "\t", "\n\n", " x ", "text\n", "\n    "]
 _EXPRS = ["m.role", "m.content", "loop.index", "loop.first", "loop.last", "loop.length", "loop.revindex",
           "ns.n", "x", "messages | length", "m.content[:3]", "bos_token", "loop.index0 ~ '/' ~ loop.length",
@@ -441,7 +445,18 @@ def _body(rng, depth, in_loop):
             parts.append(_body(rng, depth + 1, in_loop))
             parts.append(_tag(rng, "endset"))
             parts.append(_tag(rng, "z", "{"))
-        elif r < 0.9 and in_loop:
+        elif r < 0.88:
+            parts.append(_tag(rng, rng.choice(["filter upper", "filter trim", "filter lower", "filter indent"])))
+            parts.append(_body(rng, depth + 1, in_loop))
+            parts.append(_tag(rng, "endfilter"))
+        elif r < 0.9:
+            parts.append(_tag(rng, "macro mk(who, sep='-')"))
+            parts.append(rng.choice(_WS) + _tag(rng, "who ~ sep ~ x", "{") + rng.choice(_WS))
+            if rng.random() < 0.5:
+                parts.append(_tag(rng, "set x = x ~ '!'"))
+            parts.append(_tag(rng, "endmacro"))
+            parts.append(_tag(rng, rng.choice(["mk('a')", "mk('b', sep='+')", "mk(who='c')", "mk(1, 2)", "mk()"]), "{"))
+        elif r < 0.92 and in_loop:
             parts.append(_tag(rng, rng.choice(["break", "continue"])))
         else:
             parts.append(_tag(rng, "comment", "#"))
