@@ -216,8 +216,7 @@ int mf_tokenizer_pre_split(const mf_tokenizer* t, const char* text, size_t len, 
  * "parameters"} (or NULL for none), the objects the reference builds from its
  * Message/Tool structs (any JSON messages are accepted, e.g. OpenAI-shaped
  * tool calls). MF_E_STATE for errors the template raises, MF_E_UNSUPPORTED
- * for template constructs not built (recursive loops, argument expansion,
- * call blocks). */
+ * for template constructs not built (recursive loops, call blocks). */
 int mf_tokenizer_apply_chat_template(const mf_tokenizer* t, const char* messages_json, const char* tools_json,
                                      int add_generation_prompt, char* out, size_t cap, size_t* n);
 

@@ -692,8 +692,18 @@ bool is_test(const std::string& t, const Value& v) {
 CallArgs eval_args(const Expr& e, const Ctx& ctx) {
     CallArgs a;
     for (const auto& x : e.args) {
-        if (x->kind == Expr::UNARY && (x->name == "*" || x->name == "**"))
-            throw std::domain_error("argument expansion is not supported");
+        if (x->kind == Expr::UNARY && x->name == "*") {  // *list: its items as positional arguments
+            Value v = eval(*x->a, ctx);
+            if (!v.is_array()) throw std::runtime_error("Expansion operator only supported on arrays");
+            for (const Value& item : v.arr()) a.pos.push_back(item);
+            continue;
+        }
+        if (x->kind == Expr::UNARY && x->name == "**") {  // **dict: its entries as keyword arguments
+            Value v = eval(*x->a, ctx);
+            if (!v.is_object()) throw std::runtime_error("ExpansionDict operator only supported on objects");
+            for (const auto& kv : v.obj()) a.kw.emplace_back(kv.first, kv.second);
+            continue;
+        }
         a.pos.push_back(eval(*x, ctx));
     }
     for (const auto& kv : e.kwargs) a.kw.emplace_back(kv.first, eval(*kv.second, ctx));
@@ -1935,11 +1945,15 @@ Ctx builtins() {
     }
     def("default", [](CallArgs& a) {
         expect_args(a, "default", 2, 3, 0, 1);
+        auto as_bool = [](const Value& v) {
+            if (v.kind() != Value::BOOL) throw std::runtime_error("type must be boolean: " + v.dump());
+            return v.b();
+        };
         bool boolean = false;
         if (a.pos.size() == 3)
-            boolean = a.pos[2].truthy();
+            boolean = as_bool(a.pos[2]);
         else if (const Value* b = opt(a, 99, "boolean"))
-            boolean = b->truthy();
+            boolean = b->is_null() ? false : as_bool(*b);
         const Value &v = a.pos[0], &d = a.pos[1];
         return boolean ? (v.truthy() ? v : d) : (v.is_null() ? d : v);
     });

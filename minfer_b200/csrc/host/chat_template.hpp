@@ -14,8 +14,7 @@
 // probes and every polyfill of its chat_template (system role, typed content,
 // tools with an inferred tool-call example, tool calls, tool responses,
 // object arguments). Not built (rendering raises std::domain_error): call
-// blocks (the reference's engine has none either), recursive loops, and
-// argument expansion (*args / **kwargs) in calls.
+// blocks (the reference's engine has none either) and recursive loops.
 #pragma once
 
 #include <cstdint>

@@ -343,7 +343,8 @@ def _random_expression(rng, d=0):
                         "items", "dictsort", "safe", "escape", "join(',')", "default('dflt')", "default('d', true)",
                         "map(attribute='role')", "selectattr('role')", "select('equalto', 1)", "reject('equalto', 1)",
                         "tojson(indent=2)", "join", "first", "indent(2)", "indent(3, true)", "indent(first=true)",
-                        "length(1)", "tojson(bogus=1)", "trim('x')", "string"])
+                        "length(1)", "tojson(bogus=1)", "trim('x')", "string", "join(*['-'])", "tojson(**{'indent': 1})",
+                        "default(*[1, 2])"])
         return f"({a} | {f})"
     if r < 0.6:
         m = rng.choice(["strip()", "strip('a')", "lstrip()", "rstrip('\\n')", "split(' ')", "split('-')", "upper()",
