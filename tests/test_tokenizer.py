@@ -330,7 +330,12 @@ def _random_expression(rng, d=0):
              "[1, 2, 3]", "[]", "['x', 'y']", "{'k': 1, 'j': 'v'}", "{}", "messages", "messages[0]",
              "messages[0].content", "messages[-1].role", "add_generation_prompt", "bos_token", "undefined_thing",
              "(1, 'a')", "[none, 0, '']", "'  pad\\n'", "'A-b-C'", "10", "7", "3.0", "'l1\\nl2\\n\\nl4'",
-             "'\\n'"]
+             "'\\n'", "range(3)", "range(1, 7, 2)", "range(5, 0, -2)", "namespace(a=1).a", "namespace(a=1, b='x')",
+             "(messages | selectattr('role', 'equalto', 'user') | list)",
+             "(messages | map(attribute='content') | join(' '))", "(['b', 'a'] | map('upper') | list)",
+             "({'b': 1, 'a': 2} | dictsort)", "joiner(',')()", "(messages | rejectattr('role') | list)",
+             "([1, 2, 1] | select('equalto', 1) | list)", "({'a': 1}.items() | list)", "[3, 1].pop(0)",
+             "range(end=3)", "(messages | map(attribute='nope', default='d') | list)"]
     if d > 3 or rng.random() < 0.3:
         return rng.choice(atoms)
     r = rng.random()
