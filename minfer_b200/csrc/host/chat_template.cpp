@@ -31,8 +31,9 @@ Value Value::object() {
     return v;
 }
 Value Value::function(Fn f) {
-    Value v;
-    v.k_ = FUNC;
+    // a callable is also an (empty) object: it prints as {}, counts as a
+    // mapping, is true, and can carry attributes (a loop's cycle, ...)
+    Value v = object();
     v.fn_ = std::make_shared<Fn>(std::move(f));
     return v;
 }
@@ -64,7 +65,7 @@ Value::Obj& Value::obj() const {
     return *o_;
 }
 Value Value::call(CallArgs& a) const {
-    if (k_ != FUNC) throw std::runtime_error("Value is not callable: " + dump());
+    if (!fn_) throw std::runtime_error("Value is not callable: " + dump());
     return (*fn_)(a);
 }
 void Value::push(Value v) { arr().push_back(std::move(v)); }
@@ -241,7 +242,6 @@ void Value::dump_to(std::string& out, int indent, int level, bool json) const {
             nl(level);
             out += '}';
             break;
-        case FUNC: throw std::runtime_error("Cannot dump callable to JSON");
     }
 }
 
@@ -308,7 +308,7 @@ std::string Value::to_str() const {
 }
 
 bool Value::equals(const Value& o) const {
-    if (k_ == FUNC || o.k_ == FUNC) return k_ == o.k_ && fn_ == o.fn_;
+    if ((fn_ || o.fn_) && fn_ != o.fn_) return false;  // (the same callable: compared as objects below)
     if (k_ == ARR) {
         if (o.k_ != ARR || a_->size() != o.a_->size()) return false;
         for (size_t i = 0; i < a_->size(); ++i) {
@@ -845,6 +845,17 @@ Value method_call(const Value& obj, const std::string& m, CallArgs& a) {
     throw std::runtime_error("Unknown method: " + m);
 }
 
+// a binary operator or test whose left side is evaluated
+Value apply_operator(const Expr& e, const Value& l, const Ctx& ctx) {
+    if (e.kind == Expr::IS) {
+        const bool r = is_test(e.name, l);
+        return Value(e.negate ? !r : r);
+    }
+    if (e.name == "and") return l.truthy() ? Value(eval(*e.b, ctx).truthy()) : Value(false);
+    if (e.name == "or") return l.truthy() ? l : eval(*e.b, ctx);
+    return binary(e.name, l, eval(*e.b, ctx));
+}
+
 Value eval(const Expr& e, const Ctx& ctx) {
     switch (e.kind) {
         case Expr::LIT: return e.lit;
@@ -944,17 +955,17 @@ Value eval(const Expr& e, const Ctx& ctx) {
             if (e.name == "-") return v.kind() == Value::INT ? Value(-v.i()) : Value(-v.f());
             return v;
         }
-        case Expr::BIN: {
-            Value l = eval(*e.a, ctx);
-            if (l.is_callable()) throw std::domain_error("operators on callables are not supported");
-            if (e.name == "and") return l.truthy() ? Value(eval(*e.b, ctx).truthy()) : Value(false);
-            if (e.name == "or") return l.truthy() ? l : eval(*e.b, ctx);
-            return binary(e.name, l, eval(*e.b, ctx));
-        }
+        case Expr::BIN:
         case Expr::IS: {
             Value l = eval(*e.a, ctx);
-            const bool r = is_test(e.name, l);
-            return Value(e.negate ? !r : r);
+            if (l.is_callable()) {
+                // an operator on a callable makes a callable: called, it calls
+                // the left side and applies the operator to the result
+                const Expr* ep = &e;
+                Ctx c = ctx;
+                return Value::function([l, ep, c](CallArgs& a) { return apply_operator(*ep, l.call(a), c); });
+            }
+            return apply_operator(e, l, ctx);
         }
         case Expr::IFX:
             if (eval(*e.a, ctx).truthy()) return eval(*e.b, ctx);

@@ -34,7 +34,7 @@ struct CallArgs {
 
 class Value {
 public:
-    enum Kind { NUL, BOOL, INT, FLOAT, STR, ARR, OBJ, FUNC };
+    enum Kind { NUL, BOOL, INT, FLOAT, STR, ARR, OBJ };  // (a callable is an OBJ with a function)
     using Arr = std::vector<Value>;
     using Obj = std::vector<std::pair<std::string, Value>>;  // insertion order
     using Fn = std::function<Value(CallArgs&)>;
@@ -56,7 +56,7 @@ public:
     bool is_array() const { return k_ == ARR; }
     bool is_object() const { return k_ == OBJ; }
     bool is_number() const { return k_ == INT || k_ == FLOAT; }
-    bool is_callable() const { return k_ == FUNC; }
+    bool is_callable() const { return fn_ != nullptr; }
 
     bool b() const { return b_; }
     int64_t i() const;  // integers; floats truncate; anything else throws

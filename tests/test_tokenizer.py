@@ -335,7 +335,8 @@ def _random_expression(rng, d=0):
              "(messages | map(attribute='content') | join(' '))", "(['b', 'a'] | map('upper') | list)",
              "({'b': 1, 'a': 2} | dictsort)", "joiner(',')()", "(messages | rejectattr('role') | list)",
              "([1, 2, 1] | select('equalto', 1) | list)", "({'a': 1}.items() | list)", "[3, 1].pop(0)",
-             "range(end=3)", "(messages | map(attribute='nope', default='d') | list)"]
+             "range(end=3)", "(messages | map(attribute='nope', default='d') | list)", "range", "namespace",
+             "joiner(',')", "length", "(range == range)", "(range is defined)"]
     if d > 3 or rng.random() < 0.3:
         return rng.choice(atoms)
     r = rng.random()
