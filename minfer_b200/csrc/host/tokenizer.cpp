@@ -334,17 +334,16 @@ std::vector<uint32_t> Qwen3Tokenizer::bpe(const char* p, size_t n) const {
         std::sort(at.begin(), at.end());
         const Rule& rule = rules_[(size_t)rank];
         merged.clear();
-        int32_t prev_merged = -1;
         for (int32_t i : at) {
-            // stale entries (a symbol merged since) no longer show the rule's pair
+            // stale entries (a symbol merged since, or a repeated entry) no
+            // longer show the rule's pair
             const int32_t j = w[i].next;
-            if (i == prev_merged || j < 0 || w[i].sym != rule.left || w[j].sym != rule.right) continue;
+            if (j < 0 || w[i].sym != rule.left || w[j].sym != rule.right) continue;
             w[i].sym = rule.merged;
             w[i].next = w[j].next;
             if (w[j].next >= 0) w[w[j].next].prev = i;
             w[j].sym = -1;  // (removed)
             merged.push_back(i);
-            prev_merged = i;
         }
         // the pairs the merges made, at their lowest rank above this one
         for (int32_t i : merged) {
