@@ -402,6 +402,18 @@ def measure_long_context(workload: str, ctx: int, steps: int, warmup: int, rank:
             "file_seconds": round(t_gen, 1)}
 
 
+def guarded(fn, *args, **kw) -> dict:
+    """A secondary record: a failure is reported in the record instead of
+    ending the run (the main line is already measured)."""
+    try:
+        return fn(*args, **kw)
+    except Exception as e:  # reported, not fatal
+        import gc
+
+        gc.collect()  # (drops the failed record's model, whose frames the exception held)
+        return {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+
+
 def measure_sampled(workload: str, ctx: int, gen: int, local_rank: int) -> dict:
     """Sampled decode through the public generate call (the 1.7B workload's
     sampler: top-k 20, temperature 0.7, top-p 0.9, seed 42) after a ctx-token
@@ -668,11 +680,11 @@ def main():
             room = box[0]
         if room:
             m.close()
-            long_rec = measure_long_context(args.long_workload, args.long_context, args.steps, args.warmup, rank,
-                                            world, local_rank, peaks)
-            if not args.no_long_kv_bf16:  # the same run with the opt-in bf16 KV cache
-                long_rec["kv_bf16"] = measure_long_context(args.long_workload, args.long_context, args.steps,
-                                                           args.warmup, rank, world, local_rank, peaks, "bf16")
+            long_rec = guarded(measure_long_context, args.long_workload, args.long_context, args.steps,
+                               args.warmup, rank, world, local_rank, peaks)
+            if not args.no_long_kv_bf16 and "error" not in long_rec:  # the same run with the opt-in bf16 KV cache
+                long_rec["kv_bf16"] = guarded(measure_long_context, args.long_workload, args.long_context, args.steps,
+                                              args.warmup, rank, world, local_rank, peaks, "bf16")
         else:
             long_rec = {"skipped": f"no room for the {args.long_workload} file under {lp.parent}"}
 
@@ -690,8 +702,8 @@ def main():
             dist.broadcast_object_list(box, src=0)
             room = box[0]
         if room:
-            moe_rec = measure_long_context(args.moe_workload, args.moe_context, args.steps, args.warmup, rank, world,
-                                           local_rank, peaks, parity=True)
+            moe_rec = guarded(measure_long_context, args.moe_workload, args.moe_context, args.steps, args.warmup,
+                              rank, world, local_rank, peaks, parity=True)
         else:
             moe_rec = {"skipped": f"no room for the {args.moe_workload} file under {mp.parent}"}
 
@@ -740,7 +752,8 @@ def main():
             line["exchange_status"] = status
             line["parity"] = parity
         print(json.dumps(line), flush=True)
-    moe_bad = bool(moe_rec) and (moe_rec.get("parity_ok") is False or moe_rec.get("exchange_status", 0) != 0)
+    moe_bad = bool(moe_rec) and (moe_rec.get("parity_ok") is False or moe_rec.get("exchange_status", 0) != 0 or
+                                 "error" in moe_rec)
     failed = world > 1 and (not (parity["ok"] and status == 0) or moe_bad)
     if world > 1:
         import torch.distributed as dist
