@@ -25,6 +25,9 @@
  *       reference's tokenizer interface (include/minfer/base/tokenizer.hpp)
  *       over this runtime's tokenizer (mf_tokenizer_*), in place of the
  *       PCRE2/minja Qwen3Tokenizer; the loop prints what the reference prints.
+ *   minfer_cuda_app tokenize MODEL --prompt TEXT
+ *       CudaTokenizer alone (no GPU): the chat-template prompt of one user
+ *       message and its ids, as one JSON line.
  *
  * The layers are assembled as src/models/qwen3/model.cpp:9-86 does (views of
  * the mapped file, never run here) so BaseModel::get_read_bytes reports the
@@ -204,7 +207,8 @@ int usage() {
                  "usage: minfer_cuda_app bench MODEL [--seed S] [--max-seq N]\n"
                  "       minfer_cuda_app generate MODEL --prompt-file F --gen G [--max-seq N]\n"
                  "           [--temp T --top-k K --top-p P --min-p M --pres X --seed S]\n"
-                 "       minfer_cuda_app text MODEL --prompt TEXT --gen G [--max-seq N] [sampler flags]\n");
+                 "       minfer_cuda_app text MODEL --prompt TEXT --gen G [--max-seq N] [sampler flags]\n"
+                 "       minfer_cuda_app tokenize MODEL --prompt TEXT\n");
     return 2;
 }
 
@@ -234,6 +238,26 @@ int main(int argc, char** argv) {
         else return usage();
     }
     try {
+        if (mode == "tokenize") {  // the BaseTokenizer adapter alone, on the host
+            mf_tokenizer* probe = nullptr;
+            ck(mf_tokenizer_load(model.c_str(), &probe), "mf_tokenizer_load");
+            uint32_t eos = 0, pad = 0;
+            ck(mf_tokenizer_info(probe, nullptr, &eos, &pad), "mf_tokenizer_info");
+            mf_tokenizer_free(probe);
+            CudaTokenizer tok(model, eos, pad);
+            std::vector<BaseTokenizer::Message> msgs;
+            msgs.emplace_back("user", prompt_text);
+            const std::string formatted = tok.apply_chat_template(msgs, {}, true);
+            const std::vector<uint32_t> ids = tok.encode(formatted);
+            nlohmann::ordered_json j;
+            j["mode"] = "tokenize";
+            j["formatted"] = formatted;
+            j["ids"] = ids;
+            j["round_trip"] = tok.decode(ids) == formatted;
+            j["eos"] = tok.get_eos_id();
+            std::printf("%s\n", j.dump().c_str());
+            return 0;
+        }
         std::vector<uint32_t> prompt;
         if (mode == "generate") {
             std::ifstream f(prompt_file, std::ios::binary);

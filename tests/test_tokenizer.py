@@ -504,3 +504,29 @@ def test_long_pieces_vs_reference(vocab):
             s = "".join(rng.choice(alphabet) for _ in range(n)).encode()
             assert len(t.pre_split(s)) == 1
             assert t.encode(s) == ref.encode(s), (n, alphabet)
+
+
+def test_integration_adapter_vs_reference():
+    """minfer's BaseTokenizer interface over this tokenizer (CudaTokenizer in
+    integration/cuda_backend.cpp, run here without a GPU) gives the
+    reference tokenizer's prompt and ids for a model file's vocabulary and
+    chat template."""
+    import subprocess
+
+    from conftest import TEXT_MODEL, text_model
+    from minfer_b200.gguf_synth import CHAT_TEMPLATE, synth_vocab
+
+    app = Path(__file__).resolve().parent.parent / "integration" / "_build" / "minfer_cuda_app"
+    if not app.exists() or not tokenizer_ref.available():
+        pytest.skip("the integration app or the reference tokenizer is not built (both need the reference sources)")
+    path = text_model()
+    text = "Hello, world! It's 2 + 2 = 4; 世界\n  tabs\there"
+    r = subprocess.run([str(app), "tokenize", path, "--prompt", text], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr[-2000:]
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    tokens, types, merges, eos, pad = synth_vocab(TEXT_MODEL.vocab, TEXT_MODEL.seed, TEXT_MODEL.byte_vocab)
+    ref = tokenizer_ref.RefTokenizer(tokens, types, merges, CHAT_TEMPLATE, eos, pad)
+    expected = ref.chat([{"role": "user", "content": text}], [], True)
+    assert out["formatted"] == expected
+    assert out["ids"] == ref.encode(expected.encode())
+    assert out["round_trip"] and out["eos"] == eos
