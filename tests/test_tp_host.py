@@ -100,7 +100,7 @@ def test_shard_load_splits(size):
     m = C.c_void_p()
     rc = host_lib().mf_model_load_tp(tiny_model("tiny-bf16").encode(), C.byref(rp), 0, 0, 4, C.byref(m))
     assert rc != MF_OK and "n_kv_heads" in last_error()
-    # the MoE model splits its 16 experts instead (expert parallelism): 2 ranks load, 3 do not divide
+    # the MoE model (2 KV heads, 16 experts): rows split at 2 ranks, experts at 4, 3 divides neither
     rc = host_lib().mf_model_load_tp(tiny_model("tiny-moe").encode(), C.byref(rp), 0, 1, 2, C.byref(m))
     assert rc == MF_OK, last_error()
     info = mf_model_info()
@@ -110,3 +110,36 @@ def test_shard_load_splits(size):
     assert rc != MF_OK and "expert_count" in last_error()
     rc = host_lib().mf_model_load_tp(tiny_model("tiny-bf16").encode(), C.byref(rp), 0, 2, 2, C.byref(m))
     assert rc != MF_OK
+
+
+def _expert_parallel(path, rank, size):
+    import ctypes as C
+
+    from minfer_b200._lib import MF_OK, host_lib, last_error, mf_model_info, mf_run_params
+
+    rp = mf_run_params(8, 64, 1, 0.0, 1.0, 0.0, 0.0, 0)
+    m = C.c_void_p()
+    rc = host_lib().mf_model_load_tp(path.encode(), C.byref(rp), 0, rank, size, C.byref(m))
+    assert rc == MF_OK, last_error()
+    info = mf_model_info()
+    assert host_lib().mf_model_info_get(m, C.byref(info)) == MF_OK
+    host_lib().mf_model_free(m)
+    return info.expert_parallel
+
+
+def test_moe_split_choice(monkeypatch):
+    """How a MoE model splits over the ranks (CPU side, at load): by FFN rows
+    inside every expert (attention by KV-head group) when the KV heads divide
+    over the ranks, else by experts; MF_MOE_EP=1 forces experts. The 4-KV-head
+    shape is 30B-A3B's head layout: rows at 2 and 4 ranks, experts at 8."""
+    from conftest import model_dir, tiny_model
+    from minfer_b200.gguf_synth import Qwen3Shape, ensure_gguf
+
+    kv2 = tiny_model("tiny-moe")
+    kv4 = ensure_gguf(model_dir() / "tiny-moe-kv4.gguf",
+                      Qwen3Shape(2, 256, 8, 4, 128, 128, 1024, "bf16", False, 16, 4, seed=108))
+    for path, size, want in [(kv2, 2, 0), (kv2, 4, 1), (kv2, 8, 1), (kv4, 2, 0), (kv4, 4, 0), (kv4, 8, 1)]:
+        for rank in range(size):
+            assert _expert_parallel(path, rank, size) == want, (path, size, rank)
+    monkeypatch.setenv("MF_MOE_EP", "1")
+    assert _expert_parallel(kv4, 0, 4) == 1
