@@ -530,3 +530,33 @@ def test_integration_adapter_vs_reference():
     assert out["formatted"] == expected
     assert out["ids"] == ref.encode(expected.encode())
     assert out["round_trip"] and out["eos"] == eos
+
+
+def test_c_abi_short_buffers(vocab):
+    """The C entry points write at most `cap` items and report the full count,
+    so a caller can size its buffer and call again."""
+    import ctypes as C
+
+    from minfer_b200._lib import MF_OK, host_lib
+    from minfer_b200.tokenizer import Qwen3Tokenizer
+
+    tokens, merges, types = _args(vocab)
+    t = Qwen3Tokenizer.from_vocab(tokens, merges, types, vocab["templates"]["chatml_min"], vocab["eos"], vocab["pad"])
+    lib = host_lib()
+    text = b"The quick brown fox jumps over the lazy dog."
+    full = t.encode(text)
+    ids = (C.c_uint32 * 3)(7, 7, 7)
+    n = C.c_size_t()
+    assert lib.mf_tokenizer_encode(t._h, text, len(text), ids, 2, C.byref(n)) == MF_OK
+    assert n.value == len(full) and list(ids) == full[:2] + [7]
+    arr = (C.c_uint32 * len(full))(*full)
+    out = C.create_string_buffer(b"#" * 8, 8)
+    assert lib.mf_tokenizer_decode(t._h, arr, len(full), out, 5, C.byref(n)) == MF_OK
+    assert n.value == len(text) and out.raw[:5] == text[:5] and out.raw[5:8] == b"###"
+    out = C.create_string_buffer(4)
+    mj = b'[{"role": "user", "content": "hi"}]'
+    assert lib.mf_tokenizer_apply_chat_template(t._h, mj, None, 1, out, 4, C.byref(n)) == MF_OK
+    assert n.value == len(t.apply_chat_template([{"role": "user", "content": "hi"}]).encode())
+    ends = (C.c_size_t * 1)()
+    assert lib.mf_tokenizer_pre_split(t._h, text, len(text), ends, 1, C.byref(n)) == MF_OK
+    assert n.value == len(t.pre_split(text)) and ends[0] == len(t.pre_split(text)[0])
