@@ -560,3 +560,25 @@ def test_c_abi_short_buffers(vocab):
     ends = (C.c_size_t * 1)()
     assert lib.mf_tokenizer_pre_split(t._h, text, len(text), ends, 1, C.byref(n)) == MF_OK
     assert n.value == len(t.pre_split(text)) and ends[0] == len(t.pre_split(text)[0])
+
+
+def test_byte_vocabulary_generator():
+    """The synthetic models' byte-level vocabulary (gguf_synth.synth_byte_vocab,
+    used by the text tests): every single byte, every merge's result an entry,
+    the chat specials typed as control tokens, and any byte string encodes and
+    decodes back unchanged."""
+    from minfer_b200.gguf_synth import CHAT_TEMPLATE, synth_byte_vocab
+    from minfer_b200.tokenizer import Qwen3Tokenizer
+
+    tokens, types, merges, eos, pad = synth_byte_vocab(1024, 107)
+    assert len(tokens) == len(types) == 1024 and len(set(tokens[:256])) == 256
+    vocab = set(tokens)
+    for m in merges:  # "left right", where either part may hold spaces: some split gives an entry
+        assert any(m[k:k + 1] == b" " and m[:k] + m[k + 1:] in vocab for k in range(1, len(m) - 1)), m
+    assert tokens[eos] == b"<|im_end|>" and tokens[pad] == b"<|endoftext|>"
+    assert types[tokens.index(b"<|im_start|>")] == 3 and types[-1] == 5
+    t = Qwen3Tokenizer.from_vocab(tokens, merges, types, CHAT_TEMPLATE, eos, pad)
+    rng = random.Random(8)
+    for _ in range(200):
+        b = bytes(rng.randrange(256) for _ in range(rng.randint(0, 64)))
+        assert t.decode(t.encode(b)) == b
