@@ -114,9 +114,44 @@ bool Value::truthy() const {
 
 namespace {
 
+// Well-formed UTF-8 (no overlong forms, surrogates or code points past
+// U+10FFFF): what a JSON writer accepts.
+bool valid_utf8(const std::string& s) {
+    const auto* p = reinterpret_cast<const unsigned char*>(s.data());
+    const size_t n = s.size();
+    for (size_t i = 0; i < n;) {
+        const unsigned c = p[i];
+        size_t len;
+        unsigned lo = 0x80, hi = 0xBF;
+        if (c < 0x80) {
+            ++i;
+            continue;
+        } else if (c >= 0xC2 && c <= 0xDF) {
+            len = 2;
+        } else if (c >= 0xE0 && c <= 0xEF) {
+            len = 3;
+            if (c == 0xE0) lo = 0xA0;
+            if (c == 0xED) hi = 0x9F;
+        } else if (c >= 0xF0 && c <= 0xF4) {
+            len = 4;
+            if (c == 0xF0) lo = 0x90;
+            if (c == 0xF4) hi = 0x8F;
+        } else {
+            return false;
+        }
+        if (i + len > n || p[i + 1] < lo || p[i + 1] > hi) return false;
+        for (size_t k = 2; k < len; ++k)
+            if ((p[i + k] & 0xC0) != 0x80) return false;
+        i += len;
+    }
+    return true;
+}
+
 // JSON text of a string: quotes, backslash and control characters escaped
-// (\b \f \n \r \t, others as \u00xx); other bytes unchanged.
+// (\b \f \n \r \t, others as \u00xx); other bytes unchanged. Text that is
+// not UTF-8 cannot be written as JSON (the reference's engine throws too).
 std::string json_quote(const std::string& s) {
+    if (!valid_utf8(s)) throw std::runtime_error("invalid UTF-8 in a string written as JSON");
     std::string out = "\"";
     for (unsigned char c : s) {
         switch (c) {

@@ -582,3 +582,26 @@ def test_byte_vocabulary_generator():
     for _ in range(200):
         b = bytes(rng.randrange(256) for _ in range(rng.randint(0, 64)))
         assert t.decode(t.encode(b)) == b
+
+
+def test_json_output_needs_utf8():
+    """Strings written as JSON (tojson, printed lists and objects) must be
+    UTF-8; printed directly they pass through as bytes."""
+    import ctypes as C
+
+    from minfer_b200._lib import MF_E_STATE, MF_OK
+    from minfer_b200.tokenizer import Qwen3Tokenizer
+
+    t = Qwen3Tokenizer.from_vocab([bytes([i]) for i in range(256)], [], [1] * 256,
+                                  "{{ messages[0].content }}{% if messages[0].role == 'json' %}"
+                                  "|{{ messages[0].content | tojson }}{% endif %}")
+    out = C.create_string_buffer(256)
+    n = C.c_size_t()
+
+    def render(role, content):
+        mj = b'[{"role": "' + role + b'", "content": "' + content + b'"}]'
+        return t._lib.mf_tokenizer_apply_chat_template(t._h, mj, None, 1, out, 256, C.byref(n))
+
+    assert render(b"user", b"bad \xff") == MF_OK and out.raw[:n.value] == b"bad \xff"
+    assert render(b"json", b"ok \xc3\xa9") == MF_OK and out.raw[:n.value] == b'ok \xc3\xa9|"ok \xc3\xa9"'
+    assert render(b"json", b"bad \xff") == MF_E_STATE
