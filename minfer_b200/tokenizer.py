@@ -109,6 +109,13 @@ class Qwen3Tokenizer:
     def decode_token(self, token_id: int) -> bytes:
         return self.decode([token_id])
 
+    # BaseTokenizer::get_eos_id / get_pad_id (include/minfer/base/tokenizer.hpp:39-40)
+    def get_eos_id(self) -> int:
+        return self.eos_id
+
+    def get_pad_id(self) -> int:
+        return self.pad_id
+
     def pre_split(self, text) -> list[bytes]:
         """The pieces encode turns into ids (the reference's regex_split)."""
         b = _b(text)

@@ -169,6 +169,7 @@ def test_reference_error_behaviour(vocab):
     unused = types.index(5)
     assert t.decode_token(unused) == b"<UNK>"
     assert t.decode_token(vocab["eos"]) == b"<|im_end|>"
+    assert (t.get_eos_id(), t.get_pad_id()) == (vocab["eos"], vocab["pad"])
     # a vocabulary without the byte the text needs: the reference throws
     no_z = Qwen3Tokenizer.from_vocab([b"a", b"b"], [], [1, 1])
     assert no_z.encode("abba") == [0, 1, 1, 0]
