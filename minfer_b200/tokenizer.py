@@ -109,7 +109,7 @@ class Qwen3Tokenizer:
     def decode_token(self, token_id: int) -> bytes:
         return self.decode([token_id])
 
-    # BaseTokenizer::get_eos_id / get_pad_id (include/minfer/base/tokenizer.hpp:39-40)
+    # BaseTokenizer::get_eos_id / get_pad_id (include/minfer/base/tokenizer.hpp:41-42)
     def get_eos_id(self) -> int:
         return self.eos_id
 
